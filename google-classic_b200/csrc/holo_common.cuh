@@ -1,0 +1,221 @@
+// holo_common.cuh -- shared definitions of the B200 decode-path library.
+//
+// Block formats are GGUF's (src/ai/quant.h:43-120 of the reference engine);
+// everything else here is this library's own: the per-device runtime state,
+// the repacked ("tiled") weight layout, and the sm_100a PTX helpers for
+// mbarriers and bulk (TMA) copies.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "cuda_ops.h"
+#include "holo_b200.h"
+
+// ---------------------------------------------------------------------------
+// ggml type ids (src/ai/quant.h:20-33)
+// ---------------------------------------------------------------------------
+enum : int {
+    GT_F32 = 0, GT_F16 = 1, GT_Q4_0 = 2, GT_Q8_0 = 8, GT_Q4_K = 12, GT_Q6_K = 14,
+};
+
+// ---------------------------------------------------------------------------
+// Tiled weight layout (format version 1)
+//
+// Rows are grouped in row-blocks of 32 (padded with zero rows).  A row-block's
+// K extent is cut into K-chunks; one (row-block, K-chunk) pair is a tile and
+// tiles are stored back to back in (row-block, K-chunk) order, so tile t of a
+// matrix starts at rb*32*row_bytes + kc*TILE_FULL and any run of consecutive
+// tiles is one contiguous byte range.  Inside a tile, data is transposed so
+// that lane r of a warp reads row r with unit stride between lanes:
+//   Q8_0 (32 blocks per K-chunk): qs [blk][half][row][16 B], then d [blk][row] f16
+//   Q4_0 (64 blocks per K-chunk): qs [blk][row][16 B],       then d [blk][row] f16
+//   Q4_K (8 super-blocks):        [sb][row][144 B], super-block in the quant.c
+//                                 (src/ai/quant.c:277-311) semantics
+// The byte count equals the GGUF count for the padded rows (no bloat).
+// ---------------------------------------------------------------------------
+constexpr int TILE_ROWS = 32;
+
+template <int T> struct TileGeom;
+template <> struct TileGeom<GT_Q8_0> {
+    static constexpr int BLK_ELEMS = 32, BLK_BYTES = 34, BLKS_PER_TILE = 32, BLKS_PER_WARP = 4;
+    static constexpr int TILE_FULL = TILE_ROWS * BLKS_PER_TILE * BLK_BYTES;   // 34816
+};
+template <> struct TileGeom<GT_Q4_0> {
+    static constexpr int BLK_ELEMS = 32, BLK_BYTES = 18, BLKS_PER_TILE = 64, BLKS_PER_WARP = 8;
+    static constexpr int TILE_FULL = TILE_ROWS * BLKS_PER_TILE * BLK_BYTES;   // 36864
+};
+template <> struct TileGeom<GT_Q4_K> {
+    static constexpr int BLK_ELEMS = 256, BLK_BYTES = 144, BLKS_PER_TILE = 8, BLKS_PER_WARP = 1;
+    static constexpr int TILE_FULL = TILE_ROWS * BLKS_PER_TILE * BLK_BYTES;   // 36864
+};
+
+static inline int64_t gguf_row_bytes(int type, int64_t cols) {
+    switch (type) {
+    case GT_F32:  return cols * 4;
+    case GT_F16:  return cols * 2;
+    case GT_Q8_0: return (cols / 32) * 34;
+    case GT_Q4_0: return (cols / 32) * 18;
+    case GT_Q4_K: return (cols / 256) * 144;
+    case GT_Q6_K: return (cols / 256) * 210;
+    default: return -1;
+    }
+}
+static inline int gguf_block_elems(int type) {
+    switch (type) {
+    case GT_Q8_0: case GT_Q4_0: return 32;
+    case GT_Q4_K: case GT_Q6_K: return 256;
+    default: return 1;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host runtime (runtime.cu)
+// ---------------------------------------------------------------------------
+struct HoloDevice {
+    bool ready = false;
+    int id = 0;
+    int sms = 0;
+    cudaStream_t stream = nullptr;       // the ABI's implicit compute stream
+    cudaStream_t copy_stream = nullptr;  // cuda_memcpy_*_async
+    cudaDeviceProp prop{};
+    // split-K fix-up scratch of the tiled matvec (zeroed once; self-cleaning)
+    float *mv_partials = nullptr;        // [MV_MAX_CTAS][2][32]
+    int *mv_counters = nullptr;          // [MV_MAX_ROWBLOCKS]
+    int *status = nullptr;               // device-side error word (bounded waits)
+    // small persistent buffers for reductions that return to the host
+    void *reduce_buf = nullptr;          // 64 KB
+    void *pinned = nullptr;              // 64 KB pinned host buffer
+    void *tmp = nullptr;                 // growable scratch of the ABI helpers
+    size_t tmp_bytes = 0;
+};
+constexpr int MV_MAX_CTAS = 1024;
+constexpr int MV_MAX_ROWBLOCKS = 1 << 16;
+
+HoloDevice *holo_dev();                  // current device's state, initialised on demand
+cudaStream_t holo_stream();
+void holo_set_status(int code, const char *what);   // sticky host-side status
+bool holo_check_launch(const char *what);           // cudaGetLastError -> status
+// Scratch of at least `bytes` on the current device for ABI helpers whose
+// reference signature has no workspace argument (grows; synchronises then).
+void *holo_tmp(size_t bytes);
+
+// Registry of repacked weights: device pointer -> geometry.
+struct WeightInfo {
+    int type = 0;
+    int rows = 0, cols = 0;
+    int rows_padded = 0;
+    int q4k_layout = 0;     // layout of the source blocks before normalisation
+    size_t bytes = 0;
+};
+bool holo_registry_find(const void *ptr, WeightInfo *out);
+void holo_registry_add(const void *ptr, const WeightInfo &info);
+bool holo_registry_remove(const void *ptr);
+
+int holo_act_mode();        // HOLO_ACT_F32 / HOLO_ACT_Q8 (env HOLO_ACT, cuda_set_act_mode)
+int holo_q4k_layout();      // HOLO_Q4K_REF / HOLO_Q4K_GGML (env HOLO_Q4K_LAYOUT)
+
+// matvec dispatch (matvec.cu / matvec_raw.cu)
+void holo_matvec_tiled(float *dst, const void *M, const WeightInfo &wi, const float *v,
+                       int out_dim, int in_dim, int act_mode, const float *residual,
+                       cudaStream_t st);
+void holo_matvec_raw(float *dst, const void *M, int type, const float *v,
+                     int out_dim, int in_dim, int act_mode, int q4k_layout, cudaStream_t st,
+                     const float *residual);
+
+#define HOLO_CUDA_TRY(call, what)                                                     \
+    do {                                                                              \
+        cudaError_t e_ = (call);                                                      \
+        if (e_ != cudaSuccess) { holo_set_status((int)e_, what); }                    \
+    } while (0)
+
+// ---------------------------------------------------------------------------
+// Device helpers
+// ---------------------------------------------------------------------------
+#ifdef __CUDACC__
+
+// Bounded waits: give up after this many nanoseconds of %globaltimer.
+constexpr unsigned long long HOLO_WAIT_LIMIT_NS = 1000000000ull;   // 1 s
+
+__device__ __forceinline__ unsigned long long holo_globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" :: "r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }"
+                 :: "r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Wait for phase `parity` of `bar` to complete, for at most HOLO_WAIT_LIMIT_NS.
+// On time-out, records `code` in *status and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *status, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    unsigned long long t0 = holo_globaltimer();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 255u && holo_globaltimer() - t0 > HOLO_WAIT_LIMIT_NS) {
+            if (status) atomicExch(status, code);
+            return false;
+        }
+    }
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (no multicast).
+__device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src_gmem, uint32_t bytes,
+                                         uint64_t *bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        :: "r"(smem_addr(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// named barrier among a subset of warps
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(const void *p) {
+    return *reinterpret_cast<const uint4 *>(p);
+}
+
+// exact small-integer <-> float through the 2^23 mantissa (|v| < 2^22)
+__device__ __forceinline__ float int_to_float_exact(int v) {
+    return __int_as_float(v + 0x4B400000) - 12582912.0f;
+}
+// byte k of w (0..255) as an exact float
+__device__ __forceinline__ float ubyte_to_float(uint32_t w, int k) {
+    return __int_as_float(__byte_perm(w, 0x4B000000u, 0x7440u + k)) - 8388608.0f;
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t h16) {
+    return __half2float(__ushort_as_half((unsigned short)h16));
+}
+
+#endif  // __CUDACC__

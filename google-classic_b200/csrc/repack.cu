@@ -1,0 +1,180 @@
+// repack.cu -- one-time rewrite of raw GGUF blocks into the tiled layout
+// (holo_common.cuh).  Takes over from upload_tensor (src/ai/llm_cuda.c:189-196),
+// which copies the raw blocks as they are.
+#include "holo_common.cuh"
+
+#include <cstdio>
+
+namespace {
+
+__device__ __forceinline__ size_t tile_offset(int rb, int kc, size_t row_bytes, int tile_full) {
+    return (size_t)rb * TILE_ROWS * row_bytes + (size_t)kc * tile_full;
+}
+
+// Q8_0: one thread per (row, block).
+__global__ void repack_q8_0_kernel(uint8_t *__restrict__ out, const uint8_t *__restrict__ in,
+                                   int rows, int nblk) {
+    using G = TileGeom<GT_Q8_0>;
+    int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)rows * nblk) return;
+    int r = (int)(gid / nblk), b = (int)(gid % nblk);
+    size_t row_bytes = (size_t)nblk * G::BLK_BYTES;
+    const uint8_t *src = in + (size_t)r * row_bytes + (size_t)b * G::BLK_BYTES;
+    int rb = r / TILE_ROWS, lr = r % TILE_ROWS;
+    int kc = b / G::BLKS_PER_TILE, bi = b % G::BLKS_PER_TILE;
+    int nb = min(G::BLKS_PER_TILE, nblk - kc * G::BLKS_PER_TILE);
+    uint8_t *tile = out + tile_offset(rb, kc, row_bytes, G::TILE_FULL);
+    uint8_t *q0 = tile + ((size_t)(bi * 2 + 0) * TILE_ROWS + lr) * 16;
+    uint8_t *q1 = tile + ((size_t)(bi * 2 + 1) * TILE_ROWS + lr) * 16;
+    for (int i = 0; i < 16; i++) { q0[i] = src[2 + i]; q1[i] = src[18 + i]; }
+    uint8_t *dd = tile + (size_t)nb * 1024 + ((size_t)bi * TILE_ROWS + lr) * 2;
+    dd[0] = src[0]; dd[1] = src[1];
+}
+
+__global__ void repack_q4_0_kernel(uint8_t *__restrict__ out, const uint8_t *__restrict__ in,
+                                   int rows, int nblk) {
+    using G = TileGeom<GT_Q4_0>;
+    int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)rows * nblk) return;
+    int r = (int)(gid / nblk), b = (int)(gid % nblk);
+    size_t row_bytes = (size_t)nblk * G::BLK_BYTES;
+    const uint8_t *src = in + (size_t)r * row_bytes + (size_t)b * G::BLK_BYTES;
+    int rb = r / TILE_ROWS, lr = r % TILE_ROWS;
+    int kc = b / G::BLKS_PER_TILE, bi = b % G::BLKS_PER_TILE;
+    int nb = min(G::BLKS_PER_TILE, nblk - kc * G::BLKS_PER_TILE);
+    uint8_t *tile = out + tile_offset(rb, kc, row_bytes, G::TILE_FULL);
+    uint8_t *q = tile + ((size_t)bi * TILE_ROWS + lr) * 16;
+    for (int i = 0; i < 16; i++) q[i] = src[2 + i];
+    uint8_t *dd = tile + (size_t)nb * 512 + ((size_t)bi * TILE_ROWS + lr) * 2;
+    dd[0] = src[0]; dd[1] = src[1];
+}
+
+// Q4_K: one thread per (row, super-block); ggml-semantics blocks are rewritten
+// into the quant.c semantics with identical dequantized values:
+//   scales: get_scale_min_k4 (cuda_ops.cu:684-692) -> quant.c:290-297 packing
+//   nibbles: 32 B per 64 values (cuda_ops.cu:712-729) -> 16 B per 32 values
+__global__ void repack_q4_k_kernel(uint8_t *__restrict__ out, const uint8_t *__restrict__ in,
+                                   int rows, int nsb, int ggml) {
+    using G = TileGeom<GT_Q4_K>;
+    int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)rows * nsb) return;
+    int r = (int)(gid / nsb), s = (int)(gid % nsb);
+    size_t row_bytes = (size_t)nsb * G::BLK_BYTES;
+    const uint8_t *src = in + (size_t)r * row_bytes + (size_t)s * G::BLK_BYTES;
+    int rb = r / TILE_ROWS, lr = r % TILE_ROWS;
+    int kc = s / G::BLKS_PER_TILE, si = s % G::BLKS_PER_TILE;
+    uint8_t *dst = out + tile_offset(rb, kc, row_bytes, G::TILE_FULL) + ((size_t)si * TILE_ROWS + lr) * 144;
+    if (!ggml) {
+        for (int i = 0; i < 144; i++) dst[i] = src[i];
+        return;
+    }
+    uint8_t sc[8], mn[8];
+    const uint8_t *q = src + 4;
+    for (int j = 0; j < 8; j++) {
+        if (j < 4) { sc[j] = q[j] & 63; mn[j] = q[j + 4] & 63; }
+        else {
+            sc[j] = (uint8_t)((q[j + 4] & 0x0f) | ((q[j - 4] >> 6) << 4));
+            mn[j] = (uint8_t)((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
+        }
+    }
+    for (int i = 0; i < 4; i++) dst[i] = src[i];
+    for (int j = 0; j < 4; j++) {
+        dst[4 + j] = (uint8_t)(sc[j] | ((sc[j + 4] & 3) << 6));
+        dst[8 + j] = (uint8_t)(mn[j] | ((mn[j + 4] & 3) << 6));
+        dst[12 + j] = (uint8_t)((sc[j + 4] >> 2) | ((mn[j + 4] >> 2) << 4));
+    }
+    // value v of sub-block j, position l (0..31): ggml group g = j/2 holds it in
+    // byte qs[g*32 + l], low nibble for even j, high nibble for odd j.
+    const uint8_t *qs = src + 16;
+    for (int j = 0; j < 8; j++) {
+        int g = j >> 1, hi = j & 1;
+        for (int l = 0; l < 16; l++) {
+            uint8_t a = qs[g * 32 + l], b = qs[g * 32 + l + 16];
+            uint8_t na = hi ? (a >> 4) : (a & 0x0f);
+            uint8_t nb = hi ? (b >> 4) : (b & 0x0f);
+            dst[16 + j * 16 + l] = (uint8_t)(na | (nb << 4));
+        }
+    }
+}
+
+bool check_shape(int type, int rows, int cols) {
+    if (rows <= 0 || cols <= 0) return false;
+    if (type == GT_Q4_K) return cols % 256 == 0;
+    if (type == GT_Q8_0 || type == GT_Q4_0) return cols % 32 == 0;
+    return false;
+}
+
+}  // namespace
+
+extern "C" size_t cuda_quant_tiled_bytes(int ggml_type, int rows, int cols) {
+    if (!check_shape(ggml_type, rows, cols)) return 0;
+    int rp = (rows + TILE_ROWS - 1) / TILE_ROWS * TILE_ROWS;
+    return (size_t)rp * (size_t)gguf_row_bytes(ggml_type, cols);
+}
+
+extern "C" void *cuda_repack_quant(const void *dev_blocks, int ggml_type, int rows, int cols) {
+    if (!check_shape(ggml_type, rows, cols) || !dev_blocks) {
+        holo_set_status(HOLO_E_ARG, "cuda_repack_quant: unsupported type or shape");
+        return nullptr;
+    }
+    HoloDevice *D = holo_dev();
+    if (!D) return nullptr;
+    cudaStream_t st = holo_stream();
+    size_t bytes = cuda_quant_tiled_bytes(ggml_type, rows, cols);
+    void *out = nullptr;
+    if (cudaMalloc(&out, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        holo_set_status(HOLO_E_NOMEM, "cuda_repack_quant: allocation");
+        return nullptr;
+    }
+    cudaMemsetAsync(out, 0, bytes, st);   // padding rows are zero
+    int layout = holo_q4k_layout();
+    const int threads = 256;
+    if (ggml_type == GT_Q8_0) {
+        int nblk = cols / 32;
+        int64_t n = (int64_t)rows * nblk;
+        repack_q8_0_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
+            (uint8_t *)out, (const uint8_t *)dev_blocks, rows, nblk);
+    } else if (ggml_type == GT_Q4_0) {
+        int nblk = cols / 32;
+        int64_t n = (int64_t)rows * nblk;
+        repack_q4_0_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
+            (uint8_t *)out, (const uint8_t *)dev_blocks, rows, nblk);
+    } else {
+        int nsb = cols / 256;
+        int64_t n = (int64_t)rows * nsb;
+        repack_q4_k_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
+            (uint8_t *)out, (const uint8_t *)dev_blocks, rows, nsb, layout == HOLO_Q4K_GGML);
+    }
+    if (!holo_check_launch("repack kernel")) { cudaFree(out); return nullptr; }
+    WeightInfo wi;
+    wi.type = ggml_type;
+    wi.rows = rows;
+    wi.cols = cols;
+    wi.rows_padded = (rows + TILE_ROWS - 1) / TILE_ROWS * TILE_ROWS;
+    wi.q4k_layout = layout;
+    wi.bytes = bytes;
+    holo_registry_add(out, wi);
+    return out;
+}
+
+extern "C" void *cuda_upload_quant(const void *host_blocks, int ggml_type, int rows, int cols) {
+    if (!check_shape(ggml_type, rows, cols) || !host_blocks) {
+        holo_set_status(HOLO_E_ARG, "cuda_upload_quant: unsupported type or shape");
+        return nullptr;
+    }
+    if (!holo_dev()) return nullptr;
+    cudaStream_t st = holo_stream();
+    size_t raw = (size_t)rows * (size_t)gguf_row_bytes(ggml_type, cols);
+    void *staging = nullptr;
+    if (cudaMalloc(&staging, raw) != cudaSuccess) {
+        cudaGetLastError();
+        holo_set_status(HOLO_E_NOMEM, "cuda_upload_quant: staging allocation");
+        return nullptr;
+    }
+    HOLO_CUDA_TRY(cudaMemcpyAsync(staging, host_blocks, raw, cudaMemcpyHostToDevice, st), "cuda_upload_quant: copy");
+    void *out = cuda_repack_quant(staging, ggml_type, rows, cols);
+    cudaStreamSynchronize(st);
+    cudaFree(staging);
+    return out;
+}

@@ -1,0 +1,137 @@
+"""ctypes binding of the checker libraries (TEST INFRASTRUCTURE ONLY).
+
+* ``Oracle``    -> oracle/_build/liboracle.so: the CPU restatement (holo_oracle.c)
+* ``Reference`` -> oracle/_ref/libholo_ref.so: the reference engine's own C code
+                   compiled from source (oracle/Makefile)
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+legs import this module; the product library never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import pathlib
+import subprocess
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+ORACLE_SO = HERE / "_build" / "liboracle.so"
+REF_SO = HERE / "_ref" / "libholo_ref.so"
+
+_vp, _i, _f = C.c_void_p, C.c_int, C.c_float
+_i64 = C.c_int64
+
+
+def build():
+    """Compile the restatement (and the reference, where its sources exist)."""
+    subprocess.run(["make", "-s", "-C", str(HERE), "all"], check=True)
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class Oracle:
+    def __init__(self):
+        if not ORACLE_SO.exists():
+            build()
+        lib = C.CDLL(str(ORACLE_SO))
+        lib.ho_f16_to_f32.restype = _f
+        lib.ho_f16_to_f32.argtypes = [C.c_uint16]
+        lib.ho_f32_to_f16_rn.restype = C.c_uint16
+        lib.ho_f32_to_f16_rn.argtypes = [_f]
+        lib.ho_row_bytes.restype = _i64
+        lib.ho_row_bytes.argtypes = [_i, _i64]
+        lib.ho_dequant_row.argtypes = [_i, _vp, _vp, _i64, _i]
+        lib.ho_matvec_f32act.argtypes = [_i, _vp, _vp, _vp, _i, _i, _i, _i]
+        lib.ho_quantize_act_q8.argtypes = [_vp, _i64, _vp, _vp, _vp]
+        lib.ho_matvec_q8act.argtypes = [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i]
+        lib.ho_q4k_to_ref_layout.argtypes = [_vp, _vp, _i]
+        self.lib = lib
+
+    def dequant(self, gtype, blocks, rows, cols, q4k_layout=0):
+        blocks = np.ascontiguousarray(blocks)
+        out = np.empty((rows, cols), np.float32)
+        rb = self.lib.ho_row_bytes(gtype, cols)
+        for r in range(rows):
+            self.lib.ho_dequant_row(gtype, _ptr(blocks) + r * rb, _ptr(out) + r * cols * 4, cols, q4k_layout)
+        return out
+
+    def matvec_f32(self, gtype, blocks, x, rows, cols, q4k_layout=0, threads=1):
+        blocks = np.ascontiguousarray(blocks)
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.empty(rows, np.float32)
+        self.lib.ho_matvec_f32act(gtype, _ptr(blocks), _ptr(x), _ptr(y), rows, cols, q4k_layout, threads)
+        return y
+
+    def quantize_act(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        n = x.size
+        q = np.empty(n, np.int8)
+        d = np.empty(n // 32, np.float32)
+        s = np.empty(n // 32, np.int32)
+        self.lib.ho_quantize_act_q8(_ptr(x), n, _ptr(q), _ptr(d), _ptr(s))
+        return q, d, s
+
+    def matvec_q8(self, gtype, blocks, x, rows, cols, q4k_layout=0, want_isums=False, threads=1):
+        blocks = np.ascontiguousarray(blocks)
+        q, d, s = self.quantize_act(x)
+        y = np.empty(rows, np.float32)
+        isums = np.empty((rows, cols // 32), np.int32) if want_isums else None
+        self.lib.ho_matvec_q8act(gtype, _ptr(blocks), _ptr(q), _ptr(d), _ptr(s), _ptr(y), rows, cols,
+                                 q4k_layout, _ptr(isums) if want_isums else None, threads)
+        return (y, isums) if want_isums else y
+
+    def q4k_to_ref(self, blocks, layout):
+        blocks = np.ascontiguousarray(blocks).reshape(-1, 144)
+        out = np.empty_like(blocks)
+        for i in range(blocks.shape[0]):
+            self.lib.ho_q4k_to_ref_layout(_ptr(blocks) + i * 144, _ptr(out) + i * 144, layout)
+        return out.reshape(-1)
+
+
+class Reference:
+    """The reference engine's own CPU functions (src/ai/*.c built from source)."""
+
+    def __init__(self):
+        if not REF_SO.exists():
+            build()
+        if not REF_SO.exists():
+            raise RuntimeError("oracle/_ref/libholo_ref.so is absent and the reference sources are not here")
+        lib = C.CDLL(str(REF_SO))
+        lib.matmul_q.argtypes = [_vp, _vp, _vp, _i, _i, _i]
+        lib.href_matmul_q_threads.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i]
+        for name in ("dequantize_row_q8_0", "dequantize_row_q4_0", "dequantize_row_q4_k"):
+            getattr(lib, name).argtypes = [_vp, _vp, _i]
+        lib.f16_to_f32.restype = _f
+        lib.f16_to_f32.argtypes = [C.c_uint16]
+        lib.href_model_create.restype = _vp
+        lib.href_model_create.argtypes = [_i, _i, _i, _i, _i, _i, _i, _i, _f, _f]
+        lib.href_model_set_types.argtypes = [_vp, _i, _i, _i]
+        lib.href_model_set_layer.argtypes = [_vp, _i] + [_vp] * 9
+        lib.href_model_set_globals.argtypes = [_vp, _vp, _vp, _vp]
+        lib.href_forward.restype = _i
+        lib.href_forward.argtypes = [_vp, _i]
+        lib.href_logits.restype = C.POINTER(C.c_float)
+        lib.href_logits.argtypes = [_vp]
+        lib.href_reset.argtypes = [_vp]
+        lib.href_push_token.argtypes = [_vp, _i]
+        lib.href_sample.restype = _i
+        lib.href_sample.argtypes = [_vp, _f, _f, _i, _f, _i]
+        lib.href_model_free.argtypes = [_vp]
+        self.lib = lib
+
+    def matmul_q(self, gtype, blocks, x, rows, cols, threads=1):
+        blocks = np.ascontiguousarray(blocks)
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.empty(rows, np.float32)
+        self.lib.href_matmul_q_threads(_ptr(y), _ptr(blocks), _ptr(x), rows, cols, gtype, threads)
+        return y
+
+    def dequant(self, gtype, blocks, rows, cols):
+        name = {8: "dequantize_row_q8_0", 2: "dequantize_row_q4_0", 12: "dequantize_row_q4_k"}[gtype]
+        blocks = np.ascontiguousarray(blocks)
+        out = np.empty((rows, cols), np.float32)
+        getattr(self.lib, name)(_ptr(blocks), _ptr(out), rows * cols)
+        return out

@@ -1,0 +1,149 @@
+/*
+ * ref_harness.c -- drives the reference engine's own C code (test
+ * infrastructure only).
+ *
+ * oracle/Makefile compiles this file together with the reference sources
+ * src/ai/{quant,tensor,gguf,llm}.c, taken where they lie, into
+ * oracle/_ref/libholo_ref.so.  The functions here only fill the reference's
+ * public structs (src/ai/llm.h:22-200) in memory, so no GGUF file is needed,
+ * and call the reference's own entry points: matmul_q (llm.c:770),
+ * llm_forward (llm.c:1015), llm_sample (llm.c:1281), llm_reset (llm.c:732).
+ */
+#include "llm.h"
+#include "quant.h"
+
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* weight-type globals of src/ai/llm.c:335-342 */
+extern int g_emb_type, g_weight_type, g_v_weight_type, g_w1_weight_type;
+extern int g_w2_weight_type, g_w3_weight_type, g_output_type, g_emb_vocab_size;
+extern void matmul_q(float *dst, const void *M, const float *v,
+                     int out_dim, int in_dim, int quant_type);
+
+/* Reference matmul_q over row slices, one slice per thread.  matmul_q itself
+ * is unchanged; each row's arithmetic is the same whatever the slicing. */
+void href_matmul_q_threads(float *dst, const void *M, const float *v,
+                           int out_dim, int in_dim, int qtype, int nthreads) {
+    size_t row_bytes = quant_row_size(qtype, in_dim);
+    if (qtype == GGML_TYPE_F32) row_bytes = (size_t)in_dim * 4;
+    if (nthreads <= 1) { matmul_q(dst, M, v, out_dim, in_dim, qtype); return; }
+#pragma omp parallel num_threads(nthreads)
+    {
+        int t = omp_get_thread_num(), n = omp_get_num_threads();
+        int r0 = (int)((long long)out_dim * t / n), r1 = (int)((long long)out_dim * (t + 1) / n);
+        if (r1 > r0)
+            matmul_q(dst + r0, (const char *)M + (size_t)r0 * row_bytes, v, r1 - r0, in_dim, qtype);
+    }
+}
+
+typedef struct {
+    llm_ctx_t ctx;
+} href_model_t;
+
+href_model_t *href_model_create(int n_layers, int dim, int n_heads, int n_kv_heads,
+                                int head_dim, int ffn_dim, int vocab, int max_seq,
+                                float rope_base, float eps) {
+    href_model_t *m = (href_model_t *)calloc(1, sizeof(href_model_t));
+    llm_ctx_t *c = &m->ctx;
+    strcpy(c->config.arch, "llama");
+    c->config.vocab_size = vocab;
+    c->config.context_length = max_seq;
+    c->config.embedding_dim = dim;
+    c->config.n_layers = n_layers;
+    c->config.n_heads = n_heads;
+    c->config.n_kv_heads = n_kv_heads;
+    c->config.head_dim = head_dim;
+    c->config.ffn_dim = ffn_dim;
+    c->config.rope_freq_base = rope_base;
+    c->config.rms_norm_eps = eps;
+    c->config.eos_token = -1;
+    c->weights.n_layers = n_layers;
+    c->weights.layers = calloc(n_layers, sizeof(*c->weights.layers));
+    int q_dim = n_heads * head_dim, kv_dim = n_kv_heads * head_dim;
+    int big = dim > q_dim ? dim : q_dim;
+    /* buffer sizes follow alloc_state (llm.c:534-560) */
+    c->state.x = calloc(big, 4);
+    c->state.xb = calloc(big, 4);
+    c->state.xb2 = calloc(big, 4);
+    c->state.hb = calloc(ffn_dim, 4);
+    c->state.hb2 = calloc(ffn_dim, 4);
+    c->state.q = calloc(big, 4);
+    c->state.k = calloc(big > kv_dim ? big : kv_dim, 4);
+    c->state.v = calloc(big > kv_dim ? big : kv_dim, 4);
+    c->state.att = calloc((size_t)n_heads * max_seq, 4);
+    c->state.logits = calloc(vocab, 4);
+    size_t kv = (size_t)n_layers * max_seq * kv_dim;
+    c->kv_cache.key_cache = calloc(kv, 4);
+    c->kv_cache.value_cache = calloc(kv, 4);
+    c->kv_cache.max_seq_len = max_seq;
+    c->kv_cache.n_layers = n_layers;
+    c->kv_cache.n_kv_heads = n_kv_heads;
+    c->kv_cache.head_dim = head_dim;
+    c->max_tokens = max_seq;
+    c->tokens = calloc(max_seq, sizeof(int));
+    c->loaded = true;
+    return m;
+}
+
+/* Types of the weight globals llm_forward reads (llm.c:1035, 1107, 1250). */
+void href_model_set_types(href_model_t *m, int layer_type, int emb_type, int out_type) {
+    (void)m;
+    g_weight_type = g_v_weight_type = layer_type;
+    g_w1_weight_type = g_w2_weight_type = g_w3_weight_type = layer_type;
+    g_emb_type = emb_type;
+    g_output_type = out_type;
+    g_emb_vocab_size = m->ctx.config.vocab_size;
+    for (int l = 0; l < m->ctx.weights.n_layers; l++) {
+        m->ctx.weights.layers[l].wv_type = layer_type;
+        m->ctx.weights.layers[l].w2_type = layer_type;
+    }
+}
+
+void href_model_set_layer(href_model_t *m, int l, void *attn_norm, void *wq, void *wk,
+                          void *wv, void *wo, void *ffn_norm, void *w1, void *w2, void *w3) {
+    typeof(m->ctx.weights.layers[0]) *L = &m->ctx.weights.layers[l];
+    L->attn_norm = attn_norm; L->wq = wq; L->wk = wk; L->wv = wv; L->wo = wo;
+    L->ffn_norm = ffn_norm; L->w1 = w1; L->w2 = w2; L->w3 = w3;
+}
+
+void href_model_set_globals(href_model_t *m, void *tok_emb, void *final_norm, void *output) {
+    m->ctx.weights.tok_embeddings = tok_emb;
+    m->ctx.weights.norm = final_norm;
+    m->ctx.weights.output = output;
+}
+
+int href_forward(href_model_t *m, int token) { return llm_forward(&m->ctx, &token, 1); }
+float *href_logits(href_model_t *m) { return m->ctx.state.logits; }
+int href_pos(href_model_t *m) { return m->ctx.pos; }
+void href_reset(href_model_t *m) { llm_reset(&m->ctx); }
+
+/* token history used by the repetition penalty (llm.c:1292-1298) */
+void href_push_token(href_model_t *m, int token) {
+    if (m->ctx.n_tokens < m->ctx.max_tokens) m->ctx.tokens[m->ctx.n_tokens++] = token;
+}
+
+int href_sample(href_model_t *m, float temperature, float top_p, int top_k,
+                float repeat_penalty, int repeat_last_n) {
+    llm_sampler_t s;
+    s.temperature = temperature;
+    s.top_p = top_p;
+    s.top_k = top_k;
+    s.repeat_penalty = repeat_penalty;
+    s.repeat_last_n = repeat_last_n;
+    s.seed = 0;
+    return llm_sample(&m->ctx, &s);
+}
+
+void href_model_free(href_model_t *m) {
+    llm_ctx_t *c = &m->ctx;
+    free(c->state.x); free(c->state.xb); free(c->state.xb2); free(c->state.hb);
+    free(c->state.hb2); free(c->state.q); free(c->state.k); free(c->state.v);
+    free(c->state.att); free(c->state.logits);
+    free(c->kv_cache.key_cache); free(c->kv_cache.value_cache);
+    free(c->weights.layers); free(c->tokens);
+    free(m);
+}

@@ -1,0 +1,54 @@
+"""The drop-in boundary: libholo_cuda.so loads without a GPU and exports every
+function declared in include/*.h, including every entry point of the
+reference's include/cuda_ops.h.  CPU only (no compute calls)."""
+import subprocess
+
+import holo_b200 as hb
+
+# the 48 functions of the reference header include/cuda_ops.h (lines 18-133)
+REFERENCE_ABI = """
+cuda_init cuda_cleanup cuda_available cuda_print_info cuda_get_device_count cuda_get_free_memory
+cuda_get_device_name cuda_malloc cuda_free cuda_memcpy_h2d cuda_memcpy_d2h cuda_memcpy_d2d
+cuda_memcpy_d2d_async cuda_memcpy_d2h_async cuda_memset cuda_sync cuda_sync_copy cuda_vec_add
+cuda_vec_mul cuda_vec_scale cuda_vec_dot cuda_matmul_f32 cuda_matmul_f16 cuda_matmul_q8_0
+cuda_matmul_q4_0 cuda_matmul_q4_k cuda_matmul_q6_k cuda_batched_qkv_q8_0
+cuda_batched_ffn_gate_up_q8_0 cuda_silu cuda_silu_mul cuda_gelu cuda_relu cuda_rms_norm
+cuda_layer_norm cuda_softmax cuda_softmax_inplace cuda_attention_scores cuda_attention_apply
+cuda_attention_single cuda_multi_head_attention cuda_rope_apply cuda_get_embedding_f32
+cuda_get_embedding_f16 cuda_get_embedding_q8_0 cuda_get_embedding_q4_0 cuda_get_embedding_q6_k
+cuda_argmax
+""".split()
+
+
+def exported():
+    out = subprocess.run(["nm", "-D", "--defined-only", str(hb.LIB_PATH)], capture_output=True, text=True, check=True)
+    return {line.split()[-1] for line in out.stdout.splitlines() if " T " in line}
+
+
+def test_library_loads_without_gpu(lib):
+    assert lib is not None
+
+
+def test_every_header_symbol_is_exported():
+    names = hb.header_symbols()
+    assert len(names) >= len(REFERENCE_ABI)
+    missing = sorted(set(names) - exported())
+    assert not missing, missing
+
+
+def test_reference_abi_is_complete():
+    declared = set(hb.header_symbols())
+    assert len(REFERENCE_ABI) == 48
+    assert set(REFERENCE_ABI) <= declared
+    assert set(REFERENCE_ABI) <= exported()
+
+
+def test_python_signatures_cover_headers():
+    assert set(hb.header_symbols()) <= set(hb.SIGNATURES)
+
+
+def test_kernels_are_built_for_sm100a_only():
+    out = subprocess.run(["/usr/local/cuda/bin/cuobjdump", "--list-elf", str(hb.LIB_PATH)],
+                         capture_output=True, text=True)
+    archs = {w for w in out.stdout.split() if "sm_" in w}
+    assert archs and all("sm_100a" in a for a in archs), archs
