@@ -22,7 +22,7 @@ enum : int {
 };
 
 // ---------------------------------------------------------------------------
-// Tiled weight layout (format version 1)
+// Tiled weight layout (format version 2: ~18 KB tiles)
 //
 // Rows are grouped in row-blocks of 32 (padded with zero rows).  A row-block's
 // K extent is cut into K-chunks; one (row-block, K-chunk) pair is a tile and
@@ -30,9 +30,9 @@ enum : int {
 // matrix starts at rb*32*row_bytes + kc*TILE_FULL and any run of consecutive
 // tiles is one contiguous byte range.  Inside a tile, data is transposed so
 // that lane r of a warp reads row r with unit stride between lanes:
-//   Q8_0 (32 blocks per K-chunk): qs [blk][half][row][16 B], then d [blk][row] f16
-//   Q4_0 (64 blocks per K-chunk): qs [blk][row][16 B],       then d [blk][row] f16
-//   Q4_K (8 super-blocks):        [sb][row][144 B], super-block in the quant.c
+//   Q8_0 (16 blocks per K-chunk): qs [blk][half][row][16 B], then d [blk][row] f16
+//   Q4_0 (32 blocks per K-chunk): qs [blk][row][16 B],       then d [blk][row] f16
+//   Q4_K (4 super-blocks):        [sb][row][144 B], super-block in the quant.c
 //                                 (src/ai/quant.c:277-311) semantics
 // The byte count equals the GGUF count for the padded rows (no bloat).
 // ---------------------------------------------------------------------------
@@ -40,16 +40,16 @@ constexpr int TILE_ROWS = 32;
 
 template <int T> struct TileGeom;
 template <> struct TileGeom<GT_Q8_0> {
-    static constexpr int BLK_ELEMS = 32, BLK_BYTES = 34, BLKS_PER_TILE = 32, BLKS_PER_WARP = 4;
-    static constexpr int TILE_FULL = TILE_ROWS * BLKS_PER_TILE * BLK_BYTES;   // 34816
+    static constexpr int BLK_ELEMS = 32, BLK_BYTES = 34, BLKS_PER_TILE = 16, BLKS_PER_WARP = 2;
+    static constexpr int TILE_FULL = TILE_ROWS * BLKS_PER_TILE * BLK_BYTES;   // 17408
 };
 template <> struct TileGeom<GT_Q4_0> {
-    static constexpr int BLK_ELEMS = 32, BLK_BYTES = 18, BLKS_PER_TILE = 64, BLKS_PER_WARP = 8;
-    static constexpr int TILE_FULL = TILE_ROWS * BLKS_PER_TILE * BLK_BYTES;   // 36864
+    static constexpr int BLK_ELEMS = 32, BLK_BYTES = 18, BLKS_PER_TILE = 32, BLKS_PER_WARP = 4;
+    static constexpr int TILE_FULL = TILE_ROWS * BLKS_PER_TILE * BLK_BYTES;   // 18432
 };
-template <> struct TileGeom<GT_Q4_K> {
-    static constexpr int BLK_ELEMS = 256, BLK_BYTES = 144, BLKS_PER_TILE = 8, BLKS_PER_WARP = 1;
-    static constexpr int TILE_FULL = TILE_ROWS * BLKS_PER_TILE * BLK_BYTES;   // 36864
+template <> struct TileGeom<GT_Q4_K> {   // blocks are 256-value super-blocks; two warps share one
+    static constexpr int BLK_ELEMS = 256, BLK_BYTES = 144, BLKS_PER_TILE = 4, BLKS_PER_WARP = 1;
+    static constexpr int TILE_FULL = TILE_ROWS * BLKS_PER_TILE * BLK_BYTES;   // 18432
 };
 
 static inline int64_t gguf_row_bytes(int type, int64_t cols) {
@@ -116,6 +116,7 @@ bool holo_registry_remove(const void *ptr);
 
 int holo_act_mode();        // HOLO_ACT_F32 / HOLO_ACT_Q8 (env HOLO_ACT, cuda_set_act_mode)
 int holo_q4k_layout();      // HOLO_Q4K_REF / HOLO_Q4K_GGML (env HOLO_Q4K_LAYOUT)
+int holo_pdl();             // programmatic dependent launch of tiled matvecs (env HOLO_PDL)
 
 // matvec dispatch (matvec.cu / matvec_raw.cu)
 void holo_matvec_tiled(float *dst, const void *M, const WeightInfo &wi, const float *v,

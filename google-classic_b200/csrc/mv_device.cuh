@@ -10,15 +10,7 @@
 // Each operation is correctly rounded, so results equal a C implementation
 // built without contraction.  Packs q into 8 little-endian int8x4 words.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void quantize_block_q8(const float *__restrict__ xb, uint32_t w[8],
-                                                  float &d_out, int &asum_out) {
-    float v[32];
-    const float4 *x4 = reinterpret_cast<const float4 *>(xb);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        float4 t = __ldg(x4 + i);
-        v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
-    }
+__device__ __forceinline__ void quantize_vals_q8(const float v[32], uint32_t w[8], float &d_out, int &asum_out) {
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(v[i]));
@@ -39,6 +31,18 @@ __device__ __forceinline__ void quantize_block_q8(const float *__restrict__ xb, 
     }
     d_out = d;
     asum_out = asum;
+}
+
+__device__ __forceinline__ void quantize_block_q8(const float *__restrict__ xb, uint32_t w[8],
+                                                  float &d_out, int &asum_out) {
+    float v[32];
+    const float4 *x4 = reinterpret_cast<const float4 *>(xb);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        float4 t = __ldg(x4 + i);
+        v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+    }
+    quantize_vals_q8(v, w, d_out, asum_out);
 }
 
 // ---------------------------------------------------------------------------
@@ -63,6 +67,29 @@ __device__ __forceinline__ int dot_nib16_q8(uint4 q, uint4 a0, uint4 a1) {
     return s;
 }
 
+// dp4a with unsigned bytes in a, signed bytes in b
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// 16 * sum nib*qa, same layout as dot_nib16_q8; the high nibbles are used in
+// place (byte = 16*nib) so no shift is needed; exact (|result| < 2^20).
+__device__ __forceinline__ int dot_nib16_q8_x16(uint4 q, uint4 a0, uint4 a1) {
+    constexpr uint32_t HI4 = 0xF0F0F0F0u;
+    int lo = 0, hi = 0;
+    lo = __dp4a((int)(q.x & LO4), (int)a0.x, lo);
+    hi = dp4a_us(q.x & HI4, a1.x, hi);
+    lo = __dp4a((int)(q.y & LO4), (int)a0.y, lo);
+    hi = dp4a_us(q.y & HI4, a1.y, hi);
+    lo = __dp4a((int)(q.z & LO4), (int)a0.z, lo);
+    hi = dp4a_us(q.z & HI4, a1.z, hi);
+    lo = __dp4a((int)(q.w & LO4), (int)a0.w, lo);
+    hi = dp4a_us(q.w & HI4, a1.w, hi);
+    return (lo << 4) + hi;
+}
+
 // 32 int8 codes (q0: positions 0..15, q1: 16..31) against 32 int8 activations
 __device__ __forceinline__ int dot_i8x32_q8(uint4 q0, uint4 q1, uint4 a0, uint4 a1) {
     int s = 0;
@@ -81,6 +108,14 @@ __device__ __forceinline__ int dot_i8x32_q8(uint4 q0, uint4 q1, uint4 a0, uint4 
 // fp32-activation block dots: sum code*x over one 32-element block, codes
 // turned into exact floats through the 2^23 mantissa (no I2F).
 // ---------------------------------------------------------------------------
+// SMEM: xb points into shared memory (plain loads); else global (read-only path)
+template <bool SMEM = false>
+__device__ __forceinline__ float4 ld_x4(const float4 *p) {
+    if constexpr (SMEM) return *p;
+    else return __ldg(p);
+}
+
+template <bool SMEM = false>
 __device__ __forceinline__ float dot_nib16_f32(uint4 q, const float *__restrict__ xb) {
     const float4 *x4 = reinterpret_cast<const float4 *>(xb);
     uint32_t lo[4] = {q.x & LO4, q.y & LO4, q.z & LO4, q.w & LO4};
@@ -88,7 +123,7 @@ __device__ __forceinline__ float dot_nib16_f32(uint4 q, const float *__restrict_
     float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        float4 xl = __ldg(x4 + i), xh = __ldg(x4 + 4 + i);
+        float4 xl = ld_x4<SMEM>(x4 + i), xh = ld_x4<SMEM>(x4 + 4 + i);
         s0 = fmaf(ubyte_to_float(lo[i], 0), xl.x, s0);
         s1 = fmaf(ubyte_to_float(lo[i], 1), xl.y, s1);
         s0 = fmaf(ubyte_to_float(lo[i], 2), xl.z, s0);
@@ -106,6 +141,7 @@ __device__ __forceinline__ float sbyte_to_float(uint32_t w_biased, int k) {
     return __int_as_float(__byte_perm(w_biased, 0x4B000000u, 0x7440u + k)) - 8388736.0f;
 }
 
+template <bool SMEM = false>
 __device__ __forceinline__ float dot_i8x32_f32(uint4 q0, uint4 q1, const float *__restrict__ xb) {
     const float4 *x4 = reinterpret_cast<const float4 *>(xb);
     uint32_t w[8] = {q0.x ^ 0x80808080u, q0.y ^ 0x80808080u, q0.z ^ 0x80808080u, q0.w ^ 0x80808080u,
@@ -113,7 +149,7 @@ __device__ __forceinline__ float dot_i8x32_f32(uint4 q0, uint4 q1, const float *
     float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        float4 xv = __ldg(x4 + i);
+        float4 xv = ld_x4<SMEM>(x4 + i);
         s0 = fmaf(sbyte_to_float(w[i], 0), xv.x, s0);
         s1 = fmaf(sbyte_to_float(w[i], 1), xv.y, s1);
         s0 = fmaf(sbyte_to_float(w[i], 2), xv.z, s0);

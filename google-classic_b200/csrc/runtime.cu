@@ -26,6 +26,7 @@ std::unordered_map<const void *, WeightInfo> g_registry;
 
 int g_act_mode = -1;
 int g_q4k_layout = -1;
+int g_pdl = -1;
 
 int current_device() {
     int d = 0;
@@ -134,6 +135,13 @@ int holo_act_mode() {
     }
     return g_act_mode;
 }
+int holo_pdl() {
+    if (g_pdl < 0) {
+        const char *e = getenv("HOLO_PDL");
+        g_pdl = (e && e[0] == '1') ? 1 : 0;
+    }
+    return g_pdl;
+}
 int holo_q4k_layout() {
     if (g_q4k_layout < 0) {
         const char *e = getenv("HOLO_Q4K_LAYOUT");
@@ -180,6 +188,8 @@ void cuda_clear_status(void) {
     cudaGetLastError();
 }
 
+void cuda_set_pdl(int on) { g_pdl = on ? 1 : 0; }
+int cuda_get_pdl(void) { return holo_pdl(); }
 void cuda_set_act_mode(int mode) { g_act_mode = (mode == HOLO_ACT_F32) ? HOLO_ACT_F32 : HOLO_ACT_Q8; }
 int cuda_get_act_mode(void) { return holo_act_mode(); }
 void cuda_set_q4k_layout(int layout) { g_q4k_layout = (layout == HOLO_Q4K_GGML) ? HOLO_Q4K_GGML : HOLO_Q4K_REF; }

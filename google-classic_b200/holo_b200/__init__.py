@@ -81,6 +81,7 @@ SIGNATURES = {
     "cuda_block_sums_q8": (None, [_vp, _vp, _vp, _i, _i, _i]),
     "cuda_get_stream": (_vp, []), "cuda_set_stream": (None, [_vp]),
     "cuda_init_rank": (_i, [_i, _i]), "cuda_sm_count": (_i, []),
+    "cuda_set_pdl": (None, [_i]), "cuda_get_pdl": (_i, []),
     "cuda_capture_begin": (_i, []), "cuda_capture_end": (_vp, []),
     "cuda_graph_launch": (None, [_vp]), "cuda_graph_free": (None, [_vp]),
 }

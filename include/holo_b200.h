@@ -63,6 +63,16 @@ void *cuda_repack_quant(const void *dev_blocks, int ggml_type, int rows, int col
 /* Bytes of the tiled copy of a rows x cols matrix (rows padded to 32). */
 size_t cuda_quant_tiled_bytes(int ggml_type, int rows, int cols);
 
+/* ---- programmatic dependent launch ------------------------------------------
+ * When on, the tiled matvecs are launched with programmatic stream
+ * serialisation: a matvec may start streaming its weights while the previous
+ * kernel on the stream is still running, and waits for that kernel only
+ * before it reads activations or writes outputs.  Safe when the weights are
+ * not written by the kernel just before the matvec (they never are after
+ * cuda_upload_quant returns).  Default off; env HOLO_PDL=1 turns it on. */
+void cuda_set_pdl(int on);
+int cuda_get_pdl(void);
+
 /* ---- explicit matvec -------------------------------------------------------
  * dst = M . v (+ residual when residual != NULL, may alias dst), with the
  * activation mode given per call.  M raw or tiled as for cuda_matmul_*. */

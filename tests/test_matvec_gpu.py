@@ -225,6 +225,45 @@ def test_repeated_calls_are_deterministic(dev):
     dev.free(Wd)
 
 
+def test_dependent_chain_with_pdl_and_graph(dev, oracle):
+    """A chain of dependent matvecs (y1 = W1.x; y2 = y1 + W2.y1) gives the same
+    bits with programmatic dependent launch on and off, and replayed from a
+    CUDA graph."""
+    n = 4096
+    W1 = synth.quant_matrix(hb.Q4_K, n, n, 50)
+    W2 = synth.quant_matrix(hb.Q8_0, n, n, 51)
+    x = synth.activation(n, 50)
+    W1d, W2d = dev.upload_quant(W1, hb.Q4_K, n, n), dev.upload_quant(W2, hb.Q8_0, n, n)
+    xd, y1, y2 = dev.upload(x), dev.alloc(4 * n), dev.alloc(4 * n)
+
+    def chain():
+        dev.lib.cuda_matvec(y1, W1d, xd, n, n, hb.Q4_K, hb.ACT_Q8, None)
+        dev.lib.cuda_matvec(y2, W2d, y1, n, n, hb.Q8_0, hb.ACT_Q8, y1)
+
+    outs = []
+    for pdl in (0, 1):
+        dev.lib.cuda_set_pdl(pdl)
+        chain()
+        outs.append(dev.download(y2, (n,), np.float32))
+    dev.lib.cuda_set_pdl(1)
+    assert dev.lib.cuda_capture_begin() == 0
+    chain()
+    g = dev.lib.cuda_capture_end()
+    dev.lib.cuda_memset(y2, 0, 4 * n)
+    for _ in range(3):
+        dev.lib.cuda_graph_launch(g)
+    outs.append(dev.download(y2, (n,), np.float32))
+    dev.lib.cuda_graph_free(g)
+    dev.lib.cuda_set_pdl(0)
+    dev.check()
+    for o in outs[1:]:
+        assert np.array_equal(o.view(np.uint32), outs[0].view(np.uint32))
+    r1 = oracle.matvec_q8(hb.Q4_K, W1, x, n, n)
+    assert rel_err(outs[0], r1 + oracle.matvec_q8(hb.Q8_0, W2, r1, n, n)) <= 1e-3
+    for p in (W1d, W2d, xd, y1, y2):
+        dev.free(p)
+
+
 def test_unsupported_shape_sets_status_not_fault(dev):
     """A K extent beyond the tiled kernel's shared memory is refused on the
     host with HOLO_E_UNSUPPORTED; the context stays usable."""

@@ -79,8 +79,9 @@ def rope_ref(v, pos, hd, base):
     v = v.astype(np.float64).reshape(-1, hd).copy()
     half = hd // 2
     i = np.arange(half)
-    freq = 1.0 / np.power(np.float32(base), (2 * i).astype(np.float32) / hd)
-    th = pos * freq
+    # the reference computes freq and theta in float32 (src/ai/llm.c:1139-1141)
+    freq = (np.float32(1.0) / np.power(np.float32(base), (2 * i).astype(np.float32) / np.float32(hd))).astype(np.float32)
+    th = (np.float32(pos) * freq).astype(np.float32).astype(np.float64)
     c, s = np.cos(th), np.sin(th)
     a, b = v[:, :half].copy(), v[:, half:].copy()
     v[:, :half] = a * c - b * s
@@ -94,8 +95,8 @@ def test_rope(dev, pos, base):
     q, k = synth.activation(nh * hd, 8), synth.activation(nkv * hd, 9)
     qd, kd = up(dev, q), up(dev, k)
     dev.lib.cuda_rope_apply(qd, kd, pos, hd, nh, nkv, np.float32(base))
-    assert np.abs(dev.download(qd, (nh * hd,), np.float32) - rope_ref(q, pos, hd, base)).max() <= 2e-4
-    assert np.abs(dev.download(kd, (nkv * hd,), np.float32) - rope_ref(k, pos, hd, base)).max() <= 2e-4
+    assert np.abs(dev.download(qd, (nh * hd,), np.float32) - rope_ref(q, pos, hd, base)).max() <= 2e-5
+    assert np.abs(dev.download(kd, (nkv * hd,), np.float32) - rope_ref(k, pos, hd, base)).max() <= 2e-5
     dev.check()
     dev.free(qd)
     dev.free(kd)
