@@ -22,35 +22,65 @@ enum : int {
 };
 
 // ---------------------------------------------------------------------------
-// Tiled weight layout (format version 2: ~18 KB tiles)
+// Tiled weight layout (format version 3: units)
 //
 // Rows are grouped in row-blocks of 32 (padded with zero rows).  A row-block's
-// K extent is cut into K-chunks; one (row-block, K-chunk) pair is a tile and
-// tiles are stored back to back in (row-block, K-chunk) order, so tile t of a
-// matrix starts at rb*32*row_bytes + kc*TILE_FULL and any run of consecutive
-// tiles is one contiguous byte range.  Inside a tile, data is transposed so
-// that lane r of a warp reads row r with unit stride between lanes:
-//   Q8_0 (16 blocks per K-chunk): qs [blk][half][row][16 B], then d [blk][row] f16
-//   Q4_0 (32 blocks per K-chunk): qs [blk][row][16 B],       then d [blk][row] f16
-//   Q4_K (4 super-blocks):        [sb][row][144 B], super-block in the quant.c
-//                                 (src/ai/quant.c:277-311) semantics
-// The byte count equals the GGUF count for the padded rows (no bloat).
+// K extent is cut into units of a fixed number of values (Q4_K: one 256-value
+// super-block; Q4_0: eight 32-blocks; Q8_0: four 32-blocks), and units are
+// stored back to back in (row-block, unit) order: unit u = rb*units_per_row + s
+// starts at u * UNIT_BYTES.  Inside a unit, data is transposed so that lane r
+// of a warp reads row r with unit stride between lanes:
+//   head  [row][HEAD_BYTES]   Q4_K: the 16-byte super-block head (fp16 d, fp16
+//                             dmin, 12 bytes of 6-bit scales/mins, quant.c
+//                             packing, src/ai/quant.c:277-311);
+//                             Q4_0: eight fp16 block scales; Q8_0: four
+//   plane [p][row][16 B]      p = 0..7: Q4_K sub-block p / Q4_0 block p, 32
+//                             nibbles (low nibble of byte l = position l, high
+//                             = l+16); Q8_0 half p&1 of block p>>1, 16 int8
+// A row whose block count is not a multiple of the unit's is padded with zero
+// blocks (d = 0); Q4_K rows are whole units by definition.
 // ---------------------------------------------------------------------------
 constexpr int TILE_ROWS = 32;
+constexpr int UNIT_PLANES = 8;
 
-template <int T> struct TileGeom;
-template <> struct TileGeom<GT_Q8_0> {
-    static constexpr int BLK_ELEMS = 32, BLK_BYTES = 34, BLKS_PER_TILE = 16, BLKS_PER_WARP = 2;
-    static constexpr int TILE_FULL = TILE_ROWS * BLKS_PER_TILE * BLK_BYTES;   // 17408
+template <int T> struct UnitGeom;
+template <> struct UnitGeom<GT_Q8_0> {
+    static constexpr int BLK_ELEMS = 32, BLK_BYTES = 34, VALS = 128, BLKS32 = 4, HEAD_BYTES = 8;
+    static constexpr int UNIT_BYTES = TILE_ROWS * HEAD_BYTES + UNIT_PLANES * TILE_ROWS * 16;   // 4352
 };
-template <> struct TileGeom<GT_Q4_0> {
-    static constexpr int BLK_ELEMS = 32, BLK_BYTES = 18, BLKS_PER_TILE = 32, BLKS_PER_WARP = 4;
-    static constexpr int TILE_FULL = TILE_ROWS * BLKS_PER_TILE * BLK_BYTES;   // 18432
+template <> struct UnitGeom<GT_Q4_0> {
+    static constexpr int BLK_ELEMS = 32, BLK_BYTES = 18, VALS = 256, BLKS32 = 8, HEAD_BYTES = 16;
+    static constexpr int UNIT_BYTES = TILE_ROWS * HEAD_BYTES + UNIT_PLANES * TILE_ROWS * 16;   // 4608
 };
-template <> struct TileGeom<GT_Q4_K> {   // blocks are 256-value super-blocks; two warps share one
-    static constexpr int BLK_ELEMS = 256, BLK_BYTES = 144, BLKS_PER_TILE = 4, BLKS_PER_WARP = 1;
-    static constexpr int TILE_FULL = TILE_ROWS * BLKS_PER_TILE * BLK_BYTES;   // 18432
+template <> struct UnitGeom<GT_Q4_K> {
+    static constexpr int BLK_ELEMS = 256, BLK_BYTES = 144, VALS = 256, BLKS32 = 8, HEAD_BYTES = 16;
+    static constexpr int UNIT_BYTES = TILE_ROWS * HEAD_BYTES + UNIT_PLANES * TILE_ROWS * 16;   // 4608
 };
+
+template <int T> __host__ __device__ constexpr size_t unit_head_off(int r) {
+    return (size_t)r * UnitGeom<T>::HEAD_BYTES;
+}
+template <int T> __host__ __device__ constexpr size_t unit_plane_off(int p, int r) {
+    return (size_t)TILE_ROWS * UnitGeom<T>::HEAD_BYTES + ((size_t)p * TILE_ROWS + r) * 16;
+}
+
+// units per row and bytes of the tiled copy (0: type without a tiled layout)
+static inline int units_per_row(int type, int cols) {
+    switch (type) {
+    case GT_Q8_0: return (cols + UnitGeom<GT_Q8_0>::VALS - 1) / UnitGeom<GT_Q8_0>::VALS;
+    case GT_Q4_0: return (cols + UnitGeom<GT_Q4_0>::VALS - 1) / UnitGeom<GT_Q4_0>::VALS;
+    case GT_Q4_K: return cols / UnitGeom<GT_Q4_K>::VALS;
+    default: return 0;
+    }
+}
+static inline int unit_bytes(int type) {
+    switch (type) {
+    case GT_Q8_0: return UnitGeom<GT_Q8_0>::UNIT_BYTES;
+    case GT_Q4_0: return UnitGeom<GT_Q4_0>::UNIT_BYTES;
+    case GT_Q4_K: return UnitGeom<GT_Q4_K>::UNIT_BYTES;
+    default: return 0;
+    }
+}
 
 static inline int64_t gguf_row_bytes(int type, int64_t cols) {
     switch (type) {
@@ -107,6 +137,7 @@ struct WeightInfo {
     int type = 0;
     int rows = 0, cols = 0;
     int rows_padded = 0;
+    int units = 0;          // units per row of the tiled layout
     int q4k_layout = 0;     // layout of the source blocks before normalisation
     size_t bytes = 0;
 };

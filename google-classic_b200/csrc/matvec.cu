@@ -4,26 +4,27 @@
 // 618-676, 694-732, 859-1060), which read 34/18/144-byte blocks with byte
 // loads, one block or warp per row.
 //
-// Design (persistent, two CTAs per SM when shared memory allows, 9 warps each):
-//   * warp 8 is the producer: one lane streams the CTA's tiles (~18 KB) from
-//     HBM into a ring of shared-memory stages with 1-D bulk copies
-//     (cp.async.bulk, L2 evict-first), completion counted on an mbarrier per
-//     stage; weights are constant, so it starts before the PDL wait;
-//   * warps 0..7 consume: lane r owns row r of the 32-row tile, warp w owns
-//     1/8 of the tile's K extent, so the shared-memory reads of a warp are 32
-//     consecutive 16-byte pieces (conflict-free) and activation reads are
-//     broadcasts; per-row partials meet in shared memory at the end of each
-//     row-block;
-//   * the CTAs split the (row-block, K-chunk) tile sequence evenly (stream-K);
-//     a row-block cut between CTAs is finished deterministically by the last
-//     CTA to contribute (acq_rel atomic counter, partials summed in CTA order);
-//   * prologue (consumers, after the PDL wait): optional RMSNorm of x (the
-//     reference's rms_norm, src/ai/tensor.c:242-255), then HOLO_ACT_Q8
-//     quantizes per 32-block into shared memory (dp4a dots) or HOLO_ACT_F32
-//     stages fp32 x in shared memory (fp32 FMA dots);
+// Design (one 256-thread CTA per SM, room for a second one):
+//   * the weights are in the unit layout (holo_common.cuh): warp w of a CTA
+//     takes every NWARP-th unit of the CTA's contiguous unit range, and lane r
+//     holds row r of the unit -- eight coalesced 16-byte loads per lane per
+//     unit, so the per-unit index work is amortised over 144 bytes a row;
+//   * before the PDL wait, the CTA prefetches its first units into L2 with
+//     bulk prefetches (nothing returns to the SM) -- the next kernel's CTAs
+//     are resident while this one runs, so HBM streams the next matrix while
+//     the current one finishes; after the wait, x (and the RMSNorm weights)
+//     arrive in shared memory through one bulk copy each, and each warp keeps
+//     MV_DEPTH units loading into registers and MV_L2_AHEAD units in L2;
+//   * prologue: optional RMSNorm of x (the reference's rms_norm,
+//     src/ai/tensor.c:242-255), then HOLO_ACT_Q8 quantizes x per 32-block
+//     (one thread per block) or HOLO_ACT_F32 takes fp32 block sums;
+//   * per-warp partials of each row-block meet in shared memory; a row-block
+//     cut between CTAs is finished deterministically by the last CTA to
+//     contribute (acq_rel atomic counter, partials summed in CTA order);
 //   * epilogues: store, residual add (src/ai/llm.c:1217, 1245), or the SwiGLU
 //     gate (silu(g)*u, llm.c:1231-1236) over row pairs interleaved by 16.
-// Every wait is bounded (1 s); a time-out sets the device status word.
+// The kernel has no waits on other CTAs: the fix-up is last-arriver, not spin;
+// its one wait (the activation copy) is bounded.
 #include "holo_common.cuh"
 #include "mv_device.cuh"
 #include "matvec.cuh"
@@ -32,9 +33,12 @@
 
 namespace {
 
-constexpr int NCWARP = 8;                 // consumer warps
-constexpr int NTHREADS = (NCWARP + 1) * 32;
-constexpr int BAR_CONSUMERS = 1;          // named barrier id of the consumer warps
+constexpr int NWARP = 8;                  // warps per CTA
+constexpr int NTHREADS = NWARP * 32;
+constexpr int MIN_CTAS_PER_SM = 2;        // room for the next kernel's CTA (PDL overlap)
+constexpr int MV_DEPTH = 2;               // units of loads kept in flight per warp (ring)
+constexpr int MV_L2_AHEAD = 5;            // units per warp prefetched into L2 ahead of use
+constexpr size_t SMEM_LIMIT = 227 * 1024;
 
 struct MvParams {
     const uint8_t *W;
@@ -45,104 +49,171 @@ struct MvParams {
     float eps;
     int out_dim, in_dim;
     int nblk32;          // in_dim / 32
-    int blks_per_row;    // GGUF blocks per row (Q4_K: super-blocks)
-    int nkc, nrb, total_tiles, nctas, stages;
-    size_t row_bytes;
+    int nblk32p;         // 32-blocks per row of the tiled layout (padded to whole units)
+    int units;           // units per row
+    int nrb, total_units, nctas;
+    int max_local_rb;    // row-blocks one CTA can touch (size of the reduction buffer)
+    int bulk;            // x (and norm_w) 16-byte aligned: staged by one bulk copy each
     float *partials;
     int *counters;
-    int *status;
+    int *status;         // device status word (bounded waits)
 };
 
-__device__ __forceinline__ int tile_owner(long long t, long long T, long long C) {
+// Shared-memory map of one CTA (byte offsets), the same on host and device:
+//   red   [max_local_rb][NWARP][32] f32   per-warp row-block partials
+//   act   ACT_Q8: q8 [nblk32p*32] i8, (d, d*asum) [nblk32p] f32x2
+//   stage x as copied in, padded with zeros to nblk32p*32 values
+//         (ACT_F32: this is the activation itself, followed by xsum [nblk32p])
+//   nw    RMSNorm weights (NORM only)
+//   misc  mbarrier, per-warp sums of squares
+struct MvSmem {
+    size_t red, act, stage, nw, misc, total;
+};
+__host__ __device__ __forceinline__ MvSmem mv_smem_layout(int act, bool norm, int max_local_rb, int nblk32p) {
+    MvSmem L;
+    size_t o = 0;
+    L.red = o;
+    o += (size_t)max_local_rb * NWARP * 32 * sizeof(float);
+    L.act = o;
+    if (act == HOLO_ACT_Q8) {
+        o += (size_t)nblk32p * 40;
+        L.stage = o;
+        o += (size_t)nblk32p * 128;
+    } else {
+        L.stage = o;
+        o += (size_t)nblk32p * 132;
+    }
+    L.nw = o;
+    if (norm) o += (size_t)nblk32p * 128;
+    L.misc = o;
+    o += 128;
+    L.total = o;
+    return L;
+}
+
+// L2 prefetch of a byte range (no data returns to the SM)
+__device__ __forceinline__ void prefetch_l2_bulk(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(src), "r"(bytes) : "memory");
+}
+
+// 1-D bulk copy global -> shared (no multicast, no cache hint)
+__device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
+}
+
+// Even split of T units over C CTAs (T*C < 2^32 is checked on the host).
+__device__ __forceinline__ int tile_owner(unsigned t, unsigned T, unsigned C) {
     return (int)(((t + 1) * C - 1) / T);
 }
-__device__ __forceinline__ int tile_begin(long long c, long long T, long long C) {
+__device__ __forceinline__ int tile_begin(unsigned c, unsigned T, unsigned C) {
     return (int)(T * c / C);
 }
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// ---------------------------------------------------------------------------
-// per-tile consumer arithmetic: this lane's (row's) partial over the warp's
-// share of the tile
-// ---------------------------------------------------------------------------
-template <int TYPE, int ACT>
-__device__ __forceinline__ float consume_tile(const uint8_t *__restrict__ tile, int kc, int nb, int warp, int lane,
-                                              const uint8_t *__restrict__ aq, const float2 *__restrict__ ads,
-                                              const float *__restrict__ xs, const float *__restrict__ xsum) {
-    float acc = 0.0f;
-    if constexpr (TYPE == GT_Q4_K) {
-        const int sb = warp >> 1, half = warp & 1;
-        if (sb < nb) {
-            const uint8_t *sbp = tile + (size_t)(sb * TILE_ROWS + lane) * 144;
-            const uint4 h = lds128(sbp);
-            const float d = half_bits_to_float(h.x & 0xffffu), dmin = half_bits_to_float(h.x >> 16);
-            uint32_t scw, mw;
-            if (half == 0) {
-                scw = h.y & 0x3F3F3F3Fu;
-                mw = h.z & 0x3F3F3F3Fu;
-            } else {
-                scw = ((h.w & LO4) << 2) | ((h.y >> 6) & 0x03030303u);
-                mw = (((h.w >> 4) & LO4) << 2) | ((h.z >> 6) & 0x03030303u);
-            }
-            const int blk0 = (kc * TileGeom<GT_Q4_K>::BLKS_PER_TILE + sb) * 8 + half * 4;
+// rint(v) for |v| < 2^22 through the 1.5*2^23 mantissa: round half to even,
+// the same result as cvt.rni (and C rintf) without the conversion unit
+__device__ __forceinline__ int rint_small(float v) {
+    return __float_as_int(__fadd_rn(v, 12582912.0f)) - 0x4B400000;
+}
+
+// streaming loads: read once, not kept in L1
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ldg_stream2(const void *p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+// What one warp loads for one unit (lane = row): eight 16-byte code planes and
+// the row's head (Q4_K head / Q4_0 eight fp16 scales / Q8_0 four).
+struct Frag {
+    uint4 q[UNIT_PLANES];
+    uint4 h;
+};
+
+template <int TYPE>
+__device__ __forceinline__ void load_unit(Frag &f, const uint8_t *__restrict__ unit, int lane) {
+    const uint8_t *row = unit + (size_t)TILE_ROWS * UnitGeom<TYPE>::HEAD_BYTES + lane * 16;
 #pragma unroll
-            for (int jj = 0; jj < 4; jj++) {
-                const uint4 q = lds128(sbp + 16 + 16 * (half * 4 + jj));
-                const int blk = blk0 + jj;
-                const float sc = d * ubyte_to_float(scw, jj), mn = dmin * ubyte_to_float(mw, jj);
-                if constexpr (ACT == HOLO_ACT_Q8) {
-                    const uint4 a0 = lds128(aq + (size_t)blk * 32), a1 = lds128(aq + (size_t)blk * 32 + 16);
-                    const float2 ds = ads[blk];
-                    const float f16 = int_to_float_exact(dot_nib16_q8_x16(q, a0, a1));
-                    acc = fmaf(sc * 0.0625f, ds.x * f16, acc);
-                    acc = fmaf(-mn, ds.y, acc);
-                } else {
-                    acc = fmaf(sc, dot_nib16_f32<true>(q, xs + (size_t)blk * 32), acc);
-                    acc = fmaf(-mn, xsum[blk], acc);
-                }
+    for (int pl = 0; pl < UNIT_PLANES; ++pl) f.q[pl] = ldg_stream(row + pl * TILE_ROWS * 16);
+    if constexpr (TYPE == GT_Q8_0) {
+        const uint2 h = ldg_stream2(unit + lane * 8);
+        f.h = make_uint4(h.x, h.y, 0u, 0u);
+    } else {
+        f.h = ldg_stream(unit + lane * 16);
+    }
+}
+
+// fp16 scale k (0..7) of a head word set
+__device__ __forceinline__ float head_half(const uint4 &h, int k) {
+    const uint32_t w = k < 2 ? h.x : k < 4 ? h.y : k < 6 ? h.z : h.w;
+    return half_bits_to_float((k & 1) ? (w >> 16) : (w & 0xffffu));
+}
+
+// this lane's (row's) contribution of one unit, added into acc; b0 = index of
+// the unit's first 32-block in the activation vector
+template <int TYPE, int ACT>
+__device__ __forceinline__ void unit_dot(float &acc, const Frag &f, int b0, const uint8_t *__restrict__ aq,
+                                         const float2 *__restrict__ ads, const float *__restrict__ xs,
+                                         const float *__restrict__ xsum) {
+    if constexpr (TYPE == GT_Q4_K) {
+        const uint4 h = f.h;
+        // d/16 is exact, so (d/16)*sc rounds like (d*sc)/16
+        const float d = half_bits_to_float(h.x & 0xffffu) * (ACT == HOLO_ACT_Q8 ? 0.0625f : 1.0f);
+        const float dmin = half_bits_to_float(h.x >> 16);
+        const uint32_t sc_lo = h.y & 0x3F3F3F3Fu, m_lo = h.z & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = ((h.w & LO4) << 2) | ((h.y >> 6) & 0x03030303u);
+        const uint32_t m_hi = (((h.w >> 4) & LO4) << 2) | ((h.z >> 6) & 0x03030303u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float sc = d * ubyte_to_float(j < 4 ? sc_lo : sc_hi, j & 3);
+            const float mn = dmin * ubyte_to_float(j < 4 ? m_lo : m_hi, j & 3);
+            const int blk = b0 + j;
+            if constexpr (ACT == HOLO_ACT_Q8) {
+                const uint4 a0 = lds128(aq + (size_t)blk * 32), a1 = lds128(aq + (size_t)blk * 32 + 16);
+                const float2 ds = ads[blk];
+                const float f16 = int_to_float_exact(dot_nib16_q8_x16(f.q[j], a0, a1));
+                acc += fmaf(sc, ds.x * f16, -mn * ds.y);
+            } else {
+                acc += fmaf(sc, dot_nib16_f32<true>(f.q[j], xs + (size_t)blk * 32), -mn * xsum[blk]);
             }
         }
     } else if constexpr (TYPE == GT_Q4_0) {
-        constexpr int BPW = TileGeom<GT_Q4_0>::BLKS_PER_WARP;
-        const uint8_t *dbase = tile + (size_t)nb * 512;
 #pragma unroll
-        for (int i = 0; i < BPW; i++) {
-            const int b = warp * BPW + i;
-            if (b >= nb) break;
-            const uint4 q = lds128(tile + (size_t)(b * TILE_ROWS + lane) * 16);
-            const float dw = half_bits_to_float(*reinterpret_cast<const uint16_t *>(dbase + (b * TILE_ROWS + lane) * 2));
-            const int gb = kc * TileGeom<GT_Q4_0>::BLKS_PER_TILE + b;
+        for (int j = 0; j < 8; ++j) {
+            const float dw = head_half(f.h, j);
+            const int blk = b0 + j;
             if constexpr (ACT == HOLO_ACT_Q8) {
-                const uint4 a0 = lds128(aq + (size_t)gb * 32), a1 = lds128(aq + (size_t)gb * 32 + 16);
-                const float2 ds = ads[gb];
-                const float f16 = int_to_float_exact(dot_nib16_q8_x16(q, a0, a1));
-                acc = fmaf(dw, fmaf(ds.x * 0.0625f, f16, -8.0f * ds.y), acc);
+                const uint4 a0 = lds128(aq + (size_t)blk * 32), a1 = lds128(aq + (size_t)blk * 32 + 16);
+                const float2 ds = ads[blk];
+                const float f16 = int_to_float_exact(dot_nib16_q8_x16(f.q[j], a0, a1));
+                acc += dw * fmaf(ds.x * 0.0625f, f16, -8.0f * ds.y);
             } else {
-                acc = fmaf(dw, dot_nib16_f32<true>(q, xs + (size_t)gb * 32) - 8.0f * xsum[gb], acc);
+                acc += dw * (dot_nib16_f32<true>(f.q[j], xs + (size_t)blk * 32) - 8.0f * xsum[blk]);
             }
         }
-    } else {  // Q8_0
-        constexpr int BPW = TileGeom<GT_Q8_0>::BLKS_PER_WARP;
-        const uint8_t *dbase = tile + (size_t)nb * 1024;
+    } else {  // Q8_0: block j = planes 2j, 2j+1
 #pragma unroll
-        for (int i = 0; i < BPW; i++) {
-            const int b = warp * BPW + i;
-            if (b >= nb) break;
-            const uint4 q0 = lds128(tile + (size_t)((b * 2 + 0) * TILE_ROWS + lane) * 16);
-            const uint4 q1 = lds128(tile + (size_t)((b * 2 + 1) * TILE_ROWS + lane) * 16);
-            const float dw = half_bits_to_float(*reinterpret_cast<const uint16_t *>(dbase + (b * TILE_ROWS + lane) * 2));
-            const int gb = kc * TileGeom<GT_Q8_0>::BLKS_PER_TILE + b;
+        for (int j = 0; j < 4; ++j) {
+            const float dw = head_half(f.h, j);
+            const int blk = b0 + j;
             if constexpr (ACT == HOLO_ACT_Q8) {
-                const uint4 a0 = lds128(aq + (size_t)gb * 32), a1 = lds128(aq + (size_t)gb * 32 + 16);
-                acc = fmaf(dw * ads[gb].x, int_to_float_exact(dot_i8x32_q8(q0, q1, a0, a1)), acc);
+                const uint4 a0 = lds128(aq + (size_t)blk * 32), a1 = lds128(aq + (size_t)blk * 32 + 16);
+                const int s = dot_i8x32_q8(f.q[2 * j], f.q[2 * j + 1], a0, a1);
+                acc += (dw * ads[blk].x) * int_to_float_exact(s);
             } else {
-                acc = fmaf(dw, dot_i8x32_f32<true>(q0, q1, xs + (size_t)gb * 32), acc);
+                acc += dw * dot_i8x32_f32<true>(f.q[2 * j], f.q[2 * j + 1], xs + (size_t)blk * 32);
             }
         }
     }
-    return acc;
 }
 
 // Final value of the 32 rows of row-block rb (v held by lane r = row r),
@@ -162,169 +233,227 @@ __device__ __forceinline__ void finish_rowblock(const MvParams &p, int rb, int l
     }
 }
 
-template <int TYPE, int ACT, int EPI, bool NORM>
-__global__ void __launch_bounds__(NTHREADS, 2) mv_tiled_kernel(const MvParams p) {
-    using G = TileGeom<TYPE>;
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int S = p.stages;
-    uint8_t *stages = smem;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * G::TILE_FULL);
-    uint64_t *empty = full + S;
-    float *red = reinterpret_cast<float *>(empty + S);               // [NCWARP][32]
-    uint8_t *act = reinterpret_cast<uint8_t *>(red + NCWARP * 32);     // 16-B aligned
-    // ACT_Q8: q8[in_dim] | (d, d*asum)[nblk32];  ACT_F32: xs[in_dim] | xsum[nblk32]
-    uint8_t *aq = act;
-    float2 *ads = reinterpret_cast<float2 *>(act + p.in_dim);
-    float *xs = reinterpret_cast<float *>(act);
-    float *xsum = xs + p.in_dim;
-
-    pdl_trigger();
-    const long long T = p.total_tiles, C = p.nctas;
-    const int t0 = tile_begin(blockIdx.x, T, C), t1 = tile_begin(blockIdx.x + 1, T, C);
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < S; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], NCWARP); }
-        fence_barrier_init();
-    }
-    __syncthreads();
-
-    if (warp == NCWARP) {
-        // ------------------------------ producer ------------------------------
-        if (lane == 0) {
-            const uint64_t pol = l2_policy_evict_first();
-            int issued = 0;
-            for (int t = t0; t < t1; ++t, ++issued) {
-                const int s = issued % S;
-                if (issued >= S && !mbar_wait_bounded(&empty[s], ((issued / S) - 1) & 1, p.status, HOLO_E_TIMEOUT))
-                    break;
-                const int rb = t / p.nkc, kc = t % p.nkc;
-                const int nb = min(G::BLKS_PER_TILE, p.blks_per_row - kc * G::BLKS_PER_TILE);
-                const uint32_t bytes = (uint32_t)(TILE_ROWS * nb * G::BLK_BYTES);
-                mbar_arrive_expect_tx(&full[s], bytes);
-                bulk_g2s(stages + (size_t)s * G::TILE_FULL, p.W + tile_base(rb, kc, p.row_bytes, G::TILE_FULL),
-                         bytes, &full[s], pol);
-            }
-            // never leave with copies in flight
-            for (int k = max(0, issued - S); k < issued; ++k)
-                mbar_wait_bounded(&full[k % S], (k / S) & 1, p.status, HOLO_E_TIMEOUT);
-        }
+// Row-block rb's sum over this CTA's units is v (lane r = row r): store it,
+// or -- when other CTAs hold part of the row-block -- publish it and let the
+// last contributor sum all parts in CTA order (stream-K fix-up).
+template <int EPI>
+__device__ __forceinline__ void complete_rowblock(const MvParams &p, int rb, int rb_first, int t0, int t1,
+                                                  unsigned T, unsigned C, int lane, float v) {
+    const unsigned tb = (unsigned)rb * p.units, te = tb + p.units - 1;
+    if ((int)tb >= t0 && (int)te < t1) {
+        finish_rowblock<EPI>(p, rb, lane, v);
         return;
     }
+    const int c_first = tile_owner(tb, T, C), c_last = tile_owner(te, T, C);
+    const int slot = (rb == rb_first) ? 0 : 1;
+    p.partials[((size_t)blockIdx.x * 2 + slot) * 32 + lane] = v;
+    __syncwarp();
+    int prev = 0;
+    if (lane == 0)
+        asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(&p.counters[rb]) : "memory");
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev == c_last - c_first) {
+        __syncwarp();   // lane 0's acquire orders the reads below
+        float tot = 0.0f;
+        for (int c = c_first; c <= c_last; ++c) {
+            const int sl = (rb == tile_begin(c, T, C) / p.units) ? 0 : 1;
+            tot += __ldcg(&p.partials[((size_t)c * 2 + sl) * 32 + lane]);
+        }
+        finish_rowblock<EPI>(p, rb, lane, tot);
+        if (lane == 0) p.counters[rb] = 0;
+    }
+}
 
-    // -------------------------------- consumers --------------------------------
-    pdl_wait();   // x, norm weights and residual come from earlier kernels
-    const int ctid = threadIdx.x;   // 0..255
+template <int TYPE, int ACT, int EPI, bool NORM>
+__global__ void __launch_bounds__(NTHREADS, MIN_CTAS_PER_SM) mv_tiled_kernel(const MvParams p) {
+    constexpr int BLKS32 = UnitGeom<TYPE>::BLKS32;
+    constexpr size_t UB = UnitGeom<TYPE>::UNIT_BYTES;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const MvSmem SL = mv_smem_layout(ACT, NORM, p.max_local_rb, p.nblk32p);
+    float *red = reinterpret_cast<float *>(smem + SL.red);
+    uint8_t *aq = smem + SL.act;
+    float2 *ads = reinterpret_cast<float2 *>(smem + SL.act + (size_t)p.nblk32p * 32);
+    float *xst = reinterpret_cast<float *>(smem + SL.stage);
+    float *xs = xst;                                            // ACT_F32 activation
+    float *xsum = xst + (size_t)p.nblk32p * 32;
+    float *nw = reinterpret_cast<float *>(smem + SL.nw);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + SL.misc);
+    float *wsum = reinterpret_cast<float *>(smem + SL.misc + 64);
+
+    pdl_trigger();
+    const unsigned T = p.total_units, C = p.nctas;
+    const int u0 = tile_begin(blockIdx.x, T, C), u1 = tile_begin(blockIdx.x + 1, T, C);
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_barrier_init();
+    }
+
+    // Warp w takes units u0+w, u0+w+NWARP, ... (the CTA's warps read NWARP
+    // consecutive units at a time).  Weights are constant, so before waiting
+    // for the kernel this one depends on, the first MV_L2_AHEAD units of every
+    // warp are prefetched into L2: HBM streams them while the previous kernel
+    // finishes, and nothing returns to this SM yet, so the activation copy
+    // below is not queued behind them.  In the loop, each warp keeps
+    // MV_L2_AHEAD units prefetched and MV_DEPTH units loading into registers.
+    // The activation (and norm weights, residual) go first: it is on the
+    // critical path after the wait, and a line the previous kernel is still
+    // writing is simply updated in L2.
+    if (threadIdx.x == 32 && p.bulk) {
+        prefetch_l2_bulk(p.x, (uint32_t)p.in_dim * 4u);
+        if constexpr (NORM) prefetch_l2_bulk(p.norm_w, (uint32_t)p.in_dim * 4u);
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < MV_L2_AHEAD; ++k) {
+            const int uu = u0 + warp + k * NWARP;
+            if (uu < u1) prefetch_l2_bulk(p.W + (size_t)uu * UB, (uint32_t)UB);
+        }
+    }
+    __syncthreads();   // barrier initialised
+
+    // ------------------------------ prologue ---------------------------------
+    // x (and the norm weights) land in shared memory through one bulk copy each
+    // -- one round trip, however long the vector -- then 8 threads per 32-value
+    // block normalise and quantize from there.
+    pdl_wait();   // x and residual come from earlier kernels
+    const int ctid = threadIdx.x;
+    const uint32_t xbytes = (uint32_t)p.in_dim * 4u;
+    if (p.bulk) {
+        if (ctid == 0) {
+            mbar_arrive_expect_tx(bar, NORM ? 2u * xbytes : xbytes);
+            bulk_copy_g2s(xst, p.x, xbytes, bar);
+            if constexpr (NORM) bulk_copy_g2s(nw, p.norm_w, xbytes, bar);
+        }
+    } else {
+        for (int i = ctid; i < p.in_dim; i += NTHREADS) {
+            xst[i] = __ldg(p.x + i);
+            if constexpr (NORM) nw[i] = __ldg(p.norm_w + i);
+        }
+    }
+    Frag ring[MV_DEPTH];
+#pragma unroll
+    for (int k = 0; k < MV_DEPTH; ++k) {
+        const int uu = u0 + warp + k * NWARP;
+        if (uu < u1) load_unit<TYPE>(ring[k], p.W + (size_t)uu * UB, lane);
+    }
+    for (int i = p.in_dim + ctid; i < p.nblk32p * 32; i += NTHREADS) {
+        xst[i] = 0.0f;
+        if constexpr (NORM) nw[i] = 0.0f;
+    }
+    const int rb_first = u0 / p.units;
+    const int n_local = (u1 - 1) / p.units - rb_first + 1;
+    for (int i = ctid; i < n_local * NWARP * 32; i += NTHREADS) red[i] = 0.0f;
+    bool ok = true;
+    if (p.bulk) ok = mbar_wait_bounded(bar, 0, p.status, HOLO_E_TIMEOUT);
+    if (!__syncthreads_and(ok)) return;
+
     float scale = 1.0f;
     if constexpr (NORM) {
         float ss = 0.0f;
-        for (int i = ctid * 4; i < p.in_dim; i += NCWARP * 32 * 4) {
-            const float4 v = __ldg(reinterpret_cast<const float4 *>(p.x + i));
+        for (int i = ctid * 4; i < p.in_dim; i += NTHREADS * 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(xst + i);
             ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss); ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) red[warp * 32] = ss;
-        named_bar_sync(BAR_CONSUMERS, NCWARP * 32);
+        if (lane == 0) wsum[warp] = ss;
+        __syncthreads();
         float tot = 0.0f;
 #pragma unroll
-        for (int w = 0; w < NCWARP; w++) tot += red[w * 32];
+        for (int w = 0; w < NWARP; w++) tot += wsum[w];
         scale = 1.0f / sqrtf(tot / (float)p.in_dim + p.eps);
     }
-    for (int b = ctid; b < p.nblk32; b += NCWARP * 32) {
-        float v[32];
-        const float4 *x4 = reinterpret_cast<const float4 *>(p.x + (size_t)b * 32);
+    {
+        // One thread per 32-value block (no shuffles): normalise it (NORM,
+        // written back), then ACT_Q8 finds amax, d = amax/127, id = 1/d and
+        // packs rint(x*id) clamped to [-127, 127] -- the arithmetic of
+        // quantize_vals_q8, with the clamp applied before rounding, which gives
+        // the same integers for every finite x*id -- and ACT_F32 takes the block
+        // sum.  Thread l reads the eight 16-byte chunks of its block starting at
+        // chunk (l + l/8) % 8, so every shared-memory wavefront hits distinct
+        // banks (loads: 8 lanes, word stores: 32 lanes).
+        for (int b = ctid; b < p.nblk32p; b += NTHREADS) {
+            float4 *xb = reinterpret_cast<float4 *>(xst + (size_t)b * 32);
+            const int rot = ctid + (ctid >> 3);
+            float amax = 0.0f, xsb = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            float4 t = __ldg(x4 + i);
-            v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
-        }
-        if constexpr (NORM) {
-            const float4 *w4 = reinterpret_cast<const float4 *>(p.norm_w + (size_t)b * 32);
+            for (int k = 0; k < 8; ++k) {
+                const int c = (k + rot) & 7;
+                float4 v = xb[c];
+                if constexpr (NORM) {
+                    const float4 w4 = reinterpret_cast<const float4 *>(nw + (size_t)b * 32)[c];
+                    v.x = (v.x * scale) * w4.x; v.y = (v.y * scale) * w4.y;
+                    v.z = (v.z * scale) * w4.z; v.w = (v.w * scale) * w4.w;
+                    xb[c] = v;
+                }
+                if constexpr (ACT == HOLO_ACT_Q8)
+                    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                else
+                    xsb += (v.x + v.y) + (v.z + v.w);
+            }
+            if constexpr (ACT == HOLO_ACT_Q8) {
+                const float d = __fdiv_rn(amax, 127.0f);
+                const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+                uint32_t *qb = reinterpret_cast<uint32_t *>(aq + (size_t)b * 32);
+                int sum = 0;
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                float4 t = __ldg(w4 + i);
-                v[4 * i] = (v[4 * i] * scale) * t.x;
-                v[4 * i + 1] = (v[4 * i + 1] * scale) * t.y;
-                v[4 * i + 2] = (v[4 * i + 2] * scale) * t.z;
-                v[4 * i + 3] = (v[4 * i + 3] * scale) * t.w;
+                for (int k = 0; k < 8; ++k) {
+                    const int c = (k + rot) & 7;
+                    const float4 v = xb[c];
+                    // |clamped value| <= 127: the low byte of v + 1.5*2^23 is the
+                    // two's-complement code
+                    const uint32_t b0 = __float_as_uint(__fadd_rn(fminf(fmaxf(__fmul_rn(v.x, id), -127.0f), 127.0f), 12582912.0f));
+                    const uint32_t b1 = __float_as_uint(__fadd_rn(fminf(fmaxf(__fmul_rn(v.y, id), -127.0f), 127.0f), 12582912.0f));
+                    const uint32_t b2 = __float_as_uint(__fadd_rn(fminf(fmaxf(__fmul_rn(v.z, id), -127.0f), 127.0f), 12582912.0f));
+                    const uint32_t b3 = __float_as_uint(__fadd_rn(fminf(fmaxf(__fmul_rn(v.w, id), -127.0f), 127.0f), 12582912.0f));
+                    const uint32_t word = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+                    qb[c] = word;
+                    sum = __dp4a((int)word, 0x01010101, sum);
+                }
+                ads[b] = make_float2(d, d * (float)sum);
+            } else {
+                xsum[b] = xsb;
             }
         }
-        if constexpr (ACT == HOLO_ACT_Q8) {
-            uint32_t w[8];
-            float d;
-            int asum;
-            quantize_vals_q8(v, w, d, asum);
-            uint4 *dst = reinterpret_cast<uint4 *>(aq + (size_t)b * 32);
-            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-            ads[b] = make_float2(d, d * (float)asum);
-        } else {
-            float4 *dst = reinterpret_cast<float4 *>(xs + (size_t)b * 32);
-            float s = 0.0f;
+        __syncthreads();
+    }
+
+    // ------------------------------- main loop --------------------------------
+    // The warp's running sum of one row-block is parked in red[row-block][warp]
+    // when the warp moves on to the next row-block (no barrier); one barrier at
+    // the end, then the row-blocks are reduced over the warps in warp order.
+    int rb = (u0 + warp) / p.units, s = u0 + warp - rb * p.units;   // unit (rb, s)
+    const int dq = NWARP / p.units, dr = NWARP - dq * p.units;      // step of NWARP units
+    int cur_rb = rb;
+    float acc = 0.0f;
+    for (int ub = u0 + warp; ub < u1; ub += MV_DEPTH * NWARP) {
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                s += (v[4 * i] + v[4 * i + 1]) + (v[4 * i + 2] + v[4 * i + 3]);
+        for (int k = 0; k < MV_DEPTH; ++k) {
+            const int u = ub + k * NWARP;
+            if (u >= u1) break;
+            if (rb != cur_rb) {
+                red[((cur_rb - rb_first) * NWARP + warp) * 32 + lane] = acc;
+                acc = 0.0f;
+                cur_rb = rb;
             }
-            xsum[b] = s;
+            unit_dot<TYPE, ACT>(acc, ring[k], s * BLKS32, aq, ads, xs, xsum);
+            const int un = u + MV_DEPTH * NWARP;
+            if (un < u1) load_unit<TYPE>(ring[k], p.W + (size_t)un * UB, lane);
+            const int up = u + MV_L2_AHEAD * NWARP;
+            if (lane == 0 && up < u1) prefetch_l2_bulk(p.W + (size_t)up * UB, (uint32_t)UB);
+            s += dr;
+            rb += dq;
+            if (s >= p.units) { s -= p.units; ++rb; }
         }
     }
-    named_bar_sync(BAR_CONSUMERS, NCWARP * 32);
-
-    float acc = 0.0f;
-    bool dead = false;
-    const int rb_first = t0 / p.nkc;
-    for (int t = t0, i = 0; t < t1; ++t, ++i) {
-        const int s = i % S;
-        const int rb = t / p.nkc, kc = t % p.nkc;
-        const int nb = min(G::BLKS_PER_TILE, p.blks_per_row - kc * G::BLKS_PER_TILE);
-        if (!dead) {
-            if (mbar_wait_bounded(&full[s], (i / S) & 1, p.status, HOLO_E_TIMEOUT)) {
-                acc += consume_tile<TYPE, ACT>(stages + (size_t)s * G::TILE_FULL, kc, nb, warp, lane, aq, ads, xs, xsum);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
-            } else {
-                dead = true;
-            }
-        }
-        if (kc == p.nkc - 1 || t == t1 - 1) {
-            // end of this CTA's share of row-block rb: combine the warps
-            red[warp * 32 + lane] = acc;
-            named_bar_sync(BAR_CONSUMERS, NCWARP * 32);
-            if (warp == 0 && !dead) {
-                float v = 0.0f;
+    if (u0 + warp < u1) red[((cur_rb - rb_first) * NWARP + warp) * 32 + lane] = acc;
+    __syncthreads();
+    for (int l = warp; l < n_local; l += NWARP) {
+        float v = 0.0f;
 #pragma unroll
-                for (int w = 0; w < NCWARP; w++) v += red[w * 32 + lane];
-                const long long tb = (long long)rb * p.nkc, te = tb + p.nkc - 1;
-                if (tb >= t0 && te < t1) {
-                    finish_rowblock<EPI>(p, rb, lane, v);
-                } else {
-                    // stream-K fix-up: publish my partial (release), count the
-                    // contributors; the last one sums all partials in CTA order
-                    const int c_first = tile_owner(tb, T, C), c_last = tile_owner(te, T, C);
-                    const int slot = (rb == rb_first) ? 0 : 1;
-                    p.partials[((size_t)blockIdx.x * 2 + slot) * 32 + lane] = v;
-                    __syncwarp();
-                    int prev = 0;
-                    if (lane == 0)
-                        asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(&p.counters[rb]) : "memory");
-                    prev = __shfl_sync(0xffffffffu, prev, 0);
-                    if (prev == c_last - c_first) {
-                        __threadfence();
-                        float tot = 0.0f;
-                        for (int c = c_first; c <= c_last; ++c) {
-                            const int sl = (rb == tile_begin(c, T, C) / p.nkc) ? 0 : 1;
-                            tot += __ldcg(&p.partials[((size_t)c * 2 + sl) * 32 + lane]);
-                        }
-                        finish_rowblock<EPI>(p, rb, lane, tot);
-                        if (lane == 0) p.counters[rb] = 0;
-                    }
-                }
-            }
-            named_bar_sync(BAR_CONSUMERS, NCWARP * 32);
-            acc = 0.0f;
-        }
+        for (int w = 0; w < NWARP; w++) v += red[(l * NWARP + w) * 32 + lane];
+        complete_rowblock<EPI>(p, rb_first + l, rb_first, u0, u1, T, C, lane, v);
     }
 }
 
@@ -333,50 +462,53 @@ __global__ void __launch_bounds__(NTHREADS, 2) mv_tiled_kernel(const MvParams p)
 // ---------------------------------------------------------------------------
 template <int TYPE, int ACT, int EPI, bool NORM>
 bool launch_tiled(const MvParams &base, int sms, bool pdl, cudaStream_t st) {
-    using G = TileGeom<TYPE>;
     MvParams p = base;
-    size_t act_bytes = (ACT == HOLO_ACT_Q8) ? (size_t)p.in_dim + 8 * (size_t)p.nblk32
-                                             : 4 * (size_t)p.in_dim + 4 * (size_t)p.nblk32;
-    act_bytes = (act_bytes + 15) & ~(size_t)15;
-    const size_t fixed = NCWARP * 32 * 4 + act_bytes;
-    const size_t per_stage = G::TILE_FULL + 16;
-    // two CTAs per SM when at least 3 stages fit in half of the SM's shared
-    // memory, else one CTA with up to 8 stages
-    const size_t half_budget = 113 * 1024, full_budget = 227 * 1024;
-    int per_sm = 2, stages = (int)((half_budget - fixed) / per_stage);
-    if (fixed >= half_budget || stages < 3) {
-        per_sm = 1;
-        stages = fixed >= full_budget ? 0 : (int)((full_budget - fixed) / per_stage);
-    }
-    stages = min(stages, 8);
-    if (stages < 2) {
-        holo_set_status(HOLO_E_UNSUPPORTED, "tiled matvec: in_dim too large for shared memory");
+    if ((unsigned long long)p.total_units * (unsigned long long)MV_MAX_CTAS >= (1ull << 32)) {
+        holo_set_status(HOLO_E_UNSUPPORTED, "tiled matvec: too many units");
         return false;
     }
-    p.stages = stages;
-    const size_t smem = (size_t)stages * per_stage + fixed;
+    // One CTA per SM; more (in further waves) only when a CTA's share of the
+    // row-blocks would not fit its reduction buffer.
+    size_t smem = 0;
+    p.nctas = min(p.total_units, sms);
+    for (;;) {
+        const int per_cta = (p.total_units + p.nctas - 1) / p.nctas;
+        p.max_local_rb = (p.units + per_cta - 2) / p.units + 1;
+        smem = mv_smem_layout(ACT, NORM, p.max_local_rb, p.nblk32p).total;
+        if (smem <= SMEM_LIMIT) break;
+        if (p.nctas >= min(p.total_units, MV_MAX_CTAS) || mv_smem_layout(ACT, NORM, 2, p.nblk32p).total > SMEM_LIMIT) {
+            holo_set_status(HOLO_E_UNSUPPORTED, "tiled matvec: in_dim too large for shared memory");
+            return false;
+        }
+        p.nctas = min(min(p.total_units, MV_MAX_CTAS), p.nctas + sms);
+    }
     auto kern = mv_tiled_kernel<TYPE, ACT, EPI, NORM>;
     static bool configured[16] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 16 && !configured[dev]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)full_budget) != cudaSuccess) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_LIMIT) != cudaSuccess ||
+            cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
             holo_check_launch("tiled matvec: smem attribute");
             return false;
         }
         configured[dev] = true;
     }
-    p.nctas = min(p.total_tiles, min(per_sm * sms, MV_MAX_CTAS));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.nctas);
     cfg.blockDim = dim3(NTHREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = na;
     if (cudaLaunchKernelEx(&cfg, kern, p) != cudaSuccess) return holo_check_launch("tiled matvec launch");
     return holo_check_launch("tiled matvec launch");
 }
@@ -417,11 +549,13 @@ bool holo_matvec_launch(const void *M, const WeightInfo &wi, const MvLaunch &L, 
     p.out_dim = wi.rows;
     p.in_dim = wi.cols;
     p.nblk32 = wi.cols / 32;
-    p.row_bytes = (size_t)gguf_row_bytes(wi.type, wi.cols);
+    p.units = wi.units;
     p.nrb = wi.rows_padded / TILE_ROWS;
+    p.total_units = p.nrb * p.units;
     p.partials = L.partials ? L.partials : D->mv_partials;
     p.counters = L.counters ? L.counters : D->mv_counters;
     p.status = D->status;
+    p.bulk = ((uintptr_t)L.x % 16 == 0) && ((uintptr_t)L.norm_w % 16 == 0);
     if (p.nrb > MV_MAX_ROWBLOCKS) {
         holo_set_status(HOLO_E_UNSUPPORTED, "matvec: too many rows");
         return false;
@@ -433,19 +567,13 @@ bool holo_matvec_launch(const void *M, const WeightInfo &wi, const MvLaunch &L, 
     const bool norm = L.norm_w != nullptr;
     switch (wi.type) {
     case GT_Q8_0:
-        p.blks_per_row = wi.cols / 32;
-        p.nkc = (p.blks_per_row + TileGeom<GT_Q8_0>::BLKS_PER_TILE - 1) / TileGeom<GT_Q8_0>::BLKS_PER_TILE;
-        p.total_tiles = p.nrb * p.nkc;
+        p.nblk32p = p.units * UnitGeom<GT_Q8_0>::BLKS32;
         return dispatch_act<GT_Q8_0>(p, L.act, L.epi, norm, D->sms, L.pdl, st);
     case GT_Q4_0:
-        p.blks_per_row = wi.cols / 32;
-        p.nkc = (p.blks_per_row + TileGeom<GT_Q4_0>::BLKS_PER_TILE - 1) / TileGeom<GT_Q4_0>::BLKS_PER_TILE;
-        p.total_tiles = p.nrb * p.nkc;
+        p.nblk32p = p.units * UnitGeom<GT_Q4_0>::BLKS32;
         return dispatch_act<GT_Q4_0>(p, L.act, L.epi, norm, D->sms, L.pdl, st);
     case GT_Q4_K:
-        p.blks_per_row = wi.cols / 256;
-        p.nkc = (p.blks_per_row + TileGeom<GT_Q4_K>::BLKS_PER_TILE - 1) / TileGeom<GT_Q4_K>::BLKS_PER_TILE;
-        p.total_tiles = p.nrb * p.nkc;
+        p.nblk32p = p.units * UnitGeom<GT_Q4_K>::BLKS32;
         return dispatch_act<GT_Q4_K>(p, L.act, L.epi, norm, D->sms, L.pdl, st);
     default:
         holo_set_status(HOLO_E_ARG, "matvec: type has no tiled kernel");

@@ -62,6 +62,7 @@ struct BlockRef {
     const uint8_t *W;
     bool tiled;
     int nblk32;            // 32-blocks per row
+    int units;             // tiled: units per row
     size_t row_bytes;
     int ggml;              // raw Q4_K semantics
 };
@@ -71,13 +72,11 @@ __device__ __forceinline__ void load_block(const BlockRef &R, int r, int b, uint
                                            Q4KHead *kh) {
     if constexpr (TYPE == GT_Q8_0) {
         if (R.tiled) {
-            using G = TileGeom<GT_Q8_0>;
-            int rb = r / TILE_ROWS, lr = r % TILE_ROWS, kc = b / G::BLKS_PER_TILE, bi = b % G::BLKS_PER_TILE;
-            int nb = min(G::BLKS_PER_TILE, R.nblk32 - kc * G::BLKS_PER_TILE);
-            const uint8_t *t = R.W + tile_base(rb, kc, R.row_bytes, G::TILE_FULL);
-            q0 = *reinterpret_cast<const uint4 *>(t + ((size_t)(bi * 2) * TILE_ROWS + lr) * 16);
-            q1 = *reinterpret_cast<const uint4 *>(t + ((size_t)(bi * 2 + 1) * TILE_ROWS + lr) * 16);
-            d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(t + (size_t)nb * 1024 + ((size_t)bi * TILE_ROWS + lr) * 2));
+            const uint8_t *u = unit_ptr<GT_Q8_0>(R.W, R.units, r, b / 4);
+            const int lr = r % TILE_ROWS, bi = b % 4;
+            q0 = *reinterpret_cast<const uint4 *>(u + unit_plane_off<GT_Q8_0>(bi * 2, lr));
+            q1 = *reinterpret_cast<const uint4 *>(u + unit_plane_off<GT_Q8_0>(bi * 2 + 1, lr));
+            d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(u + unit_head_off<GT_Q8_0>(lr) + 2 * bi));
         } else {
             const uint8_t *blk = R.W + (size_t)r * R.row_bytes + (size_t)b * 34;
             d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(blk));
@@ -86,12 +85,10 @@ __device__ __forceinline__ void load_block(const BlockRef &R, int r, int b, uint
         }
     } else if constexpr (TYPE == GT_Q4_0) {
         if (R.tiled) {
-            using G = TileGeom<GT_Q4_0>;
-            int rb = r / TILE_ROWS, lr = r % TILE_ROWS, kc = b / G::BLKS_PER_TILE, bi = b % G::BLKS_PER_TILE;
-            int nb = min(G::BLKS_PER_TILE, R.nblk32 - kc * G::BLKS_PER_TILE);
-            const uint8_t *t = R.W + tile_base(rb, kc, R.row_bytes, G::TILE_FULL);
-            q0 = *reinterpret_cast<const uint4 *>(t + ((size_t)bi * TILE_ROWS + lr) * 16);
-            d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(t + (size_t)nb * 512 + ((size_t)bi * TILE_ROWS + lr) * 2));
+            const uint8_t *u = unit_ptr<GT_Q4_0>(R.W, R.units, r, b / 8);
+            const int lr = r % TILE_ROWS, bi = b % 8;
+            q0 = *reinterpret_cast<const uint4 *>(u + unit_plane_off<GT_Q4_0>(bi, lr));
+            d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(u + unit_head_off<GT_Q4_0>(lr) + 2 * bi));
         } else {
             const uint8_t *blk = R.W + (size_t)r * R.row_bytes + (size_t)b * 18;
             d = half_bits_to_float(*reinterpret_cast<const uint16_t *>(blk));
@@ -99,15 +96,16 @@ __device__ __forceinline__ void load_block(const BlockRef &R, int r, int b, uint
         }
     } else {  // Q4_K: b is the 32-block index, sub-block j = b % 8
         int s = b >> 3, j = b & 7;
-        const uint8_t *blk;
         if (R.tiled) {
-            using G = TileGeom<GT_Q4_K>;
-            int rb = r / TILE_ROWS, lr = r % TILE_ROWS, kc = s / G::BLKS_PER_TILE, si = s % G::BLKS_PER_TILE;
-            blk = R.W + tile_base(rb, kc, R.row_bytes, G::TILE_FULL) + ((size_t)si * TILE_ROWS + lr) * 144;
-        } else {
-            blk = R.W + (size_t)r * R.row_bytes + (size_t)s * 144;
+            const uint8_t *u = unit_ptr<GT_Q4_K>(R.W, R.units, r, s);
+            const int lr = r % TILE_ROWS;
+            *kh = q4k_head(*reinterpret_cast<const uint4 *>(u + unit_head_off<GT_Q4_K>(lr)));
+            q0 = *reinterpret_cast<const uint4 *>(u + unit_plane_off<GT_Q4_K>(j, lr));
+            d = 0.0f;
+            return;
         }
-        if (!R.tiled && R.ggml) {
+        const uint8_t *blk = R.W + (size_t)r * R.row_bytes + (size_t)s * 144;
+        if (R.ggml) {
             *kh = q4k_head(q4k_ggml_head(blk));
             q0 = q4k_ggml_sub(blk + 16, j);
         } else {
@@ -318,6 +316,7 @@ BlockRef make_ref(const void *M, int type, int cols, bool tiled, int ggml) {
     R.tiled = tiled;
     R.nblk32 = cols / 32;
     R.row_bytes = (size_t)gguf_row_bytes(type, cols);
+    R.units = units_per_row(type, cols);
     R.ggml = ggml;
     return R;
 }

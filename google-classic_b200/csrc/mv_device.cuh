@@ -184,9 +184,34 @@ __device__ __forceinline__ float q4k_min(const Q4KHead &h, int j) {
 }
 
 // ---------------------------------------------------------------------------
-// Tiled-layout addressing (holo_common.cuh).  `nb` is the block count of the
-// tile (smaller for the last K-chunk).
+// RoPE angle of pair i at position pos (src/ai/llm.c:1139-1142):
+//   freq = 1 / base^((2i)/hd), theta = pos * freq, in float32.
+// pow, cos and sin are evaluated in double and rounded once to float, so the
+// float32 values are the correctly rounded ones (what a correctly rounded
+// libm returns); the float operations around them round as in the C code.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ size_t tile_base(int rb, int kc, size_t row_bytes, int tile_full) {
-    return (size_t)rb * TILE_ROWS * row_bytes + (size_t)kc * tile_full;
+__device__ __forceinline__ void rope_cos_sin(int pos, int i, int hd, float base, float &c, float &s) {
+    const float ex = __fdiv_rn((float)(2 * i), (float)hd);
+    const float pw = (float)pow((double)base, (double)ex);
+    const float freq = __fdiv_rn(1.0f, pw);
+    const float theta = __fmul_rn((float)pos, freq);
+    double sd, cd;
+    sincos((double)theta, &sd, &cd);
+    c = (float)cd;
+    s = (float)sd;
+}
+// (a, b) <- (a*c - b*s, a*s + b*c), each product and sum rounded separately
+__device__ __forceinline__ void rope_rotate(float &a, float &b, float c, float s) {
+    const float a0 = a, b0 = b;
+    a = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(b0, s));
+    b = __fadd_rn(__fmul_rn(a0, s), __fmul_rn(b0, c));
+}
+
+// ---------------------------------------------------------------------------
+// Tiled-layout addressing (holo_common.cuh): the unit holding row r and
+// position block b (32-value block for Q8_0/Q4_0, super-block for Q4_K).
+// ---------------------------------------------------------------------------
+template <int TYPE>
+__device__ __forceinline__ const uint8_t *unit_ptr(const uint8_t *W, int units, int r, int s) {
+    return W + ((size_t)(r / TILE_ROWS) * units + s) * UnitGeom<TYPE>::UNIT_BYTES;
 }

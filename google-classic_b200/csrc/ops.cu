@@ -224,20 +224,15 @@ __global__ void att_apply_kernel(float *dst, const float *S, const float *V, int
 __global__ void rope_kernel(float *q, float *k, int pos, int hd, int n_heads, int n_kv_heads, float base) {
     const int h = blockIdx.x, i = threadIdx.x, half = hd / 2;
     if (i >= half) return;
-    const float freq = 1.0f / powf(base, (float)(2 * i) / (float)hd);
-    const float theta = (float)pos * freq;
-    const float c = cosf(theta), s = sinf(theta);
+    float c, s;
+    rope_cos_sin(pos, i, hd, base, c, s);
     if (h < n_heads) {
         float *qh = q + (size_t)h * hd;
-        float a = qh[i], b = qh[i + half];
-        qh[i] = a * c - b * s;
-        qh[i + half] = a * s + b * c;
+        rope_rotate(qh[i], qh[i + half], c, s);
     }
     if (h < n_kv_heads) {
         float *kh = k + (size_t)h * hd;
-        float a = kh[i], b = kh[i + half];
-        kh[i] = a * c - b * s;
-        kh[i + half] = a * s + b * c;
+        rope_rotate(kh[i], kh[i + half], c, s);
     }
 }
 

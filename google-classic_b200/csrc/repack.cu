@@ -7,45 +7,35 @@
 
 namespace {
 
-__device__ __forceinline__ size_t tile_offset(int rb, int kc, size_t row_bytes, int tile_full) {
-    return (size_t)rb * TILE_ROWS * row_bytes + (size_t)kc * tile_full;
-}
-
-// Q8_0: one thread per (row, block).
+// Q8_0: one thread per (row, 32-block); padding blocks stay zero.
 __global__ void repack_q8_0_kernel(uint8_t *__restrict__ out, const uint8_t *__restrict__ in,
-                                   int rows, int nblk) {
-    using G = TileGeom<GT_Q8_0>;
+                                   int rows, int nblk, int units) {
+    using G = UnitGeom<GT_Q8_0>;
     int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (int64_t)rows * nblk) return;
     int r = (int)(gid / nblk), b = (int)(gid % nblk);
-    size_t row_bytes = (size_t)nblk * G::BLK_BYTES;
-    const uint8_t *src = in + (size_t)r * row_bytes + (size_t)b * G::BLK_BYTES;
-    int rb = r / TILE_ROWS, lr = r % TILE_ROWS;
-    int kc = b / G::BLKS_PER_TILE, bi = b % G::BLKS_PER_TILE;
-    int nb = min(G::BLKS_PER_TILE, nblk - kc * G::BLKS_PER_TILE);
-    uint8_t *tile = out + tile_offset(rb, kc, row_bytes, G::TILE_FULL);
-    uint8_t *q0 = tile + ((size_t)(bi * 2 + 0) * TILE_ROWS + lr) * 16;
-    uint8_t *q1 = tile + ((size_t)(bi * 2 + 1) * TILE_ROWS + lr) * 16;
+    const uint8_t *src = in + (size_t)r * nblk * G::BLK_BYTES + (size_t)b * G::BLK_BYTES;
+    int lr = r % TILE_ROWS, s = b / G::BLKS32, bi = b % G::BLKS32;
+    uint8_t *unit = out + ((size_t)(r / TILE_ROWS) * units + s) * G::UNIT_BYTES;
+    uint8_t *q0 = unit + unit_plane_off<GT_Q8_0>(bi * 2, lr);
+    uint8_t *q1 = unit + unit_plane_off<GT_Q8_0>(bi * 2 + 1, lr);
     for (int i = 0; i < 16; i++) { q0[i] = src[2 + i]; q1[i] = src[18 + i]; }
-    uint8_t *dd = tile + (size_t)nb * 1024 + ((size_t)bi * TILE_ROWS + lr) * 2;
+    uint8_t *dd = unit + unit_head_off<GT_Q8_0>(lr) + 2 * bi;
     dd[0] = src[0]; dd[1] = src[1];
 }
 
 __global__ void repack_q4_0_kernel(uint8_t *__restrict__ out, const uint8_t *__restrict__ in,
-                                   int rows, int nblk) {
-    using G = TileGeom<GT_Q4_0>;
+                                   int rows, int nblk, int units) {
+    using G = UnitGeom<GT_Q4_0>;
     int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (int64_t)rows * nblk) return;
     int r = (int)(gid / nblk), b = (int)(gid % nblk);
-    size_t row_bytes = (size_t)nblk * G::BLK_BYTES;
-    const uint8_t *src = in + (size_t)r * row_bytes + (size_t)b * G::BLK_BYTES;
-    int rb = r / TILE_ROWS, lr = r % TILE_ROWS;
-    int kc = b / G::BLKS_PER_TILE, bi = b % G::BLKS_PER_TILE;
-    int nb = min(G::BLKS_PER_TILE, nblk - kc * G::BLKS_PER_TILE);
-    uint8_t *tile = out + tile_offset(rb, kc, row_bytes, G::TILE_FULL);
-    uint8_t *q = tile + ((size_t)bi * TILE_ROWS + lr) * 16;
+    const uint8_t *src = in + (size_t)r * nblk * G::BLK_BYTES + (size_t)b * G::BLK_BYTES;
+    int lr = r % TILE_ROWS, s = b / G::BLKS32, bi = b % G::BLKS32;
+    uint8_t *unit = out + ((size_t)(r / TILE_ROWS) * units + s) * G::UNIT_BYTES;
+    uint8_t *q = unit + unit_plane_off<GT_Q4_0>(bi, lr);
     for (int i = 0; i < 16; i++) q[i] = src[2 + i];
-    uint8_t *dd = tile + (size_t)nb * 512 + ((size_t)bi * TILE_ROWS + lr) * 2;
+    uint8_t *dd = unit + unit_head_off<GT_Q4_0>(lr) + 2 * bi;
     dd[0] = src[0]; dd[1] = src[1];
 }
 
@@ -55,17 +45,18 @@ __global__ void repack_q4_0_kernel(uint8_t *__restrict__ out, const uint8_t *__r
 //   nibbles: 32 B per 64 values (cuda_ops.cu:712-729) -> 16 B per 32 values
 __global__ void repack_q4_k_kernel(uint8_t *__restrict__ out, const uint8_t *__restrict__ in,
                                    int rows, int nsb, int ggml) {
-    using G = TileGeom<GT_Q4_K>;
+    using G = UnitGeom<GT_Q4_K>;
     int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (int64_t)rows * nsb) return;
     int r = (int)(gid / nsb), s = (int)(gid % nsb);
-    size_t row_bytes = (size_t)nsb * G::BLK_BYTES;
-    const uint8_t *src = in + (size_t)r * row_bytes + (size_t)s * G::BLK_BYTES;
-    int rb = r / TILE_ROWS, lr = r % TILE_ROWS;
-    int kc = s / G::BLKS_PER_TILE, si = s % G::BLKS_PER_TILE;
-    uint8_t *dst = out + tile_offset(rb, kc, row_bytes, G::TILE_FULL) + ((size_t)si * TILE_ROWS + lr) * 144;
+    const uint8_t *src = in + (size_t)r * nsb * G::BLK_BYTES + (size_t)s * G::BLK_BYTES;
+    int lr = r % TILE_ROWS;
+    uint8_t *unit = out + ((size_t)(r / TILE_ROWS) * nsb + s) * G::UNIT_BYTES;
+    uint8_t *head = unit + unit_head_off<GT_Q4_K>(lr);
     if (!ggml) {
-        for (int i = 0; i < 144; i++) dst[i] = src[i];
+        for (int i = 0; i < 16; i++) head[i] = src[i];
+        for (int j = 0; j < 8; j++)
+            for (int l = 0; l < 16; l++) unit[unit_plane_off<GT_Q4_K>(j, lr) + l] = src[16 + j * 16 + l];
         return;
     }
     uint8_t sc[8], mn[8];
@@ -77,11 +68,11 @@ __global__ void repack_q4_k_kernel(uint8_t *__restrict__ out, const uint8_t *__r
             mn[j] = (uint8_t)((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
         }
     }
-    for (int i = 0; i < 4; i++) dst[i] = src[i];
+    for (int i = 0; i < 4; i++) head[i] = src[i];
     for (int j = 0; j < 4; j++) {
-        dst[4 + j] = (uint8_t)(sc[j] | ((sc[j + 4] & 3) << 6));
-        dst[8 + j] = (uint8_t)(mn[j] | ((mn[j + 4] & 3) << 6));
-        dst[12 + j] = (uint8_t)((sc[j + 4] >> 2) | ((mn[j + 4] >> 2) << 4));
+        head[4 + j] = (uint8_t)(sc[j] | ((sc[j + 4] & 3) << 6));
+        head[8 + j] = (uint8_t)(mn[j] | ((mn[j + 4] & 3) << 6));
+        head[12 + j] = (uint8_t)((sc[j + 4] >> 2) | ((mn[j + 4] >> 2) << 4));
     }
     // value v of sub-block j, position l (0..31): ggml group g = j/2 holds it in
     // byte qs[g*32 + l], low nibble for even j, high nibble for odd j.
@@ -92,7 +83,7 @@ __global__ void repack_q4_k_kernel(uint8_t *__restrict__ out, const uint8_t *__r
             uint8_t a = qs[g * 32 + l], b = qs[g * 32 + l + 16];
             uint8_t na = hi ? (a >> 4) : (a & 0x0f);
             uint8_t nb = hi ? (b >> 4) : (b & 0x0f);
-            dst[16 + j * 16 + l] = (uint8_t)(na | (nb << 4));
+            unit[unit_plane_off<GT_Q4_K>(j, lr) + l] = (uint8_t)(na | (nb << 4));
         }
     }
 }
@@ -108,8 +99,8 @@ bool check_shape(int type, int rows, int cols) {
 
 extern "C" size_t cuda_quant_tiled_bytes(int ggml_type, int rows, int cols) {
     if (!check_shape(ggml_type, rows, cols)) return 0;
-    int rp = (rows + TILE_ROWS - 1) / TILE_ROWS * TILE_ROWS;
-    return (size_t)rp * (size_t)gguf_row_bytes(ggml_type, cols);
+    size_t nrb = (size_t)(rows + TILE_ROWS - 1) / TILE_ROWS;
+    return nrb * (size_t)units_per_row(ggml_type, cols) * (size_t)unit_bytes(ggml_type);
 }
 
 extern "C" void *cuda_repack_quant(const void *dev_blocks, int ggml_type, int rows, int cols) {
@@ -127,19 +118,20 @@ extern "C" void *cuda_repack_quant(const void *dev_blocks, int ggml_type, int ro
         holo_set_status(HOLO_E_NOMEM, "cuda_repack_quant: allocation");
         return nullptr;
     }
-    cudaMemsetAsync(out, 0, bytes, st);   // padding rows are zero
+    cudaMemsetAsync(out, 0, bytes, st);   // padding rows and blocks are zero
     int layout = holo_q4k_layout();
+    const int units = units_per_row(ggml_type, cols);
     const int threads = 256;
     if (ggml_type == GT_Q8_0) {
         int nblk = cols / 32;
         int64_t n = (int64_t)rows * nblk;
         repack_q8_0_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
-            (uint8_t *)out, (const uint8_t *)dev_blocks, rows, nblk);
+            (uint8_t *)out, (const uint8_t *)dev_blocks, rows, nblk, units);
     } else if (ggml_type == GT_Q4_0) {
         int nblk = cols / 32;
         int64_t n = (int64_t)rows * nblk;
         repack_q4_0_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
-            (uint8_t *)out, (const uint8_t *)dev_blocks, rows, nblk);
+            (uint8_t *)out, (const uint8_t *)dev_blocks, rows, nblk, units);
     } else {
         int nsb = cols / 256;
         int64_t n = (int64_t)rows * nsb;
@@ -152,6 +144,7 @@ extern "C" void *cuda_repack_quant(const void *dev_blocks, int ggml_type, int ro
     wi.rows = rows;
     wi.cols = cols;
     wi.rows_padded = (rows + TILE_ROWS - 1) / TILE_ROWS * TILE_ROWS;
+    wi.units = units;
     wi.q4k_layout = layout;
     wi.bytes = bytes;
     holo_registry_add(out, wi);

@@ -120,7 +120,15 @@ class Reference:
         lib.href_sample.restype = _i
         lib.href_sample.argtypes = [_vp, _f, _f, _i, _f, _i]
         lib.href_model_free.argtypes = [_vp]
+        lib.rope_apply.argtypes = [_vp, _vp, _i, _i, _i, _f]
         self.lib = lib
+
+    def rope(self, v, pos, head_dim, n_heads, base):
+        """src/ai/tensor.c:347-373 applied to one tensor of n_heads heads."""
+        a = np.ascontiguousarray(v, np.float32).copy()
+        b = np.zeros_like(a)
+        self.lib.rope_apply(_ptr(a), _ptr(b), pos, head_dim, n_heads, base)
+        return a
 
     def matmul_q(self, gtype, blocks, x, rows, cols, threads=1):
         blocks = np.ascontiguousarray(blocks)

@@ -56,6 +56,22 @@ def test_tiled_matvec_parity(dev, oracle, reference, gtype, rows, cols):
     dev.free(Wd)
 
 
+@pytest.mark.parametrize("gtype", [hb.Q8_0, hb.Q4_0])
+@pytest.mark.parametrize("rows,cols", [(45, 96), (70, 1440), (33, 4128), (5, 32)])
+def test_padded_last_unit_parity(dev, oracle, reference, gtype, rows, cols):
+    """Rows whose 32-block count is not a multiple of the unit's (4 blocks for
+    Q8_0, 8 for Q4_0): the tiled copy pads the last unit with zero blocks."""
+    seed = 7 * rows + cols + gtype
+    W = synth.quant_matrix(gtype, rows, cols, seed)
+    x = synth.activation(cols, seed)
+    Wd = dev.upload_quant(W, gtype, rows, cols)
+    y32 = run_matvec(dev, Wd, gtype, x, rows, cols, hb.ACT_F32)
+    assert rel_err(y32, reference.matmul_q(gtype, W, x, rows, cols)) <= TOL
+    y8 = run_matvec(dev, Wd, gtype, x, rows, cols, hb.ACT_Q8)
+    assert rel_err(y8, oracle.matvec_q8(gtype, W, x, rows, cols)) <= TOL
+    dev.free(Wd)
+
+
 @pytest.mark.parametrize("gtype", TYPES)
 def test_raw_blocks_path_parity(dev, oracle, reference, gtype):
     """Weights uploaded as the reference's upload_tensor does (cuda_malloc +
@@ -81,7 +97,7 @@ def test_raw_blocks_path_parity(dev, oracle, reference, gtype):
 @pytest.mark.parametrize("gtype", TYPES)
 @pytest.mark.parametrize("tiled", [True, False])
 def test_dequantized_values_bit_exact(dev, reference, gtype, tiled):
-    rows, cols = 45, 2304
+    rows, cols = 45, (2304 if gtype == hb.Q4_K else 2336)   # 73 blocks: a padded last unit
     W = synth.quant_matrix(gtype, rows, cols, 21)
     Wd = dev.upload_quant(W, gtype, rows, cols) if tiled else dev.upload(W)
     od = dev.alloc(rows * cols * 4)
@@ -96,7 +112,7 @@ def test_dequantized_values_bit_exact(dev, reference, gtype, tiled):
 @pytest.mark.parametrize("gtype", TYPES)
 @pytest.mark.parametrize("tiled", [True, False])
 def test_block_integer_sums_bit_exact(dev, oracle, gtype, tiled):
-    rows, cols = 70, 4096
+    rows, cols = 70, (4096 if gtype == hb.Q4_K else 4128)
     W = synth.quant_matrix(gtype, rows, cols, 31)
     x = synth.activation(cols, 31)
     Wd = dev.upload_quant(W, gtype, rows, cols) if tiled else dev.upload(W)
@@ -267,7 +283,7 @@ def test_dependent_chain_with_pdl_and_graph(dev, oracle):
 def test_unsupported_shape_sets_status_not_fault(dev):
     """A K extent beyond the tiled kernel's shared memory is refused on the
     host with HOLO_E_UNSUPPORTED; the context stays usable."""
-    rows, cols = 32, 256 * 640
+    rows, cols = 32, 256 * 1024
     W = np.zeros(rows * hb.row_bytes(hb.Q4_K, cols), np.uint8)
     Wd = dev.upload_quant(W, hb.Q4_K, rows, cols)
     xd, yd = dev.upload(np.zeros(cols, np.float32)), dev.alloc(rows * 4)

@@ -79,10 +79,13 @@ def rope_ref(v, pos, hd, base):
     v = v.astype(np.float64).reshape(-1, hd).copy()
     half = hd // 2
     i = np.arange(half)
-    # the reference computes freq and theta in float32 (src/ai/llm.c:1139-1141)
-    freq = (np.float32(1.0) / np.power(np.float32(base), (2 * i).astype(np.float32) / np.float32(hd))).astype(np.float32)
+    # float32 angle as in src/ai/llm.c:1139-1141, with a correctly rounded pow,
+    # cos and sin (fp64 rounded once to float32)
+    ex = (2 * i).astype(np.float32) / np.float32(hd)
+    pw = np.power(np.float64(base), ex.astype(np.float64)).astype(np.float32)
+    freq = (np.float32(1.0) / pw).astype(np.float32)
     th = (np.float32(pos) * freq).astype(np.float32).astype(np.float64)
-    c, s = np.cos(th), np.sin(th)
+    c, s = np.cos(th).astype(np.float32).astype(np.float64), np.sin(th).astype(np.float32).astype(np.float64)
     a, b = v[:, :half].copy(), v[:, half:].copy()
     v[:, :half] = a * c - b * s
     v[:, half:] = a * s + b * c
@@ -90,13 +93,19 @@ def rope_ref(v, pos, hd, base):
 
 
 @pytest.mark.parametrize("pos,base", [(0, 10000.0), (17, 10000.0), (2047, 10000.0), (4000, 500000.0)])
-def test_rope(dev, pos, base):
+def test_rope(dev, reference, pos, base):
+    """Against the reference's own rope_apply (src/ai/tensor.c:347, glibc libm).
+    The angle is pos * freq in float32, so a one-ulp difference of powf between
+    two libms moves it by up to pos * ulp(freq): the bound grows with pos."""
     hd, nh, nkv = 128, 32, 8
     q, k = synth.activation(nh * hd, 8), synth.activation(nkv * hd, 9)
     qd, kd = up(dev, q), up(dev, k)
     dev.lib.cuda_rope_apply(qd, kd, pos, hd, nh, nkv, np.float32(base))
-    assert np.abs(dev.download(qd, (nh * hd,), np.float32) - rope_ref(q, pos, hd, base)).max() <= 2e-5
-    assert np.abs(dev.download(kd, (nkv * hd,), np.float32) - rope_ref(k, pos, hd, base)).max() <= 2e-5
+    tol = 2e-6 + 1.5e-7 * pos
+    assert np.abs(dev.download(qd, (nh * hd,), np.float32) - reference.rope(q, pos, hd, nh, base)).max() <= tol
+    assert np.abs(dev.download(kd, (nkv * hd,), np.float32) - reference.rope(k, pos, hd, nkv, base)).max() <= tol
+    # and against the correctly rounded restatement: the same angle bits
+    assert np.abs(dev.download(qd, (nh * hd,), np.float32) - rope_ref(q, pos, hd, base)).max() <= 1e-6
     dev.check()
     dev.free(qd)
     dev.free(kd)
