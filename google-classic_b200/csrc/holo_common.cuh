@@ -126,6 +126,9 @@ constexpr int MV_MAX_ROWBLOCKS = 1 << 16;
 
 HoloDevice *holo_dev();                  // current device's state, initialised on demand
 cudaStream_t holo_stream();
+// the stream calls use without initialising anything: the thread's override,
+// else the device's library stream if it exists, else the legacy stream (0)
+cudaStream_t holo_stream_if_ready();
 void holo_set_status(int code, const char *what);   // sticky host-side status
 bool holo_check_launch(const char *what);           // cudaGetLastError -> status
 // Scratch of at least `bytes` on the current device for ABI helpers whose

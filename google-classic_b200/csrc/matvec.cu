@@ -461,26 +461,26 @@ __global__ void __launch_bounds__(NTHREADS, MIN_CTAS_PER_SM) mv_tiled_kernel(con
 // host side
 // ---------------------------------------------------------------------------
 template <int TYPE, int ACT, int EPI, bool NORM>
-bool launch_tiled(const MvParams &base, int sms, bool pdl, cudaStream_t st) {
+bool launch_tiled(const MvParams &base, int sms, int max_ctas, bool pdl, cudaStream_t st) {
     MvParams p = base;
-    if ((unsigned long long)p.total_units * (unsigned long long)MV_MAX_CTAS >= (1ull << 32)) {
+    if ((unsigned long long)p.total_units * (unsigned long long)max_ctas >= (1ull << 32)) {
         holo_set_status(HOLO_E_UNSUPPORTED, "tiled matvec: too many units");
         return false;
     }
     // One CTA per SM; more (in further waves) only when a CTA's share of the
     // row-blocks would not fit its reduction buffer.
     size_t smem = 0;
-    p.nctas = min(p.total_units, sms);
+    p.nctas = min(p.total_units, min(sms, max_ctas));
     for (;;) {
         const int per_cta = (p.total_units + p.nctas - 1) / p.nctas;
         p.max_local_rb = (p.units + per_cta - 2) / p.units + 1;
         smem = mv_smem_layout(ACT, NORM, p.max_local_rb, p.nblk32p).total;
         if (smem <= SMEM_LIMIT) break;
-        if (p.nctas >= min(p.total_units, MV_MAX_CTAS) || mv_smem_layout(ACT, NORM, 2, p.nblk32p).total > SMEM_LIMIT) {
+        if (p.nctas >= min(p.total_units, max_ctas) || mv_smem_layout(ACT, NORM, 2, p.nblk32p).total > SMEM_LIMIT) {
             holo_set_status(HOLO_E_UNSUPPORTED, "tiled matvec: in_dim too large for shared memory");
             return false;
         }
-        p.nctas = min(min(p.total_units, MV_MAX_CTAS), p.nctas + sms);
+        p.nctas = min(min(p.total_units, max_ctas), p.nctas + sms);
     }
     auto kern = mv_tiled_kernel<TYPE, ACT, EPI, NORM>;
     static bool configured[16] = {false};
@@ -514,24 +514,24 @@ bool launch_tiled(const MvParams &base, int sms, bool pdl, cudaStream_t st) {
 }
 
 template <int TYPE, int ACT>
-bool dispatch_epi(const MvParams &p, int epi, bool norm, int sms, bool pdl, cudaStream_t st) {
+bool dispatch_epi(const MvParams &p, int epi, bool norm, int sms, int mc, bool pdl, cudaStream_t st) {
     switch (epi) {
     case MV_EPI_ADD:
-        return norm ? launch_tiled<TYPE, ACT, MV_EPI_ADD, true>(p, sms, pdl, st)
-                    : launch_tiled<TYPE, ACT, MV_EPI_ADD, false>(p, sms, pdl, st);
+        return norm ? launch_tiled<TYPE, ACT, MV_EPI_ADD, true>(p, sms, mc, pdl, st)
+                    : launch_tiled<TYPE, ACT, MV_EPI_ADD, false>(p, sms, mc, pdl, st);
     case MV_EPI_SILU_MUL:
-        return norm ? launch_tiled<TYPE, ACT, MV_EPI_SILU_MUL, true>(p, sms, pdl, st)
-                    : launch_tiled<TYPE, ACT, MV_EPI_SILU_MUL, false>(p, sms, pdl, st);
+        return norm ? launch_tiled<TYPE, ACT, MV_EPI_SILU_MUL, true>(p, sms, mc, pdl, st)
+                    : launch_tiled<TYPE, ACT, MV_EPI_SILU_MUL, false>(p, sms, mc, pdl, st);
     default:
-        return norm ? launch_tiled<TYPE, ACT, MV_EPI_STORE, true>(p, sms, pdl, st)
-                    : launch_tiled<TYPE, ACT, MV_EPI_STORE, false>(p, sms, pdl, st);
+        return norm ? launch_tiled<TYPE, ACT, MV_EPI_STORE, true>(p, sms, mc, pdl, st)
+                    : launch_tiled<TYPE, ACT, MV_EPI_STORE, false>(p, sms, mc, pdl, st);
     }
 }
 
 template <int TYPE>
-bool dispatch_act(const MvParams &p, int act, int epi, bool norm, int sms, bool pdl, cudaStream_t st) {
-    if (act == HOLO_ACT_Q8) return dispatch_epi<TYPE, HOLO_ACT_Q8>(p, epi, norm, sms, pdl, st);
-    return dispatch_epi<TYPE, HOLO_ACT_F32>(p, epi, norm, sms, pdl, st);
+bool dispatch_act(const MvParams &p, int act, int epi, bool norm, int sms, int mc, bool pdl, cudaStream_t st) {
+    if (act == HOLO_ACT_Q8) return dispatch_epi<TYPE, HOLO_ACT_Q8>(p, epi, norm, sms, mc, pdl, st);
+    return dispatch_epi<TYPE, HOLO_ACT_F32>(p, epi, norm, sms, mc, pdl, st);
 }
 
 }  // namespace
@@ -539,6 +539,18 @@ bool dispatch_act(const MvParams &p, int act, int epi, bool norm, int sms, bool 
 bool holo_matvec_launch(const void *M, const WeightInfo &wi, const MvLaunch &L, cudaStream_t st) {
     HoloDevice *D = holo_dev();
     if (!D) return false;
+    MvScratch S;
+    S.partials = L.partials ? L.partials : D->mv_partials;
+    S.counters = L.counters ? L.counters : D->mv_counters;
+    S.status = D->status;
+    S.sms = D->sms;
+    S.max_ctas = MV_MAX_CTAS;
+    S.max_rowblocks = MV_MAX_ROWBLOCKS;
+    return holo_matvec_launch_with(M, wi, L, st, S);
+}
+
+bool holo_matvec_launch_with(const void *M, const WeightInfo &wi, const MvLaunch &L, cudaStream_t st,
+                             const MvScratch &S) {
     MvParams p{};
     p.W = (const uint8_t *)M;
     p.x = L.x;
@@ -552,11 +564,11 @@ bool holo_matvec_launch(const void *M, const WeightInfo &wi, const MvLaunch &L, 
     p.units = wi.units;
     p.nrb = wi.rows_padded / TILE_ROWS;
     p.total_units = p.nrb * p.units;
-    p.partials = L.partials ? L.partials : D->mv_partials;
-    p.counters = L.counters ? L.counters : D->mv_counters;
-    p.status = D->status;
+    p.partials = S.partials;
+    p.counters = S.counters;
+    p.status = S.status;
     p.bulk = ((uintptr_t)L.x % 16 == 0) && ((uintptr_t)L.norm_w % 16 == 0);
-    if (p.nrb > MV_MAX_ROWBLOCKS) {
+    if (p.nrb > S.max_rowblocks) {
         holo_set_status(HOLO_E_UNSUPPORTED, "matvec: too many rows");
         return false;
     }
@@ -568,13 +580,13 @@ bool holo_matvec_launch(const void *M, const WeightInfo &wi, const MvLaunch &L, 
     switch (wi.type) {
     case GT_Q8_0:
         p.nblk32p = p.units * UnitGeom<GT_Q8_0>::BLKS32;
-        return dispatch_act<GT_Q8_0>(p, L.act, L.epi, norm, D->sms, L.pdl, st);
+        return dispatch_act<GT_Q8_0>(p, L.act, L.epi, norm, S.sms, S.max_ctas, L.pdl, st);
     case GT_Q4_0:
         p.nblk32p = p.units * UnitGeom<GT_Q4_0>::BLKS32;
-        return dispatch_act<GT_Q4_0>(p, L.act, L.epi, norm, D->sms, L.pdl, st);
+        return dispatch_act<GT_Q4_0>(p, L.act, L.epi, norm, S.sms, S.max_ctas, L.pdl, st);
     case GT_Q4_K:
         p.nblk32p = p.units * UnitGeom<GT_Q4_K>::BLKS32;
-        return dispatch_act<GT_Q4_K>(p, L.act, L.epi, norm, D->sms, L.pdl, st);
+        return dispatch_act<GT_Q4_K>(p, L.act, L.epi, norm, S.sms, S.max_ctas, L.pdl, st);
     default:
         holo_set_status(HOLO_E_ARG, "matvec: type has no tiled kernel");
         return false;

@@ -18,4 +18,19 @@ struct MvLaunch {
     int *counters = nullptr;
 };
 
+// Where a launch finds its scratch and limits: partials [max_ctas][2][32] f32,
+// counters [max_rowblocks] i32 (zero between launches), the device status word.
+struct MvScratch {
+    float *partials = nullptr;
+    int *counters = nullptr;
+    int *status = nullptr;
+    int sms = 0;
+    int max_ctas = 0;
+    int max_rowblocks = 0;
+};
+
+// launch on the current device's state (initialises it on first use)
 bool holo_matvec_launch(const void *M, const WeightInfo &wi, const MvLaunch &L, cudaStream_t st);
+// launch with caller-provided scratch; touches no per-device state
+bool holo_matvec_launch_with(const void *M, const WeightInfo &wi, const MvLaunch &L, cudaStream_t st,
+                             const MvScratch &S);

@@ -94,6 +94,13 @@ cudaStream_t holo_stream() {
     return D ? D->stream : nullptr;
 }
 
+cudaStream_t holo_stream_if_ready() {
+    if (t_stream_override) return t_stream_override;
+    int id = current_device();
+    if (id >= 0 && id < kMaxDevices && g_dev[id].ready) return g_dev[id].stream;
+    return nullptr;
+}
+
 void holo_set_status(int code, const char *what) {
     std::lock_guard<std::mutex> lk(g_status_mu);
     if (g_status == 0 && code != 0) {
@@ -184,7 +191,13 @@ void cuda_clear_status(void) {
         g_status_what.clear();
     }
     int id = current_device();
-    if (id >= 0 && id < kMaxDevices && g_dev[id].ready) cudaMemset(g_dev[id].status, 0, sizeof(int));
+    if (id >= 0 && id < kMaxDevices && g_dev[id].ready) {
+        // a launch that gave up (bounded wait) may leave split-K counters raised
+        cudaStreamSynchronize(g_dev[id].stream);
+        cudaMemset(g_dev[id].status, 0, sizeof(int));
+        cudaMemset(g_dev[id].mv_counters, 0, sizeof(int) * MV_MAX_ROWBLOCKS);
+        cudaDeviceSynchronize();
+    }
     cudaGetLastError();
 }
 

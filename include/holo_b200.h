@@ -79,6 +79,21 @@ int cuda_get_pdl(void);
 void cuda_matvec(float *dst, const void *M, const float *v, int out_dim, int in_dim,
                  int ggml_type, int act_mode, const float *residual);
 
+/* ---- matvec without allocation ------------------------------------------------
+ * No counterpart in the reference.  dst = M . v like cuda_matvec (no residual)
+ * for a tiled weight M from cuda_upload_quant, but its split-K scratch is
+ * static device memory (file-scope arrays found with cudaGetSymbolAddress),
+ * so the call allocates and frees nothing: for callers that must not touch
+ * the allocator after set-up.  Limits: out_dim <= 262144 (8192 row-blocks);
+ * the grid is capped at 296 CTAs.  Runs on the thread's cuda_set_stream
+ * stream, else the library stream if the device is initialised, else the
+ * legacy default stream.  Every call clears the counters it uses first.
+ * The scratch is shared by all calls on a device: overlapping calls (other
+ * streams or threads) race.  Returns 0, or the error code it also records
+ * (HOLO_E_ARG, HOLO_E_UNSUPPORTED for the row limit, a CUDA error). */
+int cuda_matvec_noalloc(float *dst, const void *M, const float *v, int out_dim, int in_dim,
+                        int ggml_type, int act_mode);
+
 /* ---- parity probes (run the device decode code on their own) ------------- */
 /* dst[rows][cols] = dequantized values of M (raw or tiled). */
 void cuda_dequantize_rows(float *dst, const void *M, int ggml_type, int rows, int cols);
