@@ -1,0 +1,1089 @@
+// decode.cu -- batch-1 decode of a Llama-family model on one GPU.
+//
+// One token step restates llm_forward for one position (src/ai/llm.c:1015-1269)
+// and llm_sample (llm.c:1281-1328, tensor.c:460-667) on the device:
+//
+//   embed   x = emb[seq[pos]]                                  (llm.c:1058, 943-1008)
+//   per layer l:
+//     mv    qkv = [Wq;Wk;Wv] . rmsnorm(x, attn_norm)           (llm.c:1075-1087)
+//     rope  rotate-half RoPE of q and k at pos, k and v appended to the
+//           layer's cache at [pos][kv_dim]                       (llm.c:1131-1170)
+//     attn  softmax(q.K^T / sqrt(hd)) . V over positions 0..pos, GQA
+//           (llm.c:1172-1210), split over positions then merged
+//     mv    x = x + Wo . att                                     (llm.c:1214-1222)
+//     mv    h = silu(W1 . xn) * (W3 . xn), xn = rmsnorm(x, ffn_norm), with W1 and
+//           W3 rows interleaved by 16 so one row-block yields 16 outputs
+//                                                                (llm.c:1226-1240)
+//     mv    x = x + W2 . h                                       (llm.c:1243-1252)
+//   mv      logits = Wout . rmsnorm(x, norm)                     (llm.c:1256-1267)
+//   sample  temperature, repetition penalty, softmax, top-k, top-p, draw
+//
+// pos, the token sequence and the history live in device memory, so the step
+// is captured once as a CUDA graph and replayed for every position; every
+// kernel of the step is launched with programmatic dependent launch, so the
+// next matvec's CTAs are resident early and prefetch its weights into L2.
+#include "holo_common.cuh"
+#include "mv_device.cuh"
+#include "matvec.cuh"
+
+#include <cfloat>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+namespace {
+
+__device__ __forceinline__ void dec_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void dec_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename KV> __device__ __forceinline__ KV to_kv(float v);
+template <> __device__ __forceinline__ float to_kv<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half to_kv<__half>(float v) { return __float2half_rn(v); }
+
+// ---------------------------------------------------------------------------
+// embedding row of the token at pos (F32 copy, F16 exact widening)
+// ---------------------------------------------------------------------------
+template <bool F16>
+__global__ void dec_embed_kernel(float *__restrict__ x, const void *__restrict__ emb, const int *__restrict__ seq,
+                                 const int *__restrict__ pos_p, int dim, int vocab) {
+    dec_pdl_trigger();
+    dec_pdl_wait();
+    const int tok = seq[*pos_p];
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= dim) return;
+    if (tok < 0 || tok >= vocab) {
+        x[i] = 0.0f;
+        return;
+    }
+    if constexpr (F16) x[i] = __half2float(reinterpret_cast<const __half *>(emb)[(size_t)tok * dim + i]);
+    else x[i] = reinterpret_cast<const float *>(emb)[(size_t)tok * dim + i];
+}
+
+// ---------------------------------------------------------------------------
+// RoPE of q (n_heads) and k (n_kv_heads) at pos, then k and v appended to the
+// layer's cache; one CTA per head, one thread per rotation pair
+// ---------------------------------------------------------------------------
+template <typename KV>
+__global__ void dec_rope_append_kernel(float *__restrict__ qkv, KV *__restrict__ kc, KV *__restrict__ vc,
+                                       const int *__restrict__ pos_p, int hd, int n_heads, int n_kv_heads,
+                                       float base) {
+    dec_pdl_trigger();
+    dec_pdl_wait();
+    const int pos = *pos_p;
+    const int h = blockIdx.x, i = threadIdx.x, half = hd / 2;
+    if (i >= half) return;
+    const int q_dim = n_heads * hd, kv_dim = n_kv_heads * hd;
+    float c, s;
+    rope_cos_sin(pos, i, hd, base, c, s);
+    if (h < n_heads) {
+        float *qh = qkv + (size_t)h * hd;
+        rope_rotate(qh[i], qh[i + half], c, s);
+    }
+    if (h < n_kv_heads) {
+        const float *kh = qkv + q_dim + (size_t)h * hd;
+        const float *vh = qkv + q_dim + kv_dim + (size_t)h * hd;
+        float a = kh[i], b = kh[i + half];
+        rope_rotate(a, b, c, s);
+        KV *kd = kc + (size_t)pos * kv_dim + (size_t)h * hd;
+        KV *vd = vc + (size_t)pos * kv_dim + (size_t)h * hd;
+        kd[i] = to_kv<KV>(a);
+        kd[i + half] = to_kv<KV>(b);
+        vd[i] = to_kv<KV>(vh[i]);
+        vd[i + half] = to_kv<KV>(vh[i + half]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// decode attention, split over positions (flash-decoding).  CTA (head h, split
+// s) folds positions [s*per_split, ...) of 0..pos with an online softmax.  An
+// 8-lane group owns one position at a time (HD/8 dims per lane), so a warp
+// works on four positions at once and each score needs 3 shuffles.
+// ---------------------------------------------------------------------------
+constexpr int AT_WARPS = 4;
+constexpr int AT_GROUPS = AT_WARPS * 4;     // position groups per CTA
+
+template <typename KV, int N> struct KvVec;
+template <int N> struct KvVec<float, N> {
+    static __device__ __forceinline__ void load(const float *p, float (&o)[N]) {
+#pragma unroll
+        for (int i = 0; i < N; i += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(p + i);
+            o[i] = v.x; o[i + 1] = v.y; o[i + 2] = v.z; o[i + 3] = v.w;
+        }
+    }
+};
+template <int N> struct KvVec<__half, N> {
+    static __device__ __forceinline__ void load(const __half *p, float (&o)[N]) {
+#pragma unroll
+        for (int i = 0; i < N; i += 8) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(p + i);
+            const __half2 *h2 = reinterpret_cast<const __half2 *>(&v);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = __half22float2(h2[k]);
+                o[i + 2 * k] = f.x;
+                o[i + 2 * k + 1] = f.y;
+            }
+        }
+    }
+};
+
+template <typename KV, int HD>
+__global__ void __launch_bounds__(AT_WARPS * 32)
+dec_attn_split_kernel(float *__restrict__ part, const float *__restrict__ q, const KV *__restrict__ kc,
+                      const KV *__restrict__ vc, const int *__restrict__ pos_p, int kv_dim, int group,
+                      int per_split, int max_splits, float sqrt_hd) {
+    constexpr int DPL = HD / 8;
+    dec_pdl_trigger();
+    dec_pdl_wait();
+    const int kv_len = *pos_p + 1;
+    const int h = blockIdx.x, sp = blockIdx.y;
+    const int p0 = sp * per_split;
+    float *out = part + ((size_t)h * max_splits + sp) * (HD + 2);
+    if (p0 >= kv_len) {
+        if (threadIdx.x == 0) { out[0] = -FLT_MAX; out[1] = 0.0f; }
+        return;
+    }
+    const int p1 = min(kv_len, p0 + per_split);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 3, l8 = lane & 7;
+    const int kvh = h / group;
+    float qf[DPL], acc[DPL];
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) {
+        qf[d] = q[(size_t)h * HD + l8 * DPL + d];
+        acc[d] = 0.0f;
+    }
+    float m = -FLT_MAX, l = 0.0f;
+    for (int base = p0 + warp * 4; base < p1; base += AT_GROUPS) {
+        const int p = base + g;
+        const bool live = p < p1;
+        float kf[DPL];
+        float dot = 0.0f;
+        if (live) {
+            KvVec<KV, DPL>::load(kc + (size_t)p * kv_dim + (size_t)kvh * HD + l8 * DPL, kf);
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) dot = fmaf(qf[d], kf[d], dot);
+        }
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 4);
+        if (live) {
+            const float sc = __fdiv_rn(dot, sqrt_hd);     // score / sqrtf(hd), llm.c:1187
+            const float mn = fmaxf(m, sc);
+            const float corr = __expf(m - mn), e = __expf(sc - mn);
+            l = fmaf(l, corr, e);
+            float vf[DPL];
+            KvVec<KV, DPL>::load(vc + (size_t)p * kv_dim + (size_t)kvh * HD + l8 * DPL, vf);
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) acc[d] = fmaf(acc[d], corr, e * vf[d]);
+            m = mn;
+        }
+    }
+    // merge the CTA's position groups
+    __shared__ float sm_m[AT_GROUPS], sm_l[AT_GROUPS];
+    __shared__ float sm_acc[AT_GROUPS][HD];
+    const int gi = warp * 4 + g;
+    if (l8 == 0) { sm_m[gi] = m; sm_l[gi] = l; }
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) sm_acc[gi][l8 * DPL + d] = acc[d];
+    __syncthreads();
+    float M = -FLT_MAX;
+#pragma unroll
+    for (int k = 0; k < AT_GROUPS; ++k)
+        if (sm_l[k] > 0.0f) M = fmaxf(M, sm_m[k]);
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+        float a = 0.0f;
+#pragma unroll
+        for (int k = 0; k < AT_GROUPS; ++k)
+            if (sm_l[k] > 0.0f) a = fmaf(sm_acc[k][d], __expf(sm_m[k] - M), a);
+        out[2 + d] = a;
+    }
+    if (threadIdx.x == 0) {
+        float L = 0.0f;
+#pragma unroll
+        for (int k = 0; k < AT_GROUPS; ++k)
+            if (sm_l[k] > 0.0f) L = fmaf(sm_l[k], __expf(sm_m[k] - M), L);
+        out[0] = M;
+        out[1] = L;
+    }
+}
+
+template <int HD>
+__global__ void dec_attn_merge_kernel(float *__restrict__ att, const float *__restrict__ part,
+                                      const int *__restrict__ pos_p, int per_split, int max_splits) {
+    dec_pdl_trigger();
+    dec_pdl_wait();
+    const int kv_len = *pos_p + 1;
+    const int nsp = min(max_splits, (kv_len + per_split - 1) / per_split);
+    const int h = blockIdx.x;
+    const float *ph = part + (size_t)h * max_splits * (HD + 2);
+    float M = -FLT_MAX;
+    for (int s = 0; s < nsp; ++s)
+        if (ph[(size_t)s * (HD + 2) + 1] > 0.0f) M = fmaxf(M, ph[(size_t)s * (HD + 2)]);
+    float L = 0.0f;
+    for (int s = 0; s < nsp; ++s) {
+        const float *ps = ph + (size_t)s * (HD + 2);
+        if (ps[1] > 0.0f) L = fmaf(ps[1], __expf(ps[0] - M), L);
+    }
+    const float inv = 1.0f / L;
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+        float a = 0.0f;
+        for (int s = 0; s < nsp; ++s) {
+            const float *ps = ph + (size_t)s * (HD + 2);
+            if (ps[1] > 0.0f) a = fmaf(ps[2 + d], __expf(ps[0] - M), a);
+        }
+        att[(size_t)h * HD + d] = a * inv;
+    }
+}
+
+__global__ void dec_step_end_kernel(int *pos_p) {
+    dec_pdl_trigger();
+    dec_pdl_wait();
+    if (threadIdx.x == 0) *pos_p += 1;
+}
+
+__global__ void dec_set_token_kernel(int *seq, const int *pos_p, int token) { seq[*pos_p] = token; }
+__global__ void dec_push_kernel(int *hist, int *nhist_p, int token) {
+    hist[*nhist_p] = token;
+    *nhist_p += 1;
+}
+
+// ---------------------------------------------------------------------------
+// sampler: llm_sample (llm.c:1281-1328) on the device, one 1024-thread CTA.
+//  1. temperature: logits *= 1/T when T > 0 and T != 1 (tensor.c:636-642)
+//  2. repetition penalty over the last repeat_last_n history tokens, once per
+//     occurrence: /= penalty if positive, *= penalty otherwise (tensor.c:644-657)
+//  3. greedy (T == 0): the first index of the largest penalised logit
+//  4. softmax; 5. top-k (keep p >= the k-th largest p, renormalise);
+//  6. top-p (sort descending, keep through the first cumulative sum > p,
+//     renormalise); 7. draw: first index whose cumulative sum exceeds r.
+// The sums of the renormalisations and the draw run in the reference's order
+// (index order; descending order for top-p).  Two steps differ in rounding
+// only: exp is evaluated in double and rounded once, and the softmax
+// denominator is summed as a tree.
+// ---------------------------------------------------------------------------
+constexpr int SM_THREADS = 1024;
+constexpr int SM_SORT_MAX = 4096;           // top-p candidates sorted in shared memory
+
+struct SampleArgs {
+    int vocab;
+    int use_temp;          // T > 0 and T != 1
+    float tscale;          // 1/T
+    int greedy;            // T == 0
+    float penalty;
+    int last_n;
+    int top_k;
+    float top_p;
+    int gen;               // 1: generation step (skip during the prompt, append the token)
+    int n_prompt;
+};
+
+__device__ __forceinline__ void block_reduce_max_first(float &v, int &idx, float *sv, int *si) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
+    }
+    if (lane == 0) { sv[warp] = v; si[warp] = idx; }
+    __syncthreads();
+    if (warp == 0) {
+        v = lane < (int)(blockDim.x >> 5) ? sv[lane] : -FLT_MAX;
+        idx = lane < (int)(blockDim.x >> 5) ? si[lane] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+            if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
+        }
+        if (lane == 0) { sv[0] = v; si[0] = idx; }
+    }
+    __syncthreads();
+    v = sv[0];
+    idx = si[0];
+    __syncthreads();
+}
+
+__device__ __forceinline__ float block_sum(float v, float *sv) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) sv[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        v = lane < (int)(blockDim.x >> 5) ? sv[lane] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) sv[0] = v;
+    }
+    __syncthreads();
+    v = sv[0];
+    __syncthreads();
+    return v;
+}
+
+__device__ __forceinline__ int block_exclusive_scan(int v, int *si, int &total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) si[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < (int)(blockDim.x >> 5) ? si[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        si[lane] = w;   // inclusive over warps
+    }
+    __syncthreads();
+    const int before = (warp > 0 ? si[warp - 1] : 0) + x - v;
+    total = si[(blockDim.x >> 5) - 1];
+    __syncthreads();
+    return before;
+}
+
+__global__ void __launch_bounds__(SM_THREADS)
+dec_sample_kernel(float *__restrict__ logits, float *__restrict__ probs, int *__restrict__ kept_idx,
+                  float *__restrict__ kept_p, int *__restrict__ seq, int *__restrict__ hist, int *__restrict__ nhist_p,
+                  const int *__restrict__ pos_p, const float *__restrict__ rvals, int *__restrict__ out_tokens,
+                  int *__restrict__ last_token, int *__restrict__ status, const SampleArgs a) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    __shared__ unsigned hist256[256];
+    __shared__ unsigned s_prefix;
+    __shared__ int s_krem;
+    __shared__ float s_scale;
+    __shared__ int s_ncut;
+    __shared__ int s_token;
+    __shared__ float sort_p[SM_SORT_MAX];
+    __shared__ int sort_i[SM_SORT_MAX];
+    dec_pdl_trigger();
+    dec_pdl_wait();
+    const int pos = *pos_p;
+    if (a.gen && pos < a.n_prompt - 1) return;
+    const int gi = a.gen ? pos - (a.n_prompt - 1) : 0;
+    const int V = a.vocab, tid = threadIdx.x;
+    const int nhist = *nhist_p;
+
+    // 1-2. temperature, repetition penalty (in place, as the reference)
+    if (a.use_temp)
+        for (int i = tid; i < V; i += SM_THREADS) logits[i] = logits[i] * a.tscale;
+    __syncthreads();
+    if (a.penalty != 1.0f && nhist > 0) {
+        if (tid == 0) {
+            const int start = nhist > a.last_n ? nhist - a.last_n : 0;
+            for (int t = start; t < nhist; ++t) {
+                const int tok = hist[t];
+                if (tok >= 0 && tok < V) {
+                    const float v = logits[tok];
+                    logits[tok] = v > 0.0f ? __fdiv_rn(v, a.penalty) : v * a.penalty;
+                }
+            }
+        }
+        __syncthreads();
+    }
+    // index-order chunk of this thread (compaction keeps index order)
+    const int chunk = (V + SM_THREADS - 1) / SM_THREADS;
+    const int c0 = min(V, tid * chunk), c1 = min(V, c0 + chunk);
+
+    int token;
+    if (a.greedy) {
+        float bv = -FLT_MAX;
+        int bi = 0x7fffffff;
+        for (int i = c0; i < c1; ++i)
+            if (logits[i] > bv || bi == 0x7fffffff) { bv = logits[i]; bi = i; }
+        block_reduce_max_first(bv, bi, sv, si);
+        token = bi;
+    } else {
+        // 4. softmax
+        float mx = -FLT_MAX;
+        int mi = 0;
+        for (int i = c0; i < c1; ++i)
+            if (logits[i] > mx) mx = logits[i];
+        block_reduce_max_first(mx, mi, sv, si);
+        float part = 0.0f;
+        for (int i = c0; i < c1; ++i) {
+            const float e = (float)exp((double)(logits[i] - mx));
+            probs[i] = e;
+            part += e;
+        }
+        const float S = block_sum(part, sv);
+        const float scale = __fdiv_rn(1.0f, S);
+        for (int i = c0; i < c1; ++i) probs[i] = probs[i] * scale;
+        __syncthreads();
+
+        // 5. top-k: the k-th largest probability by radix selection on its bits
+        int nkept;
+        if (a.top_k > 0 && a.top_k < V) {
+            if (tid == 0) { s_prefix = 0u; s_krem = a.top_k; }
+            unsigned mask = 0u;
+            for (int shift = 24; shift >= 0; shift -= 8) {
+                for (int b = tid; b < 256; b += SM_THREADS) hist256[b] = 0u;
+                __syncthreads();
+                const unsigned prefix = s_prefix;
+                for (int i = c0; i < c1; ++i) {
+                    const unsigned key = __float_as_uint(probs[i]);
+                    if ((key & mask) == prefix) atomicAdd(&hist256[(key >> shift) & 255u], 1u);
+                }
+                __syncthreads();
+                if (tid == 0) {
+                    int cum = 0, krem = s_krem;
+                    for (int d = 255; d >= 0; --d) {
+                        const int c = (int)hist256[d];
+                        if (cum + c >= krem) {
+                            s_prefix = prefix | ((unsigned)d << shift);
+                            s_krem = krem - cum;
+                            break;
+                        }
+                        cum += c;
+                    }
+                }
+                mask |= 255u << shift;
+                __syncthreads();
+            }
+            const float thr = __uint_as_float(s_prefix);
+            int cnt = 0;
+            for (int i = c0; i < c1; ++i) cnt += probs[i] >= thr;
+            int total;
+            int off = block_exclusive_scan(cnt, si, total);
+            for (int i = c0; i < c1; ++i)
+                if (probs[i] >= thr) { kept_idx[off] = i; kept_p[off] = probs[i]; ++off; }
+            nkept = total;
+            __syncthreads();
+            if (tid == 0) {
+                float sum = 0.0f;
+                for (int j = 0; j < nkept; ++j) sum += kept_p[j];
+                s_scale = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 1.0f;
+            }
+            __syncthreads();
+            for (int j = tid; j < nkept; j += SM_THREADS) kept_p[j] = kept_p[j] * s_scale;
+            __syncthreads();
+        } else {
+            for (int i = tid; i < V; i += SM_THREADS) { kept_idx[i] = i; kept_p[i] = probs[i]; }
+            nkept = V;
+            __syncthreads();
+        }
+
+        // 6. top-p over the kept candidates (sorted descending in shared memory)
+        if (a.top_p > 0.0f && a.top_p < 1.0f) {
+            if (nkept > SM_SORT_MAX) {
+                if (tid == 0) atomicExch(status, HOLO_E_UNSUPPORTED);
+                return;
+            }
+            int n2 = 1;
+            while (n2 < nkept) n2 <<= 1;
+            for (int j = tid; j < n2; j += SM_THREADS) {
+                sort_p[j] = j < nkept ? kept_p[j] : -1.0f;
+                sort_i[j] = j < nkept ? j : 0x7fffffff;
+            }
+            __syncthreads();
+            // bitonic sort: descending probability, ties by ascending position
+            for (int k = 2; k <= n2; k <<= 1) {
+                for (int jj = k >> 1; jj > 0; jj >>= 1) {
+                    for (int t = tid; t < n2; t += SM_THREADS) {
+                        const int u = t ^ jj;
+                        if (u > t) {
+                            const bool desc = (t & k) == 0;
+                            const float pt = sort_p[t], pu = sort_p[u];
+                            const int it = sort_i[t], iu = sort_i[u];
+                            const bool t_first = pt > pu || (pt == pu && it < iu);
+                            if (desc ? !t_first : t_first) {
+                                sort_p[t] = pu; sort_p[u] = pt;
+                                sort_i[t] = iu; sort_i[u] = it;
+                            }
+                        }
+                    }
+                    __syncthreads();
+                }
+            }
+            if (tid == 0) {
+                float cum = 0.0f;
+                int cut = nkept;
+                for (int j = 0; j < nkept; ++j) {
+                    cum += sort_p[j];
+                    if (cum > a.top_p) { cut = j + 1; break; }
+                }
+                s_ncut = cut;
+            }
+            __syncthreads();
+            // zero the candidates past the cut (sorted order), then renormalise
+            for (int j = tid; j < nkept; j += SM_THREADS)
+                if (j >= s_ncut) kept_p[sort_i[j]] = 0.0f;
+            __syncthreads();
+            if (tid == 0) {
+                float sum = 0.0f;
+                for (int j = 0; j < nkept; ++j) sum += kept_p[j];
+                s_scale = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 1.0f;
+            }
+            __syncthreads();
+            for (int j = tid; j < nkept; j += SM_THREADS) kept_p[j] = kept_p[j] * s_scale;
+            __syncthreads();
+        }
+
+        // 7. draw (sample_prob, tensor.c:473-482): candidates are in index order
+        if (tid == 0) {
+            const float r = rvals[gi];
+            float cum = 0.0f;
+            int tok = V - 1;
+            for (int j = 0; j < nkept; ++j) {
+                cum += kept_p[j];
+                if (r < cum) { tok = kept_idx[j]; break; }
+            }
+            s_token = tok;
+        }
+        __syncthreads();
+        token = s_token;
+    }
+    if (tid == 0) {
+        *last_token = token;
+        if (a.gen) {
+            seq[pos + 1] = token;
+            hist[nhist] = token;
+            *nhist_p = nhist + 1;
+            out_tokens[gi] = token;
+        }
+    }
+}
+
+template <typename K, typename... Args>
+bool launch_pdl(K kern, dim3 grid, dim3 block, cudaStream_t st, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, kern, args...) != cudaSuccess) return holo_check_launch("decode kernel launch");
+    return holo_check_launch("decode kernel launch");
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// model object
+// ---------------------------------------------------------------------------
+struct HoloLayer {
+    float *attn_norm = nullptr, *ffn_norm = nullptr;
+    uint8_t *wqkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr;
+    WeightInfo i_qkv, i_o, i_13, i_2;
+    bool ready = false;
+};
+
+struct HoloModel {
+    holo_model_desc d{};
+    int q_dim = 0, kv_dim = 0;
+    std::vector<HoloLayer> layers;
+    void *emb = nullptr;
+    float *final_norm = nullptr;
+    uint8_t *out = nullptr;
+    WeightInfo i_out;
+    bool globals_ready = false;
+    void *kc = nullptr, *vc = nullptr;
+    float *x = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+    float *part = nullptr, *probs = nullptr, *kept_p = nullptr, *rvals = nullptr;
+    int *kept_idx = nullptr;
+    int *d_pos = nullptr, *d_seq = nullptr, *d_hist = nullptr, *d_nhist = nullptr, *d_out = nullptr, *d_last = nullptr;
+    int per_split = 64, max_splits = 0;
+    int h_pos = 0, h_nhist = 0;
+    cudaGraphExec_t g_forward = nullptr, g_gen = nullptr;
+    SampleArgs gen_args{};
+    int gen_n_prompt = -1;
+};
+
+namespace {
+
+bool dev_alloc(void **p, size_t bytes) {
+    if (cudaMalloc(p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        holo_set_status(HOLO_E_NOMEM, "holo_model: device allocation");
+        *p = nullptr;
+        return false;
+    }
+    return true;
+}
+
+// upload raw GGUF blocks of `rows` x `cols` and repack them into dst
+bool upload_repack(uint8_t *dst, const void *host, int type, int rows, int cols, cudaStream_t st) {
+    const size_t raw = (size_t)rows * (size_t)gguf_row_bytes(type, cols);
+    void *staging = nullptr;
+    if (!dev_alloc(&staging, raw)) return false;
+    bool ok = cudaMemcpyAsync(staging, host, raw, cudaMemcpyHostToDevice, st) == cudaSuccess;
+    ok = ok && holo_repack_to(dst, staging, type, rows, cols, holo_q4k_layout(), st);
+    cudaStreamSynchronize(st);
+    cudaFree(staging);
+    if (!ok) holo_set_status(HOLO_E_ARG, "holo_model: weight upload");
+    return ok;
+}
+
+bool upload_plain(void **dst, const void *host, size_t bytes, cudaStream_t st) {
+    if (!dev_alloc(dst, bytes)) return false;
+    if (cudaMemcpyAsync(*dst, host, bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+        holo_check_launch("holo_model: upload");
+        return false;
+    }
+    return true;
+}
+
+void drop_graphs(HoloModel *m) {
+    if (m->g_forward) cudaGraphExecDestroy(m->g_forward);
+    if (m->g_gen) cudaGraphExecDestroy(m->g_gen);
+    m->g_forward = m->g_gen = nullptr;
+}
+
+// enqueue one token step (embed .. logits [.. sample] .. pos+1)
+bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &sa) {
+    const holo_model_desc &d = m->d;
+    const bool pdl = true;
+    const int hd = d.head_dim;
+    bool ok = true;
+    // the step's first kernel follows whatever precedes the graph in full
+    ok = ok && (d.emb_type == 1
+                    ? launch_pdl(dec_embed_kernel<true>, dim3((d.dim + 255) / 256), dim3(256), st, false, m->x,
+                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab)
+                    : launch_pdl(dec_embed_kernel<false>, dim3((d.dim + 255) / 256), dim3(256), st, false, m->x,
+                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab));
+    const size_t kv_layer = (size_t)d.max_seq * m->kv_dim;
+    const size_t kv_es = d.kv_f16 ? 2 : 4;
+    const float sqrt_hd = sqrtf((float)hd);
+    for (int l = 0; l < d.n_layers && ok; ++l) {
+        HoloLayer &L = m->layers[l];
+        MvLaunch a;
+        a.x = m->x; a.y = m->qkv; a.norm_w = L.attn_norm; a.eps = d.eps; a.act = d.act_mode;
+        a.epi = MV_EPI_STORE; a.pdl = pdl;
+        ok = ok && holo_matvec_launch(L.wqkv, L.i_qkv, a, st);
+        uint8_t *kc = (uint8_t *)m->kc + (size_t)l * kv_layer * kv_es;
+        uint8_t *vc = (uint8_t *)m->vc + (size_t)l * kv_layer * kv_es;
+        const int heads = max(d.n_heads, d.n_kv_heads);
+        if (d.kv_f16)
+            ok = ok && launch_pdl(dec_rope_append_kernel<__half>, dim3(heads), dim3(hd / 2), st, pdl, m->qkv,
+                                  (__half *)kc, (__half *)vc, (const int *)m->d_pos, hd, d.n_heads, d.n_kv_heads,
+                                  d.rope_base);
+        else
+            ok = ok && launch_pdl(dec_rope_append_kernel<float>, dim3(heads), dim3(hd / 2), st, pdl, m->qkv,
+                                  (float *)kc, (float *)vc, (const int *)m->d_pos, hd, d.n_heads, d.n_kv_heads,
+                                  d.rope_base);
+        const int group = d.n_heads / d.n_kv_heads;
+        const dim3 ag(d.n_heads, m->max_splits);
+#define HOLO_ATTN(KVT, HDV)                                                                                   \
+    launch_pdl(dec_attn_split_kernel<KVT, HDV>, ag, dim3(AT_WARPS * 32), st, pdl, m->part,                    \
+               (const float *)m->qkv, (const KVT *)kc, (const KVT *)vc, (const int *)m->d_pos, m->kv_dim, group, \
+               m->per_split, m->max_splits, sqrt_hd) &&                                                       \
+        launch_pdl(dec_attn_merge_kernel<HDV>, dim3(d.n_heads), dim3(HDV), st, pdl, m->att,                   \
+                   (const float *)m->part, (const int *)m->d_pos, m->per_split, m->max_splits)
+        if (d.kv_f16) {
+            if (hd == 64) ok = ok && HOLO_ATTN(__half, 64);
+            else if (hd == 128) ok = ok && HOLO_ATTN(__half, 128);
+            else ok = ok && HOLO_ATTN(__half, 256);
+        } else {
+            if (hd == 64) ok = ok && HOLO_ATTN(float, 64);
+            else if (hd == 128) ok = ok && HOLO_ATTN(float, 128);
+            else ok = ok && HOLO_ATTN(float, 256);
+        }
+#undef HOLO_ATTN
+        MvLaunch o;
+        o.x = m->att; o.y = m->x; o.residual = m->x; o.act = d.act_mode; o.epi = MV_EPI_ADD; o.pdl = pdl;
+        ok = ok && holo_matvec_launch(L.wo, L.i_o, o, st);
+        MvLaunch f;
+        f.x = m->x; f.y = m->h; f.norm_w = L.ffn_norm; f.eps = d.eps; f.act = d.act_mode;
+        f.epi = MV_EPI_SILU_MUL; f.pdl = pdl;
+        ok = ok && holo_matvec_launch(L.w13, L.i_13, f, st);
+        MvLaunch w;
+        w.x = m->h; w.y = m->x; w.residual = m->x; w.act = d.act_mode; w.epi = MV_EPI_ADD; w.pdl = pdl;
+        ok = ok && holo_matvec_launch(L.w2, L.i_2, w, st);
+    }
+    MvLaunch lo;
+    lo.x = m->x; lo.y = m->logits; lo.norm_w = m->final_norm; lo.eps = d.eps; lo.act = d.act_mode;
+    lo.epi = MV_EPI_STORE; lo.pdl = pdl;
+    ok = ok && holo_matvec_launch(m->out, m->i_out, lo, st);
+    if (sample) {
+        HoloDevice *D = holo_dev();
+        ok = ok && launch_pdl(dec_sample_kernel, dim3(1), dim3(SM_THREADS), st, pdl, m->logits, m->probs,
+                              m->kept_idx, m->kept_p, m->d_seq, m->d_hist, m->d_nhist, (const int *)m->d_pos,
+                              (const float *)m->rvals, m->d_out, m->d_last, D ? D->status : nullptr, sa);
+    }
+    ok = ok && launch_pdl(dec_step_end_kernel, dim3(1), dim3(32), st, pdl, m->d_pos);
+    return ok;
+}
+
+// one-time per-kernel set-up of every matvec variant of the step, which must
+// not happen inside a stream capture
+bool prepare_step(HoloModel *m) {
+    const holo_model_desc &d = m->d;
+    HoloLayer &L = m->layers[0];
+    MvLaunch a;
+    a.norm_w = L.attn_norm; a.act = d.act_mode; a.epi = MV_EPI_STORE;
+    MvLaunch o;
+    o.residual = m->x; o.act = d.act_mode; o.epi = MV_EPI_ADD;
+    MvLaunch f;
+    f.norm_w = L.ffn_norm; f.act = d.act_mode; f.epi = MV_EPI_SILU_MUL;
+    return holo_matvec_prepare(L.i_qkv, a) && holo_matvec_prepare(L.i_o, o) && holo_matvec_prepare(L.i_13, f) &&
+           holo_matvec_prepare(L.i_2, o) && holo_matvec_prepare(m->i_out, a);
+}
+
+cudaGraphExec_t capture_step(HoloModel *m, bool sample, const SampleArgs &sa) {
+    cudaStream_t st = holo_stream();
+    cudaGraph_t g = nullptr;
+    if (!prepare_step(m)) return nullptr;
+    if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        holo_check_launch("holo_model: begin capture");
+        return nullptr;
+    }
+    const bool ok = enqueue_step(m, st, sample, sa);
+    const cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (!ok || e != cudaSuccess || !g) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        holo_set_status(HOLO_E_ARG, "holo_model: step capture failed");
+        return nullptr;
+    }
+    cudaGraphExec_t ex = nullptr;
+    if (cudaGraphInstantiate(&ex, g, 0) != cudaSuccess) {
+        cudaGetLastError();
+        ex = nullptr;
+        holo_set_status(HOLO_E_ARG, "holo_model: graph instantiation failed");
+    }
+    cudaGraphDestroy(g);
+    return ex;
+}
+
+bool model_ready(HoloModel *m) {
+    if (!m) return false;
+    for (auto &L : m->layers)
+        if (!L.ready) {
+            holo_set_status(HOLO_E_ARG, "holo_model: a layer has no weights");
+            return false;
+        }
+    if (!m->globals_ready) {
+        holo_set_status(HOLO_E_ARG, "holo_model: embeddings / output not set");
+        return false;
+    }
+    return true;
+}
+
+SampleArgs make_args(const HoloModel *m, const holo_sampler_desc *s) {
+    SampleArgs a{};
+    a.vocab = m->d.vocab;
+    a.greedy = s->temperature == 0.0f;
+    a.use_temp = s->temperature > 0.0f && s->temperature != 1.0f;
+    a.tscale = a.use_temp ? 1.0f / s->temperature : 1.0f;
+    a.penalty = s->repeat_penalty;
+    a.last_n = s->repeat_last_n;
+    a.top_k = s->top_k;
+    a.top_p = s->top_p;
+    return a;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" {
+
+void *holo_model_create(const holo_model_desc *desc) {
+    if (!desc) return nullptr;
+    const holo_model_desc &d = *desc;
+    const int hd = d.head_dim;
+    if (d.n_layers <= 0 || d.dim <= 0 || d.n_heads <= 0 || d.n_kv_heads <= 0 || d.n_heads % d.n_kv_heads ||
+        !(hd == 64 || hd == 128 || hd == 256) || d.ffn_dim <= 0 || d.ffn_dim % 16 || d.vocab <= 0 ||
+        d.max_seq <= 0 || (d.act_mode != HOLO_ACT_Q8 && d.act_mode != HOLO_ACT_F32) ||
+        (d.emb_type != 0 && d.emb_type != 1) ||
+        !holo_quant_shape_ok(d.layer_type, d.n_heads * hd, d.dim) ||
+        !holo_quant_shape_ok(d.layer_type, d.dim, d.n_heads * hd) ||
+        !holo_quant_shape_ok(d.layer_type, d.ffn_dim, d.dim) ||
+        !holo_quant_shape_ok(d.layer_type, d.dim, d.ffn_dim) ||
+        !holo_quant_shape_ok(d.out_type, d.vocab, d.dim)) {
+        holo_set_status(HOLO_E_ARG, "holo_model_create: unsupported shape or type");
+        return nullptr;
+    }
+    HoloDevice *D = holo_dev();
+    if (!D) return nullptr;
+    HoloModel *m = new HoloModel();
+    m->d = d;
+    m->q_dim = d.n_heads * hd;
+    m->kv_dim = d.n_kv_heads * hd;
+    m->layers.resize(d.n_layers);
+    m->max_splits = (d.max_seq + m->per_split - 1) / m->per_split;
+    const size_t kv_bytes = (size_t)d.n_layers * d.max_seq * m->kv_dim * (d.kv_f16 ? 2 : 4);
+    bool ok = dev_alloc(&m->kc, kv_bytes) && dev_alloc(&m->vc, kv_bytes);
+    ok = ok && dev_alloc((void **)&m->x, sizeof(float) * d.dim);
+    ok = ok && dev_alloc((void **)&m->qkv, sizeof(float) * (m->q_dim + 2 * m->kv_dim));
+    ok = ok && dev_alloc((void **)&m->att, sizeof(float) * m->q_dim);
+    ok = ok && dev_alloc((void **)&m->h, sizeof(float) * d.ffn_dim);
+    ok = ok && dev_alloc((void **)&m->logits, sizeof(float) * d.vocab);
+    ok = ok && dev_alloc((void **)&m->probs, sizeof(float) * d.vocab);
+    ok = ok && dev_alloc((void **)&m->kept_p, sizeof(float) * d.vocab);
+    ok = ok && dev_alloc((void **)&m->kept_idx, sizeof(int) * d.vocab);
+    ok = ok && dev_alloc((void **)&m->part, sizeof(float) * (size_t)d.n_heads * m->max_splits * (hd + 2));
+    ok = ok && dev_alloc((void **)&m->rvals, sizeof(float) * (d.max_seq + 1));
+    ok = ok && dev_alloc((void **)&m->d_pos, sizeof(int) * 4);
+    ok = ok && dev_alloc((void **)&m->d_seq, sizeof(int) * (d.max_seq + 1));
+    ok = ok && dev_alloc((void **)&m->d_hist, sizeof(int) * (d.max_seq + 1));
+    ok = ok && dev_alloc((void **)&m->d_nhist, sizeof(int) * 4);
+    ok = ok && dev_alloc((void **)&m->d_out, sizeof(int) * (d.max_seq + 1));
+    ok = ok && dev_alloc((void **)&m->d_last, sizeof(int) * 4);
+    if (!ok) {
+        holo_model_free(m);
+        return nullptr;
+    }
+    cudaMemset(m->kc, 0, kv_bytes);
+    cudaMemset(m->vc, 0, kv_bytes);
+    cudaMemset(m->d_pos, 0, sizeof(int) * 4);
+    cudaMemset(m->d_nhist, 0, sizeof(int) * 4);
+    cudaMemset(m->d_seq, 0, sizeof(int) * (d.max_seq + 1));
+    cudaMemset(m->rvals, 0, sizeof(float) * (d.max_seq + 1));
+    cudaDeviceSynchronize();
+    return m;
+}
+
+int holo_model_set_layer(void *model, int l, const float *attn_norm, const void *wq, const void *wk, const void *wv,
+                         const void *wo, const float *ffn_norm, const void *w1, const void *w2, const void *w3) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m || l < 0 || l >= m->d.n_layers || !attn_norm || !wq || !wk || !wv || !wo || !ffn_norm || !w1 || !w2 ||
+        !w3) {
+        holo_set_status(HOLO_E_ARG, "holo_model_set_layer: bad arguments");
+        return HOLO_E_ARG;
+    }
+    const holo_model_desc &d = m->d;
+    const int t = d.layer_type;
+    cudaStream_t st = holo_stream();
+    HoloLayer &L = m->layers[l];
+    drop_graphs(m);
+    if (!L.attn_norm && !upload_plain((void **)&L.attn_norm, attn_norm, sizeof(float) * d.dim, st))
+        return HOLO_E_NOMEM;
+    if (!L.ffn_norm && !upload_plain((void **)&L.ffn_norm, ffn_norm, sizeof(float) * d.dim, st))
+        return HOLO_E_NOMEM;
+    cudaMemcpyAsync(L.attn_norm, attn_norm, sizeof(float) * d.dim, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(L.ffn_norm, ffn_norm, sizeof(float) * d.dim, cudaMemcpyHostToDevice, st);
+    // [Wq; Wk; Wv] in one tiled buffer (each part a whole number of row-blocks)
+    const size_t bq = cuda_quant_tiled_bytes(t, m->q_dim, d.dim), bk = cuda_quant_tiled_bytes(t, m->kv_dim, d.dim);
+    if (!L.wqkv && !dev_alloc((void **)&L.wqkv, bq + 2 * bk)) return HOLO_E_NOMEM;
+    if (!upload_repack(L.wqkv, wq, t, m->q_dim, d.dim, st) ||
+        !upload_repack(L.wqkv + bq, wk, t, m->kv_dim, d.dim, st) ||
+        !upload_repack(L.wqkv + bq + bk, wv, t, m->kv_dim, d.dim, st))
+        return cuda_last_status();
+    L.i_qkv = holo_weight_info(t, m->q_dim + 2 * m->kv_dim, d.dim, holo_q4k_layout());
+    if (!L.wo && !dev_alloc((void **)&L.wo, cuda_quant_tiled_bytes(t, d.dim, m->q_dim))) return HOLO_E_NOMEM;
+    if (!upload_repack(L.wo, wo, t, d.dim, m->q_dim, st)) return cuda_last_status();
+    L.i_o = holo_weight_info(t, d.dim, m->q_dim, holo_q4k_layout());
+    // W1 and W3 interleaved by 16 rows: row-block b = W1 rows 16b..16b+15, W3 rows 16b..16b+15
+    const size_t rb = (size_t)gguf_row_bytes(t, d.dim);
+    std::vector<uint8_t> inter((size_t)2 * d.ffn_dim * rb);
+    for (int b = 0; b < d.ffn_dim / 16; ++b) {
+        memcpy(inter.data() + (size_t)(32 * b) * rb, (const uint8_t *)w1 + (size_t)(16 * b) * rb, 16 * rb);
+        memcpy(inter.data() + (size_t)(32 * b + 16) * rb, (const uint8_t *)w3 + (size_t)(16 * b) * rb, 16 * rb);
+    }
+    if (!L.w13 && !dev_alloc((void **)&L.w13, cuda_quant_tiled_bytes(t, 2 * d.ffn_dim, d.dim))) return HOLO_E_NOMEM;
+    if (!upload_repack(L.w13, inter.data(), t, 2 * d.ffn_dim, d.dim, st)) return cuda_last_status();
+    L.i_13 = holo_weight_info(t, 2 * d.ffn_dim, d.dim, holo_q4k_layout());
+    if (!L.w2 && !dev_alloc((void **)&L.w2, cuda_quant_tiled_bytes(t, d.dim, d.ffn_dim))) return HOLO_E_NOMEM;
+    if (!upload_repack(L.w2, w2, t, d.dim, d.ffn_dim, st)) return cuda_last_status();
+    L.i_2 = holo_weight_info(t, d.dim, d.ffn_dim, holo_q4k_layout());
+    cudaStreamSynchronize(st);
+    L.ready = cuda_last_status() == HOLO_OK;
+    return L.ready ? HOLO_OK : cuda_last_status();
+}
+
+int holo_model_set_globals(void *model, const void *tok_embeddings, const float *final_norm, const void *output) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m || !tok_embeddings || !final_norm || !output) {
+        holo_set_status(HOLO_E_ARG, "holo_model_set_globals: bad arguments");
+        return HOLO_E_ARG;
+    }
+    const holo_model_desc &d = m->d;
+    cudaStream_t st = holo_stream();
+    drop_graphs(m);
+    const size_t eb = (size_t)d.vocab * d.dim * (d.emb_type == 1 ? 2 : 4);
+    if (!m->emb && !dev_alloc(&m->emb, eb)) return HOLO_E_NOMEM;
+    cudaMemcpyAsync(m->emb, tok_embeddings, eb, cudaMemcpyHostToDevice, st);
+    if (!m->final_norm && !dev_alloc((void **)&m->final_norm, sizeof(float) * d.dim)) return HOLO_E_NOMEM;
+    cudaMemcpyAsync(m->final_norm, final_norm, sizeof(float) * d.dim, cudaMemcpyHostToDevice, st);
+    if (!m->out && !dev_alloc((void **)&m->out, cuda_quant_tiled_bytes(d.out_type, d.vocab, d.dim)))
+        return HOLO_E_NOMEM;
+    if (!upload_repack(m->out, output, d.out_type, d.vocab, d.dim, st)) return cuda_last_status();
+    m->i_out = holo_weight_info(d.out_type, d.vocab, d.dim, holo_q4k_layout());
+    cudaStreamSynchronize(st);
+    m->globals_ready = cuda_last_status() == HOLO_OK;
+    return m->globals_ready ? HOLO_OK : cuda_last_status();
+}
+
+int holo_model_forward(void *model, int token, float *logits) {
+    HoloModel *m = (HoloModel *)model;
+    if (!model_ready(m)) return HOLO_E_ARG;
+    if (m->h_pos >= m->d.max_seq || token < 0 || token >= m->d.vocab) {
+        holo_set_status(HOLO_E_ARG, "holo_model_forward: position past max_seq or token out of range");
+        return HOLO_E_ARG;
+    }
+    cudaStream_t st = holo_stream();
+    dec_set_token_kernel<<<1, 1, 0, st>>>(m->d_seq, m->d_pos, token);
+    if (!m->g_forward) {
+        SampleArgs none{};
+        m->g_forward = capture_step(m, false, none);
+        if (!m->g_forward) return cuda_last_status();
+    }
+    if (cudaGraphLaunch(m->g_forward, st) != cudaSuccess) {
+        holo_check_launch("holo_model_forward: graph launch");
+        return cuda_last_status();
+    }
+    m->h_pos++;
+    if (logits) {
+        if (cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->d.vocab, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            holo_check_launch("holo_model_forward: logits copy");
+        cudaStreamSynchronize(st);
+    }
+    return cuda_last_status();
+}
+
+int holo_model_load_logits(void *model, const float *logits) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m || !logits) {
+        holo_set_status(HOLO_E_ARG, "holo_model_load_logits: bad arguments");
+        return HOLO_E_ARG;
+    }
+    cudaStream_t st = holo_stream();
+    if (cudaMemcpyAsync(m->logits, logits, sizeof(float) * m->d.vocab, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        holo_check_launch("holo_model_load_logits");
+    cudaStreamSynchronize(st);
+    return cuda_last_status();
+}
+
+int holo_model_push_token(void *model, int token) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m || m->h_nhist >= m->d.max_seq) {
+        holo_set_status(HOLO_E_ARG, "holo_model_push_token: history full");
+        return HOLO_E_ARG;
+    }
+    dec_push_kernel<<<1, 1, 0, holo_stream()>>>(m->d_hist, m->d_nhist, token);
+    m->h_nhist++;
+    return holo_check_launch("holo_model_push_token") ? HOLO_OK : cuda_last_status();
+}
+
+int holo_model_sample(void *model, const holo_sampler_desc *s, float r) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m || !s) {
+        holo_set_status(HOLO_E_ARG, "holo_model_sample: bad arguments");
+        return -1;
+    }
+    cudaStream_t st = holo_stream();
+    HoloDevice *D = holo_dev();
+    SampleArgs a = make_args(m, s);
+    a.gen = 0;
+    cudaMemcpyAsync(m->rvals, &r, sizeof(float), cudaMemcpyHostToDevice, st);
+    launch_pdl(dec_sample_kernel, dim3(1), dim3(SM_THREADS), st, false, m->logits, m->probs, m->kept_idx, m->kept_p,
+               m->d_seq, m->d_hist, m->d_nhist, (const int *)m->d_pos, (const float *)m->rvals, m->d_out,
+               m->d_last, D ? D->status : nullptr, a);
+    int tok = -1;
+    cudaMemcpyAsync(&tok, m->d_last, sizeof(int), cudaMemcpyDeviceToHost, st);
+    cudaStreamSynchronize(st);
+    return cuda_last_status() == HOLO_OK ? tok : -1;
+}
+
+int holo_model_generate(void *model, const int *prompt, int n_prompt, int n_new, const holo_sampler_desc *s,
+                        int seed, int *out) {
+    HoloModel *m = (HoloModel *)model;
+    if (!model_ready(m) || !prompt || !s || !out || n_prompt <= 0 || n_new <= 0 ||
+        n_prompt + n_new > m->d.max_seq) {
+        holo_set_status(HOLO_E_ARG, "holo_model_generate: bad arguments");
+        return -1;
+    }
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= m->d.vocab) {
+            holo_set_status(HOLO_E_ARG, "holo_model_generate: prompt token out of range");
+            return -1;
+        }
+    cudaStream_t st = holo_stream();
+    // llm_generate (llm.c:1340-1420): srand(seed); one rand() per sampled token
+    // when T != 0 (llm.c:1318-1321)
+    std::vector<float> r(n_new, 0.0f);
+    srand((unsigned)seed);
+    if (s->temperature != 0.0f)
+        for (int i = 0; i < n_new; ++i) r[i] = (float)rand() / RAND_MAX;
+    holo_model_reset(m);
+    cudaMemcpyAsync(m->rvals, r.data(), sizeof(float) * n_new, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(m->d_seq, prompt, sizeof(int) * n_prompt, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(m->d_hist, prompt, sizeof(int) * n_prompt, cudaMemcpyHostToDevice, st);
+    const int nh = n_prompt;
+    cudaMemcpyAsync(m->d_nhist, &nh, sizeof(int), cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
+    SampleArgs a = make_args(m, s);
+    a.gen = 1;
+    a.n_prompt = n_prompt;
+    if (m->g_gen && memcmp(&a, &m->gen_args, sizeof(a)) != 0) {
+        cudaGraphExecDestroy(m->g_gen);
+        m->g_gen = nullptr;
+    }
+    if (!m->g_gen) {
+        m->g_gen = capture_step(m, true, a);
+        if (!m->g_gen) return -1;
+        m->gen_args = a;
+    }
+    const int steps = n_prompt + n_new - 1;
+    for (int i = 0; i < steps; ++i)
+        if (cudaGraphLaunch(m->g_gen, st) != cudaSuccess) {
+            holo_check_launch("holo_model_generate: graph launch");
+            return -1;
+        }
+    cudaMemcpyAsync(out, m->d_out, sizeof(int) * n_new, cudaMemcpyDeviceToHost, st);
+    cudaStreamSynchronize(st);
+    m->h_pos = steps;
+    m->h_nhist = n_prompt + n_new;
+    return cuda_last_status() == HOLO_OK ? n_new : -1;
+}
+
+int holo_model_launch_steps(void *model, int n_steps) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m || !m->g_gen || n_steps < 0 || m->h_pos + n_steps > m->d.max_seq - 1) {
+        holo_set_status(HOLO_E_ARG, "holo_model_launch_steps: no generation graph or past max_seq");
+        return HOLO_E_ARG;
+    }
+    cudaStream_t st = holo_stream();
+    for (int i = 0; i < n_steps; ++i)
+        if (cudaGraphLaunch(m->g_gen, st) != cudaSuccess) {
+            holo_check_launch("holo_model_launch_steps");
+            return cuda_last_status();
+        }
+    m->h_pos += n_steps;
+    return HOLO_OK;
+}
+
+int holo_model_pos(void *model) { return model ? ((HoloModel *)model)->h_pos : -1; }
+
+void holo_model_reset(void *model) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m) return;
+    cudaStream_t st = holo_stream();
+    cudaMemsetAsync(m->d_pos, 0, sizeof(int), st);
+    cudaMemsetAsync(m->d_nhist, 0, sizeof(int), st);
+    cudaStreamSynchronize(st);
+    m->h_pos = 0;
+    m->h_nhist = 0;
+}
+
+void holo_model_free(void *model) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m) return;
+    cudaDeviceSynchronize();
+    drop_graphs(m);
+    for (auto &L : m->layers) {
+        cudaFree(L.attn_norm); cudaFree(L.ffn_norm); cudaFree(L.wqkv); cudaFree(L.wo); cudaFree(L.w13);
+        cudaFree(L.w2);
+    }
+    void *bufs[] = {m->emb, m->final_norm, m->out, m->kc, m->vc, m->x, m->qkv, m->att, m->h, m->logits,
+                    m->part, m->probs, m->kept_p, m->rvals, m->kept_idx, m->d_pos, m->d_seq, m->d_hist,
+                    m->d_nhist, m->d_out, m->d_last};
+    for (void *p : bufs) cudaFree(p);
+    delete m;
+}
+
+}  // extern "C"

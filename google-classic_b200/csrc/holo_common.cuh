@@ -145,6 +145,12 @@ struct WeightInfo {
     size_t bytes = 0;
 };
 bool holo_registry_find(const void *ptr, WeightInfo *out);
+// repack.cu: shape check, geometry, and repack of raw device blocks into a
+// caller-provided buffer of cuda_quant_tiled_bytes() bytes (no allocation)
+bool holo_quant_shape_ok(int ggml_type, int rows, int cols);
+WeightInfo holo_weight_info(int ggml_type, int rows, int cols, int q4k_layout);
+bool holo_repack_to(void *dst, const void *dev_blocks, int ggml_type, int rows, int cols, int q4k_layout,
+                    cudaStream_t st);
 void holo_registry_add(const void *ptr, const WeightInfo &info);
 bool holo_registry_remove(const void *ptr);
 

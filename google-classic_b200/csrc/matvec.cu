@@ -460,8 +460,29 @@ __global__ void __launch_bounds__(NTHREADS, MIN_CTAS_PER_SM) mv_tiled_kernel(con
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
+// kernel attributes (dynamic shared memory limit, carveout), once per device
+template <int TYPE, int ACT, int EPI, bool NORM>
+bool configure_tiled() {
+    auto kern = mv_tiled_kernel<TYPE, ACT, EPI, NORM>;
+    static bool configured[16] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 16 || configured[dev]) return true;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_LIMIT) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
+        holo_check_launch("tiled matvec: kernel attributes");
+        return false;
+    }
+    configured[dev] = true;
+    return true;
+}
+
+// max_ctas == 0: set-up only (holo_matvec_prepare)
 template <int TYPE, int ACT, int EPI, bool NORM>
 bool launch_tiled(const MvParams &base, int sms, int max_ctas, bool pdl, cudaStream_t st) {
+    if (!configure_tiled<TYPE, ACT, EPI, NORM>()) return false;
+    if (max_ctas == 0) return true;
     MvParams p = base;
     if ((unsigned long long)p.total_units * (unsigned long long)max_ctas >= (1ull << 32)) {
         holo_set_status(HOLO_E_UNSUPPORTED, "tiled matvec: too many units");
@@ -483,18 +504,6 @@ bool launch_tiled(const MvParams &base, int sms, int max_ctas, bool pdl, cudaStr
         p.nctas = min(min(p.total_units, max_ctas), p.nctas + sms);
     }
     auto kern = mv_tiled_kernel<TYPE, ACT, EPI, NORM>;
-    static bool configured[16] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 16 && !configured[dev]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_LIMIT) != cudaSuccess ||
-            cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
-            holo_check_launch("tiled matvec: smem attribute");
-            return false;
-        }
-        configured[dev] = true;
-    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.nctas);
     cfg.blockDim = dim3(NTHREADS);
@@ -547,6 +556,13 @@ bool holo_matvec_launch(const void *M, const WeightInfo &wi, const MvLaunch &L, 
     S.max_ctas = MV_MAX_CTAS;
     S.max_rowblocks = MV_MAX_ROWBLOCKS;
     return holo_matvec_launch_with(M, wi, L, st, S);
+}
+
+bool holo_matvec_prepare(const WeightInfo &wi, const MvLaunch &L) {
+    MvScratch S;   // max_ctas == 0: set-up only, nothing is launched
+    S.sms = 1;
+    S.max_rowblocks = MV_MAX_ROWBLOCKS;
+    return holo_matvec_launch_with(nullptr, wi, L, nullptr, S);
 }
 
 bool holo_matvec_launch_with(const void *M, const WeightInfo &wi, const MvLaunch &L, cudaStream_t st,

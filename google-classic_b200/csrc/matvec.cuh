@@ -31,6 +31,9 @@ struct MvScratch {
 
 // launch on the current device's state (initialises it on first use)
 bool holo_matvec_launch(const void *M, const WeightInfo &wi, const MvLaunch &L, cudaStream_t st);
+// one-time set-up (kernel attributes) of the variant a launch of L on wi uses;
+// call before capturing such a launch into a graph
+bool holo_matvec_prepare(const WeightInfo &wi, const MvLaunch &L);
 // launch with caller-provided scratch; touches no per-device state
 bool holo_matvec_launch_with(const void *M, const WeightInfo &wi, const MvLaunch &L, cudaStream_t st,
                              const MvScratch &S);

@@ -88,23 +88,64 @@ __global__ void repack_q4_k_kernel(uint8_t *__restrict__ out, const uint8_t *__r
     }
 }
 
-bool check_shape(int type, int rows, int cols) {
+}  // namespace
+
+bool holo_quant_shape_ok(int type, int rows, int cols) {
     if (rows <= 0 || cols <= 0) return false;
     if (type == GT_Q4_K) return cols % 256 == 0;
     if (type == GT_Q8_0 || type == GT_Q4_0) return cols % 32 == 0;
     return false;
 }
 
-}  // namespace
-
 extern "C" size_t cuda_quant_tiled_bytes(int ggml_type, int rows, int cols) {
-    if (!check_shape(ggml_type, rows, cols)) return 0;
+    if (!holo_quant_shape_ok(ggml_type, rows, cols)) return 0;
     size_t nrb = (size_t)(rows + TILE_ROWS - 1) / TILE_ROWS;
     return nrb * (size_t)units_per_row(ggml_type, cols) * (size_t)unit_bytes(ggml_type);
 }
 
+bool holo_repack_to(void *dst, const void *dev_blocks, int ggml_type, int rows, int cols, int q4k_layout,
+                    cudaStream_t st) {
+    if (!holo_quant_shape_ok(ggml_type, rows, cols) || !dev_blocks || !dst) {
+        holo_set_status(HOLO_E_ARG, "repack: unsupported type or shape");
+        return false;
+    }
+    const size_t bytes = cuda_quant_tiled_bytes(ggml_type, rows, cols);
+    cudaMemsetAsync(dst, 0, bytes, st);   // padding rows and blocks are zero
+    const int units = units_per_row(ggml_type, cols);
+    const int threads = 256;
+    if (ggml_type == GT_Q8_0) {
+        int nblk = cols / 32;
+        int64_t n = (int64_t)rows * nblk;
+        repack_q8_0_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
+            (uint8_t *)dst, (const uint8_t *)dev_blocks, rows, nblk, units);
+    } else if (ggml_type == GT_Q4_0) {
+        int nblk = cols / 32;
+        int64_t n = (int64_t)rows * nblk;
+        repack_q4_0_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
+            (uint8_t *)dst, (const uint8_t *)dev_blocks, rows, nblk, units);
+    } else {
+        int nsb = cols / 256;
+        int64_t n = (int64_t)rows * nsb;
+        repack_q4_k_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
+            (uint8_t *)dst, (const uint8_t *)dev_blocks, rows, nsb, q4k_layout == HOLO_Q4K_GGML);
+    }
+    return holo_check_launch("repack kernel");
+}
+
+WeightInfo holo_weight_info(int ggml_type, int rows, int cols, int q4k_layout) {
+    WeightInfo wi;
+    wi.type = ggml_type;
+    wi.rows = rows;
+    wi.cols = cols;
+    wi.rows_padded = (rows + TILE_ROWS - 1) / TILE_ROWS * TILE_ROWS;
+    wi.units = units_per_row(ggml_type, cols);
+    wi.q4k_layout = q4k_layout;
+    wi.bytes = cuda_quant_tiled_bytes(ggml_type, rows, cols);
+    return wi;
+}
+
 extern "C" void *cuda_repack_quant(const void *dev_blocks, int ggml_type, int rows, int cols) {
-    if (!check_shape(ggml_type, rows, cols) || !dev_blocks) {
+    if (!holo_quant_shape_ok(ggml_type, rows, cols) || !dev_blocks) {
         holo_set_status(HOLO_E_ARG, "cuda_repack_quant: unsupported type or shape");
         return nullptr;
     }
@@ -118,41 +159,17 @@ extern "C" void *cuda_repack_quant(const void *dev_blocks, int ggml_type, int ro
         holo_set_status(HOLO_E_NOMEM, "cuda_repack_quant: allocation");
         return nullptr;
     }
-    cudaMemsetAsync(out, 0, bytes, st);   // padding rows and blocks are zero
-    int layout = holo_q4k_layout();
-    const int units = units_per_row(ggml_type, cols);
-    const int threads = 256;
-    if (ggml_type == GT_Q8_0) {
-        int nblk = cols / 32;
-        int64_t n = (int64_t)rows * nblk;
-        repack_q8_0_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
-            (uint8_t *)out, (const uint8_t *)dev_blocks, rows, nblk, units);
-    } else if (ggml_type == GT_Q4_0) {
-        int nblk = cols / 32;
-        int64_t n = (int64_t)rows * nblk;
-        repack_q4_0_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
-            (uint8_t *)out, (const uint8_t *)dev_blocks, rows, nblk, units);
-    } else {
-        int nsb = cols / 256;
-        int64_t n = (int64_t)rows * nsb;
-        repack_q4_k_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
-            (uint8_t *)out, (const uint8_t *)dev_blocks, rows, nsb, layout == HOLO_Q4K_GGML);
+    const int layout = holo_q4k_layout();
+    if (!holo_repack_to(out, dev_blocks, ggml_type, rows, cols, layout, st)) {
+        cudaFree(out);
+        return nullptr;
     }
-    if (!holo_check_launch("repack kernel")) { cudaFree(out); return nullptr; }
-    WeightInfo wi;
-    wi.type = ggml_type;
-    wi.rows = rows;
-    wi.cols = cols;
-    wi.rows_padded = (rows + TILE_ROWS - 1) / TILE_ROWS * TILE_ROWS;
-    wi.units = units;
-    wi.q4k_layout = layout;
-    wi.bytes = bytes;
-    holo_registry_add(out, wi);
+    holo_registry_add(out, holo_weight_info(ggml_type, rows, cols, layout));
     return out;
 }
 
 extern "C" void *cuda_upload_quant(const void *host_blocks, int ggml_type, int rows, int cols) {
-    if (!check_shape(ggml_type, rows, cols) || !host_blocks) {
+    if (!holo_quant_shape_ok(ggml_type, rows, cols) || !host_blocks) {
         holo_set_status(HOLO_E_ARG, "cuda_upload_quant: unsupported type or shape");
         return nullptr;
     }

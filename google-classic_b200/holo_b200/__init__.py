@@ -85,6 +85,16 @@ SIGNATURES = {
     "cuda_set_pdl": (None, [_i]), "cuda_get_pdl": (_i, []),
     "cuda_capture_begin": (_i, []), "cuda_capture_end": (_vp, []),
     "cuda_graph_launch": (None, [_vp]), "cuda_graph_free": (None, [_vp]),
+    "holo_model_create": (_vp, [_vp]),
+    "holo_model_set_layer": (_i, [_vp, _i] + [_vp] * 9),
+    "holo_model_set_globals": (_i, [_vp, _vp, _vp, _vp]),
+    "holo_model_forward": (_i, [_vp, _i, _vp]),
+    "holo_model_load_logits": (_i, [_vp, _vp]),
+    "holo_model_push_token": (_i, [_vp, _i]),
+    "holo_model_sample": (_i, [_vp, _vp, _f]),
+    "holo_model_generate": (_i, [_vp, _vp, _i, _i, _vp, _i, _vp]),
+    "holo_model_launch_steps": (_i, [_vp, _i]),
+    "holo_model_pos": (_i, [_vp]), "holo_model_reset": (None, [_vp]), "holo_model_free": (None, [_vp]),
 }
 
 _LIB = None

@@ -132,3 +132,33 @@ def quantize(w: np.ndarray, gtype: int) -> np.ndarray:
     if gtype == F16:
         return w.astype(np.float16).view(np.uint8).reshape(-1)
     raise ValueError(f"no quantizer for type {gtype}")
+
+
+# ---------------------------------------------------------------------------
+# random-init Llama-shape models (weights N(0, std) quantized round-to-nearest)
+# ---------------------------------------------------------------------------
+def llama_weights(cfg: dict, seed: int, std: float = 0.02) -> dict:
+    """Host arrays of a random-init model of shape cfg (keys of
+    holo_b200.model.ModelDesc): GGUF blocks of cfg['layer_type'] for the seven
+    layer matrices, fp16 (emb_type 1) or fp32 token embeddings, output
+    matrix of cfg['out_type'], RMSNorm weights 1.0."""
+    rng = _rng(seed)
+    dim, hd, nh, nkv, ffn, V = (cfg[k] for k in ("dim", "head_dim", "n_heads", "n_kv_heads", "ffn_dim", "vocab"))
+    q_dim, kv_dim = nh * hd, nkv * hd
+    lt, ot = cfg["layer_type"], cfg["out_type"]
+
+    def mat(rows, cols, t):
+        return quantize(rng.normal(0.0, std, size=(rows, cols)).astype(np.float32), t)
+
+    layers = []
+    for _ in range(cfg["n_layers"]):
+        layers.append({
+            "attn_norm": np.ones(dim, np.float32), "ffn_norm": np.ones(dim, np.float32),
+            "wq": mat(q_dim, dim, lt), "wk": mat(kv_dim, dim, lt), "wv": mat(kv_dim, dim, lt),
+            "wo": mat(dim, q_dim, lt), "w1": mat(ffn, dim, lt), "w2": mat(dim, ffn, lt), "w3": mat(ffn, dim, lt),
+        })
+    emb = rng.normal(0.0, std, size=(V, dim)).astype(np.float32)
+    if cfg.get("emb_type", 1) == 1:
+        emb = emb.astype(np.float16)
+    return {"layers": layers, "tok_emb": np.ascontiguousarray(emb), "final_norm": np.ones(dim, np.float32),
+            "output": mat(V, dim, ot)}

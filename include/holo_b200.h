@@ -116,6 +116,68 @@ int cuda_init_rank(int local_rank, int world_size);
 /* Number of SMs of the current device (grid sizing). */
 int cuda_sm_count(void);
 
+/* ---- batch-1 decode engine ----------------------------------------------------
+ * The decode call sequence of the reference -- llm_forward for one token
+ * (src/ai/llm.c:1015-1269; its GPU twin llm_forward_cuda, llm_cuda.c:558-946)
+ * and llm_sample (llm.c:1281-1328) -- as one model object whose token step is
+ * a single CUDA graph: RMSNorm fused into the QKV, gate/up and output
+ * matvecs, [Wq;Wk;Wv] and [W1;W3] each one weight, residual adds and SwiGLU
+ * in matvec epilogues, the KV cache resident on the device, and the sampler on
+ * the device.  Weights are given as host pointers to GGUF blocks laid out as
+ * the reference loader reads them (row-major, rows of in-dim values). */
+typedef struct {
+    int n_layers, dim, n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_seq;
+    float rope_base;     /* RoPE frequency base (llm_config_t.rope_freq_base) */
+    float eps;           /* RMSNorm epsilon */
+    int layer_type;      /* GGUF type of wq wk wv wo w1 w2 w3: 8 Q8_0, 2 Q4_0, 12 Q4_K */
+    int emb_type;        /* token embeddings: 0 F32, 1 F16 */
+    int out_type;        /* GGUF type of the output (lm_head) matrix */
+    int kv_f16;          /* 1: fp16 KV cache, 0: fp32 (the reference's) */
+    int act_mode;        /* HOLO_ACT_Q8 or HOLO_ACT_F32 for every matvec */
+} holo_model_desc;
+
+typedef struct {         /* llm_sampler_t (src/ai/llm.h:167-174) without the seed */
+    float temperature;   /* 0: greedy */
+    float top_p;         /* in (0,1): nucleus; otherwise off */
+    int top_k;           /* > 0: top-k; 0: off */
+    float repeat_penalty;
+    int repeat_last_n;
+} holo_sampler_desc;
+
+/* NULL on failure (status set).  head_dim 64/128/256, ffn_dim % 16 == 0. */
+void *holo_model_create(const holo_model_desc *desc);
+/* Layer weights: attn_norm/ffn_norm fp32 [dim]; wq [n_heads*hd][dim], wk wv
+ * [n_kv_heads*hd][dim], wo [dim][n_heads*hd], w1 w3 [ffn][dim], w2 [dim][ffn]. */
+int holo_model_set_layer(void *model, int layer, const float *attn_norm, const void *wq, const void *wk,
+                         const void *wv, const void *wo, const float *ffn_norm, const void *w1, const void *w2,
+                         const void *w3);
+/* tok_embeddings [vocab][dim] (emb_type), final_norm [dim], output [vocab][dim]. */
+int holo_model_set_globals(void *model, const void *tok_embeddings, const float *final_norm, const void *output);
+/* One position (llm_forward with n_tokens = 1): token at the current position,
+ * position + 1; logits (host, vocab floats) copied out when not NULL. */
+int holo_model_forward(void *model, int token, float *logits);
+/* Replace the current logits (vocab host floats), e.g. to sample logits
+ * computed elsewhere. */
+int holo_model_load_logits(void *model, const float *logits);
+/* Append a token to the repetition-penalty history (ctx->tokens). */
+int holo_model_push_token(void *model, int token);
+/* llm_sample on the current logits and history with the uniform draw r
+ * ((float)rand() / RAND_MAX in the reference); returns the token, -1 on error.
+ * The logits are modified in place by temperature and penalty, as there. */
+int holo_model_sample(void *model, const holo_sampler_desc *s, float r);
+/* llm_generate without tokenizer and EOS: reset, prefill the prompt, then
+ * n_new sample + forward steps, all as graph replays; srand(seed) and one
+ * rand() per sampled token when temperature != 0.  out[n_new]; returns n_new
+ * or -1. */
+int holo_model_generate(void *model, const int *prompt, int n_prompt, int n_new, const holo_sampler_desc *s,
+                        int seed, int *out);
+/* Replays n more steps of the last holo_model_generate's graph without
+ * synchronising (for timing); the sampled tokens past n_new are discarded. */
+int holo_model_launch_steps(void *model, int n_steps);
+int holo_model_pos(void *model);
+void holo_model_reset(void *model);
+void holo_model_free(void *model);
+
 /* ---- CUDA graphs of the library stream --------------------------------------
  * The reference launches every op separately on the legacy stream
  * (src/ai/llm_cuda.c:558-946, ~13 launches per layer).  Calls made between

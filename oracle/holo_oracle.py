@@ -143,3 +143,71 @@ class Reference:
         out = np.empty((rows, cols), np.float32)
         getattr(self.lib, name)(_ptr(blocks), _ptr(out), rows * cols)
         return out
+
+
+class RefModel:
+    """A model in the reference engine's own structs (oracle/ref_harness.c),
+    run by its llm_forward (src/ai/llm.c:1015) and llm_sample (llm.c:1281).
+    `w` holds the host arrays of holo_b200.synth.llama_weights; they are kept
+    alive here because the reference reads them in place."""
+
+    def __init__(self, ref: Reference, cfg: dict, w: dict):
+        self.lib = ref.lib
+        self.cfg = cfg
+        self.w = w
+        self.h = self.lib.href_model_create(cfg["n_layers"], cfg["dim"], cfg["n_heads"], cfg["n_kv_heads"],
+                                            cfg["head_dim"], cfg["ffn_dim"], cfg["vocab"], cfg["max_seq"],
+                                            cfg.get("rope_base", 10000.0), cfg.get("eps", 1e-5))
+        self.lib.href_model_set_types(self.h, cfg["layer_type"], cfg.get("emb_type", 1), cfg["out_type"])
+        for l, L in enumerate(w["layers"]):
+            self.lib.href_model_set_layer(self.h, l, _ptr(L["attn_norm"]), _ptr(L["wq"]), _ptr(L["wk"]),
+                                          _ptr(L["wv"]), _ptr(L["wo"]), _ptr(L["ffn_norm"]), _ptr(L["w1"]),
+                                          _ptr(L["w2"]), _ptr(L["w3"]))
+        self.lib.href_model_set_globals(self.h, _ptr(w["tok_emb"]), _ptr(w["final_norm"]), _ptr(w["output"]))
+        self.libc = C.CDLL(None)
+        self.libc.rand.restype = _i
+
+    def forward(self, token: int) -> np.ndarray:
+        assert self.lib.href_forward(self.h, int(token)) == 0
+        return np.ctypeslib.as_array(self.lib.href_logits(self.h), shape=(self.cfg["vocab"],)).copy()
+
+    def set_logits(self, logits: np.ndarray):
+        dst = np.ctypeslib.as_array(self.lib.href_logits(self.h), shape=(self.cfg["vocab"],))
+        dst[:] = np.asarray(logits, np.float32)
+
+    def push(self, token: int):
+        self.lib.href_push_token(self.h, int(token))
+
+    def sample(self, temperature, top_p, top_k, penalty, last_n) -> int:
+        return self.lib.href_sample(self.h, temperature, top_p, top_k, penalty, last_n)
+
+    def srand(self, seed: int):
+        self.libc.srand(C.c_uint(seed))
+
+    def rand_r(self) -> float:
+        """(float)rand() / RAND_MAX, as llm_sample draws it (llm.c:1320)."""
+        return float(np.float32(np.float32(self.libc.rand()) / np.float32(2147483647)))
+
+    def reset(self):
+        self.lib.href_reset(self.h)
+
+    def generate(self, prompt, n_new, temperature, top_p, top_k, penalty, last_n, seed):
+        """llm_generate's loop (llm.c:1340-1420) without tokenizer or EOS."""
+        self.srand(seed)
+        self.reset()
+        for t in prompt:
+            self.push(t)
+        for t in prompt:
+            self.forward(t)
+        out = []
+        for _ in range(n_new):
+            tok = self.sample(temperature, top_p, top_k, penalty, last_n)
+            out.append(tok)
+            self.push(tok)
+            self.forward(tok)
+        return np.array(out, np.int32)
+
+    def close(self):
+        if self.h:
+            self.lib.href_model_free(self.h)
+            self.h = None

@@ -1,0 +1,139 @@
+"""Decode engine (holo_model_*, csrc/decode.cu) against the reference engine's
+own llm_forward / llm_sample / llm_generate loop (oracle/ref_harness.c) on a
+small random-init model with the 7B layer structure (GQA, SwiGLU, Q4_K
+layers, fp16 embeddings, Q8_0 output).
+
+Bars (fixed here):
+* HOLO_ACT_F32 with an fp32 KV cache (the reference's arithmetic): logits
+  within 1e-2 absolute and 1e-3 norm-wise relative at every position; greedy
+  token stream identical for 64 steps; sampled stream (T 0.8, top-k 40,
+  top-p 0.95, penalty 1.1) identical for 32 steps.
+* The device sampler on identical logits and the same uniform draw returns
+  the reference's token.
+* HOLO_ACT_Q8 with an fp16 KV cache (the bench configuration): logits within
+  the bound stated in test_q8_fp16_kv_logits_close.
+"""
+import numpy as np
+import pytest
+
+import holo_b200 as hb
+from holo_b200 import synth
+from holo_b200.model import Model, SamplerDesc
+from conftest import rel_err
+from holo_oracle import RefModel
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(n_layers=2, dim=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn_dim=768, vocab=1000, max_seq=160,
+           rope_base=10000.0, eps=1e-5, layer_type=hb.Q4_K, emb_type=1, out_type=hb.Q8_0)
+
+
+@pytest.fixture(scope="module")
+def weights():
+    return synth.llama_weights(CFG, seed=11)
+
+
+@pytest.fixture(scope="module")
+def ref_model(reference, weights):
+    m = RefModel(reference, CFG, weights)
+    yield m
+    m.close()
+
+
+def make_model(dev, weights, act, kv_f16):
+    m = Model(CFG, act_mode=act, kv_f16=kv_f16)
+    m.set_weights(weights)
+    return m
+
+
+def prompt(n, seed):
+    return np.random.default_rng(seed).integers(0, CFG["vocab"], size=n).astype(np.int32)
+
+
+def test_forward_logits_match_reference_f32(dev, weights, ref_model):
+    m = make_model(dev, weights, hb.ACT_F32, kv_f16=False)
+    ref_model.reset()
+    worst_abs, worst_rel = 0.0, 0.0
+    for t in prompt(40, 1):
+        y = m.forward(t)
+        r = ref_model.forward(t)
+        worst_abs = max(worst_abs, float(np.abs(y - r).max()))
+        worst_rel = max(worst_rel, rel_err(y, r))
+    print(f"f32 logits: max abs {worst_abs:.3e}, max rel {worst_rel:.3e}")
+    assert worst_abs <= 1e-2 and worst_rel <= 1e-3
+    m.close()
+
+
+def test_greedy_stream_identical_64_steps(dev, weights, ref_model):
+    m = make_model(dev, weights, hb.ACT_F32, kv_f16=False)
+    p = prompt(16, 2)
+    s = SamplerDesc(0.0, 0.95, 40, 1.1, 64)
+    got = m.generate(p, 64, s, seed=5)
+    want = ref_model.generate(p, 64, 0.0, 0.95, 40, 1.1, 64, seed=5)
+    # top-1/top-2 margins of the reference's penalised logits, so a near tie is visible
+    print("greedy tokens equal:", np.array_equal(got, want), "first difference:",
+          int(np.argmax(got != want)) if not np.array_equal(got, want) else None)
+    assert np.array_equal(got, want)
+    m.close()
+
+
+def test_sampled_stream_identical_32_steps(dev, weights, ref_model):
+    m = make_model(dev, weights, hb.ACT_F32, kv_f16=False)
+    p = prompt(16, 3)
+    s = SamplerDesc(0.8, 0.95, 40, 1.1, 64)
+    got = m.generate(p, 32, s, seed=7)
+    want = ref_model.generate(p, 32, 0.8, 0.95, 40, 1.1, 64, seed=7)
+    assert np.array_equal(got, want), (got, want)
+    m.close()
+
+
+@pytest.mark.parametrize("temperature,top_p,top_k,penalty", [
+    (0.8, 0.95, 40, 1.1), (1.0, 0.9, 40, 1.0), (0.5, 0.5, 10, 1.3), (1.3, 1.0, 40, 1.1),
+    (0.7, 0.9, 0, 1.1), (0.0, 0.95, 40, 1.1),
+])
+def test_sampler_matches_reference_on_same_logits(dev, weights, ref_model, temperature, top_p, top_k, penalty):
+    m = make_model(dev, weights, hb.ACT_F32, kv_f16=False)
+    rng = np.random.default_rng(int(temperature * 100 + top_k))
+    hist = rng.integers(0, CFG["vocab"], size=80).astype(np.int32)
+    ref_model.reset()
+    for t in hist:
+        m.push_token(t)
+        ref_model.push(t)
+    for trial in range(40):
+        logits = (rng.standard_normal(CFG["vocab"]) * rng.uniform(0.5, 4.0)).astype(np.float32)
+        m.load_logits(logits)
+        ref_model.set_logits(logits)
+        seed = 1000 + trial
+        ref_model.srand(seed)
+        r = ref_model.rand_r()
+        got = m.sample(SamplerDesc(temperature, top_p, top_k, penalty, 64), r)
+        ref_model.srand(seed)
+        want = ref_model.sample(temperature, top_p, top_k, penalty, 64)
+        assert got == want, (trial, got, want)
+    m.close()
+
+
+def test_q8_fp16_kv_logits_close(dev, weights, ref_model):
+    """The bench configuration.  Activations quantized to int8 per 32 values
+    (relative error ~0.4 % per matvec input) and an fp16 cache move the logits
+    away from the fp32 reference; the bound is 5 % of the largest logit
+    magnitude, norm-wise."""
+    m = make_model(dev, weights, hb.ACT_Q8, kv_f16=True)
+    ref_model.reset()
+    worst = 0.0
+    for t in prompt(24, 4):
+        y = m.forward(t)
+        r = ref_model.forward(t)
+        worst = max(worst, rel_err(y, r))
+    print(f"q8/fp16-kv logits: max norm-wise rel {worst:.3e}")
+    assert worst <= 5e-2
+    m.close()
+
+
+def test_forward_rejects_bad_token(dev, weights):
+    m = make_model(dev, weights, hb.ACT_Q8, kv_f16=True)
+    dev.lib.cuda_clear_status()
+    rc = dev.lib.holo_model_forward(m.h, CFG["vocab"], None)
+    assert rc == hb.HOLO_E_ARG
+    dev.lib.cuda_clear_status()
+    m.close()
