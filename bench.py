@@ -266,6 +266,10 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(mats, bytes_step, budget_s=args.cpu_budget)
 
+    decode = None
+    if not args.no_decode:
+        decode = decode_bench(args, world, rank, torch)
+
     traffic = read_traffic()
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -287,6 +291,8 @@ def run_ours(args, rank, world, local_rank):
         "other_act_mode": {"act": other, "value": round(world * bytes_step / (ms_other * 1e-3) / 1e9, 2),
                            "ms_per_step": round(ms_other, 5)},
     }
+    if decode:
+        line["decode"] = decode
     if ref_gpu:
         line["reference_gpu_kernels"] = ref_gpu
     if cpu:
@@ -370,6 +376,102 @@ def cpu_baseline(mats, bytes_step, budget_s):
 
 
 # ---------------------------------------------------------------------------
+# batch-1 decode of the Llama-2-7B-shape Q4_K model
+# ---------------------------------------------------------------------------
+DECODE_PROMPT, DECODE_NEW = 128, 256
+
+
+def decode_bytes_per_token(cfg, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW, kv_bytes=2):
+    """Algorithmic HBM bytes per generated token: every layer matrix and the
+    output matrix in GGUF packing, one embedding row, and the K and V rows of
+    every cached position (mean over the decode positions)."""
+    dim, ffn, V = cfg["dim"], cfg["ffn_dim"], cfg["vocab"]
+    q_dim, kv_dim = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
+    lt = cfg["layer_type"]
+    layer = (hb.row_bytes(lt, dim) * (q_dim + 2 * kv_dim + 2 * ffn) + hb.row_bytes(lt, q_dim) * dim
+             + hb.row_bytes(lt, ffn) * dim)
+    weights = cfg["n_layers"] * layer + hb.row_bytes(cfg["out_type"], dim) * V + dim * 2
+    mean_kv_len = n_prompt + (n_new - 1) / 2.0
+    kv = cfg["n_layers"] * 2 * mean_kv_len * kv_dim * kv_bytes
+    return weights + kv, weights
+
+
+def decode_bench(args, world, rank, torch):
+    """Full C4 generation (128-token prompt, 256 new tokens at T 0.8 / top-k 40
+    / top-p 0.95 / repeat penalty 1.1, fp16 KV cache) on a random-init
+    Llama-2-7B-shape model built on the device.  tok/s from the device time of
+    the decode phase; e2e from the wall time of the public holo_model_generate
+    call (prompt in, tokens out, prefill included)."""
+    from holo_b200.model import LLAMA2_7B, SamplerDesc, synthetic_model
+    cfg = dict(LLAMA2_7B)
+    act = hb.ACT_Q8 if args.act == "q8" else hb.ACT_F32
+    want_cpu = rank == 0 and world == 1 and not args.no_cpu
+    t0 = time.perf_counter()
+    built = synthetic_model(cfg, seed=0, act_mode=act, kv_f16=True, keep_host=want_cpu)
+    m, host = built if want_cpu else (built, None)
+    build_s = time.perf_counter() - t0
+    prompt = np.random.default_rng(0).integers(0, cfg["vocab"], size=DECODE_PROMPT).astype(np.int32)
+    s = SamplerDesc(0.8, 0.95, 40, 1.1, 64)
+    m.generate(prompt, DECODE_NEW, s, seed=0)            # warm-up (graph capture, caches)
+    runs = []
+    for i in range(3):
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        toks = m.generate(prompt, DECODE_NEW, s, seed=i)
+        wall = time.perf_counter() - w0
+        pre_ms, dec_ms = m.last_timing()
+        runs.append((dec_ms, pre_ms, wall, toks))
+    runs.sort(key=lambda r: r[0])
+    dec_ms, pre_ms, wall, toks = runs[len(runs) // 2]
+    tok_s = DECODE_NEW / (dec_ms * 1e-3)
+    bpt, wbytes = decode_bytes_per_token(cfg)
+    peak, peak_kind = peaks()
+    out = {
+        "config": "Llama-2-7B shape, Q4_K layers, Q8_0 lm_head, fp16 embeddings and KV cache, ctx 2048; "
+                  f"prompt {DECODE_PROMPT}, {DECODE_NEW} new tokens, T 0.8 / top-k 40 / top-p 0.95 / rep 1.1",
+        "act_mode": args.act, "value": round(tok_s, 1), "unit": "tokens/s", "ms_per_token": round(dec_ms / DECODE_NEW, 4),
+        "prefill_ms": round(pre_ms, 2), "prefill_tokens_s": round((DECODE_PROMPT - 1) / (pre_ms * 1e-3), 1),
+        "roofline": {"bound": "hbm", "bytes_per_token": int(bpt), "weight_bytes_per_token": int(wbytes),
+                     "achieved": round(bpt * tok_s / 1e9, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(bpt * tok_s / 1e9 / peak, 4), "peak_source": peak_kind},
+        "e2e": {"value": round(DECODE_NEW / wall, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * DECODE_PROMPT,
+                "d2h_bytes_per_step": 4 * DECODE_NEW,
+                "path": "holo_model_generate: prompt ids in, generated ids out, prefill included"},
+        "gpu_launches_per_token": cfg["n_layers"] * 7 + 4,
+        "model_build_s": round(build_s, 1),
+        "tokens_head": [int(t) for t in toks[:8]],
+    }
+    if want_cpu and host is not None:
+        out["cpu_baseline"] = decode_cpu_baseline(cfg, host, prompt, budget_s=args.cpu_budget)
+    m.close()
+    return out
+
+
+def decode_cpu_baseline(cfg, host, prompt, budget_s):
+    """The reference's llm_forward (src/ai/llm.c:1015) on the host cores with the
+    same weights: seconds per token over a bounded sample of positions."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import holo_oracle
+    try:
+        ref = holo_oracle.Reference()
+    except Exception as e:  # noqa: BLE001
+        return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
+    rm = holo_oracle.RefModel(ref, cfg, host)
+    n, t0 = 0, time.perf_counter()
+    for t in prompt:
+        rm.forward(int(t))
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    rm.close()
+    threads = os.cpu_count() or 1
+    return {"value": round(n / dt, 4), "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": f"llm_forward for the first {n} prompt positions of the same model, {dt:.1f} s "
+                      f"(Q4_K matvecs single-threaded as in the reference; OpenMP up to {threads} threads elsewhere)"}
+
+
+# ---------------------------------------------------------------------------
 # reference arm: the reference's CPU matvec on the host cores
 # ---------------------------------------------------------------------------
 def run_reference(args, rank, world):
@@ -422,6 +524,26 @@ def run_reference(args, rank, world):
     }), flush=True)
 
 
+def run_profile_decode(args):
+    """Small decode case for ncu launch lists: the 7B model, 2 prompt + 2 new
+    tokens; the profiled generate is inside the NVTX range "profiled"."""
+    import torch
+    from holo_b200.model import LLAMA2_7B, SamplerDesc, synthetic_model
+    dev = hb.Device(0, 1)
+    m = synthetic_model(dict(LLAMA2_7B), seed=0, act_mode=hb.ACT_Q8 if args.act == "q8" else hb.ACT_F32)
+    s = SamplerDesc(0.8, 0.95, 40, 1.1, 64)
+    p = np.array([1, 2], np.int32)
+    m.generate(p, 2, s, seed=0)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("profiled")
+    m.generate(p, 2, s, seed=0)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    dev.check("profile decode")
+    print(json.dumps({"profile_decode": "llama2-7b q4_k", "steps": 3, "kernels_per_step": 228}))
+    m.close()
+
+
 def run_profile_case(args):
     """Small case for ncu: one matvec shape, a few plain launches, no graph."""
     name, shape = args.profile_case.split(":")
@@ -451,9 +573,14 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the 7B decode sub-benchmark")
+    ap.add_argument("--profile-decode", action="store_true", help="small 7B decode case for ncu")
     ap.add_argument("--profile-case", default=None, help="e.g. q4_k:11008x4096 (ncu small case)")
     ap.add_argument("--iters", type=int, default=4)
     args = ap.parse_args()
+    if args.profile_decode:
+        run_profile_decode(args)
+        return
     if args.profile_case:
         run_profile_case(args)
         return

@@ -599,6 +599,8 @@ struct HoloModel {
     cudaGraphExec_t g_forward = nullptr, g_gen = nullptr;
     SampleArgs gen_args{};
     int gen_n_prompt = -1;
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};   // generate: start, prefill done, end
+    float last_prefill_ms = 0.0f, last_decode_ms = 0.0f;
 };
 
 namespace {
@@ -613,12 +615,13 @@ bool dev_alloc(void **p, size_t bytes) {
     return true;
 }
 
-// upload raw GGUF blocks of `rows` x `cols` and repack them into dst
-bool upload_repack(uint8_t *dst, const void *host, int type, int rows, int cols, cudaStream_t st) {
+// copy raw GGUF blocks of `rows` x `cols` (host or device memory) and repack
+// them into dst
+bool upload_repack(uint8_t *dst, const void *src, int type, int rows, int cols, cudaStream_t st) {
     const size_t raw = (size_t)rows * (size_t)gguf_row_bytes(type, cols);
     void *staging = nullptr;
     if (!dev_alloc(&staging, raw)) return false;
-    bool ok = cudaMemcpyAsync(staging, host, raw, cudaMemcpyHostToDevice, st) == cudaSuccess;
+    bool ok = cudaMemcpyAsync(staging, src, raw, cudaMemcpyDefault, st) == cudaSuccess;
     ok = ok && holo_repack_to(dst, staging, type, rows, cols, holo_q4k_layout(), st);
     cudaStreamSynchronize(st);
     cudaFree(staging);
@@ -626,9 +629,9 @@ bool upload_repack(uint8_t *dst, const void *host, int type, int rows, int cols,
     return ok;
 }
 
-bool upload_plain(void **dst, const void *host, size_t bytes, cudaStream_t st) {
+bool upload_plain(void **dst, const void *src, size_t bytes, cudaStream_t st) {
     if (!dev_alloc(dst, bytes)) return false;
-    if (cudaMemcpyAsync(*dst, host, bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+    if (cudaMemcpyAsync(*dst, src, bytes, cudaMemcpyDefault, st) != cudaSuccess) {
         holo_check_launch("holo_model: upload");
         return false;
     }
@@ -837,6 +840,12 @@ void *holo_model_create(const holo_model_desc *desc) {
         holo_model_free(m);
         return nullptr;
     }
+    for (auto &e : m->ev)
+        if (cudaEventCreate(&e) != cudaSuccess) {
+            holo_check_launch("holo_model_create: events");
+            holo_model_free(m);
+            return nullptr;
+        }
     cudaMemset(m->kc, 0, kv_bytes);
     cudaMemset(m->vc, 0, kv_bytes);
     cudaMemset(m->d_pos, 0, sizeof(int) * 4);
@@ -864,8 +873,8 @@ int holo_model_set_layer(void *model, int l, const float *attn_norm, const void 
         return HOLO_E_NOMEM;
     if (!L.ffn_norm && !upload_plain((void **)&L.ffn_norm, ffn_norm, sizeof(float) * d.dim, st))
         return HOLO_E_NOMEM;
-    cudaMemcpyAsync(L.attn_norm, attn_norm, sizeof(float) * d.dim, cudaMemcpyHostToDevice, st);
-    cudaMemcpyAsync(L.ffn_norm, ffn_norm, sizeof(float) * d.dim, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(L.attn_norm, attn_norm, sizeof(float) * d.dim, cudaMemcpyDefault, st);
+    cudaMemcpyAsync(L.ffn_norm, ffn_norm, sizeof(float) * d.dim, cudaMemcpyDefault, st);
     // [Wq; Wk; Wv] in one tiled buffer (each part a whole number of row-blocks)
     const size_t bq = cuda_quant_tiled_bytes(t, m->q_dim, d.dim), bk = cuda_quant_tiled_bytes(t, m->kv_dim, d.dim);
     if (!L.wqkv && !dev_alloc((void **)&L.wqkv, bq + 2 * bk)) return HOLO_E_NOMEM;
@@ -879,13 +888,24 @@ int holo_model_set_layer(void *model, int l, const float *attn_norm, const void 
     L.i_o = holo_weight_info(t, d.dim, m->q_dim, holo_q4k_layout());
     // W1 and W3 interleaved by 16 rows: row-block b = W1 rows 16b..16b+15, W3 rows 16b..16b+15
     const size_t rb = (size_t)gguf_row_bytes(t, d.dim);
-    std::vector<uint8_t> inter((size_t)2 * d.ffn_dim * rb);
-    for (int b = 0; b < d.ffn_dim / 16; ++b) {
-        memcpy(inter.data() + (size_t)(32 * b) * rb, (const uint8_t *)w1 + (size_t)(16 * b) * rb, 16 * rb);
-        memcpy(inter.data() + (size_t)(32 * b + 16) * rb, (const uint8_t *)w3 + (size_t)(16 * b) * rb, 16 * rb);
+    void *inter = nullptr;
+    if (!dev_alloc(&inter, (size_t)2 * d.ffn_dim * rb)) return HOLO_E_NOMEM;
+    const size_t band = 16 * rb;
+    bool ok = cudaMemcpy2DAsync(inter, 2 * band, w1, band, band, d.ffn_dim / 16, cudaMemcpyDefault, st) ==
+                  cudaSuccess &&
+              cudaMemcpy2DAsync((uint8_t *)inter + band, 2 * band, w3, band, band, d.ffn_dim / 16,
+                                cudaMemcpyDefault, st) == cudaSuccess;
+    if (!L.w13 && !dev_alloc((void **)&L.w13, cuda_quant_tiled_bytes(t, 2 * d.ffn_dim, d.dim))) {
+        cudaFree(inter);
+        return HOLO_E_NOMEM;
     }
-    if (!L.w13 && !dev_alloc((void **)&L.w13, cuda_quant_tiled_bytes(t, 2 * d.ffn_dim, d.dim))) return HOLO_E_NOMEM;
-    if (!upload_repack(L.w13, inter.data(), t, 2 * d.ffn_dim, d.dim, st)) return cuda_last_status();
+    ok = ok && upload_repack(L.w13, inter, t, 2 * d.ffn_dim, d.dim, st);
+    cudaStreamSynchronize(st);
+    cudaFree(inter);
+    if (!ok) {
+        holo_check_launch("holo_model_set_layer: w1/w3");
+        return cuda_last_status() ? cuda_last_status() : HOLO_E_ARG;
+    }
     L.i_13 = holo_weight_info(t, 2 * d.ffn_dim, d.dim, holo_q4k_layout());
     if (!L.w2 && !dev_alloc((void **)&L.w2, cuda_quant_tiled_bytes(t, d.dim, d.ffn_dim))) return HOLO_E_NOMEM;
     if (!upload_repack(L.w2, w2, t, d.dim, d.ffn_dim, st)) return cuda_last_status();
@@ -906,9 +926,9 @@ int holo_model_set_globals(void *model, const void *tok_embeddings, const float 
     drop_graphs(m);
     const size_t eb = (size_t)d.vocab * d.dim * (d.emb_type == 1 ? 2 : 4);
     if (!m->emb && !dev_alloc(&m->emb, eb)) return HOLO_E_NOMEM;
-    cudaMemcpyAsync(m->emb, tok_embeddings, eb, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(m->emb, tok_embeddings, eb, cudaMemcpyDefault, st);
     if (!m->final_norm && !dev_alloc((void **)&m->final_norm, sizeof(float) * d.dim)) return HOLO_E_NOMEM;
-    cudaMemcpyAsync(m->final_norm, final_norm, sizeof(float) * d.dim, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(m->final_norm, final_norm, sizeof(float) * d.dim, cudaMemcpyDefault, st);
     if (!m->out && !dev_alloc((void **)&m->out, cuda_quant_tiled_bytes(d.out_type, d.vocab, d.dim)))
         return HOLO_E_NOMEM;
     if (!upload_repack(m->out, output, d.out_type, d.vocab, d.dim, st)) return cuda_last_status();
@@ -1028,14 +1048,22 @@ int holo_model_generate(void *model, const int *prompt, int n_prompt, int n_new,
         if (!m->g_gen) return -1;
         m->gen_args = a;
     }
+    // steps 0 .. n_prompt-2 are prefill; each later step forwards one position
+    // and samples one token (the first forwards the last prompt token)
     const int steps = n_prompt + n_new - 1;
-    for (int i = 0; i < steps; ++i)
+    cudaEventRecord(m->ev[0], st);
+    for (int i = 0; i < steps; ++i) {
+        if (i == n_prompt - 1) cudaEventRecord(m->ev[1], st);
         if (cudaGraphLaunch(m->g_gen, st) != cudaSuccess) {
             holo_check_launch("holo_model_generate: graph launch");
             return -1;
         }
+    }
+    cudaEventRecord(m->ev[2], st);
     cudaMemcpyAsync(out, m->d_out, sizeof(int) * n_new, cudaMemcpyDeviceToHost, st);
     cudaStreamSynchronize(st);
+    cudaEventElapsedTime(&m->last_prefill_ms, m->ev[0], m->ev[1]);
+    cudaEventElapsedTime(&m->last_decode_ms, m->ev[1], m->ev[2]);
     m->h_pos = steps;
     m->h_nhist = n_prompt + n_new;
     return cuda_last_status() == HOLO_OK ? n_new : -1;
@@ -1059,6 +1087,14 @@ int holo_model_launch_steps(void *model, int n_steps) {
 
 int holo_model_pos(void *model) { return model ? ((HoloModel *)model)->h_pos : -1; }
 
+int holo_model_last_timing(void *model, float *prefill_ms, float *decode_ms) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m) return HOLO_E_ARG;
+    if (prefill_ms) *prefill_ms = m->last_prefill_ms;
+    if (decode_ms) *decode_ms = m->last_decode_ms;
+    return HOLO_OK;
+}
+
 void holo_model_reset(void *model) {
     HoloModel *m = (HoloModel *)model;
     if (!m) return;
@@ -1075,6 +1111,8 @@ void holo_model_free(void *model) {
     if (!m) return;
     cudaDeviceSynchronize();
     drop_graphs(m);
+    for (auto &e : m->ev)
+        if (e) cudaEventDestroy(e);
     for (auto &L : m->layers) {
         cudaFree(L.attn_norm); cudaFree(L.ffn_norm); cudaFree(L.wqkv); cudaFree(L.wo); cudaFree(L.w13);
         cudaFree(L.w2);

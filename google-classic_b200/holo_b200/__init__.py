@@ -94,6 +94,8 @@ SIGNATURES = {
     "holo_model_sample": (_i, [_vp, _vp, _f]),
     "holo_model_generate": (_i, [_vp, _vp, _i, _i, _vp, _i, _vp]),
     "holo_model_launch_steps": (_i, [_vp, _i]),
+    "cuda_synth_weights": (_i, [_vp, _i, _i, _i, C.c_ulonglong, _f]),
+    "holo_model_last_timing": (_i, [_vp, _vp, _vp]),
     "holo_model_pos": (_i, [_vp]), "holo_model_reset": (None, [_vp]), "holo_model_free": (None, [_vp]),
 }
 

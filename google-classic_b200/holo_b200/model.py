@@ -86,6 +86,12 @@ class Model:
         self._check("holo_model_generate", n == n_new)
         return out
 
+    def last_timing(self) -> tuple[float, float]:
+        """(prefill_ms, decode_ms) of the last generate, device time."""
+        a, b = C.c_float(), C.c_float()
+        self.lib.holo_model_last_timing(self.h, C.byref(a), C.byref(b))
+        return a.value, b.value
+
     def reset(self):
         self.lib.holo_model_reset(self.h)
 
@@ -99,3 +105,70 @@ class Model:
             self.close()
         except Exception:
             pass
+
+
+LLAMA2_7B = dict(n_layers=32, dim=4096, n_heads=32, n_kv_heads=32, head_dim=128, ffn_dim=11008, vocab=32000,
+                 max_seq=2048, rope_base=10000.0, eps=1e-5, layer_type=12, emb_type=1, out_type=8)
+LLAMA3_70B = dict(n_layers=80, dim=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn_dim=28672, vocab=128256,
+                  max_seq=4096, rope_base=500000.0, eps=1e-5, layer_type=2, emb_type=1, out_type=2)
+
+
+def _tensor_seed(seed: int, layer: int, idx: int) -> int:
+    return (seed * 1000003 + layer * 64 + idx) & 0xFFFFFFFFFFFFFFFF
+
+
+def synthetic_model(cfg: dict, seed: int, act_mode: int = ACT_Q8, kv_f16: bool = True, std: float = 0.02,
+                    keep_host: bool = False):
+    """A random-init model built on the device: every weight N(0, std),
+    quantized round-to-nearest by cuda_synth_weights into GGUF blocks, then
+    repacked by holo_model_set_layer/_globals.  keep_host also returns the raw
+    blocks (the dict layout of synth.llama_weights) for the reference engine."""
+    lib = load()
+    m = Model(cfg, act_mode=act_mode, kv_f16=kv_f16)
+    dim, hd, ffn, V = cfg["dim"], cfg["head_dim"], cfg["ffn_dim"], cfg["vocab"]
+    q_dim, kv_dim = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    lt, ot, et = cfg["layer_type"], cfg["out_type"], cfg.get("emb_type", 1)
+    from . import row_bytes
+    shapes = {"wq": (q_dim, dim), "wk": (kv_dim, dim), "wv": (kv_dim, dim), "wo": (dim, q_dim),
+              "w1": (ffn, dim), "w2": (dim, ffn), "w3": (ffn, dim)}
+    ones = np.ones(dim, np.float32)
+    host = {"layers": []} if keep_host else None
+
+    def gen(t, rows, cols, s):
+        nbytes = rows * (row_bytes(t, cols) if t not in (0, 1) else cols * (4 if t == 0 else 2))
+        p = lib.cuda_malloc(nbytes)
+        if not p:
+            raise MemoryError("synthetic_model: cuda_malloc")
+        rc = lib.cuda_synth_weights(p, t, rows, cols, s, std)
+        m._check("cuda_synth_weights", rc == HOLO_OK)
+        return p, nbytes
+
+    def to_host(p, nbytes, dtype=np.uint8):
+        a = np.empty(nbytes // np.dtype(dtype).itemsize, dtype)
+        lib.cuda_memcpy_d2h(a.ctypes.data, p, a.nbytes)
+        return a
+
+    for l in range(cfg["n_layers"]):
+        ptrs = {}
+        for i, (name, (r, c)) in enumerate(shapes.items()):
+            ptrs[name] = gen(lt, r, c, _tensor_seed(seed, l, i))
+        rc = lib.holo_model_set_layer(m.h, l, ones.ctypes.data, ptrs["wq"][0], ptrs["wk"][0], ptrs["wv"][0],
+                                      ptrs["wo"][0], ones.ctypes.data, ptrs["w1"][0], ptrs["w2"][0], ptrs["w3"][0])
+        m._check(f"holo_model_set_layer {l}", rc == HOLO_OK)
+        if keep_host:
+            L = {k: to_host(*v) for k, v in ptrs.items()}
+            L["attn_norm"], L["ffn_norm"] = ones.copy(), ones.copy()
+            host["layers"].append(L)
+        for p, _ in ptrs.values():
+            lib.cuda_free(p)
+    emb = gen(et, V, dim, _tensor_seed(seed, 1 << 20, 0))
+    out = gen(ot, V, dim, _tensor_seed(seed, 1 << 20, 1))
+    rc = lib.holo_model_set_globals(m.h, emb[0], ones.ctypes.data, out[0])
+    m._check("holo_model_set_globals", rc == HOLO_OK)
+    if keep_host:
+        host["tok_emb"] = to_host(*emb, dtype=np.float16 if et == 1 else np.float32).reshape(V, dim)
+        host["final_norm"] = ones.copy()
+        host["output"] = to_host(*out)
+    lib.cuda_free(emb[0])
+    lib.cuda_free(out[0])
+    return (m, host) if keep_host else m

@@ -123,8 +123,9 @@ int cuda_sm_count(void);
  * a single CUDA graph: RMSNorm fused into the QKV, gate/up and output
  * matvecs, [Wq;Wk;Wv] and [W1;W3] each one weight, residual adds and SwiGLU
  * in matvec epilogues, the KV cache resident on the device, and the sampler on
- * the device.  Weights are given as host pointers to GGUF blocks laid out as
- * the reference loader reads them (row-major, rows of in-dim values). */
+ * the device.  Weights are given as pointers (host or device memory) to GGUF
+ * blocks laid out as the reference loader reads them (row-major, rows of
+ * in-dim values); they are copied and repacked, not kept. */
 typedef struct {
     int n_layers, dim, n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_seq;
     float rope_base;     /* RoPE frequency base (llm_config_t.rope_freq_base) */
@@ -175,8 +176,18 @@ int holo_model_generate(void *model, const int *prompt, int n_prompt, int n_new,
  * synchronising (for timing); the sampled tokens past n_new are discarded. */
 int holo_model_launch_steps(void *model, int n_steps);
 int holo_model_pos(void *model);
+/* Device time of the last holo_model_generate: prefill (the steps before the
+ * first draw) and decode (n_new steps of forward + sample), in ms. */
+int holo_model_last_timing(void *model, float *prefill_ms, float *decode_ms);
 void holo_model_reset(void *model);
 void holo_model_free(void *model);
+
+/* Seeded synthetic weights on the device: rows x cols values N(0, std) from a
+ * counter-based generator, written to dst as raw GGUF blocks of ggml_type
+ * (0 F32, 1 F16 plain values; 8 Q8_0, 2 Q4_0, 12 Q4_K round-to-nearest), the
+ * layout holo_model_set_layer and the reference loader read.  No counterpart
+ * in the reference (it has no f32 -> Q8_0/Q4_0/Q4_K quantizer). */
+int cuda_synth_weights(void *dst, int ggml_type, int rows, int cols, unsigned long long seed, float std);
 
 /* ---- CUDA graphs of the library stream --------------------------------------
  * The reference launches every op separately on the legacy stream

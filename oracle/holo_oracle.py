@@ -191,20 +191,24 @@ class RefModel:
     def reset(self):
         self.lib.href_reset(self.h)
 
-    def generate(self, prompt, n_new, temperature, top_p, top_k, penalty, last_n, seed):
-        """llm_generate's loop (llm.c:1340-1420) without tokenizer or EOS."""
+    def generate(self, prompt, n_new, temperature, top_p, top_k, penalty, last_n, seed, margins=None):
+        """llm_generate's loop (llm.c:1340-1420) without tokenizer or EOS.
+        margins (a list) collects the top-1 minus top-2 logit before each draw."""
         self.srand(seed)
         self.reset()
         for t in prompt:
             self.push(t)
         for t in prompt:
-            self.forward(t)
+            logits = self.forward(t)
         out = []
         for _ in range(n_new):
+            if margins is not None:
+                top2 = np.sort(logits)[-2:]
+                margins.append(float(top2[1] - top2[0]))
             tok = self.sample(temperature, top_p, top_k, penalty, last_n)
             out.append(tok)
             self.push(tok)
-            self.forward(tok)
+            logits = self.forward(tok)
         return np.array(out, np.int32)
 
     def close(self):
