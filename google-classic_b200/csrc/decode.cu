@@ -265,6 +265,7 @@ __global__ void dec_push_kernel(int *hist, int *nhist_p, int token) {
 // ---------------------------------------------------------------------------
 constexpr int SM_THREADS = 1024;
 constexpr int SM_SORT_MAX = 4096;           // top-p candidates sorted in shared memory
+constexpr int SM_VOCAB_SMEM = 36864;        // vocabularies up to this size are sampled in shared memory
 
 struct SampleArgs {
     int vocab;
@@ -350,199 +351,310 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int *si, int &total) 
     return before;
 }
 
+// Shared state of the sampler (static shared memory of the kernel that runs it).
+struct SampleSmem {
+    float sv[32];
+    int si[32];
+    unsigned hist256[256];
+    unsigned prefix;
+    int krem;
+    float scale;
+    int ncut;
+    int token;
+    float cand_p[SM_SORT_MAX];   // candidates (index order), then the top-p sort
+    int cand_i[SM_SORT_MAX];
+    float sort_p[SM_SORT_MAX];
+    int sort_j[SM_SORT_MAX];
+    float work[SM_VOCAB_SMEM];   // the logits, then the probabilities (small vocabularies)
+};
+
+// The sampler body, run by one CTA of any size (a multiple of 32, <= 1024).
+// The logits are copied into a work array -- shared memory for vocabularies
+// up to SM_VOCAB_SMEM, else the global `probs` buffer -- and every step runs
+// there; the logits themselves are left as they are.  Candidates (the top-k
+// set, or every index when top-k is off) live in shared memory when they fit,
+// so the reference's sequential sums read shared memory.  Returns the token
+// (all threads), -1 when top-p needs more candidates than fit.
+__device__ int sample_body(SampleSmem &S, const float *__restrict__ logits, float *__restrict__ probs,
+                           int *__restrict__ kept_idx, float *__restrict__ kept_p, const int *__restrict__ hist,
+                           int nhist, float r, int *__restrict__ status, const SampleArgs &a) {
+    const int V = a.vocab, tid = threadIdx.x, NT = blockDim.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    float *work = V <= SM_VOCAB_SMEM ? S.work : probs;
+    // 1. copy (eight loads in flight per thread) with the temperature applied
+    //    (logits * (1/T) when T > 0 and T != 1, tensor.c:636-642)
+    {
+        const float ts = a.use_temp ? a.tscale : 1.0f;
+        for (int i0 = 0; i0 < V; i0 += 8 * NT) {
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int i = i0 + k * NT + tid;
+                v[k] = i < V ? logits[i] : 0.0f;
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int i = i0 + k * NT + tid;
+                if (i < V) work[i] = a.use_temp ? v[k] * ts : v[k];
+            }
+        }
+    }
+    __syncthreads();
+    // 2. repetition penalty, once per occurrence (tensor.c:644-657).  Applying
+    //    the same operation c times does not depend on the order of the
+    //    occurrences, so the first occurrence of each token applies all c.
+    if (a.penalty != 1.0f && nhist > 0) {
+        const int start = nhist > a.last_n ? nhist - a.last_n : 0;
+        for (int t = start + tid; t < nhist; t += NT) {
+            const int tok = hist[t];
+            bool first = true;
+            int c = 1;
+            for (int u = start; u < nhist; ++u) {
+                if (u == t) continue;
+                if (hist[u] == tok) {
+                    if (u < t) { first = false; break; }
+                    ++c;
+                }
+            }
+            if (first && tok >= 0 && tok < V) {
+                float v = work[tok];
+                for (int k = 0; k < c; ++k) v = v > 0.0f ? __fdiv_rn(v, a.penalty) : v * a.penalty;
+                work[tok] = v;
+            }
+        }
+        __syncthreads();
+    }
+    // every pass over the vocabulary is strided (coalesced); where the
+    // reference's index order matters, candidates are put back in index order
+    if (a.greedy) {
+        float bv = -FLT_MAX;
+        int bi = 0x7fffffff;
+        for (int i = tid; i < V; i += NT)
+            if (work[i] > bv || bi == 0x7fffffff) { bv = work[i]; bi = i; }
+        block_reduce_max_first(bv, bi, S.sv, S.si);
+        return bi;
+    }
+    // 4. softmax
+    float mx = -FLT_MAX;
+    int mi = 0;
+    for (int i = tid; i < V; i += NT) mx = fmaxf(mx, work[i]);
+    block_reduce_max_first(mx, mi, S.sv, S.si);
+    float part = 0.0f;
+    for (int i = tid; i < V; i += NT) {
+        const float e = (float)exp((double)(work[i] - mx));
+        work[i] = e;
+        part += e;
+    }
+    const float sum_e = block_sum(part, S.sv);
+    const float scale = __fdiv_rn(1.0f, sum_e);
+    for (int i = tid; i < V; i += NT) work[i] = work[i] * scale;
+    __syncthreads();
+
+    // 5. top-k: the k-th largest probability by radix selection on its bits
+    //    (probabilities are >= 0, so their bit patterns order like the values)
+    float thr = 0.0f;
+    const bool topk = a.top_k > 0 && a.top_k < V;
+    if (topk) {
+        if (tid == 0) { S.prefix = 0u; S.krem = a.top_k; }
+        unsigned mask = 0u;
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            for (int b = tid; b < 256; b += NT) S.hist256[b] = 0u;
+            __syncthreads();
+            const unsigned prefix = S.prefix;
+            for (int i = tid; i < V; i += NT) {
+                const unsigned key = __float_as_uint(work[i]);
+                if ((key & mask) == prefix) atomicAdd(&S.hist256[(key >> shift) & 255u], 1u);
+            }
+            __syncthreads();
+            if (warp == 0) {
+                // lane l owns digits 255-8l .. 248-8l (descending); find the digit
+                // where the count of larger-or-equal digits reaches krem
+                unsigned cnt[8], tot = 0;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) { cnt[k] = S.hist256[255 - 8 * lane - k]; tot += cnt[k]; }
+                unsigned incl = tot;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                const int krem = S.krem;
+                const unsigned before = incl - tot;
+                if ((int)before < krem && (int)incl >= krem) {
+                    unsigned cum = before;
+                    for (int k = 0; k < 8; ++k) {
+                        if ((int)(cum + cnt[k]) >= krem) {
+                            S.prefix = prefix | ((unsigned)(255 - 8 * lane - k) << shift);
+                            S.krem = krem - (int)cum;
+                            break;
+                        }
+                        cum += cnt[k];
+                    }
+                }
+            }
+            mask |= 255u << shift;
+            __syncthreads();
+        }
+        thr = __uint_as_float(S.prefix);
+    }
+    // candidates (p >= thr; every index without top-k), in index order
+    if (tid == 0) S.ncut = 0;   // candidate counter
+    __syncthreads();
+    for (int i = tid; i < V; i += NT)
+        if (work[i] >= thr) {
+            const int slot = atomicAdd(&S.ncut, 1);
+            if (slot < SM_SORT_MAX) { S.cand_i[slot] = i; S.cand_p[slot] = work[i]; }
+        }
+    __syncthreads();
+    const int nk = S.ncut;
+    const bool in_smem = nk <= SM_SORT_MAX;
+    float *cp = S.cand_p;
+    int *ci = S.cand_i;
+    if (in_smem) {
+        // bitonic sort of the candidates by index
+        int n2 = 1;
+        while (n2 < nk) n2 <<= 1;
+        for (int j = nk + tid; j < n2; j += NT) { ci[j] = 0x7fffffff; cp[j] = 0.0f; }
+        __syncthreads();
+        for (int k = 2; k <= n2; k <<= 1)
+            for (int jj = k >> 1; jj > 0; jj >>= 1) {
+                for (int t = tid; t < n2; t += NT) {
+                    const int u = t ^ jj;
+                    if (u > t) {
+                        const bool up = (t & k) == 0;
+                        const int it = ci[t], iu = ci[u];
+                        if (up ? it > iu : it < iu) {
+                            ci[t] = iu; ci[u] = it;
+                            const float pt = cp[t];
+                            cp[t] = cp[u]; cp[u] = pt;
+                        }
+                    }
+                }
+                __syncthreads();
+            }
+    } else {
+        // more candidates than shared memory holds (top-k off): ordered
+        // compaction into global memory, NT indices at a time
+        cp = kept_p;
+        ci = kept_idx;
+        int base = 0;
+        for (int k0 = 0; k0 < V; k0 += NT) {
+            const int i = k0 + tid;
+            const bool pred = i < V && work[i] >= thr;
+            const unsigned bal = __ballot_sync(0xffffffffu, pred);
+            if (lane == 0) S.si[warp] = __popc(bal);
+            __syncthreads();
+            int woff = 0, tot = 0;
+            for (int w = 0; w < (NT >> 5); ++w) {
+                if (w < warp) woff += S.si[w];
+                tot += S.si[w];
+            }
+            if (pred) {
+                const int o = base + woff + __popc(bal & ((1u << lane) - 1u));
+                ci[o] = i;
+                cp[o] = work[i];
+            }
+            base += tot;
+            __syncthreads();
+        }
+    }
+    __syncthreads();
+    if (topk) {
+        if (tid == 0) {
+            float sum = 0.0f;
+            for (int j = 0; j < nk; ++j) sum += cp[j];
+            S.scale = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 1.0f;
+        }
+        __syncthreads();
+        for (int j = tid; j < nk; j += NT) cp[j] = cp[j] * S.scale;
+        __syncthreads();
+    }
+
+    // 6. top-p over the candidates, sorted descending in shared memory
+    if (a.top_p > 0.0f && a.top_p < 1.0f) {
+        if (nk > SM_SORT_MAX) {
+            if (tid == 0) atomicExch(status, HOLO_E_UNSUPPORTED);
+            return -1;
+        }
+        int n2 = 1;
+        while (n2 < nk) n2 <<= 1;
+        for (int j = tid; j < n2; j += NT) {
+            S.sort_p[j] = j < nk ? cp[j] : -1.0f;
+            S.sort_j[j] = j < nk ? j : 0x7fffffff;
+        }
+        __syncthreads();
+        // bitonic sort: descending probability, ties by ascending candidate
+        for (int k = 2; k <= n2; k <<= 1) {
+            for (int jj = k >> 1; jj > 0; jj >>= 1) {
+                for (int t = tid; t < n2; t += NT) {
+                    const int u = t ^ jj;
+                    if (u > t) {
+                        const bool desc = (t & k) == 0;
+                        const float pt = S.sort_p[t], pu = S.sort_p[u];
+                        const int it = S.sort_j[t], iu = S.sort_j[u];
+                        const bool t_first = pt > pu || (pt == pu && it < iu);
+                        if (desc ? !t_first : t_first) {
+                            S.sort_p[t] = pu; S.sort_p[u] = pt;
+                            S.sort_j[t] = iu; S.sort_j[u] = it;
+                        }
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        if (tid == 0) {
+            float cum = 0.0f;
+            int cut = nk;
+            for (int j = 0; j < nk; ++j) {
+                cum += S.sort_p[j];
+                if (cum > a.top_p) { cut = j + 1; break; }
+            }
+            S.ncut = cut;
+        }
+        __syncthreads();
+        for (int j = tid; j < nk; j += NT)
+            if (j >= S.ncut) cp[S.sort_j[j]] = 0.0f;
+        __syncthreads();
+        if (tid == 0) {
+            float sum = 0.0f;
+            for (int j = 0; j < nk; ++j) sum += cp[j];
+            S.scale = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 1.0f;
+        }
+        __syncthreads();
+        for (int j = tid; j < nk; j += NT) cp[j] = cp[j] * S.scale;
+        __syncthreads();
+    }
+
+    // 7. draw (sample_prob, tensor.c:473-482) over the candidates in index order
+    if (tid == 0) {
+        float cum = 0.0f;
+        int tok = V - 1;
+        for (int j = 0; j < nk; ++j) {
+            cum += cp[j];
+            if (r < cum) { tok = ci[j]; break; }
+        }
+        S.token = tok;
+    }
+    __syncthreads();
+    return S.token;
+}
+
 __global__ void __launch_bounds__(SM_THREADS)
 dec_sample_kernel(float *__restrict__ logits, float *__restrict__ probs, int *__restrict__ kept_idx,
                   float *__restrict__ kept_p, int *__restrict__ seq, int *__restrict__ hist, int *__restrict__ nhist_p,
                   const int *__restrict__ pos_p, const float *__restrict__ rvals, int *__restrict__ out_tokens,
                   int *__restrict__ last_token, int *__restrict__ status, const SampleArgs a) {
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    __shared__ unsigned hist256[256];
-    __shared__ unsigned s_prefix;
-    __shared__ int s_krem;
-    __shared__ float s_scale;
-    __shared__ int s_ncut;
-    __shared__ int s_token;
-    __shared__ float sort_p[SM_SORT_MAX];
-    __shared__ int sort_i[SM_SORT_MAX];
+    extern __shared__ __align__(16) uint8_t sm_raw[];
+    SampleSmem &S = *reinterpret_cast<SampleSmem *>(sm_raw);
     dec_pdl_trigger();
     dec_pdl_wait();
     const int pos = *pos_p;
     if (a.gen && pos < a.n_prompt - 1) return;
     const int gi = a.gen ? pos - (a.n_prompt - 1) : 0;
-    const int V = a.vocab, tid = threadIdx.x;
     const int nhist = *nhist_p;
-
-    // 1-2. temperature, repetition penalty (in place, as the reference)
-    if (a.use_temp)
-        for (int i = tid; i < V; i += SM_THREADS) logits[i] = logits[i] * a.tscale;
-    __syncthreads();
-    if (a.penalty != 1.0f && nhist > 0) {
-        if (tid == 0) {
-            const int start = nhist > a.last_n ? nhist - a.last_n : 0;
-            for (int t = start; t < nhist; ++t) {
-                const int tok = hist[t];
-                if (tok >= 0 && tok < V) {
-                    const float v = logits[tok];
-                    logits[tok] = v > 0.0f ? __fdiv_rn(v, a.penalty) : v * a.penalty;
-                }
-            }
-        }
-        __syncthreads();
-    }
-    // index-order chunk of this thread (compaction keeps index order)
-    const int chunk = (V + SM_THREADS - 1) / SM_THREADS;
-    const int c0 = min(V, tid * chunk), c1 = min(V, c0 + chunk);
-
-    int token;
-    if (a.greedy) {
-        float bv = -FLT_MAX;
-        int bi = 0x7fffffff;
-        for (int i = c0; i < c1; ++i)
-            if (logits[i] > bv || bi == 0x7fffffff) { bv = logits[i]; bi = i; }
-        block_reduce_max_first(bv, bi, sv, si);
-        token = bi;
-    } else {
-        // 4. softmax
-        float mx = -FLT_MAX;
-        int mi = 0;
-        for (int i = c0; i < c1; ++i)
-            if (logits[i] > mx) mx = logits[i];
-        block_reduce_max_first(mx, mi, sv, si);
-        float part = 0.0f;
-        for (int i = c0; i < c1; ++i) {
-            const float e = (float)exp((double)(logits[i] - mx));
-            probs[i] = e;
-            part += e;
-        }
-        const float S = block_sum(part, sv);
-        const float scale = __fdiv_rn(1.0f, S);
-        for (int i = c0; i < c1; ++i) probs[i] = probs[i] * scale;
-        __syncthreads();
-
-        // 5. top-k: the k-th largest probability by radix selection on its bits
-        int nkept;
-        if (a.top_k > 0 && a.top_k < V) {
-            if (tid == 0) { s_prefix = 0u; s_krem = a.top_k; }
-            unsigned mask = 0u;
-            for (int shift = 24; shift >= 0; shift -= 8) {
-                for (int b = tid; b < 256; b += SM_THREADS) hist256[b] = 0u;
-                __syncthreads();
-                const unsigned prefix = s_prefix;
-                for (int i = c0; i < c1; ++i) {
-                    const unsigned key = __float_as_uint(probs[i]);
-                    if ((key & mask) == prefix) atomicAdd(&hist256[(key >> shift) & 255u], 1u);
-                }
-                __syncthreads();
-                if (tid == 0) {
-                    int cum = 0, krem = s_krem;
-                    for (int d = 255; d >= 0; --d) {
-                        const int c = (int)hist256[d];
-                        if (cum + c >= krem) {
-                            s_prefix = prefix | ((unsigned)d << shift);
-                            s_krem = krem - cum;
-                            break;
-                        }
-                        cum += c;
-                    }
-                }
-                mask |= 255u << shift;
-                __syncthreads();
-            }
-            const float thr = __uint_as_float(s_prefix);
-            int cnt = 0;
-            for (int i = c0; i < c1; ++i) cnt += probs[i] >= thr;
-            int total;
-            int off = block_exclusive_scan(cnt, si, total);
-            for (int i = c0; i < c1; ++i)
-                if (probs[i] >= thr) { kept_idx[off] = i; kept_p[off] = probs[i]; ++off; }
-            nkept = total;
-            __syncthreads();
-            if (tid == 0) {
-                float sum = 0.0f;
-                for (int j = 0; j < nkept; ++j) sum += kept_p[j];
-                s_scale = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 1.0f;
-            }
-            __syncthreads();
-            for (int j = tid; j < nkept; j += SM_THREADS) kept_p[j] = kept_p[j] * s_scale;
-            __syncthreads();
-        } else {
-            for (int i = tid; i < V; i += SM_THREADS) { kept_idx[i] = i; kept_p[i] = probs[i]; }
-            nkept = V;
-            __syncthreads();
-        }
-
-        // 6. top-p over the kept candidates (sorted descending in shared memory)
-        if (a.top_p > 0.0f && a.top_p < 1.0f) {
-            if (nkept > SM_SORT_MAX) {
-                if (tid == 0) atomicExch(status, HOLO_E_UNSUPPORTED);
-                return;
-            }
-            int n2 = 1;
-            while (n2 < nkept) n2 <<= 1;
-            for (int j = tid; j < n2; j += SM_THREADS) {
-                sort_p[j] = j < nkept ? kept_p[j] : -1.0f;
-                sort_i[j] = j < nkept ? j : 0x7fffffff;
-            }
-            __syncthreads();
-            // bitonic sort: descending probability, ties by ascending position
-            for (int k = 2; k <= n2; k <<= 1) {
-                for (int jj = k >> 1; jj > 0; jj >>= 1) {
-                    for (int t = tid; t < n2; t += SM_THREADS) {
-                        const int u = t ^ jj;
-                        if (u > t) {
-                            const bool desc = (t & k) == 0;
-                            const float pt = sort_p[t], pu = sort_p[u];
-                            const int it = sort_i[t], iu = sort_i[u];
-                            const bool t_first = pt > pu || (pt == pu && it < iu);
-                            if (desc ? !t_first : t_first) {
-                                sort_p[t] = pu; sort_p[u] = pt;
-                                sort_i[t] = iu; sort_i[u] = it;
-                            }
-                        }
-                    }
-                    __syncthreads();
-                }
-            }
-            if (tid == 0) {
-                float cum = 0.0f;
-                int cut = nkept;
-                for (int j = 0; j < nkept; ++j) {
-                    cum += sort_p[j];
-                    if (cum > a.top_p) { cut = j + 1; break; }
-                }
-                s_ncut = cut;
-            }
-            __syncthreads();
-            // zero the candidates past the cut (sorted order), then renormalise
-            for (int j = tid; j < nkept; j += SM_THREADS)
-                if (j >= s_ncut) kept_p[sort_i[j]] = 0.0f;
-            __syncthreads();
-            if (tid == 0) {
-                float sum = 0.0f;
-                for (int j = 0; j < nkept; ++j) sum += kept_p[j];
-                s_scale = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 1.0f;
-            }
-            __syncthreads();
-            for (int j = tid; j < nkept; j += SM_THREADS) kept_p[j] = kept_p[j] * s_scale;
-            __syncthreads();
-        }
-
-        // 7. draw (sample_prob, tensor.c:473-482): candidates are in index order
-        if (tid == 0) {
-            const float r = rvals[gi];
-            float cum = 0.0f;
-            int tok = V - 1;
-            for (int j = 0; j < nkept; ++j) {
-                cum += kept_p[j];
-                if (r < cum) { tok = kept_idx[j]; break; }
-            }
-            s_token = tok;
-        }
-        __syncthreads();
-        token = s_token;
-    }
-    if (tid == 0) {
+    const int token = sample_body(S, logits, probs, kept_idx, kept_p, hist, nhist, rvals[gi], status, a);
+    if (token < 0) return;
+    if (threadIdx.x == 0) {
         *last_token = token;
         if (a.gen) {
             seq[pos + 1] = token;
@@ -554,10 +666,11 @@ dec_sample_kernel(float *__restrict__ logits, float *__restrict__ probs, int *__
 }
 
 template <typename K, typename... Args>
-bool launch_pdl(K kern, dim3 grid, dim3 block, cudaStream_t st, bool pdl, Args... args) {
+bool launch_pdl_smem(K kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -566,6 +679,11 @@ bool launch_pdl(K kern, dim3 grid, dim3 block, cudaStream_t st, bool pdl, Args..
     cfg.numAttrs = pdl ? 1 : 0;
     if (cudaLaunchKernelEx(&cfg, kern, args...) != cudaSuccess) return holo_check_launch("decode kernel launch");
     return holo_check_launch("decode kernel launch");
+}
+
+template <typename K, typename... Args>
+bool launch_pdl(K kern, dim3 grid, dim3 block, cudaStream_t st, bool pdl, Args... args) {
+    return launch_pdl_smem(kern, grid, block, 0, st, pdl, args...);
 }
 
 }  // namespace
@@ -711,12 +829,21 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
     ok = ok && holo_matvec_launch(m->out, m->i_out, lo, st);
     if (sample) {
         HoloDevice *D = holo_dev();
-        ok = ok && launch_pdl(dec_sample_kernel, dim3(1), dim3(SM_THREADS), st, pdl, m->logits, m->probs,
+        ok = ok && launch_pdl_smem(dec_sample_kernel, dim3(1), dim3(SM_THREADS), sizeof(SampleSmem), st, pdl,
+                                   m->logits, m->probs,
                               m->kept_idx, m->kept_p, m->d_seq, m->d_hist, m->d_nhist, (const int *)m->d_pos,
                               (const float *)m->rvals, m->d_out, m->d_last, D ? D->status : nullptr, sa);
     }
     ok = ok && launch_pdl(dec_step_end_kernel, dim3(1), dim3(32), st, pdl, m->d_pos);
     return ok;
+}
+
+// the sampler's shared memory exceeds the default 48 KB
+bool prepare_sampler() {
+    if (cudaFuncSetAttribute(dec_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(SampleSmem)) != cudaSuccess)
+        return holo_check_launch("sampler attributes");
+    return true;
 }
 
 // one-time per-kernel set-up of every matvec variant of the step, which must
@@ -730,8 +857,8 @@ bool prepare_step(HoloModel *m) {
     o.residual = m->x; o.act = d.act_mode; o.epi = MV_EPI_ADD;
     MvLaunch f;
     f.norm_w = L.ffn_norm; f.act = d.act_mode; f.epi = MV_EPI_SILU_MUL;
-    return holo_matvec_prepare(L.i_qkv, a) && holo_matvec_prepare(L.i_o, o) && holo_matvec_prepare(L.i_13, f) &&
-           holo_matvec_prepare(L.i_2, o) && holo_matvec_prepare(m->i_out, a);
+    return prepare_sampler() && holo_matvec_prepare(L.i_qkv, a) && holo_matvec_prepare(L.i_o, o) &&
+           holo_matvec_prepare(L.i_13, f) && holo_matvec_prepare(L.i_2, o) && holo_matvec_prepare(m->i_out, a);
 }
 
 cudaGraphExec_t capture_step(HoloModel *m, bool sample, const SampleArgs &sa) {
@@ -999,8 +1126,10 @@ int holo_model_sample(void *model, const holo_sampler_desc *s, float r) {
     HoloDevice *D = holo_dev();
     SampleArgs a = make_args(m, s);
     a.gen = 0;
+    if (!prepare_sampler()) return -1;
     cudaMemcpyAsync(m->rvals, &r, sizeof(float), cudaMemcpyHostToDevice, st);
-    launch_pdl(dec_sample_kernel, dim3(1), dim3(SM_THREADS), st, false, m->logits, m->probs, m->kept_idx, m->kept_p,
+    launch_pdl_smem(dec_sample_kernel, dim3(1), dim3(SM_THREADS), sizeof(SampleSmem), st, false, m->logits,
+                    m->probs, m->kept_idx, m->kept_p,
                m->d_seq, m->d_hist, m->d_nhist, (const int *)m->d_pos, (const float *)m->rvals, m->d_out,
                m->d_last, D ? D->status : nullptr, a);
     int tok = -1;

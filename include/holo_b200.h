@@ -164,7 +164,8 @@ int holo_model_load_logits(void *model, const float *logits);
 int holo_model_push_token(void *model, int token);
 /* llm_sample on the current logits and history with the uniform draw r
  * ((float)rand() / RAND_MAX in the reference); returns the token, -1 on error.
- * The logits are modified in place by temperature and penalty, as there. */
+ * Unlike the reference, the logits are left unmodified (temperature and
+ * penalty are applied to a copy). */
 int holo_model_sample(void *model, const holo_sampler_desc *s, float r);
 /* llm_generate without tokenizer and EOS: reset, prefill the prompt, then
  * n_new sample + forward steps, all as graph replays; srand(seed) and one
