@@ -25,7 +25,10 @@
 #include "holo_common.cuh"
 #include "mv_device.cuh"
 #include "matvec.cuh"
+#include "sampler.cuh"
+#include "step.cuh"
 
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 #include <cstdlib>
@@ -33,6 +36,8 @@
 #include <vector>
 
 namespace {
+
+using namespace holo_dec;
 
 __device__ __forceinline__ void dec_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void dec_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -249,396 +254,6 @@ __global__ void dec_push_kernel(int *hist, int *nhist_p, int token) {
     *nhist_p += 1;
 }
 
-// ---------------------------------------------------------------------------
-// sampler: llm_sample (llm.c:1281-1328) on the device, one 1024-thread CTA.
-//  1. temperature: logits *= 1/T when T > 0 and T != 1 (tensor.c:636-642)
-//  2. repetition penalty over the last repeat_last_n history tokens, once per
-//     occurrence: /= penalty if positive, *= penalty otherwise (tensor.c:644-657)
-//  3. greedy (T == 0): the first index of the largest penalised logit
-//  4. softmax; 5. top-k (keep p >= the k-th largest p, renormalise);
-//  6. top-p (sort descending, keep through the first cumulative sum > p,
-//     renormalise); 7. draw: first index whose cumulative sum exceeds r.
-// The sums of the renormalisations and the draw run in the reference's order
-// (index order; descending order for top-p).  Two steps differ in rounding
-// only: exp is evaluated in double and rounded once, and the softmax
-// denominator is summed as a tree.
-// ---------------------------------------------------------------------------
-constexpr int SM_THREADS = 1024;
-constexpr int SM_SORT_MAX = 4096;           // top-p candidates sorted in shared memory
-constexpr int SM_VOCAB_SMEM = 36864;        // vocabularies up to this size are sampled in shared memory
-
-struct SampleArgs {
-    int vocab;
-    int use_temp;          // T > 0 and T != 1
-    float tscale;          // 1/T
-    int greedy;            // T == 0
-    float penalty;
-    int last_n;
-    int top_k;
-    float top_p;
-    int gen;               // 1: generation step (skip during the prompt, append the token)
-    int n_prompt;
-};
-
-__device__ __forceinline__ void block_reduce_max_first(float &v, int &idx, float *sv, int *si) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
-    }
-    if (lane == 0) { sv[warp] = v; si[warp] = idx; }
-    __syncthreads();
-    if (warp == 0) {
-        v = lane < (int)(blockDim.x >> 5) ? sv[lane] : -FLT_MAX;
-        idx = lane < (int)(blockDim.x >> 5) ? si[lane] : 0x7fffffff;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-            if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
-        }
-        if (lane == 0) { sv[0] = v; si[0] = idx; }
-    }
-    __syncthreads();
-    v = sv[0];
-    idx = si[0];
-    __syncthreads();
-}
-
-__device__ __forceinline__ float block_sum(float v, float *sv) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) sv[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-        v = lane < (int)(blockDim.x >> 5) ? sv[lane] : 0.0f;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) sv[0] = v;
-    }
-    __syncthreads();
-    v = sv[0];
-    __syncthreads();
-    return v;
-}
-
-__device__ __forceinline__ int block_exclusive_scan(int v, int *si, int &total) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    if (lane == 31) si[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-        int w = lane < (int)(blockDim.x >> 5) ? si[lane] : 0;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, w, o);
-            if (lane >= o) w += y;
-        }
-        si[lane] = w;   // inclusive over warps
-    }
-    __syncthreads();
-    const int before = (warp > 0 ? si[warp - 1] : 0) + x - v;
-    total = si[(blockDim.x >> 5) - 1];
-    __syncthreads();
-    return before;
-}
-
-// Shared state of the sampler (static shared memory of the kernel that runs it).
-struct SampleSmem {
-    float sv[32];
-    int si[32];
-    unsigned hist256[256];
-    unsigned prefix;
-    int krem;
-    float scale;
-    int ncut;
-    int token;
-    float cand_p[SM_SORT_MAX];   // candidates (index order), then the top-p sort
-    int cand_i[SM_SORT_MAX];
-    float sort_p[SM_SORT_MAX];
-    int sort_j[SM_SORT_MAX];
-    float work[SM_VOCAB_SMEM];   // the logits, then the probabilities (small vocabularies)
-};
-
-// The sampler body, run by one CTA of any size (a multiple of 32, <= 1024).
-// The logits are copied into a work array -- shared memory for vocabularies
-// up to SM_VOCAB_SMEM, else the global `probs` buffer -- and every step runs
-// there; the logits themselves are left as they are.  Candidates (the top-k
-// set, or every index when top-k is off) live in shared memory when they fit,
-// so the reference's sequential sums read shared memory.  Returns the token
-// (all threads), -1 when top-p needs more candidates than fit.
-__device__ int sample_body(SampleSmem &S, const float *__restrict__ logits, float *__restrict__ probs,
-                           int *__restrict__ kept_idx, float *__restrict__ kept_p, const int *__restrict__ hist,
-                           int nhist, float r, int *__restrict__ status, const SampleArgs &a) {
-    const int V = a.vocab, tid = threadIdx.x, NT = blockDim.x;
-    const int lane = tid & 31, warp = tid >> 5;
-    float *work = V <= SM_VOCAB_SMEM ? S.work : probs;
-    // 1. copy (eight loads in flight per thread) with the temperature applied
-    //    (logits * (1/T) when T > 0 and T != 1, tensor.c:636-642)
-    {
-        const float ts = a.use_temp ? a.tscale : 1.0f;
-        for (int i0 = 0; i0 < V; i0 += 8 * NT) {
-            float v[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const int i = i0 + k * NT + tid;
-                v[k] = i < V ? logits[i] : 0.0f;
-            }
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const int i = i0 + k * NT + tid;
-                if (i < V) work[i] = a.use_temp ? v[k] * ts : v[k];
-            }
-        }
-    }
-    __syncthreads();
-    // 2. repetition penalty, once per occurrence (tensor.c:644-657).  Applying
-    //    the same operation c times does not depend on the order of the
-    //    occurrences, so the first occurrence of each token applies all c.
-    if (a.penalty != 1.0f && nhist > 0) {
-        const int start = nhist > a.last_n ? nhist - a.last_n : 0;
-        for (int t = start + tid; t < nhist; t += NT) {
-            const int tok = hist[t];
-            bool first = true;
-            int c = 1;
-            for (int u = start; u < nhist; ++u) {
-                if (u == t) continue;
-                if (hist[u] == tok) {
-                    if (u < t) { first = false; break; }
-                    ++c;
-                }
-            }
-            if (first && tok >= 0 && tok < V) {
-                float v = work[tok];
-                for (int k = 0; k < c; ++k) v = v > 0.0f ? __fdiv_rn(v, a.penalty) : v * a.penalty;
-                work[tok] = v;
-            }
-        }
-        __syncthreads();
-    }
-    // every pass over the vocabulary is strided (coalesced); where the
-    // reference's index order matters, candidates are put back in index order
-    if (a.greedy) {
-        float bv = -FLT_MAX;
-        int bi = 0x7fffffff;
-        for (int i = tid; i < V; i += NT)
-            if (work[i] > bv || bi == 0x7fffffff) { bv = work[i]; bi = i; }
-        block_reduce_max_first(bv, bi, S.sv, S.si);
-        return bi;
-    }
-    // 4. softmax
-    float mx = -FLT_MAX;
-    int mi = 0;
-    for (int i = tid; i < V; i += NT) mx = fmaxf(mx, work[i]);
-    block_reduce_max_first(mx, mi, S.sv, S.si);
-    float part = 0.0f;
-    for (int i = tid; i < V; i += NT) {
-        const float e = (float)exp((double)(work[i] - mx));
-        work[i] = e;
-        part += e;
-    }
-    const float sum_e = block_sum(part, S.sv);
-    const float scale = __fdiv_rn(1.0f, sum_e);
-    for (int i = tid; i < V; i += NT) work[i] = work[i] * scale;
-    __syncthreads();
-
-    // 5. top-k: the k-th largest probability by radix selection on its bits
-    //    (probabilities are >= 0, so their bit patterns order like the values)
-    float thr = 0.0f;
-    const bool topk = a.top_k > 0 && a.top_k < V;
-    if (topk) {
-        if (tid == 0) { S.prefix = 0u; S.krem = a.top_k; }
-        unsigned mask = 0u;
-        for (int shift = 24; shift >= 0; shift -= 8) {
-            for (int b = tid; b < 256; b += NT) S.hist256[b] = 0u;
-            __syncthreads();
-            const unsigned prefix = S.prefix;
-            for (int i = tid; i < V; i += NT) {
-                const unsigned key = __float_as_uint(work[i]);
-                if ((key & mask) == prefix) atomicAdd(&S.hist256[(key >> shift) & 255u], 1u);
-            }
-            __syncthreads();
-            if (warp == 0) {
-                // lane l owns digits 255-8l .. 248-8l (descending); find the digit
-                // where the count of larger-or-equal digits reaches krem
-                unsigned cnt[8], tot = 0;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) { cnt[k] = S.hist256[255 - 8 * lane - k]; tot += cnt[k]; }
-                unsigned incl = tot;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= o) incl += y;
-                }
-                const int krem = S.krem;
-                const unsigned before = incl - tot;
-                if ((int)before < krem && (int)incl >= krem) {
-                    unsigned cum = before;
-                    for (int k = 0; k < 8; ++k) {
-                        if ((int)(cum + cnt[k]) >= krem) {
-                            S.prefix = prefix | ((unsigned)(255 - 8 * lane - k) << shift);
-                            S.krem = krem - (int)cum;
-                            break;
-                        }
-                        cum += cnt[k];
-                    }
-                }
-            }
-            mask |= 255u << shift;
-            __syncthreads();
-        }
-        thr = __uint_as_float(S.prefix);
-    }
-    // candidates (p >= thr; every index without top-k), in index order
-    if (tid == 0) S.ncut = 0;   // candidate counter
-    __syncthreads();
-    for (int i = tid; i < V; i += NT)
-        if (work[i] >= thr) {
-            const int slot = atomicAdd(&S.ncut, 1);
-            if (slot < SM_SORT_MAX) { S.cand_i[slot] = i; S.cand_p[slot] = work[i]; }
-        }
-    __syncthreads();
-    const int nk = S.ncut;
-    const bool in_smem = nk <= SM_SORT_MAX;
-    float *cp = S.cand_p;
-    int *ci = S.cand_i;
-    if (in_smem) {
-        // bitonic sort of the candidates by index
-        int n2 = 1;
-        while (n2 < nk) n2 <<= 1;
-        for (int j = nk + tid; j < n2; j += NT) { ci[j] = 0x7fffffff; cp[j] = 0.0f; }
-        __syncthreads();
-        for (int k = 2; k <= n2; k <<= 1)
-            for (int jj = k >> 1; jj > 0; jj >>= 1) {
-                for (int t = tid; t < n2; t += NT) {
-                    const int u = t ^ jj;
-                    if (u > t) {
-                        const bool up = (t & k) == 0;
-                        const int it = ci[t], iu = ci[u];
-                        if (up ? it > iu : it < iu) {
-                            ci[t] = iu; ci[u] = it;
-                            const float pt = cp[t];
-                            cp[t] = cp[u]; cp[u] = pt;
-                        }
-                    }
-                }
-                __syncthreads();
-            }
-    } else {
-        // more candidates than shared memory holds (top-k off): ordered
-        // compaction into global memory, NT indices at a time
-        cp = kept_p;
-        ci = kept_idx;
-        int base = 0;
-        for (int k0 = 0; k0 < V; k0 += NT) {
-            const int i = k0 + tid;
-            const bool pred = i < V && work[i] >= thr;
-            const unsigned bal = __ballot_sync(0xffffffffu, pred);
-            if (lane == 0) S.si[warp] = __popc(bal);
-            __syncthreads();
-            int woff = 0, tot = 0;
-            for (int w = 0; w < (NT >> 5); ++w) {
-                if (w < warp) woff += S.si[w];
-                tot += S.si[w];
-            }
-            if (pred) {
-                const int o = base + woff + __popc(bal & ((1u << lane) - 1u));
-                ci[o] = i;
-                cp[o] = work[i];
-            }
-            base += tot;
-            __syncthreads();
-        }
-    }
-    __syncthreads();
-    if (topk) {
-        if (tid == 0) {
-            float sum = 0.0f;
-            for (int j = 0; j < nk; ++j) sum += cp[j];
-            S.scale = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 1.0f;
-        }
-        __syncthreads();
-        for (int j = tid; j < nk; j += NT) cp[j] = cp[j] * S.scale;
-        __syncthreads();
-    }
-
-    // 6. top-p over the candidates, sorted descending in shared memory
-    if (a.top_p > 0.0f && a.top_p < 1.0f) {
-        if (nk > SM_SORT_MAX) {
-            if (tid == 0) atomicExch(status, HOLO_E_UNSUPPORTED);
-            return -1;
-        }
-        int n2 = 1;
-        while (n2 < nk) n2 <<= 1;
-        for (int j = tid; j < n2; j += NT) {
-            S.sort_p[j] = j < nk ? cp[j] : -1.0f;
-            S.sort_j[j] = j < nk ? j : 0x7fffffff;
-        }
-        __syncthreads();
-        // bitonic sort: descending probability, ties by ascending candidate
-        for (int k = 2; k <= n2; k <<= 1) {
-            for (int jj = k >> 1; jj > 0; jj >>= 1) {
-                for (int t = tid; t < n2; t += NT) {
-                    const int u = t ^ jj;
-                    if (u > t) {
-                        const bool desc = (t & k) == 0;
-                        const float pt = S.sort_p[t], pu = S.sort_p[u];
-                        const int it = S.sort_j[t], iu = S.sort_j[u];
-                        const bool t_first = pt > pu || (pt == pu && it < iu);
-                        if (desc ? !t_first : t_first) {
-                            S.sort_p[t] = pu; S.sort_p[u] = pt;
-                            S.sort_j[t] = iu; S.sort_j[u] = it;
-                        }
-                    }
-                }
-                __syncthreads();
-            }
-        }
-        if (tid == 0) {
-            float cum = 0.0f;
-            int cut = nk;
-            for (int j = 0; j < nk; ++j) {
-                cum += S.sort_p[j];
-                if (cum > a.top_p) { cut = j + 1; break; }
-            }
-            S.ncut = cut;
-        }
-        __syncthreads();
-        for (int j = tid; j < nk; j += NT)
-            if (j >= S.ncut) cp[S.sort_j[j]] = 0.0f;
-        __syncthreads();
-        if (tid == 0) {
-            float sum = 0.0f;
-            for (int j = 0; j < nk; ++j) sum += cp[j];
-            S.scale = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 1.0f;
-        }
-        __syncthreads();
-        for (int j = tid; j < nk; j += NT) cp[j] = cp[j] * S.scale;
-        __syncthreads();
-    }
-
-    // 7. draw (sample_prob, tensor.c:473-482) over the candidates in index order
-    if (tid == 0) {
-        float cum = 0.0f;
-        int tok = V - 1;
-        for (int j = 0; j < nk; ++j) {
-            cum += cp[j];
-            if (r < cum) { tok = ci[j]; break; }
-        }
-        S.token = tok;
-    }
-    __syncthreads();
-    return S.token;
-}
-
 __global__ void __launch_bounds__(SM_THREADS)
 dec_sample_kernel(float *__restrict__ logits, float *__restrict__ probs, int *__restrict__ kept_idx,
                   float *__restrict__ kept_p, int *__restrict__ seq, int *__restrict__ hist, int *__restrict__ nhist_p,
@@ -712,13 +327,20 @@ struct HoloModel {
     float *part = nullptr, *probs = nullptr, *kept_p = nullptr, *rvals = nullptr;
     int *kept_idx = nullptr;
     int *d_pos = nullptr, *d_seq = nullptr, *d_hist = nullptr, *d_nhist = nullptr, *d_out = nullptr, *d_last = nullptr;
-    int per_split = 64, max_splits = 0;
+    int per_split = 64, max_splits = 0, step_max_splits = 0;
     int h_pos = 0, h_nhist = 0;
     cudaGraphExec_t g_forward = nullptr, g_gen = nullptr;
     SampleArgs gen_args{};
     int gen_n_prompt = -1;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};   // generate: start, prefill done, end
     float last_prefill_ms = 0.0f, last_decode_ms = 0.0f;
+    // persistent step kernel (step.cu)
+    bool use_step = false;
+    bool step_ready = false;
+    StepLayer *d_layers = nullptr;
+    StepPrefetch *d_pf = nullptr;
+    unsigned long long *d_bar = nullptr;
+    int *d_att_cnt = nullptr;
 };
 
 namespace {
@@ -901,6 +523,97 @@ bool model_ready(HoloModel *m) {
     return true;
 }
 
+// L2 prefetch table of the step kernel: the matvec weights in execution order
+// form one circular byte sequence; at each phase every CTA requests its share
+// of the bytes up to STEP_PF_WINDOW past the end of the phase's matvec.  The
+// table is the steady state (second of two simulated steps), so the output
+// phase of one token already requests the first matrices of the next.
+constexpr unsigned long long STEP_PF_WINDOW_DEFAULT = 32ull << 20;
+
+bool build_step(HoloModel *m) {
+    const holo_model_desc &d = m->d;
+    // window: HOLO_PF_MB (MB ahead of the current matrix), default 32
+    unsigned long long STEP_PF_WINDOW = STEP_PF_WINDOW_DEFAULT;
+    if (const char *e = getenv("HOLO_PF_MB")) STEP_PF_WINDOW = (unsigned long long)atoi(e) << 20;
+    const int L = d.n_layers, P = step_phases(L);
+    std::vector<StepLayer> layers(L);
+    struct Seg { const uint8_t *p; unsigned long long n; int phase; };
+    std::vector<Seg> seg;
+    for (int l = 0; l < L; ++l) {
+        const HoloLayer &H = m->layers[l];
+        layers[l] = StepLayer{H.wqkv, H.wo, H.w13, H.w2, H.attn_norm, H.ffn_norm};
+        seg.push_back({H.wqkv, H.i_qkv.bytes, 1 + 5 * l});
+        seg.push_back({H.wo, H.i_o.bytes, 3 + 5 * l});
+        seg.push_back({H.w13, H.i_13.bytes, 4 + 5 * l});
+        seg.push_back({H.w2, H.i_2.bytes, 5 + 5 * l});
+    }
+    seg.push_back({m->out, m->i_out.bytes, P - 1});
+    std::vector<unsigned long long> start(seg.size() + 1, 0);
+    for (size_t i = 0; i < seg.size(); ++i) start[i + 1] = start[i] + seg[i].n;
+    const unsigned long long T = start.back();
+    // end offset (within a step) of the matvec of each phase; attention and
+    // embedding phases keep the previous one
+    std::vector<unsigned long long> end(P, 0);
+    {
+        unsigned long long cur = 0;
+        size_t si = 0;
+        for (int ph = 0; ph < P; ++ph) {
+            if (si < seg.size() && seg[si].phase == ph) { cur = start[si + 1]; ++si; }
+            end[ph] = cur;
+        }
+    }
+    std::vector<StepPrefetch> pf((size_t)P * STEP_PF_MAX, StepPrefetch{nullptr, 0});
+    unsigned long long done = 0;   // bytes requested so far (absolute, over steps)
+    for (int step = 0; step < 2; ++step)
+        for (int ph = 0; ph < P; ++ph) {
+            const unsigned long long target = (unsigned long long)step * T + end[ph] + STEP_PF_WINDOW;
+            unsigned long long lo = std::max(done, target > T ? target - T : 0ull), hi = target;
+            if (hi <= lo) continue;
+            done = hi;
+            if (step == 0) continue;
+            int k = 0;
+            while (lo < hi && k < STEP_PF_MAX) {
+                const unsigned long long off = lo % T;
+                size_t si = 0;
+                while (start[si + 1] <= off) ++si;
+                const unsigned long long n = std::min(hi - lo, start[si + 1] - off);
+                pf[(size_t)ph * STEP_PF_MAX + k++] = StepPrefetch{seg[si].p + (off - start[si]), n};
+                lo += n;
+            }
+        }
+    bool ok = dev_alloc((void **)&m->d_layers, sizeof(StepLayer) * L) &&
+              dev_alloc((void **)&m->d_pf, sizeof(StepPrefetch) * pf.size());
+    if (!ok) return false;
+    cudaMemcpy(m->d_layers, layers.data(), sizeof(StepLayer) * L, cudaMemcpyHostToDevice);
+    cudaMemcpy(m->d_pf, pf.data(), sizeof(StepPrefetch) * pf.size(), cudaMemcpyHostToDevice);
+    m->step_ready = holo_check_launch("decode step: tables");
+    return m->step_ready;
+}
+
+StepArgs step_args(HoloModel *m, bool sample, const SampleArgs &sa) {
+    const holo_model_desc &d = m->d;
+    StepArgs a{};
+    a.n_layers = d.n_layers; a.dim = d.dim; a.n_heads = d.n_heads; a.n_kv_heads = d.n_kv_heads;
+    a.hd = d.head_dim; a.ffn = d.ffn_dim; a.vocab = d.vocab; a.max_seq = d.max_seq;
+    a.eps = d.eps; a.rope_base = d.rope_base; a.out_type = d.out_type; a.emb_f16 = d.emb_type == 1;
+    a.layers = m->d_layers; a.emb = m->emb; a.final_norm = m->final_norm; a.out_w = m->out;
+    a.x = m->x; a.qkv = m->qkv; a.att = m->att; a.h = m->h; a.logits = m->logits;
+    a.kc = m->kc; a.vc = m->vc; a.att_part = m->part; a.att_cnt = m->d_att_cnt;
+    a.per_split = 16; a.max_splits = m->step_max_splits;
+    a.pos = m->d_pos; a.seq = m->d_seq; a.hist = m->d_hist; a.nhist = m->d_nhist; a.out_tokens = m->d_out;
+    a.last = m->d_last; a.rvals = m->rvals; a.probs = m->probs; a.kept_p = m->kept_p; a.kept_idx = m->kept_idx;
+    a.sa = sa; a.sample = sample; a.prefetch = m->d_pf; a.bar = m->d_bar;
+    HoloDevice *D = holo_dev();
+    a.status = D ? D->status : nullptr;
+    a.grid = D ? D->sms : 1;
+    return a;
+}
+
+bool run_step(HoloModel *m, bool sample, const SampleArgs &sa, cudaStream_t st) {
+    if (!m->step_ready && !build_step(m)) return false;
+    return holo_step_launch(step_args(m, sample, sa), m->d.layer_type, m->d.act_mode, m->d.kv_f16, st);
+}
+
 SampleArgs make_args(const HoloModel *m, const holo_sampler_desc *s) {
     SampleArgs a{};
     a.vocab = m->d.vocab;
@@ -945,6 +658,8 @@ void *holo_model_create(const holo_model_desc *desc) {
     m->kv_dim = d.n_kv_heads * hd;
     m->layers.resize(d.n_layers);
     m->max_splits = (d.max_seq + m->per_split - 1) / m->per_split;
+    // the step kernel splits attention into 16-position pieces at the least
+    m->step_max_splits = (d.max_seq + 15) / 16;
     const size_t kv_bytes = (size_t)d.n_layers * d.max_seq * m->kv_dim * (d.kv_f16 ? 2 : 4);
     bool ok = dev_alloc(&m->kc, kv_bytes) && dev_alloc(&m->vc, kv_bytes);
     ok = ok && dev_alloc((void **)&m->x, sizeof(float) * d.dim);
@@ -955,7 +670,8 @@ void *holo_model_create(const holo_model_desc *desc) {
     ok = ok && dev_alloc((void **)&m->probs, sizeof(float) * d.vocab);
     ok = ok && dev_alloc((void **)&m->kept_p, sizeof(float) * d.vocab);
     ok = ok && dev_alloc((void **)&m->kept_idx, sizeof(int) * d.vocab);
-    ok = ok && dev_alloc((void **)&m->part, sizeof(float) * (size_t)d.n_heads * m->max_splits * (hd + 2));
+    ok = ok && dev_alloc((void **)&m->part,
+                         sizeof(float) * (size_t)d.n_heads * std::max(m->max_splits, m->step_max_splits) * (hd + 4));
     ok = ok && dev_alloc((void **)&m->rvals, sizeof(float) * (d.max_seq + 1));
     ok = ok && dev_alloc((void **)&m->d_pos, sizeof(int) * 4);
     ok = ok && dev_alloc((void **)&m->d_seq, sizeof(int) * (d.max_seq + 1));
@@ -963,6 +679,8 @@ void *holo_model_create(const holo_model_desc *desc) {
     ok = ok && dev_alloc((void **)&m->d_nhist, sizeof(int) * 4);
     ok = ok && dev_alloc((void **)&m->d_out, sizeof(int) * (d.max_seq + 1));
     ok = ok && dev_alloc((void **)&m->d_last, sizeof(int) * 4);
+    ok = ok && dev_alloc((void **)&m->d_bar, sizeof(unsigned long long) * 4);
+    ok = ok && dev_alloc((void **)&m->d_att_cnt, sizeof(int) * d.n_heads);
     if (!ok) {
         holo_model_free(m);
         return nullptr;
@@ -973,6 +691,14 @@ void *holo_model_create(const holo_model_desc *desc) {
             holo_model_free(m);
             return nullptr;
         }
+    {
+        // the persistent step kernel serves head_dim 128; HOLO_STEP=graph keeps
+        // the one-launch-per-op graph
+        const char *e = getenv("HOLO_STEP");
+        m->use_step = hd == 128 && !(e && strcmp(e, "graph") == 0);
+    }
+    cudaMemset(m->d_bar, 0, sizeof(unsigned long long) * 4);
+    cudaMemset(m->d_att_cnt, 0, sizeof(int) * d.n_heads);
     cudaMemset(m->kc, 0, kv_bytes);
     cudaMemset(m->vc, 0, kv_bytes);
     cudaMemset(m->d_pos, 0, sizeof(int) * 4);
@@ -996,6 +722,7 @@ int holo_model_set_layer(void *model, int l, const float *attn_norm, const void 
     cudaStream_t st = holo_stream();
     HoloLayer &L = m->layers[l];
     drop_graphs(m);
+    m->step_ready = false;
     if (!L.attn_norm && !upload_plain((void **)&L.attn_norm, attn_norm, sizeof(float) * d.dim, st))
         return HOLO_E_NOMEM;
     if (!L.ffn_norm && !upload_plain((void **)&L.ffn_norm, ffn_norm, sizeof(float) * d.dim, st))
@@ -1051,6 +778,7 @@ int holo_model_set_globals(void *model, const void *tok_embeddings, const float 
     const holo_model_desc &d = m->d;
     cudaStream_t st = holo_stream();
     drop_graphs(m);
+    m->step_ready = false;
     const size_t eb = (size_t)d.vocab * d.dim * (d.emb_type == 1 ? 2 : 4);
     if (!m->emb && !dev_alloc(&m->emb, eb)) return HOLO_E_NOMEM;
     cudaMemcpyAsync(m->emb, tok_embeddings, eb, cudaMemcpyDefault, st);
@@ -1074,6 +802,18 @@ int holo_model_forward(void *model, int token, float *logits) {
     }
     cudaStream_t st = holo_stream();
     dec_set_token_kernel<<<1, 1, 0, st>>>(m->d_seq, m->d_pos, token);
+    if (m->use_step) {
+        SampleArgs none{};
+        if (!run_step(m, false, none, st)) return cuda_last_status() ? cuda_last_status() : HOLO_E_ARG;
+        m->h_pos++;
+        if (logits) {
+            if (cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->d.vocab, cudaMemcpyDeviceToHost, st) !=
+                cudaSuccess)
+                holo_check_launch("holo_model_forward: logits copy");
+            cudaStreamSynchronize(st);
+        }
+        return cuda_last_status();
+    }
     if (!m->g_forward) {
         SampleArgs none{};
         m->g_forward = capture_step(m, false, none);
@@ -1168,6 +908,23 @@ int holo_model_generate(void *model, const int *prompt, int n_prompt, int n_new,
     SampleArgs a = make_args(m, s);
     a.gen = 1;
     a.n_prompt = n_prompt;
+    const int steps = n_prompt + n_new - 1;
+    if (m->use_step) {
+        m->gen_args = a;
+        cudaEventRecord(m->ev[0], st);
+        for (int i = 0; i < steps; ++i) {
+            if (i == n_prompt - 1) cudaEventRecord(m->ev[1], st);
+            if (!run_step(m, true, a, st)) return -1;
+        }
+        cudaEventRecord(m->ev[2], st);
+        cudaMemcpyAsync(out, m->d_out, sizeof(int) * n_new, cudaMemcpyDeviceToHost, st);
+        cudaStreamSynchronize(st);
+        cudaEventElapsedTime(&m->last_prefill_ms, m->ev[0], m->ev[1]);
+        cudaEventElapsedTime(&m->last_decode_ms, m->ev[1], m->ev[2]);
+        m->h_pos = steps;
+        m->h_nhist = n_prompt + n_new;
+        return cuda_last_status() == HOLO_OK ? n_new : -1;
+    }
     if (m->g_gen && memcmp(&a, &m->gen_args, sizeof(a)) != 0) {
         cudaGraphExecDestroy(m->g_gen);
         m->g_gen = nullptr;
@@ -1179,7 +936,6 @@ int holo_model_generate(void *model, const int *prompt, int n_prompt, int n_new,
     }
     // steps 0 .. n_prompt-2 are prefill; each later step forwards one position
     // and samples one token (the first forwards the last prompt token)
-    const int steps = n_prompt + n_new - 1;
     cudaEventRecord(m->ev[0], st);
     for (int i = 0; i < steps; ++i) {
         if (i == n_prompt - 1) cudaEventRecord(m->ev[1], st);
@@ -1200,6 +956,13 @@ int holo_model_generate(void *model, const int *prompt, int n_prompt, int n_new,
 
 int holo_model_launch_steps(void *model, int n_steps) {
     HoloModel *m = (HoloModel *)model;
+    if (m && m->use_step && n_steps >= 0 && m->h_pos + n_steps <= m->d.max_seq - 1) {
+        cudaStream_t st = holo_stream();
+        for (int i = 0; i < n_steps; ++i)
+            if (!run_step(m, true, m->gen_args, st)) return cuda_last_status();
+        m->h_pos += n_steps;
+        return HOLO_OK;
+    }
     if (!m || !m->g_gen || n_steps < 0 || m->h_pos + n_steps > m->d.max_seq - 1) {
         holo_set_status(HOLO_E_ARG, "holo_model_launch_steps: no generation graph or past max_seq");
         return HOLO_E_ARG;
@@ -1230,6 +993,8 @@ void holo_model_reset(void *model) {
     cudaStream_t st = holo_stream();
     cudaMemsetAsync(m->d_pos, 0, sizeof(int), st);
     cudaMemsetAsync(m->d_nhist, 0, sizeof(int), st);
+    cudaMemsetAsync(m->d_bar, 0, sizeof(unsigned long long) * 4, st);
+    cudaMemsetAsync(m->d_att_cnt, 0, sizeof(int) * m->d.n_heads, st);
     cudaStreamSynchronize(st);
     m->h_pos = 0;
     m->h_nhist = 0;
@@ -1248,7 +1013,7 @@ void holo_model_free(void *model) {
     }
     void *bufs[] = {m->emb, m->final_norm, m->out, m->kc, m->vc, m->x, m->qkv, m->att, m->h, m->logits,
                     m->part, m->probs, m->kept_p, m->rvals, m->kept_idx, m->d_pos, m->d_seq, m->d_hist,
-                    m->d_nhist, m->d_out, m->d_last};
+                    m->d_nhist, m->d_out, m->d_last, m->d_layers, m->d_pf, m->d_bar, m->d_att_cnt};
     for (void *p : bufs) cudaFree(p);
     delete m;
 }

@@ -27,11 +27,14 @@
 // its one wait (the activation copy) is bounded.
 #include "holo_common.cuh"
 #include "mv_device.cuh"
+#include "mv_unit.cuh"
 #include "matvec.cuh"
 
 #include <cstdio>
 
 namespace {
+
+using namespace holo_mv;
 
 constexpr int NWARP = 8;                  // warps per CTA
 constexpr int NTHREADS = NWARP * 32;
@@ -91,17 +94,6 @@ __host__ __device__ __forceinline__ MvSmem mv_smem_layout(int act, bool norm, in
     return L;
 }
 
-// L2 prefetch of a byte range (no data returns to the SM)
-__device__ __forceinline__ void prefetch_l2_bulk(const void *src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(src), "r"(bytes) : "memory");
-}
-
-// 1-D bulk copy global -> shared (no multicast, no cache hint)
-__device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 :: "r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
-}
-
 // Even split of T units over C CTAs (T*C < 2^32 is checked on the host).
 __device__ __forceinline__ int tile_owner(unsigned t, unsigned T, unsigned C) {
     return (int)(((t + 1) * C - 1) / T);
@@ -112,109 +104,6 @@ __device__ __forceinline__ int tile_begin(unsigned c, unsigned T, unsigned C) {
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
-// rint(v) for |v| < 2^22 through the 1.5*2^23 mantissa: round half to even,
-// the same result as cvt.rni (and C rintf) without the conversion unit
-__device__ __forceinline__ int rint_small(float v) {
-    return __float_as_int(__fadd_rn(v, 12582912.0f)) - 0x4B400000;
-}
-
-// streaming loads: read once, not kept in L1
-__device__ __forceinline__ uint4 ldg_stream(const void *p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint2 ldg_stream2(const void *p) {
-    uint2 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-    return v;
-}
-
-// What one warp loads for one unit (lane = row): eight 16-byte code planes and
-// the row's head (Q4_K head / Q4_0 eight fp16 scales / Q8_0 four).
-struct Frag {
-    uint4 q[UNIT_PLANES];
-    uint4 h;
-};
-
-template <int TYPE>
-__device__ __forceinline__ void load_unit(Frag &f, const uint8_t *__restrict__ unit, int lane) {
-    const uint8_t *row = unit + (size_t)TILE_ROWS * UnitGeom<TYPE>::HEAD_BYTES + lane * 16;
-#pragma unroll
-    for (int pl = 0; pl < UNIT_PLANES; ++pl) f.q[pl] = ldg_stream(row + pl * TILE_ROWS * 16);
-    if constexpr (TYPE == GT_Q8_0) {
-        const uint2 h = ldg_stream2(unit + lane * 8);
-        f.h = make_uint4(h.x, h.y, 0u, 0u);
-    } else {
-        f.h = ldg_stream(unit + lane * 16);
-    }
-}
-
-// fp16 scale k (0..7) of a head word set
-__device__ __forceinline__ float head_half(const uint4 &h, int k) {
-    const uint32_t w = k < 2 ? h.x : k < 4 ? h.y : k < 6 ? h.z : h.w;
-    return half_bits_to_float((k & 1) ? (w >> 16) : (w & 0xffffu));
-}
-
-// this lane's (row's) contribution of one unit, added into acc; b0 = index of
-// the unit's first 32-block in the activation vector
-template <int TYPE, int ACT>
-__device__ __forceinline__ void unit_dot(float &acc, const Frag &f, int b0, const uint8_t *__restrict__ aq,
-                                         const float2 *__restrict__ ads, const float *__restrict__ xs,
-                                         const float *__restrict__ xsum) {
-    if constexpr (TYPE == GT_Q4_K) {
-        const uint4 h = f.h;
-        // d/16 is exact, so (d/16)*sc rounds like (d*sc)/16
-        const float d = half_bits_to_float(h.x & 0xffffu) * (ACT == HOLO_ACT_Q8 ? 0.0625f : 1.0f);
-        const float dmin = half_bits_to_float(h.x >> 16);
-        const uint32_t sc_lo = h.y & 0x3F3F3F3Fu, m_lo = h.z & 0x3F3F3F3Fu;
-        const uint32_t sc_hi = ((h.w & LO4) << 2) | ((h.y >> 6) & 0x03030303u);
-        const uint32_t m_hi = (((h.w >> 4) & LO4) << 2) | ((h.z >> 6) & 0x03030303u);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float sc = d * ubyte_to_float(j < 4 ? sc_lo : sc_hi, j & 3);
-            const float mn = dmin * ubyte_to_float(j < 4 ? m_lo : m_hi, j & 3);
-            const int blk = b0 + j;
-            if constexpr (ACT == HOLO_ACT_Q8) {
-                const uint4 a0 = lds128(aq + (size_t)blk * 32), a1 = lds128(aq + (size_t)blk * 32 + 16);
-                const float2 ds = ads[blk];
-                const float f16 = int_to_float_exact(dot_nib16_q8_x16(f.q[j], a0, a1));
-                acc += fmaf(sc, ds.x * f16, -mn * ds.y);
-            } else {
-                acc += fmaf(sc, dot_nib16_f32<true>(f.q[j], xs + (size_t)blk * 32), -mn * xsum[blk]);
-            }
-        }
-    } else if constexpr (TYPE == GT_Q4_0) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float dw = head_half(f.h, j);
-            const int blk = b0 + j;
-            if constexpr (ACT == HOLO_ACT_Q8) {
-                const uint4 a0 = lds128(aq + (size_t)blk * 32), a1 = lds128(aq + (size_t)blk * 32 + 16);
-                const float2 ds = ads[blk];
-                const float f16 = int_to_float_exact(dot_nib16_q8_x16(f.q[j], a0, a1));
-                acc += dw * fmaf(ds.x * 0.0625f, f16, -8.0f * ds.y);
-            } else {
-                acc += dw * (dot_nib16_f32<true>(f.q[j], xs + (size_t)blk * 32) - 8.0f * xsum[blk]);
-            }
-        }
-    } else {  // Q8_0: block j = planes 2j, 2j+1
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float dw = head_half(f.h, j);
-            const int blk = b0 + j;
-            if constexpr (ACT == HOLO_ACT_Q8) {
-                const uint4 a0 = lds128(aq + (size_t)blk * 32), a1 = lds128(aq + (size_t)blk * 32 + 16);
-                const int s = dot_i8x32_q8(f.q[2 * j], f.q[2 * j + 1], a0, a1);
-                acc += (dw * ads[blk].x) * int_to_float_exact(s);
-            } else {
-                acc += dw * dot_i8x32_f32<true>(f.q[2 * j], f.q[2 * j + 1], xs + (size_t)blk * 32);
-            }
-        }
-    }
-}
 
 // Final value of the 32 rows of row-block rb (v held by lane r = row r),
 // executed by all lanes of one warp.
@@ -348,76 +237,7 @@ __global__ void __launch_bounds__(NTHREADS, MIN_CTAS_PER_SM) mv_tiled_kernel(con
     if (p.bulk) ok = mbar_wait_bounded(bar, 0, p.status, HOLO_E_TIMEOUT);
     if (!__syncthreads_and(ok)) return;
 
-    float scale = 1.0f;
-    if constexpr (NORM) {
-        float ss = 0.0f;
-        for (int i = ctid * 4; i < p.in_dim; i += NTHREADS * 4) {
-            const float4 v = *reinterpret_cast<const float4 *>(xst + i);
-            ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss); ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) wsum[warp] = ss;
-        __syncthreads();
-        float tot = 0.0f;
-#pragma unroll
-        for (int w = 0; w < NWARP; w++) tot += wsum[w];
-        scale = 1.0f / sqrtf(tot / (float)p.in_dim + p.eps);
-    }
-    {
-        // One thread per 32-value block (no shuffles): normalise it (NORM,
-        // written back), then ACT_Q8 finds amax, d = amax/127, id = 1/d and
-        // packs rint(x*id) clamped to [-127, 127] -- the arithmetic of
-        // quantize_vals_q8, with the clamp applied before rounding, which gives
-        // the same integers for every finite x*id -- and ACT_F32 takes the block
-        // sum.  Thread l reads the eight 16-byte chunks of its block starting at
-        // chunk (l + l/8) % 8, so every shared-memory wavefront hits distinct
-        // banks (loads: 8 lanes, word stores: 32 lanes).
-        for (int b = ctid; b < p.nblk32p; b += NTHREADS) {
-            float4 *xb = reinterpret_cast<float4 *>(xst + (size_t)b * 32);
-            const int rot = ctid + (ctid >> 3);
-            float amax = 0.0f, xsb = 0.0f;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const int c = (k + rot) & 7;
-                float4 v = xb[c];
-                if constexpr (NORM) {
-                    const float4 w4 = reinterpret_cast<const float4 *>(nw + (size_t)b * 32)[c];
-                    v.x = (v.x * scale) * w4.x; v.y = (v.y * scale) * w4.y;
-                    v.z = (v.z * scale) * w4.z; v.w = (v.w * scale) * w4.w;
-                    xb[c] = v;
-                }
-                if constexpr (ACT == HOLO_ACT_Q8)
-                    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-                else
-                    xsb += (v.x + v.y) + (v.z + v.w);
-            }
-            if constexpr (ACT == HOLO_ACT_Q8) {
-                const float d = __fdiv_rn(amax, 127.0f);
-                const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-                uint32_t *qb = reinterpret_cast<uint32_t *>(aq + (size_t)b * 32);
-                int sum = 0;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const int c = (k + rot) & 7;
-                    const float4 v = xb[c];
-                    // |clamped value| <= 127: the low byte of v + 1.5*2^23 is the
-                    // two's-complement code
-                    const uint32_t b0 = __float_as_uint(__fadd_rn(fminf(fmaxf(__fmul_rn(v.x, id), -127.0f), 127.0f), 12582912.0f));
-                    const uint32_t b1 = __float_as_uint(__fadd_rn(fminf(fmaxf(__fmul_rn(v.y, id), -127.0f), 127.0f), 12582912.0f));
-                    const uint32_t b2 = __float_as_uint(__fadd_rn(fminf(fmaxf(__fmul_rn(v.z, id), -127.0f), 127.0f), 12582912.0f));
-                    const uint32_t b3 = __float_as_uint(__fadd_rn(fminf(fmaxf(__fmul_rn(v.w, id), -127.0f), 127.0f), 12582912.0f));
-                    const uint32_t word = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
-                    qb[c] = word;
-                    sum = __dp4a((int)word, 0x01010101, sum);
-                }
-                ads[b] = make_float2(d, d * (float)sum);
-            } else {
-                xsum[b] = xsb;
-            }
-        }
-        __syncthreads();
-    }
+    act_prologue<ACT, NORM, NTHREADS>(xst, nw, aq, ads, xsum, wsum, p.in_dim, p.nblk32p, p.eps);
 
     // ------------------------------- main loop --------------------------------
     // The warp's running sum of one row-block is parked in red[row-block][warp]

@@ -1,0 +1,669 @@
+// step.cu -- one decode step (one token) as a single persistent kernel.
+//
+// The step of decode.cu as phases of one cooperative launch, one 256-thread
+// CTA per SM, with bounded grid barriers between the phases:
+//
+//   embed | per layer: QKV (RMSNorm fused) | RoPE + KV append + attention |
+//   Wo (+x) | W1/W3 (RMSNorm, SwiGLU) | W2 (+x) | output matrix (RMSNorm) |
+//   sampler (CTA 0)
+//
+// The reference's sequence is the same as in decode.cu (src/ai/llm.c:1015-1269,
+// 1281-1328).  What the single kernel buys over one launch per op:
+//   * no launch or drain between ops: a phase starts when the barrier opens;
+//   * every matvec phase gives each CTA whole row-blocks, so outputs are final
+//     in the CTA (no split-K fix-up, no atomics);
+//   * an L2 prefetch table keeps ~32 MB of upcoming weights requested from
+//     HBM at all times (cp.async.bulk.prefetch.L2, split over the CTAs), so HBM
+//     streams while the phases compute from L2.
+// Every wait (barriers, bulk copies) is bounded; a CTA that gives up records
+// HOLO_E_TIMEOUT, and later launches see the status and return at once.
+#include "holo_common.cuh"
+#include "mv_device.cuh"
+#include "mv_unit.cuh"
+#include "step.cuh"
+
+#include <algorithm>
+#include <cfloat>
+#include <type_traits>
+
+namespace {
+
+using namespace holo_mv;
+using namespace holo_dec;
+
+constexpr int ST_WARPS = 8;
+constexpr int ST_THREADS = ST_WARPS * 32;
+constexpr int ST_DEPTH = 3;                        // units loading per warp
+constexpr int ST_HD = 128;                         // head_dim of this kernel
+constexpr unsigned long long ST_WAIT_NS = 1000000000ull;
+constexpr size_t ST_PERSIST = 2048;                // bytes of the persistent shared region
+
+// shared memory kept across phases (start of the dynamic allocation)
+struct StepPersist {
+    float2 rope[ST_HD / 2];    // (cos, sin) of the RoPE pairs at pos
+    uint64_t mbar;             // bulk-copy completion
+    unsigned long long launch; // launch index (barrier targets)
+    int ok;
+    int pos;
+};
+static_assert(sizeof(StepPersist) <= ST_PERSIST, "persistent region");
+
+template <int T> __device__ __forceinline__ int units_of(int cols) {
+    return (cols + UnitGeom<T>::VALS - 1) / UnitGeom<T>::VALS;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+
+// Grid barrier: arrivals counted on a 64-bit counter (bar[0]) that only
+// grows; barrier e of launch L of a kernel with n barriers per launch opens at
+// (L * n + e + 1) * grid arrivals.  bar[1] counts the kernel's launches.
+__device__ bool step_barrier(const StepArgs &a, StepPersist &P, unsigned long long *bar, int e, int n) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned long long target = (P.launch * (unsigned long long)n + e + 1) * (unsigned long long)a.grid;
+        // release: the CTA's writes (ordered before this thread by the CTA
+        // barrier) are visible to whoever acquires the count
+        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" :: "l"(bar) : "memory");
+        bool ok = true;
+        if (ld_acquire_u64(bar) < target) {
+            const unsigned long long t0 = holo_globaltimer();
+            for (unsigned it = 1;; ++it) {
+                if (ld_acquire_u64(bar) >= target) break;
+                if ((it & 63u) == 0 && holo_globaltimer() - t0 > ST_WAIT_NS) {
+                    ok = false;
+                    atomicExch(a.status, HOLO_E_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        P.ok = ok;
+    }
+    __syncthreads();
+    return P.ok != 0;
+}
+
+// this CTA's share of the phase's L2 prefetch ranges (warp 0, 32 KB requests)
+__device__ void step_prefetch(const StepArgs &a, int phase) {
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
+    const StepPrefetch *pf = a.prefetch + (size_t)phase * STEP_PF_MAX;
+    constexpr unsigned long long CH = 32768;
+    for (int k = 0; k < STEP_PF_MAX; ++k) {
+        const unsigned long long n = pf[k].bytes;
+        if (n == 0) continue;
+        const unsigned long long c = blockIdx.x, G = a.grid;
+        const unsigned long long b0 = (n * c / G) & ~15ull;
+        const unsigned long long b1 = c + 1 == G ? n : ((n * (c + 1) / G) & ~15ull);
+        for (unsigned long long o = b0 + (unsigned long long)lane * CH; o < b1; o += 32 * CH)
+            prefetch_l2_bulk(pf[k].ptr + o, (uint32_t)(b1 - o < CH ? b1 - o : CH));
+    }
+}
+
+__device__ __forceinline__ size_t align128(size_t v) { return (v + 127) & ~(size_t)127; }
+
+// ---------------------------------------------------------------------------
+// matvec phase: rows x in_dim unit-layout weight, whole row-blocks per CTA
+// ---------------------------------------------------------------------------
+// epi: 0 store, 1 y = residual + W.x, 2 SwiGLU over rows interleaved by 16;
+// norm_w non-NULL: RMSNorm of x first.  One instance per weight type: the
+// kernel calls it from a single site (separate inlined copies per phase
+// exhaust the register file).
+template <int TYPE, int ACT>
+__device__ __forceinline__ void step_mv(const StepArgs &a, StepPersist &P, uint8_t *sm, unsigned &mb_par,
+                        const uint8_t *__restrict__ W, int rows, int in_dim, const float *x, float *y,
+                        const float *residual, const float *norm_w, int epi) {
+    const bool norm = norm_w != nullptr;
+    constexpr int BLKS32 = UnitGeom<TYPE>::BLKS32;
+    constexpr size_t UB = UnitGeom<TYPE>::UNIT_BYTES;
+    const int units = units_of<TYPE>(in_dim), nblk32p = units * BLKS32;
+    const int nrb = (rows + TILE_ROWS - 1) / TILE_ROWS;
+    const int G = a.grid, c = blockIdx.x;
+    const int rb0 = (int)((long long)nrb * c / G), rb1 = (int)((long long)nrb * (c + 1) / G);
+    if (rb0 >= rb1) return;
+    const int nloc = rb1 - rb0;
+    const int u0 = rb0 * units, u1 = rb1 * units;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    float *red = reinterpret_cast<float *>(sm);
+    size_t o = align128((size_t)nloc * ST_WARPS * 32 * sizeof(float));
+    uint8_t *aq = sm + o;
+    float2 *ads = reinterpret_cast<float2 *>(sm + o + (size_t)nblk32p * 32);
+    float *xst, *xsum = nullptr;
+    if constexpr (ACT == HOLO_ACT_Q8) {
+        o += align128((size_t)nblk32p * 40);
+        xst = reinterpret_cast<float *>(sm + o);
+        o += (size_t)nblk32p * 128;
+    } else {
+        xst = reinterpret_cast<float *>(sm + o);
+        xsum = xst + (size_t)nblk32p * 32;
+        o += align128((size_t)nblk32p * 132);
+    }
+    float *nw = reinterpret_cast<float *>(sm + o);
+    if (norm) o += (size_t)nblk32p * 128;
+    float *wsum = reinterpret_cast<float *>(sm + o);
+
+    // activations (and norm weights) by bulk copy: through L2, never a stale L1
+    const uint32_t xbytes = (uint32_t)in_dim * 4u;
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&P.mbar, norm ? 2u * xbytes : xbytes);
+        bulk_copy_g2s(xst, x, xbytes, &P.mbar);
+        if (norm) bulk_copy_g2s(nw, norm_w, xbytes, &P.mbar);
+    }
+    Frag ring[ST_DEPTH];
+#pragma unroll
+    for (int k = 0; k < ST_DEPTH; ++k) {
+        const int uu = u0 + warp + k * ST_WARPS;
+        if (uu < u1) load_unit<TYPE>(ring[k], W + (size_t)uu * UB, lane);
+    }
+    for (int i = in_dim + tid; i < nblk32p * 32; i += ST_THREADS) {
+        xst[i] = 0.0f;
+        if (norm) nw[i] = 0.0f;
+    }
+    for (int i = tid; i < nloc * ST_WARPS * 32; i += ST_THREADS) red[i] = 0.0f;
+    const bool ok = mbar_wait_bounded(&P.mbar, mb_par, a.status, HOLO_E_TIMEOUT);
+    mb_par ^= 1u;
+    if (!__syncthreads_and(ok)) return;
+    if (norm) act_prologue<ACT, true, ST_THREADS>(xst, nw, aq, ads, xsum, wsum, in_dim, nblk32p, a.eps);
+    else act_prologue<ACT, false, ST_THREADS>(xst, nw, aq, ads, xsum, wsum, in_dim, nblk32p, a.eps);
+    const float *xs = xst;
+
+    int rb = (u0 + warp) / units, s = u0 + warp - rb * units;
+    const int dq = ST_WARPS / units, dr = ST_WARPS - dq * units;
+    int cur_rb = rb;
+    float acc = 0.0f;
+    for (int ub = u0 + warp; ub < u1; ub += ST_DEPTH * ST_WARPS) {
+#pragma unroll
+        for (int k = 0; k < ST_DEPTH; ++k) {
+            const int u = ub + k * ST_WARPS;
+            if (u >= u1) break;
+            if (rb != cur_rb) {
+                red[((cur_rb - rb0) * ST_WARPS + warp) * 32 + lane] = acc;
+                acc = 0.0f;
+                cur_rb = rb;
+            }
+            unit_dot<TYPE, ACT>(acc, ring[k], s * BLKS32, aq, ads, xs, xsum);
+            const int un = u + ST_DEPTH * ST_WARPS;
+            if (un < u1) load_unit<TYPE>(ring[k], W + (size_t)un * UB, lane);
+            s += dr;
+            rb += dq;
+            if (s >= units) { s -= units; ++rb; }
+        }
+    }
+    if (u0 + warp < u1) red[((cur_rb - rb0) * ST_WARPS + warp) * 32 + lane] = acc;
+    __syncthreads();
+    for (int l = warp; l < nloc; l += ST_WARPS) {
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < ST_WARPS; ++w) v += red[(l * ST_WARPS + w) * 32 + lane];
+        const int rbl = rb0 + l;
+        if (epi == 2) {   // SwiGLU over rows interleaved by 16
+            const float u = __shfl_down_sync(0xffffffffu, v, 16);
+            const int r = rbl * 16 + lane;
+            if (lane < 16 && r < (rows >> 1)) y[r] = (v / (1.0f + expf(-v))) * u;
+        } else {
+            const int row = rbl * TILE_ROWS + lane;
+            if (row < rows) {
+                if (epi == 1) v += __ldcg(residual + row);
+                y[row] = v;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// attention phase: one warp per (head, 64-position split); 8-lane groups
+// hold 16 dims each, a warp folds four positions at a time
+// ---------------------------------------------------------------------------
+template <typename KV> __device__ __forceinline__ KV to_kv_st(float v);
+template <> __device__ __forceinline__ float to_kv_st<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half to_kv_st<__half>(float v) { return __float2half_rn(v); }
+__device__ __forceinline__ float kv_f(float v) { return v; }
+__device__ __forceinline__ float kv_f(__half v) { return __half2float(v); }
+
+template <typename KV>
+__device__ __forceinline__ void load16(const KV *p, float (&o)[16]) {
+    if constexpr (sizeof(KV) == 2) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 8) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(p + i);
+            const __half2 *h2 = reinterpret_cast<const __half2 *>(&v);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = __half22float2(h2[k]);
+                o[i + 2 * k] = f.x;
+                o[i + 2 * k + 1] = f.y;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(p + i);
+            o[i] = v.x; o[i + 1] = v.y; o[i + 2] = v.z; o[i + 3] = v.w;
+        }
+    }
+}
+
+// rotate-half RoPE of 16 dims per lane: lanes l8 < 4 hold pair firsts
+// (dims i), lanes l8 >= 4 the seconds (dims i + 64); rounding as rope_rotate
+__device__ __forceinline__ void rope16(float (&v)[16], int l8, const StepPersist &P) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[j], 4);
+        const int i = 16 * (l8 & 3) + j;
+        const float c = P.rope[i].x, s = P.rope[i].y;
+        if (l8 < 4) v[j] = __fsub_rn(__fmul_rn(v[j], c), __fmul_rn(other, s));
+        else v[j] = __fadd_rn(__fmul_rn(other, s), __fmul_rn(v[j], c));
+    }
+}
+
+// split length so that the (head, split) items about fill the grid's warps:
+// a multiple of 4 positions, at least 16
+__device__ __forceinline__ int attn_split_len(const StepArgs &a, int kv_len) {
+    const int warps = a.grid * ST_WARPS;
+    int ps = (kv_len * a.n_heads + warps - 1) / warps;
+    ps = (ps + 3) & ~3;
+    return ps < 16 ? 16 : ps;
+}
+
+// partial (m, l, acc[HD]) of one (head, split): header at 0, 1; acc at 4..
+// (stride HD + 4 floats keeps every acc row 16-byte aligned)
+constexpr int ATT_STRIDE = ST_HD + 4;
+
+template <typename KV>
+__device__ __noinline__ void step_attn(const StepArgs &a, const StepPersist &P, uint8_t *sm, int layer, int pos) {
+    constexpr int HD = ST_HD;
+    const int kv_len = pos + 1;
+    const int per_split = attn_split_len(a, kv_len);
+    const int nsp = (kv_len + per_split - 1) / per_split;
+    const int items = a.n_heads * nsp;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 3, l8 = lane & 7;
+    const int q_dim = a.n_heads * HD, kv_dim = a.n_kv_heads * HD, group = a.n_heads / a.n_kv_heads;
+    KV *kc = reinterpret_cast<KV *>(a.kc) + (size_t)layer * a.max_seq * kv_dim;
+    KV *vc = reinterpret_cast<KV *>(a.vc) + (size_t)layer * a.max_seq * kv_dim;
+    const float sqrt_hd = sqrtf((float)HD);
+    for (int it = blockIdx.x * ST_WARPS + warp; it < items; it += a.grid * ST_WARPS) {
+        const int h = it % a.n_heads, sp = it / a.n_heads, kvh = h / group;
+        const int p0 = sp * per_split, p1 = min(kv_len, p0 + per_split);
+        float qf[16];
+        {
+            const float4 *q4 = reinterpret_cast<const float4 *>(a.qkv + (size_t)h * HD + 16 * l8);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 v = __ldcg(q4 + k);
+                qf[4 * k] = v.x; qf[4 * k + 1] = v.y; qf[4 * k + 2] = v.z; qf[4 * k + 3] = v.w;
+            }
+        }
+        rope16(qf, l8, P);
+        // this position's k (rotated) and v, rounded as the cache stores them,
+        // kept in the warp's shared scratch (the cache row may not be written yet)
+        const bool has_pos = pos >= p0 && pos < p1;
+        float *kps = reinterpret_cast<float *>(sm) + (size_t)warp * 2 * HD + 16 * l8;
+        float *vps = kps + HD;
+        if (has_pos) {
+            float kp[16], vp[16];
+            const float4 *k4 = reinterpret_cast<const float4 *>(a.qkv + q_dim + (size_t)kvh * HD + 16 * l8);
+            const float4 *v4 = reinterpret_cast<const float4 *>(a.qkv + q_dim + kv_dim + (size_t)kvh * HD + 16 * l8);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 kv = __ldcg(k4 + k), vv = __ldcg(v4 + k);
+                kp[4 * k] = kv.x; kp[4 * k + 1] = kv.y; kp[4 * k + 2] = kv.z; kp[4 * k + 3] = kv.w;
+                vp[4 * k] = vv.x; vp[4 * k + 1] = vv.y; vp[4 * k + 2] = vv.z; vp[4 * k + 3] = vv.w;
+            }
+            rope16(kp, l8, P);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                kp[j] = kv_f(to_kv_st<KV>(kp[j]));
+                vp[j] = kv_f(to_kv_st<KV>(vp[j]));
+            }
+            if (h % group == 0 && g == 0) {   // one writer per KV head
+                KV *kd = kc + (size_t)pos * kv_dim + (size_t)kvh * HD + 16 * l8;
+                KV *vd = vc + (size_t)pos * kv_dim + (size_t)kvh * HD + 16 * l8;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    kd[j] = to_kv_st<KV>(kp[j]);
+                    vd[j] = to_kv_st<KV>(vp[j]);
+                }
+            }
+            if (g == 0) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) { kps[j] = kp[j]; vps[j] = vp[j]; }
+            }
+            __syncwarp();
+        }
+        float m = -FLT_MAX, l = 0.0f, acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+        for (int base = p0; base < p1; base += 4) {
+            const int p = base + g;
+            const bool live = p < p1;
+            float kf[16], vf[16];
+            float dot = 0.0f;
+            if (live) {
+                // k and v of the position requested together: one round trip
+                if (p == pos) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) { kf[j] = kps[j]; vf[j] = vps[j]; }
+                } else {
+                    load16<KV>(kc + (size_t)p * kv_dim + (size_t)kvh * HD + 16 * l8, kf);
+                    load16<KV>(vc + (size_t)p * kv_dim + (size_t)kvh * HD + 16 * l8, vf);
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) dot = fmaf(qf[j], kf[j], dot);
+            }
+            dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+            dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+            dot += __shfl_xor_sync(0xffffffffu, dot, 4);
+            if (live) {
+                const float sc = __fdiv_rn(dot, sqrt_hd);     // score / sqrtf(hd), llm.c:1187
+                const float mn = fmaxf(m, sc);
+                const float corr = __expf(m - mn), e = __expf(sc - mn);
+                l = fmaf(l, corr, e);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc[j] = fmaf(acc[j], corr, e * vf[j]);
+                m = mn;
+            }
+        }
+        // the four position groups of the warp
+#pragma unroll
+        for (int off = 8; off <= 16; off <<= 1) {
+            const float om = __shfl_xor_sync(0xffffffffu, m, off), ol = __shfl_xor_sync(0xffffffffu, l, off);
+            const float M = fmaxf(m, om);
+            const float ca = l > 0.0f ? __expf(m - M) : 0.0f, cb = ol > 0.0f ? __expf(om - M) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const float oa = __shfl_xor_sync(0xffffffffu, acc[j], off);
+                acc[j] = acc[j] * ca + oa * cb;
+            }
+            l = l * ca + ol * cb;
+            m = M;
+        }
+        float *out = a.att_part + ((size_t)h * a.max_splits + sp) * ATT_STRIDE;
+        if (g == 0) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<float4 *>(out + 4 + 16 * l8 + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        }
+        if (lane == 0) { out[0] = m; out[1] = l; }
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            // acq_rel: publishes this split's partial, and the last arrival
+            // sees every other split's
+            int prev;
+            asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(prev) : "l"(a.att_cnt + h) : "memory");
+            last = prev == nsp - 1;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            // the last split of head h merges all of them (the arithmetic of
+            // dec_attn_merge_kernel): split headers one per lane, warp
+            // reductions, then one aligned float4 of the output per lane and
+            // split with the split loads in flight together
+            const float *ph = a.att_part + (size_t)h * a.max_splits * ATT_STRIDE;
+            float M = -FLT_MAX;
+            for (int s0 = 0; s0 < nsp; s0 += 32) {
+                const int s2 = s0 + lane;
+                if (s2 < nsp) {
+                    const float2 ml = __ldcg(reinterpret_cast<const float2 *>(ph + (size_t)s2 * ATT_STRIDE));
+                    if (ml.y > 0.0f) M = fmaxf(M, ml.x);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            float L = 0.0f;
+            float4 o4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int s0 = 0; s0 < nsp; s0 += 32) {
+                const int s2 = s0 + lane;
+                float w = 0.0f;
+                if (s2 < nsp) {
+                    const float2 ml = __ldcg(reinterpret_cast<const float2 *>(ph + (size_t)s2 * ATT_STRIDE));
+                    if (ml.y > 0.0f) { w = __expf(ml.x - M); L = fmaf(ml.y, w, L); }
+                }
+                const int n = min(32, nsp - s0);
+#pragma unroll 8
+                for (int j = 0; j < n; ++j) {
+                    const float wj = __shfl_sync(0xffffffffu, w, j);
+                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(ph + (size_t)(s0 + j) * ATT_STRIDE + 4) + lane);
+                    o4.x = fmaf(v.x, wj, o4.x); o4.y = fmaf(v.y, wj, o4.y);
+                    o4.z = fmaf(v.z, wj, o4.z); o4.w = fmaf(v.w, wj, o4.w);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+            const float inv = 1.0f / L;
+            *reinterpret_cast<float4 *>(a.att + (size_t)h * HD + 4 * lane) =
+                make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv);
+            if (lane == 0) a.att_cnt[h] = 0;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// the kernels: the layers (embed + 5 phases per layer), then the output
+// matrix and the sampler.  Two kernels because a second weight type in one
+// kernel (a Q8_0 output matrix after Q4_K layers) doubles the live registers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool step_begin(const StepArgs &a, StepPersist &P, const unsigned long long *bar) {
+    if (threadIdx.x == 0) {
+        P.launch = ld_acquire_u64(bar + 1);
+        P.pos = __ldcg(a.pos);
+        P.ok = __ldcg(a.status) == 0;
+        mbar_init(&P.mbar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    return P.ok != 0;   // an earlier launch failed: do nothing
+}
+
+__device__ __forceinline__ void step_end(unsigned long long *bar, const StepPersist &P) {
+    __syncthreads();
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        __threadfence();
+        st_release_u64(bar + 1, P.launch + 1);
+    }
+}
+
+template <int LT, int ACT, bool KVF16>
+__global__ void __launch_bounds__(ST_THREADS, 1) dec_step_kernel(const StepArgs a) {
+    using KV = typename std::conditional<KVF16, __half, float>::type;
+    extern __shared__ __align__(128) uint8_t smem[];
+    StepPersist &P = *reinterpret_cast<StepPersist *>(smem);
+    uint8_t *sm = smem + ST_PERSIST;
+    unsigned long long *bar = a.bar;
+    if (!step_begin(a, P, bar)) return;
+    const int tid = threadIdx.x, pos = P.pos;
+    const int nbar = 5 * a.n_layers;                 // after the embedding and every phase but the last
+    const int q_dim = a.n_heads * ST_HD, kv_dim = a.n_kv_heads * ST_HD;
+    if (tid < ST_HD / 2) {
+        float c, s;
+        rope_cos_sin(pos, tid, ST_HD, a.rope_base, c, s);
+        P.rope[tid] = make_float2(c, s);
+    }
+    unsigned mb_par = 0;
+    int e = 0;
+
+    // embed: x = emb[seq[pos]]
+    step_prefetch(a, 0);
+    {
+        const int tok = __ldcg(a.seq + pos);
+        for (int i = blockIdx.x * ST_THREADS + tid; i < a.dim; i += a.grid * ST_THREADS) {
+            float v = 0.0f;
+            if (tok >= 0 && tok < a.vocab)
+                v = a.emb_f16 ? __half2float(reinterpret_cast<const __half *>(a.emb)[(size_t)tok * a.dim + i])
+                              : reinterpret_cast<const float *>(a.emb)[(size_t)tok * a.dim + i];
+            a.x[i] = v;
+        }
+    }
+    if (!step_barrier(a, P, bar, e++, nbar)) return;
+
+    // layers: 5 phases each, one matvec call site
+    const int last = 5 * a.n_layers;
+    const size_t kv_es = KVF16 ? 2 : 4;
+    for (int ph = 1; ph <= last; ++ph) {
+        step_prefetch(a, ph);
+        const int l = (ph - 1) / 5, k = (ph - 1) % 5;
+        if (k == 0 && pos > 0 && tid < 32) {
+            // the layer's cached K and V rows (positions 0..pos-1) into L2 for
+            // the attention phase that follows
+            const unsigned long long n = (unsigned long long)pos * kv_dim * kv_es;
+            const unsigned long long c = blockIdx.x, G = a.grid, CH = 32768;
+            const unsigned long long b0 = (n * c / G) & ~15ull, b1 = c + 1 == G ? n : ((n * (c + 1) / G) & ~15ull);
+            const uint8_t *kb = reinterpret_cast<const uint8_t *>(a.kc) + (size_t)l * a.max_seq * kv_dim * kv_es;
+            const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vc) + (size_t)l * a.max_seq * kv_dim * kv_es;
+            for (unsigned long long o = b0 + (unsigned long long)tid * CH; o < b1; o += 32 * CH) {
+                const uint32_t len = (uint32_t)(b1 - o < CH ? b1 - o : CH);
+                prefetch_l2_bulk(kb + o, len);
+                prefetch_l2_bulk(vb + o, len);
+            }
+        }
+        if (k == 1) {
+            step_attn<KV>(a, P, sm, l, pos);
+        } else {
+            const StepLayer &L = a.layers[l];
+            const uint8_t *W = k == 0 ? L.wqkv : k == 2 ? L.wo : k == 3 ? L.w13 : L.w2;
+            const int rows = k == 0 ? q_dim + 2 * kv_dim : k == 3 ? 2 * a.ffn : a.dim;
+            const int in_dim = k == 2 ? q_dim : k == 4 ? a.ffn : a.dim;
+            const float *x = k == 2 ? a.att : k == 4 ? a.h : a.x;
+            float *y = k == 0 ? a.qkv : k == 3 ? a.h : a.x;
+            const float *nw = k == 0 ? L.attn_norm : k == 3 ? L.ffn_norm : nullptr;
+            const int epi = k == 3 ? 2 : (k == 2 || k == 4) ? 1 : 0;
+            step_mv<LT, ACT>(a, P, sm, mb_par, W, rows, in_dim, x, y, a.x, nw, epi);
+        }
+        if (ph < last && !step_barrier(a, P, bar, e++, nbar)) return;
+    }
+    step_end(bar, P);
+}
+
+// output matrix (RMSNorm fused; skipped for prompt positions of a
+// generation), then the sampler on CTA 0, then the next position
+template <int OT, int ACT>
+__global__ void __launch_bounds__(ST_THREADS, 1) dec_out_kernel(const StepArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    StepPersist &P = *reinterpret_cast<StepPersist *>(smem);
+    uint8_t *sm = smem + ST_PERSIST;
+    unsigned long long *bar = a.bar + 2;
+    if (!step_begin(a, P, bar)) return;
+    const int tid = threadIdx.x, pos = P.pos;
+    unsigned mb_par = 0;
+    step_prefetch(a, step_phases(a.n_layers) - 1);
+    const bool need = !a.sa.gen || pos >= a.sa.n_prompt - 1;
+    if (need) step_mv<OT, ACT>(a, P, sm, mb_par, a.out_w, a.vocab, a.dim, a.x, a.logits, nullptr, a.final_norm, 0);
+    if (!step_barrier(a, P, bar, 0, 1)) return;
+    if (blockIdx.x == 0) {
+        if (a.sample && need) {
+            SampleSmem &S = *reinterpret_cast<SampleSmem *>(sm);
+            const int gi = a.sa.gen ? pos - (a.sa.n_prompt - 1) : 0;
+            const int nhist = __ldcg(a.nhist);
+            const int token = sample_body(S, a.logits, a.probs, a.kept_idx, a.kept_p, a.hist, nhist,
+                                          __ldcg(a.rvals + gi), a.status, a.sa);
+            if (token >= 0 && tid == 0) {
+                *a.last = token;
+                if (a.sa.gen) {
+                    a.seq[pos + 1] = token;
+                    a.hist[nhist] = token;
+                    *a.nhist = nhist + 1;
+                    a.out_tokens[gi] = token;
+                }
+            }
+        }
+        if (tid == 0) *a.pos = pos + 1;
+    }
+    step_end(bar, P);
+}
+
+size_t mv_smem(const StepArgs &a, int act, int type, int rows, int in_dim, bool norm) {
+    const int vals = type == GT_Q8_0 ? 128 : 256, b32 = type == GT_Q8_0 ? 4 : 8;
+    const int units = (in_dim + vals - 1) / vals, nblk32p = units * b32;
+    const int nrb = (rows + 31) / 32, nloc = (nrb + a.grid - 1) / a.grid;
+    size_t o = ((size_t)nloc * ST_WARPS * 32 * 4 + 127) & ~(size_t)127;
+    if (act == HOLO_ACT_Q8) o += (((size_t)nblk32p * 40 + 127) & ~(size_t)127) + (size_t)nblk32p * 128;
+    else o += ((size_t)nblk32p * 132 + 127) & ~(size_t)127;
+    if (norm) o += (size_t)nblk32p * 128;
+    return o + ST_WARPS * 4;
+}
+
+size_t layer_smem(const StepArgs &a, int lt, int act) {
+    const int q_dim = a.n_heads * ST_HD, kv_dim = a.n_kv_heads * ST_HD;
+    size_t m = mv_smem(a, act, lt, q_dim + 2 * kv_dim, a.dim, true);
+    m = std::max(m, mv_smem(a, act, lt, a.dim, q_dim, false));
+    m = std::max(m, mv_smem(a, act, lt, 2 * a.ffn, a.dim, true));
+    m = std::max(m, mv_smem(a, act, lt, a.dim, a.ffn, false));
+    m = std::max(m, (size_t)ST_WARPS * 2 * ST_HD * sizeof(float));   // attention scratch
+    return ST_PERSIST + m;
+}
+
+size_t out_smem(const StepArgs &a, int act) {
+    size_t m = mv_smem(a, act, a.out_type, a.vocab, a.dim, true);
+    if (a.sample) m = std::max(m, sizeof(SampleSmem));
+    return ST_PERSIST + m;
+}
+
+template <typename K>
+bool coop_launch(K kern, const StepArgs &a, size_t smem, cudaStream_t st) {
+    if (smem > 227 * 1024) {
+        holo_set_status(HOLO_E_UNSUPPORTED, "decode step: shared memory");
+        return false;
+    }
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+        return holo_check_launch("decode step: attributes");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.grid);
+    cfg.blockDim = dim3(ST_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;   // all CTAs resident: the grid barriers need it
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) return holo_check_launch("decode step launch");
+    return holo_check_launch("decode step launch");
+}
+
+template <int LT>
+bool launch_layers(const StepArgs &a, int act, int kv_f16, cudaStream_t st) {
+    const size_t smem = layer_smem(a, LT, act);
+    if (act == HOLO_ACT_Q8)
+        return kv_f16 ? coop_launch(dec_step_kernel<LT, HOLO_ACT_Q8, true>, a, smem, st)
+                      : coop_launch(dec_step_kernel<LT, HOLO_ACT_Q8, false>, a, smem, st);
+    return kv_f16 ? coop_launch(dec_step_kernel<LT, HOLO_ACT_F32, true>, a, smem, st)
+                  : coop_launch(dec_step_kernel<LT, HOLO_ACT_F32, false>, a, smem, st);
+}
+
+template <int OT>
+bool launch_out(const StepArgs &a, int act, cudaStream_t st) {
+    const size_t smem = out_smem(a, act);
+    return act == HOLO_ACT_Q8 ? coop_launch(dec_out_kernel<OT, HOLO_ACT_Q8>, a, smem, st)
+                              : coop_launch(dec_out_kernel<OT, HOLO_ACT_F32>, a, smem, st);
+}
+
+}  // namespace
+
+bool holo_step_launch(const StepArgs &a, int layer_type, int act, int kv_f16, cudaStream_t st) {
+    bool ok;
+    switch (layer_type) {
+    case GT_Q8_0: ok = launch_layers<GT_Q8_0>(a, act, kv_f16, st); break;
+    case GT_Q4_0: ok = launch_layers<GT_Q4_0>(a, act, kv_f16, st); break;
+    case GT_Q4_K: ok = launch_layers<GT_Q4_K>(a, act, kv_f16, st); break;
+    default:
+        holo_set_status(HOLO_E_ARG, "decode step: layer type");
+        return false;
+    }
+    if (!ok) return false;
+    switch (a.out_type) {
+    case GT_Q8_0: return launch_out<GT_Q8_0>(a, act, st);
+    case GT_Q4_0: return launch_out<GT_Q4_0>(a, act, st);
+    case GT_Q4_K: return launch_out<GT_Q4_K>(a, act, st);
+    default:
+        holo_set_status(HOLO_E_ARG, "decode step: output type");
+        return false;
+    }
+}
