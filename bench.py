@@ -401,15 +401,27 @@ def decode_bench(args, world, rank, torch):
     / top-p 0.95 / repeat penalty 1.1, fp16 KV cache) on a random-init
     Llama-2-7B-shape model built on the device.  tok/s from the device time of
     the decode phase; e2e from the wall time of the public holo_model_generate
-    call (prompt in, tokens out, prefill included)."""
-    from holo_b200.model import LLAMA2_7B, SamplerDesc, synthetic_model
+    call (prompt in, tokens out, prefill included).  With N ranks the model is
+    row-sharded over the N GPUs (strong scaling: one model, one token stream);
+    times are the maximum over the ranks."""
+    from holo_b200.model import LLAMA2_7B, SamplerDesc, connect_peers, synthetic_model
     cfg = dict(LLAMA2_7B)
     act = hb.ACT_Q8 if args.act == "q8" else hb.ACT_F32
     want_cpu = rank == 0 and world == 1 and not args.no_cpu
     t0 = time.perf_counter()
-    built = synthetic_model(cfg, seed=0, act_mode=act, kv_f16=True, keep_host=want_cpu)
+    built = synthetic_model(cfg, seed=0, act_mode=act, kv_f16=True, keep_host=want_cpu, world=world, rank=rank)
     m, host = built if want_cpu else (built, None)
+    if world > 1:
+        connect_peers(m)
     build_s = time.perf_counter() - t0
+
+    def max_over_ranks(*vals):
+        if world == 1:
+            return vals
+        import torch.distributed as dist
+        t = torch.tensor(vals, device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return tuple(float(v) for v in t.tolist())
     prompt = np.random.default_rng(0).integers(0, cfg["vocab"], size=DECODE_PROMPT).astype(np.int32)
     s = SamplerDesc(0.8, 0.95, 40, 1.1, 64)
     m.generate(prompt, DECODE_NEW, s, seed=0)            # warm-up (graph capture, caches)
@@ -420,15 +432,21 @@ def decode_bench(args, world, rank, torch):
         toks = m.generate(prompt, DECODE_NEW, s, seed=i)
         wall = time.perf_counter() - w0
         pre_ms, dec_ms = m.last_timing()
+        dec_ms, pre_ms, wall = max_over_ranks(dec_ms, pre_ms, wall)
         runs.append((dec_ms, pre_ms, wall, toks))
+    first_tokens = runs[0][3]      # seed 0
     runs.sort(key=lambda r: r[0])
     dec_ms, pre_ms, wall, toks = runs[len(runs) // 2]
     tok_s = DECODE_NEW / (dec_ms * 1e-3)
     bpt, wbytes = decode_bytes_per_token(cfg)
     peak, peak_kind = peaks()
+    peak *= world                 # the shards stream from every GPU's HBM at once
+    step_kernel = cfg["head_dim"] == 128 and os.environ.get("HOLO_STEP") != "graph"
     out = {
         "config": "Llama-2-7B shape, Q4_K layers, Q8_0 lm_head, fp16 embeddings and KV cache, ctx 2048; "
-                  f"prompt {DECODE_PROMPT}, {DECODE_NEW} new tokens, T 0.8 / top-k 40 / top-p 0.95 / rep 1.1",
+                  f"prompt {DECODE_PROMPT}, {DECODE_NEW} new tokens, T 0.8 / top-k 40 / top-p 0.95 / rep 1.1"
+                  + (f"; row-sharded over {world} GPUs" if world > 1 else ""),
+        "scaling": "strong", "n_gpus": world,
         "act_mode": args.act, "value": round(tok_s, 1), "unit": "tokens/s", "ms_per_token": round(dec_ms / DECODE_NEW, 4),
         "prefill_ms": round(pre_ms, 2), "prefill_tokens_s": round((DECODE_PROMPT - 1) / (pre_ms * 1e-3), 1),
         "roofline": {"bound": "hbm", "bytes_per_token": int(bpt), "weight_bytes_per_token": int(wbytes),
@@ -437,9 +455,9 @@ def decode_bench(args, world, rank, torch):
         "e2e": {"value": round(DECODE_NEW / wall, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * DECODE_PROMPT,
                 "d2h_bytes_per_step": 4 * DECODE_NEW,
                 "path": "holo_model_generate: prompt ids in, generated ids out, prefill included"},
-        "gpu_launches_per_token": cfg["n_layers"] * 7 + 4,
+        "gpu_launches_per_token": 2 if step_kernel else cfg["n_layers"] * 7 + 4,
         "model_build_s": round(build_s, 1),
-        "tokens_head": [int(t) for t in toks[:8]],
+        "tokens_head_seed0": [int(t) for t in first_tokens[:8]],
     }
     if want_cpu and host is not None:
         out["cpu_baseline"] = decode_cpu_baseline(cfg, host, prompt, budget_s=args.cpu_budget)
@@ -575,6 +593,7 @@ def main():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 7B decode sub-benchmark")
     ap.add_argument("--profile-decode", action="store_true", help="small 7B decode case for ncu")
+    ap.add_argument("--decode-only", action="store_true", help="only the 7B decode sub-benchmark")
     ap.add_argument("--profile-case", default=None, help="e.g. q4_k:11008x4096 (ncu small case)")
     ap.add_argument("--iters", type=int, default=4)
     args = ap.parse_args()
@@ -600,7 +619,16 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.decode_only:
+            import torch
+            torch.cuda.set_device(local_rank)
+            hb.Device(local_rank, world)
+            args.no_cpu = True
+            d = decode_bench(args, world, rank, torch)
+            if rank == 0:
+                print(json.dumps({"decode": d}), flush=True)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

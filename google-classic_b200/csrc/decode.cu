@@ -315,7 +315,21 @@ struct HoloLayer {
 
 struct HoloModel {
     holo_model_desc d{};
-    int q_dim = 0, kv_dim = 0;
+    int q_dim = 0, kv_dim = 0;     // this rank's query / KV rows (all of them when world == 1)
+    int q_dim_g = 0;               // query rows of the model (the attention output length)
+    // row shard of this rank (StepArgs): heads [h0, h0 + nh), KV heads
+    // [kh0, kh0 + nkv), Wo/W2 rows [d0, d0 + dim_loc), SwiGLU outputs
+    // [f0, f0 + ffn_loc), output rows [v0, v0 + vocab_loc)
+    int world = 1, rank = 0;
+    int nh = 0, h0 = 0, nkv = 0, kh0 = 0, dim_loc = 0, d0 = 0, ffn_loc = 0, f0 = 0, vocab_loc = 0, v0 = 0;
+    // the step kernel's LL vectors (step.cuh) of x, the attention output, the
+    // SwiGLU output and the logits in one allocation that the other ranks map
+    // (cudaIpc*), and the local LL QKV output
+    uint8_t *comm = nullptr;
+    size_t comm_bytes = 0, off_x = 0, off_att = 0, off_h = 0, off_log = 0;
+    StepWord *qkv_ll = nullptr;
+    uint8_t *peer[STEP_MAX_RANKS] = {};
+    bool peers_ready = false;
     std::vector<HoloLayer> layers;
     void *emb = nullptr;
     float *final_norm = nullptr;
@@ -342,6 +356,15 @@ struct HoloModel {
     unsigned long long *d_bar = nullptr;
     int *d_att_cnt = nullptr;
 };
+
+// the handle one rank gives the others
+struct CommHandle {
+    cudaIpcMemHandle_t ipc;
+    int rank, world, grid, magic;
+    unsigned long long comm_bytes;
+};
+static_assert(sizeof(CommHandle) <= HOLO_COMM_HANDLE_BYTES, "comm handle");
+constexpr int COMM_MAGIC = 0x484f4c4f;
 
 namespace {
 
@@ -593,11 +616,14 @@ bool build_step(HoloModel *m) {
 StepArgs step_args(HoloModel *m, bool sample, const SampleArgs &sa) {
     const holo_model_desc &d = m->d;
     StepArgs a{};
-    a.n_layers = d.n_layers; a.dim = d.dim; a.n_heads = d.n_heads; a.n_kv_heads = d.n_kv_heads;
+    a.n_layers = d.n_layers; a.dim = d.dim; a.n_heads = m->nh; a.n_kv_heads = m->nkv; a.h0 = m->h0;
+    a.n_heads_g = d.n_heads;
+    a.dim_loc = m->dim_loc; a.d0 = m->d0; a.ffn_loc = m->ffn_loc; a.f0 = m->f0;
+    a.vocab_loc = m->vocab_loc; a.v0 = m->v0;
     a.hd = d.head_dim; a.ffn = d.ffn_dim; a.vocab = d.vocab; a.max_seq = d.max_seq;
     a.eps = d.eps; a.rope_base = d.rope_base; a.out_type = d.out_type; a.emb_f16 = d.emb_type == 1;
     a.layers = m->d_layers; a.emb = m->emb; a.final_norm = m->final_norm; a.out_w = m->out;
-    a.x = m->x; a.qkv = m->qkv; a.att = m->att; a.h = m->h; a.logits = m->logits;
+    a.qkv = m->qkv_ll; a.logits = m->logits;
     a.kc = m->kc; a.vc = m->vc; a.att_part = m->part; a.att_cnt = m->d_att_cnt;
     a.per_split = 16; a.max_splits = m->step_max_splits;
     a.pos = m->d_pos; a.seq = m->d_seq; a.hist = m->d_hist; a.nhist = m->d_nhist; a.out_tokens = m->d_out;
@@ -606,12 +632,47 @@ StepArgs step_args(HoloModel *m, bool sample, const SampleArgs &sa) {
     HoloDevice *D = holo_dev();
     a.status = D ? D->status : nullptr;
     a.grid = D ? D->sms : 1;
+    a.world = m->world;
+    a.rank = m->rank;
+    for (int r = 0; r < m->world; ++r) {
+        uint8_t *c = r == m->rank ? m->comm : m->peer[r];
+        a.px[r] = reinterpret_cast<StepWord *>(c + m->off_x);
+        a.patt[r] = reinterpret_cast<StepWord *>(c + m->off_att);
+        a.ph[r] = reinterpret_cast<StepWord *>(c + m->off_h);
+        a.plog[r] = reinterpret_cast<StepWord *>(c + m->off_log);
+    }
     return a;
 }
 
 bool run_step(HoloModel *m, bool sample, const SampleArgs &sa, cudaStream_t st) {
+    if (m->world > 1 && !m->peers_ready) {
+        holo_set_status(HOLO_E_ARG, "holo_model: sharded model without peers (holo_model_open_peers)");
+        return false;
+    }
     if (!m->step_ready && !build_step(m)) return false;
     return holo_step_launch(step_args(m, sample, sa), m->d.layer_type, m->d.act_mode, m->d.kv_f16, st);
+}
+
+// the row shard of d.rank (host only): ranges = first and count of query
+// heads, KV heads, Wo/W2 rows, SwiGLU outputs (16-row bands), output rows
+bool shard_of(const holo_model_desc &d, int ranges[10]) {
+    const int world = d.world <= 1 ? 1 : d.world, r = d.rank;
+    if (world > STEP_MAX_RANKS || r < 0 || r >= world || d.n_heads <= 0 || d.n_kv_heads <= 0 ||
+        d.n_heads % world || d.n_kv_heads % world || d.dim < 32 * world || d.ffn_dim % 16 ||
+        d.ffn_dim < 16 * world || d.vocab < world)
+        return false;
+    auto split = [&](int n, int unit, int *o) {
+        const long long b = n / unit;
+        const int lo = (int)(b * r / world), hi = (int)(b * (r + 1) / world);
+        o[0] = unit * lo;
+        o[1] = unit * (hi - lo);
+    };
+    split(d.n_heads, 1, ranges);
+    split(d.n_kv_heads, 1, ranges + 2);
+    split(d.dim, 1, ranges + 4);
+    split(d.ffn_dim, 16, ranges + 6);
+    split(d.vocab, 1, ranges + 8);
+    return true;
 }
 
 SampleArgs make_args(const HoloModel *m, const holo_sampler_desc *s) {
@@ -638,6 +699,12 @@ void *holo_model_create(const holo_model_desc *desc) {
     if (!desc) return nullptr;
     const holo_model_desc &d = *desc;
     const int hd = d.head_dim;
+    const int world = d.world <= 1 ? 1 : d.world;
+    int sh[10];
+    if (!shard_of(d, sh) || (world > 1 && hd != 128)) {
+        holo_set_status(HOLO_E_ARG, "holo_model_create: unsupported sharding");
+        return nullptr;
+    }
     if (d.n_layers <= 0 || d.dim <= 0 || d.n_heads <= 0 || d.n_kv_heads <= 0 || d.n_heads % d.n_kv_heads ||
         !(hd == 64 || hd == 128 || hd == 256) || d.ffn_dim <= 0 || d.ffn_dim % 16 || d.vocab <= 0 ||
         d.max_seq <= 0 || (d.act_mode != HOLO_ACT_Q8 && d.act_mode != HOLO_ACT_F32) ||
@@ -654,24 +721,46 @@ void *holo_model_create(const holo_model_desc *desc) {
     if (!D) return nullptr;
     HoloModel *m = new HoloModel();
     m->d = d;
-    m->q_dim = d.n_heads * hd;
-    m->kv_dim = d.n_kv_heads * hd;
+    m->d.world = world;
+    m->world = world;
+    m->rank = d.rank;
+    m->h0 = sh[0]; m->nh = sh[1];
+    m->kh0 = sh[2]; m->nkv = sh[3];
+    m->d0 = sh[4]; m->dim_loc = sh[5];
+    m->f0 = sh[6]; m->ffn_loc = sh[7];
+    m->v0 = sh[8]; m->vocab_loc = sh[9];
+    m->q_dim = m->nh * hd;
+    m->kv_dim = m->nkv * hd;
+    m->q_dim_g = d.n_heads * hd;
     m->layers.resize(d.n_layers);
     m->max_splits = (d.max_seq + m->per_split - 1) / m->per_split;
     // the step kernel splits attention into 16-position pieces at the least
     m->step_max_splits = (d.max_seq + 15) / 16;
     const size_t kv_bytes = (size_t)d.n_layers * d.max_seq * m->kv_dim * (d.kv_f16 ? 2 : 4);
     bool ok = dev_alloc(&m->kc, kv_bytes) && dev_alloc(&m->vc, kv_bytes);
+    // comm: the LL vectors x, att, h, logits (full length), 256-byte aligned
+    {
+        auto a256 = [](size_t v) { return (v + 255) & ~(size_t)255; };
+        size_t o = 0;
+        m->off_x = o; o = a256(o + sizeof(StepWord) * d.dim);
+        m->off_att = o; o = a256(o + sizeof(StepWord) * m->q_dim_g);
+        m->off_h = o; o = a256(o + sizeof(StepWord) * d.ffn_dim);
+        m->off_log = o; o = a256(o + sizeof(StepWord) * d.vocab);
+        m->comm_bytes = o;
+    }
+    ok = ok && dev_alloc((void **)&m->comm, m->comm_bytes);
+    ok = ok && dev_alloc((void **)&m->qkv_ll, sizeof(StepWord) * (m->q_dim + 2 * m->kv_dim));
+    // plain vectors of the one-launch-per-op graph (and the logits of both)
     ok = ok && dev_alloc((void **)&m->x, sizeof(float) * d.dim);
     ok = ok && dev_alloc((void **)&m->qkv, sizeof(float) * (m->q_dim + 2 * m->kv_dim));
-    ok = ok && dev_alloc((void **)&m->att, sizeof(float) * m->q_dim);
+    ok = ok && dev_alloc((void **)&m->att, sizeof(float) * m->q_dim_g);
     ok = ok && dev_alloc((void **)&m->h, sizeof(float) * d.ffn_dim);
     ok = ok && dev_alloc((void **)&m->logits, sizeof(float) * d.vocab);
     ok = ok && dev_alloc((void **)&m->probs, sizeof(float) * d.vocab);
     ok = ok && dev_alloc((void **)&m->kept_p, sizeof(float) * d.vocab);
     ok = ok && dev_alloc((void **)&m->kept_idx, sizeof(int) * d.vocab);
     ok = ok && dev_alloc((void **)&m->part,
-                         sizeof(float) * (size_t)d.n_heads * std::max(m->max_splits, m->step_max_splits) * (hd + 4));
+                         sizeof(float) * (size_t)m->nh * std::max(m->max_splits, m->step_max_splits) * (hd + 4));
     ok = ok && dev_alloc((void **)&m->rvals, sizeof(float) * (d.max_seq + 1));
     ok = ok && dev_alloc((void **)&m->d_pos, sizeof(int) * 4);
     ok = ok && dev_alloc((void **)&m->d_seq, sizeof(int) * (d.max_seq + 1));
@@ -680,7 +769,7 @@ void *holo_model_create(const holo_model_desc *desc) {
     ok = ok && dev_alloc((void **)&m->d_out, sizeof(int) * (d.max_seq + 1));
     ok = ok && dev_alloc((void **)&m->d_last, sizeof(int) * 4);
     ok = ok && dev_alloc((void **)&m->d_bar, sizeof(unsigned long long) * 4);
-    ok = ok && dev_alloc((void **)&m->d_att_cnt, sizeof(int) * d.n_heads);
+    ok = ok && dev_alloc((void **)&m->d_att_cnt, sizeof(int) * m->nh);
     if (!ok) {
         holo_model_free(m);
         return nullptr;
@@ -697,8 +786,15 @@ void *holo_model_create(const holo_model_desc *desc) {
         const char *e = getenv("HOLO_STEP");
         m->use_step = hd == 128 && !(e && strcmp(e, "graph") == 0);
     }
+    if (world > 1 && !m->use_step) {
+        holo_set_status(HOLO_E_UNSUPPORTED, "holo_model_create: sharding needs the step kernel (HOLO_STEP)");
+        holo_model_free(m);
+        return nullptr;
+    }
+    cudaMemset(m->comm, 0, m->comm_bytes);
+    cudaMemset(m->qkv_ll, 0, sizeof(StepWord) * (m->q_dim + 2 * m->kv_dim));
     cudaMemset(m->d_bar, 0, sizeof(unsigned long long) * 4);
-    cudaMemset(m->d_att_cnt, 0, sizeof(int) * d.n_heads);
+    cudaMemset(m->d_att_cnt, 0, sizeof(int) * m->nh);
     cudaMemset(m->kc, 0, kv_bytes);
     cudaMemset(m->vc, 0, kv_bytes);
     cudaMemset(m->d_pos, 0, sizeof(int) * 4);
@@ -729,41 +825,49 @@ int holo_model_set_layer(void *model, int l, const float *attn_norm, const void 
         return HOLO_E_NOMEM;
     cudaMemcpyAsync(L.attn_norm, attn_norm, sizeof(float) * d.dim, cudaMemcpyDefault, st);
     cudaMemcpyAsync(L.ffn_norm, ffn_norm, sizeof(float) * d.dim, cudaMemcpyDefault, st);
+    // this rank's rows of each matrix (all rows when world == 1); GGUF rows
+    // are contiguous, so a row range is a byte range of the source
+    const size_t row_dim = (size_t)gguf_row_bytes(t, d.dim);
+    const int hd = d.head_dim;
+    auto rows_of = [](const void *p, size_t first_row, size_t row_bytes) {
+        return static_cast<const void *>(static_cast<const uint8_t *>(p) + first_row * row_bytes);
+    };
     // [Wq; Wk; Wv] in one tiled buffer (each part a whole number of row-blocks)
     const size_t bq = cuda_quant_tiled_bytes(t, m->q_dim, d.dim), bk = cuda_quant_tiled_bytes(t, m->kv_dim, d.dim);
     if (!L.wqkv && !dev_alloc((void **)&L.wqkv, bq + 2 * bk)) return HOLO_E_NOMEM;
-    if (!upload_repack(L.wqkv, wq, t, m->q_dim, d.dim, st) ||
-        !upload_repack(L.wqkv + bq, wk, t, m->kv_dim, d.dim, st) ||
-        !upload_repack(L.wqkv + bq + bk, wv, t, m->kv_dim, d.dim, st))
+    if (!upload_repack(L.wqkv, rows_of(wq, (size_t)m->h0 * hd, row_dim), t, m->q_dim, d.dim, st) ||
+        !upload_repack(L.wqkv + bq, rows_of(wk, (size_t)m->kh0 * hd, row_dim), t, m->kv_dim, d.dim, st) ||
+        !upload_repack(L.wqkv + bq + bk, rows_of(wv, (size_t)m->kh0 * hd, row_dim), t, m->kv_dim, d.dim, st))
         return cuda_last_status();
     L.i_qkv = holo_weight_info(t, m->q_dim + 2 * m->kv_dim, d.dim, holo_q4k_layout());
-    if (!L.wo && !dev_alloc((void **)&L.wo, cuda_quant_tiled_bytes(t, d.dim, m->q_dim))) return HOLO_E_NOMEM;
-    if (!upload_repack(L.wo, wo, t, d.dim, m->q_dim, st)) return cuda_last_status();
-    L.i_o = holo_weight_info(t, d.dim, m->q_dim, holo_q4k_layout());
+    if (!L.wo && !dev_alloc((void **)&L.wo, cuda_quant_tiled_bytes(t, m->dim_loc, m->q_dim_g))) return HOLO_E_NOMEM;
+    if (!upload_repack(L.wo, rows_of(wo, m->d0, gguf_row_bytes(t, m->q_dim_g)), t, m->dim_loc, m->q_dim_g, st))
+        return cuda_last_status();
+    L.i_o = holo_weight_info(t, m->dim_loc, m->q_dim_g, holo_q4k_layout());
     // W1 and W3 interleaved by 16 rows: row-block b = W1 rows 16b..16b+15, W3 rows 16b..16b+15
-    const size_t rb = (size_t)gguf_row_bytes(t, d.dim);
     void *inter = nullptr;
-    if (!dev_alloc(&inter, (size_t)2 * d.ffn_dim * rb)) return HOLO_E_NOMEM;
-    const size_t band = 16 * rb;
-    bool ok = cudaMemcpy2DAsync(inter, 2 * band, w1, band, band, d.ffn_dim / 16, cudaMemcpyDefault, st) ==
-                  cudaSuccess &&
-              cudaMemcpy2DAsync((uint8_t *)inter + band, 2 * band, w3, band, band, d.ffn_dim / 16,
-                                cudaMemcpyDefault, st) == cudaSuccess;
-    if (!L.w13 && !dev_alloc((void **)&L.w13, cuda_quant_tiled_bytes(t, 2 * d.ffn_dim, d.dim))) {
+    if (!dev_alloc(&inter, (size_t)2 * m->ffn_loc * row_dim)) return HOLO_E_NOMEM;
+    const size_t band = 16 * row_dim;
+    bool ok = cudaMemcpy2DAsync(inter, 2 * band, rows_of(w1, m->f0, row_dim), band, band, m->ffn_loc / 16,
+                                cudaMemcpyDefault, st) == cudaSuccess &&
+              cudaMemcpy2DAsync((uint8_t *)inter + band, 2 * band, rows_of(w3, m->f0, row_dim), band, band,
+                                m->ffn_loc / 16, cudaMemcpyDefault, st) == cudaSuccess;
+    if (!L.w13 && !dev_alloc((void **)&L.w13, cuda_quant_tiled_bytes(t, 2 * m->ffn_loc, d.dim))) {
         cudaFree(inter);
         return HOLO_E_NOMEM;
     }
-    ok = ok && upload_repack(L.w13, inter, t, 2 * d.ffn_dim, d.dim, st);
+    ok = ok && upload_repack(L.w13, inter, t, 2 * m->ffn_loc, d.dim, st);
     cudaStreamSynchronize(st);
     cudaFree(inter);
     if (!ok) {
         holo_check_launch("holo_model_set_layer: w1/w3");
         return cuda_last_status() ? cuda_last_status() : HOLO_E_ARG;
     }
-    L.i_13 = holo_weight_info(t, 2 * d.ffn_dim, d.dim, holo_q4k_layout());
-    if (!L.w2 && !dev_alloc((void **)&L.w2, cuda_quant_tiled_bytes(t, d.dim, d.ffn_dim))) return HOLO_E_NOMEM;
-    if (!upload_repack(L.w2, w2, t, d.dim, d.ffn_dim, st)) return cuda_last_status();
-    L.i_2 = holo_weight_info(t, d.dim, d.ffn_dim, holo_q4k_layout());
+    L.i_13 = holo_weight_info(t, 2 * m->ffn_loc, d.dim, holo_q4k_layout());
+    if (!L.w2 && !dev_alloc((void **)&L.w2, cuda_quant_tiled_bytes(t, m->dim_loc, d.ffn_dim))) return HOLO_E_NOMEM;
+    if (!upload_repack(L.w2, rows_of(w2, m->d0, gguf_row_bytes(t, d.ffn_dim)), t, m->dim_loc, d.ffn_dim, st))
+        return cuda_last_status();
+    L.i_2 = holo_weight_info(t, m->dim_loc, d.ffn_dim, holo_q4k_layout());
     cudaStreamSynchronize(st);
     L.ready = cuda_last_status() == HOLO_OK;
     return L.ready ? HOLO_OK : cuda_last_status();
@@ -784,10 +888,12 @@ int holo_model_set_globals(void *model, const void *tok_embeddings, const float 
     cudaMemcpyAsync(m->emb, tok_embeddings, eb, cudaMemcpyDefault, st);
     if (!m->final_norm && !dev_alloc((void **)&m->final_norm, sizeof(float) * d.dim)) return HOLO_E_NOMEM;
     cudaMemcpyAsync(m->final_norm, final_norm, sizeof(float) * d.dim, cudaMemcpyDefault, st);
-    if (!m->out && !dev_alloc((void **)&m->out, cuda_quant_tiled_bytes(d.out_type, d.vocab, d.dim)))
+    if (!m->out && !dev_alloc((void **)&m->out, cuda_quant_tiled_bytes(d.out_type, m->vocab_loc, d.dim)))
         return HOLO_E_NOMEM;
-    if (!upload_repack(m->out, output, d.out_type, d.vocab, d.dim, st)) return cuda_last_status();
-    m->i_out = holo_weight_info(d.out_type, d.vocab, d.dim, holo_q4k_layout());
+    const void *out_rows =
+        static_cast<const uint8_t *>(output) + (size_t)m->v0 * gguf_row_bytes(d.out_type, d.dim);
+    if (!upload_repack(m->out, out_rows, d.out_type, m->vocab_loc, d.dim, st)) return cuda_last_status();
+    m->i_out = holo_weight_info(d.out_type, m->vocab_loc, d.dim, holo_q4k_layout());
     cudaStreamSynchronize(st);
     m->globals_ready = cuda_last_status() == HOLO_OK;
     return m->globals_ready ? HOLO_OK : cuda_last_status();
@@ -987,14 +1093,84 @@ int holo_model_last_timing(void *model, float *prefill_ms, float *decode_ms) {
     return HOLO_OK;
 }
 
+int holo_model_shard(const holo_model_desc *desc, int *ranges) {
+    if (!desc || !ranges || !shard_of(*desc, ranges)) {
+        holo_set_status(HOLO_E_ARG, "holo_model_shard: desc cannot be sharded");
+        return HOLO_E_ARG;
+    }
+    return HOLO_OK;
+}
+
+int holo_model_comm_handle(void *model, void *handle) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m || !handle) {
+        holo_set_status(HOLO_E_ARG, "holo_model_comm_handle: bad arguments");
+        return HOLO_E_ARG;
+    }
+    CommHandle h{};
+    if (cudaIpcGetMemHandle(&h.ipc, m->comm) != cudaSuccess) {
+        holo_check_launch("holo_model_comm_handle: cudaIpcGetMemHandle");
+        return cuda_last_status() ? cuda_last_status() : HOLO_E_COMM;
+    }
+    HoloDevice *D = holo_dev();
+    h.rank = m->rank;
+    h.world = m->world;
+    h.grid = D ? D->sms : 0;
+    h.magic = COMM_MAGIC;
+    h.comm_bytes = m->comm_bytes;
+    memset(handle, 0, HOLO_COMM_HANDLE_BYTES);
+    memcpy(handle, &h, sizeof(h));
+    return HOLO_OK;
+}
+
+int holo_model_open_peers(void *model, const void *handles) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m || !handles) {
+        holo_set_status(HOLO_E_ARG, "holo_model_open_peers: bad arguments");
+        return HOLO_E_ARG;
+    }
+    HoloDevice *D = holo_dev();
+    const int grid = D ? D->sms : 0;
+    // every rank's handle must describe the same model and grid, in rank order
+    for (int r = 0; r < m->world; ++r) {
+        CommHandle h;
+        memcpy(&h, static_cast<const uint8_t *>(handles) + (size_t)r * HOLO_COMM_HANDLE_BYTES, sizeof(h));
+        if (h.magic != COMM_MAGIC || h.rank != r || h.world != m->world || h.grid != grid ||
+            h.comm_bytes != m->comm_bytes) {
+            holo_set_status(HOLO_E_COMM, "holo_model_open_peers: handles differ in rank, world, grid or model");
+            return HOLO_E_COMM;
+        }
+    }
+    for (int r = 0; r < m->world; ++r) {
+        if (r == m->rank || m->peer[r]) continue;
+        CommHandle h;
+        memcpy(&h, static_cast<const uint8_t *>(handles) + (size_t)r * HOLO_COMM_HANDLE_BYTES, sizeof(h));
+        void *p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, h.ipc, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            holo_check_launch("holo_model_open_peers: cudaIpcOpenMemHandle");
+            return cuda_last_status() ? cuda_last_status() : HOLO_E_COMM;
+        }
+        m->peer[r] = static_cast<uint8_t *>(p);
+    }
+    m->peers_ready = true;
+    return HOLO_OK;
+}
+
 void holo_model_reset(void *model) {
     HoloModel *m = (HoloModel *)model;
     if (!m) return;
     cudaStream_t st = holo_stream();
     cudaMemsetAsync(m->d_pos, 0, sizeof(int), st);
     cudaMemsetAsync(m->d_nhist, 0, sizeof(int), st);
-    cudaMemsetAsync(m->d_bar, 0, sizeof(unsigned long long) * 4, st);
-    cudaMemsetAsync(m->d_att_cnt, 0, sizeof(int) * m->d.n_heads, st);
+    // one GPU: launch counters (the LL epochs) restart with cleared LL
+    // vectors.  Sharded, they only grow: the epochs must agree across ranks,
+    // which reset at different times.
+    if (m->world == 1) {
+        cudaMemsetAsync(m->d_bar, 0, sizeof(unsigned long long) * 4, st);
+        cudaMemsetAsync(m->comm, 0, m->comm_bytes, st);
+        cudaMemsetAsync(m->qkv_ll, 0, sizeof(StepWord) * (m->q_dim + 2 * m->kv_dim), st);
+    }
+    cudaMemsetAsync(m->d_att_cnt, 0, sizeof(int) * m->nh, st);
     cudaStreamSynchronize(st);
     m->h_pos = 0;
     m->h_nhist = 0;
@@ -1007,12 +1183,17 @@ void holo_model_free(void *model) {
     drop_graphs(m);
     for (auto &e : m->ev)
         if (e) cudaEventDestroy(e);
+    for (uint8_t *&p : m->peer)
+        if (p) {
+            cudaIpcCloseMemHandle(p);
+            p = nullptr;
+        }
     for (auto &L : m->layers) {
         cudaFree(L.attn_norm); cudaFree(L.ffn_norm); cudaFree(L.wqkv); cudaFree(L.wo); cudaFree(L.w13);
         cudaFree(L.w2);
     }
-    void *bufs[] = {m->emb, m->final_norm, m->out, m->kc, m->vc, m->x, m->qkv, m->att, m->h, m->logits,
-                    m->part, m->probs, m->kept_p, m->rvals, m->kept_idx, m->d_pos, m->d_seq, m->d_hist,
+    void *bufs[] = {m->emb, m->final_norm, m->out, m->kc, m->vc, m->comm, m->qkv_ll, m->x, m->qkv, m->att,
+                    m->h, m->logits, m->part, m->probs, m->kept_p, m->rvals, m->kept_idx, m->d_pos, m->d_seq, m->d_hist,
                     m->d_nhist, m->d_out, m->d_last, m->d_layers, m->d_pf, m->d_bar, m->d_att_cnt};
     for (void *p : bufs) cudaFree(p);
     delete m;

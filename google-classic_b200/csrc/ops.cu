@@ -110,10 +110,10 @@ __global__ void softmax_kernel(float *dst, const float *x, int n) {
 constexpr int ATT_WARPS = 4;
 constexpr int ATT_MAX_HD = 256;
 
+// the cache element as float (fp32 caches: the reference's; an fp16 cache
+// would convert here)
 template <typename KV>
-__device__ __forceinline__ float kv_load(const KV *p) { return (float)*p; }
-template <>
-__device__ __forceinline__ float kv_load<__half>(const __half *p) { return __half2float(*p); }
+__device__ __forceinline__ float kv_load(const KV *p) { return static_cast<float>(*p); }
 
 template <typename KV>
 __global__ void __launch_bounds__(ATT_WARPS * 32)

@@ -1,7 +1,7 @@
 // step.cu -- one decode step (one token) as a single persistent kernel.
 //
 // The step of decode.cu as phases of one cooperative launch, one 256-thread
-// CTA per SM, with bounded grid barriers between the phases:
+// CTA per SM:
 //
 //   embed | per layer: QKV (RMSNorm fused) | RoPE + KV append + attention |
 //   Wo (+x) | W1/W3 (RMSNorm, SwiGLU) | W2 (+x) | output matrix (RMSNorm) |
@@ -9,14 +9,19 @@
 //
 // The reference's sequence is the same as in decode.cu (src/ai/llm.c:1015-1269,
 // 1281-1328).  What the single kernel buys over one launch per op:
-//   * no launch or drain between ops: a phase starts when the barrier opens;
+//   * no launch, drain or grid barrier between ops: the vectors between
+//     phases are LL vectors (step.cuh), so a CTA starts a phase as soon as the
+//     elements it reads carry the producing phase's epoch;
 //   * every matvec phase gives each CTA whole row-blocks, so outputs are final
 //     in the CTA (no split-K fix-up, no atomics);
 //   * an L2 prefetch table keeps ~32 MB of upcoming weights requested from
 //     HBM at all times (cp.async.bulk.prefetch.L2, split over the CTAs), so HBM
 //     streams while the phases compute from L2.
-// Every wait (barriers, bulk copies) is bounded; a CTA that gives up records
-// HOLO_E_TIMEOUT, and later launches see the status and return at once.
+// Sharded over several GPUs (one process each), the phases store their
+// slices into every rank's LL copies over NVLink; nothing else changes.
+// Every wait (LL polls, bulk copies) is bounded; a CTA that gives up records
+// HOLO_E_TIMEOUT, waits elsewhere see the status and give up too, and later
+// launches return at once.
 #include "holo_common.cuh"
 #include "mv_device.cuh"
 #include "mv_unit.cuh"
@@ -61,32 +66,119 @@ __device__ __forceinline__ void st_release_u64(unsigned long long *p, unsigned l
     asm volatile("st.release.gpu.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
 }
 
-// Grid barrier: arrivals counted on a 64-bit counter (bar[0]) that only
-// grows; barrier e of launch L of a kernel with n barriers per launch opens at
-// (L * n + e + 1) * grid arrivals.  bar[1] counts the kernel's launches.
-__device__ bool step_barrier(const StepArgs &a, StepPersist &P, unsigned long long *bar, int e, int n) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned long long target = (P.launch * (unsigned long long)n + e + 1) * (unsigned long long)a.grid;
-        // release: the CTA's writes (ordered before this thread by the CTA
-        // barrier) are visible to whoever acquires the count
-        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" :: "l"(bar) : "memory");
-        bool ok = true;
-        if (ld_acquire_u64(bar) < target) {
-            const unsigned long long t0 = holo_globaltimer();
-            for (unsigned it = 1;; ++it) {
-                if (ld_acquire_u64(bar) >= target) break;
-                if ((it & 63u) == 0 && holo_globaltimer() - t0 > ST_WAIT_NS) {
-                    ok = false;
-                    atomicExch(a.status, HOLO_E_TIMEOUT);
-                    break;
-                }
-            }
+// ---------------------------------------------------------------------------
+// LL words (step.cuh): float in the low half, epoch in the high half.  The
+// accesses are volatile (never served from L1) and 8 or 16 bytes wide; every
+// 8-byte word is written and read whole.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ StepWord ll_word(float v, unsigned e) {
+    return ((StepWord)e << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ float ll_val(StepWord w) { return __uint_as_float((unsigned)w); }
+__device__ __forceinline__ bool ll_ok(StepWord w, unsigned e) { return (unsigned)(w >> 32) == e; }
+__device__ __forceinline__ void ll_st(StepWord *p, float v, unsigned e) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" :: "l"(p), "l"(ll_word(v, e)) : "memory");
+}
+__device__ __forceinline__ void ll_st2(StepWord *p, float a, float b, unsigned e) {
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" :: "l"(p), "l"(ll_word(a, e)), "l"(ll_word(b, e))
+                 : "memory");
+}
+__device__ __forceinline__ StepWord ll_ld(const StepWord *p) {
+    StepWord v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void ll_ld2(const StepWord *p, StepWord &a, StepWord &b) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// bookkeeping of one poll loop: false once ST_WAIT_NS has passed (status set)
+// or another CTA has already recorded an error
+struct Poll {
+    unsigned it = 0;
+    unsigned long long t0 = 0;
+    __device__ __forceinline__ bool again(int *status) {
+        if ((++it & 31u) != 0) return true;
+        if (*reinterpret_cast<volatile int *>(status) != 0) return false;
+        const unsigned long long t = holo_globaltimer();
+        if (t0 == 0) {
+            t0 = t;
+        } else if (t - t0 > ST_WAIT_NS) {
+            atomicExch(status, HOLO_E_TIMEOUT);
+            return false;
         }
-        P.ok = ok;
+        return true;
     }
-    __syncthreads();
-    return P.ok != 0;
+};
+
+// dst[0..n) <- the values of src[0..n) once every word holds epoch e (n even,
+// src 16-byte aligned; dst shared or global).  Each thread keeps LL_BATCH
+// 16-byte loads in flight and re-polls the batch until all are current.
+constexpr int LL_BATCH = 8;
+__device__ bool ll_gather(float *dst, const StepWord *src, int n, unsigned e, int *status) {
+    const int npair = n >> 1;
+    for (int base = threadIdx.x; base < npair; base += ST_THREADS * LL_BATCH) {
+        StepWord w[2 * LL_BATCH];
+        Poll poll;
+        for (;;) {
+#pragma unroll
+            for (int k = 0; k < LL_BATCH; ++k) {
+                const int i = base + k * ST_THREADS;
+                if (i < npair) ll_ld2(src + 2 * i, w[2 * k], w[2 * k + 1]);
+                else w[2 * k] = w[2 * k + 1] = (StepWord)e << 32;
+            }
+            bool ready = true;
+#pragma unroll
+            for (int k = 0; k < 2 * LL_BATCH; ++k) ready &= ll_ok(w[k], e);
+            if (ready) break;
+            if (!poll.again(status)) return false;
+        }
+#pragma unroll
+        for (int k = 0; k < LL_BATCH; ++k) {
+            const int i = base + k * ST_THREADS;
+            if (i < npair) *reinterpret_cast<float2 *>(dst + 2 * i) = make_float2(ll_val(w[2 * k]), ll_val(w[2 * k + 1]));
+        }
+    }
+    return true;
+}
+
+// one value (a word already known to be written, or nearly)
+__device__ __forceinline__ bool ll_get(const StepWord *p, unsigned e, int *status, float &v) {
+    Poll poll;
+    for (;;) {
+        const StepWord w = ll_ld(p);
+        if (ll_ok(w, e)) {
+            v = ll_val(w);
+            return true;
+        }
+        if (!poll.again(status)) return false;
+    }
+}
+
+// 16 consecutive values (16-byte aligned) into registers
+__device__ __forceinline__ bool ll_get16(const StepWord *p, unsigned e, int *status, float (&o)[16]) {
+    Poll poll;
+    for (;;) {
+        StepWord w[16];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ll_ld2(p + 2 * k, w[2 * k], w[2 * k + 1]);
+        bool ready = true;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) ready &= ll_ok(w[k], e);
+        if (ready) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) o[k] = ll_val(w[k]);
+            return true;
+        }
+        if (!poll.again(status)) return false;
+    }
+}
+
+// epoch of phase ph of the step that launch number `launch` runs: phase 0
+// embedding, 1 .. 5L the layers' phases, 5L + 1 the output matrix (never 0:
+// the buffers start zeroed)
+__device__ __forceinline__ unsigned step_epoch(const StepArgs &a, unsigned long long launch, int ph) {
+    return (unsigned)(launch * (unsigned long long)step_phases(a.n_layers) + (unsigned long long)ph + 1ull);
 }
 
 // this CTA's share of the phase's L2 prefetch ranges (warp 0, 32 KB requests)
@@ -111,14 +203,17 @@ __device__ __forceinline__ size_t align128(size_t v) { return (v + 127) & ~(size
 // ---------------------------------------------------------------------------
 // matvec phase: rows x in_dim unit-layout weight, whole row-blocks per CTA
 // ---------------------------------------------------------------------------
-// epi: 0 store, 1 y = residual + W.x, 2 SwiGLU over rows interleaved by 16;
-// norm_w non-NULL: RMSNorm of x first.  One instance per weight type: the
-// kernel calls it from a single site (separate inlined copies per phase
-// exhaust the register file).
+// x: LL input vector (epoch ex); epi: 0 store, 1 y = residual + W.x (residual
+// an LL vector of epoch er), 2 SwiGLU over rows interleaved by 16; norm_w
+// non-NULL: RMSNorm of x first.  rows: this rank's rows of W; output row j
+// goes to element yoff + j of ydst[0..ncopy) (every rank's copy) with epoch
+// ey.  One instance per weight type: the kernel calls it from a single site
+// (separate inlined copies per phase exhaust the register file).
 template <int TYPE, int ACT>
-__device__ __forceinline__ void step_mv(const StepArgs &a, StepPersist &P, uint8_t *sm, unsigned &mb_par,
-                        const uint8_t *__restrict__ W, int rows, int in_dim, const float *x, float *y,
-                        const float *residual, const float *norm_w, int epi) {
+__device__ __forceinline__ bool step_mv(const StepArgs &a, StepPersist &P, uint8_t *sm, unsigned &mb_par,
+                        const uint8_t *__restrict__ W, int rows, int in_dim, const StepWord *x, unsigned ex,
+                        StepWord *const *ydst, int ncopy, int yoff, unsigned ey, const StepWord *residual,
+                        unsigned er, const float *norm_w, int epi) {
     const bool norm = norm_w != nullptr;
     constexpr int BLKS32 = UnitGeom<TYPE>::BLKS32;
     constexpr size_t UB = UnitGeom<TYPE>::UNIT_BYTES;
@@ -126,7 +221,7 @@ __device__ __forceinline__ void step_mv(const StepArgs &a, StepPersist &P, uint8
     const int nrb = (rows + TILE_ROWS - 1) / TILE_ROWS;
     const int G = a.grid, c = blockIdx.x;
     const int rb0 = (int)((long long)nrb * c / G), rb1 = (int)((long long)nrb * (c + 1) / G);
-    if (rb0 >= rb1) return;
+    if (rb0 >= rb1) return true;
     const int nloc = rb1 - rb0;
     const int u0 = rb0 * units, u1 = rb1 * units;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -149,12 +244,12 @@ __device__ __forceinline__ void step_mv(const StepArgs &a, StepPersist &P, uint8
     if (norm) o += (size_t)nblk32p * 128;
     float *wsum = reinterpret_cast<float *>(sm + o);
 
-    // activations (and norm weights) by bulk copy: through L2, never a stale L1
+    // norm weights by bulk copy; the first weight units into registers while
+    // the activations are polled
     const uint32_t xbytes = (uint32_t)in_dim * 4u;
-    if (tid == 0) {
-        mbar_arrive_expect_tx(&P.mbar, norm ? 2u * xbytes : xbytes);
-        bulk_copy_g2s(xst, x, xbytes, &P.mbar);
-        if (norm) bulk_copy_g2s(nw, norm_w, xbytes, &P.mbar);
+    if (norm && tid == 0) {
+        mbar_arrive_expect_tx(&P.mbar, xbytes);
+        bulk_copy_g2s(nw, norm_w, xbytes, &P.mbar);
     }
     Frag ring[ST_DEPTH];
 #pragma unroll
@@ -167,9 +262,12 @@ __device__ __forceinline__ void step_mv(const StepArgs &a, StepPersist &P, uint8
         if (norm) nw[i] = 0.0f;
     }
     for (int i = tid; i < nloc * ST_WARPS * 32; i += ST_THREADS) red[i] = 0.0f;
-    const bool ok = mbar_wait_bounded(&P.mbar, mb_par, a.status, HOLO_E_TIMEOUT);
-    mb_par ^= 1u;
-    if (!__syncthreads_and(ok)) return;
+    bool ok = ll_gather(xst, x, in_dim, ex, a.status);
+    if (norm) {
+        ok = mbar_wait_bounded(&P.mbar, mb_par, a.status, HOLO_E_TIMEOUT) && ok;
+        mb_par ^= 1u;
+    }
+    if (!__syncthreads_and(ok)) return false;
     if (norm) act_prologue<ACT, true, ST_THREADS>(xst, nw, aq, ads, xsum, wsum, in_dim, nblk32p, a.eps);
     else act_prologue<ACT, false, ST_THREADS>(xst, nw, aq, ads, xsum, wsum, in_dim, nblk32p, a.eps);
     const float *xs = xst;
@@ -198,6 +296,7 @@ __device__ __forceinline__ void step_mv(const StepArgs &a, StepPersist &P, uint8
     }
     if (u0 + warp < u1) red[((cur_rb - rb0) * ST_WARPS + warp) * 32 + lane] = acc;
     __syncthreads();
+    ok = true;
     for (int l = warp; l < nloc; l += ST_WARPS) {
         float v = 0.0f;
 #pragma unroll
@@ -206,16 +305,24 @@ __device__ __forceinline__ void step_mv(const StepArgs &a, StepPersist &P, uint8
         if (epi == 2) {   // SwiGLU over rows interleaved by 16
             const float u = __shfl_down_sync(0xffffffffu, v, 16);
             const int r = rbl * 16 + lane;
-            if (lane < 16 && r < (rows >> 1)) y[r] = (v / (1.0f + expf(-v))) * u;
+            if (lane < 16 && r < (rows >> 1)) {
+                const float y = (v / (1.0f + expf(-v))) * u;
+                for (int c2 = 0; c2 < ncopy; ++c2) ll_st(ydst[c2] + yoff + r, y, ey);
+            }
         } else {
             const int row = rbl * TILE_ROWS + lane;
             if (row < rows) {
-                if (epi == 1) v += __ldcg(residual + row);
-                y[row] = v;
+                if (epi == 1) {
+                    float r;
+                    ok = ll_get(residual + yoff + row, er, a.status, r) && ok;
+                    v += r;
+                }
+                for (int c2 = 0; c2 < ncopy; ++c2) ll_st(ydst[c2] + yoff + row, v, ey);
             }
         }
     }
-    __syncthreads();
+    // the reduction scratch is reused by the next phase
+    return __syncthreads_and(ok) != 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -277,8 +384,11 @@ __device__ __forceinline__ int attn_split_len(const StepArgs &a, int kv_len) {
 // (stride HD + 4 floats keeps every acc row 16-byte aligned)
 constexpr int ATT_STRIDE = ST_HD + 4;
 
+// q, k, v: the LL QKV output of epoch eq; the output goes to every rank's
+// attention vector with epoch eo.  False on a time-out.
 template <typename KV>
-__device__ __noinline__ void step_attn(const StepArgs &a, const StepPersist &P, uint8_t *sm, int layer, int pos) {
+__device__ __noinline__ bool step_attn(const StepArgs &a, const StepPersist &P, uint8_t *sm, int layer, int pos,
+                                       unsigned eq, unsigned eo) {
     constexpr int HD = ST_HD;
     const int kv_len = pos + 1;
     const int per_split = attn_split_len(a, kv_len);
@@ -293,14 +403,7 @@ __device__ __noinline__ void step_attn(const StepArgs &a, const StepPersist &P, 
         const int h = it % a.n_heads, sp = it / a.n_heads, kvh = h / group;
         const int p0 = sp * per_split, p1 = min(kv_len, p0 + per_split);
         float qf[16];
-        {
-            const float4 *q4 = reinterpret_cast<const float4 *>(a.qkv + (size_t)h * HD + 16 * l8);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float4 v = __ldcg(q4 + k);
-                qf[4 * k] = v.x; qf[4 * k + 1] = v.y; qf[4 * k + 2] = v.z; qf[4 * k + 3] = v.w;
-            }
-        }
+        if (!__all_sync(0xffffffffu, ll_get16(a.qkv + (size_t)h * HD + 16 * l8, eq, a.status, qf))) return false;
         rope16(qf, l8, P);
         // this position's k (rotated) and v, rounded as the cache stores them,
         // kept in the warp's shared scratch (the cache row may not be written yet)
@@ -309,14 +412,9 @@ __device__ __noinline__ void step_attn(const StepArgs &a, const StepPersist &P, 
         float *vps = kps + HD;
         if (has_pos) {
             float kp[16], vp[16];
-            const float4 *k4 = reinterpret_cast<const float4 *>(a.qkv + q_dim + (size_t)kvh * HD + 16 * l8);
-            const float4 *v4 = reinterpret_cast<const float4 *>(a.qkv + q_dim + kv_dim + (size_t)kvh * HD + 16 * l8);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float4 kv = __ldcg(k4 + k), vv = __ldcg(v4 + k);
-                kp[4 * k] = kv.x; kp[4 * k + 1] = kv.y; kp[4 * k + 2] = kv.z; kp[4 * k + 3] = kv.w;
-                vp[4 * k] = vv.x; vp[4 * k + 1] = vv.y; vp[4 * k + 2] = vv.z; vp[4 * k + 3] = vv.w;
-            }
+            const bool got = ll_get16(a.qkv + q_dim + (size_t)kvh * HD + 16 * l8, eq, a.status, kp) &&
+                             ll_get16(a.qkv + q_dim + kv_dim + (size_t)kvh * HD + 16 * l8, eq, a.status, vp);
+            if (!__all_sync(0xffffffffu, got)) return false;
             rope16(kp, l8, P);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -439,11 +537,15 @@ __device__ __noinline__ void step_attn(const StepArgs &a, const StepPersist &P, 
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
             const float inv = 1.0f / L;
-            *reinterpret_cast<float4 *>(a.att + (size_t)h * HD + 4 * lane) =
-                make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv);
+            for (int c = 0; c < a.world; ++c) {
+                StepWord *dst = a.patt[c] + (size_t)(a.h0 + h) * HD + 4 * lane;
+                ll_st2(dst, o4.x * inv, o4.y * inv, eo);
+                ll_st2(dst + 2, o4.z * inv, o4.w * inv, eo);
+            }
             if (lane == 0) a.att_cnt[h] = 0;
         }
     }
+    return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -451,9 +553,9 @@ __device__ __noinline__ void step_attn(const StepArgs &a, const StepPersist &P, 
 // matrix and the sampler.  Two kernels because a second weight type in one
 // kernel (a Q8_0 output matrix after Q4_K layers) doubles the live registers.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ bool step_begin(const StepArgs &a, StepPersist &P, const unsigned long long *bar) {
+__device__ __forceinline__ bool step_begin(const StepArgs &a, StepPersist &P, const unsigned long long *launches) {
     if (threadIdx.x == 0) {
-        P.launch = ld_acquire_u64(bar + 1);
+        P.launch = ld_acquire_u64(launches);
         P.pos = __ldcg(a.pos);
         P.ok = __ldcg(a.status) == 0;
         mbar_init(&P.mbar, 1);
@@ -463,12 +565,9 @@ __device__ __forceinline__ bool step_begin(const StepArgs &a, StepPersist &P, co
     return P.ok != 0;   // an earlier launch failed: do nothing
 }
 
-__device__ __forceinline__ void step_end(unsigned long long *bar, const StepPersist &P) {
+__device__ __forceinline__ void step_end(unsigned long long *launches, const StepPersist &P) {
     __syncthreads();
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-        __threadfence();
-        st_release_u64(bar + 1, P.launch + 1);
-    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) st_release_u64(launches, P.launch + 1);
 }
 
 template <int LT, int ACT, bool KVF16>
@@ -477,39 +576,40 @@ __global__ void __launch_bounds__(ST_THREADS, 1) dec_step_kernel(const StepArgs 
     extern __shared__ __align__(128) uint8_t smem[];
     StepPersist &P = *reinterpret_cast<StepPersist *>(smem);
     uint8_t *sm = smem + ST_PERSIST;
-    unsigned long long *bar = a.bar;
-    if (!step_begin(a, P, bar)) return;
+    unsigned long long *launches = a.bar + 1;
+    if (!step_begin(a, P, launches)) return;
     const int tid = threadIdx.x, pos = P.pos;
-    const int nbar = 5 * a.n_layers;                 // after the embedding and every phase but the last
     const int q_dim = a.n_heads * ST_HD, kv_dim = a.n_kv_heads * ST_HD;
     if (tid < ST_HD / 2) {
         float c, s;
         rope_cos_sin(pos, tid, ST_HD, a.rope_base, c, s);
         P.rope[tid] = make_float2(c, s);
     }
+    __syncthreads();
     unsigned mb_par = 0;
-    int e = 0;
+    StepWord *const x = a.px[a.rank];
 
-    // embed: x = emb[seq[pos]]
+    // embed: x = emb[seq[pos]] (every rank, whole vector, own copy)
     step_prefetch(a, 0);
     {
+        const unsigned e0 = step_epoch(a, P.launch, 0);
         const int tok = __ldcg(a.seq + pos);
         for (int i = blockIdx.x * ST_THREADS + tid; i < a.dim; i += a.grid * ST_THREADS) {
             float v = 0.0f;
             if (tok >= 0 && tok < a.vocab)
                 v = a.emb_f16 ? __half2float(reinterpret_cast<const __half *>(a.emb)[(size_t)tok * a.dim + i])
                               : reinterpret_cast<const float *>(a.emb)[(size_t)tok * a.dim + i];
-            a.x[i] = v;
+            ll_st(x + i, v, e0);
         }
     }
-    if (!step_barrier(a, P, bar, e++, nbar)) return;
 
-    // layers: 5 phases each, one matvec call site
+    // layers: 5 phases each, one matvec call site; each phase polls its inputs
     const int last = 5 * a.n_layers;
     const size_t kv_es = KVF16 ? 2 : 4;
     for (int ph = 1; ph <= last; ++ph) {
         step_prefetch(a, ph);
         const int l = (ph - 1) / 5, k = (ph - 1) % 5;
+        const unsigned ein = step_epoch(a, P.launch, ph - 1), eout = step_epoch(a, P.launch, ph);
         if (k == 0 && pos > 0 && tid < 32) {
             // the layer's cached K and V rows (positions 0..pos-1) into L2 for
             // the attention phase that follows
@@ -524,40 +624,55 @@ __global__ void __launch_bounds__(ST_THREADS, 1) dec_step_kernel(const StepArgs 
                 prefetch_l2_bulk(vb + o, len);
             }
         }
+        bool ok;
         if (k == 1) {
-            step_attn<KV>(a, P, sm, l, pos);
+            ok = step_attn<KV>(a, P, sm, l, pos, ein, eout);
+            __syncthreads();   // the attention scratch is the next phase's
         } else {
             const StepLayer &L = a.layers[l];
             const uint8_t *W = k == 0 ? L.wqkv : k == 2 ? L.wo : k == 3 ? L.w13 : L.w2;
-            const int rows = k == 0 ? q_dim + 2 * kv_dim : k == 3 ? 2 * a.ffn : a.dim;
-            const int in_dim = k == 2 ? q_dim : k == 4 ? a.ffn : a.dim;
-            const float *x = k == 2 ? a.att : k == 4 ? a.h : a.x;
-            float *y = k == 0 ? a.qkv : k == 3 ? a.h : a.x;
+            // local rows: QKV of the local heads, a dim slice, a ffn slice (x2 interleaved)
+            const int rows = k == 0 ? q_dim + 2 * kv_dim : k == 3 ? 2 * a.ffn_loc : a.dim_loc;
+            const int in_dim = k == 2 ? a.n_heads_g * ST_HD : k == 4 ? a.ffn : a.dim;
+            const StepWord *xin = k == 2 ? a.patt[a.rank] : k == 4 ? a.ph[a.rank] : x;
+            StepWord *const *ydst = k == 0 ? &a.qkv : k == 3 ? a.ph : a.px;
+            const int ncopy = k == 0 ? 1 : a.world;
+            const int yoff = k == 0 ? 0 : k == 3 ? a.f0 : a.d0;
+            // the residual x: written by the phase before the attention (Wo)
+            // or by Wo (W2)
+            const unsigned er = step_epoch(a, P.launch, k == 2 ? ph - 3 : ph - 2);
             const float *nw = k == 0 ? L.attn_norm : k == 3 ? L.ffn_norm : nullptr;
             const int epi = k == 3 ? 2 : (k == 2 || k == 4) ? 1 : 0;
-            step_mv<LT, ACT>(a, P, sm, mb_par, W, rows, in_dim, x, y, a.x, nw, epi);
+            ok = step_mv<LT, ACT>(a, P, sm, mb_par, W, rows, in_dim, xin, ein, ydst, ncopy, yoff, eout, x, er, nw,
+                                  epi);
         }
-        if (ph < last && !step_barrier(a, P, bar, e++, nbar)) return;
+        if (!__syncthreads_or(!ok)) continue;
+        return;
     }
-    step_end(bar, P);
+    step_end(launches, P);
 }
 
 // output matrix (RMSNorm fused; skipped for prompt positions of a
-// generation), then the sampler on CTA 0, then the next position
+// generation), then on CTA 0 the logits gathered into the plain buffer, the
+// sampler and the next position
 template <int OT, int ACT>
 __global__ void __launch_bounds__(ST_THREADS, 1) dec_out_kernel(const StepArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     StepPersist &P = *reinterpret_cast<StepPersist *>(smem);
     uint8_t *sm = smem + ST_PERSIST;
-    unsigned long long *bar = a.bar + 2;
-    if (!step_begin(a, P, bar)) return;
+    unsigned long long *launches = a.bar + 3;
+    if (!step_begin(a, P, launches)) return;
     const int tid = threadIdx.x, pos = P.pos;
     unsigned mb_par = 0;
-    step_prefetch(a, step_phases(a.n_layers) - 1);
+    const int ph = step_phases(a.n_layers) - 1;
+    step_prefetch(a, ph);
+    const unsigned ein = step_epoch(a, P.launch, ph - 1), eout = step_epoch(a, P.launch, ph);
     const bool need = !a.sa.gen || pos >= a.sa.n_prompt - 1;
-    if (need) step_mv<OT, ACT>(a, P, sm, mb_par, a.out_w, a.vocab, a.dim, a.x, a.logits, nullptr, a.final_norm, 0);
-    if (!step_barrier(a, P, bar, 0, 1)) return;
+    if (need && !step_mv<OT, ACT>(a, P, sm, mb_par, a.out_w, a.vocab_loc, a.dim, a.px[a.rank], ein, a.plog,
+                                  a.world, a.v0, eout, nullptr, 0, a.final_norm, 0))
+        return;
     if (blockIdx.x == 0) {
+        if (need && !__syncthreads_and(ll_gather(a.logits, a.plog[a.rank], a.vocab, eout, a.status))) return;
         if (a.sample && need) {
             SampleSmem &S = *reinterpret_cast<SampleSmem *>(sm);
             const int gi = a.sa.gen ? pos - (a.sa.n_prompt - 1) : 0;
@@ -576,7 +691,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) dec_out_kernel(const StepArgs a
         }
         if (tid == 0) *a.pos = pos + 1;
     }
-    step_end(bar, P);
+    step_end(launches, P);
 }
 
 size_t mv_smem(const StepArgs &a, int act, int type, int rows, int in_dim, bool norm) {
@@ -593,15 +708,15 @@ size_t mv_smem(const StepArgs &a, int act, int type, int rows, int in_dim, bool 
 size_t layer_smem(const StepArgs &a, int lt, int act) {
     const int q_dim = a.n_heads * ST_HD, kv_dim = a.n_kv_heads * ST_HD;
     size_t m = mv_smem(a, act, lt, q_dim + 2 * kv_dim, a.dim, true);
-    m = std::max(m, mv_smem(a, act, lt, a.dim, q_dim, false));
-    m = std::max(m, mv_smem(a, act, lt, 2 * a.ffn, a.dim, true));
-    m = std::max(m, mv_smem(a, act, lt, a.dim, a.ffn, false));
+    m = std::max(m, mv_smem(a, act, lt, a.dim_loc, a.n_heads_g * ST_HD, false));
+    m = std::max(m, mv_smem(a, act, lt, 2 * a.ffn_loc, a.dim, true));
+    m = std::max(m, mv_smem(a, act, lt, a.dim_loc, a.ffn, false));
     m = std::max(m, (size_t)ST_WARPS * 2 * ST_HD * sizeof(float));   // attention scratch
     return ST_PERSIST + m;
 }
 
 size_t out_smem(const StepArgs &a, int act) {
-    size_t m = mv_smem(a, act, a.out_type, a.vocab, a.dim, true);
+    size_t m = mv_smem(a, act, a.out_type, a.vocab_loc, a.dim, true);
     if (a.sample) m = std::max(m, sizeof(SampleSmem));
     return ST_PERSIST + m;
 }

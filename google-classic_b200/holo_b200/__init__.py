@@ -30,6 +30,7 @@ Q4K_REF, Q4K_GGML = 0, 1
 
 HOLO_OK = 0
 HOLO_E_ARG, HOLO_E_NOMEM, HOLO_E_UNSUPPORTED, HOLO_E_TIMEOUT, HOLO_E_COMM = 1001, 1002, 1003, 1004, 1005
+COMM_HANDLE_BYTES = 128   # HOLO_COMM_HANDLE_BYTES
 
 
 def row_bytes(gtype: int, cols: int) -> int:
@@ -97,6 +98,7 @@ SIGNATURES = {
     "cuda_synth_weights": (_i, [_vp, _i, _i, _i, C.c_ulonglong, _f]),
     "holo_model_last_timing": (_i, [_vp, _vp, _vp]),
     "holo_model_pos": (_i, [_vp]), "holo_model_reset": (None, [_vp]), "holo_model_free": (None, [_vp]),
+    "holo_model_comm_handle": (_i, [_vp, _vp]), "holo_model_shard": (_i, [_vp, _vp]), "holo_model_open_peers": (_i, [_vp, _vp]),
 }
 
 _LIB = None

@@ -10,14 +10,15 @@ import ctypes as C
 
 import numpy as np
 
-from . import load, ACT_Q8, HOLO_OK
+from . import load, ACT_Q8, HOLO_OK, COMM_HANDLE_BYTES
 
 
 class ModelDesc(C.Structure):
     _fields_ = [("n_layers", C.c_int), ("dim", C.c_int), ("n_heads", C.c_int), ("n_kv_heads", C.c_int),
                 ("head_dim", C.c_int), ("ffn_dim", C.c_int), ("vocab", C.c_int), ("max_seq", C.c_int),
                 ("rope_base", C.c_float), ("eps", C.c_float), ("layer_type", C.c_int), ("emb_type", C.c_int),
-                ("out_type", C.c_int), ("kv_f16", C.c_int), ("act_mode", C.c_int)]
+                ("out_type", C.c_int), ("kv_f16", C.c_int), ("act_mode", C.c_int), ("world", C.c_int),
+                ("rank", C.c_int)]
 
 
 class SamplerDesc(C.Structure):
@@ -31,15 +32,20 @@ def _ptr(a: np.ndarray) -> int:
 
 
 class Model:
-    """One decode model on the current device (raises on library errors)."""
+    """One decode model on the current device (raises on library errors).
 
-    def __init__(self, cfg: dict, act_mode: int = ACT_Q8, kv_f16: bool = True):
+    world > 1: this process's row shard of a model sharded over `world` GPUs
+    (one process per GPU); set the weights (the full matrices: each rank keeps
+    its rows), then connect_peers, then make every step call on every rank."""
+
+    def __init__(self, cfg: dict, act_mode: int = ACT_Q8, kv_f16: bool = True, world: int = 1, rank: int = 0):
         self.lib = load()
         self.cfg = dict(cfg)
+        self.world, self.rank = world, rank
         d = ModelDesc(cfg["n_layers"], cfg["dim"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"],
                       cfg["ffn_dim"], cfg["vocab"], cfg["max_seq"], cfg.get("rope_base", 10000.0),
                       cfg.get("eps", 1e-5), cfg["layer_type"], cfg.get("emb_type", 1), cfg["out_type"],
-                      int(kv_f16), act_mode)
+                      int(kv_f16), act_mode, world, rank)
         self.desc = d
         self.h = self.lib.holo_model_create(C.byref(d))
         self._check("holo_model_create", ok=bool(self.h))
@@ -92,6 +98,19 @@ class Model:
         self.lib.holo_model_last_timing(self.h, C.byref(a), C.byref(b))
         return a.value, b.value
 
+    def comm_handle(self) -> bytes:
+        """This rank's handle for the other ranks (HOLO_COMM_HANDLE_BYTES)."""
+        buf = C.create_string_buffer(COMM_HANDLE_BYTES)
+        self._check("holo_model_comm_handle", self.lib.holo_model_comm_handle(self.h, buf) == HOLO_OK)
+        return buf.raw
+
+    def open_peers(self, handles: list[bytes]):
+        """Every rank's handle, in rank order."""
+        if len(handles) != self.world or any(len(h) != COMM_HANDLE_BYTES for h in handles):
+            raise ValueError("open_peers: one handle of COMM_HANDLE_BYTES per rank")
+        blob = C.create_string_buffer(b"".join(handles), COMM_HANDLE_BYTES * self.world)
+        self._check("holo_model_open_peers", self.lib.holo_model_open_peers(self.h, blob) == HOLO_OK)
+
     def reset(self):
         self.lib.holo_model_reset(self.h)
 
@@ -107,6 +126,32 @@ class Model:
             pass
 
 
+def connect_peers(model, group=None):
+    """All-gather of the ranks' comm handles over torch.distributed (any
+    backend), then open them: the set-up collective of a sharded model."""
+    import torch.distributed as dist
+    handles = [None] * model.world
+    dist.all_gather_object(handles, model.comm_handle(), group=group)
+    model.open_peers(handles)
+
+
+def shard_ranges(cfg: dict, world: int, rank: int) -> dict:
+    """The rows a rank of a sharded model holds (holo_model_shard, host
+    only): query heads, KV heads, rows of Wo/W2, SwiGLU outputs (whole 16-row
+    bands), output-matrix rows, each (first, count)."""
+    lib = load()
+    d = ModelDesc(cfg["n_layers"], cfg["dim"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"],
+                  cfg["ffn_dim"], cfg["vocab"], cfg["max_seq"], cfg.get("rope_base", 10000.0),
+                  cfg.get("eps", 1e-5), cfg["layer_type"], cfg.get("emb_type", 1), cfg["out_type"], 1, ACT_Q8,
+                  world, rank)
+    r = (C.c_int * 10)()
+    if lib.holo_model_shard(C.byref(d), r) != HOLO_OK:
+        lib.cuda_clear_status()
+        raise ValueError(f"shard_ranges: cannot shard over {world} (rank {rank})")
+    names = ("heads", "kv_heads", "dim", "ffn", "vocab")
+    return {n: (r[2 * i], r[2 * i + 1]) for i, n in enumerate(names)}
+
+
 LLAMA2_7B = dict(n_layers=32, dim=4096, n_heads=32, n_kv_heads=32, head_dim=128, ffn_dim=11008, vocab=32000,
                  max_seq=2048, rope_base=10000.0, eps=1e-5, layer_type=12, emb_type=1, out_type=8)
 LLAMA3_70B = dict(n_layers=80, dim=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn_dim=28672, vocab=128256,
@@ -118,13 +163,13 @@ def _tensor_seed(seed: int, layer: int, idx: int) -> int:
 
 
 def synthetic_model(cfg: dict, seed: int, act_mode: int = ACT_Q8, kv_f16: bool = True, std: float = 0.02,
-                    keep_host: bool = False):
+                    keep_host: bool = False, world: int = 1, rank: int = 0):
     """A random-init model built on the device: every weight N(0, std),
     quantized round-to-nearest by cuda_synth_weights into GGUF blocks, then
     repacked by holo_model_set_layer/_globals.  keep_host also returns the raw
     blocks (the dict layout of synth.llama_weights) for the reference engine."""
     lib = load()
-    m = Model(cfg, act_mode=act_mode, kv_f16=kv_f16)
+    m = Model(cfg, act_mode=act_mode, kv_f16=kv_f16, world=world, rank=rank)
     dim, hd, ffn, V = cfg["dim"], cfg["head_dim"], cfg["ffn_dim"], cfg["vocab"]
     q_dim, kv_dim = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
     lt, ot, et = cfg["layer_type"], cfg["out_type"], cfg.get("emb_type", 1)

@@ -135,6 +135,8 @@ typedef struct {
     int out_type;        /* GGUF type of the output (lm_head) matrix */
     int kv_f16;          /* 1: fp16 KV cache, 0: fp32 (the reference's) */
     int act_mode;        /* HOLO_ACT_Q8 or HOLO_ACT_F32 for every matvec */
+    int world;           /* row sharding over this many GPUs (one process each); 0 or 1: none */
+    int rank;            /* this process's shard, 0 <= rank < world */
 } holo_model_desc;
 
 typedef struct {         /* llm_sampler_t (src/ai/llm.h:167-174) without the seed */
@@ -180,6 +182,26 @@ int holo_model_pos(void *model);
 /* Device time of the last holo_model_generate: prefill (the steps before the
  * first draw) and decode (n_new steps of forward + sample), in ms. */
 int holo_model_last_timing(void *model, float *prefill_ms, float *decode_ms);
+/* Sharded decode (world > 1; head_dim 128): rank r holds query heads
+ * [r*n_heads/world, ...) with their KV heads and cache, a 1/world slice of
+ * the rows of wo, w2, w1/w3 (in 16-row bands) and output; every phase stores
+ * its slice of x, the attention output, the SwiGLU output and the logits into
+ * every rank's copy over NVLink, and the step's barriers span the GPUs.  Each
+ * rank creates its model with the same desc (rank differing) and passes the
+ * full, unsharded weights to set_layer / set_globals, which keep the rank's
+ * slice.  Then the ranks exchange handles (all-gather of
+ * HOLO_COMM_HANDLE_BYTES each, in rank order) and open them.  Every call that
+ * runs a step (forward, generate, launch_steps) must then be made by every
+ * rank with the same arguments; a rank that recorded an error (a barrier
+ * time-out) leaves the group unusable -- free and recreate it on every rank.
+ * No counterpart in the reference (single-device only). */
+#define HOLO_COMM_HANDLE_BYTES 128
+/* The rows desc->rank holds (host only, no device needed): ranges[10] =
+ * first and count of query heads, KV heads, rows of wo/w2, SwiGLU outputs
+ * (rows of w1/w3; whole 16-row bands), rows of output. */
+int holo_model_shard(const holo_model_desc *desc, int *ranges);
+int holo_model_comm_handle(void *model, void *handle);
+int holo_model_open_peers(void *model, const void *handles);
 void holo_model_reset(void *model);
 void holo_model_free(void *model);
 

@@ -1,0 +1,120 @@
+"""One rank of the sharded-decode tests, run under torch.distributed.run by
+test_shard_host.py (gloo, CPU) and test_shard_gpu.py (one GPU per rank).
+
+  python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
+      --master-port P tests/shard_worker.py {host|gpu} OUT_DIR
+
+host: every rank computes its row shard through the library (holo_model_shard)
+      and exchanges comm handles of a stand-in model through connect_peers;
+      the ranks check that the shards tile every matrix and that every rank
+      received every handle in rank order.
+gpu:  every rank builds its shard of the test model, connects the peers and
+      runs the decode calls; rank 0 writes the logits and token streams to
+      OUT_DIR/gpu.npz for the parent test to compare with the reference.
+"""
+import datetime
+import json
+import os
+import pathlib
+import sys
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT / "google-classic_b200"))
+
+import holo_b200 as hb  # noqa: E402
+from holo_b200.model import (LLAMA2_7B, LLAMA3_70B, Model, SamplerDesc, connect_peers,  # noqa: E402
+                             shard_ranges)
+
+# the decode test model (GQA, SwiGLU, Q4_K layers, fp16 embeddings, Q8_0 output)
+CFG = dict(n_layers=2, dim=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn_dim=768, vocab=1000, max_seq=160,
+           rope_base=10000.0, eps=1e-5, layer_type=hb.Q4_K, emb_type=1, out_type=hb.Q8_0)
+PROMPT_SEED, N_PROMPT, N_GREEDY, N_SAMPLED = 21, 24, 48, 32
+
+
+class StandInModel:
+    """comm_handle / open_peers of a model, without a device."""
+
+    def __init__(self, world, rank):
+        self.world, self.rank, self.opened = world, rank, None
+
+    def comm_handle(self):
+        return bytes([self.rank]) * hb.COMM_HANDLE_BYTES
+
+    def open_peers(self, handles):
+        self.opened = handles
+
+
+def tiles(parts, n, unit=1):
+    """parts: (first, count) per rank, in rank order: contiguous, covering [0, n)."""
+    pos = 0
+    for first, count in parts:
+        if first != pos or count <= 0 or first % unit or count % unit:
+            return False
+        pos += count
+    return pos == n
+
+
+def run_host(rank, world, out):
+    import torch.distributed as dist
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+    res = {}
+    for name, cfg in (("test", CFG), ("7b", LLAMA2_7B), ("70b", LLAMA3_70B)):
+        if cfg["n_kv_heads"] % world:
+            continue
+        mine = shard_ranges(cfg, world, rank)
+        every = [None] * world
+        dist.all_gather_object(every, mine)
+        res[name] = all(tiles([e[k] for e in every], n, u) for k, n, u in
+                        (("heads", cfg["n_heads"], 1), ("kv_heads", cfg["n_kv_heads"], 1), ("dim", cfg["dim"], 1),
+                         ("ffn", cfg["ffn_dim"], 16), ("vocab", cfg["vocab"], 1)))
+        # GQA groups stay whole: the rank's KV heads serve exactly its query heads
+        h, kv = mine["heads"], mine["kv_heads"]
+        g = cfg["n_heads"] // cfg["n_kv_heads"]
+        res[name + "_gqa"] = h[0] == kv[0] * g and h[1] == kv[1] * g
+    m = StandInModel(world, rank)
+    connect_peers(m)
+    res["handles"] = m.opened == [bytes([r]) * hb.COMM_HANDLE_BYTES for r in range(world)]
+    dist.barrier()
+    dist.destroy_process_group()
+    (pathlib.Path(out) / f"host_{rank}.json").write_text(json.dumps(res))
+
+
+def run_gpu(rank, world, out):
+    import torch
+    import torch.distributed as dist
+    from holo_b200 import synth
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    hb.Device(local, world)
+    w = synth.llama_weights(CFG, seed=11)
+    prompt = np.random.default_rng(PROMPT_SEED).integers(0, CFG["vocab"], size=N_PROMPT).astype(np.int32)
+    res = {}
+    try:
+        for tag, act, kv16 in (("f32", hb.ACT_F32, False), ("q8", hb.ACT_Q8, True)):
+            m = Model(CFG, act_mode=act, kv_f16=kv16, world=world, rank=rank)
+            m.set_weights(w)
+            connect_peers(m)
+            res[f"{tag}_logits"] = np.stack([m.forward(t) for t in prompt])
+            res[f"{tag}_greedy"] = m.generate(prompt[:16], N_GREEDY, SamplerDesc(0.0, 0.95, 40, 1.1, 64), seed=5)
+            res[f"{tag}_sampled"] = m.generate(prompt[:16], N_SAMPLED, SamplerDesc(0.8, 0.95, 40, 1.1, 64), seed=7)
+            dist.barrier()
+            m.close()
+        # every rank computed the same logits and tokens
+        for k in sorted(res):
+            every = [None] * world
+            dist.all_gather_object(every, res[k])
+            res[k + "_ranks_equal"] = np.array(all(np.array_equal(e, every[0]) for e in every))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        np.savez(pathlib.Path(out) / "gpu.npz", **res)
+
+
+if __name__ == "__main__":
+    mode, out = sys.argv[1], sys.argv[2]
+    r, n = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    (run_host if mode == "host" else run_gpu)(r, n, out)

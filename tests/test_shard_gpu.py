@@ -1,0 +1,102 @@
+"""Sharded decode over two GPUs (one process each, tests/shard_worker.py gpu)
+against the reference engine (oracle/ref_harness.c) and the one-GPU model.
+
+Every phase of a sharded step computes a slice of its output rows with the
+same per-row arithmetic as one GPU; only the order in which a row's units are
+summed across warps can differ, so the bars are those of test_decode_gpu:
+* HOLO_ACT_F32, fp32 KV cache: logits within 1e-2 absolute and 1e-3
+  norm-wise relative of the reference; greedy (48 steps) and sampled (32
+  steps) token streams identical to the reference's.
+* HOLO_ACT_Q8, fp16 KV cache: logits within 1e-3 norm-wise relative of the
+  one-GPU model's, greedy stream identical to it.
+* Both ranks return the same logits and tokens.
+Needs two GPUs; skipped otherwise.
+"""
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import holo_b200 as hb
+from holo_b200 import synth
+from holo_b200.model import Model, SamplerDesc
+from conftest import ROOT, rel_err
+from holo_oracle import RefModel
+
+sys.path.insert(0, str(ROOT / "tests"))
+from shard_worker import CFG, N_GREEDY, N_PROMPT, N_SAMPLED, PROMPT_SEED  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def gpu_count():
+    import torch
+    return torch.cuda.device_count()
+
+
+@pytest.fixture(scope="module")
+def sharded(tmp_path_factory):
+    if gpu_count() < 2:
+        pytest.skip("needs two GPUs")
+    out = tmp_path_factory.mktemp("shard")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    # NVLS off: the sharded step uses plain peer stores, NCCL only for set-up
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", OMP_NUM_THREADS="1")
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
+           str(ROOT / "tests" / "shard_worker.py"), "gpu", str(out)]
+    p = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert p.returncode == 0, p.stdout[-4000:] + p.stderr[-4000:]
+    return dict(np.load(out / "gpu.npz"))
+
+
+@pytest.fixture(scope="module")
+def weights():
+    return synth.llama_weights(CFG, seed=11)
+
+
+def prompt():
+    return np.random.default_rng(PROMPT_SEED).integers(0, CFG["vocab"], size=N_PROMPT).astype(np.int32)
+
+
+def test_ranks_agree(sharded):
+    bad = [k for k in sharded if k.endswith("_ranks_equal") and not bool(sharded[k])]
+    assert not bad, bad
+
+
+def test_sharded_f32_logits_match_reference(sharded, reference, weights):
+    ref = RefModel(reference, CFG, weights)
+    worst_abs = worst_rel = 0.0
+    for y, t in zip(sharded["f32_logits"], prompt()):
+        r = ref.forward(t)
+        worst_abs = max(worst_abs, float(np.abs(y - r).max()))
+        worst_rel = max(worst_rel, rel_err(y, r))
+    ref.close()
+    print(f"sharded f32 logits: max abs {worst_abs:.3e}, max rel {worst_rel:.3e}")
+    assert worst_abs <= 1e-2 and worst_rel <= 1e-3
+
+
+def test_sharded_streams_match_reference(sharded, reference, weights):
+    ref = RefModel(reference, CFG, weights)
+    p = prompt()[:16]
+    want_g = ref.generate(p, N_GREEDY, 0.0, 0.95, 40, 1.1, 64, seed=5)
+    want_s = ref.generate(p, N_SAMPLED, 0.8, 0.95, 40, 1.1, 64, seed=7)
+    ref.close()
+    assert np.array_equal(sharded["f32_greedy"], want_g)
+    assert np.array_equal(sharded["f32_sampled"], want_s)
+
+
+def test_sharded_q8_matches_one_gpu(sharded, dev, weights):
+    m = Model(CFG, act_mode=hb.ACT_Q8, kv_f16=True)
+    m.set_weights(weights)
+    worst = max(rel_err(y, m.forward(t)) for y, t in zip(sharded["q8_logits"], prompt()))
+    got = m.generate(prompt()[:16], N_GREEDY, SamplerDesc(0.0, 0.95, 40, 1.1, 64), seed=5)
+    m.close()
+    print(f"sharded q8 vs one GPU: max norm-wise rel {worst:.3e}")
+    assert worst <= 1e-3
+    assert np.array_equal(sharded["q8_greedy"], got)
