@@ -543,12 +543,16 @@ def run_reference(args, rank, world):
 
 
 def run_profile_decode(args):
-    """Small decode case for ncu launch lists: the 7B model, 2 prompt + 2 new
+    """Small decode case for ncu: the 7B model (--layers: only the first N
+    layers, context 256, so a capture holds well under a GB), 2 prompt + 2 new
     tokens; the profiled generate is inside the NVTX range "profiled"."""
     import torch
     from holo_b200.model import LLAMA2_7B, SamplerDesc, synthetic_model
     dev = hb.Device(0, 1)
-    m = synthetic_model(dict(LLAMA2_7B), seed=0, act_mode=hb.ACT_Q8 if args.act == "q8" else hb.ACT_F32)
+    cfg = dict(LLAMA2_7B)
+    if args.layers:
+        cfg.update(n_layers=args.layers, max_seq=256)
+    m = synthetic_model(cfg, seed=0, act_mode=hb.ACT_Q8 if args.act == "q8" else hb.ACT_F32)
     s = SamplerDesc(0.8, 0.95, 40, 1.1, 64)
     p = np.array([1, 2], np.int32)
     m.generate(p, 2, s, seed=0)
@@ -558,7 +562,8 @@ def run_profile_decode(args):
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
     dev.check("profile decode")
-    print(json.dumps({"profile_decode": "llama2-7b q4_k", "steps": 3, "kernels_per_step": 228}))
+    print(json.dumps({"profile_decode": "llama2-7b q4_k", "layers": cfg["n_layers"], "steps": 3,
+                      "kernels_per_step": 2}))
     m.close()
 
 
@@ -594,6 +599,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the 7B decode sub-benchmark")
     ap.add_argument("--profile-decode", action="store_true", help="small 7B decode case for ncu")
     ap.add_argument("--decode-only", action="store_true", help="only the 7B decode sub-benchmark")
+    ap.add_argument("--layers", type=int, default=0, help="--profile-decode: first N layers only")
     ap.add_argument("--profile-case", default=None, help="e.g. q4_k:11008x4096 (ncu small case)")
     ap.add_argument("--iters", type=int, default=4)
     args = ap.parse_args()

@@ -52,6 +52,27 @@ __device__ __forceinline__ void load_unit(Frag &f, const uint8_t *__restrict__ u
     }
 }
 
+// the same fragment from a unit staged in shared memory (16-byte rows: the
+// 32 lanes of a plane read 512 contiguous bytes, no bank conflicts)
+template <int TYPE>
+__device__ __forceinline__ void load_unit_smem(Frag &f, const uint8_t *unit, int lane) {
+    const uint8_t *row = unit + (size_t)TILE_ROWS * UnitGeom<TYPE>::HEAD_BYTES + lane * 16;
+#pragma unroll
+    for (int pl = 0; pl < UNIT_PLANES; ++pl) f.q[pl] = lds128(row + pl * TILE_ROWS * 16);
+    if constexpr (TYPE == GT_Q8_0) {
+        const uint2 h = *reinterpret_cast<const uint2 *>(unit + lane * 8);
+        f.h = make_uint4(h.x, h.y, 0u, 0u);
+    } else {
+        f.h = lds128(unit + lane * 16);
+    }
+}
+
+// order this thread's (and, after a warp or CTA barrier, its peers') generic
+// shared-memory accesses before later async-proxy (bulk copy) writes
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // fp16 scale k (0..7) of a head word set
 __device__ __forceinline__ float head_half(const uint4 &h, int k) {
     const uint32_t w = k < 2 ? h.x : k < 4 ? h.y : k < 6 ? h.z : h.w;

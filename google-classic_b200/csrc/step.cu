@@ -36,9 +36,18 @@ namespace {
 using namespace holo_mv;
 using namespace holo_dec;
 
-constexpr int ST_WARPS = 8;
-constexpr int ST_THREADS = ST_WARPS * 32;
-constexpr int ST_DEPTH = 3;                        // units loading per warp
+// The layers kernel runs 8 warps a CTA with each warp's next weight units in
+// a register ring (255 registers a thread): its phases are short, and the
+// register path starts computing soonest.  The output kernel, one long
+// matvec, runs 16 warps with the weight units staged in shared memory by bulk
+// copies (128 registers a thread, twice the warps to hide latency).
+constexpr int LY_WARPS = 8;
+constexpr int LY_THREADS = LY_WARPS * 32;
+constexpr int OUT_WARPS = 16;
+constexpr int OUT_THREADS = OUT_WARPS * 32;
+constexpr int MAX_WARPS = 16;
+constexpr int ST_RING = 3;                         // register ring: units loading per warp
+constexpr int ST_MAX_DEPTH = 3;                    // shared-memory slots per warp, at most
 constexpr int ST_HD = 128;                         // head_dim of this kernel
 constexpr unsigned long long ST_WAIT_NS = 1000000000ull;
 constexpr size_t ST_PERSIST = 2048;                // bytes of the persistent shared region
@@ -46,7 +55,8 @@ constexpr size_t ST_PERSIST = 2048;                // bytes of the persistent sh
 // shared memory kept across phases (start of the dynamic allocation)
 struct StepPersist {
     float2 rope[ST_HD / 2];    // (cos, sin) of the RoPE pairs at pos
-    uint64_t mbar;             // bulk-copy completion
+    uint64_t mbar;             // bulk-copy completion (norm weights)
+    uint64_t slot[MAX_WARPS * ST_MAX_DEPTH];  // weight slot k of warp w: [w * ST_MAX_DEPTH + k]
     unsigned long long launch; // launch index (barrier targets)
     int ok;
     int pos;
@@ -115,15 +125,16 @@ struct Poll {
 // src 16-byte aligned; dst shared or global).  Each thread keeps LL_BATCH
 // 16-byte loads in flight and re-polls the batch until all are current.
 constexpr int LL_BATCH = 8;
+template <int NT>
 __device__ bool ll_gather(float *dst, const StepWord *src, int n, unsigned e, int *status) {
     const int npair = n >> 1;
-    for (int base = threadIdx.x; base < npair; base += ST_THREADS * LL_BATCH) {
+    for (int base = threadIdx.x; base < npair; base += NT * LL_BATCH) {
         StepWord w[2 * LL_BATCH];
         Poll poll;
         for (;;) {
 #pragma unroll
             for (int k = 0; k < LL_BATCH; ++k) {
-                const int i = base + k * ST_THREADS;
+                const int i = base + k * NT;
                 if (i < npair) ll_ld2(src + 2 * i, w[2 * k], w[2 * k + 1]);
                 else w[2 * k] = w[2 * k + 1] = (StepWord)e << 32;
             }
@@ -135,7 +146,7 @@ __device__ bool ll_gather(float *dst, const StepWord *src, int n, unsigned e, in
         }
 #pragma unroll
         for (int k = 0; k < LL_BATCH; ++k) {
-            const int i = base + k * ST_THREADS;
+            const int i = base + k * NT;
             if (i < npair) *reinterpret_cast<float2 *>(dst + 2 * i) = make_float2(ll_val(w[2 * k]), ll_val(w[2 * k + 1]));
         }
     }
@@ -207,27 +218,37 @@ __device__ __forceinline__ size_t align128(size_t v) { return (v + 127) & ~(size
 // an LL vector of epoch er), 2 SwiGLU over rows interleaved by 16; norm_w
 // non-NULL: RMSNorm of x first.  rows: this rank's rows of W; output row j
 // goes to element yoff + j of ydst[0..ncopy) (every rank's copy) with epoch
-// ey.  One instance per weight type: the kernel calls it from a single site
-// (separate inlined copies per phase exhaust the register file).
-template <int TYPE, int ACT>
+// ey.  One instance per weight type and kernel: the kernel calls it from a
+// single site (separate inlined copies per phase exhaust the register file).
+//
+// NW warps; warp w takes the CTA's units w, w + NW, ...  SMEMW false: each
+// warp keeps its next ST_RING units in registers.  SMEMW true: warp w owns
+// a.mv_depth shared-memory slots that its lane 0 fills by 1-D bulk copies
+// and refills with the warp's next unit once the warp has folded the current
+// one; spar holds the warp's slot parities across phases.
+template <int TYPE, int ACT, int NW, bool SMEMW>
 __device__ __forceinline__ bool step_mv(const StepArgs &a, StepPersist &P, uint8_t *sm, unsigned &mb_par,
-                        const uint8_t *__restrict__ W, int rows, int in_dim, const StepWord *x, unsigned ex,
-                        StepWord *const *ydst, int ncopy, int yoff, unsigned ey, const StepWord *residual,
-                        unsigned er, const float *norm_w, int epi) {
+                        unsigned &spar, const uint8_t *__restrict__ W, int rows, int in_dim, const StepWord *x,
+                        unsigned ex, StepWord *const *ydst, int ncopy, int yoff, unsigned ey,
+                        const StepWord *residual, unsigned er, const float *norm_w, int epi) {
+    constexpr int NT = NW * 32;
     const bool norm = norm_w != nullptr;
     constexpr int BLKS32 = UnitGeom<TYPE>::BLKS32;
     constexpr size_t UB = UnitGeom<TYPE>::UNIT_BYTES;
+    const int D = SMEMW ? a.mv_depth : 0;
     const int units = units_of<TYPE>(in_dim), nblk32p = units * BLKS32;
     const int nrb = (rows + TILE_ROWS - 1) / TILE_ROWS;
     const int G = a.grid, c = blockIdx.x;
     const int rb0 = (int)((long long)nrb * c / G), rb1 = (int)((long long)nrb * (c + 1) / G);
     if (rb0 >= rb1) return true;
     const int nloc = rb1 - rb0;
-    const int u0 = rb0 * units, u1 = rb1 * units;
+    const int u0 = rb0 * units, n = (rb1 - rb0) * units;   // this CTA's units [u0, u0 + n)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    float *red = reinterpret_cast<float *>(sm);
-    size_t o = align128((size_t)nloc * ST_WARPS * 32 * sizeof(float));
+    uint8_t *ring = sm;                                    // SMEMW: [NW * D] slots of UB bytes
+    size_t o = SMEMW ? align128((size_t)NW * D * UB) : 0;
+    float *red = reinterpret_cast<float *>(sm + o);
+    o += align128((size_t)nloc * NW * 32 * sizeof(float));
     uint8_t *aq = sm + o;
     float2 *ads = reinterpret_cast<float2 *>(sm + o + (size_t)nblk32p * 32);
     float *xst, *xsum = nullptr;
@@ -244,63 +265,130 @@ __device__ __forceinline__ bool step_mv(const StepArgs &a, StepPersist &P, uint8
     if (norm) o += (size_t)nblk32p * 128;
     float *wsum = reinterpret_cast<float *>(sm + o);
 
-    // norm weights by bulk copy; the first weight units into registers while
-    // the activations are polled
+    // the warp's first units (registers or slots), and the norm weights,
+    // requested while the activations are polled
+    Frag ring_r[SMEMW ? 1 : ST_RING];
+    uint64_t pol = 0;
+    if constexpr (SMEMW) {
+        pol = l2_policy_evict_first();
+        if (lane == 0) {
+            for (int k = 0; k < D; ++k) {
+                const int i = warp + k * NW;
+                if (i < n) {
+                    uint64_t *fb = &P.slot[warp * ST_MAX_DEPTH + k];
+                    mbar_arrive_expect_tx(fb, (uint32_t)UB);
+                    bulk_g2s(ring + (size_t)(warp * D + k) * UB, W + (size_t)(u0 + i) * UB, (uint32_t)UB, fb, pol);
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < ST_RING; ++k) {
+            const int i = warp + k * NW;
+            if (i < n) load_unit<TYPE>(ring_r[k], W + (size_t)(u0 + i) * UB, lane);
+        }
+    }
     const uint32_t xbytes = (uint32_t)in_dim * 4u;
     if (norm && tid == 0) {
         mbar_arrive_expect_tx(&P.mbar, xbytes);
         bulk_copy_g2s(nw, norm_w, xbytes, &P.mbar);
     }
-    Frag ring[ST_DEPTH];
-#pragma unroll
-    for (int k = 0; k < ST_DEPTH; ++k) {
-        const int uu = u0 + warp + k * ST_WARPS;
-        if (uu < u1) load_unit<TYPE>(ring[k], W + (size_t)uu * UB, lane);
-    }
-    for (int i = in_dim + tid; i < nblk32p * 32; i += ST_THREADS) {
+    // the residual of the warp's first row-block, requested now (it was
+    // written phases ago) rather than on the epilogue's critical path
+    StepWord rw = 0;
+    if (epi == 1 && warp < nloc && (rb0 + warp) * TILE_ROWS + lane < rows)
+        rw = ll_ld(residual + yoff + (rb0 + warp) * TILE_ROWS + lane);
+    for (int i = in_dim + tid; i < nblk32p * 32; i += NT) {
         xst[i] = 0.0f;
         if (norm) nw[i] = 0.0f;
     }
-    for (int i = tid; i < nloc * ST_WARPS * 32; i += ST_THREADS) red[i] = 0.0f;
-    bool ok = ll_gather(xst, x, in_dim, ex, a.status);
+    for (int i = tid; i < nloc * NW * 32; i += NT) red[i] = 0.0f;
+    bool ok = ll_gather<NT>(xst, x, in_dim, ex, a.status);
     if (norm) {
         ok = mbar_wait_bounded(&P.mbar, mb_par, a.status, HOLO_E_TIMEOUT) && ok;
         mb_par ^= 1u;
     }
-    if (!__syncthreads_and(ok)) return false;
-    if (norm) act_prologue<ACT, true, ST_THREADS>(xst, nw, aq, ads, xsum, wsum, in_dim, nblk32p, a.eps);
-    else act_prologue<ACT, false, ST_THREADS>(xst, nw, aq, ads, xsum, wsum, in_dim, nblk32p, a.eps);
+    ok = __syncthreads_and(ok) != 0;
+    if (ok) {
+        if (norm) act_prologue<ACT, true, NT>(xst, nw, aq, ads, xsum, wsum, in_dim, nblk32p, a.eps);
+        else act_prologue<ACT, false, NT>(xst, nw, aq, ads, xsum, wsum, in_dim, nblk32p, a.eps);
+    }
     const float *xs = xst;
 
+    // unit u0 + i, i = warp, warp + NW, ...: row-block rb, unit s of its row
     int rb = (u0 + warp) / units, s = u0 + warp - rb * units;
-    const int dq = ST_WARPS / units, dr = ST_WARPS - dq * units;
+    const int dq = NW / units, dr = NW - dq * units;
     int cur_rb = rb;
     float acc = 0.0f;
-    for (int ub = u0 + warp; ub < u1; ub += ST_DEPTH * ST_WARPS) {
-#pragma unroll
-        for (int k = 0; k < ST_DEPTH; ++k) {
-            const int u = ub + k * ST_WARPS;
-            if (u >= u1) break;
+    bool wok = ok;   // a failed slot wait skips the warp's remaining units
+    if constexpr (SMEMW) {
+        int k = 0, i = warp;
+        for (; wok && i < n; i += NW) {
+            uint64_t *fb = &P.slot[warp * ST_MAX_DEPTH + k];
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(fb, (spar >> k) & 1u, a.status, HOLO_E_TIMEOUT))) {
+                wok = false;
+                break;
+            }
+            spar ^= 1u << k;
+            Frag f;
+            load_unit_smem<TYPE>(f, ring + (size_t)(warp * D + k) * UB, lane);
             if (rb != cur_rb) {
-                red[((cur_rb - rb0) * ST_WARPS + warp) * 32 + lane] = acc;
+                red[((cur_rb - rb0) * NW + warp) * 32 + lane] = acc;
                 acc = 0.0f;
                 cur_rb = rb;
             }
-            unit_dot<TYPE, ACT>(acc, ring[k], s * BLKS32, aq, ads, xs, xsum);
-            const int un = u + ST_DEPTH * ST_WARPS;
-            if (un < u1) load_unit<TYPE>(ring[k], W + (size_t)un * UB, lane);
+            unit_dot<TYPE, ACT>(acc, f, s * BLKS32, aq, ads, xs, xsum);
+            // the slot's next unit: the fold above consumed every lane's
+            // reads of the slot, and the proxy fence orders them before the
+            // bulk copy's writes
+            __syncwarp();
+            const int inext = i + D * NW;
+            if (lane == 0 && inext < n) {
+                fence_proxy_async_smem();
+                mbar_arrive_expect_tx(fb, (uint32_t)UB);
+                bulk_g2s(ring + (size_t)(warp * D + k) * UB, W + (size_t)(u0 + inext) * UB, (uint32_t)UB, fb, pol);
+            }
             s += dr;
             rb += dq;
             if (s >= units) { s -= units; ++rb; }
+            k = k + 1 == D ? 0 : k + 1;
+        }
+        if (!wok) {
+            // the warp's copies still in flight (at most D, from unit i on)
+            // land before the slots are given up (bounded)
+            for (int t = 0; t < D && i < n; ++t, i += NW) {
+                if (mbar_wait_bounded(&P.slot[warp * ST_MAX_DEPTH + k], (spar >> k) & 1u, nullptr, 0))
+                    spar ^= 1u << k;
+                k = k + 1 == D ? 0 : k + 1;
+            }
+            ok = false;
+        }
+    } else {
+        for (int ib = warp; ok && ib < n; ib += ST_RING * NW) {
+#pragma unroll
+            for (int k = 0; k < ST_RING; ++k) {
+                const int i = ib + k * NW;
+                if (i >= n) break;
+                if (rb != cur_rb) {
+                    red[((cur_rb - rb0) * NW + warp) * 32 + lane] = acc;
+                    acc = 0.0f;
+                    cur_rb = rb;
+                }
+                unit_dot<TYPE, ACT>(acc, ring_r[k], s * BLKS32, aq, ads, xs, xsum);
+                const int inext = i + ST_RING * NW;
+                if (inext < n) load_unit<TYPE>(ring_r[k], W + (size_t)(u0 + inext) * UB, lane);
+                s += dr;
+                rb += dq;
+                if (s >= units) { s -= units; ++rb; }
+            }
         }
     }
-    if (u0 + warp < u1) red[((cur_rb - rb0) * ST_WARPS + warp) * 32 + lane] = acc;
-    __syncthreads();
-    ok = true;
-    for (int l = warp; l < nloc; l += ST_WARPS) {
+    if (warp < n) red[((cur_rb - rb0) * NW + warp) * 32 + lane] = acc;
+    const bool cta_ok = __syncthreads_and(ok) != 0;
+    for (int l = warp; cta_ok && l < nloc; l += NW) {
         float v = 0.0f;
 #pragma unroll
-        for (int w = 0; w < ST_WARPS; ++w) v += red[(l * ST_WARPS + w) * 32 + lane];
+        for (int w = 0; w < NW; ++w) v += red[(l * NW + w) * 32 + lane];
         const int rbl = rb0 + l;
         if (epi == 2) {   // SwiGLU over rows interleaved by 16
             const float u = __shfl_down_sync(0xffffffffu, v, 16);
@@ -314,14 +402,15 @@ __device__ __forceinline__ bool step_mv(const StepArgs &a, StepPersist &P, uint8
             if (row < rows) {
                 if (epi == 1) {
                     float r;
-                    ok = ll_get(residual + yoff + row, er, a.status, r) && ok;
+                    if (l == warp && ll_ok(rw, er)) r = ll_val(rw);
+                    else ok = ll_get(residual + yoff + row, er, a.status, r) && ok;
                     v += r;
                 }
                 for (int c2 = 0; c2 < ncopy; ++c2) ll_st(ydst[c2] + yoff + row, v, ey);
             }
         }
     }
-    // the reduction scratch is reused by the next phase
+    // the slots and the reduction scratch are the next phase's
     return __syncthreads_and(ok) != 0;
 }
 
@@ -334,29 +423,6 @@ template <> __device__ __forceinline__ float to_kv_st<float>(float v) { return v
 template <> __device__ __forceinline__ __half to_kv_st<__half>(float v) { return __float2half_rn(v); }
 __device__ __forceinline__ float kv_f(float v) { return v; }
 __device__ __forceinline__ float kv_f(__half v) { return __half2float(v); }
-
-template <typename KV>
-__device__ __forceinline__ void load16(const KV *p, float (&o)[16]) {
-    if constexpr (sizeof(KV) == 2) {
-#pragma unroll
-        for (int i = 0; i < 16; i += 8) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(p + i);
-            const __half2 *h2 = reinterpret_cast<const __half2 *>(&v);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float2 f = __half22float2(h2[k]);
-                o[i + 2 * k] = f.x;
-                o[i + 2 * k + 1] = f.y;
-            }
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-            const float4 v = *reinterpret_cast<const float4 *>(p + i);
-            o[i] = v.x; o[i + 1] = v.y; o[i + 2] = v.z; o[i + 3] = v.w;
-        }
-    }
-}
 
 // rotate-half RoPE of 16 dims per lane: lanes l8 < 4 hold pair firsts
 // (dims i), lanes l8 >= 4 the seconds (dims i + 64); rounding as rope_rotate
@@ -371,90 +437,125 @@ __device__ __forceinline__ void rope16(float (&v)[16], int l8, const StepPersist
     }
 }
 
-// split length so that the (head, split) items about fill the grid's warps:
-// a multiple of 4 positions, at least 16
-__device__ __forceinline__ int attn_split_len(const StepArgs &a, int kv_len) {
-    const int warps = a.grid * ST_WARPS;
-    int ps = (kv_len * a.n_heads + warps - 1) / warps;
-    ps = (ps + 3) & ~3;
-    return ps < 16 ? 16 : ps;
-}
+// positions a CTA folds per iteration: 8 warps x 4 groups of 8 lanes
+constexpr int ATT_SLOTS = LY_WARPS * 4;
 
 // partial (m, l, acc[HD]) of one (head, split): header at 0, 1; acc at 4..
 // (stride HD + 4 floats keeps every acc row 16-byte aligned)
 constexpr int ATT_STRIDE = ST_HD + 4;
 
+// raw K or V elements of one lane (16 dims) as loaded, converted when used
+template <typename KV> struct KvRaw;
+template <> struct KvRaw<__half> {
+    uint4 r[2];
+    __device__ __forceinline__ void load(const __half *p) {
+        r[0] = *reinterpret_cast<const uint4 *>(p);
+        r[1] = *reinterpret_cast<const uint4 *>(p + 8);
+    }
+    __device__ __forceinline__ float at(int j) const {
+        const __half2 h2 = reinterpret_cast<const __half2 *>(&r[j >> 3])[(j & 7) >> 1];
+        return (j & 1) ? __high2float(h2) : __low2float(h2);
+    }
+};
+template <> struct KvRaw<float> {
+    float4 r[4];
+    __device__ __forceinline__ void load(const float *p) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) r[i] = *reinterpret_cast<const float4 *>(p + 4 * i);
+    }
+    __device__ __forceinline__ float at(int j) const {
+        const float4 v = r[j >> 2];
+        return (j & 3) == 0 ? v.x : (j & 3) == 1 ? v.y : (j & 3) == 2 ? v.z : v.w;
+    }
+};
+
+// Attention of one position (llm.c:1173-1213 per head): an item is (local
+// head h, split sp) and takes one CTA; its 32 position slots (warp w, group g)
+// fold positions p0 + slot, p0 + 32 + slot, ... with an online softmax, the
+// next position's K and V in flight while the current one is folded.  Groups
+// merge by shuffles, warps through shared memory; with several splits the
+// last CTA of a head (acq_rel counter) merges the split partials.  The
+// current position's K and V come from the QKV output (rotated and rounded
+// as the cache stores them); the head's first query head of its KV group
+// also writes them to the cache.
 // q, k, v: the LL QKV output of epoch eq; the output goes to every rank's
 // attention vector with epoch eo.  False on a time-out.
 template <typename KV>
-__device__ __noinline__ bool step_attn(const StepArgs &a, const StepPersist &P, uint8_t *sm, int layer, int pos,
+__device__ __forceinline__ bool step_attn(const StepArgs &a, const StepPersist &P, uint8_t *sm, int layer, int pos,
                                        unsigned eq, unsigned eo) {
     constexpr int HD = ST_HD;
-    const int kv_len = pos + 1;
-    const int per_split = attn_split_len(a, kv_len);
+    const int kv_len = pos + 1, nh = a.n_heads;
+    // about grid / heads CTAs per head, whole iterations each
+    const int per_head = max(1, a.grid / nh);
+    int per_split = (kv_len + per_head - 1) / per_head;
+    per_split = (per_split + ATT_SLOTS - 1) / ATT_SLOTS * ATT_SLOTS;
     const int nsp = (kv_len + per_split - 1) / per_split;
-    const int items = a.n_heads * nsp;
+    const int items = nh * nsp;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 3, l8 = lane & 7;
-    const int q_dim = a.n_heads * HD, kv_dim = a.n_kv_heads * HD, group = a.n_heads / a.n_kv_heads;
+    const int slot = warp * 4 + g;
+    const int q_dim = nh * HD, kv_dim = a.n_kv_heads * HD, group = nh / a.n_kv_heads;
     KV *kc = reinterpret_cast<KV *>(a.kc) + (size_t)layer * a.max_seq * kv_dim;
     KV *vc = reinterpret_cast<KV *>(a.vc) + (size_t)layer * a.max_seq * kv_dim;
     const float sqrt_hd = sqrtf((float)HD);
-    for (int it = blockIdx.x * ST_WARPS + warp; it < items; it += a.grid * ST_WARPS) {
-        const int h = it % a.n_heads, sp = it / a.n_heads, kvh = h / group;
+    float *wpart = reinterpret_cast<float *>(sm);                  // [LY_WARPS][ATT_STRIDE]
+    for (int it = blockIdx.x; it < items; it += a.grid) {
+        const int h = it % nh, sp = it / nh, kvh = h / group;
         const int p0 = sp * per_split, p1 = min(kv_len, p0 + per_split);
+        // (waits are CTA-uniform: every warp leaves together on a time-out)
         float qf[16];
-        if (!__all_sync(0xffffffffu, ll_get16(a.qkv + (size_t)h * HD + 16 * l8, eq, a.status, qf))) return false;
+        if (!__syncthreads_and(ll_get16(a.qkv + (size_t)h * HD + 16 * l8, eq, a.status, qf))) return false;
         rope16(qf, l8, P);
-        // this position's k (rotated) and v, rounded as the cache stores them,
-        // kept in the warp's shared scratch (the cache row may not be written yet)
-        const bool has_pos = pos >= p0 && pos < p1;
-        float *kps = reinterpret_cast<float *>(sm) + (size_t)warp * 2 * HD + 16 * l8;
-        float *vps = kps + HD;
-        if (has_pos) {
+        // the current position: its warp takes k and v from the QKV output,
+        // rotated and rounded as the cache stores them, into shared memory
+        const int pslot = (pos - p0) % ATT_SLOTS;
+        const bool pos_warp = pos >= p0 && pos < p1 && pslot / 4 == warp;
+        float *kps = wpart + LY_WARPS * ATT_STRIDE, *vps = kps + HD;
+        {
             float kp[16], vp[16];
-            const bool got = ll_get16(a.qkv + q_dim + (size_t)kvh * HD + 16 * l8, eq, a.status, kp) &&
-                             ll_get16(a.qkv + q_dim + kv_dim + (size_t)kvh * HD + 16 * l8, eq, a.status, vp);
-            if (!__all_sync(0xffffffffu, got)) return false;
-            rope16(kp, l8, P);
+            bool got = true;
+            if (pos_warp)
+                got = ll_get16(a.qkv + q_dim + (size_t)kvh * HD + 16 * l8, eq, a.status, kp) &&
+                      ll_get16(a.qkv + q_dim + kv_dim + (size_t)kvh * HD + 16 * l8, eq, a.status, vp);
+            if (!__syncthreads_and(got)) return false;
+            if (pos_warp) {
+                rope16(kp, l8, P);
+                if (g == pslot % 4) {
+                    const bool writer = h % group == 0;   // one writer per KV head
+                    KV *kd = kc + (size_t)pos * kv_dim + (size_t)kvh * HD + 16 * l8;
+                    KV *vd = vc + (size_t)pos * kv_dim + (size_t)kvh * HD + 16 * l8;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                kp[j] = kv_f(to_kv_st<KV>(kp[j]));
-                vp[j] = kv_f(to_kv_st<KV>(vp[j]));
-            }
-            if (h % group == 0 && g == 0) {   // one writer per KV head
-                KV *kd = kc + (size_t)pos * kv_dim + (size_t)kvh * HD + 16 * l8;
-                KV *vd = vc + (size_t)pos * kv_dim + (size_t)kvh * HD + 16 * l8;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    kd[j] = to_kv_st<KV>(kp[j]);
-                    vd[j] = to_kv_st<KV>(vp[j]);
+                    for (int j = 0; j < 16; ++j) {
+                        const KV kq = to_kv_st<KV>(kp[j]), vq = to_kv_st<KV>(vp[j]);
+                        kps[16 * l8 + j] = kv_f(kq);
+                        vps[16 * l8 + j] = kv_f(vq);
+                        if (writer) { kd[j] = kq; vd[j] = vq; }
+                    }
                 }
+                __syncwarp();
             }
-            if (g == 0) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) { kps[j] = kp[j]; vps[j] = vp[j]; }
-            }
-            __syncwarp();
         }
         float m = -FLT_MAX, l = 0.0f, acc[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
-        for (int base = p0; base < p1; base += 4) {
-            const int p = base + g;
-            const bool live = p < p1;
-            float kf[16], vf[16];
+        const size_t koff = (size_t)kvh * HD + 16 * l8;
+        KvRaw<KV> kn, vn;   // the next position's, in flight
+        int p = p0 + slot;
+        if (p < p1 && p != pos) {
+            kn.load(kc + (size_t)p * kv_dim + koff);
+            vn.load(vc + (size_t)p * kv_dim + koff);
+        }
+        for (; p - slot < p1; p += ATT_SLOTS) {
+            const bool live = p < p1, here = p == pos;
+            const KvRaw<KV> kr = kn, vr = vn;
+            const int pn = p + ATT_SLOTS;
+            if (pn < p1 && pn != pos) {
+                kn.load(kc + (size_t)pn * kv_dim + koff);
+                vn.load(vc + (size_t)pn * kv_dim + koff);
+            }
             float dot = 0.0f;
             if (live) {
-                // k and v of the position requested together: one round trip
-                if (p == pos) {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) { kf[j] = kps[j]; vf[j] = vps[j]; }
-                } else {
-                    load16<KV>(kc + (size_t)p * kv_dim + (size_t)kvh * HD + 16 * l8, kf);
-                    load16<KV>(vc + (size_t)p * kv_dim + (size_t)kvh * HD + 16 * l8, vf);
-                }
-#pragma unroll
-                for (int j = 0; j < 16; ++j) dot = fmaf(qf[j], kf[j], dot);
+                for (int j = 0; j < 16; ++j) dot = fmaf(qf[j], here ? kps[16 * l8 + j] : kr.at(j), dot);
             }
             dot += __shfl_xor_sync(0xffffffffu, dot, 1);
             dot += __shfl_xor_sync(0xffffffffu, dot, 2);
@@ -465,11 +566,11 @@ __device__ __noinline__ bool step_attn(const StepArgs &a, const StepPersist &P, 
                 const float corr = __expf(m - mn), e = __expf(sc - mn);
                 l = fmaf(l, corr, e);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) acc[j] = fmaf(acc[j], corr, e * vf[j]);
+                for (int j = 0; j < 16; ++j) acc[j] = fmaf(acc[j], corr, e * (here ? vps[16 * l8 + j] : vr.at(j)));
                 m = mn;
             }
         }
-        // the four position groups of the warp
+        // the four groups of the warp
 #pragma unroll
         for (int off = 8; off <= 16; off <<= 1) {
             const float om = __shfl_xor_sync(0xffffffffu, m, off), ol = __shfl_xor_sync(0xffffffffu, l, off);
@@ -483,67 +584,92 @@ __device__ __noinline__ bool step_attn(const StepArgs &a, const StepPersist &P, 
             l = l * ca + ol * cb;
             m = M;
         }
-        float *out = a.att_part + ((size_t)h * a.max_splits + sp) * ATT_STRIDE;
+        // the warps of the CTA: warp 0 merges, one float4 of dims a lane
+        float *wp = wpart + warp * ATT_STRIDE;
         if (g == 0) {
 #pragma unroll
             for (int j = 0; j < 16; j += 4)
-                *reinterpret_cast<float4 *>(out + 4 + 16 * l8 + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                *reinterpret_cast<float4 *>(wp + 4 + 16 * l8 + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
         }
-        if (lane == 0) { out[0] = m; out[1] = l; }
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-            // acq_rel: publishes this split's partial, and the last arrival
-            // sees every other split's
-            int prev;
-            asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(prev) : "l"(a.att_cnt + h) : "memory");
-            last = prev == nsp - 1;
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-            // the last split of head h merges all of them (the arithmetic of
-            // dec_attn_merge_kernel): split headers one per lane, warp
-            // reductions, then one aligned float4 of the output per lane and
-            // split with the split loads in flight together
-            const float *ph = a.att_part + (size_t)h * a.max_splits * ATT_STRIDE;
+        if (lane == 0) { wp[0] = m; wp[1] = l; }
+        __syncthreads();
+        if (warp == 0) {
             float M = -FLT_MAX;
-            for (int s0 = 0; s0 < nsp; s0 += 32) {
-                const int s2 = s0 + lane;
-                if (s2 < nsp) {
-                    const float2 ml = __ldcg(reinterpret_cast<const float2 *>(ph + (size_t)s2 * ATT_STRIDE));
-                    if (ml.y > 0.0f) M = fmaxf(M, ml.x);
-                }
-            }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            for (int w = 0; w < LY_WARPS; ++w)
+                if (wpart[w * ATT_STRIDE + 1] > 0.0f) M = fmaxf(M, wpart[w * ATT_STRIDE]);
             float L = 0.0f;
             float4 o4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            for (int s0 = 0; s0 < nsp; s0 += 32) {
-                const int s2 = s0 + lane;
-                float w = 0.0f;
-                if (s2 < nsp) {
-                    const float2 ml = __ldcg(reinterpret_cast<const float2 *>(ph + (size_t)s2 * ATT_STRIDE));
-                    if (ml.y > 0.0f) { w = __expf(ml.x - M); L = fmaf(ml.y, w, L); }
-                }
-                const int n = min(32, nsp - s0);
-#pragma unroll 8
-                for (int j = 0; j < n; ++j) {
-                    const float wj = __shfl_sync(0xffffffffu, w, j);
-                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(ph + (size_t)(s0 + j) * ATT_STRIDE + 4) + lane);
-                    o4.x = fmaf(v.x, wj, o4.x); o4.y = fmaf(v.y, wj, o4.y);
-                    o4.z = fmaf(v.z, wj, o4.z); o4.w = fmaf(v.w, wj, o4.w);
-                }
-            }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-            const float inv = 1.0f / L;
-            for (int c = 0; c < a.world; ++c) {
-                StepWord *dst = a.patt[c] + (size_t)(a.h0 + h) * HD + 4 * lane;
-                ll_st2(dst, o4.x * inv, o4.y * inv, eo);
-                ll_st2(dst + 2, o4.z * inv, o4.w * inv, eo);
+            for (int w = 0; w < LY_WARPS; ++w) {
+                const float lw = wpart[w * ATT_STRIDE + 1];
+                const float s = lw > 0.0f ? __expf(wpart[w * ATT_STRIDE] - M) : 0.0f;
+                L = fmaf(lw, s, L);
+                const float4 v = *reinterpret_cast<const float4 *>(wpart + w * ATT_STRIDE + 4 + 4 * lane);
+                o4.x = fmaf(v.x, s, o4.x); o4.y = fmaf(v.y, s, o4.y);
+                o4.z = fmaf(v.z, s, o4.z); o4.w = fmaf(v.w, s, o4.w);
             }
-            if (lane == 0) a.att_cnt[h] = 0;
+            bool out = nsp == 1;
+            if (!out) {
+                float *part = a.att_part + ((size_t)h * a.max_splits + sp) * ATT_STRIDE;
+                reinterpret_cast<float4 *>(part + 4)[lane] = o4;
+                if (lane == 0) { part[0] = M; part[1] = L; }
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) {
+                    // acq_rel: publishes this split's partial, and the last
+                    // arrival sees every other split's
+                    int prev;
+                    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(prev) : "l"(a.att_cnt + h) : "memory");
+                    last = prev == nsp - 1;
+                }
+                out = __shfl_sync(0xffffffffu, last, 0);
+                if (out) {
+                    // the splits' partials, in split order (dec_attn_merge_kernel's arithmetic)
+                    const float *ph = a.att_part + (size_t)h * a.max_splits * ATT_STRIDE;
+                    M = -FLT_MAX;
+                    for (int s0 = 0; s0 < nsp; s0 += 32) {
+                        const int s2 = s0 + lane;
+                        if (s2 < nsp) {
+                            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(ph + (size_t)s2 * ATT_STRIDE));
+                            if (ml.y > 0.0f) M = fmaxf(M, ml.x);
+                        }
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+                    L = 0.0f;
+                    o4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    for (int s0 = 0; s0 < nsp; s0 += 32) {
+                        const int s2 = s0 + lane;
+                        float w = 0.0f;
+                        if (s2 < nsp) {
+                            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(ph + (size_t)s2 * ATT_STRIDE));
+                            if (ml.y > 0.0f) { w = __expf(ml.x - M); L = fmaf(ml.y, w, L); }
+                        }
+                        const int n = min(32, nsp - s0);
+#pragma unroll 8
+                        for (int j = 0; j < n; ++j) {
+                            const float wj = __shfl_sync(0xffffffffu, w, j);
+                            const float4 v = __ldcg(reinterpret_cast<const float4 *>(ph + (size_t)(s0 + j) * ATT_STRIDE + 4) + lane);
+                            o4.x = fmaf(v.x, wj, o4.x); o4.y = fmaf(v.y, wj, o4.y);
+                            o4.z = fmaf(v.z, wj, o4.z); o4.w = fmaf(v.w, wj, o4.w);
+                        }
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+                    if (lane == 0) a.att_cnt[h] = 0;
+                }
+            }
+            if (out) {
+                const float inv = 1.0f / L;
+                for (int c = 0; c < a.world; ++c) {
+                    StepWord *dst = a.patt[c] + (size_t)(a.h0 + h) * HD + 4 * lane;
+                    ll_st2(dst, o4.x * inv, o4.y * inv, eo);
+                    ll_st2(dst + 2, o4.z * inv, o4.w * inv, eo);
+                }
+            }
         }
+        __syncthreads();   // wpart is the next item's
     }
     return true;
 }
@@ -559,6 +685,7 @@ __device__ __forceinline__ bool step_begin(const StepArgs &a, StepPersist &P, co
         P.pos = __ldcg(a.pos);
         P.ok = __ldcg(a.status) == 0;
         mbar_init(&P.mbar, 1);
+        for (int k = 0; k < MAX_WARPS * ST_MAX_DEPTH; ++k) mbar_init(&P.slot[k], 1);
         fence_barrier_init();
     }
     __syncthreads();
@@ -571,7 +698,7 @@ __device__ __forceinline__ void step_end(unsigned long long *launches, const Ste
 }
 
 template <int LT, int ACT, bool KVF16>
-__global__ void __launch_bounds__(ST_THREADS, 1) dec_step_kernel(const StepArgs a) {
+__global__ void __launch_bounds__(LY_THREADS, 1) dec_step_kernel(const StepArgs a) {
     using KV = typename std::conditional<KVF16, __half, float>::type;
     extern __shared__ __align__(128) uint8_t smem[];
     StepPersist &P = *reinterpret_cast<StepPersist *>(smem);
@@ -586,7 +713,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) dec_step_kernel(const StepArgs 
         P.rope[tid] = make_float2(c, s);
     }
     __syncthreads();
-    unsigned mb_par = 0;
+    unsigned mb_par = 0, spar = 0;
     StepWord *const x = a.px[a.rank];
 
     // embed: x = emb[seq[pos]] (every rank, whole vector, own copy)
@@ -594,7 +721,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) dec_step_kernel(const StepArgs 
     {
         const unsigned e0 = step_epoch(a, P.launch, 0);
         const int tok = __ldcg(a.seq + pos);
-        for (int i = blockIdx.x * ST_THREADS + tid; i < a.dim; i += a.grid * ST_THREADS) {
+        for (int i = blockIdx.x * LY_THREADS + tid; i < a.dim; i += a.grid * LY_THREADS) {
             float v = 0.0f;
             if (tok >= 0 && tok < a.vocab)
                 v = a.emb_f16 ? __half2float(reinterpret_cast<const __half *>(a.emb)[(size_t)tok * a.dim + i])
@@ -643,7 +770,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) dec_step_kernel(const StepArgs 
             const unsigned er = step_epoch(a, P.launch, k == 2 ? ph - 3 : ph - 2);
             const float *nw = k == 0 ? L.attn_norm : k == 3 ? L.ffn_norm : nullptr;
             const int epi = k == 3 ? 2 : (k == 2 || k == 4) ? 1 : 0;
-            ok = step_mv<LT, ACT>(a, P, sm, mb_par, W, rows, in_dim, xin, ein, ydst, ncopy, yoff, eout, x, er, nw,
+            ok = step_mv<LT, ACT, LY_WARPS, false>(a, P, sm, mb_par, spar, W, rows, in_dim, xin, ein, ydst, ncopy, yoff, eout, x, er, nw,
                                   epi);
         }
         if (!__syncthreads_or(!ok)) continue;
@@ -656,23 +783,24 @@ __global__ void __launch_bounds__(ST_THREADS, 1) dec_step_kernel(const StepArgs 
 // generation), then on CTA 0 the logits gathered into the plain buffer, the
 // sampler and the next position
 template <int OT, int ACT>
-__global__ void __launch_bounds__(ST_THREADS, 1) dec_out_kernel(const StepArgs a) {
+__global__ void __launch_bounds__(OUT_THREADS, 1) dec_out_kernel(const StepArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     StepPersist &P = *reinterpret_cast<StepPersist *>(smem);
     uint8_t *sm = smem + ST_PERSIST;
     unsigned long long *launches = a.bar + 3;
     if (!step_begin(a, P, launches)) return;
     const int tid = threadIdx.x, pos = P.pos;
-    unsigned mb_par = 0;
+    unsigned mb_par = 0, spar = 0;
     const int ph = step_phases(a.n_layers) - 1;
     step_prefetch(a, ph);
     const unsigned ein = step_epoch(a, P.launch, ph - 1), eout = step_epoch(a, P.launch, ph);
     const bool need = !a.sa.gen || pos >= a.sa.n_prompt - 1;
-    if (need && !step_mv<OT, ACT>(a, P, sm, mb_par, a.out_w, a.vocab_loc, a.dim, a.px[a.rank], ein, a.plog,
+    if (need && !step_mv<OT, ACT, OUT_WARPS, true>(a, P, sm, mb_par, spar, a.out_w, a.vocab_loc, a.dim, a.px[a.rank], ein, a.plog,
                                   a.world, a.v0, eout, nullptr, 0, a.final_norm, 0))
         return;
     if (blockIdx.x == 0) {
-        if (need && !__syncthreads_and(ll_gather(a.logits, a.plog[a.rank], a.vocab, eout, a.status))) return;
+        if (need && !__syncthreads_and(ll_gather<OUT_THREADS>(a.logits, a.plog[a.rank], a.vocab, eout, a.status)))
+            return;
         if (a.sample && need) {
             SampleSmem &S = *reinterpret_cast<SampleSmem *>(sm);
             const int gi = a.sa.gen ? pos - (a.sa.n_prompt - 1) : 0;
@@ -694,44 +822,50 @@ __global__ void __launch_bounds__(ST_THREADS, 1) dec_out_kernel(const StepArgs a
     step_end(launches, P);
 }
 
-size_t mv_smem(const StepArgs &a, int act, int type, int rows, int in_dim, bool norm) {
+// shared memory of a matvec phase (the layout of step_mv) of nw warps with
+// `depth` shared-memory slots a warp (0: the register ring)
+size_t mv_smem(const StepArgs &a, int act, int type, int rows, int in_dim, bool norm, int nw, int depth) {
     const int vals = type == GT_Q8_0 ? 128 : 256, b32 = type == GT_Q8_0 ? 4 : 8;
+    const size_t ub = type == GT_Q8_0 ? 4352 : 4608;
     const int units = (in_dim + vals - 1) / vals, nblk32p = units * b32;
     const int nrb = (rows + 31) / 32, nloc = (nrb + a.grid - 1) / a.grid;
-    size_t o = ((size_t)nloc * ST_WARPS * 32 * 4 + 127) & ~(size_t)127;
-    if (act == HOLO_ACT_Q8) o += (((size_t)nblk32p * 40 + 127) & ~(size_t)127) + (size_t)nblk32p * 128;
-    else o += ((size_t)nblk32p * 132 + 127) & ~(size_t)127;
+    auto al = [](size_t v) { return (v + 127) & ~(size_t)127; };
+    size_t o = (depth ? al((size_t)nw * depth * ub) : 0) + al((size_t)nloc * nw * 32 * 4);
+    if (act == HOLO_ACT_Q8) o += al((size_t)nblk32p * 40) + (size_t)nblk32p * 128;
+    else o += al((size_t)nblk32p * 132);
     if (norm) o += (size_t)nblk32p * 128;
-    return o + ST_WARPS * 4;
+    return o + nw * 4;
 }
 
 size_t layer_smem(const StepArgs &a, int lt, int act) {
     const int q_dim = a.n_heads * ST_HD, kv_dim = a.n_kv_heads * ST_HD;
-    size_t m = mv_smem(a, act, lt, q_dim + 2 * kv_dim, a.dim, true);
-    m = std::max(m, mv_smem(a, act, lt, a.dim_loc, a.n_heads_g * ST_HD, false));
-    m = std::max(m, mv_smem(a, act, lt, 2 * a.ffn_loc, a.dim, true));
-    m = std::max(m, mv_smem(a, act, lt, a.dim_loc, a.ffn, false));
-    m = std::max(m, (size_t)ST_WARPS * 2 * ST_HD * sizeof(float));   // attention scratch
+    size_t m = mv_smem(a, act, lt, q_dim + 2 * kv_dim, a.dim, true, LY_WARPS, 0);
+    m = std::max(m, mv_smem(a, act, lt, a.dim_loc, a.n_heads_g * ST_HD, false, LY_WARPS, 0));
+    m = std::max(m, mv_smem(a, act, lt, 2 * a.ffn_loc, a.dim, true, LY_WARPS, 0));
+    m = std::max(m, mv_smem(a, act, lt, a.dim_loc, a.ffn, false, LY_WARPS, 0));
+    m = std::max(m, (size_t)(LY_WARPS * ATT_STRIDE + 2 * ST_HD) * sizeof(float));   // attention scratch
     return ST_PERSIST + m;
 }
 
-size_t out_smem(const StepArgs &a, int act) {
-    size_t m = mv_smem(a, act, a.out_type, a.vocab_loc, a.dim, true);
+size_t out_smem(const StepArgs &a, int act, int depth) {
+    size_t m = mv_smem(a, act, a.out_type, a.vocab_loc, a.dim, true, OUT_WARPS, depth);
     if (a.sample) m = std::max(m, sizeof(SampleSmem));
     return ST_PERSIST + m;
 }
 
+constexpr size_t ST_SMEM_MAX = 227 * 1024;
+
 template <typename K>
-bool coop_launch(K kern, const StepArgs &a, size_t smem, cudaStream_t st) {
-    if (smem > 227 * 1024) {
+bool coop_launch(K kern, const StepArgs &a, size_t smem, int threads, cudaStream_t st) {
+    if (smem > ST_SMEM_MAX) {
         holo_set_status(HOLO_E_UNSUPPORTED, "decode step: shared memory");
         return false;
     }
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ST_SMEM_MAX) != cudaSuccess)
         return holo_check_launch("decode step: attributes");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.grid);
-    cfg.blockDim = dim3(ST_THREADS);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -747,17 +881,26 @@ template <int LT>
 bool launch_layers(const StepArgs &a, int act, int kv_f16, cudaStream_t st) {
     const size_t smem = layer_smem(a, LT, act);
     if (act == HOLO_ACT_Q8)
-        return kv_f16 ? coop_launch(dec_step_kernel<LT, HOLO_ACT_Q8, true>, a, smem, st)
-                      : coop_launch(dec_step_kernel<LT, HOLO_ACT_Q8, false>, a, smem, st);
-    return kv_f16 ? coop_launch(dec_step_kernel<LT, HOLO_ACT_F32, true>, a, smem, st)
-                  : coop_launch(dec_step_kernel<LT, HOLO_ACT_F32, false>, a, smem, st);
+        return kv_f16 ? coop_launch(dec_step_kernel<LT, HOLO_ACT_Q8, true>, a, smem, LY_THREADS, st)
+                      : coop_launch(dec_step_kernel<LT, HOLO_ACT_Q8, false>, a, smem, LY_THREADS, st);
+    return kv_f16 ? coop_launch(dec_step_kernel<LT, HOLO_ACT_F32, true>, a, smem, LY_THREADS, st)
+                  : coop_launch(dec_step_kernel<LT, HOLO_ACT_F32, false>, a, smem, LY_THREADS, st);
 }
 
 template <int OT>
-bool launch_out(const StepArgs &a, int act, cudaStream_t st) {
-    const size_t smem = out_smem(a, act);
-    return act == HOLO_ACT_Q8 ? coop_launch(dec_out_kernel<OT, HOLO_ACT_Q8>, a, smem, st)
-                              : coop_launch(dec_out_kernel<OT, HOLO_ACT_F32>, a, smem, st);
+bool launch_out(const StepArgs &args, int act, cudaStream_t st) {
+    StepArgs a = args;
+    // the deepest slot pipeline that fits
+    a.mv_depth = 0;
+    for (int d = ST_MAX_DEPTH; d >= 1 && a.mv_depth == 0; --d)
+        if (out_smem(a, act, d) <= ST_SMEM_MAX) a.mv_depth = d;
+    if (a.mv_depth == 0) {
+        holo_set_status(HOLO_E_UNSUPPORTED, "decode step: shared memory");
+        return false;
+    }
+    const size_t smem = out_smem(a, act, a.mv_depth);
+    return act == HOLO_ACT_Q8 ? coop_launch(dec_out_kernel<OT, HOLO_ACT_Q8>, a, smem, OUT_THREADS, st)
+                              : coop_launch(dec_out_kernel<OT, HOLO_ACT_F32>, a, smem, OUT_THREADS, st);
 }
 
 }  // namespace

@@ -60,6 +60,7 @@ struct StepArgs {
     unsigned long long *bar;              // [1] launches of the layers kernel, [3] of the output kernel
     int *status;
     int grid;
+    int mv_depth;                         // weight units in flight per warp (set per kernel at launch)
     int world, rank;
     // LL vectors of every rank (index rank: this rank's own)
     StepWord *px[STEP_MAX_RANKS], *patt[STEP_MAX_RANKS], *ph[STEP_MAX_RANKS], *plog[STEP_MAX_RANKS];
