@@ -1,0 +1,345 @@
+// prefill.cu -- batched quantized matmul for prompt processing on the 5th-gen
+// tensor cores: Y[M][N] = X[M][K] . W^T, W an N x K tiled Q4_K weight
+// (cuda_upload_quant), X fp32, M tokens.
+//
+// The reference has no batched path: its prefill runs llm_forward one token at
+// a time (src/ai/llm.c:1049, llm_cuda.c:574), i.e. M matvecs (cuda_ops.cu
+// kernels 976-1060 for Q4_K).  Here the weight tile is dequantized once and
+// multiplied against all M activation rows with tcgen05.mma:
+//
+//   * activations: each row quantized to Q8 per 32-block exactly as the
+//     matvec does (d = amax/127, q = rint(x/d)), then the dequantized value
+//     d*q rounded to fp16, written pre-swizzled in the tensor core's 128-byte
+//     K-major layout (pf_act_kernel) so one 1-D bulk copy stages a tile;
+//   * weights: 8 warps dequantize Q4_K (quant.c: y = (d*sc)*q - dmin*m in
+//     fp32, then fp16) straight into the same swizzled layout in shared memory;
+//   * one thread issues tcgen05.mma.kind::f16 (fp32 accumulation in TMEM,
+//     128 weight rows x TN tokens per CTA), tcgen05.commit frees each stage;
+//   * the 8 warps read the accumulators back with tcgen05.ld.
+// A CTA owns 128 weight rows, TN <= 256 tokens and a range of K; several K
+// ranges (few weight tiles, e.g. 4096 x 14336) are summed by pf_reduce_kernel
+// in a fixed order.  Every wait is bounded (HOLO_E_TIMEOUT).
+#include "holo_common.cuh"
+#include "mv_unit.cuh"
+
+#include <algorithm>
+
+namespace {
+
+using namespace holo_mv;
+
+constexpr int PF_BM = 128;                         // weight rows per CTA (MMA M)
+constexpr int PF_BK = 64;                          // K per stage: one 128-byte atom of fp16
+constexpr int PF_STAGES = 4;
+constexpr int PF_DQ_WARPS = 8;                     // dequantize, then read the accumulators
+constexpr int PF_THREADS = (PF_DQ_WARPS + 2) * 32; // + bulk-copy warp + MMA warp
+constexpr int PF_A_BYTES = PF_BM * 128;            // one stage of weights: 16 KB
+
+struct PfBars {
+    uint64_t full_a[PF_STAGES];   // 8 dequantizing warps arrived
+    uint64_t full_b[PF_STAGES];   // activation tile landed
+    uint64_t empty[PF_STAGES];    // the stage's MMAs completed
+    uint64_t done;                // the last MMA completed
+    uint32_t tmem;                // accumulator base (TMEM address)
+};
+
+// ---- tcgen05 primitives ----------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// shared-memory descriptor of a K-major, 128-byte-swizzled operand: rows of
+// 128 bytes, 8-row atoms 1024 bytes apart (SBO), 16-byte LBO, version 1
+__device__ __forceinline__ uint64_t sw128_desc(const void *smem) {
+    const uint32_t a = smem_addr(smem);
+    return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// instruction descriptor: fp16 x fp16 -> fp32, both K-major, M = 128, N = tn
+__host__ __device__ constexpr uint32_t pf_idesc(int tn) {
+    return (1u << 4) | ((uint32_t)(tn >> 3) << 17) | ((uint32_t)(PF_BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, bool acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"((uint32_t)acc) : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(smem_addr(bar)) : "memory");
+}
+
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// byte offset of element (row r, column c) of a [rows][64] fp16 tile in the
+// 128-byte-swizzled K-major layout (16-byte chunk index XOR row mod 8)
+__host__ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((((c >> 3) ^ (r & 7)) & 7) << 4) + (c & 7) * 2);
+}
+
+// ---- activations: Q8 per 32-block, dequantized to fp16, tiled + swizzled ---
+// xt tile (mt, kc) = rows [mt*tn, +tn) x columns [kc*64, +64), tn*128 bytes;
+// rows past M are zero.  One warp per (row, 32-block), lane = element.
+__global__ void pf_act_kernel(__half *__restrict__ xt, const float *__restrict__ x, int M, int Mpad, int K,
+                              int tn) {
+    const int nb = K / 32;
+    const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= (long long)Mpad * nb) return;
+    const int m = (int)(w / nb), b = (int)(w % nb);
+    float v = m < M ? x[(size_t)m * K + (size_t)b * 32 + lane] : 0.0f;
+    // quantize_act_q8's arithmetic: d = amax / 127, id = 1 / d, q = rint(v * id)
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float q = fminf(fmaxf(rintf(__fmul_rn(v, id)), -127.0f), 127.0f);
+    const __half h = __float2half_rn(__fmul_rn(d, q));
+    const int k = b * 32 + lane, mt = m / tn, r = m % tn, kc = k / PF_BK;
+    uint8_t *tile = reinterpret_cast<uint8_t *>(xt) + ((size_t)mt * (K / PF_BK) + kc) * (size_t)tn * 128;
+    *reinterpret_cast<__half *>(tile + sw128_off(r, k % PF_BK)) = h;
+}
+
+// ---- the matmul ----------------------------------------------------------------
+// out[ks][M][N] (ks = blockIdx.z, K chunks [kc0, kc1)); W tiled Q4_K with
+// `units` super-blocks a row.
+template <int TN>
+__global__ void __launch_bounds__(PF_THREADS, 1)
+pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint8_t *__restrict__ xt, int M, int N,
+              int K, int units, int kc_per_split, int *status) {
+    extern __shared__ uint8_t pf_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sa = smem;                                   // [stages][128 rows][128 B]
+    uint8_t *sb = smem + PF_STAGES * PF_A_BYTES;          // [stages][TN rows][128 B]
+    PfBars &B = *reinterpret_cast<PfBars *>(sb + PF_STAGES * TN * 128);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nkc = K / PF_BK;
+    const int n0 = blockIdx.x * PF_BM, mt = blockIdx.y, ks = blockIdx.z;
+    const int kc0 = ks * kc_per_split, kc1 = min(nkc, kc0 + kc_per_split);
+    const int nch = kc1 - kc0;   // >= 1 by construction
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PF_STAGES; ++s) {
+            mbar_init(&B.full_a[s], PF_DQ_WARPS);
+            mbar_init(&B.full_b[s], 1);
+            mbar_init(&B.empty[s], 1);
+        }
+        mbar_init(&B.done, 1);
+        fence_barrier_init();
+    }
+    if (warp == PF_DQ_WARPS + 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_addr(&B.tmem)), "r"((uint32_t)TN) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = B.tmem;
+
+    if (warp < PF_DQ_WARPS) {
+        // thread -> weight row r, sub-block half of each 64-value chunk
+        const int t = threadIdx.x, r = t & (PF_BM - 1), half = t >> 7, lr = r & 31;
+        const uint8_t *wrb = W + (size_t)((n0 + r) >> 5) * units * 4608;
+        bool ok = true;
+        for (int i = 0; i < nch && ok; ++i) {
+            const int c = kc0 + i, s = i % PF_STAGES;
+            const int sbk = c >> 2, j = 2 * (c & 3) + half;   // super-block, sub-block
+            const uint8_t *unit = wrb + (size_t)sbk * 4608;
+            const uint4 h = ldg_stream(unit + lr * 16);
+            const uint4 q = ldg_stream(unit + unit_plane_off<GT_Q4_K>(j, lr));
+            if (i >= PF_STAGES)
+                ok = mbar_wait_bounded(&B.empty[s], ((i / PF_STAGES) + 1) & 1, status, HOLO_E_TIMEOUT);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            // quant.c:290-297 scale/min unpack (the unit layout keeps the raw bytes)
+            const float d = half_bits_to_float(h.x & 0xffffu), dmin = half_bits_to_float(h.x >> 16);
+            const uint32_t scw = j < 4 ? (h.y & 0x3F3F3F3Fu) : (((h.w & LO4) << 2) | ((h.y >> 6) & 0x03030303u));
+            const uint32_t mw = j < 4 ? (h.z & 0x3F3F3F3Fu)
+                                      : ((((h.w >> 4) & LO4) << 2) | ((h.z >> 6) & 0x03030303u));
+            const float scv = __fmul_rn(d, ubyte_to_float(scw, j & 3));
+            const float mv = __fmul_rn(dmin, ubyte_to_float(mw, j & 3));
+            uint8_t *arow = sa + s * PF_A_BYTES;
+            // 16-byte chunk cc of this half: positions 8cc..8cc+7 of the
+            // sub-block = low nibbles (cc 0, 1) or high nibbles (cc 2, 3) of
+            // bytes 8(cc&1)..8(cc&1)+7
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                const uint32_t w0 = (cc & 1) ? q.z : q.x, w1 = (cc & 1) ? q.w : q.y;
+                const uint32_t n0w = (cc & 2) ? ((w0 >> 4) & LO4) : (w0 & LO4);
+                const uint32_t n1w = (cc & 2) ? ((w1 >> 4) & LO4) : (w1 & LO4);
+                uint32_t packed[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const uint32_t wv = e < 2 ? n0w : n1w;
+                    const float v0 = __fsub_rn(__fmul_rn(scv, ubyte_to_float(wv, (e & 1) * 2)), mv);
+                    const float v1 = __fsub_rn(__fmul_rn(scv, ubyte_to_float(wv, (e & 1) * 2 + 1)), mv);
+                    const __half2 hv = __floats2half2_rn(v0, v1);
+                    packed[e] = *reinterpret_cast<const uint32_t *>(&hv);
+                }
+                *reinterpret_cast<uint4 *>(arow + sw128_off(r, 32 * half + 8 * cc)) =
+                    make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            }
+            fence_proxy_async_smem();   // the tensor core reads these through the async proxy
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.full_a[s]);
+        }
+        // accumulators -> out: warp w reads TMEM lanes 32(w%4).., columns of its half
+        ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(&B.done, 0, status, HOLO_E_TIMEOUT));
+        tc_fence_after();
+        if (ok) {
+            const int quarter = warp & 3, colh = warp >> 2;
+            const int row = n0 + 32 * quarter + lane;
+            float *o = out + (size_t)ks * M * N;
+            for (int cb = colh * (TN / 2); cb < (colh + 1) * (TN / 2); cb += 32) {
+                uint32_t v[32];
+                tc_ld32(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)cb, v);
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    const int m = mt * TN + cb + jj;
+                    if (m < M) o[(size_t)m * N + row] = __uint_as_float(v[jj]);
+                }
+            }
+        }
+    } else if (warp == PF_DQ_WARPS) {
+        // activation tiles, one bulk copy a stage
+        if (lane == 0) {
+            const uint8_t *xb = xt + ((size_t)mt * (K / PF_BK)) * (size_t)TN * 128;
+            int issued = 0;
+            for (int i = 0; i < nch; ++i) {
+                const int s = i % PF_STAGES;
+                if (i >= PF_STAGES &&
+                    !mbar_wait_bounded(&B.empty[s], ((i / PF_STAGES) + 1) & 1, status, HOLO_E_TIMEOUT))
+                    break;
+                mbar_arrive_expect_tx(&B.full_b[s], (uint32_t)(TN * 128));
+                bulk_copy_g2s(sb + (size_t)s * TN * 128, xb + (size_t)(kc0 + i) * TN * 128, (uint32_t)(TN * 128),
+                              &B.full_b[s]);
+                issued = i + 1;
+            }
+            // every copy has landed before the CTA ends (the MMA thread may
+            // have stopped consuming on a time-out)
+            for (int i = max(0, issued - PF_STAGES); i < issued; ++i)
+                mbar_wait_bounded(&B.full_b[i % PF_STAGES], (i / PF_STAGES) & 1, nullptr, 0);
+        }
+    } else {
+        // MMA issue: 4 K-steps of 16 a stage
+        if (lane == 0) {
+            constexpr uint32_t idesc = pf_idesc(TN);
+            bool ok = true;
+            for (int i = 0; i < nch && ok; ++i) {
+                const int s = i % PF_STAGES;
+                const uint32_t par = (i / PF_STAGES) & 1;
+                ok = mbar_wait_bounded(&B.full_a[s], par, status, HOLO_E_TIMEOUT) &&
+                     mbar_wait_bounded(&B.full_b[s], par, status, HOLO_E_TIMEOUT);
+                if (!ok) break;
+                tc_fence_after();
+                const uint8_t *a = sa + s * PF_A_BYTES, *b = sb + (size_t)s * TN * 128;
+#pragma unroll
+                for (int kk = 0; kk < PF_BK / 16; ++kk)
+                    tc_mma(tmem, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), idesc, (i | kk) != 0);
+                tc_commit(&B.empty[s]);
+            }
+            // completes once every MMA issued above has (or at once if none was)
+            tc_commit(&B.done);
+        }
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == PF_DQ_WARPS + 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"((uint32_t)TN)
+                     : "memory");
+    }
+}
+
+// y[m][n] = sum over ks of part[ks][m][n], in ks order
+__global__ void pf_reduce_kernel(float *__restrict__ y, const float *__restrict__ part, long long mn, int splits) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += (long long)gridDim.x * blockDim.x) {
+        float s = part[i];
+        for (int k = 1; k < splits; ++k) s += part[(size_t)k * mn + i];
+        y[i] = s;
+    }
+}
+
+size_t pf_smem(int tn) { return 1024 + (size_t)PF_STAGES * (PF_A_BYTES + tn * 128) + sizeof(PfBars); }
+
+template <int TN>
+bool launch_mma(float *out, const uint8_t *W, const uint8_t *xt, int M, int N, int K, int units, int splits,
+                int kc_per_split, int mtiles, int *status, cudaStream_t st) {
+    const size_t smem = pf_smem(TN);
+    if (cudaFuncSetAttribute(pf_mma_kernel<TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return holo_check_launch("prefill: attributes");
+    pf_mma_kernel<TN><<<dim3(N / PF_BM, mtiles, splits), PF_THREADS, smem, st>>>(out, W, xt, M, N, K, units,
+                                                                                kc_per_split, status);
+    return holo_check_launch("prefill matmul");
+}
+
+}  // namespace
+
+extern "C" int cuda_matmul_quant_batched(float *Y, const void *W, const float *X, int M, int N, int K) {
+    HoloDevice *D = holo_dev();
+    if (!D) return cuda_last_status();
+    WeightInfo wi;
+    if (!Y || !W || !X || M <= 0 || !holo_registry_find(W, &wi) || wi.type != GT_Q4_K || wi.rows != N ||
+        wi.cols != K || N % PF_BM || K % 256) {
+        holo_set_status(HOLO_E_ARG, "cuda_matmul_quant_batched: needs a tiled Q4_K weight (cuda_upload_quant), "
+                                    "N % 128 == 0, K % 256 == 0");
+        return HOLO_E_ARG;
+    }
+    if (wi.q4k_layout != HOLO_Q4K_REF && wi.q4k_layout != HOLO_Q4K_GGML) {
+        holo_set_status(HOLO_E_ARG, "cuda_matmul_quant_batched: unknown Q4_K layout");
+        return HOLO_E_ARG;
+    }
+    cudaStream_t st = holo_stream();
+    const int tn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
+    const int mtiles = (M + tn - 1) / tn, Mpad = mtiles * tn;
+    const int nkc = K / PF_BK;
+    // K splits so that the CTAs cover the SMs when the weight has few row tiles
+    const int base = (N / PF_BM) * mtiles;
+    int splits = std::max(1, std::min(nkc / 8, D->sms / base));
+    const int kc_per_split = (nkc + splits - 1) / splits;
+    splits = (nkc + kc_per_split - 1) / kc_per_split;   // every split non-empty
+    const size_t xt_bytes = (size_t)Mpad * K * 2;
+    const size_t part_bytes = splits > 1 ? (size_t)splits * M * N * 4 : 0;
+    uint8_t *tmp = static_cast<uint8_t *>(holo_tmp(xt_bytes + part_bytes + 256));
+    if (!tmp) return cuda_last_status();
+    uint8_t *xt = tmp;
+    float *part = splits > 1 ? reinterpret_cast<float *>(tmp + ((xt_bytes + 255) & ~(size_t)255)) : Y;
+    const long long warps = (long long)Mpad * (K / 32);
+    pf_act_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(reinterpret_cast<__half *>(xt), X, M, Mpad,
+                                                                       K, tn);
+    if (!holo_check_launch("prefill activations")) return cuda_last_status();
+    const uint8_t *w = static_cast<const uint8_t *>(W);
+    bool ok;
+    switch (tn) {
+    case 64: ok = launch_mma<64>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st); break;
+    case 128: ok = launch_mma<128>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st); break;
+    default: ok = launch_mma<256>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st); break;
+    }
+    if (!ok) return cuda_last_status();
+    if (splits > 1) {
+        const long long mn = (long long)M * N;
+        pf_reduce_kernel<<<(unsigned)std::min<long long>((mn + 255) / 256, 4 * D->sms), 256, 0, st>>>(Y, part, mn,
+                                                                                                     splits);
+        if (!holo_check_launch("prefill reduce")) return cuda_last_status();
+    }
+    return HOLO_OK;
+}

@@ -205,6 +205,15 @@ int holo_model_open_peers(void *model, const void *handles);
 void holo_model_reset(void *model);
 void holo_model_free(void *model);
 
+/* Batched quantized matmul for prompt processing (no counterpart in the
+ * reference, whose prefill runs llm_forward one token at a time,
+ * src/ai/llm.c:1049): Y[M][N] = X[M][K] . W^T on the tensor cores, W an N x K
+ * Q4_K weight from cuda_upload_quant (N % 128 == 0, K % 256 == 0), X fp32.
+ * X is quantized to Q8 per 32-block as the matvecs do; the dequantized
+ * activations and weights are rounded to fp16 and multiplied with fp32
+ * accumulation.  Device pointers; HOLO_OK or an error status. */
+int cuda_matmul_quant_batched(float *Y, const void *W, const float *X, int M, int N, int K);
+
 /* Seeded synthetic weights on the device: rows x cols values N(0, std) from a
  * counter-based generator, written to dst as raw GGUF blocks of ggml_type
  * (0 F32, 1 F16 plain values; 8 Q8_0, 2 Q4_0, 12 Q4_K round-to-nearest), the

@@ -1,0 +1,76 @@
+"""Batched quantized matmul on the tensor cores (cuda_matmul_quant_batched,
+csrc/prefill.cu) against the oracle's Q8-activation restatement, one matvec
+per activation row (oracle/holo_oracle.c ho_matvec_q8act).
+
+Both operands reach the tensor core as fp16: the Q8 activation d*q and the
+Q4_K value (d*sc)*q - dmin*m, each rounded once (relative error <= 2^-11).
+The bar, fixed here: max |Y - R| / max |R| <= 1e-3 over the whole output
+(the north star's fp32 tolerance), R the restatement's fp32 result.
+"""
+import numpy as np
+import pytest
+
+import holo_b200 as hb
+from holo_b200 import synth
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def run(dev, W, X, M, N, K):
+    Wd = dev.upload_quant(W, hb.Q4_K, N, K)
+    Xd = dev.upload(np.ascontiguousarray(X, np.float32))
+    Yd = dev.alloc(4 * M * N)
+    rc = dev.lib.cuda_matmul_quant_batched(Yd, Wd, Xd, M, N, K)
+    dev.check("cuda_matmul_quant_batched")
+    assert rc == hb.HOLO_OK
+    Y = dev.download(Yd, (M, N), np.float32)
+    for p in (Wd, Xd, Yd):
+        dev.free(p)
+    return Y
+
+
+# (M, N, K): token counts on both sides of every tile size (64/128/256), a
+# partial last tile, K splits (few row tiles), one 128-row tile
+CASES = [(64, 256, 512), (1, 128, 256), (17, 384, 1024), (100, 256, 2048), (128, 512, 512), (200, 384, 768),
+         (256, 256, 1024), (300, 128, 2048), (512, 256, 512)]
+
+
+@pytest.mark.parametrize("M,N,K", CASES)
+def test_batched_matches_q8_restatement(dev, oracle, M, N, K):
+    W = synth.quant_matrix(hb.Q4_K, N, K, seed=M + N + K)
+    X = np.random.default_rng(M * 7 + K).standard_normal((M, K), dtype=np.float32)
+    Y = run(dev, W, X, M, N, K)
+    R = np.stack([oracle.matvec_q8(hb.Q4_K, W, X[m], N, K) for m in range(M)])
+    err = rel_err(Y, R)
+    print(f"M={M} N={N} K={K}: norm-wise rel err {err:.3e}")
+    assert err <= 1e-3
+
+
+@pytest.mark.parametrize("N,K", [(14336, 4096), (4096, 14336)])
+def test_prefill_shapes_rows_match(dev, oracle, N, K):
+    """The prefill configurations at M = 64 (K split for 4096 x 14336); 6
+    activation rows checked against the restatement."""
+    M = 64
+    W = synth.quant_matrix(hb.Q4_K, N, K, seed=0)
+    X = synth.activation(M * K, seed=0).reshape(M, K)
+    Y = run(dev, W, X, M, N, K)
+    rows = [0, 1, 17, 31, 32, 63]
+    R = np.stack([oracle.matvec_q8(hb.Q4_K, W, X[m], N, K, threads=8) for m in rows])
+    err = rel_err(Y[rows], R)
+    print(f"{N}x{K} M={M}: norm-wise rel err {err:.3e}")
+    assert err <= 1e-3
+
+
+def test_rejects_untiled_or_misaligned(dev):
+    W = synth.quant_matrix(hb.Q4_K, 100, 256, seed=1)        # 100 rows: not a multiple of 128
+    Wd = dev.upload_quant(W, hb.Q4_K, 100, 256)
+    Xd, Yd = dev.alloc(4 * 256), dev.alloc(4 * 100)
+    rc = dev.lib.cuda_matmul_quant_batched(Yd, Wd, Xd, 1, 100, 256)
+    assert rc == hb.HOLO_E_ARG
+    dev.lib.cuda_clear_status()
+    raw = dev.upload(np.zeros(256 * 144 // 256 * 128, np.uint8))   # not from cuda_upload_quant
+    assert dev.lib.cuda_matmul_quant_batched(Yd, raw, Xd, 1, 128, 256) == hb.HOLO_E_ARG
+    dev.lib.cuda_clear_status()
+    for p in (Wd, Xd, Yd, raw):
+        dev.free(p)
