@@ -269,6 +269,7 @@ def run_ours(args, rank, world, local_rank):
     decode = None
     if not args.no_decode:
         decode = decode_bench(args, world, rank, torch)
+    prefill = prefill_bench(dev, torch) if rank == 0 and not args.no_prefill else None
 
     traffic = read_traffic()
     line = {
@@ -293,6 +294,8 @@ def run_ours(args, rank, world, local_rank):
     }
     if decode:
         line["decode"] = decode
+    if prefill:
+        line["prefill"] = prefill
     if ref_gpu:
         line["reference_gpu_kernels"] = ref_gpu
     if cpu:
@@ -396,18 +399,32 @@ def decode_bytes_per_token(cfg, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW, kv_byt
     return weights + kv, weights
 
 
+# decode workloads: BASELINE configs[3] (7B, Q4_K) and configs[4] (70B, Q4_0,
+# batch 1): model, prompt tokens, new tokens, timed runs
+DECODE_MODELS = {
+    "7b": ("LLAMA2_7B", 128, 256, 3,
+           "Llama-2-7B shape, Q4_K layers, Q8_0 lm_head, fp16 embeddings and KV cache, ctx 2048"),
+    "70b": ("LLAMA3_70B", 512, 128, 1,
+            "Llama-3-70B shape (GQA 64/8), Q4_0 layers and lm_head, fp16 embeddings and KV cache, ctx 4096, batch 1"),
+}
+
+
 def decode_bench(args, world, rank, torch):
-    """Full C4 generation (128-token prompt, 256 new tokens at T 0.8 / top-k 40
-    / top-p 0.95 / repeat penalty 1.1, fp16 KV cache) on a random-init
-    Llama-2-7B-shape model built on the device.  tok/s from the device time of
-    the decode phase; e2e from the wall time of the public holo_model_generate
-    call (prompt in, tokens out, prefill included).  With N ranks the model is
-    row-sharded over the N GPUs (strong scaling: one model, one token stream);
-    times are the maximum over the ranks."""
-    from holo_b200.model import LLAMA2_7B, SamplerDesc, connect_peers, synthetic_model
-    cfg = dict(LLAMA2_7B)
+    """Full generation on a random-init model built on the device (T 0.8 /
+    top-k 40 / top-p 0.95 / repeat penalty 1.1, fp16 KV cache): the 7B
+    configuration (128-token prompt, 256 new tokens, median of 3 runs) or
+    with --decode-model 70b the 70B one (512-token prompt, 128 new tokens).
+    tok/s from the device time of the decode phase; e2e from the wall time of
+    the public holo_model_generate call (prompt in, tokens out, prefill
+    included).  With N ranks the model is row-sharded over the N GPUs (strong
+    scaling: one model, one token stream); times are the maximum over the
+    ranks."""
+    from holo_b200 import model as hm
+    from holo_b200.model import SamplerDesc, connect_peers, synthetic_model
+    cfg_name, n_prompt, n_new, runs_n, desc = DECODE_MODELS[args.decode_model]
+    cfg = dict(getattr(hm, cfg_name))
     act = hb.ACT_Q8 if args.act == "q8" else hb.ACT_F32
-    want_cpu = rank == 0 and world == 1 and not args.no_cpu
+    want_cpu = rank == 0 and world == 1 and not args.no_cpu and args.decode_model == "7b"
     t0 = time.perf_counter()
     built = synthetic_model(cfg, seed=0, act_mode=act, kv_f16=True, keep_host=want_cpu, world=world, rank=rank)
     m, host = built if want_cpu else (built, None)
@@ -422,14 +439,14 @@ def decode_bench(args, world, rank, torch):
         t = torch.tensor(vals, device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return tuple(float(v) for v in t.tolist())
-    prompt = np.random.default_rng(0).integers(0, cfg["vocab"], size=DECODE_PROMPT).astype(np.int32)
+    prompt = np.random.default_rng(0).integers(0, cfg["vocab"], size=n_prompt).astype(np.int32)
     s = SamplerDesc(0.8, 0.95, 40, 1.1, 64)
-    m.generate(prompt, DECODE_NEW, s, seed=0)            # warm-up (graph capture, caches)
+    m.generate(prompt, n_new, s, seed=0)            # warm-up (caches, clocks)
     runs = []
-    for i in range(3):
+    for i in range(runs_n):
         torch.cuda.synchronize()
         w0 = time.perf_counter()
-        toks = m.generate(prompt, DECODE_NEW, s, seed=i)
+        toks = m.generate(prompt, n_new, s, seed=i)
         wall = time.perf_counter() - w0
         pre_ms, dec_ms = m.last_timing()
         dec_ms, pre_ms, wall = max_over_ranks(dec_ms, pre_ms, wall)
@@ -437,25 +454,25 @@ def decode_bench(args, world, rank, torch):
     first_tokens = runs[0][3]      # seed 0
     runs.sort(key=lambda r: r[0])
     dec_ms, pre_ms, wall, toks = runs[len(runs) // 2]
-    tok_s = DECODE_NEW / (dec_ms * 1e-3)
-    bpt, wbytes = decode_bytes_per_token(cfg)
+    tok_s = n_new / (dec_ms * 1e-3)
+    bpt, wbytes = decode_bytes_per_token(cfg, n_prompt, n_new)
     peak, peak_kind = peaks()
     peak *= world                 # the shards stream from every GPU's HBM at once
     step_kernel = cfg["head_dim"] == 128 and os.environ.get("HOLO_STEP") != "graph"
     out = {
-        "config": "Llama-2-7B shape, Q4_K layers, Q8_0 lm_head, fp16 embeddings and KV cache, ctx 2048; "
-                  f"prompt {DECODE_PROMPT}, {DECODE_NEW} new tokens, T 0.8 / top-k 40 / top-p 0.95 / rep 1.1"
+        "config": f"{desc}; prompt {n_prompt}, {n_new} new tokens, T 0.8 / top-k 40 / top-p 0.95 / rep 1.1"
                   + (f"; row-sharded over {world} GPUs" if world > 1 else ""),
-        "scaling": "strong", "n_gpus": world,
-        "act_mode": args.act, "value": round(tok_s, 1), "unit": "tokens/s", "ms_per_token": round(dec_ms / DECODE_NEW, 4),
-        "prefill_ms": round(pre_ms, 2), "prefill_tokens_s": round((DECODE_PROMPT - 1) / (pre_ms * 1e-3), 1),
+        "model": args.decode_model, "scaling": "strong", "n_gpus": world,
+        "act_mode": args.act, "value": round(tok_s, 1), "unit": "tokens/s", "ms_per_token": round(dec_ms / n_new, 4),
+        "prefill_ms": round(pre_ms, 2), "prefill_tokens_s": round((n_prompt - 1) / (pre_ms * 1e-3), 1),
         "roofline": {"bound": "hbm", "bytes_per_token": int(bpt), "weight_bytes_per_token": int(wbytes),
                      "achieved": round(bpt * tok_s / 1e9, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(bpt * tok_s / 1e9 / peak, 4), "peak_source": peak_kind},
-        "e2e": {"value": round(DECODE_NEW / wall, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * DECODE_PROMPT,
-                "d2h_bytes_per_step": 4 * DECODE_NEW,
+        "e2e": {"value": round(n_new / wall, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * n_prompt,
+                "d2h_bytes_per_step": 4 * n_new,
                 "path": "holo_model_generate: prompt ids in, generated ids out, prefill included"},
         "gpu_launches_per_token": 2 if step_kernel else cfg["n_layers"] * 7 + 4,
+        "runs": runs_n,
         "model_build_s": round(build_s, 1),
         "tokens_head_seed0": [int(t) for t in first_tokens[:8]],
     }
@@ -463,6 +480,58 @@ def decode_bench(args, world, rank, torch):
         out["cpu_baseline"] = decode_cpu_baseline(cfg, host, prompt, budget_s=args.cpu_budget)
     m.close()
     return out
+
+
+PREFILL_SHAPES = [(14336, 4096), (4096, 14336)]
+PREFILL_M = [64, 256, 512]
+
+
+def prefill_bench(dev, torch, iters=20):
+    """C3: batched Q4_K matmul (cuda_matmul_quant_batched, tcgen05) for the
+    prefill shapes and token counts; device time per call from CUDA events on
+    the library stream over `iters` calls after 3 warm-up calls, inputs
+    resident.  Roofline: dense tensor FLOPs against the measured bf16 peak
+    (the kernel multiplies fp16 operands, same peak), and the weight bytes
+    against HBM."""
+    lib = dev.lib
+    stream = torch.cuda.ExternalStream(lib.cuda_get_stream())
+    peak_tf = None
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        peak_tf = float(json.loads(p.read_text())["bf16_tflops"])
+    hbm, _ = peaks()
+    out = []
+    for n, k in PREFILL_SHAPES:
+        W = synth.quant_matrix(hb.Q4_K, n, k, 0)
+        Wd = dev.upload_quant(W, hb.Q4_K, n, k)
+        for m in PREFILL_M:
+            X = synth.activation(m * k, 0)
+            Xd, Yd = dev.upload(X), dev.alloc(4 * m * n)
+            for _ in range(3):
+                lib.cuda_matmul_quant_batched(Yd, Wd, Xd, m, n, k)
+            dev.check("prefill warm-up")
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(iters):
+                lib.cuda_matmul_quant_batched(Yd, Wd, Xd, m, n, k)
+            e1.record(stream)
+            e1.synchronize()
+            dev.check("prefill")
+            us = e0.elapsed_time(e1) * 1e3 / iters
+            flops = 2.0 * m * n * k
+            tf = flops / (us * 1e-6) / 1e12
+            wbytes = n * hb.row_bytes(hb.Q4_K, k)
+            out.append({"N": n, "K": k, "M": m, "us": round(us, 2), "tflops": round(tf, 1),
+                        "tensor_frac": round(tf / peak_tf, 4) if peak_tf else None,
+                        "weight_gbs": round(wbytes / (us * 1e-6) / 1e9, 1),
+                        "hbm_frac": round(wbytes / (us * 1e-6) / 1e9 / hbm, 4)})
+            dev.free(Xd)
+            dev.free(Yd)
+        dev.free(Wd)
+    return {"kernel": "cuda_matmul_quant_batched (tcgen05.mma kind::f16, fp32 accumulators in TMEM)",
+            "peak_tflops": peak_tf, "peak_source": "measured bf16 (burst)", "cases": out,
+            "timing": f"CUDA events on the library stream, {iters} calls after 3 warm-up, includes the "
+                      "activation quantize/tile kernel and any K-split reduction"}
 
 
 def decode_cpu_baseline(cfg, host, prompt, budget_s):
@@ -598,8 +667,12 @@ def main():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the 7B decode sub-benchmark")
     ap.add_argument("--profile-decode", action="store_true", help="small 7B decode case for ncu")
-    ap.add_argument("--decode-only", action="store_true", help="only the 7B decode sub-benchmark")
+    ap.add_argument("--decode-only", action="store_true", help="only the decode sub-benchmark")
+    ap.add_argument("--decode-model", choices=["7b", "70b"], default="7b", help="decode sub-benchmark model")
     ap.add_argument("--layers", type=int, default=0, help="--profile-decode: first N layers only")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the tcgen05 prefill sub-benchmark")
+    ap.add_argument("--prefill-only", action="store_true", help="only the prefill sub-benchmark")
+    ap.add_argument("--profile-prefill", default=None, help="e.g. 512:14336x4096 (ncu case: M:NxK)")
     ap.add_argument("--profile-case", default=None, help="e.g. q4_k:11008x4096 (ncu small case)")
     ap.add_argument("--iters", type=int, default=4)
     args = ap.parse_args()
@@ -608,6 +681,20 @@ def main():
         return
     if args.profile_case:
         run_profile_case(args)
+        return
+    if args.profile_prefill:
+        import torch
+        m, nk = args.profile_prefill.split(":")
+        n, k = (int(v) for v in nk.split("x"))
+        m = int(m)
+        dev = hb.Device(0, 1)
+        Wd = dev.upload_quant(synth.quant_matrix(hb.Q4_K, n, k, 0), hb.Q4_K, n, k)
+        Xd, Yd = dev.upload(synth.activation(m * k, 0)), dev.alloc(4 * m * n)
+        for _ in range(args.iters):
+            dev.lib.cuda_matmul_quant_batched(Yd, Wd, Xd, m, n, k)
+        dev.check("profile prefill")
+        print(json.dumps({"profile_prefill": args.profile_prefill, "iters": args.iters,
+                          "flops_per_call": 2 * m * n * k}))
         return
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -625,7 +712,13 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.decode_only:
+        if args.prefill_only:
+            import torch
+            torch.cuda.set_device(local_rank)
+            d = prefill_bench(hb.Device(local_rank, world), torch)
+            if rank == 0:
+                print(json.dumps({"prefill": d}), flush=True)
+        elif args.decode_only:
             import torch
             torch.cuda.set_device(local_rank)
             hb.Device(local_rank, world)

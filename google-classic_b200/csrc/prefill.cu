@@ -11,11 +11,13 @@
 //     matvec does (d = amax/127, q = rint(x/d)), then the dequantized value
 //     d*q rounded to fp16, written pre-swizzled in the tensor core's 128-byte
 //     K-major layout (pf_act_kernel) so one 1-D bulk copy stages a tile;
-//   * weights: 8 warps dequantize Q4_K (quant.c: y = (d*sc)*q - dmin*m in
-//     fp32, then fp16) straight into the same swizzled layout in shared memory;
+//   * weights: 16 warps dequantize Q4_K (quant.c: y = (d*sc)*q - dmin*m, here
+//     with d*sc and dmin*m rounded to fp16 and one fp16 fma per pair of
+//     values) straight into the same swizzled layout in shared memory;
+//   * one warp bulk-copies the activation tiles, another the raw weights;
 //   * one thread issues tcgen05.mma.kind::f16 (fp32 accumulation in TMEM,
 //     128 weight rows x TN tokens per CTA), tcgen05.commit frees each stage;
-//   * the 8 warps read the accumulators back with tcgen05.ld.
+//   * the 16 warps read the accumulators back with tcgen05.ld.
 // A CTA owns 128 weight rows, TN <= 256 tokens and a range of K; several K
 // ranges (few weight tiles, e.g. 4096 x 14336) are summed by pf_reduce_kernel
 // in a fixed order.  Every wait is bounded (HOLO_E_TIMEOUT).
@@ -29,16 +31,32 @@ namespace {
 using namespace holo_mv;
 
 constexpr int PF_BM = 128;                         // weight rows per CTA (MMA M)
-constexpr int PF_BK = 64;                          // K per stage: one 128-byte atom of fp16
-constexpr int PF_STAGES = 4;
-constexpr int PF_DQ_WARPS = 8;                     // dequantize, then read the accumulators
-constexpr int PF_THREADS = (PF_DQ_WARPS + 2) * 32; // + bulk-copy warp + MMA warp
-constexpr int PF_A_BYTES = PF_BM * 128;            // one stage of weights: 16 KB
+constexpr int PF_BK = 128;                         // K per stage: two 128-byte atoms of fp16
+constexpr int PF_MAX_AST = 3;                      // dequantized weight stages, at most
+constexpr int PF_DQ_WARPS = 16;                    // dequantize, then read the accumulators
+constexpr int PF_B_WARP = PF_DQ_WARPS, PF_RAW_WARP = PF_DQ_WARPS + 1, PF_MMA_WARP = PF_DQ_WARPS + 2;
+constexpr int PF_THREADS = (PF_DQ_WARPS + 3) * 32; // + activation copies + weight copies + MMA
+constexpr int PF_A_BYTES = PF_BM * 256;            // one stage of weights: 32 KB (two atom columns)
+constexpr int PF_RAW_BYTES = 4 * 4608;             // raw Q4_K units of 128 rows x one super-block
+constexpr int PF_MAX_RAW = 2;
+constexpr int PF_MAX_BST = 4;
+
+// raw super-blocks staged ahead in shared memory, and activation-tile stages:
+// the activation tiles get their own, deeper ring (a tile is requested as soon
+// as its slot is free, so its copy latency is hidden behind several stages)
+__host__ __device__ constexpr int pf_raw_slots(int tn) { return tn == 64 ? PF_MAX_RAW : 1; }
+__host__ __device__ constexpr int pf_b_stages(int tn) { return tn == 64 ? 4 : tn == 128 ? 3 : 2; }
+// dequantized weight stages: the dequantizing warps run this many chunks
+// ahead of the MMAs that free them
+__host__ __device__ constexpr int pf_a_stages(int tn) { return tn == 256 ? 2 : 3; }
 
 struct PfBars {
-    uint64_t full_a[PF_STAGES];   // 8 dequantizing warps arrived
-    uint64_t full_b[PF_STAGES];   // activation tile landed
-    uint64_t empty[PF_STAGES];    // the stage's MMAs completed
+    uint64_t full_a[PF_MAX_AST];  // the dequantizing warps arrived
+    uint64_t empty[PF_MAX_AST];   // the weight stage's MMAs completed
+    uint64_t full_b[PF_MAX_BST];  // activation tile landed
+    uint64_t empty_b[PF_MAX_BST]; // the activation stage's MMAs completed
+    uint64_t rfull[PF_MAX_RAW];   // raw super-block landed
+    uint64_t rempty[PF_MAX_RAW];  // the dequantizing warps have read the raw super-block
     uint64_t done;                // the last MMA completed
     uint32_t tmem;                // accumulator base (TMEM address)
 };
@@ -73,16 +91,13 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
                  :: "r"(smem_addr(bar)) : "memory");
 }
 
-// 32 consecutive fp32 columns of this warp's 32 TMEM lanes
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+// 16 consecutive fp32 columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
-          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -94,8 +109,9 @@ __host__ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
 }
 
 // ---- activations: Q8 per 32-block, dequantized to fp16, tiled + swizzled ---
-// xt tile (mt, kc) = rows [mt*tn, +tn) x columns [kc*64, +64), tn*128 bytes;
-// rows past M are zero.  One warp per (row, 32-block), lane = element.
+// xt tile (mt, kc) = rows [mt*tn, +tn) x columns [kc*128, +128), tn*256 bytes:
+// two atom columns of 64 values (tn*128 bytes each); rows past M are zero.
+// One warp per (row, 32-block), lane = element.
 __global__ void pf_act_kernel(__half *__restrict__ xt, const float *__restrict__ x, int M, int Mpad, int K,
                               int tn) {
     const int nb = K / 32;
@@ -112,9 +128,9 @@ __global__ void pf_act_kernel(__half *__restrict__ xt, const float *__restrict__
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     const float q = fminf(fmaxf(rintf(__fmul_rn(v, id)), -127.0f), 127.0f);
     const __half h = __float2half_rn(__fmul_rn(d, q));
-    const int k = b * 32 + lane, mt = m / tn, r = m % tn, kc = k / PF_BK;
-    uint8_t *tile = reinterpret_cast<uint8_t *>(xt) + ((size_t)mt * (K / PF_BK) + kc) * (size_t)tn * 128;
-    *reinterpret_cast<__half *>(tile + sw128_off(r, k % PF_BK)) = h;
+    const int k = b * 32 + lane, mt = m / tn, r = m % tn, kc = k / PF_BK, kk = k % PF_BK;
+    uint8_t *tile = reinterpret_cast<uint8_t *>(xt) + ((size_t)mt * (K / PF_BK) + kc) * (size_t)tn * 256;
+    *reinterpret_cast<__half *>(tile + (kk >> 6) * tn * 128 + sw128_off(r, kk & 63)) = h;
 }
 
 // ---- the matmul ----------------------------------------------------------------
@@ -126,9 +142,11 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
               int K, int units, int kc_per_split, int *status) {
     extern __shared__ uint8_t pf_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t *sa = smem;                                   // [stages][128 rows][128 B]
-    uint8_t *sb = smem + PF_STAGES * PF_A_BYTES;          // [stages][TN rows][128 B]
-    PfBars &B = *reinterpret_cast<PfBars *>(sb + PF_STAGES * TN * 128);
+    uint8_t *sa = smem;                                   // [stages][2 atom columns][128 rows][128 B]
+    constexpr int PF_STAGES = pf_a_stages(TN), SB = pf_b_stages(TN), R = pf_raw_slots(TN);
+    uint8_t *sb = smem + PF_STAGES * PF_A_BYTES;          // [SB][2 atom columns][TN rows][128 B]
+    uint8_t *sr = sb + SB * TN * 256;                     // [R][4 row-blocks][4608 B]
+    PfBars &B = *reinterpret_cast<PfBars *>(sr + R * PF_RAW_BYTES);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkc = K / PF_BK;
     const int n0 = blockIdx.x * PF_BM, mt = blockIdx.y, ks = blockIdx.z;
@@ -138,13 +156,20 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
     if (threadIdx.x == 0) {
         for (int s = 0; s < PF_STAGES; ++s) {
             mbar_init(&B.full_a[s], PF_DQ_WARPS);
-            mbar_init(&B.full_b[s], 1);
             mbar_init(&B.empty[s], 1);
+        }
+        for (int s = 0; s < PF_MAX_BST; ++s) {
+            mbar_init(&B.full_b[s], 1);
+            mbar_init(&B.empty_b[s], 1);
+        }
+        for (int k = 0; k < PF_MAX_RAW; ++k) {
+            mbar_init(&B.rfull[k], 1);
+            mbar_init(&B.rempty[k], PF_DQ_WARPS);
         }
         mbar_init(&B.done, 1);
         fence_barrier_init();
     }
-    if (warp == PF_DQ_WARPS + 1) {
+    if (warp == PF_MMA_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      :: "r"(smem_addr(&B.tmem)), "r"((uint32_t)TN) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -155,105 +180,145 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
     const uint32_t tmem = B.tmem;
 
     if (warp < PF_DQ_WARPS) {
-        // thread -> weight row r, sub-block half of each 64-value chunk
-        const int t = threadIdx.x, r = t & (PF_BM - 1), half = t >> 7, lr = r & 31;
-        const uint8_t *wrb = W + (size_t)((n0 + r) >> 5) * units * 4608;
+        // thread -> weight row r and sub-block q of the 4 a 128-value chunk
+        // holds (all 32 positions); chunk c2 of a super-block holds its
+        // sub-blocks 4 c2 .. 4 c2 + 3.  The raw super-blocks arrive in shared
+        // memory R ahead (bulk copies).
+        const int t = threadIdx.x, r = t & (PF_BM - 1), q = t >> 7, lr = r & 31;
+        const int nsb = nch >> 1;   // K ranges are whole super-blocks
+        const __half2 k1024 = __float2half2_rn(1024.0f);
         bool ok = true;
-        for (int i = 0; i < nch && ok; ++i) {
-            const int c = kc0 + i, s = i % PF_STAGES;
-            const int sbk = c >> 2, j = 2 * (c & 3) + half;   // super-block, sub-block
-            const uint8_t *unit = wrb + (size_t)sbk * 4608;
-            const uint4 h = ldg_stream(unit + lr * 16);
-            const uint4 q = ldg_stream(unit + unit_plane_off<GT_Q4_K>(j, lr));
-            if (i >= PF_STAGES)
-                ok = mbar_wait_bounded(&B.empty[s], ((i / PF_STAGES) + 1) & 1, status, HOLO_E_TIMEOUT);
+        for (int b = 0; b < nsb && ok; ++b) {
+            const int rs = b % R;
+            ok = mbar_wait_bounded(&B.rfull[rs], (b / R) & 1, status, HOLO_E_TIMEOUT);
             if (!__all_sync(0xffffffffu, ok)) break;
+            const uint8_t *unit = sr + rs * PF_RAW_BYTES + (r >> 5) * 4608;
+            const uint4 h = lds128(unit + lr * 16);
+            const uint4 qv0 = lds128(unit + unit_plane_off<GT_Q4_K>(q, lr));
+            const uint4 qv1 = lds128(unit + unit_plane_off<GT_Q4_K>(4 + q, lr));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.rempty[rs]);   // the copy of super-block b + R may land
             // quant.c:290-297 scale/min unpack (the unit layout keeps the raw bytes)
             const float d = half_bits_to_float(h.x & 0xffffu), dmin = half_bits_to_float(h.x >> 16);
-            const uint32_t scw = j < 4 ? (h.y & 0x3F3F3F3Fu) : (((h.w & LO4) << 2) | ((h.y >> 6) & 0x03030303u));
-            const uint32_t mw = j < 4 ? (h.z & 0x3F3F3F3Fu)
-                                      : ((((h.w >> 4) & LO4) << 2) | ((h.z >> 6) & 0x03030303u));
-            const float scv = __fmul_rn(d, ubyte_to_float(scw, j & 3));
-            const float mv = __fmul_rn(dmin, ubyte_to_float(mw, j & 3));
-            uint8_t *arow = sa + s * PF_A_BYTES;
-            // 16-byte chunk cc of this half: positions 8cc..8cc+7 of the
-            // sub-block = low nibbles (cc 0, 1) or high nibbles (cc 2, 3) of
-            // bytes 8(cc&1)..8(cc&1)+7
+            const uint32_t sc_lo = h.y & 0x3F3F3F3Fu, m_lo = h.z & 0x3F3F3F3Fu;
+            const uint32_t sc_hi = ((h.w & LO4) << 2) | ((h.y >> 6) & 0x03030303u);
+            const uint32_t m_hi = (((h.w >> 4) & LO4) << 2) | ((h.z >> 6) & 0x03030303u);
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                const uint32_t w0 = (cc & 1) ? q.z : q.x, w1 = (cc & 1) ? q.w : q.y;
-                const uint32_t n0w = (cc & 2) ? ((w0 >> 4) & LO4) : (w0 & LO4);
-                const uint32_t n1w = (cc & 2) ? ((w1 >> 4) & LO4) : (w1 & LO4);
-                uint32_t packed[4];
+            for (int c2 = 0; c2 < 2; ++c2) {
+                const int i = 2 * b + c2, s = i % PF_STAGES;
+                // packed fp16: q = (0x6400 | nibble) - 1024 exactly, then
+                // sc*q - m in one fma (sc, m rounded to fp16 first)
+                const float scv = __fmul_rn(d, ubyte_to_float(c2 ? sc_hi : sc_lo, q));
+                const float mv = __fmul_rn(dmin, ubyte_to_float(c2 ? m_hi : m_lo, q));
+                const __half2 sc2 = __float2half2_rn(scv), nm2 = __float2half2_rn(-mv);
+                const uint4 qw = c2 ? qv1 : qv0;
+                // positions 8 cc .. 8 cc + 7 of the sub-block: low nibbles
+                // (cc 0, 1) or high nibbles (cc 2, 3) of bytes 8 (cc & 1) ..;
+                // a pair of positions = bytes (2e, 2e+1) of a word, moved to the
+                // two halves by a permute
+                uint4 outv[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const uint32_t wv = e < 2 ? n0w : n1w;
-                    const float v0 = __fsub_rn(__fmul_rn(scv, ubyte_to_float(wv, (e & 1) * 2)), mv);
-                    const float v1 = __fsub_rn(__fmul_rn(scv, ubyte_to_float(wv, (e & 1) * 2 + 1)), mv);
-                    const __half2 hv = __floats2half2_rn(v0, v1);
-                    packed[e] = *reinterpret_cast<const uint32_t *>(&hv);
+                for (int cc = 0; cc < 4; ++cc) {
+                    const uint32_t w0 = (cc & 1) ? qw.z : qw.x, w1 = (cc & 1) ? qw.w : qw.y;
+                    uint32_t packed[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        uint32_t tt = __byte_perm(e < 2 ? w0 : w1, 0u, (e & 1) ? 0x4342u : 0x4140u);
+                        if (cc & 2) tt >>= 4;
+                        const uint32_t hb = (tt & 0x000F000Fu) | 0x64006400u;
+                        const __half2 qh = __hsub2(*reinterpret_cast<const __half2 *>(&hb), k1024);
+                        const __half2 hv = __hfma2(qh, sc2, nm2);
+                        packed[e] = *reinterpret_cast<const uint32_t *>(&hv);
+                    }
+                    outv[cc] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
                 }
-                *reinterpret_cast<uint4 *>(arow + sw128_off(r, 32 * half + 8 * cc)) =
-                    make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                if (i >= PF_STAGES)
+                    ok = mbar_wait_bounded(&B.empty[s], ((i / PF_STAGES) + 1) & 1, status, HOLO_E_TIMEOUT);
+                if (!__all_sync(0xffffffffu, ok)) break;
+                // column 32 q + position of the chunk: atom column q / 2
+                uint8_t *acol = sa + s * PF_A_BYTES + (q >> 1) * (PF_BM * 128);
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc)
+                    *reinterpret_cast<uint4 *>(acol + sw128_off(r, 32 * (q & 1) + 8 * cc)) = outv[cc];
+                fence_proxy_async_smem();   // the tensor core reads these through the async proxy
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&B.full_a[s]);
             }
-            fence_proxy_async_smem();   // the tensor core reads these through the async proxy
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&B.full_a[s]);
         }
-        // accumulators -> out: warp w reads TMEM lanes 32(w%4).., columns of its half
+        // accumulators -> out: warp w reads TMEM lanes 32 (w % 4).., a
+        // quarter of the columns
         ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(&B.done, 0, status, HOLO_E_TIMEOUT));
         tc_fence_after();
         if (ok) {
-            const int quarter = warp & 3, colh = warp >> 2;
+            const int quarter = warp & 3, colq = warp >> 2;
             const int row = n0 + 32 * quarter + lane;
             float *o = out + (size_t)ks * M * N;
-            for (int cb = colh * (TN / 2); cb < (colh + 1) * (TN / 2); cb += 32) {
-                uint32_t v[32];
-                tc_ld32(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)cb, v);
+            for (int cb = colq * (TN / 4); cb < (colq + 1) * (TN / 4); cb += 16) {
+                uint32_t v[16];
+                tc_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)cb, v);
 #pragma unroll
-                for (int jj = 0; jj < 32; ++jj) {
+                for (int jj = 0; jj < 16; ++jj) {
                     const int m = mt * TN + cb + jj;
                     if (m < M) o[(size_t)m * N + row] = __uint_as_float(v[jj]);
                 }
             }
         }
-    } else if (warp == PF_DQ_WARPS) {
-        // activation tiles, one bulk copy a stage
+    } else if (warp == PF_B_WARP) {
+        // activation tiles, one bulk copy a stage, SB stages ahead
         if (lane == 0) {
-            const uint8_t *xb = xt + ((size_t)mt * (K / PF_BK)) * (size_t)TN * 128;
+            const uint8_t *xb = xt + ((size_t)mt * (K / PF_BK)) * (size_t)TN * 256;
             int issued = 0;
             for (int i = 0; i < nch; ++i) {
-                const int s = i % PF_STAGES;
-                if (i >= PF_STAGES &&
-                    !mbar_wait_bounded(&B.empty[s], ((i / PF_STAGES) + 1) & 1, status, HOLO_E_TIMEOUT))
+                const int s = i % SB;
+                if (i >= SB && !mbar_wait_bounded(&B.empty_b[s], ((i / SB) + 1) & 1, status, HOLO_E_TIMEOUT))
                     break;
-                mbar_arrive_expect_tx(&B.full_b[s], (uint32_t)(TN * 128));
-                bulk_copy_g2s(sb + (size_t)s * TN * 128, xb + (size_t)(kc0 + i) * TN * 128, (uint32_t)(TN * 128),
+                mbar_arrive_expect_tx(&B.full_b[s], (uint32_t)(TN * 256));
+                bulk_copy_g2s(sb + (size_t)s * TN * 256, xb + (size_t)(kc0 + i) * TN * 256, (uint32_t)(TN * 256),
                               &B.full_b[s]);
                 issued = i + 1;
             }
             // every copy has landed before the CTA ends (the MMA thread may
             // have stopped consuming on a time-out)
-            for (int i = max(0, issued - PF_STAGES); i < issued; ++i)
-                mbar_wait_bounded(&B.full_b[i % PF_STAGES], (i / PF_STAGES) & 1, nullptr, 0);
+            for (int i = max(0, issued - SB); i < issued; ++i)
+                mbar_wait_bounded(&B.full_b[i % SB], (i / SB) & 1, nullptr, 0);
+        }
+    } else if (warp == PF_RAW_WARP) {
+        // raw weight super-blocks, R ahead of the dequantizing warps
+        if (lane == 0) {
+            const int nsb = nch >> 1, sb0 = kc0 >> 1;
+            const uint8_t *wrb = W + (size_t)(n0 >> 5) * units * 4608;   // the CTA's first row-block
+            int issued = 0;
+            for (int b = 0; b < nsb; ++b) {
+                const int rs = b % R;
+                if (b >= R && !mbar_wait_bounded(&B.rempty[rs], ((b / R) + 1) & 1, status, HOLO_E_TIMEOUT)) break;
+                mbar_arrive_expect_tx(&B.rfull[rs], (uint32_t)PF_RAW_BYTES);
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    bulk_copy_g2s(sr + rs * PF_RAW_BYTES + q * 4608, wrb + ((size_t)q * units + sb0 + b) * 4608,
+                                  4608u, &B.rfull[rs]);
+                issued = b + 1;
+            }
+            for (int b = max(0, issued - R); b < issued; ++b)
+                mbar_wait_bounded(&B.rfull[b % R], (b / R) & 1, nullptr, 0);
         }
     } else {
-        // MMA issue: 4 K-steps of 16 a stage
+        // MMA issue: 8 K-steps of 16 a stage (4 in each atom column)
         if (lane == 0) {
             constexpr uint32_t idesc = pf_idesc(TN);
             bool ok = true;
             for (int i = 0; i < nch && ok; ++i) {
-                const int s = i % PF_STAGES;
-                const uint32_t par = (i / PF_STAGES) & 1;
-                ok = mbar_wait_bounded(&B.full_a[s], par, status, HOLO_E_TIMEOUT) &&
-                     mbar_wait_bounded(&B.full_b[s], par, status, HOLO_E_TIMEOUT);
+                const int s = i % PF_STAGES, t = i % SB;
+                ok = mbar_wait_bounded(&B.full_a[s], (i / PF_STAGES) & 1, status, HOLO_E_TIMEOUT) &&
+                     mbar_wait_bounded(&B.full_b[t], (i / SB) & 1, status, HOLO_E_TIMEOUT);
                 if (!ok) break;
                 tc_fence_after();
-                const uint8_t *a = sa + s * PF_A_BYTES, *b = sb + (size_t)s * TN * 128;
+                const uint8_t *a = sa + s * PF_A_BYTES, *b = sb + (size_t)t * TN * 256;
 #pragma unroll
                 for (int kk = 0; kk < PF_BK / 16; ++kk)
-                    tc_mma(tmem, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), idesc, (i | kk) != 0);
+                    tc_mma(tmem, sw128_desc(a + (kk >> 2) * (PF_BM * 128) + (kk & 3) * 32),
+                           sw128_desc(b + (kk >> 2) * (TN * 128) + (kk & 3) * 32), idesc, (i | kk) != 0);
                 tc_commit(&B.empty[s]);
+                tc_commit(&B.empty_b[t]);
             }
             // completes once every MMA issued above has (or at once if none was)
             tc_commit(&B.done);
@@ -262,7 +327,7 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == PF_DQ_WARPS + 1) {
+    if (warp == PF_MMA_WARP) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"((uint32_t)TN)
                      : "memory");
@@ -278,15 +343,24 @@ __global__ void pf_reduce_kernel(float *__restrict__ y, const float *__restrict_
     }
 }
 
-size_t pf_smem(int tn) { return 1024 + (size_t)PF_STAGES * (PF_A_BYTES + tn * 128) + sizeof(PfBars); }
+size_t pf_smem(int tn) {
+    return 1024 + (size_t)pf_a_stages(tn) * PF_A_BYTES + (size_t)pf_b_stages(tn) * tn * 256 +
+           (size_t)pf_raw_slots(tn) * PF_RAW_BYTES +
+           sizeof(PfBars);
+}
 
 template <int TN>
 bool launch_mma(float *out, const uint8_t *W, const uint8_t *xt, int M, int N, int K, int units, int splits,
                 int kc_per_split, int mtiles, int *status, cudaStream_t st) {
     const size_t smem = pf_smem(TN);
-    if (cudaFuncSetAttribute(pf_mma_kernel<TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-        return holo_check_launch("prefill: attributes");
+    static int configured = -1;   // the device the attribute was set for
+    const int dev = holo_dev() ? holo_dev()->id : -1;
+    if (configured != dev) {
+        if (cudaFuncSetAttribute(pf_mma_kernel<TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return holo_check_launch("prefill: attributes");
+        configured = dev;
+    }
     pf_mma_kernel<TN><<<dim3(N / PF_BM, mtiles, splits), PF_THREADS, smem, st>>>(out, W, xt, M, N, K, units,
                                                                                 kc_per_split, status);
     return holo_check_launch("prefill matmul");
@@ -314,8 +388,9 @@ extern "C" int cuda_matmul_quant_batched(float *Y, const void *W, const float *X
     const int nkc = K / PF_BK;
     // K splits so that the CTAs cover the SMs when the weight has few row tiles
     const int base = (N / PF_BM) * mtiles;
-    int splits = std::max(1, std::min(nkc / 8, D->sms / base));
-    const int kc_per_split = (nkc + splits - 1) / splits;
+    // (in whole super-blocks: 4 chunks of 64)
+    int splits = std::max(1, std::min(nkc / 4, D->sms / base));
+    const int kc_per_split = ((nkc + splits - 1) / splits + 1) & ~1;
     splits = (nkc + kc_per_split - 1) / kc_per_split;   // every split non-empty
     const size_t xt_bytes = (size_t)Mpad * K * 2;
     const size_t part_bytes = splits > 1 ? (size_t)splits * M * N * 4 : 0;
