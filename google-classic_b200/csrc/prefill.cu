@@ -305,6 +305,9 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
         // MMA issue: 8 K-steps of 16 a stage (4 in each atom column)
         if (lane == 0) {
             constexpr uint32_t idesc = pf_idesc(TN);
+            // descriptors of stage 0; a stage, atom column and K step move the
+            // start address (the low field, in 16-byte units) by constants
+            const uint64_t a0 = sw128_desc(sa), b0 = sw128_desc(sb);
             bool ok = true;
             for (int i = 0; i < nch && ok; ++i) {
                 const int s = i % PF_STAGES, t = i % SB;
@@ -312,11 +315,12 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
                      mbar_wait_bounded(&B.full_b[t], (i / SB) & 1, status, HOLO_E_TIMEOUT);
                 if (!ok) break;
                 tc_fence_after();
-                const uint8_t *a = sa + s * PF_A_BYTES, *b = sb + (size_t)t * TN * 256;
+                const uint64_t ad = a0 + (uint64_t)((s * PF_A_BYTES) >> 4);
+                const uint64_t bd = b0 + (uint64_t)((t * TN * 256) >> 4);
 #pragma unroll
                 for (int kk = 0; kk < PF_BK / 16; ++kk)
-                    tc_mma(tmem, sw128_desc(a + (kk >> 2) * (PF_BM * 128) + (kk & 3) * 32),
-                           sw128_desc(b + (kk >> 2) * (TN * 128) + (kk & 3) * 32), idesc, (i | kk) != 0);
+                    tc_mma(tmem, ad + (uint64_t)(((kk >> 2) * (PF_BM * 128) + (kk & 3) * 32) >> 4),
+                           bd + (uint64_t)(((kk >> 2) * (TN * 128) + (kk & 3) * 32) >> 4), idesc, (i | kk) != 0);
                 tc_commit(&B.empty[s]);
                 tc_commit(&B.empty_b[t]);
             }
