@@ -37,7 +37,7 @@ constexpr int PF_DQ_WARPS = 16;                    // dequantize, then read the 
 constexpr int PF_B_WARP = PF_DQ_WARPS, PF_RAW_WARP = PF_DQ_WARPS + 1, PF_MMA_WARP = PF_DQ_WARPS + 2;
 constexpr int PF_THREADS = (PF_DQ_WARPS + 3) * 32; // + activation copies + weight copies + MMA
 constexpr int PF_A_BYTES = PF_BM * 256;            // one stage of weights: 32 KB (two atom columns)
-constexpr int PF_RAW_BYTES = 4 * 4608;             // raw Q4_K units of 128 rows x one super-block
+constexpr int PF_RAW_BYTES = 4 * 4608;             // raw units of 128 rows (4 row-blocks), at most
 constexpr int PF_MAX_RAW = 2;
 constexpr int PF_MAX_BST = 4;
 
@@ -133,10 +133,86 @@ __global__ void pf_act_kernel(__half *__restrict__ xt, const float *__restrict__
     *reinterpret_cast<__half *>(tile + (kk >> 6) * tn * 128 + sw128_off(r, kk & 63)) = h;
 }
 
+// ---- weight dequantization (one thread: one row, 32 positions of a chunk) ---
+// The raw unit of the thread's row-block in shared memory -> the registers a
+// unit needs: the row's head and two 16-byte planes.
+template <int TYPE>
+__device__ __forceinline__ void dq_load(const uint8_t *unit, int lr, int q, uint4 &h, uint4 &p0, uint4 &p1) {
+    if constexpr (TYPE == GT_Q8_0) {
+        // one 128-value chunk a unit; block q = planes 2q (positions 0..15), 2q+1
+        const uint2 hh = *reinterpret_cast<const uint2 *>(unit + unit_head_off<GT_Q8_0>(lr));
+        h = make_uint4(hh.x, hh.y, 0u, 0u);
+        p0 = lds128(unit + unit_plane_off<GT_Q8_0>(2 * q, lr));
+        p1 = lds128(unit + unit_plane_off<GT_Q8_0>(2 * q + 1, lr));
+    } else {
+        // two chunks a unit; chunk c2 holds sub-blocks 4 c2 .. 4 c2 + 3
+        h = lds128(unit + unit_head_off<TYPE>(lr));
+        p0 = lds128(unit + unit_plane_off<TYPE>(q, lr));
+        p1 = lds128(unit + unit_plane_off<TYPE>(4 + q, lr));
+    }
+}
+
+// the 32 values (fp16, 4 x 16 bytes: positions 8 cc .. 8 cc + 7) of block
+// 4 c2 + q of the unit: Q4_K (d*sc)*q - dmin*m (quant.c:290-297 scale
+// unpack; sc, m rounded to fp16, one fp16 fma), Q4_0 d*(q - 8), Q8_0 d*q
+// (one rounding each).  Nibble pairs: bytes (2e, 2e+1) of a word moved to
+// the two halves by a permute, 0x6400 | n read as fp16 is 1024 + n.
+template <int TYPE>
+__device__ __forceinline__ void dq_block(const uint4 &h, const uint4 &p0, const uint4 &p1, int c2, int q,
+                                         uint4 (&outv)[4]) {
+    __half2 mul2, add2, off2;
+    uint4 qw = c2 ? p1 : p0;
+    if constexpr (TYPE == GT_Q4_K) {
+        const float d = half_bits_to_float(h.x & 0xffffu), dmin = half_bits_to_float(h.x >> 16);
+        const uint32_t scw = c2 ? (((h.w & LO4) << 2) | ((h.y >> 6) & 0x03030303u)) : (h.y & 0x3F3F3F3Fu);
+        const uint32_t mw = c2 ? ((((h.w >> 4) & LO4) << 2) | ((h.z >> 6) & 0x03030303u)) : (h.z & 0x3F3F3F3Fu);
+        mul2 = __float2half2_rn(__fmul_rn(d, ubyte_to_float(scw, q)));
+        add2 = __float2half2_rn(-__fmul_rn(dmin, ubyte_to_float(mw, q)));
+        off2 = __float2half2_rn(1024.0f);
+    } else if constexpr (TYPE == GT_Q4_0) {
+        mul2 = __float2half2_rn(head_half(h, 4 * c2 + q));   // an fp16 scale: exact
+        add2 = __float2half2_rn(0.0f);
+        off2 = __float2half2_rn(1032.0f);   // 1024 + the Q4_0 offset 8
+    } else {
+        mul2 = __float2half2_rn(head_half(h, q));   // an fp16 scale: exact
+        add2 = __float2half2_rn(0.0f);
+        off2 = __float2half2_rn(1152.0f);   // 1024 + 128: the sign bit is flipped below
+        (void)qw;
+    }
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+        uint32_t w0, w1;
+        if constexpr (TYPE == GT_Q8_0) {
+            const uint4 pl = (cc & 2) ? p1 : p0;   // positions 0..15 | 16..31
+            w0 = (cc & 1) ? pl.z : pl.x;
+            w1 = (cc & 1) ? pl.w : pl.y;
+        } else {
+            w0 = (cc & 1) ? qw.z : qw.x;
+            w1 = (cc & 1) ? qw.w : qw.y;
+        }
+        uint32_t packed[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            uint32_t tt = __byte_perm(e < 2 ? w0 : w1, 0u, (e & 1) ? 0x4342u : 0x4140u);
+            uint32_t hb;
+            if constexpr (TYPE == GT_Q8_0) {
+                hb = (tt ^ 0x00800080u) | 0x64006400u;   // int8 + 128 in the low byte of each half
+            } else {
+                if (cc & 2) tt >>= 4;
+                hb = (tt & 0x000F000Fu) | 0x64006400u;
+            }
+            const __half2 qh = __hsub2(*reinterpret_cast<const __half2 *>(&hb), off2);
+            const __half2 hv = TYPE == GT_Q4_K ? __hfma2(qh, mul2, add2) : __hmul2(qh, mul2);
+            packed[e] = *reinterpret_cast<const uint32_t *>(&hv);
+        }
+        outv[cc] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+}
+
 // ---- the matmul ----------------------------------------------------------------
-// out[ks][M][N] (ks = blockIdx.z, K chunks [kc0, kc1)); W tiled Q4_K with
-// `units` super-blocks a row.
-template <int TN>
+// out[ks][M][N] (ks = blockIdx.z, K chunks [kc0, kc1)); W tiled TYPE with
+// `units` units a row.
+template <int TYPE, int TN>
 __global__ void __launch_bounds__(PF_THREADS, 1)
 pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint8_t *__restrict__ xt, int M, int N,
               int K, int units, int kc_per_split, int *status) {
@@ -145,7 +221,8 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
     uint8_t *sa = smem;                                   // [stages][2 atom columns][128 rows][128 B]
     constexpr int PF_STAGES = pf_a_stages(TN), SB = pf_b_stages(TN), R = pf_raw_slots(TN);
     uint8_t *sb = smem + PF_STAGES * PF_A_BYTES;          // [SB][2 atom columns][TN rows][128 B]
-    uint8_t *sr = sb + SB * TN * 256;                     // [R][4 row-blocks][4608 B]
+    uint8_t *sr = sb + SB * TN * 256;                     // [R][4 row-blocks][UB]
+    constexpr int UB = UnitGeom<TYPE>::UNIT_BYTES, CPU = UnitGeom<TYPE>::VALS / PF_BK;   // chunks a unit
     PfBars &B = *reinterpret_cast<PfBars *>(sr + R * PF_RAW_BYTES);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkc = K / PF_BK;
@@ -180,58 +257,25 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
     const uint32_t tmem = B.tmem;
 
     if (warp < PF_DQ_WARPS) {
-        // thread -> weight row r and sub-block q of the 4 a 128-value chunk
-        // holds (all 32 positions); chunk c2 of a super-block holds its
-        // sub-blocks 4 c2 .. 4 c2 + 3.  The raw super-blocks arrive in shared
-        // memory R ahead (bulk copies).
+        // thread -> weight row r and block q of the 4 32-value blocks a
+        // 128-value chunk holds (all 32 positions).  The raw units arrive in
+        // shared memory R ahead (bulk copies).
         const int t = threadIdx.x, r = t & (PF_BM - 1), q = t >> 7, lr = r & 31;
-        const int nsb = nch >> 1;   // K ranges are whole super-blocks
-        const __half2 k1024 = __float2half2_rn(1024.0f);
+        const int nun = nch / CPU;   // K ranges are whole units
         bool ok = true;
-        for (int b = 0; b < nsb && ok; ++b) {
+        for (int b = 0; b < nun && ok; ++b) {
             const int rs = b % R;
             ok = mbar_wait_bounded(&B.rfull[rs], (b / R) & 1, status, HOLO_E_TIMEOUT);
             if (!__all_sync(0xffffffffu, ok)) break;
-            const uint8_t *unit = sr + rs * PF_RAW_BYTES + (r >> 5) * 4608;
-            const uint4 h = lds128(unit + lr * 16);
-            const uint4 qv0 = lds128(unit + unit_plane_off<GT_Q4_K>(q, lr));
-            const uint4 qv1 = lds128(unit + unit_plane_off<GT_Q4_K>(4 + q, lr));
+            uint4 h, p0, p1;
+            dq_load<TYPE>(sr + rs * PF_RAW_BYTES + (r >> 5) * UB, lr, q, h, p0, p1);
             __syncwarp();
-            if (lane == 0) mbar_arrive(&B.rempty[rs]);   // the copy of super-block b + R may land
-            // quant.c:290-297 scale/min unpack (the unit layout keeps the raw bytes)
-            const float d = half_bits_to_float(h.x & 0xffffu), dmin = half_bits_to_float(h.x >> 16);
-            const uint32_t sc_lo = h.y & 0x3F3F3F3Fu, m_lo = h.z & 0x3F3F3F3Fu;
-            const uint32_t sc_hi = ((h.w & LO4) << 2) | ((h.y >> 6) & 0x03030303u);
-            const uint32_t m_hi = (((h.w >> 4) & LO4) << 2) | ((h.z >> 6) & 0x03030303u);
+            if (lane == 0) mbar_arrive(&B.rempty[rs]);   // the copy of unit b + R may land
 #pragma unroll
-            for (int c2 = 0; c2 < 2; ++c2) {
-                const int i = 2 * b + c2, s = i % PF_STAGES;
-                // packed fp16: q = (0x6400 | nibble) - 1024 exactly, then
-                // sc*q - m in one fma (sc, m rounded to fp16 first)
-                const float scv = __fmul_rn(d, ubyte_to_float(c2 ? sc_hi : sc_lo, q));
-                const float mv = __fmul_rn(dmin, ubyte_to_float(c2 ? m_hi : m_lo, q));
-                const __half2 sc2 = __float2half2_rn(scv), nm2 = __float2half2_rn(-mv);
-                const uint4 qw = c2 ? qv1 : qv0;
-                // positions 8 cc .. 8 cc + 7 of the sub-block: low nibbles
-                // (cc 0, 1) or high nibbles (cc 2, 3) of bytes 8 (cc & 1) ..;
-                // a pair of positions = bytes (2e, 2e+1) of a word, moved to the
-                // two halves by a permute
+            for (int c2 = 0; c2 < CPU; ++c2) {
+                const int i = CPU * b + c2, s = i % PF_STAGES;
                 uint4 outv[4];
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
-                    const uint32_t w0 = (cc & 1) ? qw.z : qw.x, w1 = (cc & 1) ? qw.w : qw.y;
-                    uint32_t packed[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        uint32_t tt = __byte_perm(e < 2 ? w0 : w1, 0u, (e & 1) ? 0x4342u : 0x4140u);
-                        if (cc & 2) tt >>= 4;
-                        const uint32_t hb = (tt & 0x000F000Fu) | 0x64006400u;
-                        const __half2 qh = __hsub2(*reinterpret_cast<const __half2 *>(&hb), k1024);
-                        const __half2 hv = __hfma2(qh, sc2, nm2);
-                        packed[e] = *reinterpret_cast<const uint32_t *>(&hv);
-                    }
-                    outv[cc] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                }
+                dq_block<TYPE>(h, p0, p1, c2, q, outv);
                 if (i >= PF_STAGES)
                     ok = mbar_wait_bounded(&B.empty[s], ((i / PF_STAGES) + 1) & 1, status, HOLO_E_TIMEOUT);
                 if (!__all_sync(0xffffffffu, ok)) break;
@@ -283,19 +327,19 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
                 mbar_wait_bounded(&B.full_b[i % SB], (i / SB) & 1, nullptr, 0);
         }
     } else if (warp == PF_RAW_WARP) {
-        // raw weight super-blocks, R ahead of the dequantizing warps
+        // raw weight units (4 row-blocks each), R ahead of the dequantizing warps
         if (lane == 0) {
-            const int nsb = nch >> 1, sb0 = kc0 >> 1;
-            const uint8_t *wrb = W + (size_t)(n0 >> 5) * units * 4608;   // the CTA's first row-block
+            const int nun = nch / CPU, u0 = kc0 / CPU;
+            const uint8_t *wrb = W + (size_t)(n0 >> 5) * units * UB;   // the CTA's first row-block
             int issued = 0;
-            for (int b = 0; b < nsb; ++b) {
+            for (int b = 0; b < nun; ++b) {
                 const int rs = b % R;
                 if (b >= R && !mbar_wait_bounded(&B.rempty[rs], ((b / R) + 1) & 1, status, HOLO_E_TIMEOUT)) break;
-                mbar_arrive_expect_tx(&B.rfull[rs], (uint32_t)PF_RAW_BYTES);
+                mbar_arrive_expect_tx(&B.rfull[rs], (uint32_t)(4 * UB));
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                    bulk_copy_g2s(sr + rs * PF_RAW_BYTES + q * 4608, wrb + ((size_t)q * units + sb0 + b) * 4608,
-                                  4608u, &B.rfull[rs]);
+                    bulk_copy_g2s(sr + rs * PF_RAW_BYTES + q * UB, wrb + ((size_t)q * units + u0 + b) * UB,
+                                  (uint32_t)UB, &B.rfull[rs]);
                 issued = b + 1;
             }
             for (int b = max(0, issued - R); b < issued; ++b)
@@ -353,72 +397,86 @@ size_t pf_smem(int tn) {
            sizeof(PfBars);
 }
 
-template <int TN>
+template <int TYPE, int TN>
 bool launch_mma(float *out, const uint8_t *W, const uint8_t *xt, int M, int N, int K, int units, int splits,
                 int kc_per_split, int mtiles, int *status, cudaStream_t st) {
     const size_t smem = pf_smem(TN);
     static int configured = -1;   // the device the attribute was set for
     const int dev = holo_dev() ? holo_dev()->id : -1;
     if (configured != dev) {
-        if (cudaFuncSetAttribute(pf_mma_kernel<TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        if (cudaFuncSetAttribute(pf_mma_kernel<TYPE, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
             return holo_check_launch("prefill: attributes");
         configured = dev;
     }
-    pf_mma_kernel<TN><<<dim3(N / PF_BM, mtiles, splits), PF_THREADS, smem, st>>>(out, W, xt, M, N, K, units,
+    pf_mma_kernel<TYPE, TN><<<dim3(N / PF_BM, mtiles, splits), PF_THREADS, smem, st>>>(out, W, xt, M, N, K, units,
                                                                                 kc_per_split, status);
     return holo_check_launch("prefill matmul");
 }
 
 }  // namespace
 
-extern "C" int cuda_matmul_quant_batched(float *Y, const void *W, const float *X, int M, int N, int K) {
+// Y[M][N] = X[M][K] . W^T for a tiled weight described by wi, on stream st
+// (the ABI entry below and the batched decode engine)
+bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st) {
     HoloDevice *D = holo_dev();
-    if (!D) return cuda_last_status();
-    WeightInfo wi;
-    if (!Y || !W || !X || M <= 0 || !holo_registry_find(W, &wi) || wi.type != GT_Q4_K || wi.rows != N ||
-        wi.cols != K || N % PF_BM || K % 256) {
-        holo_set_status(HOLO_E_ARG, "cuda_matmul_quant_batched: needs a tiled Q4_K weight (cuda_upload_quant), "
-                                    "N % 128 == 0, K % 256 == 0");
-        return HOLO_E_ARG;
+    if (!D) return false;
+    const int N = wi.rows, K = wi.cols;
+    const int vals = wi.type == GT_Q8_0 ? 128 : 256;
+    if (!Y || !W || !X || M <= 0 || N % PF_BM || K % vals ||
+        (wi.type != GT_Q4_K && wi.type != GT_Q4_0 && wi.type != GT_Q8_0)) {
+        holo_set_status(HOLO_E_ARG, "batched matmul: needs a tiled Q8_0/Q4_0/Q4_K weight (cuda_upload_quant), "
+                                    "N % 128 == 0, K a whole number of blocks");
+        return false;
     }
-    if (wi.q4k_layout != HOLO_Q4K_REF && wi.q4k_layout != HOLO_Q4K_GGML) {
-        holo_set_status(HOLO_E_ARG, "cuda_matmul_quant_batched: unknown Q4_K layout");
-        return HOLO_E_ARG;
-    }
-    cudaStream_t st = holo_stream();
     const int tn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
     const int mtiles = (M + tn - 1) / tn, Mpad = mtiles * tn;
-    const int nkc = K / PF_BK;
-    // K splits so that the CTAs cover the SMs when the weight has few row tiles
+    const int nkc = K / PF_BK, cpu = vals / PF_BK;
+    // K splits (whole units) so that the CTAs cover the SMs when the weight
+    // has few row tiles
     const int base = (N / PF_BM) * mtiles;
-    // (in whole super-blocks: 4 chunks of 64)
     int splits = std::max(1, std::min(nkc / 4, D->sms / base));
-    const int kc_per_split = ((nkc + splits - 1) / splits + 1) & ~1;
+    const int kc_per_split = ((nkc + splits - 1) / splits + cpu - 1) / cpu * cpu;
     splits = (nkc + kc_per_split - 1) / kc_per_split;   // every split non-empty
     const size_t xt_bytes = (size_t)Mpad * K * 2;
     const size_t part_bytes = splits > 1 ? (size_t)splits * M * N * 4 : 0;
     uint8_t *tmp = static_cast<uint8_t *>(holo_tmp(xt_bytes + part_bytes + 256));
-    if (!tmp) return cuda_last_status();
+    if (!tmp) return false;
     uint8_t *xt = tmp;
     float *part = splits > 1 ? reinterpret_cast<float *>(tmp + ((xt_bytes + 255) & ~(size_t)255)) : Y;
     const long long warps = (long long)Mpad * (K / 32);
     pf_act_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(reinterpret_cast<__half *>(xt), X, M, Mpad,
                                                                        K, tn);
-    if (!holo_check_launch("prefill activations")) return cuda_last_status();
+    if (!holo_check_launch("batched matmul activations")) return false;
     const uint8_t *w = static_cast<const uint8_t *>(W);
     bool ok;
-    switch (tn) {
-    case 64: ok = launch_mma<64>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st); break;
-    case 128: ok = launch_mma<128>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st); break;
-    default: ok = launch_mma<256>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st); break;
+#define PF_LAUNCH(T)                                                                                              \
+    (tn == 64    ? launch_mma<T, 64>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st)  \
+     : tn == 128 ? launch_mma<T, 128>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st) \
+                 : launch_mma<T, 256>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st))
+    switch (wi.type) {
+    case GT_Q4_K: ok = PF_LAUNCH(GT_Q4_K); break;
+    case GT_Q4_0: ok = PF_LAUNCH(GT_Q4_0); break;
+    default: ok = PF_LAUNCH(GT_Q8_0); break;
     }
-    if (!ok) return cuda_last_status();
+#undef PF_LAUNCH
+    if (!ok) return false;
     if (splits > 1) {
         const long long mn = (long long)M * N;
         pf_reduce_kernel<<<(unsigned)std::min<long long>((mn + 255) / 256, 4 * D->sms), 256, 0, st>>>(Y, part, mn,
                                                                                                      splits);
-        if (!holo_check_launch("prefill reduce")) return cuda_last_status();
+        if (!holo_check_launch("batched matmul reduce")) return false;
     }
-    return HOLO_OK;
+    return true;
+}
+
+extern "C" int cuda_matmul_quant_batched(float *Y, const void *W, const float *X, int M, int N, int K) {
+    if (!holo_dev()) return cuda_last_status();
+    WeightInfo wi;
+    if (!W || !holo_registry_find(W, &wi) || wi.rows != N || wi.cols != K) {
+        holo_set_status(HOLO_E_ARG, "cuda_matmul_quant_batched: W is not a tiled weight of N x K "
+                                    "(cuda_upload_quant)");
+        return HOLO_E_ARG;
+    }
+    return holo_matmul_batched(Y, W, wi, X, M, holo_stream()) ? HOLO_OK : cuda_last_status();
 }

@@ -208,7 +208,8 @@ void holo_model_free(void *model);
 /* Batched quantized matmul for prompt processing (no counterpart in the
  * reference, whose prefill runs llm_forward one token at a time,
  * src/ai/llm.c:1049): Y[M][N] = X[M][K] . W^T on the tensor cores, W an N x K
- * Q4_K weight from cuda_upload_quant (N % 128 == 0, K % 256 == 0), X fp32.
+ * Q8_0, Q4_0 or Q4_K weight from cuda_upload_quant (N % 128 == 0, K a whole
+ * number of tiled units: 128 values for Q8_0, 256 for Q4_0/Q4_K), X fp32.
  * X is quantized to Q8 per 32-block as the matvecs do; the dequantized
  * activations and weights are rounded to fp16 and multiplied with fp32
  * accumulation.  Device pointers; HOLO_OK or an error status. */

@@ -1,9 +1,11 @@
 """Batched quantized matmul on the tensor cores (cuda_matmul_quant_batched,
 csrc/prefill.cu) against the oracle's Q8-activation restatement, one matvec
-per activation row (oracle/holo_oracle.c ho_matvec_q8act).
+per activation row (oracle/holo_oracle.c ho_matvec_q8act), for Q4_K, Q4_0
+and Q8_0 weights.
 
-Both operands reach the tensor core as fp16: the Q8 activation d*q and the
-Q4_K value (d*sc)*q - dmin*m, each rounded once (relative error <= 2^-11).
+Both operands reach the tensor core as fp16: the Q8 activation d*q rounded
+once, the weight value once (Q4_0 d*(q-8), Q8_0 d*q) or, for Q4_K, after
+its scale and min are rounded (one fp16 fma).
 The bar, fixed here: max |Y - R| / max |R| <= 1e-3 over the whole output
 (the north star's fp32 tolerance), R the restatement's fp32 result.
 """
@@ -17,8 +19,8 @@ from conftest import rel_err
 pytestmark = pytest.mark.gpu
 
 
-def run(dev, W, X, M, N, K):
-    Wd = dev.upload_quant(W, hb.Q4_K, N, K)
+def run(dev, W, X, M, N, K, gt=hb.Q4_K):
+    Wd = dev.upload_quant(W, gt, N, K)
     Xd = dev.upload(np.ascontiguousarray(X, np.float32))
     Yd = dev.alloc(4 * M * N)
     rc = dev.lib.cuda_matmul_quant_batched(Yd, Wd, Xd, M, N, K)
@@ -59,6 +61,19 @@ def test_prefill_shapes_rows_match(dev, oracle, N, K):
     R = np.stack([oracle.matvec_q8(hb.Q4_K, W, X[m], N, K, threads=8) for m in rows])
     err = rel_err(Y[rows], R)
     print(f"{N}x{K} M={M}: norm-wise rel err {err:.3e}")
+    assert err <= 1e-3
+
+
+@pytest.mark.parametrize("gt,M,N,K", [(hb.Q4_0, 64, 256, 512), (hb.Q4_0, 100, 384, 2048), (hb.Q4_0, 512, 128, 1024),
+                                      (hb.Q8_0, 64, 256, 512), (hb.Q8_0, 33, 128, 640), (hb.Q8_0, 300, 256, 1024),
+                                      (hb.Q8_0, 8, 512, 4096)])
+def test_other_types_match_q8_restatement(dev, oracle, gt, M, N, K):
+    W = synth.quant_matrix(gt, N, K, seed=M + K)
+    X = np.random.default_rng(M + 3 * K).standard_normal((M, K), dtype=np.float32)
+    Y = run(dev, W, X, M, N, K, gt)
+    R = np.stack([oracle.matvec_q8(gt, W, X[m], N, K) for m in range(M)])
+    err = rel_err(Y, R)
+    print(f"type {gt} M={M} N={N} K={K}: norm-wise rel err {err:.3e}")
     assert err <= 1e-3
 
 
