@@ -429,6 +429,8 @@ def decode_bench(args, world, rank, torch):
     ranks."""
     from holo_b200 import model as hm
     from holo_b200.model import SamplerDesc, connect_peers, synthetic_model
+    if args.decode_batch > 1:
+        return decode_batch_bench(args, world, rank, torch)
     cfg_name, n_prompt, n_new, runs_n, desc = DECODE_MODELS[args.decode_model]
     cfg = dict(getattr(hm, cfg_name))
     act = hb.ACT_Q8 if args.act == "q8" else hb.ACT_F32
@@ -540,6 +542,58 @@ def prefill_bench(dev, torch, iters=20):
             "peak_tflops": peak_tf, "peak_source": "measured bf16 (burst)", "cases": out,
             "timing": f"CUDA events on the library stream, {iters} calls after 3 warm-up, includes the "
                       "activation quantize/tile kernel and any K-split reduction"}
+
+
+def decode_batch_bench(args, world, rank, torch):
+    """Batched decode (BASELINE configs[4] batch 8 with --decode-model 70b):
+    args.decode_batch independent prompts decoded together on one GPU
+    (holo_model_generate_batch: each projection one tensor-core matmul with
+    M = batch).  Under torchrun every rank runs its own batch (data-parallel
+    replicas, weak scaling); value = all ranks' generated tokens / the slowest
+    rank's decode time."""
+    from holo_b200 import model as hm
+    from holo_b200.model import SamplerDesc, synthetic_model
+    cfg_name, n_prompt, n_new, _, desc = DECODE_MODELS[args.decode_model]
+    cfg = dict(getattr(hm, cfg_name))
+    B = args.decode_batch
+    t0 = time.perf_counter()
+    m = synthetic_model(cfg, seed=0, kv_f16=True, batch=B)
+    build_s = time.perf_counter() - t0
+    prompts = np.random.default_rng(rank).integers(0, cfg["vocab"], size=(B, n_prompt)).astype(np.int32)
+    s = SamplerDesc(0.8, 0.95, 40, 1.1, 64)
+    seeds = np.arange(B, dtype=np.int32) + 100 * rank
+    m.generate_batch(prompts, n_new, s, seeds)            # warm-up (graph capture, caches)
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    toks = m.generate_batch(prompts, n_new, s, seeds)
+    wall = time.perf_counter() - w0
+    pre_ms, dec_ms = m.last_timing()
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([dec_ms, pre_ms, wall], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dec_ms, pre_ms, wall = (float(v) for v in t.tolist())
+    tok_s = world * B * n_new / (dec_ms * 1e-3)
+    bpt, wbytes = decode_bytes_per_token(cfg, n_prompt, n_new)
+    step_bytes = wbytes + B * (bpt - wbytes)          # weights once, the KV rows of every sequence
+    peak, peak_kind = peaks()
+    step_s = dec_ms * 1e-3 / n_new
+    out = {
+        "config": f"{desc}; batch {B}, prompt {n_prompt}, {n_new} new tokens a sequence, "
+                  "T 0.8 / top-k 40 / top-p 0.95 / rep 1.1" + (f"; {world} data-parallel replicas" if world > 1 else ""),
+        "model": args.decode_model, "batch": B, "scaling": "weak" if world > 1 else "n/a", "n_gpus": world,
+        "value": round(tok_s, 1), "unit": "tokens/s (all sequences)", "ms_per_step": round(step_s * 1e3, 3),
+        "prefill_ms": round(pre_ms, 1),
+        "roofline": {"bound": "hbm", "bytes_per_step": int(step_bytes),
+                     "achieved": round(step_bytes / step_s / 1e9, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(step_bytes / step_s / 1e9 / peak, 4), "peak_source": peak_kind},
+        "e2e": {"value": round(world * B * n_new / wall, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * B * n_prompt,
+                "d2h_bytes_per_step": 4 * B * n_new, "path": "holo_model_generate_batch, prefill included"},
+        "model_build_s": round(build_s, 1),
+        "tokens_head_seq0": [int(t) for t in toks[0][:8]],
+    }
+    m.close()
+    return out
 
 
 def decode_cpu_baseline(cfg, host, prompt, budget_s):
@@ -677,6 +731,8 @@ def main():
     ap.add_argument("--profile-decode", action="store_true", help="small 7B decode case for ncu")
     ap.add_argument("--decode-only", action="store_true", help="only the decode sub-benchmark")
     ap.add_argument("--decode-model", choices=["7b", "70b"], default="7b", help="decode sub-benchmark model")
+    ap.add_argument("--decode-batch", type=int, default=1,
+                    help="sequences decoded together (batched engine; under torchrun: one batch per rank)")
     ap.add_argument("--layers", type=int, default=0, help="--profile-decode: first N layers only")
     ap.add_argument("--no-prefill", action="store_true", help="skip the tcgen05 prefill sub-benchmark")
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill sub-benchmark")

@@ -47,13 +47,16 @@ template <> __device__ __forceinline__ float to_kv<float>(float v) { return v; }
 template <> __device__ __forceinline__ __half to_kv<__half>(float v) { return __float2half_rn(v); }
 
 // ---------------------------------------------------------------------------
-// embedding row of the token at pos (F32 copy, F16 exact widening)
+// embedding row of the token at pos (F32 copy, F16 exact widening); batched:
+// sequence blockIdx.y, its token list seq_bs ints after the previous one
 // ---------------------------------------------------------------------------
 template <bool F16>
 __global__ void dec_embed_kernel(float *__restrict__ x, const void *__restrict__ emb, const int *__restrict__ seq,
-                                 const int *__restrict__ pos_p, int dim, int vocab) {
+                                 const int *__restrict__ pos_p, int dim, int vocab, int seq_bs) {
     dec_pdl_trigger();
     dec_pdl_wait();
+    seq += (size_t)blockIdx.y * seq_bs;
+    x += (size_t)blockIdx.y * dim;
     const int tok = seq[*pos_p];
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= dim) return;
@@ -67,14 +70,18 @@ __global__ void dec_embed_kernel(float *__restrict__ x, const void *__restrict__
 
 // ---------------------------------------------------------------------------
 // RoPE of q (n_heads) and k (n_kv_heads) at pos, then k and v appended to the
-// layer's cache; one CTA per head, one thread per rotation pair
+// layer's cache; one CTA per head, one thread per rotation pair; batched:
+// sequence blockIdx.y, qkv_bs floats and kv_bs cache elements apart
 // ---------------------------------------------------------------------------
 template <typename KV>
 __global__ void dec_rope_append_kernel(float *__restrict__ qkv, KV *__restrict__ kc, KV *__restrict__ vc,
                                        const int *__restrict__ pos_p, int hd, int n_heads, int n_kv_heads,
-                                       float base) {
+                                       float base, size_t qkv_bs, size_t kv_bs) {
     dec_pdl_trigger();
     dec_pdl_wait();
+    qkv += blockIdx.y * qkv_bs;
+    kc += blockIdx.y * kv_bs;
+    vc += blockIdx.y * kv_bs;
     const int pos = *pos_p;
     const int h = blockIdx.x, i = threadIdx.x, half = hd / 2;
     if (i >= half) return;
@@ -134,14 +141,20 @@ template <int N> struct KvVec<__half, N> {
     }
 };
 
+// batched: sequence blockIdx.z, q_bs floats, kv_bs cache elements and
+// part_bs partial floats apart
 template <typename KV, int HD>
 __global__ void __launch_bounds__(AT_WARPS * 32)
 dec_attn_split_kernel(float *__restrict__ part, const float *__restrict__ q, const KV *__restrict__ kc,
                       const KV *__restrict__ vc, const int *__restrict__ pos_p, int kv_dim, int group,
-                      int per_split, int max_splits, float sqrt_hd) {
+                      int per_split, int max_splits, float sqrt_hd, size_t q_bs, size_t kv_bs, size_t part_bs) {
     constexpr int DPL = HD / 8;
     dec_pdl_trigger();
     dec_pdl_wait();
+    part += blockIdx.z * part_bs;
+    q += blockIdx.z * q_bs;
+    kc += blockIdx.z * kv_bs;
+    vc += blockIdx.z * kv_bs;
     const int kv_len = *pos_p + 1;
     const int h = blockIdx.x, sp = blockIdx.y;
     const int p0 = sp * per_split;
@@ -214,11 +227,15 @@ dec_attn_split_kernel(float *__restrict__ part, const float *__restrict__ q, con
     }
 }
 
+// batched: sequence blockIdx.y, att_bs and part_bs floats apart
 template <int HD>
 __global__ void dec_attn_merge_kernel(float *__restrict__ att, const float *__restrict__ part,
-                                      const int *__restrict__ pos_p, int per_split, int max_splits) {
+                                      const int *__restrict__ pos_p, int per_split, int max_splits,
+                                      size_t att_bs, size_t part_bs) {
     dec_pdl_trigger();
     dec_pdl_wait();
+    att += blockIdx.y * att_bs;
+    part += blockIdx.y * part_bs;
     const int kv_len = *pos_p + 1;
     const int nsp = min(max_splits, (kv_len + per_split - 1) / per_split);
     const int h = blockIdx.x;
@@ -252,6 +269,40 @@ __global__ void dec_set_token_kernel(int *seq, const int *pos_p, int token) { se
 __global__ void dec_push_kernel(int *hist, int *nhist_p, int token) {
     hist[*nhist_p] = token;
     *nhist_p += 1;
+}
+
+// ---------------------------------------------------------------------------
+// batched decode: RMSNorm (rms_norm, tensor.c:242-255: 1/sqrt(sum x^2 / n +
+// eps), then x * scale * w) of sequence blockIdx.x, residual add, SwiGLU of
+// the W1/W3 output interleaved by 16 rows
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) bt_rmsnorm_kernel(float *__restrict__ out, const float *__restrict__ x,
+                                                          const float *__restrict__ w, int dim, float eps) {
+    x += (size_t)blockIdx.x * dim;
+    out += (size_t)blockIdx.x * dim;
+    __shared__ float sv[32];
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+    ss = block_sum(ss, sv);
+    const float scale = 1.0f / sqrtf(ss / (float)dim + eps);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) out[i] = x[i] * scale * w[i];
+}
+
+__global__ void bt_add_kernel(float *__restrict__ x, const float *__restrict__ t, long long n) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        x[i] += t[i];
+}
+
+// h[b][f] = silu(W1 x)[f] * (W3 x)[f]; row-block k of the product holds W1
+// rows 16k..16k+15, then W3 rows 16k..16k+15
+__global__ void bt_swiglu_kernel(float *__restrict__ h, const float *__restrict__ hh, int ffn, long long n) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const long long b = i / ffn;
+        const int f = (int)(i - b * ffn);
+        const float *row = hh + (size_t)b * 2 * ffn + (size_t)(f >> 4) * 32 + (f & 15);
+        const float v = row[0], u = row[16];
+        h[i] = (v / (1.0f + expf(-v))) * u;
+    }
 }
 
 __global__ void __launch_bounds__(SM_THREADS)
@@ -355,6 +406,19 @@ struct HoloModel {
     StepPrefetch *d_pf = nullptr;
     unsigned long long *d_bar = nullptr;
     int *d_att_cnt = nullptr;
+    // batched decode (desc.batch > 1): `batch` sequences in lockstep, every
+    // projection one tensor-core matmul with M = batch; its own KV caches,
+    // position and token lists ([b][...], b-major)
+    int batch = 1;
+    float *bx = nullptr, *bxn = nullptr, *bqkv = nullptr, *batt = nullptr, *bt = nullptr, *bhh = nullptr,
+          *bh = nullptr, *blogits = nullptr, *bpart = nullptr, *brvals = nullptr;
+    void *bkc = nullptr, *bvc = nullptr;
+    int *bseq = nullptr, *bhist = nullptr, *bnhist = nullptr, *bout = nullptr, *blast = nullptr, *bpos = nullptr;
+    int h_bpos = 0;
+    void *bscratch = nullptr;   // the batched matmuls' scratch (graphs capture its address)
+    size_t bscratch_bytes = 0;
+    cudaGraphExec_t g_bstep[3] = {nullptr, nullptr, nullptr};   // prompt step, logits, logits + sampler
+    SampleArgs b_args{};
 };
 
 // the handle one rank gives the others
@@ -405,6 +469,10 @@ void drop_graphs(HoloModel *m) {
     if (m->g_forward) cudaGraphExecDestroy(m->g_forward);
     if (m->g_gen) cudaGraphExecDestroy(m->g_gen);
     m->g_forward = m->g_gen = nullptr;
+    for (auto &g : m->g_bstep) {
+        if (g) cudaGraphExecDestroy(g);
+        g = nullptr;
+    }
 }
 
 // enqueue one token step (embed .. logits [.. sample] .. pos+1)
@@ -416,9 +484,9 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
     // the step's first kernel follows whatever precedes the graph in full
     ok = ok && (d.emb_type == 1
                     ? launch_pdl(dec_embed_kernel<true>, dim3((d.dim + 255) / 256), dim3(256), st, false, m->x,
-                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab)
+                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab, 0)
                     : launch_pdl(dec_embed_kernel<false>, dim3((d.dim + 255) / 256), dim3(256), st, false, m->x,
-                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab));
+                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab, 0));
     const size_t kv_layer = (size_t)d.max_seq * m->kv_dim;
     const size_t kv_es = d.kv_f16 ? 2 : 4;
     const float sqrt_hd = sqrtf((float)hd);
@@ -434,19 +502,19 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
         if (d.kv_f16)
             ok = ok && launch_pdl(dec_rope_append_kernel<__half>, dim3(heads), dim3(hd / 2), st, pdl, m->qkv,
                                   (__half *)kc, (__half *)vc, (const int *)m->d_pos, hd, d.n_heads, d.n_kv_heads,
-                                  d.rope_base);
+                                  d.rope_base, (size_t)0, (size_t)0);
         else
             ok = ok && launch_pdl(dec_rope_append_kernel<float>, dim3(heads), dim3(hd / 2), st, pdl, m->qkv,
                                   (float *)kc, (float *)vc, (const int *)m->d_pos, hd, d.n_heads, d.n_kv_heads,
-                                  d.rope_base);
+                                  d.rope_base, (size_t)0, (size_t)0);
         const int group = d.n_heads / d.n_kv_heads;
         const dim3 ag(d.n_heads, m->max_splits);
 #define HOLO_ATTN(KVT, HDV)                                                                                   \
     launch_pdl(dec_attn_split_kernel<KVT, HDV>, ag, dim3(AT_WARPS * 32), st, pdl, m->part,                    \
                (const float *)m->qkv, (const KVT *)kc, (const KVT *)vc, (const int *)m->d_pos, m->kv_dim, group, \
-               m->per_split, m->max_splits, sqrt_hd) &&                                                       \
+               m->per_split, m->max_splits, sqrt_hd, (size_t)0, (size_t)0, (size_t)0) &&                       \
         launch_pdl(dec_attn_merge_kernel<HDV>, dim3(d.n_heads), dim3(HDV), st, pdl, m->att,                   \
-                   (const float *)m->part, (const int *)m->d_pos, m->per_split, m->max_splits)
+                   (const float *)m->part, (const int *)m->d_pos, m->per_split, m->max_splits, (size_t)0, (size_t)0)
         if (d.kv_f16) {
             if (hd == 64) ok = ok && HOLO_ATTN(__half, 64);
             else if (hd == 128) ok = ok && HOLO_ATTN(__half, 128);
@@ -483,11 +551,130 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
     return ok;
 }
 
+// One position of all `batch` sequences (llm_forward per sequence, llm.c
+// 1015-1269): mode 0 the prompt step (no logits), 1 with the logits, 2 with
+// the logits and the sampler of every sequence (llm_sample, llm.c:1281-1328).
+bool enqueue_batch_step(HoloModel *m, cudaStream_t st, int mode, const SampleArgs &sa) {
+    const holo_model_desc &d = m->d;
+    const int B = m->batch, hd = d.head_dim, S = d.max_seq + 1;
+    const int qkv_dim = m->q_dim + 2 * m->kv_dim;
+    const size_t kv_layer = (size_t)d.max_seq * m->kv_dim, kv_bs = (size_t)d.n_layers * kv_layer;
+    const size_t part_bs = (size_t)d.n_heads * m->max_splits * (hd + 2);
+    const float sqrt_hd = sqrtf((float)hd);
+    const int group = d.n_heads / d.n_kv_heads;
+    bool ok = d.emb_type == 1
+                  ? launch_pdl(dec_embed_kernel<true>, dim3((d.dim + 255) / 256, B), dim3(256), st, false, m->bx,
+                               (const void *)m->emb, (const int *)m->bseq, (const int *)m->bpos, d.dim, d.vocab, S)
+                  : launch_pdl(dec_embed_kernel<false>, dim3((d.dim + 255) / 256, B), dim3(256), st, false, m->bx,
+                               (const void *)m->emb, (const int *)m->bseq, (const int *)m->bpos, d.dim, d.vocab, S);
+    auto norm = [&](const float *w) {
+        bt_rmsnorm_kernel<<<B, 1024, 0, st>>>(m->bxn, m->bx, w, d.dim, d.eps);
+        return holo_check_launch("batched rmsnorm");
+    };
+    auto add = [&](const float *t) {
+        const long long n = (long long)B * d.dim;
+        bt_add_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 1024), 256, 0, st>>>(m->bx, t, n);
+        return holo_check_launch("batched residual");
+    };
+    for (int l = 0; l < d.n_layers && ok; ++l) {
+        HoloLayer &L = m->layers[l];
+        ok = norm(L.attn_norm) && holo_matmul_batched(m->bqkv, L.wqkv, L.i_qkv, m->bxn, B, st, m->bscratch, m->bscratch_bytes);
+        const size_t es = d.kv_f16 ? 2 : 4;
+        uint8_t *kc = (uint8_t *)m->bkc + (size_t)l * kv_layer * es, *vc = (uint8_t *)m->bvc + (size_t)l * kv_layer * es;
+        const dim3 rg(std::max(d.n_heads, d.n_kv_heads), B), ag(d.n_heads, m->max_splits, B), mg(d.n_heads, B);
+#define BT_ATTN(KVT, HDV)                                                                                          \
+    launch_pdl(dec_rope_append_kernel<KVT>, rg, dim3(hd / 2), st, false, m->bqkv, (KVT *)kc, (KVT *)vc,             \
+               (const int *)m->bpos, hd, d.n_heads, d.n_kv_heads, d.rope_base, (size_t)qkv_dim, kv_bs) &&          \
+        launch_pdl(dec_attn_split_kernel<KVT, HDV>, ag, dim3(AT_WARPS * 32), st, false, m->bpart,                 \
+                   (const float *)m->bqkv, (const KVT *)kc, (const KVT *)vc, (const int *)m->bpos, m->kv_dim, group, \
+                   m->per_split, m->max_splits, sqrt_hd, (size_t)qkv_dim, kv_bs, part_bs) &&                       \
+        launch_pdl(dec_attn_merge_kernel<HDV>, mg, dim3(HDV), st, false, m->batt, (const float *)m->bpart,         \
+                   (const int *)m->bpos, m->per_split, m->max_splits, (size_t)m->q_dim, part_bs)
+        if (d.kv_f16) {
+            if (hd == 64) ok = ok && BT_ATTN(__half, 64);
+            else if (hd == 128) ok = ok && BT_ATTN(__half, 128);
+            else ok = ok && BT_ATTN(__half, 256);
+        } else {
+            if (hd == 64) ok = ok && BT_ATTN(float, 64);
+            else if (hd == 128) ok = ok && BT_ATTN(float, 128);
+            else ok = ok && BT_ATTN(float, 256);
+        }
+#undef BT_ATTN
+        ok = ok && holo_matmul_batched(m->bt, L.wo, L.i_o, m->batt, B, st, m->bscratch, m->bscratch_bytes) && add(m->bt);
+        ok = ok && norm(L.ffn_norm) && holo_matmul_batched(m->bhh, L.w13, L.i_13, m->bxn, B, st, m->bscratch, m->bscratch_bytes);
+        if (ok) {
+            const long long n = (long long)B * d.ffn_dim;
+            bt_swiglu_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 2048), 256, 0, st>>>(m->bh, m->bhh,
+                                                                                                d.ffn_dim, n);
+            ok = holo_check_launch("batched swiglu");
+        }
+        ok = ok && holo_matmul_batched(m->bt, L.w2, L.i_2, m->bh, B, st, m->bscratch, m->bscratch_bytes) && add(m->bt);
+    }
+    if (mode >= 1)
+        ok = ok && norm(m->final_norm) && holo_matmul_batched(m->blogits, m->out, m->i_out, m->bxn, B, st, m->bscratch, m->bscratch_bytes);
+    if (mode == 2) {
+        HoloDevice *D = holo_dev();
+        for (int b = 0; b < B && ok; ++b)
+            ok = launch_pdl_smem(dec_sample_kernel, dim3(1), dim3(SM_THREADS), sizeof(SampleSmem), st, false,
+                                 m->blogits + (size_t)b * d.vocab, m->probs, m->kept_idx, m->kept_p,
+                                 m->bseq + (size_t)b * S, m->bhist + (size_t)b * S, m->bnhist + b,
+                                 (const int *)m->bpos, (const float *)m->brvals + (size_t)b * S, m->bout + (size_t)b * S,
+                                 m->blast + b, D ? D->status : nullptr, sa);
+    }
+    return ok && launch_pdl(dec_step_end_kernel, dim3(1), dim3(32), st, false, m->bpos);
+}
+
+// the batched step of `mode` as a graph (first: one run outside capture, so
+// the kernels' one-time set-up and the scratch sizes are settled)
+bool run_batch_step(HoloModel *m, int mode, const SampleArgs &sa, cudaStream_t st);
+
 // the sampler's shared memory exceeds the default 48 KB
 bool prepare_sampler() {
     if (cudaFuncSetAttribute(dec_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)sizeof(SampleSmem)) != cudaSuccess)
         return holo_check_launch("sampler attributes");
+    return true;
+}
+
+bool run_batch_step(HoloModel *m, int mode, const SampleArgs &sa, cudaStream_t st) {
+    if (m->g_bstep[mode] && mode == 2 && memcmp(&sa, &m->b_args, sizeof(sa)) != 0) {
+        cudaGraphExecDestroy(m->g_bstep[2]);
+        m->g_bstep[2] = nullptr;
+    }
+    if (!m->bscratch) {
+        size_t need = holo_matmul_batched_scratch(m->i_out, m->batch);
+        for (auto &L : m->layers)
+            for (const WeightInfo *wi : {&L.i_qkv, &L.i_o, &L.i_13, &L.i_2})
+                need = std::max(need, holo_matmul_batched_scratch(*wi, m->batch));
+        if (!dev_alloc(&m->bscratch, need)) return false;
+        m->bscratch_bytes = need;
+    }
+    if (!m->g_bstep[mode]) {
+        // one plain step first (the kernels' one-time set-up), then the capture
+        if (!prepare_sampler() || !enqueue_batch_step(m, st, mode, sa)) return false;
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+            return holo_check_launch("batched step: begin capture");
+        const bool ok = enqueue_batch_step(m, st, mode, sa);
+        const cudaError_t e = cudaStreamEndCapture(st, &g);
+        if (!ok || e != cudaSuccess || !g) {
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();
+            holo_set_status(HOLO_E_ARG, "batched step: capture failed");
+            return false;
+        }
+        const bool inst = cudaGraphInstantiate(&m->g_bstep[mode], g, 0) == cudaSuccess;
+        cudaGraphDestroy(g);
+        if (!inst) {
+            cudaGetLastError();
+            m->g_bstep[mode] = nullptr;
+            holo_set_status(HOLO_E_ARG, "batched step: graph instantiation failed");
+            return false;
+        }
+        if (mode == 2) m->b_args = sa;
+        return true;   // the plain run above was this step
+    }
+    if (cudaGraphLaunch(m->g_bstep[mode], st) != cudaSuccess) return holo_check_launch("batched step launch");
     return true;
 }
 
@@ -705,6 +892,10 @@ void *holo_model_create(const holo_model_desc *desc) {
         holo_set_status(HOLO_E_ARG, "holo_model_create: unsupported sharding");
         return nullptr;
     }
+    if (d.batch > 1 && (world > 1 || d.batch > 64)) {
+        holo_set_status(HOLO_E_ARG, "holo_model_create: batch 2..64 on one GPU (no sharding)");
+        return nullptr;
+    }
     if (d.n_layers <= 0 || d.dim <= 0 || d.n_heads <= 0 || d.n_kv_heads <= 0 || d.n_heads % d.n_kv_heads ||
         !(hd == 64 || hd == 128 || hd == 256) || d.ffn_dim <= 0 || d.ffn_dim % 16 || d.vocab <= 0 ||
         d.max_seq <= 0 || (d.act_mode != HOLO_ACT_Q8 && d.act_mode != HOLO_ACT_F32) ||
@@ -790,6 +981,35 @@ void *holo_model_create(const holo_model_desc *desc) {
         holo_set_status(HOLO_E_UNSUPPORTED, "holo_model_create: sharding needs the step kernel (HOLO_STEP)");
         holo_model_free(m);
         return nullptr;
+    }
+    m->batch = d.batch <= 1 ? 1 : d.batch;
+    if (m->batch > 1) {
+        const int B = m->batch, S = d.max_seq + 1;
+        const size_t kv_all = (size_t)B * d.n_layers * d.max_seq * m->kv_dim * (d.kv_f16 ? 2 : 4);
+        bool bok = dev_alloc(&m->bkc, kv_all) && dev_alloc(&m->bvc, kv_all);
+        bok = bok && dev_alloc((void **)&m->bx, sizeof(float) * B * d.dim) &&
+              dev_alloc((void **)&m->bxn, sizeof(float) * B * d.dim) &&
+              dev_alloc((void **)&m->bqkv, sizeof(float) * B * (m->q_dim + 2 * m->kv_dim)) &&
+              dev_alloc((void **)&m->batt, sizeof(float) * B * m->q_dim) &&
+              dev_alloc((void **)&m->bt, sizeof(float) * B * d.dim) &&
+              dev_alloc((void **)&m->bhh, sizeof(float) * B * 2 * d.ffn_dim) &&
+              dev_alloc((void **)&m->bh, sizeof(float) * B * d.ffn_dim) &&
+              dev_alloc((void **)&m->blogits, sizeof(float) * B * d.vocab) &&
+              dev_alloc((void **)&m->bpart, sizeof(float) * B * d.n_heads * m->max_splits * (hd + 2)) &&
+              dev_alloc((void **)&m->brvals, sizeof(float) * B * S) &&
+              dev_alloc((void **)&m->bseq, sizeof(int) * B * S) && dev_alloc((void **)&m->bhist, sizeof(int) * B * S) &&
+              dev_alloc((void **)&m->bout, sizeof(int) * B * S) && dev_alloc((void **)&m->bnhist, sizeof(int) * B) &&
+              dev_alloc((void **)&m->blast, sizeof(int) * B) && dev_alloc((void **)&m->bpos, sizeof(int) * 4);
+        if (!bok) {
+            holo_model_free(m);
+            return nullptr;
+        }
+        cudaMemset(m->bkc, 0, kv_all);
+        cudaMemset(m->bvc, 0, kv_all);
+        cudaMemset(m->bpos, 0, sizeof(int) * 4);
+        cudaMemset(m->bnhist, 0, sizeof(int) * B);
+        cudaMemset(m->bseq, 0, sizeof(int) * B * S);
+        cudaMemset(m->brvals, 0, sizeof(float) * B * S);
     }
     cudaMemset(m->comm, 0, m->comm_bytes);
     cudaMemset(m->qkv_ll, 0, sizeof(StepWord) * (m->q_dim + 2 * m->kv_dim));
@@ -1093,6 +1313,86 @@ int holo_model_last_timing(void *model, float *prefill_ms, float *decode_ms) {
     return HOLO_OK;
 }
 
+int holo_model_forward_batch(void *model, const int *tokens, float *logits) {
+    HoloModel *m = (HoloModel *)model;
+    if (!model_ready(m) || m->batch < 2 || !tokens || m->h_bpos >= m->d.max_seq) {
+        holo_set_status(HOLO_E_ARG, "holo_model_forward_batch: batched model, tokens, position below max_seq");
+        return HOLO_E_ARG;
+    }
+    const int B = m->batch, S = m->d.max_seq + 1;
+    for (int b = 0; b < B; ++b)
+        if (tokens[b] < 0 || tokens[b] >= m->d.vocab) {
+            holo_set_status(HOLO_E_ARG, "holo_model_forward_batch: token out of range");
+            return HOLO_E_ARG;
+        }
+    cudaStream_t st = holo_stream();
+    // column h_bpos of every sequence's token list
+    if (cudaMemcpy2DAsync(m->bseq + m->h_bpos, sizeof(int) * S, tokens, sizeof(int), sizeof(int), B,
+                          cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return holo_check_launch("holo_model_forward_batch: tokens") ? HOLO_E_ARG : cuda_last_status();
+    SampleArgs none{};
+    if (!run_batch_step(m, 1, none, st)) return cuda_last_status() ? cuda_last_status() : HOLO_E_ARG;
+    m->h_bpos++;
+    if (logits) {
+        if (cudaMemcpyAsync(logits, m->blogits, sizeof(float) * B * m->d.vocab, cudaMemcpyDeviceToHost, st) !=
+            cudaSuccess)
+            holo_check_launch("holo_model_forward_batch: logits copy");
+    }
+    cudaStreamSynchronize(st);
+    return cuda_last_status();
+}
+
+int holo_model_generate_batch(void *model, const int *prompts, int n_prompt, int n_new, const holo_sampler_desc *s,
+                              const int *seeds, int *out) {
+    HoloModel *m = (HoloModel *)model;
+    if (!model_ready(m) || m->batch < 2 || !prompts || !s || !seeds || !out || n_prompt <= 0 || n_new <= 0 ||
+        n_prompt + n_new > m->d.max_seq) {
+        holo_set_status(HOLO_E_ARG, "holo_model_generate_batch: bad arguments");
+        return -1;
+    }
+    const int B = m->batch, S = m->d.max_seq + 1;
+    for (int i = 0; i < B * n_prompt; ++i)
+        if (prompts[i] < 0 || prompts[i] >= m->d.vocab) {
+            holo_set_status(HOLO_E_ARG, "holo_model_generate_batch: prompt token out of range");
+            return -1;
+        }
+    cudaStream_t st = holo_stream();
+    // llm_generate per sequence (llm.c:1340-1420): srand(seed_b), one rand()
+    // per sampled token when T != 0
+    std::vector<float> r((size_t)B * S, 0.0f);
+    for (int b = 0; b < B; ++b) {
+        srand((unsigned)seeds[b]);
+        if (s->temperature != 0.0f)
+            for (int i = 0; i < n_new; ++i) r[(size_t)b * S + i] = (float)rand() / RAND_MAX;
+    }
+    holo_model_reset(m);
+    std::vector<int> nh(B, n_prompt);
+    cudaMemcpyAsync(m->brvals, r.data(), sizeof(float) * B * S, cudaMemcpyHostToDevice, st);
+    cudaMemcpy2DAsync(m->bseq, sizeof(int) * S, prompts, sizeof(int) * n_prompt, sizeof(int) * n_prompt, B,
+                      cudaMemcpyHostToDevice, st);
+    cudaMemcpy2DAsync(m->bhist, sizeof(int) * S, prompts, sizeof(int) * n_prompt, sizeof(int) * n_prompt, B,
+                      cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(m->bnhist, nh.data(), sizeof(int) * B, cudaMemcpyHostToDevice, st);
+    SampleArgs a = make_args(m, s);
+    a.gen = 1;
+    a.n_prompt = n_prompt;
+    const int steps = n_prompt + n_new - 1;
+    SampleArgs none{};
+    cudaEventRecord(m->ev[0], st);
+    for (int i = 0; i < steps; ++i) {
+        if (i == n_prompt - 1) cudaEventRecord(m->ev[1], st);
+        if (!run_batch_step(m, i < n_prompt - 1 ? 0 : 2, i < n_prompt - 1 ? none : a, st)) return -1;
+    }
+    cudaEventRecord(m->ev[2], st);
+    cudaMemcpy2DAsync(out, sizeof(int) * n_new, m->bout, sizeof(int) * S, sizeof(int) * n_new, B,
+                      cudaMemcpyDeviceToHost, st);
+    cudaStreamSynchronize(st);
+    cudaEventElapsedTime(&m->last_prefill_ms, m->ev[0], m->ev[1]);
+    cudaEventElapsedTime(&m->last_decode_ms, m->ev[1], m->ev[2]);
+    m->h_bpos = steps;
+    return cuda_last_status() == HOLO_OK ? n_new : -1;
+}
+
 int holo_model_shard(const holo_model_desc *desc, int *ranges) {
     if (!desc || !ranges || !shard_of(*desc, ranges)) {
         holo_set_status(HOLO_E_ARG, "holo_model_shard: desc cannot be sharded");
@@ -1171,6 +1471,11 @@ void holo_model_reset(void *model) {
         cudaMemsetAsync(m->qkv_ll, 0, sizeof(StepWord) * (m->q_dim + 2 * m->kv_dim), st);
     }
     cudaMemsetAsync(m->d_att_cnt, 0, sizeof(int) * m->nh, st);
+    if (m->batch > 1) {
+        cudaMemsetAsync(m->bpos, 0, sizeof(int), st);
+        cudaMemsetAsync(m->bnhist, 0, sizeof(int) * m->batch, st);
+        m->h_bpos = 0;
+    }
     cudaStreamSynchronize(st);
     m->h_pos = 0;
     m->h_nhist = 0;
@@ -1192,6 +1497,9 @@ void holo_model_free(void *model) {
         cudaFree(L.attn_norm); cudaFree(L.ffn_norm); cudaFree(L.wqkv); cudaFree(L.wo); cudaFree(L.w13);
         cudaFree(L.w2);
     }
+    void *bbufs[] = {m->bx, m->bxn, m->bqkv, m->batt, m->bt, m->bhh, m->bh, m->blogits, m->bpart, m->brvals,
+                     m->bkc, m->bvc, m->bseq, m->bhist, m->bout, m->bnhist, m->blast, m->bpos, m->bscratch};
+    for (void *p : bbufs) cudaFree(p);
     void *bufs[] = {m->emb, m->final_norm, m->out, m->kc, m->vc, m->comm, m->qkv_ll, m->x, m->qkv, m->att,
                     m->h, m->logits, m->part, m->probs, m->kept_p, m->rvals, m->kept_idx, m->d_pos, m->d_seq, m->d_hist,
                     m->d_nhist, m->d_out, m->d_last, m->d_layers, m->d_pf, m->d_bar, m->d_att_cnt};

@@ -149,8 +149,12 @@ bool holo_registry_find(const void *ptr, WeightInfo *out);
 // caller-provided buffer of cuda_quant_tiled_bytes() bytes (no allocation)
 bool holo_quant_shape_ok(int ggml_type, int rows, int cols);
 WeightInfo holo_weight_info(int ggml_type, int rows, int cols, int q4k_layout);
-// Y[M][N] = X[M][K] . W^T on the tensor cores for a tiled weight (prefill.cu)
-bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st);
+// Y[M][N] = X[M][K] . W^T on the tensor cores for a tiled weight (prefill.cu);
+// scratch NULL: the library's shared scratch, else the caller's (at least
+// holo_matmul_batched_scratch bytes)
+bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st,
+                         void *scratch, size_t scratch_bytes);
+size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M);
 bool holo_repack_to(void *dst, const void *dev_blocks, int ggml_type, int rows, int cols, int q4k_layout,
                     cudaStream_t st);
 void holo_registry_add(const void *ptr, const WeightInfo &info);

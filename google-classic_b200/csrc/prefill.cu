@@ -416,9 +416,46 @@ bool launch_mma(float *out, const uint8_t *W, const uint8_t *xt, int M, int N, i
 
 }  // namespace
 
+namespace {
+
+// the launch plan of one batched matmul: token tile, K splits, scratch bytes
+struct PfPlan {
+    int tn, mtiles, Mpad, splits, kc_per_split;
+    size_t xt_bytes, part_bytes;
+};
+
+PfPlan pf_plan(const WeightInfo &wi, int M, int sms) {
+    PfPlan p;
+    const int N = wi.rows, K = wi.cols, vals = wi.type == GT_Q8_0 ? 128 : 256;
+    p.tn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
+    p.mtiles = (M + p.tn - 1) / p.tn;
+    p.Mpad = p.mtiles * p.tn;
+    const int nkc = K / PF_BK, cpu = vals / PF_BK;
+    // K splits (whole units) so that the CTAs cover the SMs when the weight
+    // has few row tiles
+    const int base = (N / PF_BM) * p.mtiles;
+    p.splits = std::max(1, std::min(nkc / 4, sms / base));
+    p.kc_per_split = ((nkc + p.splits - 1) / p.splits + cpu - 1) / cpu * cpu;
+    p.splits = (nkc + p.kc_per_split - 1) / p.kc_per_split;   // every split non-empty
+    p.xt_bytes = ((size_t)p.Mpad * K * 2 + 255) & ~(size_t)255;
+    p.part_bytes = p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0;
+    return p;
+}
+
+}  // namespace
+
+size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M) {
+    HoloDevice *D = holo_dev();
+    const PfPlan p = pf_plan(wi, M, D ? D->sms : 148);
+    return p.xt_bytes + p.part_bytes;
+}
+
 // Y[M][N] = X[M][K] . W^T for a tiled weight described by wi, on stream st
-// (the ABI entry below and the batched decode engine)
-bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st) {
+// (the ABI entry below and the batched decode engine).  scratch: the caller's
+// buffer of scratch_bytes (at least holo_matmul_batched_scratch), or NULL for
+// the library's shared one.
+bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st,
+                         void *scratch, size_t scratch_bytes) {
     HoloDevice *D = holo_dev();
     if (!D) return false;
     const int N = wi.rows, K = wi.cols;
@@ -429,21 +466,22 @@ bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const fl
                                     "N % 128 == 0, K a whole number of blocks");
         return false;
     }
-    const int tn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
-    const int mtiles = (M + tn - 1) / tn, Mpad = mtiles * tn;
-    const int nkc = K / PF_BK, cpu = vals / PF_BK;
-    // K splits (whole units) so that the CTAs cover the SMs when the weight
-    // has few row tiles
-    const int base = (N / PF_BM) * mtiles;
-    int splits = std::max(1, std::min(nkc / 4, D->sms / base));
-    const int kc_per_split = ((nkc + splits - 1) / splits + cpu - 1) / cpu * cpu;
-    splits = (nkc + kc_per_split - 1) / kc_per_split;   // every split non-empty
-    const size_t xt_bytes = (size_t)Mpad * K * 2;
-    const size_t part_bytes = splits > 1 ? (size_t)splits * M * N * 4 : 0;
-    uint8_t *tmp = static_cast<uint8_t *>(holo_tmp(xt_bytes + part_bytes + 256));
+    const PfPlan pl = pf_plan(wi, M, D->sms);
+    const int tn = pl.tn, mtiles = pl.mtiles, Mpad = pl.Mpad, splits = pl.splits, kc_per_split = pl.kc_per_split;
+    const size_t xt_bytes = pl.xt_bytes, part_bytes = pl.part_bytes;
+    uint8_t *tmp;
+    if (scratch) {
+        if (scratch_bytes < xt_bytes + part_bytes) {
+            holo_set_status(HOLO_E_ARG, "batched matmul: scratch too small");
+            return false;
+        }
+        tmp = static_cast<uint8_t *>(scratch);
+    } else {
+        tmp = static_cast<uint8_t *>(holo_tmp(xt_bytes + part_bytes));
+    }
     if (!tmp) return false;
     uint8_t *xt = tmp;
-    float *part = splits > 1 ? reinterpret_cast<float *>(tmp + ((xt_bytes + 255) & ~(size_t)255)) : Y;
+    float *part = splits > 1 ? reinterpret_cast<float *>(tmp + xt_bytes) : Y;
     const long long warps = (long long)Mpad * (K / 32);
     pf_act_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(reinterpret_cast<__half *>(xt), X, M, Mpad,
                                                                        K, tn);
@@ -478,5 +516,5 @@ extern "C" int cuda_matmul_quant_batched(float *Y, const void *W, const float *X
                                     "(cuda_upload_quant)");
         return HOLO_E_ARG;
     }
-    return holo_matmul_batched(Y, W, wi, X, M, holo_stream()) ? HOLO_OK : cuda_last_status();
+    return holo_matmul_batched(Y, W, wi, X, M, holo_stream(), nullptr, 0) ? HOLO_OK : cuda_last_status();
 }

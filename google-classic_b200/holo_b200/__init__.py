@@ -99,6 +99,8 @@ SIGNATURES = {
     "holo_model_last_timing": (_i, [_vp, _vp, _vp]),
     "holo_model_pos": (_i, [_vp]), "holo_model_reset": (None, [_vp]), "holo_model_free": (None, [_vp]),
     "cuda_matmul_quant_batched": (_i, [_vp, _vp, _vp, _i, _i, _i]),
+    "holo_model_forward_batch": (_i, [_vp, _vp, _vp]),
+    "holo_model_generate_batch": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp]),
     "holo_model_comm_handle": (_i, [_vp, _vp]), "holo_model_shard": (_i, [_vp, _vp]), "holo_model_open_peers": (_i, [_vp, _vp]),
 }
 

@@ -18,7 +18,7 @@ class ModelDesc(C.Structure):
                 ("head_dim", C.c_int), ("ffn_dim", C.c_int), ("vocab", C.c_int), ("max_seq", C.c_int),
                 ("rope_base", C.c_float), ("eps", C.c_float), ("layer_type", C.c_int), ("emb_type", C.c_int),
                 ("out_type", C.c_int), ("kv_f16", C.c_int), ("act_mode", C.c_int), ("world", C.c_int),
-                ("rank", C.c_int)]
+                ("rank", C.c_int), ("batch", C.c_int)]
 
 
 class SamplerDesc(C.Structure):
@@ -38,14 +38,15 @@ class Model:
     (one process per GPU); set the weights (the full matrices: each rank keeps
     its rows), then connect_peers, then make every step call on every rank."""
 
-    def __init__(self, cfg: dict, act_mode: int = ACT_Q8, kv_f16: bool = True, world: int = 1, rank: int = 0):
+    def __init__(self, cfg: dict, act_mode: int = ACT_Q8, kv_f16: bool = True, world: int = 1, rank: int = 0,
+                 batch: int = 1):
         self.lib = load()
         self.cfg = dict(cfg)
-        self.world, self.rank = world, rank
+        self.world, self.rank, self.batch = world, rank, batch
         d = ModelDesc(cfg["n_layers"], cfg["dim"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"],
                       cfg["ffn_dim"], cfg["vocab"], cfg["max_seq"], cfg.get("rope_base", 10000.0),
                       cfg.get("eps", 1e-5), cfg["layer_type"], cfg.get("emb_type", 1), cfg["out_type"],
-                      int(kv_f16), act_mode, world, rank)
+                      int(kv_f16), act_mode, world, rank, batch)
         self.desc = d
         self.h = self.lib.holo_model_create(C.byref(d))
         self._check("holo_model_create", ok=bool(self.h))
@@ -90,6 +91,24 @@ class Model:
         out = np.zeros(n_new, np.int32)
         n = self.lib.holo_model_generate(self.h, _ptr(prompt), len(prompt), n_new, C.byref(s), seed, _ptr(out))
         self._check("holo_model_generate", n == n_new)
+        return out
+
+    def forward_batch(self, tokens, want_logits: bool = True) -> np.ndarray | None:
+        """One position of every sequence of a batched model: logits [batch][vocab]."""
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty((self.batch, self.cfg["vocab"]), np.float32) if want_logits else None
+        rc = self.lib.holo_model_forward_batch(self.h, _ptr(tokens), _ptr(out) if want_logits else None)
+        self._check("holo_model_forward_batch", rc == HOLO_OK)
+        return out
+
+    def generate_batch(self, prompts, n_new: int, s: SamplerDesc, seeds) -> np.ndarray:
+        """llm_generate for every sequence: prompts [batch][n_prompt], seeds [batch]."""
+        prompts = np.ascontiguousarray(prompts, np.int32)
+        seeds = np.ascontiguousarray(seeds, np.int32)
+        out = np.zeros((self.batch, n_new), np.int32)
+        n = self.lib.holo_model_generate_batch(self.h, _ptr(prompts), prompts.shape[1], n_new, C.byref(s),
+                                               _ptr(seeds), _ptr(out))
+        self._check("holo_model_generate_batch", n == n_new)
         return out
 
     def last_timing(self) -> tuple[float, float]:
@@ -143,7 +162,7 @@ def shard_ranges(cfg: dict, world: int, rank: int) -> dict:
     d = ModelDesc(cfg["n_layers"], cfg["dim"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"],
                   cfg["ffn_dim"], cfg["vocab"], cfg["max_seq"], cfg.get("rope_base", 10000.0),
                   cfg.get("eps", 1e-5), cfg["layer_type"], cfg.get("emb_type", 1), cfg["out_type"], 1, ACT_Q8,
-                  world, rank)
+                  world, rank, 1)
     r = (C.c_int * 10)()
     if lib.holo_model_shard(C.byref(d), r) != HOLO_OK:
         lib.cuda_clear_status()
@@ -163,13 +182,13 @@ def _tensor_seed(seed: int, layer: int, idx: int) -> int:
 
 
 def synthetic_model(cfg: dict, seed: int, act_mode: int = ACT_Q8, kv_f16: bool = True, std: float = 0.02,
-                    keep_host: bool = False, world: int = 1, rank: int = 0):
+                    keep_host: bool = False, world: int = 1, rank: int = 0, batch: int = 1):
     """A random-init model built on the device: every weight N(0, std),
     quantized round-to-nearest by cuda_synth_weights into GGUF blocks, then
     repacked by holo_model_set_layer/_globals.  keep_host also returns the raw
     blocks (the dict layout of synth.llama_weights) for the reference engine."""
     lib = load()
-    m = Model(cfg, act_mode=act_mode, kv_f16=kv_f16, world=world, rank=rank)
+    m = Model(cfg, act_mode=act_mode, kv_f16=kv_f16, world=world, rank=rank, batch=batch)
     dim, hd, ffn, V = cfg["dim"], cfg["head_dim"], cfg["ffn_dim"], cfg["vocab"]
     q_dim, kv_dim = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
     lt, ot, et = cfg["layer_type"], cfg["out_type"], cfg.get("emb_type", 1)

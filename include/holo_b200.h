@@ -137,6 +137,7 @@ typedef struct {
     int act_mode;        /* HOLO_ACT_Q8 or HOLO_ACT_F32 for every matvec */
     int world;           /* row sharding over this many GPUs (one process each); 0 or 1: none */
     int rank;            /* this process's shard, 0 <= rank < world */
+    int batch;           /* sequences decoded together (2..64, one GPU) by the *_batch calls; 0 or 1: none */
 } holo_model_desc;
 
 typedef struct {         /* llm_sampler_t (src/ai/llm.h:167-174) without the seed */
@@ -195,6 +196,19 @@ int holo_model_last_timing(void *model, float *prefill_ms, float *decode_ms);
  * rank with the same arguments; a rank that recorded an error (a barrier
  * time-out) leaves the group unusable -- free and recreate it on every rank.
  * No counterpart in the reference (single-device only). */
+/* Batched decode (desc.batch = B > 1, one GPU): B sequences in lockstep,
+ * each projection one tensor-core matmul with M = B (cuda_matmul_quant_batched's
+ * kernel), attention and the sampler per sequence, own KV caches.
+ * forward_batch: tokens[B] at the current position of every sequence,
+ * logits[B][vocab] copied out when not NULL.  generate_batch: prompts
+ * [B][n_prompt] (equal lengths), llm_generate per sequence with seeds[B]
+ * (srand(seed), one rand() per draw when T != 0), out[B][n_new]; returns n_new
+ * or -1.  The step is a CUDA graph (prompt steps skip the output matrix and
+ * the sampler).  No counterpart in the reference (batch 1 only). */
+int holo_model_forward_batch(void *model, const int *tokens, float *logits);
+int holo_model_generate_batch(void *model, const int *prompts, int n_prompt, int n_new, const holo_sampler_desc *s,
+                              const int *seeds, int *out);
+
 #define HOLO_COMM_HANDLE_BYTES 128
 /* The rows desc->rank holds (host only, no device needed): ranges[10] =
  * first and count of query heads, KV heads, rows of wo/w2, SwiGLU outputs
