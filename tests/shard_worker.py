@@ -11,6 +11,11 @@ host: every rank computes its row shard through the library (holo_model_shard)
 gpu:  every rank builds its shard of the test model, connects the peers and
       runs the decode calls; rank 0 writes the logits and token streams to
       OUT_DIR/gpu.npz for the parent test to compare with the reference.
+timeout: failure detection without a fault: both ranks connect, then rank 1
+      stays alive but skips the step; rank 0's step waits for rank 1's slices,
+      gives up after its bound and reports HOLO_E_TIMEOUT; rank 0 then clears
+      the status and checks that its device still computes (a matvec against
+      the oracle) before the ranks meet on the host and exit.
 """
 import datetime
 import json
@@ -114,7 +119,50 @@ def run_gpu(rank, world, out):
         np.savez(pathlib.Path(out) / "gpu.npz", **res)
 
 
+def run_timeout(rank, world, out):
+    import time
+    import torch
+    import torch.distributed as dist
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    # gloo: the host-side meeting after the failure needs no GPU collective
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+    from holo_b200 import synth
+    dev = hb.Device(local, world)
+    w = synth.llama_weights(CFG, seed=11)
+    m = Model(CFG, act_mode=hb.ACT_Q8, kv_f16=True, world=world, rank=rank)
+    m.set_weights(w)
+    connect_peers(m)
+    res = {}
+    if rank == 0:
+        t0 = time.perf_counter()
+        try:
+            m.forward(5)
+            res["raised"], res["message"] = False, ""
+        except RuntimeError as e:   # the status the step recorded, cleared by the raise
+            res["raised"], res["message"] = True, str(e)
+        res["seconds"] = time.perf_counter() - t0
+        m.lib.cuda_clear_status()
+        # the context still computes: a matvec against the restatement
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import holo_oracle
+        Wq = synth.quant_matrix(hb.Q4_K, 64, 512, 3)
+        x = synth.activation(512, 3)
+        Wd, xd, yd = dev.upload_quant(Wq, hb.Q4_K, 64, 512), dev.upload(x), dev.alloc(4 * 64)
+        dev.lib.cuda_matvec(yd, Wd, xd, 64, 512, hb.Q4_K, hb.ACT_Q8, None)
+        y = dev.download(yd, (64,), np.float32)
+        dev.check("matvec after the time-out")
+        r = holo_oracle.Oracle().matvec_q8(hb.Q4_K, Wq, x, 64, 512)
+        res["after_rel_err"] = float(np.abs(y - r).max() / np.abs(r).max())
+        (pathlib.Path(out) / "timeout.json").write_text(json.dumps(res))
+    # rank 1 never launched the step; both meet here (rank 1 keeps its memory
+    # mapped until rank 0's kernels are over)
+    dist.barrier()
+    m.close()
+    dist.destroy_process_group()
+
+
 if __name__ == "__main__":
     mode, out = sys.argv[1], sys.argv[2]
     r, n = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
-    (run_host if mode == "host" else run_gpu)(r, n, out)
+    {"host": run_host, "gpu": run_gpu, "timeout": run_timeout}[mode](r, n, out)

@@ -100,3 +100,26 @@ def test_sharded_q8_matches_one_gpu(sharded, dev, weights):
     print(f"sharded q8 vs one GPU: max norm-wise rel {worst:.3e}")
     assert worst <= 1e-3
     assert np.array_equal(sharded["q8_greedy"], got)
+
+
+def test_missing_rank_times_out_and_device_recovers(tmp_path):
+    """Failure detection without a GPU fault (2 GPUs): rank 1 connects and
+    then skips the step; rank 0's step gives up on rank 1's slices after its
+    1 s bound with HOLO_E_TIMEOUT (no hang), and the device still computes."""
+    if gpu_count() < 2:
+        pytest.skip("needs two GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", OMP_NUM_THREADS="1")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
+           str(ROOT / "tests" / "shard_worker.py"), "timeout", str(tmp_path)]
+    p = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert p.returncode == 0, p.stdout[-4000:] + p.stderr[-4000:]
+    import json
+    res = json.loads((tmp_path / "timeout.json").read_text())
+    print(res)
+    assert res["raised"] and f"status {hb.HOLO_E_TIMEOUT}" in res["message"]
+    assert res["seconds"] < 30
+    assert res["after_rel_err"] <= 1e-3
