@@ -96,10 +96,12 @@ struct SampleSmem {
     int token;
     float cand_p[SM_SORT_MAX];   // candidates (index order), then the top-p sort
     int cand_i[SM_SORT_MAX];
-    float sort_p[SM_SORT_MAX];
+    float sort_p[SM_SORT_MAX];   // also the per-warp digit histograms of the top-k selection
     int sort_j[SM_SORT_MAX];
     float work[SM_VOCAB_SMEM];   // the logits, then the probabilities (small vocabularies)
 };
+// per-warp histograms of the radix selection: 32 warps x 256 digits
+static_assert(2 * SM_SORT_MAX >= 32 * 256, "digit histograms fit the sort buffers");
 
 // The sampler body, run by one CTA of any size (a multiple of 32, <= 1024).
 // The logits are copied into a work array -- shared memory for vocabularies
@@ -138,13 +140,20 @@ static __device__ int sample_body(SampleSmem &S, const float *__restrict__ logit
     //    occurrences, so the first occurrence of each token applies all c.
     if (a.penalty != 1.0f && nhist > 0) {
         const int start = nhist > a.last_n ? nhist - a.last_n : 0;
+        // the window of the history in shared memory (cand_i is free here)
+        const bool staged = nhist - start <= SM_SORT_MAX;
+        const int *hw = staged ? S.cand_i : hist + start;
+        if (staged) {
+            for (int t = tid; t < nhist - start; t += NT) S.cand_i[t] = __ldcg(hist + start + t);
+            __syncthreads();
+        }
         for (int t = start + tid; t < nhist; t += NT) {
-            const int tok = __ldcg(hist + t);
+            const int tok = staged ? hw[t - start] : __ldcg(hw + (t - start));
             bool first = true;
             int c = 1;
             for (int u = start; u < nhist; ++u) {
                 if (u == t) continue;
-                if (__ldcg(hist + u) == tok) {
+                if ((staged ? hw[u - start] : __ldcg(hw + (u - start))) == tok) {
                     if (u < t) { first = false; break; }
                     ++c;
                 }
@@ -190,13 +199,25 @@ static __device__ int sample_body(SampleSmem &S, const float *__restrict__ logit
     if (topk) {
         if (tid == 0) { S.prefix = 0u; S.krem = a.top_k; }
         unsigned mask = 0u;
+        // digit counts in one histogram per warp (most probabilities share a
+        // few exponents: a single histogram would serialise the whole CTA's
+        // atomics on one or two bins), summed per digit afterwards
+        unsigned *wh = reinterpret_cast<unsigned *>(S.sort_p);   // [warps][256]
+        const int nw = NT >> 5;
         for (int shift = 24; shift >= 0; shift -= 8) {
-            for (int b = tid; b < 256; b += NT) S.hist256[b] = 0u;
+            for (int b = tid; b < nw * 256; b += NT) wh[b] = 0u;
             __syncthreads();
             const unsigned prefix = S.prefix;
+            unsigned *mine = wh + warp * 256;
             for (int i = tid; i < V; i += NT) {
                 const unsigned key = __float_as_uint(work[i]);
-                if ((key & mask) == prefix) atomicAdd(&S.hist256[(key >> shift) & 255u], 1u);
+                if ((key & mask) == prefix) atomicAdd(&mine[(key >> shift) & 255u], 1u);
+            }
+            __syncthreads();
+            for (int b = tid; b < 256; b += NT) {
+                unsigned c = 0u;
+                for (int w = 0; w < nw; ++w) c += wh[w * 256 + b];
+                S.hist256[b] = c;
             }
             __syncthreads();
             if (warp == 0) {
