@@ -47,17 +47,19 @@ template <> __device__ __forceinline__ float to_kv<float>(float v) { return v; }
 template <> __device__ __forceinline__ __half to_kv<__half>(float v) { return __float2half_rn(v); }
 
 // ---------------------------------------------------------------------------
-// embedding row of the token at pos (F32 copy, F16 exact widening); batched:
-// sequence blockIdx.y, its token list seq_bs ints after the previous one
+// embedding row of the token at pos (F32 copy, F16 exact widening); several
+// rows: row blockIdx.y, its token list seq_bs ints after the previous one, at
+// pos + blockIdx.y * pos_inc (batched sequences: pos_inc 0; consecutive
+// prompt positions: seq_bs 0, pos_inc 1)
 // ---------------------------------------------------------------------------
 template <bool F16>
 __global__ void dec_embed_kernel(float *__restrict__ x, const void *__restrict__ emb, const int *__restrict__ seq,
-                                 const int *__restrict__ pos_p, int dim, int vocab, int seq_bs) {
+                                 const int *__restrict__ pos_p, int dim, int vocab, int seq_bs, int pos_inc) {
     dec_pdl_trigger();
     dec_pdl_wait();
     seq += (size_t)blockIdx.y * seq_bs;
     x += (size_t)blockIdx.y * dim;
-    const int tok = seq[*pos_p];
+    const int tok = seq[*pos_p + (int)blockIdx.y * pos_inc];
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= dim) return;
     if (tok < 0 || tok >= vocab) {
@@ -70,19 +72,20 @@ __global__ void dec_embed_kernel(float *__restrict__ x, const void *__restrict__
 
 // ---------------------------------------------------------------------------
 // RoPE of q (n_heads) and k (n_kv_heads) at pos, then k and v appended to the
-// layer's cache; one CTA per head, one thread per rotation pair; batched:
-// sequence blockIdx.y, qkv_bs floats and kv_bs cache elements apart
+// layer's cache; one CTA per head, one thread per rotation pair; several rows:
+// row blockIdx.y, qkv_bs floats and kv_bs cache elements apart, at pos +
+// blockIdx.y * pos_inc
 // ---------------------------------------------------------------------------
 template <typename KV>
 __global__ void dec_rope_append_kernel(float *__restrict__ qkv, KV *__restrict__ kc, KV *__restrict__ vc,
                                        const int *__restrict__ pos_p, int hd, int n_heads, int n_kv_heads,
-                                       float base, size_t qkv_bs, size_t kv_bs) {
+                                       float base, size_t qkv_bs, size_t kv_bs, int pos_inc) {
     dec_pdl_trigger();
     dec_pdl_wait();
     qkv += blockIdx.y * qkv_bs;
     kc += blockIdx.y * kv_bs;
     vc += blockIdx.y * kv_bs;
-    const int pos = *pos_p;
+    const int pos = *pos_p + (int)blockIdx.y * pos_inc;
     const int h = blockIdx.x, i = threadIdx.x, half = hd / 2;
     if (i >= half) return;
     const int q_dim = n_heads * hd, kv_dim = n_kv_heads * hd;
@@ -259,6 +262,123 @@ __global__ void dec_attn_merge_kernel(float *__restrict__ att, const float *__re
     }
 }
 
+// ---------------------------------------------------------------------------
+// prompt attention: the M consecutive positions p0 .. p0+M-1 of one sequence
+// (p0 = *pos_p), each attending to cache positions 0 .. its own, whose keys
+// and values are already appended (llm.c:1180-1200: score = q.k / sqrtf(hd),
+// softmax over the positions, sum of p * v; here with an online softmax, as
+// in the decode kernels).  CTA: KV head blockIdx.x and query tokens
+// [blockIdx.y * qt, +qt) x the group's query heads: up to PA_ROWS rows, two
+// a warp.  Each tile of PA_KT positions is staged once in shared memory for
+// all rows (keys transposed, one float of padding a row: conflict-free for
+// both the staging stores and the per-lane key reads).
+// ---------------------------------------------------------------------------
+constexpr int PA_WARPS = 8, PA_ROWS = 2 * PA_WARPS, PA_KT = 64;
+
+__host__ __device__ constexpr size_t pa_smem(int hd) {
+    return sizeof(float) * ((size_t)hd * (PA_KT + 1) + (size_t)PA_KT * hd + (size_t)PA_ROWS * hd);
+}
+
+template <typename KV> __device__ __forceinline__ float kv_f(KV v);
+template <> __device__ __forceinline__ float kv_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float kv_f<__half>(__half v) { return __half2float(v); }
+
+template <typename KV, int HD>
+__global__ void __launch_bounds__(PA_WARPS * 32)
+pf_attn_kernel(float *__restrict__ att, const float *__restrict__ qkv, const KV *__restrict__ kc,
+               const KV *__restrict__ vc, const int *__restrict__ pos_p, int M, int qt, int group, int kv_dim,
+               size_t qkv_bs, size_t att_bs, float sqrt_hd) {
+    constexpr int DPL = HD / 32, KS = PA_KT + 1;
+    extern __shared__ float pa_sm[];
+    float *kt = pa_sm;                 // [HD][KS]: keys, transposed
+    float *vs = kt + HD * KS;          // [PA_KT][HD]
+    float *qs = vs + PA_KT * HD;       // [PA_ROWS][HD]
+    const int kvh = blockIdx.x, t0 = blockIdx.y * qt;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int p0 = *pos_p;
+    const int nt = min(qt, M - t0), rows = nt * group;
+    for (int e = tid; e < rows * HD; e += blockDim.x) {
+        const int r = e / HD, dd = e - r * HD;
+        qs[e] = qkv[(size_t)(t0 + r / group) * qkv_bs + (size_t)(kvh * group + r % group) * HD + dd];
+    }
+    const int nkeys = p0 + t0 + nt;    // the CTA's last token attends to all of them
+    float mx[2], sum[2], acc[2][DPL];
+    int last[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int r = 2 * warp + i;
+        last[i] = r < rows ? p0 + t0 + r / group : -1;   // -1: no row
+        mx[i] = -FLT_MAX;
+        sum[i] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) acc[i][k] = 0.0f;
+    }
+    for (int j0 = 0; j0 < nkeys; j0 += PA_KT) {
+        __syncthreads();   // the previous tile is consumed (and, first, the queries are stored)
+        for (int e = tid; e < PA_KT * HD; e += blockDim.x) {
+            const int j = e / HD, dd = e - j * HD;
+            float kf = 0.0f, vf = 0.0f;
+            if (j0 + j < nkeys) {
+                const size_t o = (size_t)(j0 + j) * kv_dim + (size_t)kvh * HD + dd;
+                kf = kv_f<KV>(kc[o]);
+                vf = kv_f<KV>(vc[o]);
+            }
+            kt[dd * KS + j] = kf;
+            vs[j * HD + dd] = vf;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            if (last[i] < j0) continue;   // no row, or no position of this tile is visible to it (warp-uniform)
+            const float *q = qs + (2 * warp + i) * HD;
+            float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll 16
+            for (int dd = 0; dd < HD; ++dd) {
+                const float qd = q[dd];
+                s0 = fmaf(qd, kt[dd * KS + lane], s0);
+                s1 = fmaf(qd, kt[dd * KS + lane + 32], s1);
+            }
+            const bool va = j0 + lane <= last[i], vb = j0 + lane + 32 <= last[i];
+            s0 = __fdiv_rn(s0, sqrt_hd);
+            s1 = __fdiv_rn(s1, sqrt_hd);
+            float mt = fmaxf(va ? s0 : -FLT_MAX, vb ? s1 : -FLT_MAX);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+            const float mn = fmaxf(mx[i], mt);
+            const float corr = __expf(mx[i] - mn);
+            const float e0 = va ? __expf(s0 - mn) : 0.0f, e1 = vb ? __expf(s1 - mn) : 0.0f;
+            float es = e0 + e1;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) es += __shfl_xor_sync(0xffffffffu, es, o);
+            sum[i] = fmaf(sum[i], corr, es);
+#pragma unroll
+            for (int k = 0; k < DPL; ++k) acc[i][k] *= corr;
+#pragma unroll 8
+            for (int jj = 0; jj < PA_KT; ++jj) {
+                const float pj = __shfl_sync(0xffffffffu, jj < 32 ? e0 : e1, jj & 31);
+                const float *v = vs + jj * HD + lane * DPL;
+#pragma unroll
+                for (int k = 0; k < DPL; ++k) acc[i][k] = fmaf(pj, v[k], acc[i][k]);
+            }
+            mx[i] = mn;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        if (last[i] < 0) continue;
+        const int r = 2 * warp + i;
+        float *o = att + (size_t)(t0 + r / group) * att_bs + (size_t)(kvh * group + r % group) * HD + lane * DPL;
+        const float inv = 1.0f / sum[i];
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) o[k] = acc[i][k] * inv;
+    }
+}
+
+// advance the position by n (after a prompt pass of n rows)
+__global__ void dec_pos_add_kernel(int *pos_p, int n) {
+    if (threadIdx.x == 0) *pos_p += n;
+}
+
 __global__ void dec_step_end_kernel(int *pos_p) {
     dec_pdl_trigger();
     dec_pdl_wait();
@@ -419,6 +539,15 @@ struct HoloModel {
     size_t bscratch_bytes = 0;
     cudaGraphExec_t g_bstep[3] = {nullptr, nullptr, nullptr};   // prompt step, logits, logits + sampler
     SampleArgs b_args{};
+    // prompt passes (one GPU, one sequence): up to r_cap consecutive positions
+    // a pass, every projection one tensor-core matmul over the rows
+    int prompt_mode = 1;   // 1: prompts through row passes where supported, 0: one position a step
+    int r_cap = 0;
+    bool r_attr = false;
+    float *rx = nullptr, *rxn = nullptr, *rqkv = nullptr, *ratt = nullptr, *rt = nullptr, *rhh = nullptr,
+          *rh = nullptr;
+    void *rscratch = nullptr;
+    size_t rscratch_bytes = 0;
 };
 
 // the handle one rank gives the others
@@ -484,9 +613,9 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
     // the step's first kernel follows whatever precedes the graph in full
     ok = ok && (d.emb_type == 1
                     ? launch_pdl(dec_embed_kernel<true>, dim3((d.dim + 255) / 256), dim3(256), st, false, m->x,
-                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab, 0)
+                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab, 0, 0)
                     : launch_pdl(dec_embed_kernel<false>, dim3((d.dim + 255) / 256), dim3(256), st, false, m->x,
-                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab, 0));
+                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab, 0, 0));
     const size_t kv_layer = (size_t)d.max_seq * m->kv_dim;
     const size_t kv_es = d.kv_f16 ? 2 : 4;
     const float sqrt_hd = sqrtf((float)hd);
@@ -502,11 +631,11 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
         if (d.kv_f16)
             ok = ok && launch_pdl(dec_rope_append_kernel<__half>, dim3(heads), dim3(hd / 2), st, pdl, m->qkv,
                                   (__half *)kc, (__half *)vc, (const int *)m->d_pos, hd, d.n_heads, d.n_kv_heads,
-                                  d.rope_base, (size_t)0, (size_t)0);
+                                  d.rope_base, (size_t)0, (size_t)0, 0);
         else
             ok = ok && launch_pdl(dec_rope_append_kernel<float>, dim3(heads), dim3(hd / 2), st, pdl, m->qkv,
                                   (float *)kc, (float *)vc, (const int *)m->d_pos, hd, d.n_heads, d.n_kv_heads,
-                                  d.rope_base, (size_t)0, (size_t)0);
+                                  d.rope_base, (size_t)0, (size_t)0, 0);
         const int group = d.n_heads / d.n_kv_heads;
         const dim3 ag(d.n_heads, m->max_splits);
 #define HOLO_ATTN(KVT, HDV)                                                                                   \
@@ -554,42 +683,64 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
 // One position of all `batch` sequences (llm_forward per sequence, llm.c
 // 1015-1269): mode 0 the prompt step (no logits), 1 with the logits, 2 with
 // the logits and the sampler of every sequence (llm_sample, llm.c:1281-1328).
-bool enqueue_batch_step(HoloModel *m, cudaStream_t st, int mode, const SampleArgs &sa) {
+// the layers over M activation rows: `batch` sequences in lockstep (pos_inc
+// 0, caches kv_bs apart, split attention) or M consecutive prompt positions of
+// one sequence (pos_inc 1, one cache, the prompt attention kernel)
+struct RowPass {
+    int M = 0, pos_inc = 0, seq_bs = 0;
+    float *x = nullptr, *xn = nullptr, *qkv = nullptr, *att = nullptr, *t = nullptr, *hh = nullptr, *h = nullptr,
+          *part = nullptr;
+    void *kc = nullptr, *vc = nullptr;
+    size_t kv_bs = 0;
+    const int *seq = nullptr, *pos = nullptr;
+    void *scratch = nullptr;
+    size_t scratch_bytes = 0;
+};
+
+bool rows_norm(const RowPass &p, const float *w, int dim, float eps, cudaStream_t st) {
+    bt_rmsnorm_kernel<<<p.M, 1024, 0, st>>>(p.xn, p.x, w, dim, eps);
+    return holo_check_launch("rows: rmsnorm");
+}
+
+bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
     const holo_model_desc &d = m->d;
-    const int B = m->batch, hd = d.head_dim, S = d.max_seq + 1;
+    const int M = p.M, hd = d.head_dim;
     const int qkv_dim = m->q_dim + 2 * m->kv_dim;
-    const size_t kv_layer = (size_t)d.max_seq * m->kv_dim, kv_bs = (size_t)d.n_layers * kv_layer;
+    const size_t kv_layer = (size_t)d.max_seq * m->kv_dim;
     const size_t part_bs = (size_t)d.n_heads * m->max_splits * (hd + 2);
     const float sqrt_hd = sqrtf((float)hd);
     const int group = d.n_heads / d.n_kv_heads;
     bool ok = d.emb_type == 1
-                  ? launch_pdl(dec_embed_kernel<true>, dim3((d.dim + 255) / 256, B), dim3(256), st, false, m->bx,
-                               (const void *)m->emb, (const int *)m->bseq, (const int *)m->bpos, d.dim, d.vocab, S)
-                  : launch_pdl(dec_embed_kernel<false>, dim3((d.dim + 255) / 256, B), dim3(256), st, false, m->bx,
-                               (const void *)m->emb, (const int *)m->bseq, (const int *)m->bpos, d.dim, d.vocab, S);
-    auto norm = [&](const float *w) {
-        bt_rmsnorm_kernel<<<B, 1024, 0, st>>>(m->bxn, m->bx, w, d.dim, d.eps);
-        return holo_check_launch("batched rmsnorm");
-    };
+                  ? launch_pdl(dec_embed_kernel<true>, dim3((d.dim + 255) / 256, M), dim3(256), st, false, p.x,
+                               (const void *)m->emb, p.seq, p.pos, d.dim, d.vocab, p.seq_bs, p.pos_inc)
+                  : launch_pdl(dec_embed_kernel<false>, dim3((d.dim + 255) / 256, M), dim3(256), st, false, p.x,
+                               (const void *)m->emb, p.seq, p.pos, d.dim, d.vocab, p.seq_bs, p.pos_inc);
     auto add = [&](const float *t) {
-        const long long n = (long long)B * d.dim;
-        bt_add_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 1024), 256, 0, st>>>(m->bx, t, n);
-        return holo_check_launch("batched residual");
+        const long long n = (long long)M * d.dim;
+        bt_add_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 1024), 256, 0, st>>>(p.x, t, n);
+        return holo_check_launch("rows: residual");
     };
+    const int qt = std::max(1, PA_ROWS / group);
     for (int l = 0; l < d.n_layers && ok; ++l) {
         HoloLayer &L = m->layers[l];
-        ok = norm(L.attn_norm) && holo_matmul_batched(m->bqkv, L.wqkv, L.i_qkv, m->bxn, B, st, m->bscratch, m->bscratch_bytes);
+        ok = rows_norm(p, L.attn_norm, d.dim, d.eps, st) &&
+             holo_matmul_batched(p.qkv, L.wqkv, L.i_qkv, p.xn, M, st, p.scratch, p.scratch_bytes);
         const size_t es = d.kv_f16 ? 2 : 4;
-        uint8_t *kc = (uint8_t *)m->bkc + (size_t)l * kv_layer * es, *vc = (uint8_t *)m->bvc + (size_t)l * kv_layer * es;
-        const dim3 rg(std::max(d.n_heads, d.n_kv_heads), B), ag(d.n_heads, m->max_splits, B), mg(d.n_heads, B);
+        uint8_t *kc = (uint8_t *)p.kc + (size_t)l * kv_layer * es, *vc = (uint8_t *)p.vc + (size_t)l * kv_layer * es;
+        const dim3 rg(std::max(d.n_heads, d.n_kv_heads), M), ag(d.n_heads, m->max_splits, M), mg(d.n_heads, M);
+        const dim3 pg(d.n_kv_heads, (M + qt - 1) / qt);
 #define BT_ATTN(KVT, HDV)                                                                                          \
-    launch_pdl(dec_rope_append_kernel<KVT>, rg, dim3(hd / 2), st, false, m->bqkv, (KVT *)kc, (KVT *)vc,             \
-               (const int *)m->bpos, hd, d.n_heads, d.n_kv_heads, d.rope_base, (size_t)qkv_dim, kv_bs) &&          \
-        launch_pdl(dec_attn_split_kernel<KVT, HDV>, ag, dim3(AT_WARPS * 32), st, false, m->bpart,                 \
-                   (const float *)m->bqkv, (const KVT *)kc, (const KVT *)vc, (const int *)m->bpos, m->kv_dim, group, \
-                   m->per_split, m->max_splits, sqrt_hd, (size_t)qkv_dim, kv_bs, part_bs) &&                       \
-        launch_pdl(dec_attn_merge_kernel<HDV>, mg, dim3(HDV), st, false, m->batt, (const float *)m->bpart,         \
-                   (const int *)m->bpos, m->per_split, m->max_splits, (size_t)m->q_dim, part_bs)
+    launch_pdl(dec_rope_append_kernel<KVT>, rg, dim3(hd / 2), st, false, p.qkv, (KVT *)kc, (KVT *)vc, p.pos, hd,     \
+               d.n_heads, d.n_kv_heads, d.rope_base, (size_t)qkv_dim, p.kv_bs, p.pos_inc) &&                        \
+        (p.pos_inc ? launch_pdl_smem(pf_attn_kernel<KVT, HDV>, pg, dim3(PA_WARPS * 32), pa_smem(HDV), st, false,     \
+                                     p.att, (const float *)p.qkv, (const KVT *)kc, (const KVT *)vc, p.pos, M, qt,   \
+                                     group, m->kv_dim, (size_t)qkv_dim, (size_t)m->q_dim, sqrt_hd)                  \
+                   : launch_pdl(dec_attn_split_kernel<KVT, HDV>, ag, dim3(AT_WARPS * 32), st, false, p.part,        \
+                                (const float *)p.qkv, (const KVT *)kc, (const KVT *)vc, p.pos, m->kv_dim, group,    \
+                                m->per_split, m->max_splits, sqrt_hd, (size_t)qkv_dim, p.kv_bs, part_bs) &&         \
+                         launch_pdl(dec_attn_merge_kernel<HDV>, mg, dim3(HDV), st, false, p.att,                    \
+                                    (const float *)p.part, p.pos, m->per_split, m->max_splits, (size_t)m->q_dim,    \
+                                    part_bs))
         if (d.kv_f16) {
             if (hd == 64) ok = ok && BT_ATTN(__half, 64);
             else if (hd == 128) ok = ok && BT_ATTN(__half, 128);
@@ -600,16 +751,33 @@ bool enqueue_batch_step(HoloModel *m, cudaStream_t st, int mode, const SampleArg
             else ok = ok && BT_ATTN(float, 256);
         }
 #undef BT_ATTN
-        ok = ok && holo_matmul_batched(m->bt, L.wo, L.i_o, m->batt, B, st, m->bscratch, m->bscratch_bytes) && add(m->bt);
-        ok = ok && norm(L.ffn_norm) && holo_matmul_batched(m->bhh, L.w13, L.i_13, m->bxn, B, st, m->bscratch, m->bscratch_bytes);
+        ok = ok && holo_matmul_batched(p.t, L.wo, L.i_o, p.att, M, st, p.scratch, p.scratch_bytes) && add(p.t);
+        ok = ok && rows_norm(p, L.ffn_norm, d.dim, d.eps, st) &&
+             holo_matmul_batched(p.hh, L.w13, L.i_13, p.xn, M, st, p.scratch, p.scratch_bytes);
         if (ok) {
-            const long long n = (long long)B * d.ffn_dim;
-            bt_swiglu_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 2048), 256, 0, st>>>(m->bh, m->bhh,
-                                                                                                d.ffn_dim, n);
-            ok = holo_check_launch("batched swiglu");
+            const long long n = (long long)M * d.ffn_dim;
+            bt_swiglu_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 2048), 256, 0, st>>>(p.h, p.hh,
+                                                                                               d.ffn_dim, n);
+            ok = holo_check_launch("rows: swiglu");
         }
-        ok = ok && holo_matmul_batched(m->bt, L.w2, L.i_2, m->bh, B, st, m->bscratch, m->bscratch_bytes) && add(m->bt);
+        ok = ok && holo_matmul_batched(p.t, L.w2, L.i_2, p.h, M, st, p.scratch, p.scratch_bytes) && add(p.t);
     }
+    return ok;
+}
+
+bool enqueue_batch_step(HoloModel *m, cudaStream_t st, int mode, const SampleArgs &sa) {
+    const holo_model_desc &d = m->d;
+    const int B = m->batch, S = d.max_seq + 1;
+    RowPass p;
+    p.M = B;
+    p.x = m->bx; p.xn = m->bxn; p.qkv = m->bqkv; p.att = m->batt; p.t = m->bt; p.hh = m->bhh; p.h = m->bh;
+    p.part = m->bpart;
+    p.kc = m->bkc; p.vc = m->bvc;
+    p.kv_bs = (size_t)d.n_layers * d.max_seq * m->kv_dim;
+    p.seq = m->bseq; p.seq_bs = S; p.pos = m->bpos;
+    p.scratch = m->bscratch; p.scratch_bytes = m->bscratch_bytes;
+    bool ok = enqueue_rows(m, st, p);
+    auto norm = [&](const float *w) { return rows_norm(p, w, d.dim, d.eps, st); };
     if (mode >= 1)
         ok = ok && norm(m->final_norm) && holo_matmul_batched(m->blogits, m->out, m->i_out, m->bxn, B, st, m->bscratch, m->bscratch_bytes);
     if (mode == 2) {
@@ -675,6 +843,99 @@ bool run_batch_step(HoloModel *m, int mode, const SampleArgs &sa, cudaStream_t s
         return true;   // the plain run above was this step
     }
     if (cudaGraphLaunch(m->g_bstep[mode], st) != cudaSuccess) return holo_check_launch("batched step launch");
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// prompt passes: the positions of a prompt before its last token need no
+// logits, and each layer's projections over all of them are one tensor-core
+// matmul (M = positions) instead of one matvec per position.  One GPU, one
+// sequence, Q8 activations (the matmul quantizes its input rows exactly as
+// the matvecs do); otherwise prompts go one position a step.
+// ---------------------------------------------------------------------------
+constexpr int PROMPT_CAP = 512;   // positions a pass (longer prompts: several passes)
+
+bool prompt_supported(const HoloModel *m) {
+    const holo_model_desc &d = m->d;
+    if (m->prompt_mode != 1 || m->world != 1 || m->batch != 1 || d.act_mode != HOLO_ACT_Q8) return false;
+    if (d.n_heads / d.n_kv_heads > PA_ROWS || (d.head_dim != 64 && d.head_dim != 128 && d.head_dim != 256))
+        return false;
+    for (const HoloLayer &L : m->layers)
+        for (const WeightInfo *wi : {&L.i_qkv, &L.i_o, &L.i_13, &L.i_2})
+            if (wi->rows % PF_ROWS_ALIGN ||
+                (wi->type != GT_Q4_K && wi->type != GT_Q4_0 && wi->type != GT_Q8_0))
+                return false;
+    return true;
+}
+
+// buffers for passes of up to `rows` positions (grown on demand)
+bool prompt_buffers(HoloModel *m, int rows) {
+    const holo_model_desc &d = m->d;
+    size_t need = 0;
+    for (const HoloLayer &L : m->layers)
+        for (const WeightInfo *wi : {&L.i_qkv, &L.i_o, &L.i_13, &L.i_2})
+            need = std::max(need, holo_matmul_batched_scratch(*wi, rows));
+    if (need > m->rscratch_bytes) {
+        cudaFree(m->rscratch);
+        m->rscratch = nullptr;
+        m->rscratch_bytes = 0;
+        if (!dev_alloc(&m->rscratch, need)) return false;
+        m->rscratch_bytes = need;
+    }
+    if (rows <= m->r_cap) return true;
+    for (float *p : {m->rx, m->rxn, m->rqkv, m->ratt, m->rt, m->rhh, m->rh}) cudaFree(p);
+    m->r_cap = 0;
+    const size_t R = rows;
+    bool ok = dev_alloc((void **)&m->rx, sizeof(float) * R * d.dim) &&
+              dev_alloc((void **)&m->rxn, sizeof(float) * R * d.dim) &&
+              dev_alloc((void **)&m->rqkv, sizeof(float) * R * (m->q_dim + 2 * m->kv_dim)) &&
+              dev_alloc((void **)&m->ratt, sizeof(float) * R * m->q_dim) &&
+              dev_alloc((void **)&m->rt, sizeof(float) * R * d.dim) &&
+              dev_alloc((void **)&m->rhh, sizeof(float) * R * 2 * d.ffn_dim) &&
+              dev_alloc((void **)&m->rh, sizeof(float) * R * d.ffn_dim);
+    if (!ok) return false;
+    m->r_cap = rows;
+    if (!m->r_attr) {   // the prompt attention's shared memory exceeds the default 48 KB (per device)
+        bool a = true;
+        a = a && cudaFuncSetAttribute(pf_attn_kernel<__half, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)pa_smem(128)) == cudaSuccess;
+        a = a && cudaFuncSetAttribute(pf_attn_kernel<float, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)pa_smem(128)) == cudaSuccess;
+        a = a && cudaFuncSetAttribute(pf_attn_kernel<__half, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)pa_smem(256)) == cudaSuccess;
+        a = a && cudaFuncSetAttribute(pf_attn_kernel<float, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)pa_smem(256)) == cudaSuccess;
+        a = a && cudaFuncSetAttribute(pf_attn_kernel<__half, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)pa_smem(64)) == cudaSuccess;
+        a = a && cudaFuncSetAttribute(pf_attn_kernel<float, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)pa_smem(64)) == cudaSuccess;
+        if (!a) return holo_check_launch("prompt attention attributes");
+        m->r_attr = true;
+    }
+    return true;
+}
+
+// the n positions from the current one (tokens already in d_seq) through the
+// layers, their keys and values appended; the position advances by n.  The
+// last pass's rows stay in rx (the last position's row: last_rows - 1).
+bool prompt_rows(HoloModel *m, cudaStream_t st, int n, int *last_rows) {
+    const int cap = std::min(n, PROMPT_CAP);
+    if (!prompt_buffers(m, cap)) return false;
+    for (int done = 0; done < n;) {
+        const int c = std::min(cap, n - done);
+        RowPass p;
+        p.M = c;
+        p.pos_inc = 1;
+        p.x = m->rx; p.xn = m->rxn; p.qkv = m->rqkv; p.att = m->ratt; p.t = m->rt; p.hh = m->rhh; p.h = m->rh;
+        p.kc = m->kc; p.vc = m->vc;
+        p.seq = m->d_seq; p.pos = m->d_pos;
+        p.scratch = m->rscratch; p.scratch_bytes = m->rscratch_bytes;
+        if (!enqueue_rows(m, st, p)) return false;
+        dec_pos_add_kernel<<<1, 32, 0, st>>>(m->d_pos, c);
+        if (!holo_check_launch("prompt: position")) return false;
+        done += c;
+        if (last_rows) *last_rows = c;
+    }
     return true;
 }
 
@@ -1158,6 +1419,56 @@ int holo_model_forward(void *model, int token, float *logits) {
     return cuda_last_status();
 }
 
+int holo_model_prefill(void *model, const int *tokens, int n, float *logits) {
+    HoloModel *m = (HoloModel *)model;
+    if (!model_ready(m)) return HOLO_E_ARG;
+    if (!tokens || n <= 0 || m->h_pos + n > m->d.max_seq) {
+        holo_set_status(HOLO_E_ARG, "holo_model_prefill: no tokens or past max_seq");
+        return HOLO_E_ARG;
+    }
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= m->d.vocab) {
+            holo_set_status(HOLO_E_ARG, "holo_model_prefill: token out of range");
+            return HOLO_E_ARG;
+        }
+    if (!prompt_supported(m)) {
+        holo_set_status(HOLO_E_UNSUPPORTED, "holo_model_prefill: row passes need one GPU, batch 1, HOLO_ACT_Q8, "
+                                            "Q8_0/Q4_0/Q4_K layers of 128-row multiples, head_dim 64/128/256");
+        return HOLO_E_UNSUPPORTED;
+    }
+    cudaStream_t st = holo_stream();
+    if (cudaMemcpyAsync(m->d_seq + m->h_pos, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return holo_check_launch("holo_model_prefill: tokens") ? HOLO_OK : cuda_last_status();
+    int last = 0;
+    if (!prompt_rows(m, st, n, &last)) return cuda_last_status() ? cuda_last_status() : HOLO_E_ARG;
+    m->h_pos += n;
+    if (logits) {
+        // the last position's logits: final RMSNorm fused into the output matvec
+        MvLaunch a;
+        a.x = m->rx + (size_t)(last - 1) * m->d.dim;
+        a.y = m->logits;
+        a.norm_w = m->final_norm;
+        a.eps = m->d.eps;
+        a.act = m->d.act_mode;
+        a.epi = MV_EPI_STORE;
+        if (!holo_matvec_launch(m->out, m->i_out, a, st)) return cuda_last_status();
+        if (cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->d.vocab, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            holo_check_launch("holo_model_prefill: logits copy");
+    }
+    cudaStreamSynchronize(st);
+    return cuda_last_status();
+}
+
+int holo_model_set_prompt_mode(void *model, int rows) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m || (rows != 0 && rows != 1)) {
+        holo_set_status(HOLO_E_ARG, "holo_model_set_prompt_mode: mode 0 or 1");
+        return HOLO_E_ARG;
+    }
+    m->prompt_mode = rows;
+    return HOLO_OK;
+}
+
 int holo_model_load_logits(void *model, const float *logits) {
     HoloModel *m = (HoloModel *)model;
     if (!m || !logits) {
@@ -1235,10 +1546,15 @@ int holo_model_generate(void *model, const int *prompt, int n_prompt, int n_new,
     a.gen = 1;
     a.n_prompt = n_prompt;
     const int steps = n_prompt + n_new - 1;
+    // the prompt before its last token in row passes where supported; the
+    // steps then start at the last prompt token
+    const bool rows = n_prompt > 1 && prompt_supported(m);
+    const int first = rows ? n_prompt - 1 : 0;
     if (m->use_step) {
         m->gen_args = a;
         cudaEventRecord(m->ev[0], st);
-        for (int i = 0; i < steps; ++i) {
+        if (rows && !prompt_rows(m, st, n_prompt - 1, nullptr)) return -1;
+        for (int i = first; i < steps; ++i) {
             if (i == n_prompt - 1) cudaEventRecord(m->ev[1], st);
             if (!run_step(m, true, a, st)) return -1;
         }
@@ -1263,7 +1579,8 @@ int holo_model_generate(void *model, const int *prompt, int n_prompt, int n_new,
     // steps 0 .. n_prompt-2 are prefill; each later step forwards one position
     // and samples one token (the first forwards the last prompt token)
     cudaEventRecord(m->ev[0], st);
-    for (int i = 0; i < steps; ++i) {
+    if (rows && !prompt_rows(m, st, n_prompt - 1, nullptr)) return -1;
+    for (int i = first; i < steps; ++i) {
         if (i == n_prompt - 1) cudaEventRecord(m->ev[1], st);
         if (cudaGraphLaunch(m->g_gen, st) != cudaSuccess) {
             holo_check_launch("holo_model_generate: graph launch");
@@ -1500,6 +1817,8 @@ void holo_model_free(void *model) {
     void *bbufs[] = {m->bx, m->bxn, m->bqkv, m->batt, m->bt, m->bhh, m->bh, m->blogits, m->bpart, m->brvals,
                      m->bkc, m->bvc, m->bseq, m->bhist, m->bout, m->bnhist, m->blast, m->bpos, m->bscratch};
     for (void *p : bbufs) cudaFree(p);
+    void *rbufs[] = {m->rx, m->rxn, m->rqkv, m->ratt, m->rt, m->rhh, m->rh, m->rscratch};
+    for (void *p : rbufs) cudaFree(p);
     void *bufs[] = {m->emb, m->final_norm, m->out, m->kc, m->vc, m->comm, m->qkv_ll, m->x, m->qkv, m->att,
                     m->h, m->logits, m->part, m->probs, m->kept_p, m->rvals, m->kept_idx, m->d_pos, m->d_seq, m->d_hist,
                     m->d_nhist, m->d_out, m->d_last, m->d_layers, m->d_pf, m->d_bar, m->d_att_cnt};

@@ -155,6 +155,8 @@ WeightInfo holo_weight_info(int ggml_type, int rows, int cols, int q4k_layout);
 bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st,
                          void *scratch, size_t scratch_bytes);
 size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M);
+// the batched matmul's weights: rows a multiple of this (one MMA tile)
+constexpr int PF_ROWS_ALIGN = 128;
 bool holo_repack_to(void *dst, const void *dev_blocks, int ggml_type, int rows, int cols, int q4k_layout,
                     cudaStream_t st);
 void holo_registry_add(const void *ptr, const WeightInfo &info);

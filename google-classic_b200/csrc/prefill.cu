@@ -31,6 +31,7 @@ namespace {
 using namespace holo_mv;
 
 constexpr int PF_BM = 128;                         // weight rows per CTA (MMA M)
+static_assert(PF_BM == PF_ROWS_ALIGN, "row tile");
 constexpr int PF_BK = 128;                         // K per stage: two 128-byte atoms of fp16
 constexpr int PF_MAX_AST = 3;                      // dequantized weight stages, at most
 constexpr int PF_DQ_WARPS = 16;                    // dequantize, then read the accumulators

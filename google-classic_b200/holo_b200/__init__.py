@@ -90,6 +90,8 @@ SIGNATURES = {
     "holo_model_set_layer": (_i, [_vp, _i] + [_vp] * 9),
     "holo_model_set_globals": (_i, [_vp, _vp, _vp, _vp]),
     "holo_model_forward": (_i, [_vp, _i, _vp]),
+    "holo_model_prefill": (_i, [_vp, _vp, _i, _vp]),
+    "holo_model_set_prompt_mode": (_i, [_vp, _i]),
     "holo_model_load_logits": (_i, [_vp, _vp]),
     "holo_model_push_token": (_i, [_vp, _i]),
     "holo_model_sample": (_i, [_vp, _vp, _f]),

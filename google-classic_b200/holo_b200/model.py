@@ -74,6 +74,19 @@ class Model:
         self._check("holo_model_forward", rc == HOLO_OK)
         return out
 
+    def prefill(self, tokens, want_logits: bool = True) -> np.ndarray | None:
+        """Prompt pass over tokens at the next positions (row passes on the
+        tensor cores); the last position's logits."""
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty(self.cfg["vocab"], np.float32) if want_logits else None
+        rc = self.lib.holo_model_prefill(self.h, _ptr(tokens), len(tokens), _ptr(out) if want_logits else None)
+        self._check("holo_model_prefill", rc == HOLO_OK)
+        return out
+
+    def set_prompt_mode(self, rows: bool):
+        """generate's prompt: row passes (True, the default) or one position a step."""
+        self._check("holo_model_set_prompt_mode", self.lib.holo_model_set_prompt_mode(self.h, int(bool(rows))) == HOLO_OK)
+
     def load_logits(self, logits: np.ndarray):
         logits = np.ascontiguousarray(logits, np.float32)
         self._check("holo_model_load_logits", self.lib.holo_model_load_logits(self.h, _ptr(logits)) == HOLO_OK)
