@@ -47,19 +47,20 @@ template <> __device__ __forceinline__ float to_kv<float>(float v) { return v; }
 template <> __device__ __forceinline__ __half to_kv<__half>(float v) { return __float2half_rn(v); }
 
 // ---------------------------------------------------------------------------
-// embedding row of the token at pos (F32 copy, F16 exact widening); several
-// rows: row blockIdx.y, its token list seq_bs ints after the previous one, at
-// pos + blockIdx.y * pos_inc (batched sequences: pos_inc 0; consecutive
-// prompt positions: seq_bs 0, pos_inc 1)
+// embedding row of the token at pos (F32 copy, F16 exact widening).  Several
+// rows: row blockIdx.y = b * rps + i is position pos + i of sequence b, whose
+// token list starts seq_bs ints after sequence b-1's (batched decode: rps 1;
+// prompt passes: rps positions a sequence)
 // ---------------------------------------------------------------------------
 template <bool F16>
 __global__ void dec_embed_kernel(float *__restrict__ x, const void *__restrict__ emb, const int *__restrict__ seq,
-                                 const int *__restrict__ pos_p, int dim, int vocab, int seq_bs, int pos_inc) {
+                                 const int *__restrict__ pos_p, int dim, int vocab, int seq_bs, int rps) {
     dec_pdl_trigger();
     dec_pdl_wait();
-    seq += (size_t)blockIdx.y * seq_bs;
-    x += (size_t)blockIdx.y * dim;
-    const int tok = seq[*pos_p + (int)blockIdx.y * pos_inc];
+    const int r = blockIdx.y, b = r / rps;
+    seq += (size_t)b * seq_bs;
+    x += (size_t)r * dim;
+    const int tok = seq[*pos_p + (r - b * rps)];
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= dim) return;
     if (tok < 0 || tok >= vocab) {
@@ -72,20 +73,21 @@ __global__ void dec_embed_kernel(float *__restrict__ x, const void *__restrict__
 
 // ---------------------------------------------------------------------------
 // RoPE of q (n_heads) and k (n_kv_heads) at pos, then k and v appended to the
-// layer's cache; one CTA per head, one thread per rotation pair; several rows:
-// row blockIdx.y, qkv_bs floats and kv_bs cache elements apart, at pos +
-// blockIdx.y * pos_inc
+// layer's cache; one CTA per head, one thread per rotation pair.  Several
+// rows: row blockIdx.y = b * rps + i (qkv_bs floats apart) is position pos + i
+// of sequence b, whose cache starts kv_bs elements after sequence b-1's
 // ---------------------------------------------------------------------------
 template <typename KV>
 __global__ void dec_rope_append_kernel(float *__restrict__ qkv, KV *__restrict__ kc, KV *__restrict__ vc,
                                        const int *__restrict__ pos_p, int hd, int n_heads, int n_kv_heads,
-                                       float base, size_t qkv_bs, size_t kv_bs, int pos_inc) {
+                                       float base, size_t qkv_bs, size_t kv_bs, int rps) {
     dec_pdl_trigger();
     dec_pdl_wait();
-    qkv += blockIdx.y * qkv_bs;
-    kc += blockIdx.y * kv_bs;
-    vc += blockIdx.y * kv_bs;
-    const int pos = *pos_p + (int)blockIdx.y * pos_inc;
+    const int r = blockIdx.y, b = r / rps;
+    qkv += r * qkv_bs;
+    kc += b * kv_bs;
+    vc += b * kv_bs;
+    const int pos = *pos_p + (r - b * rps);
     const int h = blockIdx.x, i = threadIdx.x, half = hd / 2;
     if (i >= half) return;
     const int q_dim = n_heads * hd, kv_dim = n_kv_heads * hd;
@@ -263,9 +265,10 @@ __global__ void dec_attn_merge_kernel(float *__restrict__ att, const float *__re
 }
 
 // ---------------------------------------------------------------------------
-// prompt attention: the M consecutive positions p0 .. p0+M-1 of one sequence
-// (p0 = *pos_p), each attending to cache positions 0 .. its own, whose keys
-// and values are already appended (llm.c:1180-1200: score = q.k / sqrtf(hd),
+// prompt attention: the M consecutive positions p0 .. p0+M-1 (p0 = *pos_p) of
+// sequence blockIdx.z (its rows from z * M, its cache kv_bs elements after the
+// previous sequence's), each attending to cache positions 0 .. its own, whose
+// keys and values are already appended (llm.c:1180-1200: score = q.k / sqrtf(hd),
 // softmax over the positions, sum of p * v; here with an online softmax, as
 // in the decode kernels).  CTA: KV head blockIdx.x and query tokens
 // [blockIdx.y * qt, +qt) x the group's query heads: up to PA_ROWS rows, two
@@ -287,8 +290,12 @@ template <typename KV, int HD>
 __global__ void __launch_bounds__(PA_WARPS * 32)
 pf_attn_kernel(float *__restrict__ att, const float *__restrict__ qkv, const KV *__restrict__ kc,
                const KV *__restrict__ vc, const int *__restrict__ pos_p, int M, int qt, int group, int kv_dim,
-               size_t qkv_bs, size_t att_bs, float sqrt_hd) {
+               size_t qkv_bs, size_t att_bs, size_t kv_bs, float sqrt_hd) {
     constexpr int DPL = HD / 32, KS = PA_KT + 1;
+    qkv += (size_t)blockIdx.z * M * qkv_bs;
+    att += (size_t)blockIdx.z * M * att_bs;
+    kc += blockIdx.z * kv_bs;
+    vc += blockIdx.z * kv_bs;
     extern __shared__ float pa_sm[];
     float *kt = pa_sm;                 // [HD][KS]: keys, transposed
     float *vs = kt + HD * KS;          // [PA_KT][HD]
@@ -613,9 +620,9 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
     // the step's first kernel follows whatever precedes the graph in full
     ok = ok && (d.emb_type == 1
                     ? launch_pdl(dec_embed_kernel<true>, dim3((d.dim + 255) / 256), dim3(256), st, false, m->x,
-                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab, 0, 0)
+                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab, 0, 1)
                     : launch_pdl(dec_embed_kernel<false>, dim3((d.dim + 255) / 256), dim3(256), st, false, m->x,
-                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab, 0, 0));
+                                 (const void *)m->emb, (const int *)m->d_seq, (const int *)m->d_pos, d.dim, d.vocab, 0, 1));
     const size_t kv_layer = (size_t)d.max_seq * m->kv_dim;
     const size_t kv_es = d.kv_f16 ? 2 : 4;
     const float sqrt_hd = sqrtf((float)hd);
@@ -631,11 +638,11 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
         if (d.kv_f16)
             ok = ok && launch_pdl(dec_rope_append_kernel<__half>, dim3(heads), dim3(hd / 2), st, pdl, m->qkv,
                                   (__half *)kc, (__half *)vc, (const int *)m->d_pos, hd, d.n_heads, d.n_kv_heads,
-                                  d.rope_base, (size_t)0, (size_t)0, 0);
+                                  d.rope_base, (size_t)0, (size_t)0, 1);
         else
             ok = ok && launch_pdl(dec_rope_append_kernel<float>, dim3(heads), dim3(hd / 2), st, pdl, m->qkv,
                                   (float *)kc, (float *)vc, (const int *)m->d_pos, hd, d.n_heads, d.n_kv_heads,
-                                  d.rope_base, (size_t)0, (size_t)0, 0);
+                                  d.rope_base, (size_t)0, (size_t)0, 1);
         const int group = d.n_heads / d.n_kv_heads;
         const dim3 ag(d.n_heads, m->max_splits);
 #define HOLO_ATTN(KVT, HDV)                                                                                   \
@@ -683,11 +690,13 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
 // One position of all `batch` sequences (llm_forward per sequence, llm.c
 // 1015-1269): mode 0 the prompt step (no logits), 1 with the logits, 2 with
 // the logits and the sampler of every sequence (llm_sample, llm.c:1281-1328).
-// the layers over M activation rows: `batch` sequences in lockstep (pos_inc
-// 0, caches kv_bs apart, split attention) or M consecutive prompt positions of
-// one sequence (pos_inc 1, one cache, the prompt attention kernel)
+// the layers over M activation rows: row b * rps + i is position pos + i of
+// sequence b (token lists seq_bs ints apart, caches kv_bs elements apart).
+// Batched decode: one position a sequence (rps 1), split attention; prompt
+// passes: rps consecutive positions a sequence, the prompt attention kernel.
 struct RowPass {
-    int M = 0, pos_inc = 0, seq_bs = 0;
+    int M = 0, rps = 1, seq_bs = 0;
+    bool prompt = false;
     float *x = nullptr, *xn = nullptr, *qkv = nullptr, *att = nullptr, *t = nullptr, *hh = nullptr, *h = nullptr,
           *part = nullptr;
     void *kc = nullptr, *vc = nullptr;
@@ -712,9 +721,9 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
     const int group = d.n_heads / d.n_kv_heads;
     bool ok = d.emb_type == 1
                   ? launch_pdl(dec_embed_kernel<true>, dim3((d.dim + 255) / 256, M), dim3(256), st, false, p.x,
-                               (const void *)m->emb, p.seq, p.pos, d.dim, d.vocab, p.seq_bs, p.pos_inc)
+                               (const void *)m->emb, p.seq, p.pos, d.dim, d.vocab, p.seq_bs, p.rps)
                   : launch_pdl(dec_embed_kernel<false>, dim3((d.dim + 255) / 256, M), dim3(256), st, false, p.x,
-                               (const void *)m->emb, p.seq, p.pos, d.dim, d.vocab, p.seq_bs, p.pos_inc);
+                               (const void *)m->emb, p.seq, p.pos, d.dim, d.vocab, p.seq_bs, p.rps);
     auto add = [&](const float *t) {
         const long long n = (long long)M * d.dim;
         bt_add_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 1024), 256, 0, st>>>(p.x, t, n);
@@ -728,13 +737,13 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
         const size_t es = d.kv_f16 ? 2 : 4;
         uint8_t *kc = (uint8_t *)p.kc + (size_t)l * kv_layer * es, *vc = (uint8_t *)p.vc + (size_t)l * kv_layer * es;
         const dim3 rg(std::max(d.n_heads, d.n_kv_heads), M), ag(d.n_heads, m->max_splits, M), mg(d.n_heads, M);
-        const dim3 pg(d.n_kv_heads, (M + qt - 1) / qt);
+        const dim3 pg(d.n_kv_heads, (p.rps + qt - 1) / qt, M / p.rps);
 #define BT_ATTN(KVT, HDV)                                                                                          \
     launch_pdl(dec_rope_append_kernel<KVT>, rg, dim3(hd / 2), st, false, p.qkv, (KVT *)kc, (KVT *)vc, p.pos, hd,     \
-               d.n_heads, d.n_kv_heads, d.rope_base, (size_t)qkv_dim, p.kv_bs, p.pos_inc) &&                        \
-        (p.pos_inc ? launch_pdl_smem(pf_attn_kernel<KVT, HDV>, pg, dim3(PA_WARPS * 32), pa_smem(HDV), st, false,     \
-                                     p.att, (const float *)p.qkv, (const KVT *)kc, (const KVT *)vc, p.pos, M, qt,   \
-                                     group, m->kv_dim, (size_t)qkv_dim, (size_t)m->q_dim, sqrt_hd)                  \
+               d.n_heads, d.n_kv_heads, d.rope_base, (size_t)qkv_dim, p.kv_bs, p.rps) &&                            \
+        (p.prompt ? launch_pdl_smem(pf_attn_kernel<KVT, HDV>, pg, dim3(PA_WARPS * 32), pa_smem(HDV), st, false,      \
+                                    p.att, (const float *)p.qkv, (const KVT *)kc, (const KVT *)vc, p.pos, p.rps, qt, \
+                                    group, m->kv_dim, (size_t)qkv_dim, (size_t)m->q_dim, p.kv_bs, sqrt_hd)          \
                    : launch_pdl(dec_attn_split_kernel<KVT, HDV>, ag, dim3(AT_WARPS * 32), st, false, p.part,        \
                                 (const float *)p.qkv, (const KVT *)kc, (const KVT *)vc, p.pos, m->kv_dim, group,    \
                                 m->per_split, m->max_splits, sqrt_hd, (size_t)qkv_dim, p.kv_bs, part_bs) &&         \
@@ -848,16 +857,17 @@ bool run_batch_step(HoloModel *m, int mode, const SampleArgs &sa, cudaStream_t s
 
 // ---------------------------------------------------------------------------
 // prompt passes: the positions of a prompt before its last token need no
-// logits, and each layer's projections over all of them are one tensor-core
-// matmul (M = positions) instead of one matvec per position.  One GPU, one
-// sequence, Q8 activations (the matmul quantizes its input rows exactly as
-// the matvecs do); otherwise prompts go one position a step.
+// logits, and each layer's projections over all of them (of every sequence of
+// a batched model) are one tensor-core matmul instead of one matvec, or one
+// M = batch matmul, per position.  One GPU; batch 1 with Q8 activations (the
+// matmul quantizes its input rows as the matvecs do); otherwise prompts go one
+// position a step.
 // ---------------------------------------------------------------------------
-constexpr int PROMPT_CAP = 512;   // positions a pass (longer prompts: several passes)
+constexpr int PROMPT_ROWS = 1024;   // rows a pass (longer prompts: several passes)
 
 bool prompt_supported(const HoloModel *m) {
     const holo_model_desc &d = m->d;
-    if (m->prompt_mode != 1 || m->world != 1 || m->batch != 1 || d.act_mode != HOLO_ACT_Q8) return false;
+    if (m->prompt_mode != 1 || m->world != 1 || (m->batch == 1 && d.act_mode != HOLO_ACT_Q8)) return false;
     if (d.n_heads / d.n_kv_heads > PA_ROWS || (d.head_dim != 64 && d.head_dim != 128 && d.head_dim != 256))
         return false;
     for (const HoloLayer &L : m->layers)
@@ -915,23 +925,35 @@ bool prompt_buffers(HoloModel *m, int rows) {
     return true;
 }
 
-// the n positions from the current one (tokens already in d_seq) through the
-// layers, their keys and values appended; the position advances by n.  The
-// last pass's rows stay in rx (the last position's row: last_rows - 1).
+// the n positions from the current one (tokens already in the token lists)
+// of every sequence through the layers, their keys and values appended; the
+// position advances by n.  The last pass's rows stay in rx (batch 1: the last
+// position's row is last_rows - 1).
 bool prompt_rows(HoloModel *m, cudaStream_t st, int n, int *last_rows) {
-    const int cap = std::min(n, PROMPT_CAP);
-    if (!prompt_buffers(m, cap)) return false;
+    const holo_model_desc &d = m->d;
+    const int B = m->batch;
+    const int cap = std::max(1, std::min(n, PROMPT_ROWS / B));   // positions a pass
+    if (!prompt_buffers(m, B * cap)) return false;
+    int *pos = B == 1 ? m->d_pos : m->bpos;
     for (int done = 0; done < n;) {
         const int c = std::min(cap, n - done);
         RowPass p;
-        p.M = c;
-        p.pos_inc = 1;
+        p.M = B * c;
+        p.rps = c;
+        p.prompt = true;
         p.x = m->rx; p.xn = m->rxn; p.qkv = m->rqkv; p.att = m->ratt; p.t = m->rt; p.hh = m->rhh; p.h = m->rh;
-        p.kc = m->kc; p.vc = m->vc;
-        p.seq = m->d_seq; p.pos = m->d_pos;
+        if (B == 1) {
+            p.kc = m->kc; p.vc = m->vc;
+            p.seq = m->d_seq;
+        } else {
+            p.kc = m->bkc; p.vc = m->bvc;
+            p.kv_bs = (size_t)d.n_layers * d.max_seq * m->kv_dim;
+            p.seq = m->bseq; p.seq_bs = d.max_seq + 1;
+        }
+        p.pos = pos;
         p.scratch = m->rscratch; p.scratch_bytes = m->rscratch_bytes;
         if (!enqueue_rows(m, st, p)) return false;
-        dec_pos_add_kernel<<<1, 32, 0, st>>>(m->d_pos, c);
+        dec_pos_add_kernel<<<1, 32, 0, st>>>(pos, c);
         if (!holo_check_launch("prompt: position")) return false;
         done += c;
         if (last_rows) *last_rows = c;
@@ -1422,37 +1444,49 @@ int holo_model_forward(void *model, int token, float *logits) {
 int holo_model_prefill(void *model, const int *tokens, int n, float *logits) {
     HoloModel *m = (HoloModel *)model;
     if (!model_ready(m)) return HOLO_E_ARG;
-    if (!tokens || n <= 0 || m->h_pos + n > m->d.max_seq) {
+    const int B = m->batch, S = m->d.max_seq + 1;
+    int &hpos = B == 1 ? m->h_pos : m->h_bpos;
+    if (!tokens || n <= 0 || hpos + n > m->d.max_seq) {
         holo_set_status(HOLO_E_ARG, "holo_model_prefill: no tokens or past max_seq");
         return HOLO_E_ARG;
     }
-    for (int i = 0; i < n; ++i)
+    for (long long i = 0; i < (long long)B * n; ++i)
         if (tokens[i] < 0 || tokens[i] >= m->d.vocab) {
             holo_set_status(HOLO_E_ARG, "holo_model_prefill: token out of range");
             return HOLO_E_ARG;
         }
     if (!prompt_supported(m)) {
-        holo_set_status(HOLO_E_UNSUPPORTED, "holo_model_prefill: row passes need one GPU, batch 1, HOLO_ACT_Q8, "
-                                            "Q8_0/Q4_0/Q4_K layers of 128-row multiples, head_dim 64/128/256");
+        holo_set_status(HOLO_E_UNSUPPORTED, "holo_model_prefill: row passes need one GPU, HOLO_ACT_Q8 at batch 1, "
+                                            "Q8_0/Q4_0/Q4_K layers of 128-row multiples, head_dim 64/128/256, "
+                                            "n_heads / n_kv_heads <= 16");
         return HOLO_E_UNSUPPORTED;
     }
     cudaStream_t st = holo_stream();
-    if (cudaMemcpyAsync(m->d_seq + m->h_pos, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, st) != cudaSuccess)
-        return holo_check_launch("holo_model_prefill: tokens") ? HOLO_OK : cuda_last_status();
+    const cudaError_t ce =
+        B == 1 ? cudaMemcpyAsync(m->d_seq + hpos, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, st)
+               : cudaMemcpy2DAsync(m->bseq + hpos, sizeof(int) * S, tokens, sizeof(int) * n, sizeof(int) * n, B,
+                                   cudaMemcpyHostToDevice, st);
+    if (ce != cudaSuccess) {
+        holo_check_launch("holo_model_prefill: tokens");
+        return cuda_last_status();
+    }
     int last = 0;
     if (!prompt_rows(m, st, n, &last)) return cuda_last_status() ? cuda_last_status() : HOLO_E_ARG;
-    m->h_pos += n;
+    hpos += n;
     if (logits) {
-        // the last position's logits: final RMSNorm fused into the output matvec
-        MvLaunch a;
-        a.x = m->rx + (size_t)(last - 1) * m->d.dim;
-        a.y = m->logits;
-        a.norm_w = m->final_norm;
-        a.eps = m->d.eps;
-        a.act = m->d.act_mode;
-        a.epi = MV_EPI_STORE;
-        if (!holo_matvec_launch(m->out, m->i_out, a, st)) return cuda_last_status();
-        if (cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->d.vocab, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        // each sequence's last position: final RMSNorm fused into the output matvec
+        float *dst = B == 1 ? m->logits : m->blogits;
+        for (int b = 0; b < B; ++b) {
+            MvLaunch a;
+            a.x = m->rx + ((size_t)b * last + last - 1) * m->d.dim;
+            a.y = dst + (size_t)b * m->d.vocab;
+            a.norm_w = m->final_norm;
+            a.eps = m->d.eps;
+            a.act = m->d.act_mode;
+            a.epi = MV_EPI_STORE;
+            if (!holo_matvec_launch(m->out, m->i_out, a, st)) return cuda_last_status();
+        }
+        if (cudaMemcpyAsync(logits, dst, sizeof(float) * B * m->d.vocab, cudaMemcpyDeviceToHost, st) != cudaSuccess)
             holo_check_launch("holo_model_prefill: logits copy");
     }
     cudaStreamSynchronize(st);
@@ -1695,8 +1729,11 @@ int holo_model_generate_batch(void *model, const int *prompts, int n_prompt, int
     a.n_prompt = n_prompt;
     const int steps = n_prompt + n_new - 1;
     SampleArgs none{};
+    // the prompts before their last token in row passes where supported
+    const bool rows = n_prompt > 1 && prompt_supported(m);
     cudaEventRecord(m->ev[0], st);
-    for (int i = 0; i < steps; ++i) {
+    if (rows && !prompt_rows(m, st, n_prompt - 1, nullptr)) return -1;
+    for (int i = rows ? n_prompt - 1 : 0; i < steps; ++i) {
         if (i == n_prompt - 1) cudaEventRecord(m->ev[1], st);
         if (!run_batch_step(m, i < n_prompt - 1 ? 0 : 2, i < n_prompt - 1 ? none : a, st)) return -1;
     }

@@ -75,11 +75,13 @@ class Model:
         return out
 
     def prefill(self, tokens, want_logits: bool = True) -> np.ndarray | None:
-        """Prompt pass over tokens at the next positions (row passes on the
-        tensor cores); the last position's logits."""
+        """Prompt pass over tokens ([batch][n] for a batched model) at the next
+        positions (row passes on the tensor cores); each sequence's last
+        position's logits."""
         tokens = np.ascontiguousarray(tokens, np.int32)
-        out = np.empty(self.cfg["vocab"], np.float32) if want_logits else None
-        rc = self.lib.holo_model_prefill(self.h, _ptr(tokens), len(tokens), _ptr(out) if want_logits else None)
+        shape = (self.batch, self.cfg["vocab"]) if self.batch > 1 else (self.cfg["vocab"],)
+        out = np.empty(shape, np.float32) if want_logits else None
+        rc = self.lib.holo_model_prefill(self.h, _ptr(tokens), tokens.shape[-1], _ptr(out) if want_logits else None)
         self._check("holo_model_prefill", rc == HOLO_OK)
         return out
 

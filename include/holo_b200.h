@@ -163,13 +163,16 @@ int holo_model_forward(void *model, int token, float *logits);
 /* Prompt pass: tokens[0..n) at the positions pos .. pos+n-1 (llm_forward over
  * a prompt, llm.c:1049), position + n.  Each layer's projections over the n
  * rows are one tensor-core matmul (M = n, cuda_matmul_quant_batched's
- * arithmetic), the attention causal over the cache.  One GPU, batch 1,
- * HOLO_ACT_Q8, Q8_0/Q4_0/Q4_K layer matrices of 128-row multiples, head_dim
- * 64/128/256, n_heads / n_kv_heads <= 16; else HOLO_E_UNSUPPORTED.  logits
- * (host, vocab floats) of the last position when not NULL. */
+ * arithmetic), the attention causal over the cache.  A batched model takes
+ * tokens[batch][n] and passes all batch * n rows together.  One GPU,
+ * HOLO_ACT_Q8 at batch 1, Q8_0/Q4_0/Q4_K layer matrices of 128-row
+ * multiples, head_dim 64/128/256, n_heads / n_kv_heads <= 16; else
+ * HOLO_E_UNSUPPORTED.  logits (host, [batch][vocab] floats) of each
+ * sequence's last position when not NULL. */
 int holo_model_prefill(void *model, const int *tokens, int n, float *logits);
-/* How holo_model_generate runs the prompt before its last token: 1 (default)
- * holo_model_prefill's row passes where supported, 0 one position a step. */
+/* How holo_model_generate / holo_model_generate_batch run the prompt before
+ * its last token: 1 (default) holo_model_prefill's row passes where
+ * supported, 0 one position a step. */
 int holo_model_set_prompt_mode(void *model, int rows);
 /* Replace the current logits (vocab host floats), e.g. to sample logits
  * computed elsewhere. */

@@ -16,6 +16,9 @@ decode engine.  Bars, fixed here:
   the batch-1 Q8 engine's bound;
 * the same for a prompt longer than one pass (512 positions) and for a GQA
   group of 8 query heads per KV head;
+* a batched model passes the prompts of all its sequences together: each
+  sequence's logits within 2e-2 of the reference engine on that sequence
+  alone, also at the batched decode positions that follow;
 * generate with row passes gives the tokens of the same passes followed by
   one step a position (greedy, no penalty), bit for bit.
 """
@@ -76,6 +79,33 @@ def test_gqa_group_of_8_matches_reference(dev, reference):
 def test_prompt_longer_than_one_pass(dev, reference):
     worst = segments_vs_reference(reference, CFG_LONG, False, [600], 4, seed=33)
     print(f"600-position prompt: max norm-wise rel {worst:.3e}")
+    assert worst <= 2e-2
+
+
+def test_batched_prompts_match_reference(dev, reference):
+    cfg = dict(CFG, vocab=1024)          # the batched engine's output matmul: 128-row multiples
+    B = 4
+    w = synth.llama_weights(cfg, seed=41)
+    m = Model(cfg, act_mode=hb.ACT_Q8, kv_f16=False, batch=B)
+    m.set_weights(w)
+    refs = [RefModel(reference, cfg, w) for _ in range(B)]
+    toks = np.random.default_rng(42).integers(0, cfg["vocab"], size=(B, 36 + 5)).astype(np.int32)
+    worst, pos = 0.0, 0
+    for n in (29, 7):
+        y = m.prefill(toks[:, pos:pos + n])
+        for b in range(B):
+            for t in toks[b, pos:pos + n]:
+                r = refs[b].forward(int(t))
+            worst = max(worst, rel_err(y[b], r))
+        pos += n
+    for i in range(pos, toks.shape[1]):
+        y = m.forward_batch(toks[:, i])
+        for b in range(B):
+            worst = max(worst, rel_err(y[b], refs[b].forward(int(toks[b, i]))))
+    for r in refs:
+        r.close()
+    m.close()
+    print(f"batched prompt passes: max norm-wise rel {worst:.3e}")
     assert worst <= 2e-2
 
 
