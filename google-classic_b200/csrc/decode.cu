@@ -381,6 +381,65 @@ pf_attn_kernel(float *__restrict__ att, const float *__restrict__ qkv, const KV 
     }
 }
 
+// ---------------------------------------------------------------------------
+// sharded prompt passes: every rank computes its row shard of a projection
+// for all rows, then writes its column slice [M][w] into columns [c0, c0+w)
+// of every rank's gathered copy [M][ld] (the peers' through their mapped
+// communication buffers, plain stores over NVLink).  The last CTA to finish
+// publishes the exchange's epoch in every rank's flag slot `rank`; a rank
+// reads its gathered copy after row_wait_kernel has seen every other rank's
+// epoch.  A gathered copy is rewritten two exchanges later at the earliest,
+// and by then every rank has sent a slice computed after reading it.
+// ---------------------------------------------------------------------------
+struct RowPeers {
+    float *dst[STEP_MAX_RANKS];
+    unsigned long long *flag[STEP_MAX_RANKS];
+};
+
+__global__ void __launch_bounds__(256) row_share_kernel(RowPeers P, int world, int rank, const float *__restrict__ src,
+                                                        int M, int w, int c0, int ld, unsigned long long epoch,
+                                                        unsigned *done) {
+    const int w4 = w >> 2;
+    const long long n4 = (long long)M * w4;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int m = (int)(i / w4), c = (int)(i - (long long)m * w4) * 4;
+        const float4 v = *reinterpret_cast<const float4 *>(src + (size_t)m * w + c);
+        for (int r = 0; r < world; ++r)
+            *reinterpret_cast<float4 *>(P.dst[r] + (size_t)m * ld + c0 + c) = v;
+    }
+    __threadfence_system();   // this thread's stores, to every rank, before the CTA's arrival
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {
+            *done = 0u;   // the next exchange's count (stream-ordered after this kernel)
+            __threadfence_system();
+            for (int r = 0; r < world; ++r)
+                asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(P.flag[r] + rank), "l"(epoch) : "memory");
+        }
+    }
+}
+
+// wait (bounded) until every other rank has published `epoch`; on time-out,
+// or when an earlier wait already timed out, HOLO_E_TIMEOUT and return
+__global__ void row_wait_kernel(const unsigned long long *flags, int world, int rank, unsigned long long epoch,
+                                int *status) {
+    const int r = threadIdx.x;
+    if (r >= world || r == rank) return;
+    if (status && *(volatile int *)status == HOLO_E_TIMEOUT) return;
+    const unsigned long long t0 = holo_globaltimer();
+    for (unsigned it = 0;; ++it) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flags + r) : "memory");
+        if (v >= epoch) return;
+        if ((it & 63u) == 63u && holo_globaltimer() - t0 > HOLO_WAIT_LIMIT_NS) {
+            if (status) atomicExch(status, HOLO_E_TIMEOUT);
+            return;
+        }
+        __nanosleep(64);
+    }
+}
+
 // advance the position by n (after a prompt pass of n rows)
 __global__ void dec_pos_add_kernel(int *pos_p, int n) {
     if (threadIdx.x == 0) *pos_p += n;
@@ -505,6 +564,12 @@ struct HoloModel {
     // (cudaIpc*), and the local LL QKV output
     uint8_t *comm = nullptr;
     size_t comm_bytes = 0, off_x = 0, off_att = 0, off_h = 0, off_log = 0;
+    // sharded prompt passes: gathered row copies [PROMPT_ROWS][...] of the
+    // attention output, a projection's output over dim, the SwiGLU output,
+    // and the ranks' exchange epochs
+    size_t off_rflag = 0, off_ratt = 0, off_rt = 0, off_rh = 0;
+    unsigned long long row_epoch = 0;
+    unsigned *d_row_done = nullptr;
     StepWord *qkv_ll = nullptr;
     uint8_t *peer[STEP_MAX_RANKS] = {};
     bool peers_ready = false;
@@ -711,14 +776,38 @@ bool rows_norm(const RowPass &p, const float *w, int dim, float eps, cudaStream_
     return holo_check_launch("rows: rmsnorm");
 }
 
+// sharded: this rank's column slice src [M][w] into columns [c0, c0+w) of
+// every rank's gathered copy at comm offset `off` ([M][ld]), then the wait
+// for the other ranks' slices of the same exchange
+bool row_exchange(HoloModel *m, cudaStream_t st, const float *src, int M, int w, int c0, size_t off, int ld) {
+    HoloDevice *D = holo_dev();
+    RowPeers P{};
+    for (int r = 0; r < m->world; ++r) {
+        uint8_t *c = r == m->rank ? m->comm : m->peer[r];
+        P.dst[r] = reinterpret_cast<float *>(c + off);
+        P.flag[r] = reinterpret_cast<unsigned long long *>(c + m->off_rflag);
+    }
+    const unsigned long long e = ++m->row_epoch;
+    const long long n4 = (long long)M * (w / 4);
+    const int grid = (int)std::max<long long>(1, std::min<long long>((n4 + 255) / 256, 2LL * (D ? D->sms : 148)));
+    row_share_kernel<<<grid, 256, 0, st>>>(P, m->world, m->rank, src, M, w, c0, ld, e, m->d_row_done);
+    row_wait_kernel<<<1, 32, 0, st>>>(P.flag[m->rank], m->world, m->rank, e, D ? D->status : nullptr);
+    return holo_check_launch("rows: exchange");
+}
+
 bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
     const holo_model_desc &d = m->d;
     const int M = p.M, hd = d.head_dim;
     const int qkv_dim = m->q_dim + 2 * m->kv_dim;
     const size_t kv_layer = (size_t)d.max_seq * m->kv_dim;
-    const size_t part_bs = (size_t)d.n_heads * m->max_splits * (hd + 2);
+    const size_t part_bs = (size_t)m->nh * m->max_splits * (hd + 2);
     const float sqrt_hd = sqrtf((float)hd);
     const int group = d.n_heads / d.n_kv_heads;
+    // sharded (prompt passes only): the gathered copies every projection reads
+    const bool shard = m->world > 1;
+    const float *att_in = shard ? reinterpret_cast<const float *>(m->comm + m->off_ratt) : p.att;
+    const float *t_in = shard ? reinterpret_cast<const float *>(m->comm + m->off_rt) : p.t;
+    const float *h_in = shard ? reinterpret_cast<const float *>(m->comm + m->off_rh) : p.h;
     bool ok = d.emb_type == 1
                   ? launch_pdl(dec_embed_kernel<true>, dim3((d.dim + 255) / 256, M), dim3(256), st, false, p.x,
                                (const void *)m->emb, p.seq, p.pos, d.dim, d.vocab, p.seq_bs, p.rps)
@@ -736,11 +825,11 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
              holo_matmul_batched(p.qkv, L.wqkv, L.i_qkv, p.xn, M, st, p.scratch, p.scratch_bytes);
         const size_t es = d.kv_f16 ? 2 : 4;
         uint8_t *kc = (uint8_t *)p.kc + (size_t)l * kv_layer * es, *vc = (uint8_t *)p.vc + (size_t)l * kv_layer * es;
-        const dim3 rg(std::max(d.n_heads, d.n_kv_heads), M), ag(d.n_heads, m->max_splits, M), mg(d.n_heads, M);
-        const dim3 pg(d.n_kv_heads, (p.rps + qt - 1) / qt, M / p.rps);
+        const dim3 rg(std::max(m->nh, m->nkv), M), ag(m->nh, m->max_splits, M), mg(m->nh, M);
+        const dim3 pg(m->nkv, (p.rps + qt - 1) / qt, M / p.rps);
 #define BT_ATTN(KVT, HDV)                                                                                          \
     launch_pdl(dec_rope_append_kernel<KVT>, rg, dim3(hd / 2), st, false, p.qkv, (KVT *)kc, (KVT *)vc, p.pos, hd,     \
-               d.n_heads, d.n_kv_heads, d.rope_base, (size_t)qkv_dim, p.kv_bs, p.rps) &&                            \
+               m->nh, m->nkv, d.rope_base, (size_t)qkv_dim, p.kv_bs, p.rps) &&                                      \
         (p.prompt ? launch_pdl_smem(pf_attn_kernel<KVT, HDV>, pg, dim3(PA_WARPS * 32), pa_smem(HDV), st, false,      \
                                     p.att, (const float *)p.qkv, (const KVT *)kc, (const KVT *)vc, p.pos, p.rps, qt, \
                                     group, m->kv_dim, (size_t)qkv_dim, (size_t)m->q_dim, p.kv_bs, sqrt_hd)          \
@@ -760,16 +849,22 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
             else ok = ok && BT_ATTN(float, 256);
         }
 #undef BT_ATTN
-        ok = ok && holo_matmul_batched(p.t, L.wo, L.i_o, p.att, M, st, p.scratch, p.scratch_bytes) && add(p.t);
+        if (shard) ok = ok && row_exchange(m, st, p.att, M, m->q_dim, m->h0 * hd, m->off_ratt, m->q_dim_g);
+        ok = ok && holo_matmul_batched(p.t, L.wo, L.i_o, att_in, M, st, p.scratch, p.scratch_bytes);
+        if (shard) ok = ok && row_exchange(m, st, p.t, M, m->dim_loc, m->d0, m->off_rt, d.dim);
+        ok = ok && add(t_in);
         ok = ok && rows_norm(p, L.ffn_norm, d.dim, d.eps, st) &&
              holo_matmul_batched(p.hh, L.w13, L.i_13, p.xn, M, st, p.scratch, p.scratch_bytes);
         if (ok) {
-            const long long n = (long long)M * d.ffn_dim;
+            const long long n = (long long)M * m->ffn_loc;
             bt_swiglu_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 2048), 256, 0, st>>>(p.h, p.hh,
-                                                                                               d.ffn_dim, n);
+                                                                                               m->ffn_loc, n);
             ok = holo_check_launch("rows: swiglu");
         }
-        ok = ok && holo_matmul_batched(p.t, L.w2, L.i_2, p.h, M, st, p.scratch, p.scratch_bytes) && add(p.t);
+        if (shard) ok = ok && row_exchange(m, st, p.h, M, m->ffn_loc, m->f0, m->off_rh, d.ffn_dim);
+        ok = ok && holo_matmul_batched(p.t, L.w2, L.i_2, h_in, M, st, p.scratch, p.scratch_bytes);
+        if (shard) ok = ok && row_exchange(m, st, p.t, M, m->dim_loc, m->d0, m->off_rt, d.dim);
+        ok = ok && add(t_in);
     }
     return ok;
 }
@@ -867,7 +962,11 @@ constexpr int PROMPT_ROWS = 1024;   // rows a pass (longer prompts: several pass
 
 bool prompt_supported(const HoloModel *m) {
     const holo_model_desc &d = m->d;
-    if (m->prompt_mode != 1 || m->world != 1 || (m->batch == 1 && d.act_mode != HOLO_ACT_Q8)) return false;
+    if (m->prompt_mode != 1 || (m->batch == 1 && d.act_mode != HOLO_ACT_Q8)) return false;
+    // sharded: connected peers, and every exchanged slice in whole float4s
+    if (m->world > 1 && (!m->peers_ready || m->q_dim % 4 || (m->h0 * d.head_dim) % 4 || m->dim_loc % 4 ||
+                         m->d0 % 4 || m->ffn_loc % 4 || m->f0 % 4))
+        return false;
     if (d.n_heads / d.n_kv_heads > PA_ROWS || (d.head_dim != 64 && d.head_dim != 128 && d.head_dim != 256))
         return false;
     for (const HoloLayer &L : m->layers)
@@ -1220,7 +1319,17 @@ void *holo_model_create(const holo_model_desc *desc) {
         m->off_att = o; o = a256(o + sizeof(StepWord) * m->q_dim_g);
         m->off_h = o; o = a256(o + sizeof(StepWord) * d.ffn_dim);
         m->off_log = o; o = a256(o + sizeof(StepWord) * d.vocab);
+        if (world > 1) {   // sharded prompt passes
+            m->off_rflag = o; o = a256(o + sizeof(unsigned long long) * STEP_MAX_RANKS);
+            m->off_ratt = o; o = a256(o + sizeof(float) * PROMPT_ROWS * m->q_dim_g);
+            m->off_rt = o; o = a256(o + sizeof(float) * PROMPT_ROWS * d.dim);
+            m->off_rh = o; o = a256(o + sizeof(float) * PROMPT_ROWS * d.ffn_dim);
+        }
         m->comm_bytes = o;
+    }
+    if (world > 1) {
+        ok = ok && dev_alloc((void **)&m->d_row_done, sizeof(unsigned));
+        if (ok) cudaMemset(m->d_row_done, 0, sizeof(unsigned));
     }
     ok = ok && dev_alloc((void **)&m->comm, m->comm_bytes);
     ok = ok && dev_alloc((void **)&m->qkv_ll, sizeof(StepWord) * (m->q_dim + 2 * m->kv_dim));
@@ -1455,8 +1564,12 @@ int holo_model_prefill(void *model, const int *tokens, int n, float *logits) {
             holo_set_status(HOLO_E_ARG, "holo_model_prefill: token out of range");
             return HOLO_E_ARG;
         }
+    if (m->world > 1 && logits) {
+        holo_set_status(HOLO_E_UNSUPPORTED, "holo_model_prefill: sharded, the logits come from the next step");
+        return HOLO_E_UNSUPPORTED;
+    }
     if (!prompt_supported(m)) {
-        holo_set_status(HOLO_E_UNSUPPORTED, "holo_model_prefill: row passes need one GPU, HOLO_ACT_Q8 at batch 1, "
+        holo_set_status(HOLO_E_UNSUPPORTED, "holo_model_prefill: row passes need HOLO_ACT_Q8 at batch 1, "
                                             "Q8_0/Q4_0/Q4_K layers of 128-row multiples, head_dim 64/128/256, "
                                             "n_heads / n_kv_heads <= 16");
         return HOLO_E_UNSUPPORTED;
@@ -1858,7 +1971,7 @@ void holo_model_free(void *model) {
     for (void *p : rbufs) cudaFree(p);
     void *bufs[] = {m->emb, m->final_norm, m->out, m->kc, m->vc, m->comm, m->qkv_ll, m->x, m->qkv, m->att,
                     m->h, m->logits, m->part, m->probs, m->kept_p, m->rvals, m->kept_idx, m->d_pos, m->d_seq, m->d_hist,
-                    m->d_nhist, m->d_out, m->d_last, m->d_layers, m->d_pf, m->d_bar, m->d_att_cnt};
+                    m->d_nhist, m->d_out, m->d_last, m->d_layers, m->d_pf, m->d_bar, m->d_att_cnt, m->d_row_done};
     for (void *p : bufs) cudaFree(p);
     delete m;
 }

@@ -9,7 +9,8 @@ host: every rank computes its row shard through the library (holo_model_shard)
       the ranks check that the shards tile every matrix and that every rank
       received every handle in rank order.
 gpu:  every rank builds its shard of the test model, connects the peers and
-      runs the decode calls; rank 0 writes the logits and token streams to
+      runs the decode calls (generate's prompt and one holo_model_prefill in
+      sharded row passes); rank 0 writes the logits and token streams to
       OUT_DIR/gpu.npz for the parent test to compare with the reference.
 timeout: failure detection without a fault: both ranks connect, then rank 1
       stays alive but skips the step; rank 0's step waits for rank 1's slices,
@@ -35,7 +36,7 @@ from holo_b200.model import (LLAMA2_7B, LLAMA3_70B, Model, SamplerDesc, connect_
 # the decode test model (GQA, SwiGLU, Q4_K layers, fp16 embeddings, Q8_0 output)
 CFG = dict(n_layers=2, dim=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn_dim=768, vocab=1000, max_seq=160,
            rope_base=10000.0, eps=1e-5, layer_type=hb.Q4_K, emb_type=1, out_type=hb.Q8_0)
-PROMPT_SEED, N_PROMPT, N_GREEDY, N_SAMPLED = 21, 24, 48, 32
+PROMPT_SEED, N_PROMPT, N_GREEDY, N_SAMPLED, N_ROWS = 21, 24, 48, 32, 20
 
 
 class StandInModel:
@@ -105,6 +106,10 @@ def run_gpu(rank, world, out):
             res[f"{tag}_logits"] = np.stack([m.forward(t) for t in prompt])
             res[f"{tag}_greedy"] = m.generate(prompt[:16], N_GREEDY, SamplerDesc(0.0, 0.95, 40, 1.1, 64), seed=5)
             res[f"{tag}_sampled"] = m.generate(prompt[:16], N_SAMPLED, SamplerDesc(0.8, 0.95, 40, 1.1, 64), seed=7)
+            if act == hb.ACT_Q8:   # a sharded prompt pass, then steps that read its cache
+                m.reset()
+                m.prefill(prompt[:N_ROWS], want_logits=False)
+                res["q8_rows_logits"] = np.stack([m.forward(t) for t in prompt[N_ROWS:]])
             dist.barrier()
             m.close()
         # every rank computed the same logits and tokens

@@ -8,7 +8,10 @@ summed across warps can differ, so the bars are those of test_decode_gpu:
   norm-wise relative of the reference; greedy (48 steps) and sampled (32
   steps) token streams identical to the reference's.
 * HOLO_ACT_Q8, fp16 KV cache: logits within 1e-3 norm-wise relative of the
-  one-GPU model's, greedy stream identical to it.
+  one-GPU model's, greedy stream identical to it; the same bound for the
+  positions after a sharded prompt pass (row shards of every projection on
+  the tensor cores, column slices exchanged through peer memory) against
+  the one-GPU prompt pass.
 * Both ranks return the same logits and tokens.
 Needs two GPUs; skipped otherwise.
 """
@@ -27,7 +30,7 @@ from conftest import ROOT, rel_err
 from holo_oracle import RefModel
 
 sys.path.insert(0, str(ROOT / "tests"))
-from shard_worker import CFG, N_GREEDY, N_PROMPT, N_SAMPLED, PROMPT_SEED  # noqa: E402
+from shard_worker import CFG, N_GREEDY, N_PROMPT, N_ROWS, N_SAMPLED, PROMPT_SEED  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -100,6 +103,18 @@ def test_sharded_q8_matches_one_gpu(sharded, dev, weights):
     print(f"sharded q8 vs one GPU: max norm-wise rel {worst:.3e}")
     assert worst <= 1e-3
     assert np.array_equal(sharded["q8_greedy"], got)
+
+
+def test_sharded_prompt_pass_matches_one_gpu(sharded, dev, weights):
+    m = Model(CFG, act_mode=hb.ACT_Q8, kv_f16=True)
+    m.set_weights(weights)
+    p = prompt()
+    m.prefill(p[:N_ROWS], want_logits=False)
+    want = np.stack([m.forward(t) for t in p[N_ROWS:]])
+    m.close()
+    worst = max(rel_err(y, r) for y, r in zip(sharded["q8_rows_logits"], want))
+    print(f"sharded prompt pass vs one GPU: max norm-wise rel {worst:.3e}")
+    assert worst <= 1e-3
 
 
 def test_missing_rank_times_out_and_device_recovers(tmp_path):
