@@ -491,15 +491,30 @@ __global__ void bt_swiglu_kernel(float *__restrict__ h, const float *__restrict_
     }
 }
 
+// one CTA a sequence (blockIdx.x = b): its logits, scratch and candidate
+// buffers vocab_bs floats apart, its token list, history, draws and outputs
+// seq_bs apart (batch 1: both 0)
 __global__ void __launch_bounds__(SM_THREADS)
 dec_sample_kernel(float *__restrict__ logits, float *__restrict__ probs, int *__restrict__ kept_idx,
                   float *__restrict__ kept_p, int *__restrict__ seq, int *__restrict__ hist, int *__restrict__ nhist_p,
                   const int *__restrict__ pos_p, const float *__restrict__ rvals, int *__restrict__ out_tokens,
-                  int *__restrict__ last_token, int *__restrict__ status, const SampleArgs a) {
+                  int *__restrict__ last_token, int *__restrict__ status, const SampleArgs a, size_t vocab_bs,
+                  size_t seq_bs) {
     extern __shared__ __align__(16) uint8_t sm_raw[];
     SampleSmem &S = *reinterpret_cast<SampleSmem *>(sm_raw);
     dec_pdl_trigger();
     dec_pdl_wait();
+    const int b = blockIdx.x;
+    logits += b * vocab_bs;
+    probs += b * vocab_bs;
+    kept_idx += b * vocab_bs;
+    kept_p += b * vocab_bs;
+    seq += b * seq_bs;
+    hist += b * seq_bs;
+    rvals += b * seq_bs;
+    out_tokens += b * seq_bs;
+    nhist_p += b;
+    last_token += b;
     const int pos = *pos_p;
     if (a.gen && pos < a.n_prompt - 1) return;
     const int gi = a.gen ? pos - (a.n_prompt - 1) : 0;
@@ -604,6 +619,8 @@ struct HoloModel {
     int batch = 1;
     float *bx = nullptr, *bxn = nullptr, *bqkv = nullptr, *batt = nullptr, *bt = nullptr, *bhh = nullptr,
           *bh = nullptr, *blogits = nullptr, *bpart = nullptr, *brvals = nullptr;
+    float *bprobs = nullptr, *bkept_p = nullptr;   // per-sequence sampler scratch [batch][vocab]
+    int *bkept_idx = nullptr;
     void *bkc = nullptr, *bvc = nullptr;
     int *bseq = nullptr, *bhist = nullptr, *bnhist = nullptr, *bout = nullptr, *blast = nullptr, *bpos = nullptr;
     int h_bpos = 0;
@@ -746,15 +763,13 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
         ok = ok && launch_pdl_smem(dec_sample_kernel, dim3(1), dim3(SM_THREADS), sizeof(SampleSmem), st, pdl,
                                    m->logits, m->probs,
                               m->kept_idx, m->kept_p, m->d_seq, m->d_hist, m->d_nhist, (const int *)m->d_pos,
-                              (const float *)m->rvals, m->d_out, m->d_last, D ? D->status : nullptr, sa);
+                              (const float *)m->rvals, m->d_out, m->d_last, D ? D->status : nullptr, sa, (size_t)0,
+                              (size_t)0);
     }
     ok = ok && launch_pdl(dec_step_end_kernel, dim3(1), dim3(32), st, pdl, m->d_pos);
     return ok;
 }
 
-// One position of all `batch` sequences (llm_forward per sequence, llm.c
-// 1015-1269): mode 0 the prompt step (no logits), 1 with the logits, 2 with
-// the logits and the sampler of every sequence (llm_sample, llm.c:1281-1328).
 // the layers over M activation rows: row b * rps + i is position pos + i of
 // sequence b (token lists seq_bs ints apart, caches kv_bs elements apart).
 // Batched decode: one position a sequence (rps 1), split attention; prompt
@@ -869,6 +884,9 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
     return ok;
 }
 
+// One position of all `batch` sequences (llm_forward per sequence, llm.c
+// 1015-1269): mode 0 the prompt step (no logits), 1 with the logits, 2 with
+// the logits and the sampler of every sequence (llm_sample, llm.c:1281-1328).
 bool enqueue_batch_step(HoloModel *m, cudaStream_t st, int mode, const SampleArgs &sa) {
     const holo_model_desc &d = m->d;
     const int B = m->batch, S = d.max_seq + 1;
@@ -884,14 +902,12 @@ bool enqueue_batch_step(HoloModel *m, cudaStream_t st, int mode, const SampleArg
     auto norm = [&](const float *w) { return rows_norm(p, w, d.dim, d.eps, st); };
     if (mode >= 1)
         ok = ok && norm(m->final_norm) && holo_matmul_batched(m->blogits, m->out, m->i_out, m->bxn, B, st, m->bscratch, m->bscratch_bytes);
-    if (mode == 2) {
+    if (mode == 2) {   // the samplers of all sequences side by side, one CTA each
         HoloDevice *D = holo_dev();
-        for (int b = 0; b < B && ok; ++b)
-            ok = launch_pdl_smem(dec_sample_kernel, dim3(1), dim3(SM_THREADS), sizeof(SampleSmem), st, false,
-                                 m->blogits + (size_t)b * d.vocab, m->probs, m->kept_idx, m->kept_p,
-                                 m->bseq + (size_t)b * S, m->bhist + (size_t)b * S, m->bnhist + b,
-                                 (const int *)m->bpos, (const float *)m->brvals + (size_t)b * S, m->bout + (size_t)b * S,
-                                 m->blast + b, D ? D->status : nullptr, sa);
+        ok = ok && launch_pdl_smem(dec_sample_kernel, dim3(B), dim3(SM_THREADS), sizeof(SampleSmem), st, false,
+                                   m->blogits, m->bprobs, m->bkept_idx, m->bkept_p, m->bseq, m->bhist, m->bnhist,
+                                   (const int *)m->bpos, (const float *)m->brvals, m->bout, m->blast,
+                                   D ? D->status : nullptr, sa, (size_t)d.vocab, (size_t)S);
     }
     return ok && launch_pdl(dec_step_end_kernel, dim3(1), dim3(32), st, false, m->bpos);
 }
@@ -1387,6 +1403,9 @@ void *holo_model_create(const holo_model_desc *desc) {
               dev_alloc((void **)&m->bhh, sizeof(float) * B * 2 * d.ffn_dim) &&
               dev_alloc((void **)&m->bh, sizeof(float) * B * d.ffn_dim) &&
               dev_alloc((void **)&m->blogits, sizeof(float) * B * d.vocab) &&
+              dev_alloc((void **)&m->bprobs, sizeof(float) * B * d.vocab) &&
+              dev_alloc((void **)&m->bkept_p, sizeof(float) * B * d.vocab) &&
+              dev_alloc((void **)&m->bkept_idx, sizeof(int) * B * d.vocab) &&
               dev_alloc((void **)&m->bpart, sizeof(float) * B * d.n_heads * m->max_splits * (hd + 2)) &&
               dev_alloc((void **)&m->brvals, sizeof(float) * B * S) &&
               dev_alloc((void **)&m->bseq, sizeof(int) * B * S) && dev_alloc((void **)&m->bhist, sizeof(int) * B * S) &&
@@ -1653,9 +1672,8 @@ int holo_model_sample(void *model, const holo_sampler_desc *s, float r) {
     if (!prepare_sampler()) return -1;
     cudaMemcpyAsync(m->rvals, &r, sizeof(float), cudaMemcpyHostToDevice, st);
     launch_pdl_smem(dec_sample_kernel, dim3(1), dim3(SM_THREADS), sizeof(SampleSmem), st, false, m->logits,
-                    m->probs, m->kept_idx, m->kept_p,
-               m->d_seq, m->d_hist, m->d_nhist, (const int *)m->d_pos, (const float *)m->rvals, m->d_out,
-               m->d_last, D ? D->status : nullptr, a);
+                    m->probs, m->kept_idx, m->kept_p, m->d_seq, m->d_hist, m->d_nhist, (const int *)m->d_pos,
+                    (const float *)m->rvals, m->d_out, m->d_last, D ? D->status : nullptr, a, (size_t)0, (size_t)0);
     int tok = -1;
     cudaMemcpyAsync(&tok, m->d_last, sizeof(int), cudaMemcpyDeviceToHost, st);
     cudaStreamSynchronize(st);
@@ -1965,6 +1983,7 @@ void holo_model_free(void *model) {
         cudaFree(L.w2);
     }
     void *bbufs[] = {m->bx, m->bxn, m->bqkv, m->batt, m->bt, m->bhh, m->bh, m->blogits, m->bpart, m->brvals,
+                     m->bprobs, m->bkept_p, m->bkept_idx,
                      m->bkc, m->bvc, m->bseq, m->bhist, m->bout, m->bnhist, m->blast, m->bpos, m->bscratch};
     for (void *p : bbufs) cudaFree(p);
     void *rbufs[] = {m->rx, m->rxn, m->rqkv, m->ratt, m->rt, m->rhh, m->rh, m->rscratch};

@@ -114,6 +114,7 @@ struct HoloDevice {
     // split-K fix-up scratch of the tiled matvec (zeroed once; self-cleaning)
     float *mv_partials = nullptr;        // [MV_MAX_CTAS][2][32]
     int *mv_counters = nullptr;          // [MV_MAX_ROWBLOCKS]
+    int *mvb_counters = nullptr;         // [MVB_MAX_GROUPS] of the few-row matmul (zeroed once; self-cleaning)
     int *status = nullptr;               // device-side error word (bounded waits)
     // small persistent buffers for reductions that return to the host
     void *reduce_buf = nullptr;          // 64 KB
@@ -123,6 +124,8 @@ struct HoloDevice {
 };
 constexpr int MV_MAX_CTAS = 1024;
 constexpr int MV_MAX_ROWBLOCKS = 1 << 16;
+constexpr int MVB_MAX_GROUPS = 1 << 14;   // row groups (8 row-blocks) of one few-row matmul
+constexpr int MVB_MAX_M = 16;             // activation rows the few-row matmul takes
 
 HoloDevice *holo_dev();                  // current device's state, initialised on demand
 cudaStream_t holo_stream();
@@ -157,6 +160,12 @@ bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const fl
 size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M);
 // the batched matmul's weights: rows a multiple of this (one MMA tile)
 constexpr int PF_ROWS_ALIGN = 128;
+// Y[M][N] = X[M][K] . W^T for M <= MVB_MAX_M on the CUDA cores (matvec_batch.cu):
+// each weight unit read once and dotted with every Q8-quantized row;
+// scratch: at least holo_matmul_few_scratch bytes (split-K partials)
+bool holo_matmul_few(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st,
+                     void *scratch, size_t scratch_bytes);
+size_t holo_matmul_few_scratch(const WeightInfo &wi, int M);
 bool holo_repack_to(void *dst, const void *dev_blocks, int ggml_type, int rows, int cols, int q4k_layout,
                     cudaStream_t st);
 void holo_registry_add(const void *ptr, const WeightInfo &info);

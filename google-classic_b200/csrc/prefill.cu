@@ -446,6 +446,7 @@ PfPlan pf_plan(const WeightInfo &wi, int M, int sms) {
 }  // namespace
 
 size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M) {
+    if (M <= MVB_MAX_M) return holo_matmul_few_scratch(wi, M);
     HoloDevice *D = holo_dev();
     const PfPlan p = pf_plan(wi, M, D ? D->sms : 148);
     return p.xt_bytes + p.part_bytes;
@@ -457,6 +458,9 @@ size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M) {
 // the library's shared one.
 bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st,
                          void *scratch, size_t scratch_bytes) {
+    // a few rows: the CUDA-core kernel that reads each weight unit once for all
+    // of them (matvec_batch.cu); a tensor-core tile would be mostly padding
+    if (M > 0 && M <= MVB_MAX_M) return holo_matmul_few(Y, W, wi, X, M, st, scratch, scratch_bytes);
     HoloDevice *D = holo_dev();
     if (!D) return false;
     const int N = wi.rows, K = wi.cols;

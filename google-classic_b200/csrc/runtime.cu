@@ -43,10 +43,12 @@ bool init_device(HoloDevice &D, int id) {
     if (cudaStreamCreateWithFlags(&D.copy_stream, cudaStreamNonBlocking) != cudaSuccess) return false;
     if (cudaMalloc(&D.mv_partials, sizeof(float) * MV_MAX_CTAS * 2 * 32) != cudaSuccess) return false;
     if (cudaMalloc(&D.mv_counters, sizeof(int) * MV_MAX_ROWBLOCKS) != cudaSuccess) return false;
+    if (cudaMalloc(&D.mvb_counters, sizeof(int) * MVB_MAX_GROUPS) != cudaSuccess) return false;
     if (cudaMalloc(&D.status, sizeof(int) * 4) != cudaSuccess) return false;
     if (cudaMalloc(&D.reduce_buf, 65536) != cudaSuccess) return false;
     if (cudaMallocHost(&D.pinned, 65536) != cudaSuccess) return false;
     cudaMemset(D.mv_counters, 0, sizeof(int) * MV_MAX_ROWBLOCKS);
+    cudaMemset(D.mvb_counters, 0, sizeof(int) * MVB_MAX_GROUPS);
     cudaMemset(D.status, 0, sizeof(int) * 4);
     if (cudaDeviceSynchronize() != cudaSuccess) return false;
     D.ready = true;
@@ -196,6 +198,7 @@ void cuda_clear_status(void) {
         cudaStreamSynchronize(g_dev[id].stream);
         cudaMemset(g_dev[id].status, 0, sizeof(int));
         cudaMemset(g_dev[id].mv_counters, 0, sizeof(int) * MV_MAX_ROWBLOCKS);
+        cudaMemset(g_dev[id].mvb_counters, 0, sizeof(int) * MVB_MAX_GROUPS);
         cudaDeviceSynchronize();
     }
     cudaGetLastError();
@@ -267,6 +270,7 @@ void cuda_cleanup(void) {
     cudaStreamDestroy(D.copy_stream);
     cudaFree(D.mv_partials);
     cudaFree(D.mv_counters);
+    cudaFree(D.mvb_counters);
     cudaFree(D.status);
     cudaFree(D.reduce_buf);
     cudaFreeHost(D.pinned);

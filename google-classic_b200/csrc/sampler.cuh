@@ -86,6 +86,7 @@ __device__ __forceinline__ float block_sum(float v, float *sv) {
 
 // Shared state of the sampler (static shared memory of the kernel that runs it).
 struct SampleSmem {
+    int ncand;
     float sv[32];
     int si[32];
     unsigned hist256[256];
@@ -102,6 +103,50 @@ struct SampleSmem {
 };
 // per-warp histograms of the radix selection: 32 warps x 256 digits
 static_assert(2 * SM_SORT_MAX >= 32 * 256, "digit histograms fit the sort buffers");
+
+// a slot in a shared list for each lane with pred (one atomic a warp); the
+// whole warp calls it; -1 for the others
+__device__ __forceinline__ int warp_slot(int *counter, bool pred) {
+    const unsigned bal = __ballot_sync(0xffffffffu, pred);
+    if (!bal) return -1;
+    const int lane = threadIdx.x & 31;
+    int base = 0;
+    if (lane == __ffs(bal) - 1) base = atomicAdd(counter, __popc(bal));
+    base = __shfl_sync(0xffffffffu, base, __ffs(bal) - 1);
+    return pred ? base + __popc(bal & ((1u << lane) - 1u)) : -1;
+}
+
+// warp 0: the digit at `shift` of the k-th largest key among those counted in
+// S.hist256 (keys matching S.prefix so far); updates S.prefix and S.krem
+// (out of line: the sampler runs once a launch, so each inlined copy of its
+// code would be fetched cold into the instruction cache)
+static __device__ __noinline__ void radix_digit(SampleSmem &S, int shift, int lane) {
+    // lane l owns digits 255-8l .. 248-8l (descending); find the digit where
+    // the count of larger-or-equal digits reaches krem
+    unsigned cnt[8], tot = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) { cnt[k] = S.hist256[255 - 8 * lane - k]; tot += cnt[k]; }
+    unsigned incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    const int krem = S.krem;
+    const unsigned before = incl - tot;
+    if ((int)before < krem && (int)incl >= krem) {
+        unsigned cum = before;
+        for (int k = 0; k < 8; ++k) {
+            if ((int)(cum + cnt[k]) >= krem) {
+                S.prefix |= (unsigned)(255 - 8 * lane - k) << shift;
+                S.krem = krem - (int)cum;
+                break;
+            }
+            cum += cnt[k];
+        }
+    }
+}
+
 
 // The sampler body, run by one CTA of any size (a multiple of 32, <= 1024).
 // The logits are copied into a work array -- shared memory for vocabularies
@@ -149,13 +194,22 @@ static __device__ int sample_body(SampleSmem &S, const float *__restrict__ logit
         }
         for (int t = start + tid; t < nhist; t += NT) {
             const int tok = staged ? hw[t - start] : __ldcg(hw + (t - start));
+            // occurrences of tok in the window (itself included), and whether
+            // this is the first; no early exit, so the loop pipelines
             bool first = true;
-            int c = 1;
-            for (int u = start; u < nhist; ++u) {
-                if (u == t) continue;
-                if ((staged ? hw[u - start] : __ldcg(hw + (u - start))) == tok) {
-                    if (u < t) { first = false; break; }
-                    ++c;
+            int c = 0;
+            if (staged) {
+#pragma unroll 8
+                for (int u = 0; u < nhist - start; ++u) {
+                    const bool eq = hw[u] == tok;
+                    c += eq;
+                    first = first && !(eq && u < t - start);
+                }
+            } else {
+                for (int u = 0; u < nhist - start; ++u) {
+                    const bool eq = __ldcg(hw + u) == tok;
+                    c += eq;
+                    first = first && !(eq && u < t - start);
                 }
             }
             if (first && tok >= 0 && tok < V) {
@@ -189,78 +243,216 @@ static __device__ int sample_body(SampleSmem &S, const float *__restrict__ logit
     }
     const float sum_e = block_sum(part, S.sv);
     const float scale = __fdiv_rn(1.0f, sum_e);
-    for (int i = tid; i < V; i += NT) work[i] = work[i] * scale;
-    __syncthreads();
 
     // 5. top-k: the k-th largest probability by radix selection on its bits
-    //    (probabilities are >= 0, so their bit patterns order like the values)
+    //    (probabilities are >= 0, so their bit patterns order like the
+    //    values).  Digit counts go to one histogram per warp (most
+    //    probabilities share a few exponents: one histogram would serialise
+    //    the CTA's atomics on one or two bins), summed per digit afterwards.
+    //    The first digit is counted in the pass that scales the
+    //    probabilities; then the keys at or above the selected top byte --
+    //    the candidates and the rest of the boundary byte, usually a few
+    //    hundred -- are compacted, and the later digits are counted over
+    //    them alone.  A boundary byte too crowded to compact falls back to
+    //    passes over the vocabulary.
     float thr = 0.0f;
     const bool topk = a.top_k > 0 && a.top_k < V;
+    unsigned *wh = reinterpret_cast<unsigned *>(S.sort_p);   // [warps][256]
+    const int nw = NT >> 5;
     if (topk) {
-        if (tid == 0) { S.prefix = 0u; S.krem = a.top_k; }
-        unsigned mask = 0u;
-        // digit counts in one histogram per warp (most probabilities share a
-        // few exponents: a single histogram would serialise the whole CTA's
-        // atomics on one or two bins), summed per digit afterwards
-        unsigned *wh = reinterpret_cast<unsigned *>(S.sort_p);   // [warps][256]
-        const int nw = NT >> 5;
-        for (int shift = 24; shift >= 0; shift -= 8) {
-            for (int b = tid; b < nw * 256; b += NT) wh[b] = 0u;
-            __syncthreads();
-            const unsigned prefix = S.prefix;
-            unsigned *mine = wh + warp * 256;
-            for (int i = tid; i < V; i += NT) {
-                const unsigned key = __float_as_uint(work[i]);
-                if ((key & mask) == prefix) atomicAdd(&mine[(key >> shift) & 255u], 1u);
-            }
-            __syncthreads();
-            for (int b = tid; b < 256; b += NT) {
-                unsigned c = 0u;
-                for (int w = 0; w < nw; ++w) c += wh[w * 256 + b];
-                S.hist256[b] = c;
-            }
-            __syncthreads();
-            if (warp == 0) {
-                // lane l owns digits 255-8l .. 248-8l (descending); find the digit
-                // where the count of larger-or-equal digits reaches krem
-                unsigned cnt[8], tot = 0;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) { cnt[k] = S.hist256[255 - 8 * lane - k]; tot += cnt[k]; }
-                unsigned incl = tot;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= o) incl += y;
-                }
-                const int krem = S.krem;
-                const unsigned before = incl - tot;
-                if ((int)before < krem && (int)incl >= krem) {
-                    unsigned cum = before;
-                    for (int k = 0; k < 8; ++k) {
-                        if ((int)(cum + cnt[k]) >= krem) {
-                            S.prefix = prefix | ((unsigned)(255 - 8 * lane - k) << shift);
-                            S.krem = krem - (int)cum;
-                            break;
-                        }
-                        cum += cnt[k];
-                    }
-                }
-            }
-            mask |= 255u << shift;
-            __syncthreads();
+        for (int b = tid; b < nw * 256; b += NT) wh[b] = 0u;
+        if (tid == 0) { S.prefix = 0u; S.krem = a.top_k; S.ncut = 0; S.ncand = 0; }
+        __syncthreads();
+    }
+    {
+        unsigned *mine = wh + warp * 256;
+        for (int i = tid; i < V; i += NT) {
+            const float p = work[i] * scale;
+            work[i] = p;
+            if (topk) atomicAdd(&mine[__float_as_uint(p) >> 24], 1u);
         }
-        thr = __uint_as_float(S.prefix);
+        __syncthreads();
+    }
+    bool have_cands = false;   // candidates already collected (compacted path)
+    if (topk) {
+        for (int b = tid; b < 256; b += NT) {
+            unsigned c = 0u;
+            for (int w = 0; w < nw; ++w) c += wh[w * 256 + b];
+            S.hist256[b] = c;
+        }
+        __syncthreads();
+        if (warp == 0) radix_digit(S, 24, lane);
+        __syncthreads();
+        // compact the keys whose top byte is at least the selected one
+        const unsigned top = S.prefix >> 24;
+        for (int i0 = 0; i0 < V; i0 += NT) {
+            const int i = i0 + tid;
+            const float p = i < V ? work[i] : 0.0f;
+            const int slot = warp_slot(&S.ncut, i < V && (__float_as_uint(p) >> 24) >= top);
+            if (slot >= 0 && slot < SM_SORT_MAX) { S.sort_p[slot] = p; S.sort_j[slot] = i; }
+        }
+        __syncthreads();
+        const int nc = S.ncut;
+        unsigned mask = 0xFF000000u;
+        if (nc <= SM_SORT_MAX) {
+            for (int shift = 16; shift >= 0; shift -= 8) {
+                for (int b = tid; b < 256; b += NT) S.hist256[b] = 0u;
+                __syncthreads();
+                const unsigned prefix = S.prefix;
+                for (int j = tid; j < nc; j += NT) {
+                    const unsigned key = __float_as_uint(S.sort_p[j]);
+                    if ((key & mask) == prefix) atomicAdd(&S.hist256[(key >> shift) & 255u], 1u);
+                }
+                __syncthreads();
+                if (warp == 0) radix_digit(S, shift, lane);
+                mask |= 255u << shift;
+                __syncthreads();
+            }
+            thr = __uint_as_float(S.prefix);
+            // the candidates: the compacted keys at or above the threshold
+            for (int j0 = 0; j0 < nc; j0 += NT) {
+                const int j = j0 + tid;
+                const float p = j < nc ? S.sort_p[j] : 0.0f;
+                const int slot = warp_slot(&S.ncand, j < nc && p >= thr);
+                if (slot >= 0) {
+                    S.cand_i[slot] = S.sort_j[j];
+                    S.cand_p[slot] = p;
+                }
+            }
+            __syncthreads();
+            have_cands = true;
+        } else {
+            for (int shift = 16; shift >= 0; shift -= 8) {
+                for (int b = tid; b < nw * 256; b += NT) wh[b] = 0u;
+                __syncthreads();
+                const unsigned prefix = S.prefix;
+                unsigned *mine = wh + warp * 256;
+                for (int i = tid; i < V; i += NT) {
+                    const unsigned key = __float_as_uint(work[i]);
+                    if ((key & mask) == prefix) atomicAdd(&mine[(key >> shift) & 255u], 1u);
+                }
+                __syncthreads();
+                for (int b = tid; b < 256; b += NT) {
+                    unsigned c = 0u;
+                    for (int w = 0; w < nw; ++w) c += wh[w * 256 + b];
+                    S.hist256[b] = c;
+                }
+                __syncthreads();
+                if (warp == 0) radix_digit(S, shift, lane);
+                mask |= 255u << shift;
+                __syncthreads();
+            }
+            thr = __uint_as_float(S.prefix);
+        }
     }
     // candidates (p >= thr; every index without top-k), in index order
-    if (tid == 0) S.ncut = 0;   // candidate counter
-    __syncthreads();
-    for (int i = tid; i < V; i += NT)
-        if (work[i] >= thr) {
-            const int slot = atomicAdd(&S.ncut, 1);
-            if (slot < SM_SORT_MAX) { S.cand_i[slot] = i; S.cand_p[slot] = work[i]; }
+    if (!have_cands) {
+        if (tid == 0) S.ncand = 0;
+        __syncthreads();
+        for (int i0 = 0; i0 < V; i0 += NT) {
+            const int i = i0 + tid;
+            const float p = i < V ? work[i] : 0.0f;
+            const int slot = warp_slot(&S.ncand, i < V && p >= thr);
+            if (slot >= 0 && slot < SM_SORT_MAX) { S.cand_i[slot] = i; S.cand_p[slot] = p; }
         }
-    __syncthreads();
-    const int nk = S.ncut;
+        __syncthreads();
+    }
+    const int nk = S.ncand;
+    if (nk <= 64) {
+        // a few candidates (top-k): warp 0 finishes alone.  Orders come from
+        // ranks (a pass over the candidates in shared memory, broadcast
+        // reads), not sorting networks: candidate e (lanes e and e-32) has
+        // index rank ri and, after the top-k renormalisation, rank rp in
+        // (descending p, ascending index) order.
+        if (warp == 0) {
+            float *ap = S.sort_p, *bp = S.cand_p;   // by index rank, by p rank
+            int *ai = S.sort_j;
+            float p[2];
+            int ix[2], ri[2] = {0, 0}, rp[2] = {0, 0};
+            bool live[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int e = lane + 32 * q;
+                live[q] = e < nk;
+                p[q] = live[q] ? S.cand_p[e] : 0.0f;
+                ix[q] = live[q] ? S.cand_i[e] : 0x7fffffff;
+            }
+            for (int j = 0; j < nk; ++j) {
+                const int ij = S.cand_i[j];
+#pragma unroll
+                for (int q = 0; q < 2; ++q) ri[q] += ij < ix[q];
+            }
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 2; ++q)
+                if (live[q]) { ap[ri[q]] = p[q]; ai[ri[q]] = ix[q]; }
+            __syncwarp();
+            if (topk) {   // renormalise: sequential sum in index order
+                float sc = 0.0f;
+                if (lane == 0) {
+                    float sum = 0.0f;
+                    for (int j = 0; j < nk; ++j) sum += ap[j];
+                    sc = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 1.0f;
+                }
+                sc = __shfl_sync(0xffffffffu, sc, 0);
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    p[q] = p[q] * sc;
+                    if (live[q]) ap[ri[q]] = p[q];
+                }
+                __syncwarp();
+            }
+            if (a.top_p > 0.0f && a.top_p < 1.0f) {
+                // cut at the first cumulative sum above top_p in descending
+                // order (ties: lower index first), renormalise
+                for (int j = 0; j < nk; ++j) {
+                    const float pj = ap[j];
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) rp[q] += pj > p[q] || (pj == p[q] && j < ri[q]);
+                }
+#pragma unroll
+                for (int q = 0; q < 2; ++q)
+                    if (live[q]) bp[rp[q]] = p[q];
+                __syncwarp();
+                int cut = nk;
+                if (lane == 0) {
+                    float cum = 0.0f;
+                    for (int j = 0; j < nk; ++j) {
+                        cum += bp[j];
+                        if (cum > a.top_p) { cut = j + 1; break; }
+                    }
+                }
+                cut = __shfl_sync(0xffffffffu, cut, 0);
+#pragma unroll
+                for (int q = 0; q < 2; ++q)
+                    if (live[q] && rp[q] >= cut) { p[q] = 0.0f; ap[ri[q]] = 0.0f; }
+                __syncwarp();
+                float sc = 0.0f;
+                if (lane == 0) {
+                    float sum = 0.0f;
+                    for (int j = 0; j < nk; ++j) sum += ap[j];
+                    sc = sum > 0.0f ? __fdiv_rn(1.0f, sum) : 1.0f;
+                }
+                sc = __shfl_sync(0xffffffffu, sc, 0);
+#pragma unroll
+                for (int q = 0; q < 2; ++q)
+                    if (live[q]) ap[ri[q]] = p[q] * sc;
+                __syncwarp();
+            }
+            // 7. draw over the candidates in index order
+            if (lane == 0) {
+                float cum = 0.0f;
+                int tok = V - 1;
+                for (int j = 0; j < nk; ++j) {
+                    cum += ap[j];
+                    if (r < cum) { tok = ai[j]; break; }
+                }
+                S.token = tok;
+            }
+        }
+        __syncthreads();
+        return S.token;
+    }
     const bool in_smem = nk <= SM_SORT_MAX;
     float *cp = S.cand_p;
     int *ci = S.cand_i;

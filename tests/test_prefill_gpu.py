@@ -1,11 +1,13 @@
-"""Batched quantized matmul on the tensor cores (cuda_matmul_quant_batched,
-csrc/prefill.cu) against the oracle's Q8-activation restatement, one matvec
-per activation row (oracle/holo_oracle.c ho_matvec_q8act), for Q4_K, Q4_0
-and Q8_0 weights.
+"""Batched quantized matmul (cuda_matmul_quant_batched) against the oracle's
+Q8-activation restatement, one matvec per activation row
+(oracle/holo_oracle.c ho_matvec_q8act), for Q4_K, Q4_0 and Q8_0 weights.
 
-Both operands reach the tensor core as fp16: the Q8 activation d*q rounded
-once, the weight value once (Q4_0 d*(q-8), Q8_0 d*q) or, for Q4_K, after
-its scale and min are rounded (one fp16 fma).
+Above 16 rows it runs on the tensor cores (csrc/prefill.cu): both operands
+reach them as fp16, the Q8 activation d*q rounded once, the weight value once
+(Q4_0 d*(q-8), Q8_0 d*q) or, for Q4_K, after its scale and min are rounded
+(one fp16 fma).  Up to 16 rows it runs on the CUDA cores
+(csrc/matvec_batch.cu): integer block dots of the Q8 rows, the batch-1 Q8
+matvec's arithmetic per row, split over K with a deterministic fix-up.
 The bar, fixed here: max |Y - R| / max |R| <= 1e-3 over the whole output
 (the north star's fp32 tolerance), R the restatement's fp32 result.
 """
@@ -77,11 +79,37 @@ def test_other_types_match_q8_restatement(dev, oracle, gt, M, N, K):
     assert err <= 1e-3
 
 
+# few rows: every row count of a template (1, 2, 4, 8, 16) and between, K
+# split into several slices (long rows, few row groups), rows not a multiple
+# of 128, all three types
+FEW = [(hb.Q4_K, 1, 4096, 14336), (hb.Q4_K, 3, 384, 4096), (hb.Q4_K, 8, 4096, 14336), (hb.Q4_K, 16, 1024, 2048),
+       (hb.Q4_0, 2, 1024, 8192), (hb.Q4_0, 8, 4096, 11008), (hb.Q4_0, 13, 96, 1024), (hb.Q8_0, 4, 2048, 4096),
+       (hb.Q8_0, 8, 4096, 4096), (hb.Q8_0, 16, 160, 640)]
+
+
+@pytest.mark.parametrize("gt,M,N,K", FEW)
+def test_few_rows_match_q8_restatement(dev, oracle, gt, M, N, K):
+    W = synth.quant_matrix(gt, N, K, seed=M * 5 + K)
+    X = np.random.default_rng(M + 7 * K).standard_normal((M, K), dtype=np.float32)
+    Y = run(dev, W, X, M, N, K, gt)
+    R = np.stack([oracle.matvec_q8(gt, W, X[m], N, K, threads=8) for m in range(M)])
+    err = rel_err(Y, R)
+    print(f"few rows type {gt} M={M} N={N} K={K}: norm-wise rel err {err:.3e}")
+    assert err <= 1e-3
+
+
+def test_few_rows_deterministic(dev):
+    gt, M, N, K = hb.Q4_0, 8, 4096, 14336
+    W = synth.quant_matrix(gt, N, K, seed=9)
+    X = np.random.default_rng(9).standard_normal((M, K), dtype=np.float32)
+    assert np.array_equal(run(dev, W, X, M, N, K, gt), run(dev, W, X, M, N, K, gt))
+
+
 def test_rejects_untiled_or_misaligned(dev):
     W = synth.quant_matrix(hb.Q4_K, 100, 256, seed=1)        # 100 rows: not a multiple of 128
     Wd = dev.upload_quant(W, hb.Q4_K, 100, 256)
-    Xd, Yd = dev.alloc(4 * 256), dev.alloc(4 * 100)
-    rc = dev.lib.cuda_matmul_quant_batched(Yd, Wd, Xd, 1, 100, 256)
+    Xd, Yd = dev.alloc(4 * 256 * 17), dev.alloc(4 * 100 * 17)
+    rc = dev.lib.cuda_matmul_quant_batched(Yd, Wd, Xd, 17, 100, 256)   # tensor-core path (M > 16)
     assert rc == hb.HOLO_E_ARG
     dev.lib.cuda_clear_status()
     raw = dev.upload(np.zeros(256 * 144 // 256 * 128, np.uint8))   # not from cuda_upload_quant
