@@ -736,7 +736,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="--profile-decode: first N layers only")
     ap.add_argument("--no-prefill", action="store_true", help="skip the tcgen05 prefill sub-benchmark")
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill sub-benchmark")
-    ap.add_argument("--profile-prefill", default=None, help="e.g. 512:14336x4096 (ncu case: M:NxK)")
+    ap.add_argument("--profile-prefill", default=None,
+                    help="e.g. 512:14336x4096 or 8:57344x8192:q4_0 (ncu case: M:NxK[:type], Q4_K by default)")
     ap.add_argument("--profile-case", default=None, help="e.g. q4_k:11008x4096 (ncu small case)")
     ap.add_argument("--iters", type=int, default=4)
     args = ap.parse_args()
@@ -748,11 +749,13 @@ def main():
         return
     if args.profile_prefill:
         import torch
-        m, nk = args.profile_prefill.split(":")
+        fields = args.profile_prefill.split(":")
+        m, nk = fields[0], fields[1]
+        gt = {"q4_k": hb.Q4_K, "q4_0": hb.Q4_0, "q8_0": hb.Q8_0}[fields[2] if len(fields) > 2 else "q4_k"]
         n, k = (int(v) for v in nk.split("x"))
         m = int(m)
         dev = hb.Device(0, 1)
-        Wd = dev.upload_quant(synth.quant_matrix(hb.Q4_K, n, k, 0), hb.Q4_K, n, k)
+        Wd = dev.upload_quant(synth.quant_matrix(gt, n, k, 0), gt, n, k)
         Xd, Yd = dev.upload(synth.activation(m * k, 0)), dev.alloc(4 * m * n)
         for _ in range(args.iters):
             dev.lib.cuda_matmul_quant_batched(Yd, Wd, Xd, m, n, k)
