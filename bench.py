@@ -276,6 +276,7 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_decode:
         decode = decode_bench(args, world, rank, torch)
     prefill = prefill_bench(dev, torch) if rank == 0 and not args.no_prefill else None
+    other_types = other_types_bench(dev, torch) if rank == 0 and not args.no_prefill else None
 
     traffic = read_traffic()
     line = {
@@ -304,6 +305,8 @@ def run_ours(args, rank, world, local_rank):
         line["decode"] = decode
     if prefill:
         line["prefill"] = prefill
+    if other_types is not None:
+        line["other_types"] = other_types
     if ref_gpu:
         line["reference_gpu_kernels"] = ref_gpu
     if cpu:
@@ -494,6 +497,55 @@ def decode_bench(args, world, rank, torch):
 
 PREFILL_SHAPES = [(14336, 4096), (4096, 14336)]
 PREFILL_M = [64, 256, 512]
+
+
+def other_types_bench(dev, torch, iters=10):
+    """Q6_K and F16 matvecs (the types real Q4_K_M files keep for some
+    tensors): the tiled path (cuda_upload_quant, unit layout) against the raw
+    GGUF path (cuda_malloc + cuda_memcpy_h2d of the blocks, as the reference's
+    upload_tensor does), both through the reference entry points
+    (cuda_matmul_q6_k / cuda_matmul_f16), fp32 activations.  Device time from
+    CUDA events on the library stream over `iters` rotations of distinct
+    matrices larger than L2 together; GB/s of GGUF weight bytes."""
+    lib = dev.lib
+    stream = torch.cuda.ExternalStream(lib.cuda_get_stream())
+    hbm, _ = peaks()
+    cases = [(hb.Q6_K, 4096, 11008, 4), (hb.Q6_K, 11008, 4096, 4), (hb.F16, 4096, 11008, 2)]
+    out = []
+    for gt, r, c, n in cases:
+        fn = lib.cuda_matmul_q6_k if gt == hb.Q6_K else lib.cuda_matmul_f16
+        mats = []
+        for s in range(n):
+            W = synth.quant_matrix(gt, r, c, s) if gt == hb.Q6_K else synth.f16_matrix(r, c, s).view(np.uint8).reshape(-1)
+            raw = dev.alloc(W.nbytes)
+            lib.cuda_memcpy_h2d(raw, W.ctypes.data, W.nbytes)
+            mats.append((dev.upload_quant(W, gt, r, c), raw))
+        xd, yd = dev.upload(synth.activation(c, 0)), dev.alloc(4 * r)
+        wbytes = r * hb.row_bytes(gt, c)
+        res = {"type": hb.TYPE_NAMES[gt], "rows": r, "cols": c}
+        for label, k in (("tiled", 0), ("raw", 1)):
+            for _ in range(2):
+                for m in mats:
+                    fn(yd, m[k], xd, r, c)
+            dev.check("other types warm-up")
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(iters):
+                for m in mats:
+                    fn(yd, m[k], xd, r, c)
+            e1.record(stream)
+            e1.synchronize()
+            dev.check("other types")
+            us = e0.elapsed_time(e1) * 1e3 / (iters * len(mats))
+            res[label] = {"us": round(us, 2), "gbs": round(wbytes / (us * 1e-6) / 1e9, 1),
+                          "hbm_frac": round(wbytes / (us * 1e-6) / 1e9 / hbm, 4)}
+        out.append(res)
+        for m in mats:
+            dev.free(m[0])
+            dev.free(m[1])
+        dev.free(xd)
+        dev.free(yd)
+    return out
 
 
 def prefill_bench(dev, torch, iters=20):

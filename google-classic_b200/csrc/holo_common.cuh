@@ -56,6 +56,19 @@ template <> struct UnitGeom<GT_Q4_K> {
     static constexpr int BLK_ELEMS = 256, BLK_BYTES = 144, VALS = 256, BLKS32 = 8, HEAD_BYTES = 16;
     static constexpr int UNIT_BYTES = TILE_ROWS * HEAD_BYTES + UNIT_PLANES * TILE_ROWS * 16;   // 4608
 };
+// Q6_K: a unit is one 128-value half of a super-block (src/ai/quant.c:251-268
+// walks the halves: 64 bytes of low codes, 32 of high bits, 8 scales each).
+// head: fp16 d, the half's 8 int8 scales, 6 zero bytes; planes 0-3: ql[0..63]
+// of the half (16 bytes each), planes 4-5: qh[0..31]; 6 planes a unit.
+template <> struct UnitGeom<GT_Q6_K> {
+    static constexpr int BLK_ELEMS = 256, BLK_BYTES = 210, VALS = 128, BLKS32 = 4, HEAD_BYTES = 16, PLANES = 6;
+    static constexpr int UNIT_BYTES = TILE_ROWS * HEAD_BYTES + PLANES * TILE_ROWS * 16;   // 3584
+};
+// F16: 64 values a row a unit, plane p = values 8p..8p+7 (no head)
+template <> struct UnitGeom<GT_F16> {
+    static constexpr int BLK_ELEMS = 1, BLK_BYTES = 2, VALS = 64, BLKS32 = 2, HEAD_BYTES = 0;
+    static constexpr int UNIT_BYTES = UNIT_PLANES * TILE_ROWS * 16;   // 4096
+};
 
 template <int T> __host__ __device__ constexpr size_t unit_head_off(int r) {
     return (size_t)r * UnitGeom<T>::HEAD_BYTES;
@@ -70,6 +83,8 @@ static inline int units_per_row(int type, int cols) {
     case GT_Q8_0: return (cols + UnitGeom<GT_Q8_0>::VALS - 1) / UnitGeom<GT_Q8_0>::VALS;
     case GT_Q4_0: return (cols + UnitGeom<GT_Q4_0>::VALS - 1) / UnitGeom<GT_Q4_0>::VALS;
     case GT_Q4_K: return cols / UnitGeom<GT_Q4_K>::VALS;
+    case GT_Q6_K: return cols / UnitGeom<GT_Q6_K>::VALS;
+    case GT_F16: return cols / UnitGeom<GT_F16>::VALS;
     default: return 0;
     }
 }
@@ -78,6 +93,8 @@ static inline int unit_bytes(int type) {
     case GT_Q8_0: return UnitGeom<GT_Q8_0>::UNIT_BYTES;
     case GT_Q4_0: return UnitGeom<GT_Q4_0>::UNIT_BYTES;
     case GT_Q4_K: return UnitGeom<GT_Q4_K>::UNIT_BYTES;
+    case GT_Q6_K: return UnitGeom<GT_Q6_K>::UNIT_BYTES;
+    case GT_F16: return UnitGeom<GT_F16>::UNIT_BYTES;
     default: return 0;
     }
 }

@@ -423,6 +423,12 @@ bool holo_matvec_launch_with(const void *M, const WeightInfo &wi, const MvLaunch
     case GT_Q4_K:
         p.nblk32p = p.units * UnitGeom<GT_Q4_K>::BLKS32;
         return dispatch_act<GT_Q4_K>(p, L.act, L.epi, norm, S.sms, S.max_ctas, L.pdl, st);
+    case GT_Q6_K:
+        p.nblk32p = p.units * UnitGeom<GT_Q6_K>::BLKS32;
+        return dispatch_act<GT_Q6_K>(p, L.act, L.epi, norm, S.sms, S.max_ctas, L.pdl, st);
+    case GT_F16:   // fp32 activations whatever the mode (x as staged)
+        p.nblk32p = p.units * UnitGeom<GT_F16>::BLKS32;
+        return dispatch_act<GT_F16>(p, HOLO_ACT_F32, L.epi, norm, S.sms, S.max_ctas, L.pdl, st);
     default:
         holo_set_status(HOLO_E_ARG, "matvec: type has no tiled kernel");
         return false;

@@ -42,9 +42,12 @@ struct Frag {
 template <int TYPE>
 __device__ __forceinline__ void load_unit(Frag &f, const uint8_t *__restrict__ unit, int lane) {
     const uint8_t *row = unit + (size_t)TILE_ROWS * UnitGeom<TYPE>::HEAD_BYTES + lane * 16;
+    constexpr int NPL = TYPE == GT_Q6_K ? UnitGeom<GT_Q6_K>::PLANES : UNIT_PLANES;
 #pragma unroll
-    for (int pl = 0; pl < UNIT_PLANES; ++pl) f.q[pl] = ldg_stream(row + pl * TILE_ROWS * 16);
-    if constexpr (TYPE == GT_Q8_0) {
+    for (int pl = 0; pl < NPL; ++pl) f.q[pl] = ldg_stream(row + pl * TILE_ROWS * 16);
+    if constexpr (TYPE == GT_F16) {
+        f.h = make_uint4(0u, 0u, 0u, 0u);
+    } else if constexpr (TYPE == GT_Q8_0) {
         const uint2 h = ldg_stream2(unit + lane * 8);
         f.h = make_uint4(h.x, h.y, 0u, 0u);
     } else {
@@ -57,9 +60,12 @@ __device__ __forceinline__ void load_unit(Frag &f, const uint8_t *__restrict__ u
 template <int TYPE>
 __device__ __forceinline__ void load_unit_smem(Frag &f, const uint8_t *unit, int lane) {
     const uint8_t *row = unit + (size_t)TILE_ROWS * UnitGeom<TYPE>::HEAD_BYTES + lane * 16;
+    constexpr int NPL = TYPE == GT_Q6_K ? UnitGeom<GT_Q6_K>::PLANES : UNIT_PLANES;
 #pragma unroll
-    for (int pl = 0; pl < UNIT_PLANES; ++pl) f.q[pl] = lds128(row + pl * TILE_ROWS * 16);
-    if constexpr (TYPE == GT_Q8_0) {
+    for (int pl = 0; pl < NPL; ++pl) f.q[pl] = lds128(row + pl * TILE_ROWS * 16);
+    if constexpr (TYPE == GT_F16) {
+        f.h = make_uint4(0u, 0u, 0u, 0u);
+    } else if constexpr (TYPE == GT_Q8_0) {
         const uint2 h = *reinterpret_cast<const uint2 *>(unit + lane * 8);
         f.h = make_uint4(h.x, h.y, 0u, 0u);
     } else {
@@ -71,6 +77,12 @@ __device__ __forceinline__ void load_unit_smem(Frag &f, const uint8_t *unit, int
 // shared-memory accesses before later async-proxy (bulk copy) writes
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// signed byte k (0..15) of a head word set, as an exact float
+__device__ __forceinline__ float sbyte_to_float_s(const uint4 &h, int k) {
+    const uint32_t w = k < 4 ? h.x : k < 8 ? h.y : k < 12 ? h.z : h.w;
+    return (float)(int8_t)(uint8_t)(w >> (8 * (k & 3)));
 }
 
 // fp16 scale k (0..7) of a head word set
@@ -106,6 +118,77 @@ __device__ __forceinline__ void unit_dot(float &acc, const Frag &f, int b0, cons
             } else {
                 acc += fmaf(sc, dot_nib16_f32<true>(f.q[j], xs + (size_t)blk * 32), -mn * xsum[blk]);
             }
+        }
+    } else if constexpr (TYPE == GT_Q6_K) {
+        // 32-block j of the half: values l = 0..15 from planes (j&1 ? 2 : 0)
+        // and 4, l = 16..31 from planes (j&1 ? 3 : 1) and 5; low nibbles for
+        // j < 2, high for j >= 2; high bits 2j..2j+1 of the qh byte; codes
+        // u = nib | qh2 << 4 (0..63), value d * sc * (u - 32) with scale
+        // 2j for l < 16 and 2j+1 above (quant.c:255-264)
+        const float d = half_bits_to_float(f.h.x & 0xffffu);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int nsh = (j & 2) ? 4 : 0, hsh = 2 * j;
+            const uint4 l0 = f.q[(j & 1) ? 2 : 0], l1 = f.q[(j & 1) ? 3 : 1], h0 = f.q[4], h1 = f.q[5];
+            uint32_t u[8];
+            u[0] = ((l0.x >> nsh) & LO4) | (((h0.x >> hsh) & 0x03030303u) << 4);
+            u[1] = ((l0.y >> nsh) & LO4) | (((h0.y >> hsh) & 0x03030303u) << 4);
+            u[2] = ((l0.z >> nsh) & LO4) | (((h0.z >> hsh) & 0x03030303u) << 4);
+            u[3] = ((l0.w >> nsh) & LO4) | (((h0.w >> hsh) & 0x03030303u) << 4);
+            u[4] = ((l1.x >> nsh) & LO4) | (((h1.x >> hsh) & 0x03030303u) << 4);
+            u[5] = ((l1.y >> nsh) & LO4) | (((h1.y >> hsh) & 0x03030303u) << 4);
+            u[6] = ((l1.z >> nsh) & LO4) | (((h1.z >> hsh) & 0x03030303u) << 4);
+            u[7] = ((l1.w >> nsh) & LO4) | (((h1.w >> hsh) & 0x03030303u) << 4);
+            const float w0 = d * sbyte_to_float_s(f.h, 2 + 2 * j), w1 = d * sbyte_to_float_s(f.h, 3 + 2 * j);
+            const int blk = b0 + j;
+            if constexpr (ACT == HOLO_ACT_Q8) {
+                const uint4 a0 = lds128(aq + (size_t)blk * 32), a1 = lds128(aq + (size_t)blk * 32 + 16);
+                int s0 = 0, s1 = 0, t0 = 0, t1 = 0;
+                s0 = dp4a_us(u[0], a0.x, s0); s0 = dp4a_us(u[1], a0.y, s0);
+                s0 = dp4a_us(u[2], a0.z, s0); s0 = dp4a_us(u[3], a0.w, s0);
+                s1 = dp4a_us(u[4], a1.x, s1); s1 = dp4a_us(u[5], a1.y, s1);
+                s1 = dp4a_us(u[6], a1.z, s1); s1 = dp4a_us(u[7], a1.w, s1);
+                t0 = __dp4a((int)a0.x, 0x01010101, t0); t0 = __dp4a((int)a0.y, 0x01010101, t0);
+                t0 = __dp4a((int)a0.z, 0x01010101, t0); t0 = __dp4a((int)a0.w, 0x01010101, t0);
+                t1 = __dp4a((int)a1.x, 0x01010101, t1); t1 = __dp4a((int)a1.y, 0x01010101, t1);
+                t1 = __dp4a((int)a1.z, 0x01010101, t1); t1 = __dp4a((int)a1.w, 0x01010101, t1);
+                // sum (u-32)*q over each 16: exact integers (|.| < 2^15)
+                const float i0 = int_to_float_exact(s0 - 32 * t0), i1 = int_to_float_exact(s1 - 32 * t1);
+                acc += ads[blk].x * fmaf(w0, i0, w1 * i1);
+            } else {
+                const float *xb = xs + (size_t)blk * 32;
+                float f0 = 0.0f, f1 = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float4 x0 = *reinterpret_cast<const float4 *>(xb + 4 * k);
+                    const float4 x1 = *reinterpret_cast<const float4 *>(xb + 16 + 4 * k);
+                    f0 = fmaf(ubyte_to_float(u[k], 0) - 32.0f, x0.x, f0);
+                    f0 = fmaf(ubyte_to_float(u[k], 1) - 32.0f, x0.y, f0);
+                    f0 = fmaf(ubyte_to_float(u[k], 2) - 32.0f, x0.z, f0);
+                    f0 = fmaf(ubyte_to_float(u[k], 3) - 32.0f, x0.w, f0);
+                    f1 = fmaf(ubyte_to_float(u[4 + k], 0) - 32.0f, x1.x, f1);
+                    f1 = fmaf(ubyte_to_float(u[4 + k], 1) - 32.0f, x1.y, f1);
+                    f1 = fmaf(ubyte_to_float(u[4 + k], 2) - 32.0f, x1.z, f1);
+                    f1 = fmaf(ubyte_to_float(u[4 + k], 3) - 32.0f, x1.w, f1);
+                }
+                acc += fmaf(w0, f0, w1 * f1);
+            }
+        }
+    } else if constexpr (TYPE == GT_F16) {
+        // fp32 activation in both modes (x as staged, before any quantization)
+#pragma unroll
+        for (int pl = 0; pl < UNIT_PLANES; ++pl) {
+            const float *xb = xs + (size_t)b0 * 32 + 8 * pl;
+            const float4 x0 = *reinterpret_cast<const float4 *>(xb), x1 = *reinterpret_cast<const float4 *>(xb + 4);
+            const uint4 q = f.q[pl];
+            const float2 w0 = __half22float2(*reinterpret_cast<const __half2 *>(&q.x));
+            const float2 w1 = __half22float2(*reinterpret_cast<const __half2 *>(&q.y));
+            const float2 w2 = __half22float2(*reinterpret_cast<const __half2 *>(&q.z));
+            const float2 w3 = __half22float2(*reinterpret_cast<const __half2 *>(&q.w));
+            float t = w0.x * x0.x;
+            t = fmaf(w0.y, x0.y, t); t = fmaf(w1.x, x0.z, t); t = fmaf(w1.y, x0.w, t);
+            t = fmaf(w2.x, x1.x, t); t = fmaf(w2.y, x1.y, t); t = fmaf(w3.x, x1.z, t); t = fmaf(w3.y, x1.w, t);
+            acc += t;
         }
     } else if constexpr (TYPE == GT_Q4_0) {
 #pragma unroll

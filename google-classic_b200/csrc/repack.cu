@@ -88,11 +88,46 @@ __global__ void repack_q4_k_kernel(uint8_t *__restrict__ out, const uint8_t *__r
     }
 }
 
+// Q6_K: one thread per (row, 128-value half); the half's bytes move as they
+// are (quant.c:251-268 reads them in this order)
+__global__ void repack_q6_k_kernel(uint8_t *__restrict__ out, const uint8_t *__restrict__ in, int rows, int nsb) {
+    using G = UnitGeom<GT_Q6_K>;
+    const int units = 2 * nsb;
+    int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)rows * units) return;
+    int r = (int)(gid / units), hf = (int)(gid % units);
+    const uint8_t *src = in + (size_t)r * nsb * G::BLK_BYTES + (size_t)(hf >> 1) * G::BLK_BYTES;
+    const int n = hf & 1, lr = r % TILE_ROWS;
+    uint8_t *unit = out + ((size_t)(r / TILE_ROWS) * units + hf) * G::UNIT_BYTES;
+    uint8_t *head = unit + unit_head_off<GT_Q6_K>(lr);
+    head[0] = src[208];
+    head[1] = src[209];
+    for (int k = 0; k < 8; k++) head[2 + k] = src[192 + n * 8 + k];
+    for (int p = 0; p < 4; p++)
+        for (int l = 0; l < 16; l++) unit[unit_plane_off<GT_Q6_K>(p, lr) + l] = src[n * 64 + p * 16 + l];
+    for (int p = 0; p < 2; p++)
+        for (int l = 0; l < 16; l++) unit[unit_plane_off<GT_Q6_K>(4 + p, lr) + l] = src[128 + n * 32 + p * 16 + l];
+}
+
+// F16: one thread per (row, 8 values)
+__global__ void repack_f16_kernel(uint8_t *__restrict__ out, const uint8_t *__restrict__ in, int rows, int cols) {
+    using G = UnitGeom<GT_F16>;
+    const int chunks = cols / 8, units = cols / G::VALS;
+    int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)rows * chunks) return;
+    int r = (int)(gid / chunks), c = (int)(gid % chunks);
+    const int lr = r % TILE_ROWS, s = c / UNIT_PLANES, p = c % UNIT_PLANES;
+    const uint4 v = *reinterpret_cast<const uint4 *>(in + ((size_t)r * cols + (size_t)c * 8) * 2);
+    uint8_t *unit = out + ((size_t)(r / TILE_ROWS) * units + s) * G::UNIT_BYTES;
+    *reinterpret_cast<uint4 *>(unit + unit_plane_off<GT_F16>(p, lr)) = v;
+}
+
 }  // namespace
 
 bool holo_quant_shape_ok(int type, int rows, int cols) {
     if (rows <= 0 || cols <= 0) return false;
-    if (type == GT_Q4_K) return cols % 256 == 0;
+    if (type == GT_Q4_K || type == GT_Q6_K) return cols % 256 == 0;
+    if (type == GT_F16) return cols % UnitGeom<GT_F16>::VALS == 0;
     if (type == GT_Q8_0 || type == GT_Q4_0) return cols % 32 == 0;
     return false;
 }
@@ -123,11 +158,24 @@ bool holo_repack_to(void *dst, const void *dev_blocks, int ggml_type, int rows, 
         int64_t n = (int64_t)rows * nblk;
         repack_q4_0_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
             (uint8_t *)dst, (const uint8_t *)dev_blocks, rows, nblk, units);
-    } else {
+    } else if (ggml_type == GT_Q4_K) {
         int nsb = cols / 256;
         int64_t n = (int64_t)rows * nsb;
         repack_q4_k_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
             (uint8_t *)dst, (const uint8_t *)dev_blocks, rows, nsb, q4k_layout == HOLO_Q4K_GGML);
+    } else if (ggml_type == GT_Q6_K) {
+        int nsb = cols / 256;
+        int64_t n = (int64_t)rows * nsb * 2;
+        repack_q6_k_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
+            (uint8_t *)dst, (const uint8_t *)dev_blocks, rows, nsb);
+    } else {
+        if ((uintptr_t)dev_blocks % 16) {
+            holo_set_status(HOLO_E_ARG, "repack: F16 rows must start 16-byte aligned");
+            return false;
+        }
+        int64_t n = (int64_t)rows * (cols / 8);
+        repack_f16_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(
+            (uint8_t *)dst, (const uint8_t *)dev_blocks, rows, cols);
     }
     return holo_check_launch("repack kernel");
 }

@@ -18,7 +18,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import BLOCK_BYTES, BLOCK_ELEMS, F16, Q4_0, Q4_K, Q8_0
+from . import BLOCK_BYTES, BLOCK_ELEMS, F16, Q4_0, Q4_K, Q6_K, Q8_0
 
 
 def _rng(seed: int) -> np.random.Generator:
@@ -64,6 +64,13 @@ def quant_matrix(gtype: int, rows: int, cols: int, seed: int) -> np.ndarray:
         out[:, 2:4] = dmin.view(np.uint8).reshape(nb, 2)
         out[:, 4:16] = pack_q4k_scales(codes[:, :8], codes[:, 8:])
         out[:, 16:] = (nib[:, :, :16] | (nib[:, :, 16:] << 4)).reshape(nb, 128)
+    elif gtype == Q6_K:
+        # ql, qh uniform bytes (6-bit codes uniform in 0..63), int8 scales
+        # uniform in [-64, 63], d as above
+        d = _scales(rng, nb)
+        out[:, 0:192] = rng.integers(0, 256, size=(nb, 192), dtype=np.uint8)
+        out[:, 192:208] = rng.integers(-64, 64, size=(nb, 16), dtype=np.int8).view(np.uint8)
+        out[:, 208:210] = d.view(np.uint8).reshape(nb, 2)
     else:
         raise ValueError(f"no generator for type {gtype}")
     return out.reshape(-1)

@@ -161,6 +161,27 @@ void ho_dequant_row(int type, const void *row, float *y, int64_t cols, int q4k_l
             }
         }
         break;
+    case HO_TYPE_Q6_K:                                       /* quant.c:241-275 */
+        for (int64_t s = 0; s < cols / 256; s++, p += 210) {
+            float d = ho_f16_to_f32(rd16(p + 208));
+            for (int n = 0; n < 2; n++) {
+                const uint8_t *ql = p + n * 64, *qh = p + 128 + n * 32;
+                const int8_t *sc = (const int8_t *)(p + 192) + n * 8;
+                float *yy = y + s * 256 + n * 128;
+                for (int l = 0; l < 32; l++) {
+                    int is = l / 16;
+                    int8_t q1 = (int8_t)((ql[l] & 0xF) | (((qh[l] >> 0) & 3) << 4)) - 32;
+                    int8_t q2 = (int8_t)((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+                    int8_t q3 = (int8_t)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+                    int8_t q4 = (int8_t)((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+                    yy[l] = d * sc[is + 0] * q1;
+                    yy[l + 32] = d * sc[is + 2] * q2;
+                    yy[l + 64] = d * sc[is + 4] * q3;
+                    yy[l + 96] = d * sc[is + 6] * q4;
+                }
+            }
+        }
+        break;
     case HO_TYPE_F16:
         for (int64_t i = 0; i < cols; i++) y[i] = ho_f16_to_f32(rd16(p + 2 * i));
         break;
@@ -230,6 +251,17 @@ static float row_q4_k_f32(const uint8_t *row, const float *x, int cols, int layo
     return sum;
 }
 
+/* quant.c:582-601: each super-block dequantized (quant.c:241-275), then one
+ * running sum over the values in order */
+static float row_q6_k_f32(const uint8_t *row, const float *x, int cols) {
+    float sum = 0.0f, tmp[256];
+    for (int s = 0; s < cols / 256; s++) {
+        ho_dequant_row(HO_TYPE_Q6_K, row + (int64_t)s * 210, tmp, 256, 0);
+        for (int j = 0; j < 256; j++) sum += tmp[j] * x[s * 256 + j];
+    }
+    return sum;
+}
+
 /* llm.c:817-827 */
 static float row_f16_f32(const uint8_t *row, const float *x, int cols) {
     float sum = 0.0f;
@@ -250,6 +282,7 @@ void ho_matvec_f32act(int type, const void *W, const float *x, float *y,
         case HO_TYPE_Q8_0: v = row_q8_0_f32(row, x, cols); break;
         case HO_TYPE_Q4_0: v = row_q4_0_f32(row, x, cols); break;
         case HO_TYPE_Q4_K: v = row_q4_k_f32(row, x, cols, q4k_layout); break;
+        case HO_TYPE_Q6_K: v = row_q6_k_f32(row, x, cols); break;
         case HO_TYPE_F16:  v = row_f16_f32(row, x, cols); break;
         default: v = 0.0f;
         }
@@ -330,6 +363,32 @@ void ho_matvec_q8act(int type, const void *W, const int8_t *q, const float *d,
                     if (is_row) is_row[b] = s;
                     float t = (dd * (float)sc[j]) * (float)s - (dmin * (float)mn[j]) * (float)asum[b];
                     acc += d[b] * t;
+                }
+            }
+        } else if (type == HO_TYPE_Q6_K) {
+            /* the value layout of quant.c:241-275; per 16 values (one scale)
+             * the integer sum of code * q, then d_a * (w0 * s0 + w1 * s1) per
+             * 32-block with w = d * scale (the build's own definition) */
+            for (int sb = 0; sb < cols / 256; sb++) {
+                const uint8_t *blk = row + (int64_t)sb * 210;
+                float dd = ho_f16_to_f32(rd16(blk + 208));
+                for (int n = 0; n < 2; n++) {
+                    const uint8_t *ql = blk + n * 64, *qh = blk + 128 + n * 32;
+                    const int8_t *sc = (const int8_t *)(blk + 192) + n * 8;
+                    for (int j = 0; j < 4; j++) {
+                        int b = sb * 8 + n * 4 + j;
+                        const int8_t *qa = q + b * 32;
+                        int32_t s2[2] = {0, 0};
+                        for (int l = 0; l < 32; l++) {
+                            int byte = (j & 1) ? ql[l + 32] : ql[l];
+                            int nib = (j & 2) ? (byte >> 4) : (byte & 0xF);
+                            int code = (nib | (((qh[l] >> (2 * j)) & 3) << 4)) - 32;
+                            s2[l / 16] += code * qa[l];
+                        }
+                        if (is_row) is_row[b] = s2[0] + s2[1];
+                        float w0 = dd * (float)sc[2 * j], w1 = dd * (float)sc[2 * j + 1];
+                        acc += d[b] * (w0 * (float)s2[0] + w1 * (float)s2[1]);
+                    }
                 }
             }
         }

@@ -138,7 +138,8 @@ class Reference:
         return y
 
     def dequant(self, gtype, blocks, rows, cols):
-        name = {8: "dequantize_row_q8_0", 2: "dequantize_row_q4_0", 12: "dequantize_row_q4_k"}[gtype]
+        name = {8: "dequantize_row_q8_0", 2: "dequantize_row_q4_0", 12: "dequantize_row_q4_k",
+                14: "dequantize_row_q6_k"}[gtype]
         blocks = np.ascontiguousarray(blocks)
         out = np.empty((rows, cols), np.float32)
         getattr(self.lib, name)(_ptr(blocks), _ptr(out), rows * cols)

@@ -3,7 +3,7 @@
 Run where the reference sources are present (they are compiled from source
 into oracle/_ref/libholo_ref.so by oracle/Makefile):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [fixture names]   # all when none given
 
 Each fixture holds the inputs (GGUF blocks, activation) and the outputs of the
 REFERENCE's own CPU functions on them: matmul_q (src/ai/llm.c:770-926) and
@@ -30,14 +30,17 @@ CASES = [
     ("q4_0_40x512", hb.Q4_0, 40, 512, 12),
     ("q4_k_33x512", hb.Q4_K, 33, 512, 13),
     ("q4_k_16x2304", hb.Q4_K, 16, 2304, 14),
+    ("q6_k_24x512", hb.Q6_K, 24, 512, 16),
 ]
 
 
-def main():
+def main(only=()):
     ref = holo_oracle.Reference()
     orc = holo_oracle.Oracle()
     out = pathlib.Path(__file__).resolve().parent
     for name, gt, rows, cols, seed in CASES:
+        if only and name not in only:
+            continue
         W = synth.quant_matrix(gt, rows, cols, seed)
         x = synth.activation(cols, seed)
         y_ref = ref.matmul_q(gt, W, x, rows, cols)
@@ -48,6 +51,8 @@ def main():
                             y_ref=y_ref, deq_ref=deq_ref, act_q=q, act_d=d, act_s=s,
                             y_q8=y_q8, isums=isums)
         print("wrote", name)
+    if only and "q4_k_ref_8x512" not in only:
+        return
     # ggml-semantics Q4_K: the same values as a quant.c-semantics block set
     W = synth.quant_matrix(hb.Q4_K, 8, 512, 15)
     deq = ref.dequant(hb.Q4_K, W, 8, 512)
@@ -56,4 +61,4 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    main(tuple(sys.argv[1:]))

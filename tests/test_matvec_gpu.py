@@ -56,6 +56,48 @@ def test_tiled_matvec_parity(dev, oracle, reference, gtype, rows, cols):
     dev.free(Wd)
 
 
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_tiled_q6_k_parity(dev, oracle, reference, rows, cols):
+    """Q6_K in the unit layout (one 128-value half of a super-block a unit):
+    HOLO_ACT_F32 against the reference's matmul_q (mat_vec_q6_k), HOLO_ACT_Q8
+    against the oracle's restatement; the reference entry point on the same
+    (registered) pointer gives the fp32 result."""
+    gtype = hb.Q6_K
+    seed = rows + 3 * cols + gtype
+    W = synth.quant_matrix(gtype, rows, cols, seed)
+    x = synth.activation(cols, seed)
+    Wd = dev.upload_quant(W, gtype, rows, cols)
+    want = reference.matmul_q(gtype, W, x, rows, cols)
+    y32 = run_matvec(dev, Wd, gtype, x, rows, cols, hb.ACT_F32)
+    assert rel_err(y32, want) <= TOL
+    y8 = run_matvec(dev, Wd, gtype, x, rows, cols, hb.ACT_Q8)
+    assert rel_err(y8, oracle.matvec_q8(gtype, W, x, rows, cols)) <= TOL
+    xd, yd = dev.upload(x), dev.alloc(rows * 4)
+    dev.lib.cuda_matmul_q6_k(yd, Wd, xd, rows, cols)
+    assert np.array_equal(dev.download(yd, (rows,), np.float32), y32)
+    dev.check("cuda_matmul_q6_k")
+    for p in (Wd, xd, yd):
+        dev.free(p)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 64), (33, 512), (100, 4096), (257, 1024), (64, 11008)])
+def test_tiled_f16_parity(dev, reference, rows, cols):
+    """F16 weights in the unit layout (64 values a row a unit), fp32
+    activations in both modes: against the reference's matmul_q (llm.c:818-828)
+    and an fp64 product of the same values."""
+    gtype = hb.F16
+    Wh = synth.f16_matrix(rows, cols, seed=rows + cols)
+    W = Wh.view(np.uint8).reshape(-1)
+    x = synth.activation(cols, rows)
+    Wd = dev.upload_quant(W, gtype, rows, cols)
+    exact = (Wh.astype(np.float64) @ x.astype(np.float64)).astype(np.float32)
+    for act in (hb.ACT_F32, hb.ACT_Q8):
+        y = run_matvec(dev, Wd, gtype, x, rows, cols, act)
+        assert rel_err(y, reference.matmul_q(gtype, W, x, rows, cols)) <= TOL
+        assert rel_err(y, exact) <= 1e-5
+    dev.free(Wd)
+
+
 @pytest.mark.parametrize("gtype", [hb.Q8_0, hb.Q4_0])
 @pytest.mark.parametrize("rows,cols", [(45, 96), (70, 1440), (33, 4128), (5, 32)])
 def test_padded_last_unit_parity(dev, oracle, reference, gtype, rows, cols):

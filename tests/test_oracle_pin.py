@@ -8,7 +8,7 @@ import holo_b200 as hb
 from holo_b200 import synth
 from conftest import GOLDEN
 
-FIXTURES = ["q8_0_48x256", "q4_0_40x512", "q4_k_33x512", "q4_k_16x2304"]
+FIXTURES = ["q8_0_48x256", "q4_0_40x512", "q4_k_33x512", "q4_k_16x2304", "q6_k_24x512"]
 
 
 def bits(a):
@@ -40,7 +40,8 @@ def test_fixture_inputs_are_reproducible():
 
 
 @pytest.mark.parametrize("gt,rows,cols", [(hb.Q8_0, 37, 1024), (hb.Q4_0, 5, 11008), (hb.Q4_K, 3, 11008),
-                                          (hb.Q4_K, 65, 4096), (hb.Q8_0, 1, 32), (hb.Q4_0, 2, 32)])
+                                          (hb.Q4_K, 65, 4096), (hb.Q8_0, 1, 32), (hb.Q4_0, 2, 32),
+                                          (hb.Q6_K, 7, 4096), (hb.Q6_K, 1, 256)])
 def test_oracle_matches_compiled_reference(oracle, reference, gt, rows, cols):
     seed = rows * 7 + cols
     W = synth.quant_matrix(gt, rows, cols, seed)
