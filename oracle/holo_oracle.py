@@ -102,8 +102,14 @@ class Reference:
         lib = C.CDLL(str(REF_SO))
         lib.matmul_q.argtypes = [_vp, _vp, _vp, _i, _i, _i]
         lib.href_matmul_q_threads.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i]
-        for name in ("dequantize_row_q8_0", "dequantize_row_q4_0", "dequantize_row_q4_k"):
+        for name in ("dequantize_row_q8_0", "dequantize_row_q4_0", "dequantize_row_q4_k", "dequantize_row_q6_k"):
             getattr(lib, name).argtypes = [_vp, _vp, _i]
+        lib.href_gguf_tensor.restype = C.c_longlong
+        lib.href_gguf_tensor.argtypes = [C.c_char_p, C.c_char_p, _vp, C.c_longlong, C.POINTER(C.c_int)]
+        lib.href_gguf_int.restype = C.c_longlong
+        lib.href_gguf_int.argtypes = [C.c_char_p, C.c_char_p, C.c_longlong]
+        lib.href_gguf_float.restype = C.c_double
+        lib.href_gguf_float.argtypes = [C.c_char_p, C.c_char_p, C.c_double]
         lib.f16_to_f32.restype = _f
         lib.f16_to_f32.argtypes = [C.c_uint16]
         lib.href_model_create.restype = _vp
@@ -136,6 +142,22 @@ class Reference:
         y = np.empty(rows, np.float32)
         self.lib.href_matmul_q_threads(_ptr(y), _ptr(blocks), _ptr(x), rows, cols, gtype, threads)
         return y
+
+    def gguf_tensor(self, path, name, cap):
+        """The bytes the reference's loader reads for tensor `name` of a GGUF
+        file (its own parser), and their ggml type."""
+        buf = np.zeros(cap, np.uint8)
+        t = C.c_int(0)
+        n = self.lib.href_gguf_tensor(str(path).encode(), name.encode(), _ptr(buf), cap, C.byref(t))
+        if n < 0:
+            raise RuntimeError(f"reference gguf parser: {n} for {name}")
+        return buf[:n], t.value
+
+    def gguf_int(self, path, key, default=-1):
+        return self.lib.href_gguf_int(str(path).encode(), key.encode(), default)
+
+    def gguf_float(self, path, key, default=-1.0):
+        return self.lib.href_gguf_float(str(path).encode(), key.encode(), default)
 
     def dequant(self, gtype, blocks, rows, cols):
         name = {8: "dequantize_row_q8_0", 2: "dequantize_row_q4_0", 12: "dequantize_row_q4_k",

@@ -9,6 +9,7 @@
  * and call the reference's own entry points: matmul_q (llm.c:770),
  * llm_forward (llm.c:1015), llm_sample (llm.c:1281), llm_reset (llm.c:732).
  */
+#include "gguf.h"
 #include "llm.h"
 #include "quant.h"
 
@@ -146,4 +147,39 @@ void href_model_free(href_model_t *m) {
     free(c->kv_cache.key_cache); free(c->kv_cache.value_cache);
     free(c->weights.layers); free(c->tokens);
     free(m);
+}
+
+/* The reference's GGUF parser (gguf_open, gguf.c:280-395; gguf_mmap;
+ * gguf_get_tensor_data, gguf.c:504-510) on a file: the bytes its loader
+ * would hand to upload_tensor for tensor `name`, copied into dst (at most
+ * cap).  Returns the byte count, or -1 (open), -2 (map), -3 (no such
+ * tensor), -4 (cap too small); *type gets the tensor's ggml type. */
+long long href_gguf_tensor(const char *path, const char *name, void *dst, long long cap, int *type) {
+    gguf_ctx_t *g = gguf_open(path);
+    if (!g) return -1;
+    if (gguf_mmap(g) != 0) { gguf_close(g); return -2; }
+    const gguf_tensor_info_t *t = gguf_find_tensor(g, name);
+    if (!t) { gguf_close(g); return -3; }
+    long long n = (long long)t->size_bytes;
+    if (n > cap) { gguf_close(g); return -4; }
+    memcpy(dst, gguf_get_tensor_data(g, t), (size_t)n);
+    *type = (int)t->type;
+    gguf_close(g);
+    return n;
+}
+
+/* gguf_get_int / gguf_get_float (gguf.c) on a file's metadata */
+long long href_gguf_int(const char *path, const char *key, long long dflt) {
+    gguf_ctx_t *g = gguf_open(path);
+    if (!g) return dflt;
+    long long v = (long long)gguf_get_int(g, key, dflt);
+    gguf_close(g);
+    return v;
+}
+double href_gguf_float(const char *path, const char *key, double dflt) {
+    gguf_ctx_t *g = gguf_open(path);
+    if (!g) return dflt;
+    double v = (double)gguf_get_float(g, key, (float)dflt);
+    gguf_close(g);
+    return v;
 }
