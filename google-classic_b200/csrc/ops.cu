@@ -266,6 +266,45 @@ __global__ void embedding_kernel(float *dst, const uint8_t *table, int token, in
     }
 }
 
+// Q4_K embedding row (the reference's GPU dispatcher, llm_cuda.c:166-186, has
+// no Q4_K case): value i of the row, decoded as quant.c:277-311 does (scale
+// unpack quant.c:290-297, sub-block j = 16 bytes, low nibble -> position l,
+// high -> l + 16) or, ggml != 0, as llama.cpp packs the block
+// (get_scale_min_k4, cuda_ops.cu:684-692; 32 bytes per 64 values, low
+// nibbles the first 32).  y = (d*sc)*q - dmin*m, each product rounded once.
+__global__ void q4k_embedding_kernel(float *dst, const uint8_t *table, int token, int dim, int ggml) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= dim) return;
+    const uint8_t *blk = table + ((size_t)token * (dim / 256) + i / 256) * 144;
+    const int v = i % 256, j = v / 32, l = v % 32;
+    const uint8_t *q = blk + 4;
+    int sc, mn, nib;
+    if (!ggml) {
+        if (j < 4) {
+            sc = q[j] & 0x3f;
+            mn = q[j + 4] & 0x3f;
+        } else {
+            sc = ((q[j + 4] & 0x0f) << 2) | (q[j - 4] >> 6);
+            mn = ((q[j + 4] >> 4) << 2) | (q[j] >> 6);
+        }
+        const uint8_t byte = blk[16 + j * 16 + (l & 15)];
+        nib = l < 16 ? (byte & 0x0f) : (byte >> 4);
+    } else {
+        if (j < 4) {
+            sc = q[j] & 63;
+            mn = q[j + 4] & 63;
+        } else {
+            sc = (q[j + 4] & 0x0f) | ((q[j - 4] >> 6) << 4);
+            mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+        }
+        const uint8_t byte = blk[16 + (j >> 1) * 32 + l];
+        nib = (j & 1) ? (byte >> 4) : (byte & 0x0f);
+    }
+    const float d = half_bits_to_float(blk[0] | (blk[1] << 8)), dmin = half_bits_to_float(blk[2] | (blk[3] << 8));
+    const float scale = __fmul_rn(d, (float)sc), mval = __fmul_rn(dmin, (float)mn);
+    dst[i] = __fsub_rn(__fmul_rn(scale, (float)nib), mval);
+}
+
 // argmax, first maximum wins (tensor.c:460-470)
 __device__ __forceinline__ void argmax_merge(float &bv, int &bi, float v, int i) {
     if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
@@ -474,6 +513,16 @@ HOLO_EMB(cuda_get_embedding_f16, GT_F16, true)
 HOLO_EMB(cuda_get_embedding_q8_0, GT_Q8_0, dim % 32 == 0)
 HOLO_EMB(cuda_get_embedding_q4_0, GT_Q4_0, dim % 32 == 0)
 HOLO_EMB(cuda_get_embedding_q6_k, GT_Q6_K, dim % 256 == 0)
+void cuda_get_embedding_q4_k(float *dst, const void *emb, int token, int dim, int vocab_size) {
+    if (!args_ok(dst, dim, "cuda_get_embedding_q4_k") || dim == 0 || !emb || token < 0 ||
+        (vocab_size > 0 && token >= vocab_size) || dim % 256) {
+        holo_set_status(HOLO_E_ARG, "cuda_get_embedding_q4_k");
+        return;
+    }
+    q4k_embedding_kernel<<<ew_grid(dim), EW_THREADS, 0, holo_stream()>>>(dst, (const uint8_t *)emb, token, dim,
+                                                                         holo_q4k_layout() == HOLO_Q4K_GGML);
+    holo_check_launch("cuda_get_embedding_q4_k");
+}
 void cuda_get_embedding_f32(float *dst, const float *embeddings, int token, int dim, int vocab_size) {
     if (!args_ok(dst, dim, "cuda_get_embedding_f32") || !embeddings || token < 0 ||
         (vocab_size > 0 && token >= vocab_size)) {

@@ -69,6 +69,7 @@ SIGNATURES = {
     "cuda_get_embedding_f32": (None, [_vp, _vp, _i, _i, _i]), "cuda_get_embedding_f16": (None, [_vp, _vp, _i, _i, _i]),
     "cuda_get_embedding_q8_0": (None, [_vp, _vp, _i, _i, _i]), "cuda_get_embedding_q4_0": (None, [_vp, _vp, _i, _i, _i]),
     "cuda_get_embedding_q6_k": (None, [_vp, _vp, _i, _i, _i]),
+    "cuda_get_embedding_q4_k": (None, [_vp, _vp, _i, _i, _i]),
     "cuda_argmax": (_i, [_vp, _i]),
     # holo_b200.h
     "cuda_last_status": (_i, []), "cuda_last_status_string": (C.c_char_p, []), "cuda_clear_status": (None, []),

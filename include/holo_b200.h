@@ -51,6 +51,11 @@ int cuda_get_act_mode(void);
 #define HOLO_Q4K_GGML 1
 void cuda_set_q4k_layout(int layout);
 int cuda_get_q4k_layout(void);
+/* Embedding row of a Q4_K table (raw GGUF blocks, token x dim, dim % 256 ==
+ * 0), decoded in the current Q4_K layout.  Completes the embedding lookups of
+ * cuda_ops.h: the reference's dispatcher (src/ai/llm_cuda.c:166-186) has no
+ * Q4_K case and falls through to the F32 lookup. */
+void cuda_get_embedding_q4_k(float *dst, const void *embeddings, int token, int dim, int vocab_size);
 
 /* ---- repacked weights (replaces upload_tensor, src/ai/llm_cuda.c:189-196) ---
  * Uploads `rows` x `cols` values of GGUF blocks of `ggml_type` (Q8_0, Q4_0,

@@ -164,6 +164,36 @@ def test_attention_scores_apply(dev):
         dev.free(p)
 
 
+@pytest.mark.parametrize("layout", [hb.Q4K_REF, hb.Q4K_GGML], ids=["quant_c", "ggml"])
+def test_q4_k_and_q6_k_embeddings(dev, reference, layout):
+    """cuda_get_embedding_q4_k (no Q4_K case in the reference's dispatcher)
+    in both Q4_K packings, and cuda_get_embedding_q6_k: bit-exact with the
+    reference's dequantize_row_q4_k / _q6_k of the same row."""
+    from test_oracle_pin import ggml_from_ref
+    vocab, dim = 300, 512
+    table = synth.quant_matrix(hb.Q4_K, vocab, dim, 18)
+    stored = ggml_from_ref(table) if layout == hb.Q4K_GGML else table
+    q6 = synth.quant_matrix(hb.Q6_K, vocab, dim, 19)
+    old = dev.lib.cuda_get_q4k_layout()
+    dev.lib.cuda_set_q4k_layout(layout)
+    try:
+        td, t6, od = up(dev, stored), up(dev, q6), dev.alloc(dim * 4)
+        for tok in (0, 77, vocab - 1):
+            dev.lib.cuda_get_embedding_q4_k(od, td, tok, dim, vocab)
+            rb = hb.row_bytes(hb.Q4_K, dim)
+            want = reference.dequant(hb.Q4_K, table[tok * rb:(tok + 1) * rb], 1, dim)[0]
+            assert np.array_equal(dev.download(od, (dim,), np.float32).view(np.uint32), want.view(np.uint32))
+            dev.lib.cuda_get_embedding_q6_k(od, t6, tok, dim, vocab)
+            rb = hb.row_bytes(hb.Q6_K, dim)
+            want = reference.dequant(hb.Q6_K, q6[tok * rb:(tok + 1) * rb], 1, dim)[0]
+            assert np.array_equal(dev.download(od, (dim,), np.float32).view(np.uint32), want.view(np.uint32))
+        dev.check()
+        for p in (td, t6, od):
+            dev.free(p)
+    finally:
+        dev.lib.cuda_set_q4k_layout(old)
+
+
 @pytest.mark.parametrize("gtype", [hb.F16, hb.Q8_0, hb.Q4_0])
 def test_embeddings(dev, reference, gtype):
     vocab, dim = 300, 4096
