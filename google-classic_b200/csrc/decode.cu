@@ -72,15 +72,16 @@ __global__ void dec_embed_kernel(float *__restrict__ x, const void *__restrict__
 }
 
 // ---------------------------------------------------------------------------
-// RoPE of q (n_heads) and k (n_kv_heads) at pos, then k and v appended to the
-// layer's cache; one CTA per head, one thread per rotation pair.  Several
+// RoPE of q (n_heads) and k (n_kv_heads) at pos (pairs by `mode`,
+// holo_model_desc.rope_mode), then k and v appended to the layer's cache;
+// one CTA per head, one thread per rotation pair.  Several
 // rows: row blockIdx.y = b * rps + i (qkv_bs floats apart) is position pos + i
 // of sequence b, whose cache starts kv_bs elements after sequence b-1's
 // ---------------------------------------------------------------------------
 template <typename KV>
 __global__ void dec_rope_append_kernel(float *__restrict__ qkv, KV *__restrict__ kc, KV *__restrict__ vc,
                                        const int *__restrict__ pos_p, int hd, int n_heads, int n_kv_heads,
-                                       float base, size_t qkv_bs, size_t kv_bs, int rps) {
+                                       float base, size_t qkv_bs, size_t kv_bs, int rps, int mode) {
     dec_pdl_trigger();
     dec_pdl_wait();
     const int r = blockIdx.y, b = r / rps;
@@ -93,21 +94,23 @@ __global__ void dec_rope_append_kernel(float *__restrict__ qkv, KV *__restrict__
     const int q_dim = n_heads * hd, kv_dim = n_kv_heads * hd;
     float c, s;
     rope_cos_sin(pos, i, hd, base, c, s);
+    // the rotation pair of frequency i: (i, i + hd/2), or (2i, 2i+1)
+    const int i0 = mode == HOLO_ROPE_ADJACENT ? 2 * i : i, i1 = mode == HOLO_ROPE_ADJACENT ? 2 * i + 1 : i + half;
     if (h < n_heads) {
         float *qh = qkv + (size_t)h * hd;
-        rope_rotate(qh[i], qh[i + half], c, s);
+        rope_rotate(qh[i0], qh[i1], c, s);
     }
     if (h < n_kv_heads) {
         const float *kh = qkv + q_dim + (size_t)h * hd;
         const float *vh = qkv + q_dim + kv_dim + (size_t)h * hd;
-        float a = kh[i], b = kh[i + half];
+        float a = kh[i0], b = kh[i1];
         rope_rotate(a, b, c, s);
         KV *kd = kc + (size_t)pos * kv_dim + (size_t)h * hd;
         KV *vd = vc + (size_t)pos * kv_dim + (size_t)h * hd;
-        kd[i] = to_kv<KV>(a);
-        kd[i + half] = to_kv<KV>(b);
-        vd[i] = to_kv<KV>(vh[i]);
-        vd[i + half] = to_kv<KV>(vh[i + half]);
+        kd[i0] = to_kv<KV>(a);
+        kd[i1] = to_kv<KV>(b);
+        vd[i0] = to_kv<KV>(vh[i0]);
+        vd[i1] = to_kv<KV>(vh[i1]);
     }
 }
 
@@ -720,11 +723,11 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
         if (d.kv_f16)
             ok = ok && launch_pdl(dec_rope_append_kernel<__half>, dim3(heads), dim3(hd / 2), st, pdl, m->qkv,
                                   (__half *)kc, (__half *)vc, (const int *)m->d_pos, hd, d.n_heads, d.n_kv_heads,
-                                  d.rope_base, (size_t)0, (size_t)0, 1);
+                                  d.rope_base, (size_t)0, (size_t)0, 1, d.rope_mode);
         else
             ok = ok && launch_pdl(dec_rope_append_kernel<float>, dim3(heads), dim3(hd / 2), st, pdl, m->qkv,
                                   (float *)kc, (float *)vc, (const int *)m->d_pos, hd, d.n_heads, d.n_kv_heads,
-                                  d.rope_base, (size_t)0, (size_t)0, 1);
+                                  d.rope_base, (size_t)0, (size_t)0, 1, d.rope_mode);
         const int group = d.n_heads / d.n_kv_heads;
         const dim3 ag(d.n_heads, m->max_splits);
 #define HOLO_ATTN(KVT, HDV)                                                                                   \
@@ -844,7 +847,7 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
         const dim3 pg(m->nkv, (p.rps + qt - 1) / qt, M / p.rps);
 #define BT_ATTN(KVT, HDV)                                                                                          \
     launch_pdl(dec_rope_append_kernel<KVT>, rg, dim3(hd / 2), st, false, p.qkv, (KVT *)kc, (KVT *)vc, p.pos, hd,     \
-               m->nh, m->nkv, d.rope_base, (size_t)qkv_dim, p.kv_bs, p.rps) &&                                      \
+               m->nh, m->nkv, d.rope_base, (size_t)qkv_dim, p.kv_bs, p.rps, d.rope_mode) &&                         \
         (p.prompt ? launch_pdl_smem(pf_attn_kernel<KVT, HDV>, pg, dim3(PA_WARPS * 32), pa_smem(HDV), st, false,      \
                                     p.att, (const float *)p.qkv, (const KVT *)kc, (const KVT *)vc, p.pos, p.rps, qt, \
                                     group, m->kv_dim, (size_t)qkv_dim, (size_t)m->q_dim, p.kv_bs, sqrt_hd)          \
@@ -1207,6 +1210,7 @@ StepArgs step_args(HoloModel *m, bool sample, const SampleArgs &sa) {
     a.vocab_loc = m->vocab_loc; a.v0 = m->v0;
     a.hd = d.head_dim; a.ffn = d.ffn_dim; a.vocab = d.vocab; a.max_seq = d.max_seq;
     a.eps = d.eps; a.rope_base = d.rope_base; a.out_type = d.out_type; a.emb_f16 = d.emb_type == 1;
+    a.rope_mode = d.rope_mode;
     a.layers = m->d_layers; a.emb = m->emb; a.final_norm = m->final_norm; a.out_w = m->out;
     a.qkv = m->qkv_ll; a.logits = m->logits;
     a.kc = m->kc; a.vc = m->vc; a.att_part = m->part; a.att_cnt = m->d_att_cnt;
@@ -1288,6 +1292,10 @@ void *holo_model_create(const holo_model_desc *desc) {
     int sh[10];
     if (!shard_of(d, sh) || (world > 1 && hd != 128)) {
         holo_set_status(HOLO_E_ARG, "holo_model_create: unsupported sharding");
+        return nullptr;
+    }
+    if (d.rope_mode != HOLO_ROPE_HALF && d.rope_mode != HOLO_ROPE_ADJACENT) {
+        holo_set_status(HOLO_E_ARG, "holo_model_create: rope_mode must be HOLO_ROPE_HALF or HOLO_ROPE_ADJACENT");
         return nullptr;
     }
     if (d.batch > 1 && (world > 1 || d.batch > 64)) {

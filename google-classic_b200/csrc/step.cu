@@ -424,9 +424,20 @@ template <> __device__ __forceinline__ __half to_kv_st<__half>(float v) { return
 __device__ __forceinline__ float kv_f(float v) { return v; }
 __device__ __forceinline__ float kv_f(__half v) { return __half2float(v); }
 
-// rotate-half RoPE of 16 dims per lane: lanes l8 < 4 hold pair firsts
-// (dims i), lanes l8 >= 4 the seconds (dims i + 64); rounding as rope_rotate
-__device__ __forceinline__ void rope16(float (&v)[16], int l8, const StepPersist &P) {
+// RoPE of the 16 dims a lane holds (dims 16*l8 ..), rounding as rope_rotate.
+// Rotate-half: lanes l8 < 4 hold pair firsts (dims i), lanes l8 >= 4 the
+// seconds (dims i + 64).  Adjacent pairs (2i, 2i+1) lie within the lane.
+__device__ __forceinline__ void rope16(float (&v)[16], int l8, const StepPersist &P, int mode) {
+    if (mode == HOLO_ROPE_ADJACENT) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+            const float2 cs = P.rope[8 * l8 + j / 2];
+            const float a = v[j], b = v[j + 1];
+            v[j] = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+            v[j + 1] = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+        }
+        return;
+    }
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
         const float other = __shfl_xor_sync(0xffffffffu, v[j], 4);
@@ -504,7 +515,7 @@ __device__ __forceinline__ bool step_attn(const StepArgs &a, const StepPersist &
         // (waits are CTA-uniform: every warp leaves together on a time-out)
         float qf[16];
         if (!__syncthreads_and(ll_get16(a.qkv + (size_t)h * HD + 16 * l8, eq, a.status, qf))) return false;
-        rope16(qf, l8, P);
+        rope16(qf, l8, P, a.rope_mode);
         // the current position: its warp takes k and v from the QKV output,
         // rotated and rounded as the cache stores them, into shared memory
         const int pslot = (pos - p0) % ATT_SLOTS;
@@ -518,7 +529,7 @@ __device__ __forceinline__ bool step_attn(const StepArgs &a, const StepPersist &
                       ll_get16(a.qkv + q_dim + kv_dim + (size_t)kvh * HD + 16 * l8, eq, a.status, vp);
             if (!__syncthreads_and(got)) return false;
             if (pos_warp) {
-                rope16(kp, l8, P);
+                rope16(kp, l8, P, a.rope_mode);
                 if (g == pslot % 4) {
                     const bool writer = h % group == 0;   // one writer per KV head
                     KV *kd = kc + (size_t)pos * kv_dim + (size_t)kvh * HD + 16 * l8;

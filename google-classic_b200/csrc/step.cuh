@@ -40,6 +40,7 @@ struct StepArgs {
     int dim_loc, d0, ffn_loc, f0, vocab_loc, v0;
     float eps, rope_base;
     int out_type, emb_f16;
+    int rope_mode;                        // HOLO_ROPE_HALF / HOLO_ROPE_ADJACENT
     const StepLayer *layers;              // device array [n_layers] (this rank's shards)
     const void *emb;
     const float *final_norm;

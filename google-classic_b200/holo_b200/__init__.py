@@ -27,6 +27,7 @@ BLOCK_BYTES = {Q8_0: 34, Q4_0: 18, Q4_K: 144, Q6_K: 210, F16: 2, F32: 4}
 
 ACT_F32, ACT_Q8 = 0, 1
 Q4K_REF, Q4K_GGML = 0, 1
+ROPE_HALF, ROPE_ADJACENT = 0, 1          # holo_model_desc.rope_mode
 
 HOLO_OK = 0
 HOLO_E_ARG, HOLO_E_NOMEM, HOLO_E_UNSUPPORTED, HOLO_E_TIMEOUT, HOLO_E_COMM = 1001, 1002, 1003, 1004, 1005

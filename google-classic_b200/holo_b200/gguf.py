@@ -178,12 +178,16 @@ def model_weights(g: GGUFFile, cfg: dict) -> dict:
             "output": output.reshape(-1) if output.dtype == np.uint8 else output}
 
 
-def load_model(path, max_seq: int | None = None, **model_kw):
+def load_model(path, max_seq: int | None = None, rope_mode: int = 0, **model_kw):
     """A decode Model with the weights of a GGUF file (uploaded and repacked
-    once); model_kw go to Model (act_mode, kv_f16, world, rank, batch)."""
+    once); model_kw go to Model (act_mode, kv_f16, world, rank, batch).
+    rope_mode 0 rotates pairs (i, i + hd/2) as the reference does; files
+    converted by llama.cpp's tools expect 1, pairs (2i, 2i+1)
+    (holo_model_desc.rope_mode)."""
     from .model import Model
     with GGUFFile(path) as g:
         cfg = model_config(g, max_seq)
+        cfg["rope_mode"] = rope_mode
         m = Model(cfg, **model_kw)
         m.set_weights(model_weights(g, cfg))
     return m

@@ -18,7 +18,7 @@ class ModelDesc(C.Structure):
                 ("head_dim", C.c_int), ("ffn_dim", C.c_int), ("vocab", C.c_int), ("max_seq", C.c_int),
                 ("rope_base", C.c_float), ("eps", C.c_float), ("layer_type", C.c_int), ("emb_type", C.c_int),
                 ("out_type", C.c_int), ("kv_f16", C.c_int), ("act_mode", C.c_int), ("world", C.c_int),
-                ("rank", C.c_int), ("batch", C.c_int)]
+                ("rank", C.c_int), ("batch", C.c_int), ("rope_mode", C.c_int)]
 
 
 class SamplerDesc(C.Structure):
@@ -46,7 +46,7 @@ class Model:
         d = ModelDesc(cfg["n_layers"], cfg["dim"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"],
                       cfg["ffn_dim"], cfg["vocab"], cfg["max_seq"], cfg.get("rope_base", 10000.0),
                       cfg.get("eps", 1e-5), cfg["layer_type"], cfg.get("emb_type", 1), cfg["out_type"],
-                      int(kv_f16), act_mode, world, rank, batch)
+                      int(kv_f16), act_mode, world, rank, batch, cfg.get("rope_mode", 0))
         self.desc = d
         self.h = self.lib.holo_model_create(C.byref(d))
         self._check("holo_model_create", ok=bool(self.h))
@@ -177,7 +177,7 @@ def shard_ranges(cfg: dict, world: int, rank: int) -> dict:
     d = ModelDesc(cfg["n_layers"], cfg["dim"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"],
                   cfg["ffn_dim"], cfg["vocab"], cfg["max_seq"], cfg.get("rope_base", 10000.0),
                   cfg.get("eps", 1e-5), cfg["layer_type"], cfg.get("emb_type", 1), cfg["out_type"], 1, ACT_Q8,
-                  world, rank, 1)
+                  world, rank, 1, cfg.get("rope_mode", 0))
     r = (C.c_int * 10)()
     if lib.holo_model_shard(C.byref(d), r) != HOLO_OK:
         lib.cuda_clear_status()

@@ -143,7 +143,12 @@ typedef struct {
     int world;           /* row sharding over this many GPUs (one process each); 0 or 1: none */
     int rank;            /* this process's shard, 0 <= rank < world */
     int batch;           /* sequences decoded together (2..64, one GPU) by the *_batch calls; 0 or 1: none */
+    int rope_mode;       /* HOLO_ROPE_HALF (0): pairs (i, i + hd/2), the reference's rotation
+                          * (src/ai/llm.c:1135-1163); HOLO_ROPE_ADJACENT (1): pairs (2i, 2i+1),
+                          * the rotation llama.cpp applies to Llama weights converted to GGUF */
 } holo_model_desc;
+#define HOLO_ROPE_HALF 0
+#define HOLO_ROPE_ADJACENT 1
 
 typedef struct {         /* llm_sampler_t (src/ai/llm.h:167-174) without the seed */
     float temperature;   /* 0: greedy */
