@@ -990,8 +990,7 @@ bool prompt_supported(const HoloModel *m) {
         return false;
     for (const HoloLayer &L : m->layers)
         for (const WeightInfo *wi : {&L.i_qkv, &L.i_o, &L.i_13, &L.i_2})
-            if (wi->rows % PF_ROWS_ALIGN ||
-                (wi->type != GT_Q4_K && wi->type != GT_Q4_0 && wi->type != GT_Q8_0))
+            if (wi->type != GT_Q4_K && wi->type != GT_Q4_0 && wi->type != GT_Q8_0)
                 return false;
     return true;
 }
@@ -1597,7 +1596,7 @@ int holo_model_prefill(void *model, const int *tokens, int n, float *logits) {
     }
     if (!prompt_supported(m)) {
         holo_set_status(HOLO_E_UNSUPPORTED, "holo_model_prefill: row passes need HOLO_ACT_Q8 at batch 1, "
-                                            "Q8_0/Q4_0/Q4_K layers of 128-row multiples, head_dim 64/128/256, "
+                                            "Q8_0/Q4_0/Q4_K layers, head_dim 64/128/256, "
                                             "n_heads / n_kv_heads <= 16");
         return HOLO_E_UNSUPPORTED;
     }

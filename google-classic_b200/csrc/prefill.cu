@@ -304,7 +304,7 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
 #pragma unroll
                 for (int jj = 0; jj < 16; ++jj) {
                     const int m = mt * TN + cb + jj;
-                    if (m < M) o[(size_t)m * N + row] = __uint_as_float(v[jj]);
+                    if (m < M && row < N) o[(size_t)m * N + row] = __uint_as_float(v[jj]);
                 }
             }
         }
@@ -332,13 +332,15 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
         if (lane == 0) {
             const int nun = nch / CPU, u0 = kc0 / CPU;
             const uint8_t *wrb = W + (size_t)(n0 >> 5) * units * UB;   // the CTA's first row-block
+            // a last, partial tile holds fewer row-blocks: the missing ones are
+            // not loaded, their rows of the product are not stored
+            const int nq = min(4, (N + 31) / 32 - (n0 >> 5));
             int issued = 0;
             for (int b = 0; b < nun; ++b) {
                 const int rs = b % R;
                 if (b >= R && !mbar_wait_bounded(&B.rempty[rs], ((b / R) + 1) & 1, status, HOLO_E_TIMEOUT)) break;
-                mbar_arrive_expect_tx(&B.rfull[rs], (uint32_t)(4 * UB));
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
+                mbar_arrive_expect_tx(&B.rfull[rs], (uint32_t)(nq * UB));
+                for (int q = 0; q < nq; ++q)
                     bulk_copy_g2s(sr + rs * PF_RAW_BYTES + q * UB, wrb + ((size_t)q * units + u0 + b) * UB,
                                   (uint32_t)UB, &B.rfull[rs]);
                 issued = b + 1;
@@ -410,7 +412,7 @@ bool launch_mma(float *out, const uint8_t *W, const uint8_t *xt, int M, int N, i
             return holo_check_launch("prefill: attributes");
         configured = dev;
     }
-    pf_mma_kernel<TYPE, TN><<<dim3(N / PF_BM, mtiles, splits), PF_THREADS, smem, st>>>(out, W, xt, M, N, K, units,
+    pf_mma_kernel<TYPE, TN><<<dim3((N + PF_BM - 1) / PF_BM, mtiles, splits), PF_THREADS, smem, st>>>(out, W, xt, M, N, K, units,
                                                                                 kc_per_split, status);
     return holo_check_launch("prefill matmul");
 }
@@ -434,7 +436,7 @@ PfPlan pf_plan(const WeightInfo &wi, int M, int sms) {
     const int nkc = K / PF_BK, cpu = vals / PF_BK;
     // K splits (whole units) so that the CTAs cover the SMs when the weight
     // has few row tiles
-    const int base = (N / PF_BM) * p.mtiles;
+    const int base = (N + PF_BM - 1) / PF_BM * p.mtiles;
     p.splits = std::max(1, std::min(nkc / 4, sms / base));
     p.kc_per_split = ((nkc + p.splits - 1) / p.splits + cpu - 1) / cpu * cpu;
     p.splits = (nkc + p.kc_per_split - 1) / p.kc_per_split;   // every split non-empty
@@ -465,10 +467,10 @@ bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const fl
     if (!D) return false;
     const int N = wi.rows, K = wi.cols;
     const int vals = wi.type == GT_Q8_0 ? 128 : 256;
-    if (!Y || !W || !X || M <= 0 || N % PF_BM || K % vals ||
+    if (!Y || !W || !X || M <= 0 || K % vals ||
         (wi.type != GT_Q4_K && wi.type != GT_Q4_0 && wi.type != GT_Q8_0)) {
         holo_set_status(HOLO_E_ARG, "batched matmul: needs a tiled Q8_0/Q4_0/Q4_K weight (cuda_upload_quant), "
-                                    "N % 128 == 0, K a whole number of blocks");
+                                    "K a whole number of 128/256-value units");
         return false;
     }
     const PfPlan pl = pf_plan(wi, M, D->sms);

@@ -175,8 +175,8 @@ int holo_model_forward(void *model, int token, float *logits);
  * rows are one tensor-core matmul (M = n, cuda_matmul_quant_batched's
  * arithmetic), the attention causal over the cache.  A batched model takes
  * tokens[batch][n] and passes all batch * n rows together.  One GPU,
- * HOLO_ACT_Q8 at batch 1, Q8_0/Q4_0/Q4_K layer matrices of 128-row
- * multiples, head_dim 64/128/256, n_heads / n_kv_heads <= 16; else
+ * HOLO_ACT_Q8 at batch 1, Q8_0/Q4_0/Q4_K layer matrices, head_dim
+ * 64/128/256, n_heads / n_kv_heads <= 16; else
  * HOLO_E_UNSUPPORTED.  logits (host, [batch][vocab] floats) of each
  * sequence's last position when not NULL. */
 int holo_model_prefill(void *model, const int *tokens, int n, float *logits);
@@ -246,8 +246,10 @@ void holo_model_free(void *model);
 /* Batched quantized matmul for prompt processing (no counterpart in the
  * reference, whose prefill runs llm_forward one token at a time,
  * src/ai/llm.c:1049): Y[M][N] = X[M][K] . W^T on the tensor cores, W an N x K
- * Q8_0, Q4_0 or Q4_K weight from cuda_upload_quant (N % 128 == 0, K a whole
- * number of tiled units: 128 values for Q8_0, 256 for Q4_0/Q4_K), X fp32.
+ * Q8_0, Q4_0 or Q4_K weight from cuda_upload_quant (any N; K a whole number
+ * of tiled units: 128 values for Q8_0, 256 for Q4_0/Q4_K), X fp32.  Up to 16
+ * rows of X run on the CUDA cores (each weight unit read once for all rows,
+ * the Q8 matvec's integer block dots per row).
  * X is quantized to Q8 per 32-block as the matvecs do; the dequantized
  * activations and weights are rounded to fp16 and multiplied with fp32
  * accumulation.  Device pointers; HOLO_OK or an error status. */

@@ -83,7 +83,7 @@ def test_prompt_longer_than_one_pass(dev, reference):
 
 
 def test_batched_prompts_match_reference(dev, reference):
-    cfg = dict(CFG, vocab=1024)          # the batched engine's output matmul: 128-row multiples
+    cfg = dict(CFG)
     B = 4
     w = synth.llama_weights(cfg, seed=41)
     m = Model(cfg, act_mode=hb.ACT_Q8, kv_f16=False, batch=B)
