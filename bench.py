@@ -786,6 +786,8 @@ def main():
     ap.add_argument("--decode-batch", type=int, default=1,
                     help="sequences decoded together (batched engine; under torchrun: one batch per rank)")
     ap.add_argument("--layers", type=int, default=0, help="--profile-decode: first N layers only")
+    ap.add_argument("--profile-prompt", type=int, default=0,
+                    help="7B prompt passes of N positions (holo_model_prefill), --iters times, for ncu")
     ap.add_argument("--no-prefill", action="store_true", help="skip the tcgen05 prefill sub-benchmark")
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill sub-benchmark")
     ap.add_argument("--profile-prefill", default=None,
@@ -798,6 +800,18 @@ def main():
         return
     if args.profile_case:
         run_profile_case(args)
+        return
+    if args.profile_prompt:
+        from holo_b200 import model as hm
+        from holo_b200.model import synthetic_model
+        hb.Device(0, 1)
+        m = synthetic_model(dict(hm.LLAMA2_7B), seed=0, kv_f16=True)
+        toks = np.random.default_rng(0).integers(0, 32000, size=args.profile_prompt).astype(np.int32)
+        for _ in range(args.iters):
+            m.reset()
+            m.prefill(toks, want_logits=False)
+        m.close()
+        print(json.dumps({"profile_prompt": args.profile_prompt, "iters": args.iters}))
         return
     if args.profile_prefill:
         import torch

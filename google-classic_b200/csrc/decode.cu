@@ -307,9 +307,11 @@ pf_attn_kernel(float *__restrict__ att, const float *__restrict__ qkv, const KV 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int p0 = *pos_p;
     const int nt = min(qt, M - t0), rows = nt * group;
-    for (int e = tid; e < rows * HD; e += blockDim.x) {
-        const int r = e / HD, dd = e - r * HD;
-        qs[e] = qkv[(size_t)(t0 + r / group) * qkv_bs + (size_t)(kvh * group + r % group) * HD + dd];
+    static_assert((PA_KT * (HD / 8)) % (PA_WARPS * 32) == 0, "staging loads tile the K/V tile");
+    for (int e = tid; e < rows * HD / 4; e += blockDim.x) {   // float4 loads (HD % 4 == 0)
+        const int r = e / (HD / 4), dd = (e - r * (HD / 4)) * 4;
+        *reinterpret_cast<float4 *>(qs + r * HD + dd) = *reinterpret_cast<const float4 *>(
+            qkv + (size_t)(t0 + r / group) * qkv_bs + (size_t)(kvh * group + r % group) * HD + dd);
     }
     const int nkeys = p0 + t0 + nt;    // the CTA's last token attends to all of them
     float mx[2], sum[2], acc[2][DPL];
@@ -325,16 +327,27 @@ pf_attn_kernel(float *__restrict__ att, const float *__restrict__ qkv, const KV 
     }
     for (int j0 = 0; j0 < nkeys; j0 += PA_KT) {
         __syncthreads();   // the previous tile is consumed (and, first, the queries are stored)
-        for (int e = tid; e < PA_KT * HD; e += blockDim.x) {
-            const int j = e / HD, dd = e - j * HD;
-            float kf = 0.0f, vf = 0.0f;
+        // 8 dims a thread per vector load, PA_STAGE_IT loads of K and V each
+        // in flight before any store
+        constexpr int PA_STAGE_IT = PA_KT * (HD / 8) / (PA_WARPS * 32);
+#pragma unroll
+        for (int it = 0; it < PA_STAGE_IT; ++it) {
+            const int e = tid + it * PA_WARPS * 32;
+            const int j = e / (HD / 8), d0 = (e - j * (HD / 8)) * 8;
+            float kf[8], vf[8];
             if (j0 + j < nkeys) {
-                const size_t o = (size_t)(j0 + j) * kv_dim + (size_t)kvh * HD + dd;
-                kf = kv_f<KV>(kc[o]);
-                vf = kv_f<KV>(vc[o]);
+                const size_t o = (size_t)(j0 + j) * kv_dim + (size_t)kvh * HD + d0;
+                KvVec<KV, 8>::load(kc + o, kf);
+                KvVec<KV, 8>::load(vc + o, vf);
+            } else {
+#pragma unroll
+                for (int t = 0; t < 8; ++t) kf[t] = vf[t] = 0.0f;
             }
-            kt[dd * KS + j] = kf;
-            vs[j * HD + dd] = vf;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                kt[(d0 + t) * KS + j] = kf[t];
+                vs[j * HD + d0 + t] = vf[t];
+            }
         }
         __syncthreads();
 #pragma unroll
