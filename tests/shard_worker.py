@@ -8,7 +8,7 @@ host: every rank computes its row shard through the library (holo_model_shard)
       and exchanges comm handles of a stand-in model through connect_peers;
       the ranks check that the shards tile every matrix and that every rank
       received every handle in rank order.
-gpu:  every rank builds its shard of the test model, connects the peers and
+gpu:  every rank builds its shard of the test model (cfg_for(N)), connects the peers and
       runs the decode calls (generate's prompt and one holo_model_prefill in
       sharded row passes); rank 0 writes the logits and token streams to
       OUT_DIR/gpu.npz for the parent test to compare with the reference.
@@ -36,7 +36,14 @@ from holo_b200.model import (LLAMA2_7B, LLAMA3_70B, Model, SamplerDesc, connect_
 # the decode test model (GQA, SwiGLU, Q4_K layers, fp16 embeddings, Q8_0 output)
 CFG = dict(n_layers=2, dim=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn_dim=768, vocab=1000, max_seq=160,
            rope_base=10000.0, eps=1e-5, layer_type=hb.Q4_K, emb_type=1, out_type=hb.Q8_0)
+# four KV heads, for four ranks (one KV head and its GQA pair of query heads each)
+CFG4 = dict(CFG, dim=1024, n_heads=8, n_kv_heads=4, ffn_dim=1536)
 PROMPT_SEED, N_PROMPT, N_GREEDY, N_SAMPLED, N_ROWS = 21, 24, 48, 32, 20
+
+
+def cfg_for(world):
+    """the gpu-mode model for a world size: CFG on two ranks, CFG4 on four"""
+    return CFG if world <= 2 else CFG4
 
 
 class StandInModel:
@@ -95,12 +102,13 @@ def run_gpu(rank, world, out):
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     hb.Device(local, world)
-    w = synth.llama_weights(CFG, seed=11)
-    prompt = np.random.default_rng(PROMPT_SEED).integers(0, CFG["vocab"], size=N_PROMPT).astype(np.int32)
+    cfg = cfg_for(world)
+    w = synth.llama_weights(cfg, seed=11)
+    prompt = np.random.default_rng(PROMPT_SEED).integers(0, cfg["vocab"], size=N_PROMPT).astype(np.int32)
     res = {}
     try:
         for tag, act, kv16 in (("f32", hb.ACT_F32, False), ("q8", hb.ACT_Q8, True)):
-            m = Model(CFG, act_mode=act, kv_f16=kv16, world=world, rank=rank)
+            m = Model(cfg, act_mode=act, kv_f16=kv16, world=world, rank=rank)
             m.set_weights(w)
             connect_peers(m)
             res[f"{tag}_logits"] = np.stack([m.forward(t) for t in prompt])

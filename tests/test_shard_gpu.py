@@ -12,9 +12,12 @@ summed across warps can differ, so the bars are those of test_decode_gpu:
   positions after a sharded prompt pass (row shards of every projection on
   the tensor cores, column slices exchanged through peer memory) against
   the one-GPU prompt pass.
-* Both ranks return the same logits and tokens.
-Needs two GPUs; skipped otherwise.
+* All ranks return the same logits and tokens.
+The bars hold on two ranks (the two-KV-head test model) and, where the box
+has four GPUs, on four (a four-KV-head model, one KV head a rank); each world
+size is skipped on a box with fewer GPUs.
 """
+import functools
 import os
 import socket
 import subprocess
@@ -30,7 +33,7 @@ from conftest import ROOT, rel_err
 from holo_oracle import RefModel
 
 sys.path.insert(0, str(ROOT / "tests"))
-from shard_worker import CFG, N_GREEDY, N_PROMPT, N_ROWS, N_SAMPLED, PROMPT_SEED  # noqa: E402
+from shard_worker import CFG, N_GREEDY, N_PROMPT, N_ROWS, N_SAMPLED, PROMPT_SEED, cfg_for  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -40,27 +43,35 @@ def gpu_count():
     return torch.cuda.device_count()
 
 
-@pytest.fixture(scope="module")
-def sharded(tmp_path_factory):
-    if gpu_count() < 2:
-        pytest.skip("needs two GPUs")
-    out = tmp_path_factory.mktemp("shard")
+@pytest.fixture(scope="module", params=[2, 4], ids=["2gpu", "4gpu"])
+def sharded(request, tmp_path_factory):
+    world = request.param
+    if gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = tmp_path_factory.mktemp(f"shard{world}")
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     # NVLS off: the sharded step uses plain peer stores, NCCL only for set-up
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", OMP_NUM_THREADS="1")
     cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={port}",
            str(ROOT / "tests" / "shard_worker.py"), "gpu", str(out)]
     p = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert p.returncode == 0, p.stdout[-4000:] + p.stderr[-4000:]
-    return dict(np.load(out / "gpu.npz"))
+    res = dict(np.load(out / "gpu.npz"))
+    res["world"], res["cfg"] = world, cfg_for(world)
+    return res
 
 
-@pytest.fixture(scope="module")
-def weights():
-    return synth.llama_weights(CFG, seed=11)
+@functools.lru_cache(maxsize=2)
+def weights_of(world):
+    return synth.llama_weights(cfg_for(world), seed=11)
+
+
+@pytest.fixture
+def weights(sharded):
+    return weights_of(sharded["world"])
 
 
 def prompt():
@@ -69,11 +80,12 @@ def prompt():
 
 def test_ranks_agree(sharded):
     bad = [k for k in sharded if k.endswith("_ranks_equal") and not bool(sharded[k])]
+    assert any(k.endswith("_ranks_equal") for k in sharded)
     assert not bad, bad
 
 
 def test_sharded_f32_logits_match_reference(sharded, reference, weights):
-    ref = RefModel(reference, CFG, weights)
+    ref = RefModel(reference, sharded["cfg"], weights)
     worst_abs = worst_rel = 0.0
     for y, t in zip(sharded["f32_logits"], prompt()):
         r = ref.forward(t)
@@ -85,7 +97,7 @@ def test_sharded_f32_logits_match_reference(sharded, reference, weights):
 
 
 def test_sharded_streams_match_reference(sharded, reference, weights):
-    ref = RefModel(reference, CFG, weights)
+    ref = RefModel(reference, sharded["cfg"], weights)
     p = prompt()[:16]
     want_g = ref.generate(p, N_GREEDY, 0.0, 0.95, 40, 1.1, 64, seed=5)
     want_s = ref.generate(p, N_SAMPLED, 0.8, 0.95, 40, 1.1, 64, seed=7)
@@ -95,7 +107,7 @@ def test_sharded_streams_match_reference(sharded, reference, weights):
 
 
 def test_sharded_q8_matches_one_gpu(sharded, dev, weights):
-    m = Model(CFG, act_mode=hb.ACT_Q8, kv_f16=True)
+    m = Model(sharded["cfg"], act_mode=hb.ACT_Q8, kv_f16=True)
     m.set_weights(weights)
     worst = max(rel_err(y, m.forward(t)) for y, t in zip(sharded["q8_logits"], prompt()))
     got = m.generate(prompt()[:16], N_GREEDY, SamplerDesc(0.0, 0.95, 40, 1.1, 64), seed=5)
@@ -106,7 +118,7 @@ def test_sharded_q8_matches_one_gpu(sharded, dev, weights):
 
 
 def test_sharded_prompt_pass_matches_one_gpu(sharded, dev, weights):
-    m = Model(CFG, act_mode=hb.ACT_Q8, kv_f16=True)
+    m = Model(sharded["cfg"], act_mode=hb.ACT_Q8, kv_f16=True)
     m.set_weights(weights)
     p = prompt()
     m.prefill(p[:N_ROWS], want_logits=False)

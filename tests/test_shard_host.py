@@ -15,10 +15,10 @@ from holo_b200.model import LLAMA2_7B, LLAMA3_70B, Model, shard_ranges
 from conftest import ROOT
 
 sys.path.insert(0, str(ROOT / "tests"))
-from shard_worker import CFG, tiles  # noqa: E402
+from shard_worker import CFG, CFG4, tiles  # noqa: E402
 
 
-@pytest.mark.parametrize("cfg", [CFG, LLAMA2_7B, LLAMA3_70B], ids=["test", "7b", "70b"])
+@pytest.mark.parametrize("cfg", [CFG, CFG4, LLAMA2_7B, LLAMA3_70B], ids=["test", "test4", "7b", "70b"])
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_shards_tile_every_matrix(cfg, world):
     if cfg["n_kv_heads"] % world:
