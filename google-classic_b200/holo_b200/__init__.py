@@ -106,6 +106,9 @@ SIGNATURES = {
     "holo_model_forward_batch": (_i, [_vp, _vp, _vp]),
     "holo_model_generate_batch": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp]),
     "holo_model_comm_handle": (_i, [_vp, _vp]), "holo_model_shard": (_i, [_vp, _vp]), "holo_model_open_peers": (_i, [_vp, _vp]),
+    "holo_tokenizer_create": (_vp, [C.POINTER(C.c_char_p), _i, _i, _i]),
+    "holo_tokenize": (_i, [_vp, C.c_char_p, C.POINTER(C.c_int), _i, _i]),
+    "holo_tokenizer_free": (None, [_vp]),
 }
 
 _LIB = None
@@ -138,6 +141,41 @@ def header_symbols() -> list[str]:
         for m in re.finditer(r"^[A-Za-z_][\w \*]*?\b(\w+)\s*\([^;{]*\)\s*;", text, flags=re.M):
             names.append(m.group(1))
     return names
+
+
+class Tokenizer:
+    """The reference's greedy longest-match tokenizer (llm_tokenize,
+    src/ai/llm.c:178-221) through holo_tokenize: host code, no device needed.
+
+    vocab: token strings (bytes or str, UTF-8; None for a missing entry) in
+    vocabulary order; bos and unk as the reference's tokenizer.ggml ids."""
+
+    def __init__(self, vocab, bos: int = 1, unk: int = 0):
+        self.lib = load()
+        enc = [v.encode() if isinstance(v, str) else v for v in vocab]
+        arr = (C.c_char_p * len(enc))(*enc)
+        self.h = self.lib.holo_tokenizer_create(arr, len(enc), int(bos), int(unk))
+        if not self.h:
+            raise RuntimeError("holo_tokenizer_create failed")
+        self.vocab_size = len(enc)
+
+    def encode(self, text, add_bos: bool = False, max_tokens: int | None = None) -> np.ndarray:
+        """Token ids of text (str or bytes; the reference stops at the first
+        NUL byte), at most max_tokens (default: one per byte, plus BOS)."""
+        b = text.encode() if isinstance(text, str) else bytes(text)
+        cap = len(b) + 1 if max_tokens is None else int(max_tokens)
+        out = np.zeros(max(cap, 1), np.int32)
+        n = self.lib.holo_tokenize(self.h, b, out.ctypes.data_as(C.POINTER(C.c_int)), cap, int(add_bos))
+        if n < 0:
+            raise RuntimeError("holo_tokenize: bad arguments")
+        return out[:n].copy()
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.holo_tokenizer_free(self.h)
+            self.h = None
+
+    __del__ = close
 
 
 class Device:

@@ -61,9 +61,11 @@ class GGUFFile:
         n_tensors, n_kv = self._unpack("<QQ")
         self.version = version
         self.meta = {}
+        self._value_at = {}   # key -> (type, file offset of the value)
         for _ in range(n_kv):
             key = self._string()
             (vtype,) = self._unpack("<I")
+            self._value_at[key] = (vtype, self._pos)
             self.meta[key] = self._value(vtype)
         self.tensors = {}
         for _ in range(n_tensors):
@@ -86,13 +88,28 @@ class GGUFFile:
         self._pos += size
         return v
 
-    def _string(self):
+    def _string(self, raw=False):
         (n,) = self._unpack("<Q")
         if self._pos + n > len(self._mm):
             raise ValueError("GGUF file truncated")
-        s = bytes(self._mm[self._pos:self._pos + n]).decode("utf-8", errors="replace")
+        b = bytes(self._mm[self._pos:self._pos + n])
         self._pos += n
-        return s
+        return b if raw else b.decode("utf-8", errors="replace")
+
+    def string_array(self, key) -> list[bytes] | None:
+        """A metadata array of strings as raw bytes (.meta holds them
+        decoded), or None when the key is absent or not such an array."""
+        if key not in self._value_at:
+            return None
+        vtype, pos = self._value_at[key]
+        if vtype != T_ARR:
+            return None
+        saved, self._pos = self._pos, pos
+        try:
+            etype, n = self._unpack("<IQ")
+            return [self._string(raw=True) for _ in range(n)] if etype == T_STR else None
+        finally:
+            self._pos = saved
 
     def _value(self, vtype):
         if vtype == T_STR:
@@ -178,6 +195,27 @@ def model_weights(g: GGUFFile, cfg: dict) -> dict:
             "output": output.reshape(-1) if output.dtype == np.uint8 else output}
 
 
+def tokenizer_vocab(g: GGUFFile) -> dict:
+    """The tokenizer fields the reference's load_tokenizer reads
+    (src/ai/llm.c:61-100): the token strings of tokenizer.ggml.tokens as
+    bytes, each cut at its first NUL as strdup does, and the special ids with
+    the reference's defaults (bos 1, eos 2, padding 0, unknown 0)."""
+    toks = g.string_array("tokenizer.ggml.tokens")
+    if not toks:
+        raise ValueError("no vocabulary (tokenizer.ggml.tokens) in the file")
+    ids = {k: int(g.meta.get(f"tokenizer.ggml.{key}", d)) for k, key, d in
+           (("bos", "bos_token_id", 1), ("eos", "eos_token_id", 2), ("pad", "padding_token_id", 0),
+            ("unk", "unknown_token_id", 0))}
+    return dict(tokens=[t.split(b"\0", 1)[0] for t in toks], **ids)
+
+
+def load_tokenizer(g: GGUFFile):
+    """A holo_b200.Tokenizer over the file's vocabulary (llm_tokenize's)."""
+    from . import Tokenizer
+    v = tokenizer_vocab(g)
+    return Tokenizer(v["tokens"], bos=v["bos"], unk=v["unk"])
+
+
 def load_model(path, max_seq: int | None = None, rope_mode: int = 0, **model_kw):
     """A decode Model with the weights of a GGUF file (uploaded and repacked
     once); model_kw go to Model (act_mode, kv_f16, world, rank, batch).
@@ -204,9 +242,17 @@ def _pack_value(v):
             else struct.pack("<II", T_U32, v)
     if isinstance(v, float):
         return struct.pack("<If", T_F32, v)
-    if isinstance(v, str):
-        b = v.encode()
+    if isinstance(v, (str, bytes)):
+        b = v.encode() if isinstance(v, str) else v
         return struct.pack("<IQ", T_STR, len(b)) + b
+    if isinstance(v, (list, tuple)):
+        # arrays: of strings, of float32 or of int32 (the tokenizer.ggml.* kinds)
+        if all(isinstance(e, (str, bytes)) for e in v):
+            return struct.pack("<IIQ", T_ARR, T_STR, len(v)) + b"".join(_pack_value(e)[4:] for e in v)
+        if all(isinstance(e, float) for e in v):
+            return struct.pack("<IIQ", T_ARR, T_F32, len(v)) + np.asarray(v, "<f4").tobytes()
+        if all(isinstance(e, int) and not isinstance(e, bool) for e in v):
+            return struct.pack("<IIQ", T_ARR, T_I32, len(v)) + np.asarray(v, "<i4").tobytes()
     raise TypeError(f"metadata value {v!r}")
 
 

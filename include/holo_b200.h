@@ -262,6 +262,26 @@ int cuda_matmul_quant_batched(float *Y, const void *W, const float *X, int M, in
  * in the reference (it has no f32 -> Q8_0/Q4_0/Q4_K quantizer). */
 int cuda_synth_weights(void *dst, int ggml_type, int rows, int cols, unsigned long long seed, float std);
 
+/* ---- tokenizer (host; replaces llm_tokenize, src/ai/llm.c:178-221) ----------
+ * The reference's greedy longest-match tokenizer with the same output: at
+ * each position the longest vocabulary string that prefixes the remaining
+ * text (the lowest index among equal strings; empty and NULL entries never
+ * match), else the byte's fallback -- the first "<0xNN>" token, else the
+ * first token equal to the byte's GPT-2 byte-level string as
+ * find_byte_token builds it (llm.c:113-175), else unk_token -- one byte at a
+ * time.  The reference rescans the vocabulary at every position; here it is a
+ * byte trie built once by holo_tokenizer_create (which copies nothing it
+ * keeps pointers to: the strings may be freed afterwards).
+ * holo_tokenize mirrors llm_tokenize(ctx, text, tokens, max_tokens, add_bos):
+ * bos_token first when add_bos and max_tokens > 0, at most max_tokens ids,
+ * returns the count; -1 for a NULL tokenizer or text, or NULL tokens with
+ * max_tokens > 0.  No CUDA involved; a tokenizer may be used from several
+ * threads at once. */
+typedef struct holo_tokenizer holo_tokenizer;
+holo_tokenizer *holo_tokenizer_create(const char *const *vocab, int vocab_size, int bos_token, int unk_token);
+int holo_tokenize(const holo_tokenizer *t, const char *text, int *tokens, int max_tokens, int add_bos);
+void holo_tokenizer_free(holo_tokenizer *t);
+
 /* ---- CUDA graphs of the library stream --------------------------------------
  * The reference launches every op separately on the legacy stream
  * (src/ai/llm_cuda.c:558-946, ~13 launches per layer).  Calls made between

@@ -10,6 +10,7 @@
 #include "holo_oracle.h"
 
 #include <math.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 #ifdef _OPENMP
@@ -394,4 +395,57 @@ void ho_matvec_q8act(int type, const void *W, const int8_t *q, const float *d,
         }
         y[r] = acc;
     }
+}
+
+/* ---- tokenizer ----------------------------------------------------------------- */
+
+/* The byte-level string the reference assigns to byte b (llm.c:116-147):
+ * printable ASCII 33..126 is itself; bytes 161 and 166..172 have none; every
+ * other byte, counted in increasing order, is code point 256 + its rank,
+ * written as two UTF-8 bytes.  Returns the string length (0: none). */
+static int ho_byte_string(int b, char out[3]) {
+    if (b >= 33 && b <= 126) { out[0] = (char)b; out[1] = 0; return 1; }
+    if (b == 161 || (b >= 166 && b <= 172)) { out[0] = 0; return 0; }
+    int rank = 0;
+    for (int i = 0; i < b; i++)
+        if (!(i >= 33 && i <= 126) && !(i == 161 || (i >= 166 && i <= 172))) rank++;
+    int cp = 256 + rank;
+    out[0] = (char)(0xC0 | (cp >> 6));
+    out[1] = (char)(0x80 | (cp & 0x3F));
+    out[2] = 0;
+    return 2;
+}
+
+/* first vocabulary index whose string equals s, or -1 */
+static int ho_find_exact(const char *const *vocab, int vocab_size, const char *s) {
+    for (int i = 0; i < vocab_size; i++)
+        if (vocab[i] && strcmp(vocab[i], s) == 0) return i;
+    return -1;
+}
+
+int ho_tokenize(const char *const *vocab, int vocab_size, int bos, int unk, const char *text,
+                int *tokens, int max_tokens, int add_bos) {
+    int n = 0;
+    if (add_bos && n < max_tokens) tokens[n++] = bos;
+    const char *p = text;
+    while (*p && n < max_tokens) {
+        /* longest vocabulary string that prefixes p; the first of that length */
+        size_t best_len = 0;
+        int best = unk;
+        for (int i = 0; i < vocab_size; i++) {
+            if (!vocab[i]) continue;
+            size_t len = strlen(vocab[i]);
+            if (len > best_len && strncmp(p, vocab[i], len) == 0) { best_len = len; best = i; }
+        }
+        if (best_len > 0) { tokens[n++] = best; p += best_len; continue; }
+        /* one byte: <0xNN>, else the byte-level string, else unk */
+        unsigned char b = (unsigned char)*p;
+        char hex[8], bs[3];
+        snprintf(hex, sizeof hex, "<0x%02X>", b);
+        int id = ho_find_exact(vocab, vocab_size, hex);
+        if (id < 0 && ho_byte_string(b, bs) > 0) id = ho_find_exact(vocab, vocab_size, bs);
+        tokens[n++] = id >= 0 ? id : unk;
+        p++;
+    }
+    return n;
 }

@@ -84,6 +84,12 @@ void ho_matvec_q8act(int type, const void *W, const int8_t *q, const float *d,
  * (quant.c) semantics with identical dequantized values. */
 void ho_q4k_to_ref_layout(const void *src_block, void *dst_block, int src_layout);
 
+/* The reference's tokenizer (llm_tokenize, src/ai/llm.c:178-221, with its
+ * byte fallback find_byte_token, llm.c:113-175), restated literally: every
+ * position scans the whole vocabulary.  vocab entries may be NULL. */
+int ho_tokenize(const char *const *vocab, int vocab_size, int bos, int unk, const char *text,
+                int *tokens, int max_tokens, int add_bos);
+
 #ifdef __cplusplus
 }
 #endif

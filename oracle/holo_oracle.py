@@ -48,6 +48,8 @@ class Oracle:
         lib.ho_quantize_act_q8.argtypes = [_vp, _i64, _vp, _vp, _vp]
         lib.ho_matvec_q8act.argtypes = [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i]
         lib.ho_q4k_to_ref_layout.argtypes = [_vp, _vp, _i]
+        lib.ho_tokenize.restype = _i
+        lib.ho_tokenize.argtypes = [C.POINTER(C.c_char_p), _i, _i, _i, C.c_char_p, C.POINTER(_i), _i, _i]
         self.lib = lib
 
     def dequant(self, gtype, blocks, rows, cols, q4k_layout=0):
@@ -90,6 +92,22 @@ class Oracle:
             self.lib.ho_q4k_to_ref_layout(_ptr(blocks) + i * 144, _ptr(out) + i * 144, layout)
         return out.reshape(-1)
 
+    def tokenize(self, vocab, bos, unk, text, max_tokens=None, add_bos=False):
+        """llm_tokenize restated (ho_tokenize): the whole vocabulary scanned at
+        every position -- small vocabularies only."""
+        return _tok_call(self.lib.ho_tokenize, vocab, bos, unk, text, max_tokens, add_bos)
+
+
+def _tok_call(fn, vocab, bos, unk, text, max_tokens, add_bos):
+    """fn(vocab**, size, bos, unk, text, out*, max_tokens, add_bos) -> ids"""
+    enc = [v.encode() if isinstance(v, str) else v for v in vocab]
+    arr = (C.c_char_p * max(len(enc), 1))(*enc)
+    b = text.encode() if isinstance(text, str) else bytes(text)
+    cap = len(b) + 1 if max_tokens is None else int(max_tokens)
+    out = (_i * max(cap, 1))()
+    n = fn(arr, len(enc), int(bos), int(unk), b, out, cap, int(add_bos))
+    return np.array(out[:n], np.int32)
+
 
 class Reference:
     """The reference engine's own CPU functions (src/ai/*.c built from source)."""
@@ -110,6 +128,12 @@ class Reference:
         lib.href_gguf_int.argtypes = [C.c_char_p, C.c_char_p, C.c_longlong]
         lib.href_gguf_float.restype = C.c_double
         lib.href_gguf_float.argtypes = [C.c_char_p, C.c_char_p, C.c_double]
+        lib.href_tokenize.restype = _i
+        lib.href_tokenize.argtypes = [C.POINTER(C.c_char_p), _i, _i, _i, C.c_char_p, C.POINTER(_i), _i, _i]
+        lib.href_gguf_string_at.restype = C.c_longlong
+        lib.href_gguf_string_at.argtypes = [C.c_char_p, C.c_char_p, C.c_longlong, C.c_char_p, C.c_longlong]
+        lib.href_gguf_array_len.restype = C.c_longlong
+        lib.href_gguf_array_len.argtypes = [C.c_char_p, C.c_char_p]
         lib.f16_to_f32.restype = _f
         lib.f16_to_f32.argtypes = [C.c_uint16]
         lib.href_model_create.restype = _vp
@@ -158,6 +182,22 @@ class Reference:
 
     def gguf_float(self, path, key, default=-1.0):
         return self.lib.href_gguf_float(str(path).encode(), key.encode(), default)
+
+    def tokenize(self, vocab, bos, unk, text, max_tokens=None, add_bos=False):
+        """The reference's own llm_tokenize (src/ai/llm.c:178-221)."""
+        return _tok_call(self.lib.href_tokenize, vocab, bos, unk, text, max_tokens, add_bos)
+
+    def gguf_tokens(self, path, key="tokenizer.ggml.tokens", cap=1 << 16):
+        """A GGUF string array as load_tokenizer copies it (llm.c:78-81)."""
+        n = self.lib.href_gguf_array_len(str(path).encode(), key.encode())
+        buf = C.create_string_buffer(cap)
+        out = []
+        for i in range(n):
+            r = self.lib.href_gguf_string_at(str(path).encode(), key.encode(), i, buf, cap)
+            if r < 0:
+                raise RuntimeError(f"href_gguf_string_at({key}, {i}) = {r}")
+            out.append(buf.raw[:r])
+        return out
 
     def dequant(self, gtype, blocks, rows, cols):
         name = {8: "dequantize_row_q8_0", 2: "dequantize_row_q4_0", 12: "dequantize_row_q4_k",

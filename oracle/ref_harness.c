@@ -7,7 +7,8 @@
  * oracle/_ref/libholo_ref.so.  The functions here only fill the reference's
  * public structs (src/ai/llm.h:22-200) in memory, so no GGUF file is needed,
  * and call the reference's own entry points: matmul_q (llm.c:770),
- * llm_forward (llm.c:1015), llm_sample (llm.c:1281), llm_reset (llm.c:732).
+ * llm_forward (llm.c:1015), llm_sample (llm.c:1281), llm_reset (llm.c:732),
+ * llm_tokenize (llm.c:178), and gguf.c's metadata readers.
  */
 #include "gguf.h"
 #include "llm.h"
@@ -182,4 +183,47 @@ double href_gguf_float(const char *path, const char *key, double dflt) {
     double v = (double)gguf_get_float(g, key, (float)dflt);
     gguf_close(g);
     return v;
+}
+
+/* llm_tokenize (llm.c:178-221) with the tokenizer fields load_tokenizer
+ * fills (llm.c:61-100) set in memory; vocab entries may be NULL. */
+int href_tokenize(char **vocab, int vocab_size, int bos, int unk, const char *text, int *tokens,
+                  int max_tokens, int add_bos) {
+    llm_ctx_t *c = (llm_ctx_t *)calloc(1, sizeof(llm_ctx_t));
+    if (!c) return -1;
+    c->tokenizer.vocab = vocab;
+    c->tokenizer.vocab_size = vocab_size;
+    c->tokenizer.bos_token = bos;
+    c->tokenizer.unk_token = unk;
+    int n = llm_tokenize(c, text, tokens, max_tokens, add_bos != 0);
+    free(c);
+    return n;
+}
+
+/* Entry i of a GGUF string array as load_tokenizer copies it (strdup of the
+ * entry's data, llm.c:78-81): its length, -1 if the key or entry is absent,
+ * -2 if cap is too small (dst gets a NUL-terminated copy). */
+long long href_gguf_string_at(const char *path, const char *key, long long i, char *dst, long long cap) {
+    gguf_ctx_t *g = gguf_open(path);
+    if (!g) return -1;
+    uint64_t len = 0;
+    const gguf_string_t *arr = (const gguf_string_t *)gguf_get_array(g, key, &len);
+    long long r = -1;
+    if (arr && i >= 0 && (uint64_t)i < len) {
+        size_t n = strlen(arr[i].data);
+        if ((long long)n + 1 > cap) r = -2;
+        else { memcpy(dst, arr[i].data, n + 1); r = (long long)n; }
+    }
+    gguf_close(g);
+    return r;
+}
+
+/* length of a GGUF metadata array (gguf_get_array), 0 if absent */
+long long href_gguf_array_len(const char *path, const char *key) {
+    gguf_ctx_t *g = gguf_open(path);
+    if (!g) return 0;
+    uint64_t len = 0;
+    gguf_get_array(g, key, &len);
+    gguf_close(g);
+    return (long long)len;
 }

@@ -7,7 +7,9 @@ into oracle/_ref/libholo_ref.so by oracle/Makefile):
 
 Each fixture holds the inputs (GGUF blocks, activation) and the outputs of the
 REFERENCE's own CPU functions on them: matmul_q (src/ai/llm.c:770-926) and
-dequantize_row_* (src/ai/quant.c:118-311).  The Q8-activation outputs come
+dequantize_row_* (src/ai/quant.c:118-311); tokenize_cases.json holds
+vocabularies and texts (tests/golden/tok_cases.py) with the token ids of the
+reference's llm_tokenize (llm.c:178-221).  The Q8-activation outputs come
 from the build's restatement (the reference has no such code) and pin it
 against regressions only.
 """
@@ -19,10 +21,12 @@ import numpy as np
 ROOT = pathlib.Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT / "google-classic_b200"))
 sys.path.insert(0, str(ROOT / "oracle"))
+sys.path.insert(0, str(pathlib.Path(__file__).resolve().parent))
 
 import holo_b200 as hb  # noqa: E402
 from holo_b200 import synth  # noqa: E402
 import holo_oracle  # noqa: E402
+import tok_cases  # noqa: E402
 
 CASES = [
     # name, type, rows, cols, seed
@@ -51,6 +55,8 @@ def main(only=()):
                             y_ref=y_ref, deq_ref=deq_ref, act_q=q, act_d=d, act_s=s,
                             y_q8=y_q8, isums=isums)
         print("wrote", name)
+    if not only or "tokenize_cases" in only:
+        tokenize_cases(ref, out)
     if only and "q4_k_ref_8x512" not in only:
         return
     # ggml-semantics Q4_K: the same values as a quant.c-semantics block set
@@ -58,6 +64,26 @@ def main(only=()):
     deq = ref.dequant(hb.Q4_K, W, 8, 512)
     np.savez_compressed(out / "q4_k_ref_8x512.npz", W=W, deq_ref=deq)
     print("wrote q4_k_ref_8x512")
+
+
+# (seed, vocabulary size, "<0xNN>" tokens, byte-level tokens, bos, unk)
+TOKENIZE_CASES = [(1, 300, True, True, 1, 0), (2, 300, False, True, 1, 0), (3, 300, False, False, 2, 7)]
+
+
+def tokenize_cases(ref, out):
+    import json
+    cases = []
+    for seed, size, bt, bl, bos, unk in TOKENIZE_CASES:
+        vocab = tok_cases.vocabulary(seed, size, bt, bl)
+        for i, text in enumerate(tok_cases.texts(seed, n=6, max_len=160)):
+            add_bos, cap = bool(i % 2), (None if i != 3 else 17)   # one case cut at 17 ids
+            ids = ref.tokenize(vocab, bos, unk, text, max_tokens=cap, add_bos=add_bos)
+            cases.append(dict(seed=seed, text=text.hex(), add_bos=add_bos, max_tokens=cap, ids=ids.tolist()))
+    vocabs = {str(seed): [None if t is None else t.hex() for t in tok_cases.vocabulary(seed, size, bt, bl)]
+              for seed, size, bt, bl, _, _ in TOKENIZE_CASES}
+    ids = {str(seed): [bos, unk] for seed, _, _, _, bos, unk in TOKENIZE_CASES}
+    (out / "tokenize_cases.json").write_text(json.dumps(dict(vocabs=vocabs, bos_unk=ids, cases=cases)))
+    print("wrote tokenize_cases")
 
 
 if __name__ == "__main__":
