@@ -153,3 +153,18 @@ def test_gguf_vocabulary(tmp_path, reference):
     gguf.write(path, {"general.architecture": "llama"}, {"t": (hb.F32, (8,), np.zeros(8, np.float32))})
     with gguf.GGUFFile(path) as g, pytest.raises(ValueError, match="no vocabulary"):
         gguf.tokenizer_vocab(g)
+
+
+def test_concurrent_use():
+    """One tokenizer, eight threads at once (ctypes drops the GIL during the
+    call): the same ids as one thread."""
+    from concurrent.futures import ThreadPoolExecutor
+    vocab = tok_cases.vocabulary(41, 2000)
+    tok = hb.Tokenizer(vocab, bos=1, unk=0)
+    texts = [t * 20 for t in tok_cases.texts(41, n=16, max_len=200)]
+    want = [tok.encode(t, add_bos=True) for t in texts]
+    with ThreadPoolExecutor(8) as ex:
+        for _ in range(4):
+            got = list(ex.map(lambda t: tok.encode(t, add_bos=True), texts))
+            assert all(np.array_equal(g, w) for g, w in zip(got, want))
+    tok.close()
