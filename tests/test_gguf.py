@@ -117,3 +117,24 @@ def test_rejects_bad_files(tmp_path):
     p.write_bytes(data[:-16])   # tensor data cut short
     with gguf.GGUFFile(p) as g, pytest.raises(ValueError, match="past the end"):
         g.tensor("t")
+
+
+def test_metadata_arrays_roundtrip(tmp_path, reference):
+    """Arrays of strings, float32 and int32 (the tokenizer.ggml.* kinds):
+    written, read back here (strings also as raw bytes) and by the
+    reference's parser (gguf_get_array, gguf.c:479-487)."""
+    toks = ["a", "▁b", "中", "", "<0x0A>"]
+    meta = {"general.architecture": "llama", "tokenizer.ggml.tokens": toks,
+            "tokenizer.ggml.scores": [0.5, -1.25, 3.0, 0.0, -0.5], "tokenizer.ggml.token_type": [1, 2, 3, 1, 6]}
+    path = tmp_path / "arr.gguf"
+    gguf.write(path, meta, {"t": (hb.F32, (8,), np.zeros(8, np.float32))})
+    with gguf.GGUFFile(path) as g:
+        assert g.meta["tokenizer.ggml.tokens"] == toks
+        assert g.string_array("tokenizer.ggml.tokens") == [t.encode() for t in toks]
+        assert g.meta["tokenizer.ggml.scores"] == [0.5, -1.25, 3.0, 0.0, -0.5]
+        assert g.meta["tokenizer.ggml.token_type"] == [1, 2, 3, 1, 6]
+        assert g.string_array("tokenizer.ggml.scores") is None and g.string_array("absent") is None
+        assert np.array_equal(g.tensor("t"), np.zeros(8, np.float32))   # data section still found
+    assert reference.gguf_tokens(path) == [t.encode() for t in toks]
+    for key in ("tokenizer.ggml.scores", "tokenizer.ggml.token_type"):
+        assert reference.lib.href_gguf_array_len(str(path).encode(), key.encode()) == 5
