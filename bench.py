@@ -491,6 +491,8 @@ def decode_bench(args, world, rank, torch):
     }
     if want_cpu and host is not None:
         out["cpu_baseline"] = decode_cpu_baseline(cfg, host, prompt, budget_s=args.cpu_budget)
+    elif rank == 0 and world == 1 and not args.no_cpu:   # 70B: llm_forward is infeasible on the host
+        out["cpu_baseline"] = decode_cpu_extrapolated(cfg, budget_s=args.cpu_budget)
     m.close()
     return out
 
@@ -670,6 +672,50 @@ def decode_cpu_baseline(cfg, host, prompt, budget_s):
     return {"value": round(n / dt, 4), "unit": "tokens/s", "cores": threads, "kind": "reference",
             "sample": f"llm_forward for the first {n} prompt positions of the same model, {dt:.1f} s "
                       f"(Q4_K matvecs single-threaded as in the reference; OpenMP up to {threads} threads elsewhere)"}
+
+
+def decode_cpu_extrapolated(cfg, budget_s, sample_rows=4096):
+    """The reference's matmul_q (src/ai/llm.c:770-926) on the host cores over
+    row samples (up to sample_rows rows, tens of MB: larger than the CPU's
+    caches) of a model's seven per-layer matrix shapes and its output matrix,
+    scaled to whole matrices and n_layers layers: tokens per second of the
+    matvecs alone.  llm_forward end to end is infeasible at 70B (about a
+    minute a token); attention and the elementwise work are left out, so the
+    figure flatters the CPU.  matmul_q runs with its own threading (OpenMP for
+    Q8_0/F32, one thread for Q4_0/Q4_K)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import holo_oracle
+    try:
+        ref = holo_oracle.Reference()
+    except Exception as e:  # noqa: BLE001
+        return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
+    dim, ffn = cfg["dim"], cfg["ffn_dim"]
+    q_dim, kv_dim = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
+    lt, ot = cfg["layer_type"], cfg["out_type"]
+    shapes = [(lt, q_dim, dim), (lt, kv_dim, dim), (lt, kv_dim, dim), (lt, dim, q_dim), (lt, ffn, dim),
+              (lt, ffn, dim), (lt, dim, ffn), (ot, cfg["vocab"], dim)]
+    per_shape = budget_s / len(shapes)
+    layer_s = out_s = 0.0
+    for i, (gt, rows, cols) in enumerate(shapes):
+        r = min(rows, sample_rows)
+        W = synth.quant_matrix(gt, r, cols, seed=900 + i)
+        x = synth.activation(cols, seed=900 + i)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            ref.matmul_q(gt, W, x, r, cols)
+            n += 1
+            if time.perf_counter() - t0 >= per_shape:
+                break
+        full = (time.perf_counter() - t0) / n * rows / r
+        if i == len(shapes) - 1:
+            out_s = full
+        else:
+            layer_s += full
+    s_tok = layer_s * cfg["n_layers"] + out_s
+    return {"value": round(1.0 / s_tok, 5), "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "reference",
+            "sample": f"matmul_q on slices of up to {sample_rows} rows of the 7 layer shapes and the output "
+                      f"matrix, scaled to whole matrices x {cfg['n_layers']} layers ({s_tok:.1f} s a token; "
+                      f"matvecs only, attention left out)"}
 
 
 # ---------------------------------------------------------------------------

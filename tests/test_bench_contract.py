@@ -11,6 +11,7 @@ import sys
 
 import pytest
 
+import holo_b200 as hb
 from conftest import ROOT
 
 KEYS = {"impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
@@ -58,3 +59,18 @@ def test_reference_arm_under_torchrun():
     assert len(lines) == 1, p.stdout   # rank 0 alone
     check_line(lines[0])
     assert lines[0]["n_gpus"] == 2
+
+
+def test_decode_cpu_extrapolation():
+    """The 70B decode's CPU figure (matmul_q on row samples of the layer
+    shapes, scaled to the model): finite, and slower for more layers."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    cfg = dict(n_layers=2, dim=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn_dim=768, vocab=1000,
+               layer_type=hb.Q4_0, out_type=hb.Q4_0)
+    a = bench.decode_cpu_extrapolated(cfg, budget_s=0.2)
+    if a["value"] is None:
+        pytest.skip(a["sample"])
+    b = bench.decode_cpu_extrapolated(dict(cfg, n_layers=20), budget_s=0.2)
+    assert a["kind"] == "reference" and a["unit"] == "tokens/s" and a["cores"] >= 1
+    assert 0 < b["value"] < a["value"]
