@@ -175,7 +175,11 @@ class Tokenizer:
             self.lib.holo_tokenizer_free(self.h)
             self.h = None
 
-    __del__ = close
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 -- interpreter shutdown may have unloaded the library
+            pass
 
 
 class Device:
