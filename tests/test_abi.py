@@ -1,9 +1,15 @@
 """The drop-in boundary: libholo_cuda.so loads without a GPU and exports every
 function declared in include/*.h, including every entry point of the
 reference's include/cuda_ops.h.  CPU only (no compute calls)."""
+import ctypes
 import subprocess
 
+import pytest
+
 import holo_b200 as hb
+from conftest import ROOT
+
+DROPIN = ROOT / "oracle" / "_ref" / "libholo_ref_dropin.so"
 
 # the 48 functions of the reference header include/cuda_ops.h (lines 18-133)
 REFERENCE_ABI = """
@@ -52,3 +58,20 @@ def test_kernels_are_built_for_sm100a_only():
                          capture_output=True, text=True)
     archs = {w for w in out.stdout.split() if "sm_" in w}
     assert archs and all("sm_100a" in a for a in archs), archs
+
+
+def test_reference_gpu_host_code_links_against_library():
+    """The drop-in proof at link level: the reference's llm.c + llm_cuda.c,
+    compiled as its CUDA build compiles them (HOLO_USE_CUDA) against this
+    repository's include/cuda_ops.h, link against libholo_cuda.so in place of
+    cuda_ops.cu with no undefined symbol (oracle/Makefile, target dropin).
+    Every cuda_* function they call is a reference ABI function the library
+    exports, and the linked library loads."""
+    if not DROPIN.exists():
+        pytest.skip("no drop-in build (the reference tree is absent)")
+    out = subprocess.run(["nm", "-D", "--undefined-only", str(DROPIN)], capture_output=True, text=True, check=True)
+    called = {line.split()[-1] for line in out.stdout.splitlines() if line.split()[-1].startswith("cuda_")}
+    assert len(called) >= 20, called
+    assert called <= set(REFERENCE_ABI), called - set(REFERENCE_ABI)
+    assert called <= exported(), called - exported()
+    ctypes.CDLL(str(DROPIN))
