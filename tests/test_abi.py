@@ -1,7 +1,12 @@
 """The drop-in boundary: libholo_cuda.so loads without a GPU and exports every
 function declared in include/*.h, including every entry point of the
-reference's include/cuda_ops.h.  CPU only (no compute calls)."""
+reference's include/cuda_ops.h; the two cuda_ops.h headers declare the same
+types; the reference's own GPU host code links against the library.  CPU only
+(no compute calls)."""
 import ctypes
+import os
+import pathlib
+import re
 import subprocess
 
 import pytest
@@ -75,3 +80,39 @@ def test_reference_gpu_host_code_links_against_library():
     assert called <= set(REFERENCE_ABI), called - set(REFERENCE_ABI)
     assert called <= exported(), called - exported()
     ctypes.CDLL(str(DROPIN))
+
+
+def reference_header():
+    """include/cuda_ops.h of the reference tree that oracle/Makefile builds
+    from (its REF variable, or REF in the environment)."""
+    m = re.search(r"^REF\s*\?=\s*(\S+)", (ROOT / "oracle" / "Makefile").read_text(), re.M)
+    return pathlib.Path(os.environ.get("REF", m.group(1))) / "include" / "cuda_ops.h"
+
+
+def compile_both(ours, tmp_path):
+    """Compile one C file that includes the reference header and then ours:
+    a prototype of ours that conflicts with the reference's is an error."""
+    src = tmp_path / "both.c"
+    src.write_text(f'#include "{reference_header()}"\n#undef HOLO_CUDA_OPS_H\n#include "{ours}"\n'
+                   "int main(void) { return 0; }\n")
+    return subprocess.run(["gcc", "-std=gnu11", "-Wall", "-Werror", "-c", str(src), "-o", str(tmp_path / "both.o")],
+                          capture_output=True, text=True)
+
+
+def test_header_prototypes_match_reference(tmp_path):
+    """Type-level identity of the 48 declarations (names are checked above):
+    the C compiler accepts the reference's and this build's header in one
+    translation unit, and rejects a copy of ours with one parameter type
+    changed."""
+    if not reference_header().exists():
+        pytest.skip("reference tree absent")
+    ours = ROOT / "include" / "cuda_ops.h"
+    p = compile_both(ours, tmp_path)
+    assert p.returncode == 0, p.stderr
+    bad = tmp_path / "cuda_ops_bad.h"
+    text = ours.read_text()
+    proto = "void cuda_matmul_q4_k(float *dst, const void *M, const float *v, int out_dim, int in_dim);"
+    assert proto in text
+    bad.write_text(text.replace(proto, proto.replace("int out_dim", "long out_dim")))
+    p = compile_both(bad, tmp_path)
+    assert p.returncode != 0 and "conflicting types" in p.stderr
