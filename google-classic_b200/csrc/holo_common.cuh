@@ -14,6 +14,9 @@
 #include "cuda_ops.h"
 #include "holo_b200.h"
 
+// library-internal spelling of success (the public header says HOLO_STATUS_OK)
+#define HOLO_OK HOLO_STATUS_OK
+
 // ---------------------------------------------------------------------------
 // ggml type ids (src/ai/quant.h:20-33)
 // ---------------------------------------------------------------------------

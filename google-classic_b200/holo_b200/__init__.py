@@ -29,7 +29,7 @@ ACT_F32, ACT_Q8 = 0, 1
 Q4K_REF, Q4K_GGML = 0, 1
 ROPE_HALF, ROPE_ADJACENT = 0, 1          # holo_model_desc.rope_mode
 
-HOLO_OK = 0
+HOLO_OK = HOLO_STATUS_OK = 0   # HOLO_STATUS_OK in include/holo_b200.h
 HOLO_E_ARG, HOLO_E_NOMEM, HOLO_E_UNSUPPORTED, HOLO_E_TIMEOUT, HOLO_E_COMM = 1001, 1002, 1003, 1004, 1005
 COMM_HANDLE_BYTES = 128   # HOLO_COMM_HANDLE_BYTES
 

@@ -21,7 +21,9 @@ extern "C" {
  * failure in a sticky status: a cudaError_t value, or one of the HOLO_E_*
  * codes below.  cuda_last_status() also collects the device-side error word
  * written by kernels whose bounded waits timed out (it synchronises). */
-#define HOLO_OK               0
+#define HOLO_STATUS_OK        0   /* success (not HOLO_OK: the reference's holo.h
+                                     declares that name as an enumerator of
+                                     holo_result_t, include/holo.h:28-35) */
 #define HOLO_E_ARG         1001   /* bad shape / type / pointer               */
 #define HOLO_E_NOMEM       1002   /* device allocation failed                 */
 #define HOLO_E_UNSUPPORTED 1003   /* shape beyond a kernel's limits           */
@@ -252,7 +254,7 @@ void holo_model_free(void *model);
  * the Q8 matvec's integer block dots per row).
  * X is quantized to Q8 per 32-block as the matvecs do; the dequantized
  * activations and weights are rounded to fp16 and multiplied with fp32
- * accumulation.  Device pointers; HOLO_OK or an error status. */
+ * accumulation.  Device pointers; HOLO_STATUS_OK or an error status. */
 int cuda_matmul_quant_batched(float *Y, const void *W, const float *X, int M, int N, int K);
 
 /* Seeded synthetic weights on the device: rows x cols values N(0, std) from a

@@ -116,3 +116,20 @@ def test_header_prototypes_match_reference(tmp_path):
     bad.write_text(text.replace(proto, proto.replace("int out_dim", "long out_dim")))
     p = compile_both(bad, tmp_path)
     assert p.returncode != 0 and "conflicting types" in p.stderr
+
+
+@pytest.mark.parametrize("order", ["ours_first", "holo_first"])
+def test_header_coexists_with_reference_holo_h(tmp_path, order):
+    """A unit of the reference's app may include its holo.h (which declares
+    HOLO_OK, HOLO_ERROR... as enumerators, include/holo.h:28-35) and this
+    build's headers, in either order."""
+    holo_h = reference_header().parent / "holo.h"
+    if not holo_h.exists():
+        pytest.skip("reference tree absent")
+    ours = [f'#include "{ROOT / "include" / "cuda_ops.h"}"', f'#include "{ROOT / "include" / "holo_b200.h"}"']
+    lines = ours + [f'#include "{holo_h}"'] if order == "ours_first" else [f'#include "{holo_h}"'] + ours
+    src = tmp_path / "both.c"
+    src.write_text("\n".join(lines) + "\nint main(void) { return HOLO_OK + HOLO_STATUS_OK; }\n")
+    p = subprocess.run(["gcc", "-std=gnu11", "-Wall", "-Werror", "-c", str(src), "-o", str(tmp_path / "both.o")],
+                       capture_output=True, text=True)
+    assert p.returncode == 0, p.stderr
