@@ -99,8 +99,16 @@ extern "C" holo_tokenizer *holo_tokenizer_create(const char *const *vocab, int v
         // equal strings become one trie path holding the first index
         std::vector<std::pair<const char *, int>> ent;
         ent.reserve((size_t)vocab_size);
+        size_t total = 0;   // trie nodes <= total string bytes + 1: node ids must fit int32
         for (int i = 0; i < vocab_size; ++i)
-            if (vocab[i] && vocab[i][0]) ent.emplace_back(vocab[i], i);
+            if (vocab[i] && vocab[i][0]) {
+                ent.emplace_back(vocab[i], i);
+                total += std::strlen(vocab[i]);
+            }
+        if (total >= (size_t)INT32_MAX) {
+            delete t;
+            return nullptr;
+        }
         std::stable_sort(ent.begin(), ent.end(), [](const std::pair<const char *, int> &a,
                                                     const std::pair<const char *, int> &b) {
             return std::strcmp(a.first, b.first) < 0;   // strcmp orders bytes as unsigned char

@@ -272,8 +272,9 @@ int cuda_synth_weights(void *dst, int ggml_type, int rows, int cols, unsigned lo
  * first token equal to the byte's GPT-2 byte-level string as
  * find_byte_token builds it (llm.c:113-175), else unk_token -- one byte at a
  * time.  The reference rescans the vocabulary at every position; here it is a
- * byte trie built once by holo_tokenizer_create (which copies nothing it
- * keeps pointers to: the strings may be freed afterwards).
+ * byte trie built once by holo_tokenizer_create (which keeps no pointer into
+ * vocab: the strings may be freed afterwards; NULL for vocab_size < 0, a NULL
+ * vocab with vocab_size > 0, 2 GiB or more of token strings, or no memory).
  * holo_tokenize mirrors llm_tokenize(ctx, text, tokens, max_tokens, add_bos):
  * bos_token first when add_bos and max_tokens > 0, at most max_tokens ids,
  * returns the count; -1 for a NULL tokenizer or text, or NULL tokens with
