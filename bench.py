@@ -264,8 +264,12 @@ def run_ours(args, rank, world, local_rank):
 
     # the reference's own CUDA kernels (src/ai/cuda_ops.cu built for sm_100a) on
     # raw blocks: the GPU kernels this library replaces
+    # Single-GPU sub-benchmarks (the reference's kernels, prefill, other weight
+    # types) run at N = 1 only: they are per-GPU figures, and at N > 1 rank 0
+    # alone would run them while the other ranks wait to tear down.
+    single = rank == 0 and world == 1
     ref_gpu = None
-    if rank == 0 and not args.no_ref_gpu:
+    if single and not args.no_ref_gpu:
         ref_gpu = ref_gpu_kernels(mats, dev, torch)
 
     cpu = None
@@ -275,8 +279,8 @@ def run_ours(args, rank, world, local_rank):
     decode = None
     if not args.no_decode:
         decode = decode_bench(args, world, rank, torch)
-    prefill = prefill_bench(dev, torch) if rank == 0 and not args.no_prefill else None
-    other_types = other_types_bench(dev, torch) if rank == 0 and not args.no_prefill else None
+    prefill = prefill_bench(dev, torch) if single and not args.no_prefill else None
+    other_types = other_types_bench(dev, torch) if single and not args.no_prefill else None
 
     traffic = read_traffic()
     line = {
