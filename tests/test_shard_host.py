@@ -66,3 +66,17 @@ def test_two_gloo_ranks_exchange_handles_and_agree_on_shards(tmp_path):
     for r in range(2):
         res = json.loads((tmp_path / f"host_{r}.json").read_text())
         assert res and all(res.values()), (r, res)
+
+
+@pytest.mark.parametrize("cfg", [LLAMA2_7B, LLAMA3_70B], ids=["7b", "70b"])
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_prompt_pass_slices_are_whole_float4s(cfg, world):
+    """Sharded prompt passes exchange each rank's column slice with 16-byte
+    peer stores, so every slice's offset and width must be a multiple of 4
+    floats (holo_model_create falls back to one position a step otherwise):
+    true for the bench models at every world size."""
+    hd = cfg["head_dim"]
+    for r in range(world):
+        p = shard_ranges(cfg, world, r)
+        for first, count in ((p["heads"][0] * hd, p["heads"][1] * hd), p["dim"], p["ffn"]):
+            assert first % 4 == 0 and count % 4 == 0, (world, r, p)
