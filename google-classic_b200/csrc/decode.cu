@@ -576,8 +576,13 @@ bool launch_pdl(K kern, dim3 grid, dim3 block, cudaStream_t st, bool pdl, Args..
 // ---------------------------------------------------------------------------
 struct HoloLayer {
     float *attn_norm = nullptr, *ffn_norm = nullptr;
-    uint8_t *wqkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr;
-    WeightInfo i_qkv, i_o, i_13, i_2;
+    // [Wq; Wk; Wv] in one tiled weight -- [Wq; Wk] when Wv has its own type
+    // (then in wv) -- Wo, [W1; W3] interleaved by 16 rows, W2
+    uint8_t *wqkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr, *wv = nullptr;
+    WeightInfo i_qkv, i_o, i_13, i_2, i_v;
+    // GGUF types of Wv and W2 (the reference keeps them per layer,
+    // llm.c:445-507); the other five matrices have desc.layer_type
+    int wv_type = -1, w2_type = -1;
     bool ready = false;
 };
 
@@ -622,7 +627,12 @@ struct HoloModel {
     int gen_n_prompt = -1;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};   // generate: start, prefill done, end
     float last_prefill_ms = 0.0f, last_decode_ms = 0.0f;
-    // persistent step kernel (step.cu)
+    // the caller's embedding table type (desc.emb_type): F32 / F16 kept as
+    // given, quantized tables dequantized once into an F32 table
+    int emb_src = 1;
+    // persistent step kernel (step.cu): step_kernel is the create-time choice,
+    // use_step also needs types it serves (uniform layers, Q8_0/Q4_0/Q4_K)
+    bool step_kernel = false;
     bool use_step = false;
     bool step_ready = false;
     StepLayer *d_layers = nullptr;
@@ -730,6 +740,11 @@ bool enqueue_step(HoloModel *m, cudaStream_t st, bool sample, const SampleArgs &
         a.x = m->x; a.y = m->qkv; a.norm_w = L.attn_norm; a.eps = d.eps; a.act = d.act_mode;
         a.epi = MV_EPI_STORE; a.pdl = pdl;
         ok = ok && holo_matvec_launch(L.wqkv, L.i_qkv, a, st);
+        if (L.wv) {   // Wv of its own type: v after q and k
+            MvLaunch av = a;
+            av.y = m->qkv + m->q_dim + m->kv_dim;
+            ok = ok && holo_matvec_launch(L.wv, L.i_v, av, st);
+        }
         uint8_t *kc = (uint8_t *)m->kc + (size_t)l * kv_layer * kv_es;
         uint8_t *vc = (uint8_t *)m->vc + (size_t)l * kv_layer * kv_es;
         const int heads = max(d.n_heads, d.n_kv_heads);
@@ -1001,10 +1016,12 @@ bool prompt_supported(const HoloModel *m) {
         return false;
     if (d.n_heads / d.n_kv_heads > PA_ROWS || (d.head_dim != 64 && d.head_dim != 128 && d.head_dim != 256))
         return false;
-    for (const HoloLayer &L : m->layers)
+    for (const HoloLayer &L : m->layers) {
+        if (L.wv) return false;   // the row passes read [Wq; Wk; Wv] as one weight
         for (const WeightInfo *wi : {&L.i_qkv, &L.i_o, &L.i_13, &L.i_2})
             if (wi->type != GT_Q4_K && wi->type != GT_Q4_0 && wi->type != GT_Q8_0)
                 return false;
+    }
     return true;
 }
 
@@ -1130,6 +1147,27 @@ cudaGraphExec_t capture_step(HoloModel *m, bool sample, const SampleArgs &sa) {
     }
     cudaGraphDestroy(g);
     return ex;
+}
+
+// the types the persistent step kernel is built for (step.cu holo_step_launch)
+bool step_type(int t) { return t == GT_Q8_0 || t == GT_Q4_0 || t == GT_Q4_K; }
+
+// the step kernel runs when chosen at create and every matrix type is one it
+// serves, uniform across the layers; otherwise the one-launch-per-op graph
+void refresh_use_step(HoloModel *m) {
+    bool ok = m->step_kernel && step_type(m->d.layer_type) && step_type(m->d.out_type);
+    for (const HoloLayer &L : m->layers) ok = ok && L.wv_type == m->d.layer_type && L.w2_type == m->d.layer_type;
+    if (ok != m->use_step) {
+        m->use_step = ok;
+        m->step_ready = false;
+    }
+}
+
+// token embedding tables the engine takes: F32, F16, or GGUF blocks of Q8_0,
+// Q4_0, Q4_K, Q6_K (get_embedding, src/ai/llm.c:941-1008)
+bool emb_type_ok(int t, int dim) {
+    if (t == GT_F32 || t == GT_F16) return true;
+    return (t == GT_Q8_0 || t == GT_Q4_0 || t == GT_Q4_K || t == GT_Q6_K) && holo_quant_shape_ok(t, 1, dim);
 }
 
 bool model_ready(HoloModel *m) {
@@ -1317,7 +1355,7 @@ void *holo_model_create(const holo_model_desc *desc) {
     if (d.n_layers <= 0 || d.dim <= 0 || d.n_heads <= 0 || d.n_kv_heads <= 0 || d.n_heads % d.n_kv_heads ||
         !(hd == 64 || hd == 128 || hd == 256) || d.ffn_dim <= 0 || d.ffn_dim % 16 || d.vocab <= 0 ||
         d.max_seq <= 0 || (d.act_mode != HOLO_ACT_Q8 && d.act_mode != HOLO_ACT_F32) ||
-        (d.emb_type != 0 && d.emb_type != 1) ||
+        !emb_type_ok(d.emb_type, d.dim) ||
         !holo_quant_shape_ok(d.layer_type, d.n_heads * hd, d.dim) ||
         !holo_quant_shape_ok(d.layer_type, d.dim, d.n_heads * hd) ||
         !holo_quant_shape_ok(d.layer_type, d.ffn_dim, d.dim) ||
@@ -1403,10 +1441,15 @@ void *holo_model_create(const holo_model_desc *desc) {
         // the persistent step kernel serves head_dim 128; HOLO_STEP=graph keeps
         // the one-launch-per-op graph
         const char *e = getenv("HOLO_STEP");
-        m->use_step = hd == 128 && !(e && strcmp(e, "graph") == 0);
+        m->step_kernel = hd == 128 && !(e && strcmp(e, "graph") == 0);
     }
+    for (HoloLayer &L : m->layers) L.wv_type = L.w2_type = d.layer_type;
+    m->emb_src = d.emb_type;
+    m->d.emb_type = d.emb_type == 1 ? 1 : 0;   // quantized tables become F32 (set_globals)
+    refresh_use_step(m);
     if (world > 1 && !m->use_step) {
-        holo_set_status(HOLO_E_UNSUPPORTED, "holo_model_create: sharding needs the step kernel (HOLO_STEP)");
+        holo_set_status(HOLO_E_UNSUPPORTED,
+                        "holo_model_create: sharding needs the step kernel (HOLO_STEP; Q8_0/Q4_0/Q4_K layers and output)");
         holo_model_free(m);
         return nullptr;
     }
@@ -1456,6 +1499,36 @@ void *holo_model_create(const holo_model_desc *desc) {
     return m;
 }
 
+int holo_model_set_layer_types(void *model, int l, int wv_type, int w2_type) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m || l < 0 || l >= m->d.n_layers) {
+        holo_set_status(HOLO_E_ARG, "holo_model_set_layer_types: bad arguments");
+        return HOLO_E_ARG;
+    }
+    const holo_model_desc &d = m->d;
+    auto quant = [](int t) { return t == GT_Q8_0 || t == GT_Q4_0 || t == GT_Q4_K || t == GT_Q6_K; };
+    if (!quant(wv_type) || !quant(w2_type) || !holo_quant_shape_ok(wv_type, m->kv_dim, d.dim) ||
+        !holo_quant_shape_ok(w2_type, m->dim_loc, d.ffn_dim)) {
+        holo_set_status(HOLO_E_ARG, "holo_model_set_layer_types: Wv / W2 type must be Q8_0, Q4_0, Q4_K or Q6_K "
+                                    "and divide the matrix rows");
+        return HOLO_E_ARG;
+    }
+    const bool mixed = wv_type != d.layer_type || w2_type != d.layer_type;
+    if (mixed && (m->world > 1 || m->batch > 1)) {
+        holo_set_status(HOLO_E_UNSUPPORTED, "holo_model_set_layer_types: per-layer types need batch 1 on one GPU");
+        return HOLO_E_UNSUPPORTED;
+    }
+    HoloLayer &L = m->layers[l];
+    if (L.wv_type != wv_type || L.w2_type != w2_type) {
+        L.wv_type = wv_type;
+        L.w2_type = w2_type;
+        L.ready = false;   // the weights follow in holo_model_set_layer
+        drop_graphs(m);
+        refresh_use_step(m);
+    }
+    return HOLO_OK;
+}
+
 int holo_model_set_layer(void *model, int l, const float *attn_norm, const void *wq, const void *wk, const void *wv,
                          const void *wo, const float *ffn_norm, const void *w1, const void *w2, const void *w3) {
     HoloModel *m = (HoloModel *)model;
@@ -1468,6 +1541,7 @@ int holo_model_set_layer(void *model, int l, const float *attn_norm, const void 
     const int t = d.layer_type;
     cudaStream_t st = holo_stream();
     HoloLayer &L = m->layers[l];
+    const int tv = L.wv_type, t2 = L.w2_type;
     drop_graphs(m);
     m->step_ready = false;
     if (!L.attn_norm && !upload_plain((void **)&L.attn_norm, attn_norm, sizeof(float) * d.dim, st))
@@ -1483,14 +1557,29 @@ int holo_model_set_layer(void *model, int l, const float *attn_norm, const void 
     auto rows_of = [](const void *p, size_t first_row, size_t row_bytes) {
         return static_cast<const void *>(static_cast<const uint8_t *>(p) + first_row * row_bytes);
     };
-    // [Wq; Wk; Wv] in one tiled buffer (each part a whole number of row-blocks)
+    // [Wq; Wk; Wv] in one tiled buffer (each part a whole number of row-blocks);
+    // a Wv of another type goes into a tiled buffer of its own
+    const bool own_v = tv != t;
     const size_t bq = cuda_quant_tiled_bytes(t, m->q_dim, d.dim), bk = cuda_quant_tiled_bytes(t, m->kv_dim, d.dim);
     if (!L.wqkv && !dev_alloc((void **)&L.wqkv, bq + 2 * bk)) return HOLO_E_NOMEM;
     if (!upload_repack(L.wqkv, rows_of(wq, (size_t)m->h0 * hd, row_dim), t, m->q_dim, d.dim, st) ||
-        !upload_repack(L.wqkv + bq, rows_of(wk, (size_t)m->kh0 * hd, row_dim), t, m->kv_dim, d.dim, st) ||
-        !upload_repack(L.wqkv + bq + bk, rows_of(wv, (size_t)m->kh0 * hd, row_dim), t, m->kv_dim, d.dim, st))
+        !upload_repack(L.wqkv + bq, rows_of(wk, (size_t)m->kh0 * hd, row_dim), t, m->kv_dim, d.dim, st))
         return cuda_last_status();
-    L.i_qkv = holo_weight_info(t, m->q_dim + 2 * m->kv_dim, d.dim, holo_q4k_layout());
+    if (!own_v) {
+        if (!upload_repack(L.wqkv + bq + bk, rows_of(wv, (size_t)m->kh0 * hd, row_dim), t, m->kv_dim, d.dim, st))
+            return cuda_last_status();
+        if (L.wv) cudaFree(L.wv);
+        L.wv = nullptr;
+    } else {
+        if (L.wv) cudaFree(L.wv);
+        L.wv = nullptr;
+        if (!dev_alloc((void **)&L.wv, cuda_quant_tiled_bytes(tv, m->kv_dim, d.dim))) return HOLO_E_NOMEM;
+        if (!upload_repack(L.wv, rows_of(wv, (size_t)m->kh0 * hd, gguf_row_bytes(tv, d.dim)), tv, m->kv_dim, d.dim,
+                           st))
+            return cuda_last_status();
+        L.i_v = holo_weight_info(tv, m->kv_dim, d.dim, holo_q4k_layout());
+    }
+    L.i_qkv = holo_weight_info(t, m->q_dim + (own_v ? 1 : 2) * m->kv_dim, d.dim, holo_q4k_layout());
     if (!L.wo && !dev_alloc((void **)&L.wo, cuda_quant_tiled_bytes(t, m->dim_loc, m->q_dim_g))) return HOLO_E_NOMEM;
     if (!upload_repack(L.wo, rows_of(wo, m->d0, gguf_row_bytes(t, m->q_dim_g)), t, m->dim_loc, m->q_dim_g, st))
         return cuda_last_status();
@@ -1515,10 +1604,14 @@ int holo_model_set_layer(void *model, int l, const float *attn_norm, const void 
         return cuda_last_status() ? cuda_last_status() : HOLO_E_ARG;
     }
     L.i_13 = holo_weight_info(t, 2 * m->ffn_loc, d.dim, holo_q4k_layout());
-    if (!L.w2 && !dev_alloc((void **)&L.w2, cuda_quant_tiled_bytes(t, m->dim_loc, d.ffn_dim))) return HOLO_E_NOMEM;
-    if (!upload_repack(L.w2, rows_of(w2, m->d0, gguf_row_bytes(t, d.ffn_dim)), t, m->dim_loc, d.ffn_dim, st))
+    if (L.w2 && L.i_2.type != t2) {   // a new type: the buffer size differs
+        cudaFree(L.w2);
+        L.w2 = nullptr;
+    }
+    if (!L.w2 && !dev_alloc((void **)&L.w2, cuda_quant_tiled_bytes(t2, m->dim_loc, d.ffn_dim))) return HOLO_E_NOMEM;
+    if (!upload_repack(L.w2, rows_of(w2, m->d0, gguf_row_bytes(t2, d.ffn_dim)), t2, m->dim_loc, d.ffn_dim, st))
         return cuda_last_status();
-    L.i_2 = holo_weight_info(t, m->dim_loc, d.ffn_dim, holo_q4k_layout());
+    L.i_2 = holo_weight_info(t2, m->dim_loc, d.ffn_dim, holo_q4k_layout());
     cudaStreamSynchronize(st);
     L.ready = cuda_last_status() == HOLO_OK;
     return L.ready ? HOLO_OK : cuda_last_status();
@@ -1536,7 +1629,21 @@ int holo_model_set_globals(void *model, const void *tok_embeddings, const float 
     m->step_ready = false;
     const size_t eb = (size_t)d.vocab * d.dim * (d.emb_type == 1 ? 2 : 4);
     if (!m->emb && !dev_alloc(&m->emb, eb)) return HOLO_E_NOMEM;
-    cudaMemcpyAsync(m->emb, tok_embeddings, eb, cudaMemcpyDefault, st);
+    if (m->emb_src == GT_F32 || m->emb_src == GT_F16) {
+        cudaMemcpyAsync(m->emb, tok_embeddings, eb, cudaMemcpyDefault, st);
+    } else {
+        // GGUF blocks: the table dequantized once, each row as get_embedding
+        // (src/ai/llm.c:941-1008) decodes it
+        const size_t raw = (size_t)d.vocab * gguf_row_bytes(m->emb_src, d.dim);
+        void *staging = nullptr;
+        if (!dev_alloc(&staging, raw)) return HOLO_E_NOMEM;
+        bool ok = cudaMemcpyAsync(staging, tok_embeddings, raw, cudaMemcpyDefault, st) == cudaSuccess &&
+                  holo_embedding_table_f32((float *)m->emb, staging, m->emb_src, d.vocab, d.dim,
+                                           holo_q4k_layout() == HOLO_Q4K_GGML, st);
+        cudaStreamSynchronize(st);
+        cudaFree(staging);
+        if (!ok) return cuda_last_status() ? cuda_last_status() : HOLO_E_ARG;
+    }
     if (!m->final_norm && !dev_alloc((void **)&m->final_norm, sizeof(float) * d.dim)) return HOLO_E_NOMEM;
     cudaMemcpyAsync(m->final_norm, final_norm, sizeof(float) * d.dim, cudaMemcpyDefault, st);
     if (!m->out && !dev_alloc((void **)&m->out, cuda_quant_tiled_bytes(d.out_type, m->vocab_loc, d.dim)))
@@ -1805,6 +1912,28 @@ int holo_model_launch_steps(void *model, int n_steps) {
     return HOLO_OK;
 }
 
+int holo_model_debug_vector(void *model, int which, float *dst) {
+    HoloModel *m = (HoloModel *)model;
+    if (!m || !dst) return -1;
+    const float *src = nullptr;
+    int n = 0;
+    switch (which) {
+    case 0: src = m->x; n = m->d.dim; break;
+    case 1: src = m->qkv; n = m->q_dim + 2 * m->kv_dim; break;
+    case 2: src = m->att; n = m->q_dim_g; break;
+    case 3: src = m->h; n = m->d.ffn_dim; break;
+    case 4: src = m->logits; n = m->d.vocab; break;
+    default: return -1;
+    }
+    cudaStream_t st = holo_stream();
+    if (cudaMemcpyAsync(dst, src, sizeof(float) * n, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess) {
+        holo_check_launch("holo_model_debug_vector");
+        return -1;
+    }
+    return n;
+}
+
 int holo_model_pos(void *model) { return model ? ((HoloModel *)model)->h_pos : -1; }
 
 int holo_model_last_timing(void *model, float *prefill_ms, float *decode_ms) {
@@ -2000,7 +2129,7 @@ void holo_model_free(void *model) {
         }
     for (auto &L : m->layers) {
         cudaFree(L.attn_norm); cudaFree(L.ffn_norm); cudaFree(L.wqkv); cudaFree(L.wo); cudaFree(L.w13);
-        cudaFree(L.w2);
+        cudaFree(L.w2); cudaFree(L.wv);
     }
     void *bbufs[] = {m->bx, m->bxn, m->bqkv, m->batt, m->bt, m->bhh, m->bh, m->blogits, m->bpart, m->brvals,
                      m->bprobs, m->bkept_p, m->bkept_idx,

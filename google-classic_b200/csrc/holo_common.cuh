@@ -153,10 +153,18 @@ cudaStream_t holo_stream();
 // else the device's library stream if it exists, else the legacy stream (0)
 cudaStream_t holo_stream_if_ready();
 void holo_set_status(int code, const char *what);   // sticky host-side status
+// noalloc.cu: the static scratch's bounded-wait word on device `dev` (0 when
+// never set up), reset afterwards when `clear`
+int holo_noalloc_collect_status(int dev, bool clear);
 bool holo_check_launch(const char *what);           // cudaGetLastError -> status
 // Scratch of at least `bytes` on the current device for ABI helpers whose
 // reference signature has no workspace argument (grows; synchronises then).
 void *holo_tmp(size_t bytes);
+
+// ops.cu: every row of a raw GGUF embedding table (Q8_0, Q4_0, Q4_K, Q6_K)
+// dequantized into dst [rows][dim] as the reference's get_embedding decodes it
+bool holo_embedding_table_f32(float *dst, const void *table, int type, int rows, int dim, bool ggml_q4k,
+                              cudaStream_t st);
 
 // Registry of repacked weights: device pointer -> geometry.
 struct WeightInfo {

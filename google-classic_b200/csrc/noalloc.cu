@@ -7,14 +7,20 @@
 //   counters [NA_MAX_ROWBLOCKS] i32     -- 8192 row-blocks = 262144 output rows;
 //                                          must be zero when a launch starts
 //   status   [4] i32                    -- bounded-wait error word; starts at zero
-// Set-up, once per device, takes the arrays' addresses with
-// cudaGetSymbolAddress and clears the status word; every call clears the
-// counters of the row-blocks it uses before its launch.  All calls on one
-// device share these arrays: calls that overlap in time (other streams or
-// host threads) race and must not be issued.
+// Set-up, once per device, done by the first call on that device: it takes
+// the arrays' addresses with cudaGetSymbolAddress and clears the status word
+// (so that first call should come before any stream capture).  Every call
+// clears the counters of the row-blocks it uses before its launch.  All calls
+// on one device share these arrays: calls that overlap in time (other streams
+// or host threads) race and must not be issued.
+//
+// A launch whose bounded wait gives up writes HOLO_E_TIMEOUT into the status
+// word; cuda_last_status collects it (holo_noalloc_collect_status) and
+// cuda_clear_status resets it.
 #include "holo_common.cuh"
 #include "matvec.cuh"
 
+#include <atomic>
 #include <mutex>
 
 namespace {
@@ -28,7 +34,7 @@ __device__ __align__(256) int g_na_counters[NA_MAX_ROWBLOCKS];
 __device__ __align__(256) int g_na_status[4];
 
 struct NaDevice {
-    bool ready = false;
+    std::atomic<bool> ready{false};   // release-stored after the fields below are set
     float *partials = nullptr;
     int *counters = nullptr;
     int *status = nullptr;
@@ -41,9 +47,9 @@ std::mutex g_na_mu;
 NaDevice *na_device(int dev, cudaStream_t st) {
     if (dev < 0 || dev >= NA_MAX_DEVICES) return nullptr;
     NaDevice &N = g_na[dev];
-    if (N.ready) return &N;
+    if (N.ready.load(std::memory_order_acquire)) return &N;
     std::lock_guard<std::mutex> lk(g_na_mu);
-    if (N.ready) return &N;
+    if (N.ready.load(std::memory_order_relaxed)) return &N;
     cudaError_t e = cudaGetSymbolAddress((void **)&N.partials, g_na_partials);
     if (e == cudaSuccess) e = cudaGetSymbolAddress((void **)&N.counters, g_na_counters);
     if (e == cudaSuccess) e = cudaGetSymbolAddress((void **)&N.status, g_na_status);
@@ -54,11 +60,29 @@ NaDevice *na_device(int dev, cudaStream_t st) {
         holo_set_status((int)e, "cuda_matvec_noalloc: scratch set-up (cudaGetSymbolAddress)");
         return nullptr;
     }
-    N.ready = true;
+    N.ready.store(true, std::memory_order_release);
     return &N;
 }
 
 }  // namespace
+
+// Bounded-wait status of the static scratch on device `dev`: waits for the
+// device's queued work, returns the word (0 when the no-allocation path was
+// never set up there) and, with `clear`, resets it.
+int holo_noalloc_collect_status(int dev, bool clear) {
+    if (dev < 0 || dev >= NA_MAX_DEVICES) return 0;
+    NaDevice &N = g_na[dev];
+    if (!N.ready.load(std::memory_order_acquire)) return 0;
+    int word = 0;
+    // the call may have run on any stream of the device
+    if (cudaDeviceSynchronize() != cudaSuccess ||
+        cudaMemcpy(&word, N.status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (clear && word != 0 && cudaMemset(N.status, 0, sizeof(int) * 4) != cudaSuccess) cudaGetLastError();
+    return word;
+}
 
 extern "C" int cuda_matvec_noalloc(float *dst, const void *M, const float *v, int out_dim, int in_dim,
                                    int ggml_type, int act_mode) {
@@ -108,4 +132,14 @@ extern "C" int cuda_matvec_noalloc(float *dst, const void *M, const float *v, in
     L.pdl = false;
     if (!holo_matvec_launch_with(M, wi, L, st, S)) return cuda_last_status() ? cuda_last_status() : HOLO_E_ARG;
     return HOLO_OK;
+}
+
+extern "C" void *cuda_matvec_noalloc_status_word(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    NaDevice *N = na_device(dev, holo_stream_if_ready());
+    return N ? (void *)N->status : nullptr;
 }

@@ -236,23 +236,21 @@ __global__ void rope_kernel(float *q, float *k, int pos, int hd, int n_heads, in
     }
 }
 
-// embedding rows (llm.c:943-1008 value semantics)
+// embedding rows (llm.c:943-1008 value semantics): value i of row `token`
 template <int TYPE>
-__global__ void embedding_kernel(float *dst, const uint8_t *table, int token, int dim) {
-    int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= dim) return;
+__device__ __forceinline__ float emb_value(const uint8_t *table, int token, int dim, int i) {
     if (TYPE == GT_F32) {
-        dst[i] = reinterpret_cast<const float *>(table)[(size_t)token * dim + i];
+        return reinterpret_cast<const float *>(table)[(size_t)token * dim + i];
     } else if (TYPE == GT_F16) {
-        dst[i] = __half2float(reinterpret_cast<const __half *>(table)[(size_t)token * dim + i]);
+        return __half2float(reinterpret_cast<const __half *>(table)[(size_t)token * dim + i]);
     } else if (TYPE == GT_Q8_0) {
         const uint8_t *blk = table + ((size_t)token * (dim / 32) + i / 32) * 34;
-        dst[i] = half_bits_to_float(blk[0] | (blk[1] << 8)) * (float)(int8_t)blk[2 + i % 32];
+        return half_bits_to_float(blk[0] | (blk[1] << 8)) * (float)(int8_t)blk[2 + i % 32];
     } else if (TYPE == GT_Q4_0) {
         const uint8_t *blk = table + ((size_t)token * (dim / 32) + i / 32) * 18;
         int j = i % 32;
         int nib = j < 16 ? (blk[2 + j] & 0xf) : (blk[2 + j - 16] >> 4);
-        dst[i] = half_bits_to_float(blk[0] | (blk[1] << 8)) * (float)(nib - 8);
+        return half_bits_to_float(blk[0] | (blk[1] << 8)) * (float)(nib - 8);
     } else {  // Q6_K, value layout of quant.c:241-271
         const uint8_t *blk = table + ((size_t)token * (dim / 256) + i / 256) * 210;
         int j = i % 256, n = j / 128, pc = j % 128, l = pc % 32, which = pc / 32;
@@ -262,8 +260,14 @@ __global__ void embedding_kernel(float *dst, const uint8_t *table, int token, in
                     : (which == 2) ? (ql[l] >> 4) : (ql[l + 32] >> 4);
         int q = (lowbits | (((qh[l] >> (2 * which)) & 3) << 4)) - 32;
         float d = half_bits_to_float(blk[208] | (blk[209] << 8));
-        dst[i] = d * (float)sc[l / 16 + 2 * which] * (float)q;
+        return d * (float)sc[l / 16 + 2 * which] * (float)q;
     }
+}
+
+template <int TYPE>
+__global__ void embedding_kernel(float *dst, const uint8_t *table, int token, int dim) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < dim) dst[i] = emb_value<TYPE>(table, token, dim, i);
 }
 
 // Q4_K embedding row (the reference's GPU dispatcher, llm_cuda.c:166-186, has
@@ -272,9 +276,7 @@ __global__ void embedding_kernel(float *dst, const uint8_t *table, int token, in
 // high -> l + 16) or, ggml != 0, as llama.cpp packs the block
 // (get_scale_min_k4, cuda_ops.cu:684-692; 32 bytes per 64 values, low
 // nibbles the first 32).  y = (d*sc)*q - dmin*m, each product rounded once.
-__global__ void q4k_embedding_kernel(float *dst, const uint8_t *table, int token, int dim, int ggml) {
-    int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= dim) return;
+__device__ __forceinline__ float q4k_emb_value(const uint8_t *table, int token, int dim, int i, int ggml) {
     const uint8_t *blk = table + ((size_t)token * (dim / 256) + i / 256) * 144;
     const int v = i % 256, j = v / 32, l = v % 32;
     const uint8_t *q = blk + 4;
@@ -302,7 +304,21 @@ __global__ void q4k_embedding_kernel(float *dst, const uint8_t *table, int token
     }
     const float d = half_bits_to_float(blk[0] | (blk[1] << 8)), dmin = half_bits_to_float(blk[2] | (blk[3] << 8));
     const float scale = __fmul_rn(d, (float)sc), mval = __fmul_rn(dmin, (float)mn);
-    dst[i] = __fsub_rn(__fmul_rn(scale, (float)nib), mval);
+    return __fsub_rn(__fmul_rn(scale, (float)nib), mval);
+}
+
+__global__ void q4k_embedding_kernel(float *dst, const uint8_t *table, int token, int dim, int ggml) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < dim) dst[i] = q4k_emb_value(table, token, dim, i, ggml);
+}
+
+// every row of a table (row = blockIdx.y): dst [rows][dim] fp32
+template <int TYPE>
+__global__ void embedding_table_kernel(float *dst, const uint8_t *table, int dim, int ggml) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x, token = blockIdx.y;
+    if (i >= dim) return;
+    dst[(size_t)token * dim + i] = TYPE == GT_Q4_K ? q4k_emb_value(table, token, dim, i, ggml)
+                                                   : emb_value<TYPE>(table, token, dim, i);
 }
 
 // argmax, first maximum wins (tensor.c:460-470)
@@ -379,6 +395,25 @@ void run_attention(float *dst, const float *q, const float *kc, const float *vc,
 }
 
 }  // namespace
+
+// The fp32 values of every row of a raw GGUF embedding table (Q8_0, Q4_0,
+// Q4_K in the quant.c or, ggml_q4k, the llama.cpp packing, Q6_K), each as
+// get_embedding (src/ai/llm.c:941-1008) decodes it: dst [rows][dim].
+bool holo_embedding_table_f32(float *dst, const void *table, int type, int rows, int dim, bool ggml_q4k,
+                              cudaStream_t st) {
+    const dim3 grid((dim + EW_THREADS - 1) / EW_THREADS, rows);
+    const uint8_t *t = (const uint8_t *)table;
+    switch (type) {
+    case GT_Q8_0: embedding_table_kernel<GT_Q8_0><<<grid, EW_THREADS, 0, st>>>(dst, t, dim, 0); break;
+    case GT_Q4_0: embedding_table_kernel<GT_Q4_0><<<grid, EW_THREADS, 0, st>>>(dst, t, dim, 0); break;
+    case GT_Q4_K: embedding_table_kernel<GT_Q4_K><<<grid, EW_THREADS, 0, st>>>(dst, t, dim, ggml_q4k ? 1 : 0); break;
+    case GT_Q6_K: embedding_table_kernel<GT_Q6_K><<<grid, EW_THREADS, 0, st>>>(dst, t, dim, 0); break;
+    default:
+        holo_set_status(HOLO_E_ARG, "embedding table: type");
+        return false;
+    }
+    return holo_check_launch("embedding table");
+}
 
 extern "C" {
 

@@ -179,6 +179,10 @@ int cuda_last_status(void) {
             dev_status != 0)
             holo_set_status(dev_status, "kernel bounded wait timed out");
     }
+    if (n > 0) {
+        int na_status = holo_noalloc_collect_status(current_device(), false);
+        if (na_status != 0) holo_set_status(na_status, "cuda_matvec_noalloc: kernel bounded wait timed out");
+    }
     std::lock_guard<std::mutex> lk(g_status_mu);
     return g_status;
 }
@@ -201,6 +205,8 @@ void cuda_clear_status(void) {
         cudaMemset(g_dev[id].mvb_counters, 0, sizeof(int) * MVB_MAX_GROUPS);
         cudaDeviceSynchronize();
     }
+    int n = 0;
+    if (cudaGetDeviceCount(&n) == cudaSuccess && n > 0) holo_noalloc_collect_status(id, true);
     cudaGetLastError();
 }
 
@@ -347,6 +353,14 @@ void cuda_memcpy_d2h(void *dst, const void *src, size_t size) {
     cudaStream_t st = holo_stream();
     HOLO_CUDA_TRY(cudaMemcpyAsync(dst, src, size, cudaMemcpyDeviceToHost, st), "cuda_memcpy_d2h");
     HOLO_CUDA_TRY(cudaStreamSynchronize(st), "cuda_memcpy_d2h");
+}
+
+void cuda_memcpy_h2d_stream(void *dst, const void *src, size_t size) {
+    HOLO_CUDA_TRY(cudaMemcpyAsync(dst, src, size, cudaMemcpyHostToDevice, holo_stream()), "cuda_memcpy_h2d_stream");
+}
+
+void cuda_memcpy_d2h_stream(void *dst, const void *src, size_t size) {
+    HOLO_CUDA_TRY(cudaMemcpyAsync(dst, src, size, cudaMemcpyDeviceToHost, holo_stream()), "cuda_memcpy_d2h_stream");
 }
 
 void cuda_memcpy_d2d(void *dst, const void *src, size_t size) {

@@ -450,6 +450,8 @@ __device__ __forceinline__ void rope16(float (&v)[16], int l8, const StepPersist
 
 // positions a CTA folds per iteration: 8 warps x 4 groups of 8 lanes
 constexpr int ATT_SLOTS = LY_WARPS * 4;
+// the CTA count the attention splits are sized for (one per SM of a B200)
+constexpr int ATT_SPLIT_CTAS = 148;
 
 // partial (m, l, acc[HD]) of one (head, split): header at 0, 1; acc at 4..
 // (stride HD + 4 floats keeps every acc row 16-byte aligned)
@@ -496,8 +498,12 @@ __device__ __forceinline__ bool step_attn(const StepArgs &a, const StepPersist &
                                        unsigned eq, unsigned eo) {
     constexpr int HD = ST_HD;
     const int kv_len = pos + 1, nh = a.n_heads;
-    // about grid / heads CTAs per head, whole iterations each
-    const int per_head = max(1, a.grid / nh);
+    // A head's positions are cut into splits of whole slot iterations, about
+    // ATT_SPLIT_CTAS / (all heads of the model) of them: a function of kv_len
+    // and the model alone, so every world size (and grid) folds a head's
+    // positions in the same splits and merges them in the same order -- a
+    // sharded step's attention output is bit-identical to one GPU's.
+    const int per_head = max(1, ATT_SPLIT_CTAS / a.n_heads_g);
     int per_split = (kv_len + per_head - 1) / per_head;
     per_split = (per_split + ATT_SLOTS - 1) / ATT_SLOTS * ATT_SLOTS;
     const int nsp = (kv_len + per_split - 1) / per_split;

@@ -80,16 +80,20 @@ SIGNATURES = {
     "cuda_quant_tiled_bytes": (_sz, [_i, _i, _i]),
     "cuda_matvec": (None, [_vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "cuda_matvec_noalloc": (_i, [_vp, _vp, _vp, _i, _i, _i, _i]),
+    "cuda_matvec_noalloc_status_word": (_vp, []),
     "cuda_dequantize_rows": (None, [_vp, _vp, _i, _i, _i]),
     "cuda_quantize_act_q8": (None, [_vp, _vp, _vp, _vp, _i]),
     "cuda_block_sums_q8": (None, [_vp, _vp, _vp, _i, _i, _i]),
     "cuda_get_stream": (_vp, []), "cuda_set_stream": (None, [_vp]),
+    "cuda_memcpy_h2d_stream": (None, [_vp, _vp, _sz]), "cuda_memcpy_d2h_stream": (None, [_vp, _vp, _sz]),
     "cuda_init_rank": (_i, [_i, _i]), "cuda_sm_count": (_i, []),
     "cuda_set_pdl": (None, [_i]), "cuda_get_pdl": (_i, []),
     "cuda_capture_begin": (_i, []), "cuda_capture_end": (_vp, []),
     "cuda_graph_launch": (None, [_vp]), "cuda_graph_free": (None, [_vp]),
     "holo_model_create": (_vp, [_vp]),
     "holo_model_set_layer": (_i, [_vp, _i] + [_vp] * 9),
+    "holo_model_set_layer_types": (_i, [_vp, _i, _i, _i]),
+    "holo_model_debug_vector": (_i, [_vp, _i, _vp]),
     "holo_model_set_globals": (_i, [_vp, _vp, _vp, _vp]),
     "holo_model_forward": (_i, [_vp, _i, _vp]),
     "holo_model_prefill": (_i, [_vp, _vp, _i, _vp]),

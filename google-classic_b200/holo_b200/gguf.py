@@ -155,7 +155,10 @@ class GGUFFile:
 
 def model_config(g: GGUFFile, max_seq: int | None = None) -> dict:
     """Model configuration (holo_b200.model.ModelDesc keys) from the metadata
-    and tensor types; the layer matrices must share one type."""
+    and tensor types.  attn_q / attn_k / attn_output / ffn_gate / ffn_up share
+    one type (layer_type, the reference's g_weight_type); attn_v and ffn_down
+    may differ per layer (wv_types / w2_types, as Q4_K_M files keep some of
+    them in Q6_K; the reference binds them per layer, llm.c:445-507)."""
     arch = g.meta.get("general.architecture", "llama")
 
     def key(k, default):
@@ -164,19 +167,27 @@ def model_config(g: GGUFFile, max_seq: int | None = None) -> dict:
     dim = int(key("embedding_length", 4096))
     nh = int(key("attention.head_count", 32))
     emb_dims, emb_type, _ = g.tensors["token_embd.weight"]
-    layer_types = {g.tensors[f"blk.{l}.{n}.weight"][1] for l in range(int(key("block_count", 32)))
-                   for n in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_down", "ffn_up")}
+    n_layers = int(key("block_count", 32))
+    layer_types = {g.tensors[f"blk.{l}.{n}.weight"][1] for l in range(n_layers)
+                   for n in ("attn_q", "attn_k", "attn_output", "ffn_gate", "ffn_up")}
     if len(layer_types) != 1:
-        raise ValueError(f"layer matrices of several types {sorted(layer_types)}: the decode engine takes one")
+        raise ValueError(f"attn_q/attn_k/attn_output/ffn_gate/ffn_up of several types {sorted(layer_types)}: "
+                         "the engine (as the reference) takes one type for these")
+    wv_types = [g.tensors[f"blk.{l}.attn_v.weight"][1] for l in range(n_layers)]
+    w2_types = [g.tensors[f"blk.{l}.ffn_down.weight"][1] for l in range(n_layers)]
     out_name = "output.weight" if "output.weight" in g.tensors else "token_embd.weight"
     ctx = int(key("context_length", 4096))
-    return dict(n_layers=int(key("block_count", 32)), dim=dim, n_heads=nh,
-                n_kv_heads=int(key("attention.head_count_kv", nh)),
-                head_dim=int(key("attention.key_length", dim // nh)), ffn_dim=int(key("feed_forward_length", 11008)),
-                vocab=int(emb_dims[1]), max_seq=min(ctx, max_seq) if max_seq else ctx,
-                rope_base=float(key("rope.freq_base", 10000.0)),
-                eps=float(key("attention.layer_norm_rms_epsilon", 1e-5)), layer_type=layer_types.pop(),
-                emb_type=1 if emb_type == F16 else 0, out_type=g.tensors[out_name][1])
+    lt = layer_types.pop()
+    cfg = dict(n_layers=n_layers, dim=dim, n_heads=nh,
+               n_kv_heads=int(key("attention.head_count_kv", nh)),
+               head_dim=int(key("attention.key_length", dim // nh)), ffn_dim=int(key("feed_forward_length", 11008)),
+               vocab=int(emb_dims[1]), max_seq=min(ctx, max_seq) if max_seq else ctx,
+               rope_base=float(key("rope.freq_base", 10000.0)),
+               eps=float(key("attention.layer_norm_rms_epsilon", 1e-5)), layer_type=lt,
+               emb_type=emb_type, out_type=g.tensors[out_name][1])
+    if any(t != lt for t in wv_types + w2_types):   # per-layer types only where the file mixes them
+        cfg.update(wv_types=wv_types, w2_types=w2_types)
+    return cfg
 
 
 def model_weights(g: GGUFFile, cfg: dict) -> dict:
@@ -296,16 +307,18 @@ def write_model(path, cfg: dict, w: dict, alignment: int = DEFAULT_ALIGNMENT, ar
             f"{arch}.feed_forward_length": ffn, f"{arch}.context_length": cfg["max_seq"],
             f"{arch}.rope.freq_base": float(cfg["rope_base"]),
             f"{arch}.attention.layer_norm_rms_epsilon": float(cfg["eps"]), f"{arch}.vocab_size": V}
-    emb_t = F16 if w["tok_emb"].dtype == np.float16 else F32
+    emb_t = F16 if w["tok_emb"].dtype == np.float16 else F32 if w["tok_emb"].dtype == np.float32 \
+        else cfg["emb_type"]   # GGUF blocks (uint8)
     t = {"token_embd.weight": (emb_t, (dim, V), w["tok_emb"]),
          "output_norm.weight": (F32, (dim,), w["final_norm"]),
          "output.weight": (ot, (dim, V), w["output"])}
     shapes = {"wq": (dim, nh * hd), "wk": (dim, nkv * hd), "wv": (dim, nkv * hd), "wo": (nh * hd, dim),
               "w1": (dim, ffn), "w2": (ffn, dim), "w3": (dim, ffn)}
-    for l, L in enumerate(w["layers"]):
+    from .model import layer_types
+    for l, (L, (tv, t2)) in enumerate(zip(w["layers"], layer_types(cfg))):
         for k, n in LAYER_TENSORS.items():
             if k in ("attn_norm", "ffn_norm"):
                 t[f"blk.{l}.{n}.weight"] = (F32, (dim,), L[k])
             else:
-                t[f"blk.{l}.{n}.weight"] = (lt, shapes[k], L[k])
+                t[f"blk.{l}.{n}.weight"] = ({"wv": tv, "w2": t2}.get(k, lt), shapes[k], L[k])
     write(path, meta, t, alignment)

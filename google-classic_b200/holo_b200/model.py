@@ -13,6 +13,16 @@ import numpy as np
 from . import load, ACT_Q8, HOLO_OK, COMM_HANDLE_BYTES
 
 
+def layer_types(cfg: dict):
+    """(wv type, w2 type) of every layer: cfg's per-layer lists wv_types /
+    w2_types, else wv_type / w2_type, else layer_type (the reference binds
+    these two per layer, src/ai/llm.c:445-507)."""
+    lt, n = cfg["layer_type"], cfg["n_layers"]
+    wv = cfg.get("wv_types") or [cfg.get("wv_type", lt)] * n
+    w2 = cfg.get("w2_types") or [cfg.get("w2_type", lt)] * n
+    return list(zip(wv, w2))
+
+
 class ModelDesc(C.Structure):
     _fields_ = [("n_layers", C.c_int), ("dim", C.c_int), ("n_heads", C.c_int), ("n_kv_heads", C.c_int),
                 ("head_dim", C.c_int), ("ffn_dim", C.c_int), ("vocab", C.c_int), ("max_seq", C.c_int),
@@ -58,8 +68,19 @@ class Model:
             self.lib.cuda_clear_status()
             raise RuntimeError(f"{what}: status {st} ({msg})")
 
+    def set_layer_types(self, layer: int, wv_type: int, w2_type: int):
+        """GGUF types of one layer's wv and w2 (holo_model_set_layer_types),
+        before that layer's weights are set."""
+        rc = self.lib.holo_model_set_layer_types(self.h, int(layer), int(wv_type), int(w2_type))
+        self._check(f"holo_model_set_layer_types {layer}", rc == HOLO_OK)
+
     def set_weights(self, w: dict):
-        """w: the host arrays of synth.llama_weights (GGUF blocks, fp32 norms)."""
+        """w: the host arrays of synth.llama_weights (GGUF blocks, fp32 norms).
+        Per-layer wv / w2 types come from the config (layer_types)."""
+        lt = self.cfg["layer_type"]
+        for l, (tv, t2) in enumerate(layer_types(self.cfg)):
+            if tv != lt or t2 != lt:
+                self.set_layer_types(l, tv, t2)
         for l, L in enumerate(w["layers"]):
             rc = self.lib.holo_model_set_layer(self.h, l, _ptr(L["attn_norm"]), _ptr(L["wq"]), _ptr(L["wk"]),
                                                _ptr(L["wv"]), _ptr(L["wo"]), _ptr(L["ffn_norm"]), _ptr(L["w1"]),

@@ -90,16 +90,29 @@ void cuda_matvec(float *dst, const void *M, const float *v, int out_dim, int in_
  * No counterpart in the reference.  dst = M . v like cuda_matvec (no residual)
  * for a tiled weight M from cuda_upload_quant, but its split-K scratch is
  * static device memory (file-scope arrays found with cudaGetSymbolAddress),
- * so the call allocates and frees nothing: for callers that must not touch
- * the allocator after set-up.  Limits: out_dim <= 262144 (8192 row-blocks);
- * the grid is capped at 296 CTAs.  Runs on the thread's cuda_set_stream
- * stream, else the library stream if the device is initialised, else the
- * legacy default stream.  Every call clears the counters it uses first.
- * The scratch is shared by all calls on a device: overlapping calls (other
- * streams or threads) race.  Returns 0, or the error code it also records
- * (HOLO_E_ARG, HOLO_E_UNSUPPORTED for the row limit, a CUDA error). */
+ * so the call allocates and frees nothing.  It is for callers that cannot
+ * allocate device memory once they are running: a host engine whose memory
+ * budget is fixed and fully handed out at start-up (another allocator, such
+ * as a framework's caching pool, owns the rest of the device), or a latency
+ * loop where cudaMalloc/cudaFree would synchronise the device mid-token.
+ * The caller still owns dst, M and v.  Limits: out_dim <= 262144 (8192
+ * row-blocks; larger shapes are rejected with HOLO_E_UNSUPPORTED); the grid
+ * is capped at 296 CTAs.  The static scratch (about 44 KB) is held by every
+ * GPU that loads the library, until the process exits.
+ * The first call on a device does the set-up (symbol addresses, status word
+ * cleared), so make that first call before any stream capture.  Runs on the
+ * thread's cuda_set_stream stream, else the library stream if the device is
+ * initialised, else the legacy default stream.  Every call clears the
+ * counters it uses first.  The scratch is shared by all calls on a device:
+ * calls that overlap on the GPU (other streams or threads) race.  Returns 0,
+ * or the error code it also records (HOLO_E_ARG, HOLO_E_UNSUPPORTED, a CUDA
+ * error).  A launch whose bounded wait gave up leaves HOLO_E_TIMEOUT in the
+ * path's status word: cuda_last_status reports it, cuda_clear_status resets it. */
 int cuda_matvec_noalloc(float *dst, const void *M, const float *v, int out_dim, int in_dim,
                         int ggml_type, int act_mode);
+/* Device address of that status word on the current device (doing the
+ * set-up if needed; NULL if it failed).  For diagnostics and tests. */
+void *cuda_matvec_noalloc_status_word(void);
 
 /* ---- parity probes (run the device decode code on their own) ------------- */
 /* dst[rows][cols] = dequantized values of M (raw or tiled). */
@@ -116,6 +129,14 @@ void cuda_block_sums_q8(int32_t *dst, const void *M, const float *v, int ggml_ty
  * (created by cuda_init).  cuda_get_stream returns it as a cudaStream_t;
  * cuda_set_stream(NULL) restores the library's own stream. */
 void *cuda_get_stream(void);
+/* Stream-ordered copies on that stream (the reference's cuda_memcpy_h2d/d2h
+ * wait for the copy; these return at once): a batch of host inputs, the
+ * kernels that read them and the copy of their results back can be enqueued
+ * (or captured into one CUDA graph) and waited for once with cuda_sync().
+ * The host buffer must stay valid until then; with pinned host memory the
+ * copies overlap nothing else of the host. */
+void cuda_memcpy_h2d_stream(void *dst, const void *src, size_t size);
+void cuda_memcpy_d2h_stream(void *dst, const void *src, size_t size);
 void cuda_set_stream(void *stream);
 /* Select device `local_rank` for this thread and initialise it (one process
  * or thread per GPU); cuda_init() is cuda_init_rank(0, 1). */
@@ -138,7 +159,9 @@ typedef struct {
     float rope_base;     /* RoPE frequency base (llm_config_t.rope_freq_base) */
     float eps;           /* RMSNorm epsilon */
     int layer_type;      /* GGUF type of wq wk wv wo w1 w2 w3: 8 Q8_0, 2 Q4_0, 12 Q4_K */
-    int emb_type;        /* token embeddings: 0 F32, 1 F16 */
+    int emb_type;        /* token embedding table: 0 F32, 1 F16, or GGUF blocks of Q8_0 (8),
+                          * Q4_0 (2), Q4_K (12), Q6_K (14), dequantized once by
+                          * holo_model_set_globals as get_embedding decodes them */
     int out_type;        /* GGUF type of the output (lm_head) matrix */
     int kv_f16;          /* 1: fp16 KV cache, 0: fp32 (the reference's) */
     int act_mode;        /* HOLO_ACT_Q8 or HOLO_ACT_F32 for every matvec */
@@ -163,7 +186,16 @@ typedef struct {         /* llm_sampler_t (src/ai/llm.h:167-174) without the see
 /* NULL on failure (status set).  head_dim 64/128/256, ffn_dim % 16 == 0. */
 void *holo_model_create(const holo_model_desc *desc);
 /* Layer weights: attn_norm/ffn_norm fp32 [dim]; wq [n_heads*hd][dim], wk wv
- * [n_kv_heads*hd][dim], wo [dim][n_heads*hd], w1 w3 [ffn][dim], w2 [dim][ffn]. */
+ * [n_kv_heads*hd][dim], wo [dim][n_heads*hd], w1 w3 [ffn][dim], w2 [dim][ffn];
+ * GGUF blocks of layer_type, wv and w2 of the layer's types (below). */
+/* GGUF types of one layer's wv and w2 (Q8_0, Q4_0, Q4_K or Q6_K; default
+ * layer_type), set before that layer's holo_model_set_layer.  The reference
+ * binds these two per layer (src/ai/llm.c:445-507: Q4_K_M files keep some
+ * layers' attn_v / ffn_down in Q6_K) and dispatches each matmul on the
+ * tensor's type (llm_cuda.c:140-163).  A model whose layers mix types runs
+ * the one-launch-per-op graph and prompts one position a step; batch 1 on one
+ * GPU only (HOLO_E_UNSUPPORTED otherwise). */
+int holo_model_set_layer_types(void *model, int layer, int wv_type, int w2_type);
 int holo_model_set_layer(void *model, int layer, const float *attn_norm, const void *wq, const void *wk,
                          const void *wv, const void *wo, const float *ffn_norm, const void *w1, const void *w2,
                          const void *w3);
@@ -205,6 +237,13 @@ int holo_model_generate(void *model, const int *prompt, int n_prompt, int n_new,
 /* Replays n more steps of the last holo_model_generate's graph without
  * synchronising (for timing); the sampled tokens past n_new are discarded. */
 int holo_model_launch_steps(void *model, int n_steps);
+/* Diagnostics: a working vector of the last layer of the one-launch-per-op
+ * graph (HOLO_STEP=graph, or head_dim 64/256) after a forward, copied to the
+ * host: 0 x (residual stream, dim), 1 q|k|v (q rotated, k before rotation,
+ * q_dim + 2*kv_dim), 2 attention output, 3 SwiGLU output (ffn_dim), 4 logits.
+ * Returns the length, or -1.  The persistent step kernel keeps its vectors
+ * elsewhere; there only the logits (4) are current. */
+int holo_model_debug_vector(void *model, int which, float *dst);
 int holo_model_pos(void *model);
 /* Device time of the last holo_model_generate: prefill (the steps before the
  * first draw) and decode (n_new steps of forward + sample), in ms. */

@@ -90,6 +90,42 @@ void ho_q4k_to_ref_layout(const void *src_block, void *dst_block, int src_layout
 int ho_tokenize(const char *const *vocab, int vocab_size, int bos, int unk, const char *text,
                 int *tokens, int max_tokens, int add_bos);
 
+/* ---- end-to-end forward (holo_forward.c) -----------------------------------
+ * llm_forward (src/ai/llm.c:1015-1269) restated for the llama architecture,
+ * one position per call, with the device engine's activation mode (HO_ACT_F32:
+ * matmul_q's arithmetic; HO_ACT_Q8: Q8 activations and integer block dots)
+ * and KV cache precision (kv_f16: binary16, nearest even).  Weights are raw
+ * GGUF blocks read in place; norms are fp32. */
+#define HO_ACT_F32 0
+#define HO_ACT_Q8  1
+struct ho_fwd_model;
+struct ho_fwd_model *ho_fwd_create(int n_layers, int dim, int n_heads, int n_kv_heads, int head_dim,
+                                   int ffn_dim, int vocab, int max_seq, float rope_base, float eps,
+                                   int act_mode, int kv_f16, int nthreads);
+/* weight types per tensor role (llm.c:335-342): wq/wk/wo/w1/w3, wv, w2,
+ * token embeddings, output matrix */
+void ho_fwd_set_types(struct ho_fwd_model *m, int layer_type, int wv_type, int w2_type, int emb_type,
+                      int out_type);
+/* one layer's wv / w2 types (per tensor, llm.c:445-507); default the model's */
+void ho_fwd_set_layer_types(struct ho_fwd_model *m, int l, int wv_type, int w2_type);
+void ho_fwd_set_layer(struct ho_fwd_model *m, int l, const float *attn_norm, const void *wq, const void *wk,
+                      const void *wv, const void *wo, const float *ffn_norm, const void *w1, const void *w2,
+                      const void *w3);
+void ho_fwd_set_globals(struct ho_fwd_model *m, const void *tok_emb, const float *final_norm, const void *output);
+/* one position (the next one); 0, or -1 for a bad token or a full cache */
+int ho_fwd_forward(struct ho_fwd_model *m, int token);
+const float *ho_fwd_logits(const struct ho_fwd_model *m);
+int ho_fwd_pos(const struct ho_fwd_model *m);
+void ho_fwd_reset(struct ho_fwd_model *m);
+/* diagnostics: in HO_ACT_Q8, the matmuls of the roles whose bit is set keep
+ * fp32 activations (bits 0..7: q, k, v, o, w1, w3, w2, output) */
+void ho_fwd_set_f32_roles(struct ho_fwd_model *m, unsigned mask);
+/* diagnostics: the last layer's vectors after a forward -- 0 x (residual
+ * stream), 1 q|k|v (q, k rotated), 2 attention output, 3 SwiGLU output,
+ * 4 logits; returns the length */
+int ho_fwd_debug_vector(const struct ho_fwd_model *m, int which, float *dst);
+void ho_fwd_free(struct ho_fwd_model *m);
+
 #ifdef __cplusplus
 }
 #endif

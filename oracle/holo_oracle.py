@@ -109,6 +109,114 @@ def _tok_call(fn, vocab, bos, unk, text, max_tokens, add_bos):
     return np.array(out[:n], np.int32)
 
 
+def layer_types(cfg: dict):
+    """(wv type, w2 type) of every layer: cfg's per-layer lists wv_types /
+    w2_types, else wv_type / w2_type, else layer_type."""
+    lt, n = cfg["layer_type"], cfg["n_layers"]
+    wv = cfg.get("wv_types") or [cfg.get("wv_type", lt)] * n
+    w2 = cfg.get("w2_types") or [cfg.get("w2_type", lt)] * n
+    return list(zip(wv, w2))
+
+
+class ForwardModel:
+    """llm_forward restated (holo_forward.c, ho_fwd_*): one position per
+    forward() call, in the device engine's activation mode (HOLO_ACT_F32 = 0,
+    HOLO_ACT_Q8 = 1, as include/holo_b200.h numbers them) and KV precision.  `w` holds the host arrays of
+    holo_b200.synth.llama_weights (or synthetic_model(keep_host=True)); they
+    are kept alive here because the restatement reads them in place.
+    cfg may carry wv_type / w2_type (per-tensor types, llm.c:335-342)."""
+
+    def __init__(self, cfg: dict, w: dict, act_mode: int, kv_f16: bool, threads: int = 1):
+        lib = Oracle().lib
+        lib.ho_fwd_create.restype = _vp
+        lib.ho_fwd_create.argtypes = [_i] * 8 + [_f, _f, _i, _i, _i]
+        lib.ho_fwd_set_types.argtypes = [_vp] + [_i] * 5
+        lib.ho_fwd_set_layer.argtypes = [_vp, _i] + [_vp] * 9
+        lib.ho_fwd_set_layer_types.argtypes = [_vp, _i, _i, _i]
+        lib.ho_fwd_set_globals.argtypes = [_vp, _vp, _vp, _vp]
+        lib.ho_fwd_forward.restype = _i
+        lib.ho_fwd_forward.argtypes = [_vp, _i]
+        lib.ho_fwd_logits.restype = C.POINTER(C.c_float)
+        lib.ho_fwd_logits.argtypes = [_vp]
+        lib.ho_fwd_reset.argtypes = [_vp]
+        lib.ho_fwd_free.argtypes = [_vp]
+        self.lib, self.cfg, self.w = lib, dict(cfg), w
+        self.h = lib.ho_fwd_create(cfg["n_layers"], cfg["dim"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"],
+                                   cfg["ffn_dim"], cfg["vocab"], cfg["max_seq"], cfg.get("rope_base", 10000.0),
+                                   cfg.get("eps", 1e-5), int(act_mode), int(bool(kv_f16)), int(threads))
+        if not self.h:
+            raise MemoryError("ho_fwd_create")
+        lt = cfg["layer_type"]
+        lib.ho_fwd_set_types(self.h, lt, cfg.get("wv_type", lt), cfg.get("w2_type", lt), cfg.get("emb_type", 1),
+                             cfg["out_type"])
+        for l, (tv, t2) in enumerate(layer_types(cfg)):
+            lib.ho_fwd_set_layer_types(self.h, l, tv, t2)
+        for l, L in enumerate(w["layers"]):
+            lib.ho_fwd_set_layer(self.h, l, _ptr(L["attn_norm"]), _ptr(L["wq"]), _ptr(L["wk"]), _ptr(L["wv"]),
+                                 _ptr(L["wo"]), _ptr(L["ffn_norm"]), _ptr(L["w1"]), _ptr(L["w2"]), _ptr(L["w3"]))
+        lib.ho_fwd_set_globals(self.h, _ptr(w["tok_emb"]), _ptr(w["final_norm"]), _ptr(w["output"]))
+
+    def forward(self, token: int) -> np.ndarray:
+        if self.lib.ho_fwd_forward(self.h, int(token)) != 0:
+            raise ValueError(f"ho_fwd_forward({token}): bad token or full cache")
+        return np.ctypeslib.as_array(self.lib.ho_fwd_logits(self.h), shape=(self.cfg["vocab"],)).copy()
+
+    def reset(self):
+        self.lib.ho_fwd_reset(self.h)
+
+    def close(self):
+        if self.h:
+            self.lib.ho_fwd_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def greedy_stream(fwd, ref_model, prompt, n_new: int, penalty: float, last_n: int, margins=None, logits_out=None):
+    """llm_generate's loop (src/ai/llm.c:1340-1420) at temperature 0 with the
+    logits of `fwd` (ForwardModel, or anything with forward/reset) and the
+    reference's own llm_sample (`ref_model`, a RefModel used for its sampler
+    and token history only).  margins collects top-1 minus top-2 of the
+    penalised logits before each pick; logits_out the logits of every
+    position (prompt and generated)."""
+    fwd.reset()
+    ref_model.reset()
+    hist = [int(t) for t in prompt]
+    for t in prompt:
+        ref_model.push(t)
+    for t in prompt:
+        logits = fwd.forward(t)
+        if logits_out is not None:
+            logits_out.append(logits)
+    out = []
+    for _ in range(n_new):
+        ref_model.set_logits(logits)
+        if margins is not None:
+            margins.append(penalised_margin(logits, hist[-last_n:] if last_n > 0 else [], penalty))
+        tok = ref_model.sample(0.0, 0.95, 40, penalty, last_n)
+        out.append(tok)
+        hist.append(tok)
+        ref_model.push(tok)
+        logits = fwd.forward(tok)
+        if logits_out is not None:
+            logits_out.append(logits)
+    return np.array(out, np.int32)
+
+
+def penalised_margin(logits, hist, penalty):
+    """top-1 minus top-2 of the logits after the repetition penalty of
+    tensor.c:654-667 over the history tokens `hist` (a diagnostic)."""
+    lg = np.asarray(logits, np.float32).copy()
+    for t in hist:
+        lg[t] = lg[t] / np.float32(penalty) if lg[t] > 0 else lg[t] * np.float32(penalty)
+    top2 = np.sort(lg)[-2:]
+    return float(top2[1] - top2[0])
+
+
 class Reference:
     """The reference engine's own CPU functions (src/ai/*.c built from source)."""
 
@@ -139,6 +247,8 @@ class Reference:
         lib.href_model_create.restype = _vp
         lib.href_model_create.argtypes = [_i, _i, _i, _i, _i, _i, _i, _i, _f, _f]
         lib.href_model_set_types.argtypes = [_vp, _i, _i, _i]
+        lib.href_model_set_types_mixed.argtypes = [_vp, _i, _i, _i, _i, _i]
+        lib.href_model_set_layer_types.argtypes = [_vp, _i, _i, _i]
         lib.href_model_set_layer.argtypes = [_vp, _i] + [_vp] * 9
         lib.href_model_set_globals.argtypes = [_vp, _vp, _vp, _vp]
         lib.href_forward.restype = _i
@@ -221,7 +331,11 @@ class RefModel:
         self.h = self.lib.href_model_create(cfg["n_layers"], cfg["dim"], cfg["n_heads"], cfg["n_kv_heads"],
                                             cfg["head_dim"], cfg["ffn_dim"], cfg["vocab"], cfg["max_seq"],
                                             cfg.get("rope_base", 10000.0), cfg.get("eps", 1e-5))
-        self.lib.href_model_set_types(self.h, cfg["layer_type"], cfg.get("emb_type", 1), cfg["out_type"])
+        lt = cfg["layer_type"]
+        self.lib.href_model_set_types_mixed(self.h, lt, cfg.get("wv_type", lt), cfg.get("w2_type", lt),
+                                            cfg.get("emb_type", 1), cfg["out_type"])
+        for l, (tv, t2) in enumerate(layer_types(cfg)):
+            self.lib.href_model_set_layer_types(self.h, l, tv, t2)
         for l, L in enumerate(w["layers"]):
             self.lib.href_model_set_layer(self.h, l, _ptr(L["attn_norm"]), _ptr(L["wq"]), _ptr(L["wk"]),
                                           _ptr(L["wv"]), _ptr(L["wo"]), _ptr(L["ffn_norm"]), _ptr(L["w1"]),

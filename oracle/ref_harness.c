@@ -105,6 +105,30 @@ void href_model_set_types(href_model_t *m, int layer_type, int emb_type, int out
     }
 }
 
+/* Per-tensor types as llm.c:335-342 binds them for mixed files: wq/wk/wo/w1/w3
+ * share g_weight_type, each layer's wv and w2 carry their own type. */
+void href_model_set_types_mixed(href_model_t *m, int layer_type, int wv_type, int w2_type, int emb_type,
+                                int out_type) {
+    href_model_set_types(m, layer_type, emb_type, out_type);
+    g_v_weight_type = wv_type;
+    g_w2_weight_type = w2_type;
+    for (int l = 0; l < m->ctx.weights.n_layers; l++) {
+        m->ctx.weights.layers[l].wv_type = wv_type;
+        m->ctx.weights.layers[l].w2_type = w2_type;
+    }
+}
+
+/* One layer's wv / w2 types, as load_weights binds them per tensor
+ * (llm.c:445-447, 505-507: the globals follow layer 0). */
+void href_model_set_layer_types(href_model_t *m, int l, int wv_type, int w2_type) {
+    m->ctx.weights.layers[l].wv_type = wv_type;
+    m->ctx.weights.layers[l].w2_type = w2_type;
+    if (l == 0) {
+        g_v_weight_type = wv_type;
+        g_w2_weight_type = w2_type;
+    }
+}
+
 void href_model_set_layer(href_model_t *m, int l, void *attn_norm, void *wq, void *wk,
                           void *wv, void *wo, void *ffn_norm, void *w1, void *w2, void *w3) {
     typeof(m->ctx.weights.layers[0]) *L = &m->ctx.weights.layers[l];

@@ -53,3 +53,40 @@ def rel_err(y, r):
     y = np.asarray(y, np.float64)
     r = np.asarray(r, np.float64)
     return float(np.abs(y - r).max() / max(np.abs(r).max(), 1e-30))
+
+
+def typed_weights(cfg, seed):
+    """synth.llama_weights for cfg, with every matrix in the type cfg gives it:
+    per-layer wv / w2 types (holo_b200.model.layer_types), Q6_K anywhere
+    (seeded random blocks, synth.quant_matrix: there is no Q6_K quantizer
+    here), and a quantized token-embedding table when emb_type is a block
+    type.  Other roles: N(0, 0.02) quantized round-to-nearest."""
+    from holo_b200 import synth
+    from holo_b200.model import layer_types
+    carrier = dict(cfg, emb_type=1 if cfg.get("emb_type", 1) == 1 else 0)
+    for k in ("layer_type", "out_type"):
+        if carrier[k] == hb.Q6_K:
+            carrier[k] = hb.Q4_K
+    w = synth.llama_weights(carrier, seed)
+    rng = np.random.default_rng(seed + 1)
+
+    def mat(t, rows, cols, s):
+        if t == hb.Q6_K:
+            return synth.quant_matrix(t, rows, cols, s)
+        return synth.quantize(rng.normal(0, 0.02, (rows, cols)).astype(np.float32), t)
+
+    dim, ffn, V = cfg["dim"], cfg["ffn_dim"], cfg["vocab"]
+    q_dim, kv_dim = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
+    lt = cfg["layer_type"]
+    for l, (L, (tv, t2)) in enumerate(zip(w["layers"], layer_types(cfg))):
+        shapes = {"wq": (q_dim, dim, lt), "wk": (kv_dim, dim, lt), "wv": (kv_dim, dim, tv),
+                  "wo": (dim, q_dim, lt), "w1": (ffn, dim, lt), "w2": (dim, ffn, t2), "w3": (ffn, dim, lt)}
+        for i, (name, (r, c, t)) in enumerate(shapes.items()):
+            if t != carrier["layer_type"]:
+                L[name] = mat(t, r, c, seed * 100 + l * 10 + i)
+    if cfg["out_type"] != carrier["out_type"]:
+        w["output"] = mat(cfg["out_type"], V, dim, seed * 100 + 99)
+    et = cfg.get("emb_type", 1)
+    if et not in (0, 1):
+        w["tok_emb"] = mat(et, V, dim, seed * 100 + 98)
+    return w

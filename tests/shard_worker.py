@@ -10,8 +10,9 @@ host: every rank computes its row shard through the library (holo_model_shard)
       received every handle in rank order.
 gpu:  every rank builds its shard of the test model (cfg_for(N)), connects the peers and
       runs the decode calls (generate's prompt and one holo_model_prefill in
-      sharded row passes); rank 0 writes the logits and token streams to
-      OUT_DIR/gpu.npz for the parent test to compare with the reference.
+      sharded row passes), then a 32-head model (CFG_SPLIT) over a 176-position
+      stream; rank 0 writes the logits and token streams to OUT_DIR/gpu.npz
+      for the parent test to compare with the reference and one GPU.
 timeout: failure detection without a fault: both ranks connect, then rank 1
       stays alive but skips the step; rank 0's step waits for rank 1's slices,
       gives up after its bound and reports HOLO_E_TIMEOUT; rank 0 then clears
@@ -38,12 +39,24 @@ CFG = dict(n_layers=2, dim=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn_dim=7
            rope_base=10000.0, eps=1e-5, layer_type=hb.Q4_K, emb_type=1, out_type=hb.Q8_0)
 # four KV heads, for four ranks (one KV head and its GQA pair of query heads each)
 CFG4 = dict(CFG, dim=1024, n_heads=8, n_kv_heads=4, ffn_dim=1536)
+# eight KV heads, for eight ranks (one query and one KV head each)
+CFG8 = dict(CFG4, n_kv_heads=8)
+# the 7B's 32 heads of 128 (8 KV heads): a head's positions are cut into
+# several attention splits once the stream is long, and the cut must not
+# depend on the world size
+CFG_SPLIT = dict(n_layers=2, dim=4096, n_heads=32, n_kv_heads=8, head_dim=128, ffn_dim=1024, vocab=1024,
+                 max_seq=192, rope_base=10000.0, eps=1e-5, layer_type=hb.Q4_K, emb_type=1, out_type=hb.Q8_0)
 PROMPT_SEED, N_PROMPT, N_GREEDY, N_SAMPLED, N_ROWS = 21, 24, 48, 32, 20
+SPLIT_SEED, N_SPLIT_PROMPT, N_SPLIT_GREEDY = 12, 16, 160
 
 
 def cfg_for(world):
-    """the gpu-mode model for a world size: CFG on two ranks, CFG4 on four"""
-    return CFG if world <= 2 else CFG4
+    """the gpu-mode model for a world size: CFG on two ranks, CFG4 on four, CFG8 on eight"""
+    return CFG if world <= 2 else CFG4 if world <= 4 else CFG8
+
+
+def split_prompt():
+    return np.random.default_rng(SPLIT_SEED).integers(0, CFG_SPLIT["vocab"], size=N_SPLIT_PROMPT).astype(np.int32)
 
 
 class StandInModel:
@@ -120,6 +133,16 @@ def run_gpu(rank, world, out):
                 res["q8_rows_logits"] = np.stack([m.forward(t) for t in prompt[N_ROWS:]])
             dist.barrier()
             m.close()
+        # 32 heads, a 176-position stream: several attention splits a head
+        from holo_b200.model import synthetic_model
+        m = synthetic_model(CFG_SPLIT, seed=SPLIT_SEED, act_mode=hb.ACT_Q8, kv_f16=True, world=world, rank=rank)
+        connect_peers(m)
+        sp = split_prompt()
+        res["split_greedy"] = m.generate(sp, N_SPLIT_GREEDY, SamplerDesc(0.0, 0.95, 40, 1.1, 64), seed=5)
+        m.reset()
+        res["split_logits"] = np.stack([m.forward(t) for t in np.concatenate([sp, res["split_greedy"]])])
+        dist.barrier()
+        m.close()
         # every rank computed the same logits and tokens
         for k in sorted(res):
             every = [None] * world

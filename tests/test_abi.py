@@ -6,7 +6,6 @@ types; the reference's own GPU host code links against the library.  CPU only
 import ctypes
 import os
 import pathlib
-import re
 import subprocess
 
 import pytest
@@ -84,9 +83,10 @@ def test_reference_gpu_host_code_links_against_library():
 
 def reference_header():
     """include/cuda_ops.h of the reference tree that oracle/Makefile builds
-    from (its REF variable, or REF in the environment)."""
-    m = re.search(r"^REF\s*\?=\s*(\S+)", (ROOT / "oracle" / "Makefile").read_text(), re.M)
-    return pathlib.Path(os.environ.get("REF", m.group(1))) / "include" / "cuda_ops.h"
+    from: REF or HOLO_REFERENCE_DIR in the environment, else the checkout
+    beside this repository (the Makefile's default)."""
+    ref = os.environ.get("REF") or os.environ.get("HOLO_REFERENCE_DIR") or str(ROOT.parent / "reference")
+    return pathlib.Path(ref) / "include" / "cuda_ops.h"
 
 
 def compile_both(ours, tmp_path):

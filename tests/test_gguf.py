@@ -100,8 +100,16 @@ def test_tied_output_and_mixed_types(tmp_path, weights):
         assert c["out_type"] == hb.F16 and c["head_dim"] == 64 and c["rope_base"] == 10000.0
         w = gguf.model_weights(g, c)
         assert np.array_equal(w["output"], weights["tok_emb"])
-    # one layer matrix of another type: rejected (the engine takes one layer type)
+    # a layer's ffn_down (or attn_v) of another type: per-layer types, as the
+    # reference binds them (llm.c:445-507)
     t["blk.1.ffn_down.weight"] = (hb.Q8_0, (512, 256), synth.quant_matrix(hb.Q8_0, 256, 512, 1))
+    gguf.write(path, meta, t)
+    with gguf.GGUFFile(path) as g:
+        c = gguf.model_config(g)
+        assert c["w2_types"] == [hb.Q4_K, hb.Q8_0] and c["wv_types"] == [hb.Q4_K, hb.Q4_K]
+    # one of the five matrices that share the reference's g_weight_type in
+    # another type: rejected (llm_forward would read it as g_weight_type)
+    t["blk.1.ffn_up.weight"] = (hb.Q8_0, (256, 512), synth.quant_matrix(hb.Q8_0, 512, 256, 2))
     gguf.write(path, meta, t)
     with gguf.GGUFFile(path) as g, pytest.raises(ValueError, match="several types"):
         gguf.model_config(g)
