@@ -5,7 +5,10 @@ Workload: the quantized matvec sweep over the
 Llama-7B FFN shapes -- Q4_0 and Q4_K, 11008x4096 (up/gate) and 4096x11008
 (down), seeds 0-3: 16 distinct matrices, 406 MB of GGUF blocks per pass, so
 every pass streams more than the 126 MB L2 and no matrix is re-read from L2.
-One step = one pass of the 16 matvecs (replayed as one CUDA graph).
+One step = one pass of the 16 matvecs: the 16 independent matvecs in one
+cuda_matvec_batch call (one persistent launch per weight type), replayed as
+a CUDA graph; the same pass as 16 separate cuda_matvec calls is reported
+beside it (per_call_chain).
 
 Metric: quant matvec HBM GB/s = algorithmic bytes (GGUF weight bytes + fp32
 x + fp32 y) / time.  With --gpus N every rank runs the sweep on its own GPU
@@ -146,14 +149,25 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.ExternalStream(lib.cuda_get_stream())
     lib.cuda_set_pdl(0 if args.no_pdl else 1)   # weights are constant from here on
 
-    def capture(act):
-        for m in mats:   # one-time set-up outside capture
-            lib.cuda_matvec(m["yd"], m["Wd"], m["xd"], m["rows"], m["cols"], m["gt"], act, None)
+    import ctypes as C
+    n_m = len(mats)
+    b_dst = (C.c_void_p * n_m)(*[m["yd"] for m in mats])
+    b_w = (C.c_void_p * n_m)(*[m["Wd"] for m in mats])
+    b_x = (C.c_void_p * n_m)(*[m["xd"] for m in mats])
+
+    def enqueue(act, batched):
+        if batched:   # the 16 independent matvecs in one cuda_matvec_batch call (a launch per type)
+            lib.cuda_matvec_batch(n_m, b_dst, b_w, b_x, act)
+        else:         # one cuda_matvec call a matrix
+            for m in mats:
+                lib.cuda_matvec(m["yd"], m["Wd"], m["xd"], m["rows"], m["cols"], m["gt"], act, None)
+
+    def capture(act, batched=True):
+        enqueue(act, batched)   # one-time set-up outside capture
         dev.sync()
         if lib.cuda_capture_begin() != 0:
             dev.check("capture")
-        for m in mats:
-            lib.cuda_matvec(m["yd"], m["Wd"], m["xd"], m["rows"], m["cols"], m["gt"], act, None)
+        enqueue(act, batched)
         g = lib.cuda_capture_end()
         dev.check("capture end")
         return g
@@ -201,57 +215,82 @@ def run_ours(args, rank, world, local_rank):
     g_other = capture(acts[other])
     ms_other = timed(g_other, max(1, args.steps // 4), max(3, args.warmup // 2)) / max(1, args.steps // 4)
     lib.cuda_graph_free(g_other)
+    # the same sweep as 16 dependent-order calls (one cuda_matvec a matrix,
+    # PDL between them): what a caller issuing one matvec at a time gets
+    g_chain = capture(primary, batched=False)
+    chain_steps = max(1, args.steps // 4)
+    ms_chain = timed(g_chain, chain_steps, max(3, args.warmup // 2)) / chain_steps
+    lib.cuda_graph_free(g_chain)
 
-    # Roofline of the dominant kernel (the tiled matvec, every launch of the
-    # step): its average launch duration over the timed region = the timed
-    # region's device time / launches (CUDA events on the library stream, the
-    # launches overlapping as in the step); beside it, the duration of an
-    # isolated launch (event pair around one launch, nothing to overlap with).
-    launches_per_step = len(mats)
+    # Roofline of the dominant kernel (the batched matvec, one launch per
+    # weight type: Q4_0 and Q4_K, 8 matrices each): its average launch
+    # duration over the timed region = the timed region's device time /
+    # launches (CUDA events on the library stream); beside it, the duration
+    # of an isolated call (event pair around one cuda_matvec_batch, nothing
+    # to overlap with).
+    launches_per_step = len({m["gt"] for m in mats})
     region_us_per_launch = 1e3 * ms_step / launches_per_step
     kt = []
-    for _ in range(3):
-        for m in mats:
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            lib.cuda_matvec(m["yd"], m["Wd"], m["xd"], m["rows"], m["cols"], m["gt"], primary, None)
-            b.record(stream)
-            kt.append((a, b, algo_bytes(m["gt"], m["rows"], m["cols"])))
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        enqueue(primary, True)
+        b.record(stream)
+        kt.append((a, b))
     torch.cuda.synchronize()
-    k_ms = [a.elapsed_time(b) for a, b, _ in kt]
-    k_bytes = [nb for _, _, nb in kt]
+    k_ms = [a.elapsed_time(b) for a, b in kt]
     peak, peak_kind = peaks()
-    isolated_gbs = sum(k_bytes) / (sum(k_ms) * 1e-3) / 1e9
+    isolated_gbs = bytes_step / (statistics.median(k_ms) * 1e-3) / 1e9
     kernel_gbs = (bytes_step / launches_per_step) / (region_us_per_launch * 1e-6) / 1e9
 
-    # end to end through the reference-facing C ABI: pinned host x in, host y
-    # out, every step (cuda_memcpy_h2d, cuda_matmul_q4_*, cuda_memcpy_d2h)
+    # End to end through the C ABI, host buffers in and out, every step: the
+    # 16 activations from pinned host memory (one cuda_memcpy_h2d_stream), the
+    # 16 matvecs (cuda_matmul_q4_0 / cuda_matmul_q4_k), the 16 results back to
+    # pinned host memory (one cuda_memcpy_d2h_stream) -- enqueued once into a
+    # CUDA graph with cuda_capture_begin/end -- then cuda_graph_launch and
+    # cuda_sync() to wait for the host results.  Wall clock, max over ranks.
     lib.cuda_set_act_mode(primary)
-    pins = []
-    for m in mats:
-        hx = torch.from_numpy(m["x"]).pin_memory()
-        hy = torch.empty(m["rows"], dtype=torch.float32).pin_memory()
-        pins.append((hx, hy))
     fn = {hb.Q4_0: lib.cuda_matmul_q4_0, hb.Q4_K: lib.cuda_matmul_q4_k}
-    e2e_steps = max(3, min(args.steps, 200))
     h2d = sum(4 * m["cols"] for m in mats)
     d2h = sum(4 * m["rows"] for m in mats)
+    hx_all = torch.from_numpy(np.concatenate([m["x"] for m in mats])).pin_memory()
+    hy_all = torch.zeros(d2h // 4, dtype=torch.float32).pin_memory()
+    dx_all, dy_all = dev.alloc(h2d), dev.alloc(d2h)
+    offs_x, offs_y, ox, oy = [], [], 0, 0
+    for m in mats:
+        offs_x.append(ox)
+        offs_y.append(oy)
+        ox += 4 * m["cols"]
+        oy += 4 * m["rows"]
 
-    def e2e_step():
-        for m, (hx, hy) in zip(mats, pins):
-            lib.cuda_memcpy_h2d(m["xd"], hx.data_ptr(), 4 * m["cols"])
-            fn[m["gt"]](m["yd"], m["Wd"], m["xd"], m["rows"], m["cols"])
-            lib.cuda_memcpy_d2h(hy.data_ptr(), m["yd"], 4 * m["rows"])
+    e_dst = (C.c_void_p * n_m)(*[dy_all + yo for yo in offs_y])
+    e_x = (C.c_void_p * n_m)(*[dx_all + xo for xo in offs_x])
 
-    for _ in range(3):
-        e2e_step()
+    def e2e_enqueue():
+        lib.cuda_memcpy_h2d_stream(dx_all, hx_all.data_ptr(), h2d)
+        lib.cuda_matvec_batch(n_m, e_dst, b_w, e_x, primary)
+        lib.cuda_memcpy_d2h_stream(hy_all.data_ptr(), dy_all, d2h)
+
+    e2e_enqueue()
+    lib.cuda_sync()
+    if lib.cuda_capture_begin() != 0:
+        dev.check("e2e capture")
+    e2e_enqueue()
+    g_e2e = lib.cuda_capture_end()
+    dev.check("e2e capture end")
+    e2e_steps = max(3, min(args.steps, 2000))
+
+    def e2e_run(n):
+        for _ in range(n):
+            lib.cuda_graph_launch(g_e2e)
+            lib.cuda_sync()
+
+    e2e_run(3)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        e2e_step()
-    torch.cuda.synchronize()
+    e2e_run(e2e_steps)
     e2e_s = time.perf_counter() - t0
     t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
     if world > 1:
@@ -259,7 +298,33 @@ def run_ours(args, rank, world, local_rank):
     e2e_s = float(t.item())
     dev.check("e2e")
     e2e_value = world * bytes_step * e2e_steps / e2e_s / 1e9
-    # the library output of the last e2e step equals the graph's output
+    # the host results equal the device-timed graph's outputs
+    e2e_same = all(np.array_equal(hy_all.numpy()[yo // 4: yo // 4 + m["rows"]], dev.download(m["yd"], (m["rows"],),
+                                                                                            np.float32))
+                   for m, yo in zip(mats, offs_y))
+
+    # the same through the reference's own call pattern: per matvec a
+    # synchronous cuda_memcpy_h2d, cuda_matmul_*, synchronous cuda_memcpy_d2h
+    def sync_calls_step():
+        for m, xo, yo in zip(mats, offs_x, offs_y):
+            lib.cuda_memcpy_h2d(m["xd"], hx_all.data_ptr() + xo, 4 * m["cols"])
+            fn[m["gt"]](m["yd"], m["Wd"], m["xd"], m["rows"], m["cols"])
+            lib.cuda_memcpy_d2h(hy_all.data_ptr() + yo, m["yd"], 4 * m["rows"])
+
+    sync_steps = max(3, min(args.steps, 200))
+    for _ in range(3):
+        sync_calls_step()
+    t0 = time.perf_counter()
+    for _ in range(sync_steps):
+        sync_calls_step()
+    sync_s = time.perf_counter() - t0
+    t = torch.tensor([sync_s], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    sync_value = world * bytes_step * sync_steps / float(t.item()) / 1e9
+    lib.cuda_graph_free(g_e2e)
+    dev.free(dx_all)
+    dev.free(dy_all)
     lib.cuda_set_act_mode(hb.ACT_Q8)
 
     # the reference's own CUDA kernels (src/ai/cuda_ops.cu built for sm_100a) on
@@ -276,11 +341,19 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(mats, bytes_step, budget_s=args.cpu_budget)
 
-    decode = None
+    decode = decode70 = decode70_b8 = None
     if not args.no_decode:
         decode = decode_bench(args, world, rank, torch)
+    if not args.no_decode and not args.no_70b:
+        # the 70B Q4_0 model, row-sharded over the N GPUs
+        # at batch 1 (every N), and batch 8 on one GPU (N = 1 only)
+        a70 = argparse.Namespace(**dict(vars(args), decode_model="70b", decode_batch=1))
+        decode70 = decode_bench(a70, world, rank, torch)
+        if world == 1:
+            decode70_b8 = decode_bench(argparse.Namespace(**dict(vars(a70), decode_batch=8)), world, rank, torch)
     prefill = prefill_bench(dev, torch) if single and not args.no_prefill else None
     other_types = other_types_bench(dev, torch) if single and not args.no_prefill else None
+    c1 = c1_q8_0_bench(dev, torch) if single and not args.no_prefill else None
 
     traffic = read_traffic()
     line = {
@@ -293,24 +366,42 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(kernel_gbs / peak, 4), "peak_source": peak_kind,
                      "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                     "traffic_source": ("static: ncu dram__bytes of one isolated launch of the same kernel "
+                                        "(profiles/matvec_traffic.txt), not measured in this run") if traffic else None,
                      "algorithmic_bytes_per_launch": round(bytes_step / launches_per_step),
+                     "kernel": "mv_multi_kernel (cuda_matvec_batch), one launch per weight type",
                      "kernel_avg_us": round(region_us_per_launch, 3),
-                     "isolated_launch": {"avg_us": round(1e3 * sum(k_ms) / len(k_ms), 3),
-                                         "achieved": round(isolated_gbs, 1), "frac": round(isolated_gbs / peak, 4)},
+                     "isolated_call": {"us": round(1e3 * statistics.median(k_ms), 3), "launches": launches_per_step,
+                                       "achieved": round(isolated_gbs, 1), "frac": round(isolated_gbs / peak, 4)},
                      "step_frac": round(value / world / peak, 4)},
         "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "path": "cuda_memcpy_h2d + cuda_matmul_q4_0/q4_k + cuda_memcpy_d2h per matvec (reference ABI)"},
-        "gpu_launches": args.steps * len(mats),
+                "steps": e2e_steps, "host_results_equal_device": bool(e2e_same),
+                "path": "C ABI, pinned host buffers: cuda_memcpy_h2d_stream (16 x) + cuda_matvec_batch (16 matvecs) + "
+                        "cuda_memcpy_d2h_stream (16 y) in one CUDA graph (cuda_capture_begin/end), "
+                        "cuda_graph_launch + cuda_sync per step, wall clock",
+                "per_call_sync": {"value": round(sync_value, 3), "unit": UNIT, "steps": sync_steps,
+                                  "path": "per matvec: cuda_memcpy_h2d + cuda_matmul_q4_* + cuda_memcpy_d2h "
+                                          "(the reference's synchronous call pattern)"}},
+        "gpu_launches": args.steps * launches_per_step,
         "clocks": clocks,
         "other_act_mode": {"act": other, "value": round(world * bytes_step / (ms_other * 1e-3) / 1e9, 2),
                            "ms_per_step": round(ms_other, 5)},
+        "per_call_chain": {"value": round(world * bytes_step / (ms_chain * 1e-3) / 1e9, 2), "unit": UNIT,
+                           "ms_per_step": round(ms_chain, 5), "us_per_matvec": round(1e3 * ms_chain / len(mats), 3),
+                           "path": "16 cuda_matvec calls a step (one launch a matrix, PDL), CUDA graph"},
     }
     if decode:
         line["decode"] = decode
+    if decode70:
+        line["decode_70b"] = decode70
+    if decode70_b8:
+        line["decode_70b_batch8"] = decode70_b8
     if prefill:
         line["prefill"] = prefill
     if other_types is not None:
         line["other_types"] = other_types
+    if c1 is not None:
+        line["c1_q8_0"] = c1
     if ref_gpu:
         line["reference_gpu_kernels"] = ref_gpu
     if cpu:
@@ -416,6 +507,9 @@ def decode_bytes_per_token(cfg, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW, kv_byt
 
 # decode workloads: BASELINE configs[3] (7B, Q4_K) and configs[4] (70B, Q4_0,
 # batch 1): model, prompt tokens, new tokens, timed runs
+# the one-GPU greedy stream of the 7B decode model (tests/golden/make_greedy64_7b.py)
+GREEDY64_FIXTURE = ROOT / "tests" / "golden" / "greedy64_7b_q8.json"
+
 DECODE_MODELS = {
     "7b": ("LLAMA2_7B", 128, 256, 3,
            "Llama-2-7B shape, Q4_K layers, Q8_0 lm_head, fp16 embeddings and KV cache, ctx 2048"),
@@ -469,6 +563,15 @@ def decode_bench(args, world, rank, torch):
         dec_ms, pre_ms, wall = max_over_ranks(dec_ms, pre_ms, wall)
         runs.append((dec_ms, pre_ms, wall, toks))
     first_tokens = runs[0][3]      # seed 0
+    greedy = None
+    if args.decode_model == "7b":
+        # 64 greedy steps (the bench's prompt and penalty), against the
+        # committed one-GPU stream: a sharded model is bit-identical to one GPU
+        g64 = m.generate(prompt, 64, SamplerDesc(0.0, 0.95, 40, 1.1, 64), seed=0)
+        fx = GREEDY64_FIXTURE
+        want = json.loads(fx.read_text())["tokens"] if fx.exists() else None
+        greedy = {"equal_1gpu": None if want is None else bool(np.array_equal(g64, np.array(want))),
+                  "head": [int(t) for t in g64[:8]], "fixture": str(fx.relative_to(ROOT))}
     runs.sort(key=lambda r: r[0])
     dec_ms, pre_ms, wall, toks = runs[len(runs) // 2]
     tok_s = n_new / (dec_ms * 1e-3)
@@ -493,6 +596,9 @@ def decode_bench(args, world, rank, torch):
         "model_build_s": round(build_s, 1),
         "tokens_head_seed0": [int(t) for t in first_tokens[:8]],
     }
+    if greedy is not None:
+        out["greedy64_equal_1gpu"] = greedy["equal_1gpu"]
+        out["greedy64"] = greedy
     if want_cpu and host is not None:
         out["cpu_baseline"] = decode_cpu_baseline(cfg, host, prompt, budget_s=args.cpu_budget)
     elif rank == 0 and world == 1 and not args.no_cpu:   # 70B: llm_forward is infeasible on the host
@@ -503,6 +609,93 @@ def decode_bench(args, world, rank, torch):
 
 PREFILL_SHAPES = [(14336, 4096), (4096, 14336)]
 PREFILL_M = [64, 256, 512]
+
+
+def c1_q8_0_bench(dev, torch, iters=20):
+    """BASELINE configs[0]'s shape on the GPU: Q8_0 4096x4096 matvecs (16
+    distinct matrices, 285 MB, larger than L2), Q8 activations: the batched
+    call, one cuda_matvec_q8_0-style call a matrix in a graph, one isolated
+    call, and the reference's own cuda_matmul_q8_0 (src/ai/cuda_ops.cu built
+    for sm_100a) on the raw blocks.  GB/s of algorithmic bytes
+    (17,858,560 a matvec)."""
+    import ctypes as C
+    lib = dev.lib
+    stream = torch.cuda.ExternalStream(lib.cuda_get_stream())
+    hbm, _ = peaks()
+    n, r, c = 16, 4096, 4096
+    Ws = [synth.quant_matrix(hb.Q8_0, r, c, s) for s in range(n)]
+    mats = [dict(W=W, Wd=dev.upload_quant(W, hb.Q8_0, r, c), xd=dev.upload(synth.activation(c, s)),
+                 yd=dev.alloc(4 * r)) for s, W in enumerate(Ws)]
+    nbytes = algo_bytes(hb.Q8_0, r, c)
+    dst = (C.c_void_p * n)(*[m["yd"] for m in mats])
+    Mp = (C.c_void_p * n)(*[m["Wd"] for m in mats])
+    xp = (C.c_void_p * n)(*[m["xd"] for m in mats])
+
+    def graph(fn):
+        fn()
+        dev.sync()
+        lib.cuda_capture_begin()
+        fn()
+        return lib.cuda_capture_end()
+
+    def gtime(g, reps):
+        for _ in range(3):
+            lib.cuda_graph_launch(g)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            lib.cuda_graph_launch(g)
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    out = {"shape": "4096x4096 Q8_0 (BASELINE configs[0]), 16 distinct matrices, Q8 activations"}
+    g = graph(lambda: lib.cuda_matvec_batch(n, dst, Mp, xp, hb.ACT_Q8))
+    ms = gtime(g, iters)
+    lib.cuda_graph_free(g)
+    out["batch"] = {"gbs": round(n * nbytes / (ms * 1e-3) / 1e9, 1), "hbm_frac": round(n * nbytes / (ms * 1e-3) / 1e9 / hbm, 4),
+                    "us_per_matvec": round(1e3 * ms / n, 3)}
+    g = graph(lambda: [lib.cuda_matvec(m["yd"], m["Wd"], m["xd"], r, c, hb.Q8_0, hb.ACT_Q8, None) for m in mats])
+    ms = gtime(g, iters)
+    lib.cuda_graph_free(g)
+    out["per_call_chain"] = {"gbs": round(n * nbytes / (ms * 1e-3) / 1e9, 1), "us_per_matvec": round(1e3 * ms / n, 3)}
+    ts = []
+    for m in mats[:8]:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        lib.cuda_matvec(m["yd"], m["Wd"], m["xd"], r, c, hb.Q8_0, hb.ACT_Q8, None)
+        b.record(stream)
+        ts.append((a, b))
+    torch.cuda.synchronize()
+    us = 1e3 * statistics.median([a.elapsed_time(b) for a, b in ts])
+    out["isolated_call"] = {"us": round(us, 3), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+    so = ROOT / "oracle" / "_ref" / "libholo_ref_cuda.so"
+    if so.exists():
+        ref = C.CDLL(str(so))
+        ref.cuda_matmul_q8_0.argtypes = [C.c_void_p] * 3 + [C.c_int, C.c_int]
+        raws = [dev.upload(m["W"]) for m in mats]
+        dev.sync()
+        for _ in range(2):
+            for m, raw in zip(mats, raws):
+                ref.cuda_matmul_q8_0(m["yd"], raw, m["xd"], r, c)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(5):
+            for m, raw in zip(mats, raws):
+                ref.cuda_matmul_q8_0(m["yd"], raw, m["xd"], r, c)
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / 5
+        out["reference_gpu_kernel"] = {"gbs": round(n * nbytes / (ms * 1e-3) / 1e9, 1),
+                                       "what": "reference cuda_matmul_q8_0 (src/ai/cuda_ops.cu:1132-1155) for sm_100a"}
+        for raw in raws:
+            dev.free(raw)
+    dev.check("c1 q8_0")
+    for m in mats:
+        for k in ("Wd", "xd", "yd"):
+            dev.free(m[k])
+    return out
 
 
 def other_types_bench(dev, torch, iters=10):
@@ -829,7 +1022,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--no-pdl", action="store_true")
-    ap.add_argument("--no-decode", action="store_true", help="skip the 7B decode sub-benchmark")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-benchmarks")
+    ap.add_argument("--no-70b", action="store_true", help="skip the 70B decode sub-benchmarks")
     ap.add_argument("--profile-decode", action="store_true", help="small 7B decode case for ncu")
     ap.add_argument("--decode-only", action="store_true", help="only the decode sub-benchmark")
     ap.add_argument("--decode-model", choices=["7b", "70b"], default="7b", help="decode sub-benchmark model")

@@ -416,6 +416,17 @@ void cuda_matmul_q6_k(float *dst, const void *M, const float *v, int out_dim, in
 void cuda_batched_qkv_q8_0(float *q_out, float *k_out, float *v_out, const void *Wq, const void *Wk,
                            const void *Wv, const float *x, int q_dim, int kv_dim, int in_dim) {
     int act = holo_act_mode();
+    WeightInfo a, b, c;
+    // tiled weights of the expected shapes: the three matvecs in one batched launch
+    if (holo_registry_find(Wq, &a) && holo_registry_find(Wk, &b) && holo_registry_find(Wv, &c) &&
+        a.type == GT_Q8_0 && b.type == GT_Q8_0 && c.type == GT_Q8_0 && a.rows == q_dim && b.rows == kv_dim &&
+        c.rows == kv_dim && a.cols == in_dim && b.cols == in_dim && c.cols == in_dim && x) {
+        float *dst[3] = {q_out, k_out, v_out};
+        const void *M[3] = {Wq, Wk, Wv};
+        const float *v[3] = {x, x, x};
+        cuda_matvec_batch(3, dst, M, v, act);
+        return;
+    }
     matvec_any(q_out, Wq, x, q_dim, in_dim, GT_Q8_0, act, nullptr);
     matvec_any(k_out, Wk, x, kv_dim, in_dim, GT_Q8_0, act, nullptr);
     matvec_any(v_out, Wv, x, kv_dim, in_dim, GT_Q8_0, act, nullptr);

@@ -473,8 +473,18 @@ void cuda_batched_ffn_gate_up_q8_0(float *out, const void *W1, const void *W3, c
     if (!args_ok(out, ffn_dim, "cuda_batched_ffn_gate_up_q8_0") || ffn_dim == 0) return;
     float *up = (float *)holo_tmp((size_t)ffn_dim * sizeof(float));
     if (!up) return;
-    cuda_matvec(out, W1, x, ffn_dim, in_dim, GT_Q8_0, holo_act_mode(), nullptr);
-    cuda_matvec(up, W3, x, ffn_dim, in_dim, GT_Q8_0, holo_act_mode(), nullptr);
+    WeightInfo a, b;
+    if (holo_registry_find(W1, &a) && holo_registry_find(W3, &b) && a.type == GT_Q8_0 && b.type == GT_Q8_0 &&
+        a.rows == ffn_dim && b.rows == ffn_dim && a.cols == in_dim && b.cols == in_dim && x) {
+        // tiled weights: gate and up in one batched launch
+        float *dst[2] = {out, up};
+        const void *M[2] = {W1, W3};
+        const float *v[2] = {x, x};
+        cuda_matvec_batch(2, dst, M, v, holo_act_mode());
+    } else {
+        cuda_matvec(out, W1, x, ffn_dim, in_dim, GT_Q8_0, holo_act_mode(), nullptr);
+        cuda_matvec(up, W3, x, ffn_dim, in_dim, GT_Q8_0, holo_act_mode(), nullptr);
+    }
     silu_mul_kernel<<<ew_grid(ffn_dim), EW_THREADS, 0, holo_stream()>>>(out, out, up, ffn_dim);
     holo_check_launch("cuda_batched_ffn_gate_up_q8_0");
 }

@@ -79,6 +79,7 @@ SIGNATURES = {
     "cuda_upload_quant": (_vp, [_vp, _i, _i, _i]), "cuda_repack_quant": (_vp, [_vp, _i, _i, _i]),
     "cuda_quant_tiled_bytes": (_sz, [_i, _i, _i]),
     "cuda_matvec": (None, [_vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "cuda_matvec_batch": (_i, [_i, _vp, _vp, _vp, _i]),
     "cuda_matvec_noalloc": (_i, [_vp, _vp, _vp, _i, _i, _i, _i]),
     "cuda_matvec_noalloc_status_word": (_vp, []),
     "cuda_dequantize_rows": (None, [_vp, _vp, _i, _i, _i]),

@@ -86,6 +86,19 @@ int cuda_get_pdl(void);
 void cuda_matvec(float *dst, const void *M, const float *v, int out_dim, int in_dim,
                  int ggml_type, int act_mode, const float *residual);
 
+/* ---- independent matvecs in one launch ------------------------------------
+ * No counterpart in the reference.  dst[i] = M[i] . v[i] for i < n, each M[i]
+ * a tiled weight from cuda_upload_quant (its registered shape gives out_dim
+ * and in_dim), activations per act_mode.  The matvecs must not depend on one
+ * another (no v[j] is any dst[i]); their units form one sequence that one
+ * persistent launch per weight type splits evenly over the SMs, so the
+ * activation staging, quantization and split-K fix-up of each matrix stay off
+ * a chain of per-matrix launches.  Every output row has the arithmetic of
+ * cuda_matvec (within 1e-6: only the split points differ).  Returns 0 or the
+ * error code it records (HOLO_E_ARG: a pointer is not a tiled weight;
+ * HOLO_E_UNSUPPORTED: more than 65536 row-blocks of one type in a call). */
+int cuda_matvec_batch(int n, float *const *dst, const void *const *M, const float *const *v, int act_mode);
+
 /* ---- matvec without allocation ------------------------------------------------
  * No counterpart in the reference.  dst = M . v like cuda_matvec (no residual)
  * for a tiled weight M from cuda_upload_quant, but its split-K scratch is
