@@ -366,8 +366,9 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(kernel_gbs / peak, 4), "peak_source": peak_kind,
                      "traffic": traffic.get("bytes_per_launch") if traffic else None,
-                     "traffic_source": ("static: ncu dram__bytes of one isolated launch of the same kernel "
-                                        "(profiles/matvec_traffic.txt), not measured in this run") if traffic else None,
+                     "traffic_source": ("static: ncu dram__bytes of one isolated launch of the same kernel on the "
+                                        "same 8-matrix group (profiles/matvec_traffic.txt), not measured in this "
+                                        "run") if traffic else None,
                      "algorithmic_bytes_per_launch": round(bytes_step / launches_per_step),
                      "kernel": "mv_multi_kernel (cuda_matvec_batch), one launch per weight type",
                      "kernel_avg_us": round(region_us_per_launch, 3),
@@ -1011,6 +1012,30 @@ def run_profile_case(args):
                       "algorithmic_bytes_per_launch": algo_bytes(gt, rows, cols)}))
 
 
+def run_profile_batch(args):
+    """Small case for ncu: one cuda_matvec_batch call (one launch) over
+    --profile-batch N distinct Q4_K 11008x4096 matrices (N = 8: 203 MB, the
+    bench's per-launch group, larger than L2), --iters calls, no graph."""
+    import ctypes as C
+    n = args.profile_batch
+    dev = hb.Device(0, 1)
+    mats = []
+    for s in range(n):
+        W = synth.quant_matrix(hb.Q4_K, 11008, 4096, s)
+        mats.append((dev.upload_quant(W, hb.Q4_K, 11008, 4096), dev.upload(synth.activation(4096, s)),
+                     dev.alloc(4 * 11008)))
+    dst = (C.c_void_p * n)(*[m[2] for m in mats])
+    M = (C.c_void_p * n)(*[m[0] for m in mats])
+    v = (C.c_void_p * n)(*[m[1] for m in mats])
+    act = hb.ACT_Q8 if args.act == "q8" else hb.ACT_F32
+    for _ in range(args.iters):
+        dev.lib.cuda_matvec_batch(n, dst, M, v, act)
+    dev.sync()
+    dev.check("profile batch")
+    print(json.dumps({"profile_batch": n, "act": args.act, "iters": args.iters,
+                      "algorithmic_bytes_per_launch": n * algo_bytes(hb.Q4_K, 11008, 4096)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1037,6 +1062,8 @@ def main():
     ap.add_argument("--profile-prefill", default=None,
                     help="e.g. 512:14336x4096 or 8:57344x8192:q4_0 (ncu case: M:NxK[:type], Q4_K by default)")
     ap.add_argument("--profile-case", default=None, help="e.g. q4_k:11008x4096 (ncu small case)")
+    ap.add_argument("--profile-batch", type=int, default=0,
+                    help="one cuda_matvec_batch over N Q4_K 11008x4096 matrices, --iters times (ncu case)")
     ap.add_argument("--iters", type=int, default=4)
     args = ap.parse_args()
     if args.profile_decode:
@@ -1044,6 +1071,9 @@ def main():
         return
     if args.profile_case:
         run_profile_case(args)
+        return
+    if args.profile_batch:
+        run_profile_batch(args)
         return
     if args.profile_prompt:
         from holo_b200 import model as hm

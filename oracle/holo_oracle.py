@@ -217,15 +217,28 @@ def penalised_margin(logits, hist, penalty):
     return float(top2[1] - top2[0])
 
 
-class Reference:
-    """The reference engine's own CPU functions (src/ai/*.c built from source)."""
+DROPIN_SO = HERE / "_ref" / "libholo_ref_dropin.so"
 
-    def __init__(self):
-        if not REF_SO.exists():
+
+class Reference:
+    """The reference engine's own CPU functions (src/ai/*.c built from source).
+    path = DROPIN_SO: the drop-in build of the same code, whose GPU host path
+    (llm_cuda.c) runs on this repository's libholo_cuda.so (href_cuda_*)."""
+
+    def __init__(self, path=None):
+        so = pathlib.Path(path) if path else REF_SO
+        if not so.exists() and not path:
             build()
-        if not REF_SO.exists():
-            raise RuntimeError("oracle/_ref/libholo_ref.so is absent and the reference sources are not here")
-        lib = C.CDLL(str(REF_SO))
+        if not so.exists():
+            raise RuntimeError(f"{so} is absent and the reference sources are not here")
+        lib = C.CDLL(str(so))
+        if hasattr(lib, "href_cuda_init"):
+            lib.href_cuda_init.restype = _i
+            lib.href_cuda_init.argtypes = [_vp]
+            lib.href_cuda_forward.restype = _i
+            lib.href_cuda_forward.argtypes = [_vp, _i]
+            lib.href_cuda_reset.argtypes = [_vp]
+            lib.href_cuda_cleanup.argtypes = []
         lib.matmul_q.argtypes = [_vp, _vp, _vp, _i, _i, _i]
         lib.href_matmul_q_threads.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i]
         for name in ("dequantize_row_q8_0", "dequantize_row_q4_0", "dequantize_row_q4_k", "dequantize_row_q6_k"):

@@ -251,3 +251,21 @@ long long href_gguf_array_len(const char *path, const char *key) {
     gguf_close(g);
     return (long long)len;
 }
+
+#ifdef HOLO_USE_CUDA
+/* The reference's GPU host path (src/ai/llm_cuda.c), built only into the
+ * drop-in library (oracle/Makefile `dropin`, linked to this repository's
+ * libholo_cuda.so in place of the reference's cuda_ops.cu): llm_cuda_init
+ * uploads the model with its own upload_tensor (cuda_malloc +
+ * cuda_memcpy_h2d, llm_cuda.c:189-196), llm_forward_cuda runs one position
+ * (llm_cuda.c:558-946) and leaves the logits in ctx->state.logits. */
+extern int llm_cuda_init(llm_ctx_t *ctx);
+extern int llm_forward_cuda(llm_ctx_t *ctx, const int *tokens, int n_tokens);
+extern void llm_cuda_cleanup(void);
+extern void llm_cuda_reset(void);
+
+int href_cuda_init(href_model_t *m) { return llm_cuda_init(&m->ctx); }
+int href_cuda_forward(href_model_t *m, int token) { return llm_forward_cuda(&m->ctx, &token, 1); }
+void href_cuda_reset(href_model_t *m) { llm_reset(&m->ctx); llm_cuda_reset(); }
+void href_cuda_cleanup(void) { llm_cuda_cleanup(); }
+#endif
