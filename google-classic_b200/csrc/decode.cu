@@ -841,6 +841,17 @@ bool row_exchange(HoloModel *m, cudaStream_t st, const float *src, int M, int w,
     return holo_check_launch("rows: exchange");
 }
 
+// prompt attention on the tensor cores (fp16 cache, head_dim 128) unless
+// HOLO_PROMPT_ATTN=simt selects the SIMT kernel (pf_attn_kernel)
+bool prompt_attn_tc() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("HOLO_PROMPT_ATTN");
+        v = (e && strcmp(e, "simt") == 0) ? 0 : 1;
+    }
+    return v == 1;
+}
+
 bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
     const holo_model_desc &d = m->d;
     const int M = p.M, hd = d.head_dim;
@@ -865,10 +876,13 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
         return holo_check_launch("rows: residual");
     };
     const int qt = std::max(1, PA_ROWS / group);
+    // every projection's K split is planned for the whole matrix (not this
+    // rank's rows), so a row shard sums each row exactly as one GPU does
+    const int rows_qkv = (d.n_heads + 2 * d.n_kv_heads) * hd;
     for (int l = 0; l < d.n_layers && ok; ++l) {
         HoloLayer &L = m->layers[l];
         ok = rows_norm(p, L.attn_norm, d.dim, d.eps, st) &&
-             holo_matmul_batched(p.qkv, L.wqkv, L.i_qkv, p.xn, M, st, p.scratch, p.scratch_bytes);
+             holo_matmul_batched(p.qkv, L.wqkv, L.i_qkv, p.xn, M, st, p.scratch, p.scratch_bytes, rows_qkv);
         const size_t es = d.kv_f16 ? 2 : 4;
         uint8_t *kc = (uint8_t *)p.kc + (size_t)l * kv_layer * es, *vc = (uint8_t *)p.vc + (size_t)l * kv_layer * es;
         const dim3 rg(std::max(m->nh, m->nkv), M), ag(m->nh, m->max_splits, M), mg(m->nh, M);
@@ -885,7 +899,16 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
                          launch_pdl(dec_attn_merge_kernel<HDV>, mg, dim3(HDV), st, false, p.att,                    \
                                     (const float *)p.part, p.pos, m->per_split, m->max_splits, (size_t)m->q_dim,    \
                                     part_bs))
-        if (d.kv_f16) {
+        if (p.prompt && d.kv_f16 && hd == 128 && prompt_attn_tc()) {
+            // RoPE + append, then the causal attention on the tensor cores
+            HoloDevice *D = holo_dev();
+            ok = ok && launch_pdl(dec_rope_append_kernel<__half>, rg, dim3(hd / 2), st, false, p.qkv, (__half *)kc,
+                                  (__half *)vc, p.pos, hd, m->nh, m->nkv, d.rope_base, (size_t)qkv_dim, p.kv_bs, p.rps,
+                                  d.rope_mode) &&
+                 holo_prompt_attn_tc(p.att, p.qkv, (const __half *)kc, (const __half *)vc, p.pos, p.rps, M / p.rps,
+                                     m->nh, group, m->kv_dim, (size_t)qkv_dim, (size_t)m->q_dim, p.kv_bs, sqrt_hd,
+                                     D ? D->status : nullptr, st);
+        } else if (d.kv_f16) {
             if (hd == 64) ok = ok && BT_ATTN(__half, 64);
             else if (hd == 128) ok = ok && BT_ATTN(__half, 128);
             else ok = ok && BT_ATTN(__half, 256);
@@ -896,11 +919,11 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
         }
 #undef BT_ATTN
         if (shard) ok = ok && row_exchange(m, st, p.att, M, m->q_dim, m->h0 * hd, m->off_ratt, m->q_dim_g);
-        ok = ok && holo_matmul_batched(p.t, L.wo, L.i_o, att_in, M, st, p.scratch, p.scratch_bytes);
+        ok = ok && holo_matmul_batched(p.t, L.wo, L.i_o, att_in, M, st, p.scratch, p.scratch_bytes, d.dim);
         if (shard) ok = ok && row_exchange(m, st, p.t, M, m->dim_loc, m->d0, m->off_rt, d.dim);
         ok = ok && add(t_in);
         ok = ok && rows_norm(p, L.ffn_norm, d.dim, d.eps, st) &&
-             holo_matmul_batched(p.hh, L.w13, L.i_13, p.xn, M, st, p.scratch, p.scratch_bytes);
+             holo_matmul_batched(p.hh, L.w13, L.i_13, p.xn, M, st, p.scratch, p.scratch_bytes, 2 * d.ffn_dim);
         if (ok) {
             const long long n = (long long)M * m->ffn_loc;
             bt_swiglu_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 2048), 256, 0, st>>>(p.h, p.hh,
@@ -908,7 +931,7 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
             ok = holo_check_launch("rows: swiglu");
         }
         if (shard) ok = ok && row_exchange(m, st, p.h, M, m->ffn_loc, m->f0, m->off_rh, d.ffn_dim);
-        ok = ok && holo_matmul_batched(p.t, L.w2, L.i_2, h_in, M, st, p.scratch, p.scratch_bytes);
+        ok = ok && holo_matmul_batched(p.t, L.w2, L.i_2, h_in, M, st, p.scratch, p.scratch_bytes, d.dim);
         if (shard) ok = ok && row_exchange(m, st, p.t, M, m->dim_loc, m->d0, m->off_rt, d.dim);
         ok = ok && add(t_in);
     }
@@ -1029,9 +1052,11 @@ bool prompt_supported(const HoloModel *m) {
 bool prompt_buffers(HoloModel *m, int rows) {
     const holo_model_desc &d = m->d;
     size_t need = 0;
-    for (const HoloLayer &L : m->layers)
-        for (const WeightInfo *wi : {&L.i_qkv, &L.i_o, &L.i_13, &L.i_2})
-            need = std::max(need, holo_matmul_batched_scratch(*wi, rows));
+    const int plan[4] = {(d.n_heads + 2 * d.n_kv_heads) * d.head_dim, d.dim, 2 * d.ffn_dim, d.dim};
+    for (const HoloLayer &L : m->layers) {
+        const WeightInfo *wis[4] = {&L.i_qkv, &L.i_o, &L.i_13, &L.i_2};
+        for (int k = 0; k < 4; ++k) need = std::max(need, holo_matmul_batched_scratch(*wis[k], rows, plan[k]));
+    }
     if (need > m->rscratch_bytes) {
         cudaFree(m->rscratch);
         m->rscratch = nullptr;

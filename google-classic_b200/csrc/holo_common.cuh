@@ -166,6 +166,12 @@ void *holo_tmp(size_t bytes);
 bool holo_embedding_table_f32(float *dst, const void *table, int type, int rows, int dim, bool ggml_q4k,
                               cudaStream_t st);
 
+// prompt_attn.cu: causal prompt attention on the tensor cores (fp16 cache,
+// head_dim 128); see the file for the layout of the arguments
+bool holo_prompt_attn_tc(float *att, const float *qkv, const __half *kc, const __half *vc, const int *pos_p, int M,
+                         int nseq, int n_heads, int group, int kv_dim, size_t qkv_bs, size_t att_bs, size_t kv_bs,
+                         float sqrt_hd, int *status, cudaStream_t st);
+
 // Registry of repacked weights: device pointer -> geometry.
 struct WeightInfo {
     int type = 0;
@@ -182,10 +188,12 @@ bool holo_quant_shape_ok(int ggml_type, int rows, int cols);
 WeightInfo holo_weight_info(int ggml_type, int rows, int cols, int q4k_layout);
 // Y[M][N] = X[M][K] . W^T on the tensor cores for a tiled weight (prefill.cu);
 // scratch NULL: the library's shared scratch, else the caller's (at least
-// holo_matmul_batched_scratch bytes)
+// holo_matmul_batched_scratch bytes).  plan_rows > 0: split K as for a weight
+// of that many rows (a row shard passes the whole matrix's, so each row's sum
+// is cut at the same K points as on one GPU); 0: the weight's own rows.
 bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st,
-                         void *scratch, size_t scratch_bytes);
-size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M);
+                         void *scratch, size_t scratch_bytes, int plan_rows = 0);
+size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M, int plan_rows = 0);
 // the batched matmul's weights: rows a multiple of this (one MMA tile)
 constexpr int PF_ROWS_ALIGN = 128;
 // Y[M][N] = X[M][K] . W^T for M <= MVB_MAX_M on the CUDA cores (matvec_batch.cu):

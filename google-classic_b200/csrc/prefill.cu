@@ -23,8 +23,11 @@
 // in a fixed order.  Every wait is bounded (HOLO_E_TIMEOUT).
 #include "holo_common.cuh"
 #include "mv_unit.cuh"
+#include "tc_util.cuh"
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 namespace {
 
@@ -33,7 +36,8 @@ using namespace holo_mv;
 constexpr int PF_BM = 128;                         // weight rows per CTA (MMA M)
 static_assert(PF_BM == PF_ROWS_ALIGN, "row tile");
 constexpr int PF_BK = 128;                         // K per stage: two 128-byte atoms of fp16
-constexpr int PF_MAX_AST = 3;                      // dequantized weight stages, at most
+constexpr int PF_MAX_AST = 4;                      // dequantized weight stages, at most
+constexpr int PF_A_COLS = PF_BK / 2;               // TMEM columns of one stage in TMEM (fp16 pairs)
 constexpr int PF_DQ_WARPS = 16;                    // dequantize, then read the accumulators
 constexpr int PF_B_WARP = PF_DQ_WARPS, PF_RAW_WARP = PF_DQ_WARPS + 1, PF_MMA_WARP = PF_DQ_WARPS + 2;
 constexpr int PF_THREADS = (PF_DQ_WARPS + 3) * 32; // + activation copies + weight copies + MMA
@@ -45,11 +49,18 @@ constexpr int PF_MAX_BST = 4;
 // raw super-blocks staged ahead in shared memory, and activation-tile stages:
 // the activation tiles get their own, deeper ring (a tile is requested as soon
 // as its slot is free, so its copy latency is hidden behind several stages)
-__host__ __device__ constexpr int pf_raw_slots(int tn) { return tn == 64 ? PF_MAX_RAW : 1; }
-__host__ __device__ constexpr int pf_b_stages(int tn) { return tn == 64 ? 4 : tn == 128 ? 3 : 2; }
+// (AT: the dequantized weights go to TMEM, which frees the shared memory
+// their stages took for deeper activation and raw-weight rings)
+__host__ __device__ constexpr int pf_raw_slots(int tn, bool at) { return tn == 64 || (at && tn == 128) ? PF_MAX_RAW : 1; }
+__host__ __device__ constexpr int pf_b_stages(int tn, bool at) {
+    return tn == 64 ? 4 : tn == 128 ? (at ? 4 : 3) : (at ? 3 : 2);
+}
 // dequantized weight stages: the dequantizing warps run this many chunks
 // ahead of the MMAs that free them
-__host__ __device__ constexpr int pf_a_stages(int tn) { return tn == 256 ? 2 : 3; }
+__host__ __device__ constexpr int pf_a_stages(int tn, bool at) { return at ? 4 : tn == 256 ? 2 : 3; }
+// TMEM columns: the TN accumulator columns, then (AT) the weight stages
+__host__ __device__ constexpr uint32_t pf_tmem_cols(int tn, bool at) { return at ? 512u : (uint32_t)tn; }
+static_assert(256 + 4 * PF_A_COLS <= 512, "accumulator + weight stages fit TMEM");
 
 struct PfBars {
     uint64_t full_a[PF_MAX_AST];  // the dequantizing warps arrived
@@ -62,52 +73,11 @@ struct PfBars {
     uint32_t tmem;                // accumulator base (TMEM address)
 };
 
-// ---- tcgen05 primitives ----------------------------------------------------
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// shared-memory descriptor of a K-major, 128-byte-swizzled operand: rows of
-// 128 bytes, 8-row atoms 1024 bytes apart (SBO), 16-byte LBO, version 1
-__device__ __forceinline__ uint64_t sw128_desc(const void *smem) {
-    const uint32_t a = smem_addr(smem);
-    return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
+// ---- tcgen05 primitives: tc_util.cuh --------------------------------------
+using namespace holo_tc;
 
 // instruction descriptor: fp16 x fp16 -> fp32, both K-major, M = 128, N = tn
-__host__ __device__ constexpr uint32_t pf_idesc(int tn) {
-    return (1u << 4) | ((uint32_t)(tn >> 3) << 17) | ((uint32_t)(PF_BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, bool acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        :: "r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"((uint32_t)acc) : "memory");
-}
-
-__device__ __forceinline__ void tc_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 :: "r"(smem_addr(bar)) : "memory");
-}
-
-// 16 consecutive fp32 columns of this warp's 32 TMEM lanes
-__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// byte offset of element (row r, column c) of a [rows][64] fp16 tile in the
-// 128-byte-swizzled K-major layout (16-byte chunk index XOR row mod 8)
-__host__ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
-    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((((c >> 3) ^ (r & 7)) & 7) << 4) + (c & 7) * 2);
-}
+__host__ __device__ constexpr uint32_t pf_idesc(int tn) { return tc_idesc_f16(PF_BM, tn); }
 
 // ---- activations: Q8 per 32-block, dequantized to fp16, tiled + swizzled ---
 // xt tile (mt, kc) = rows [mt*tn, +tn) x columns [kc*128, +128), tn*256 bytes:
@@ -212,16 +182,22 @@ __device__ __forceinline__ void dq_block(const uint4 &h, const uint4 &p0, const 
 
 // ---- the matmul ----------------------------------------------------------------
 // out[ks][M][N] (ks = blockIdx.z, K chunks [kc0, kc1)); W tiled TYPE with
-// `units` units a row.
-template <int TYPE, int TN>
+// `units` units a row.  AT: the dequantizing warps store the weight tile into
+// TMEM (tcgen05.st; row r = lane r, columns TN + 64 s ..) and the MMAs read A
+// from there, so the only operand the tensor core reads from shared memory is
+// the activation tile: a stage in shared memory costs the tile's write, its
+// read by the MMAs and the staging of the activations -- the shared-memory
+// bandwidth that bounded the first version.
+template <int TYPE, int TN, bool AT>
 __global__ void __launch_bounds__(PF_THREADS, 1)
 pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint8_t *__restrict__ xt, int M, int N,
               int K, int units, int kc_per_split, int *status) {
     extern __shared__ uint8_t pf_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t *sa = smem;                                   // [stages][2 atom columns][128 rows][128 B]
-    constexpr int PF_STAGES = pf_a_stages(TN), SB = pf_b_stages(TN), R = pf_raw_slots(TN);
-    uint8_t *sb = smem + PF_STAGES * PF_A_BYTES;          // [SB][2 atom columns][TN rows][128 B]
+    constexpr int PF_STAGES = pf_a_stages(TN, AT), SB = pf_b_stages(TN, AT), R = pf_raw_slots(TN, AT);
+    constexpr uint32_t TCOLS = pf_tmem_cols(TN, AT);
+    uint8_t *sa = smem;                                   // !AT: [stages][2 atom columns][128 rows][128 B]
+    uint8_t *sb = smem + (AT ? 0 : PF_STAGES * PF_A_BYTES);   // [SB][2 atom columns][TN rows][128 B]
     uint8_t *sr = sb + SB * TN * 256;                     // [R][4 row-blocks][UB]
     constexpr int UB = UnitGeom<TYPE>::UNIT_BYTES, CPU = UnitGeom<TYPE>::VALS / PF_BK;   // chunks a unit
     PfBars &B = *reinterpret_cast<PfBars *>(sr + R * PF_RAW_BYTES);
@@ -247,11 +223,7 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
         mbar_init(&B.done, 1);
         fence_barrier_init();
     }
-    if (warp == PF_MMA_WARP) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     :: "r"(smem_addr(&B.tmem)), "r"((uint32_t)TN) : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
+    if (warp == PF_MMA_WARP) tc_alloc(&B.tmem, TCOLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -280,12 +252,27 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
                 if (i >= PF_STAGES)
                     ok = mbar_wait_bounded(&B.empty[s], ((i / PF_STAGES) + 1) & 1, status, HOLO_E_TIMEOUT);
                 if (!__all_sync(0xffffffffu, ok)) break;
-                // column 32 q + position of the chunk: atom column q / 2
-                uint8_t *acol = sa + s * PF_A_BYTES + (q >> 1) * (PF_BM * 128);
+                if constexpr (AT) {
+                    // lane r, columns TN + 64 s + 16 q ..: positions 32 q .. 32 q + 31 in pairs
+                    uint32_t v[16];
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc)
-                    *reinterpret_cast<uint4 *>(acol + sw128_off(r, 32 * (q & 1) + 8 * cc)) = outv[cc];
-                fence_proxy_async_smem();   // the tensor core reads these through the async proxy
+                    for (int cc = 0; cc < 4; ++cc) {
+                        v[4 * cc] = outv[cc].x;
+                        v[4 * cc + 1] = outv[cc].y;
+                        v[4 * cc + 2] = outv[cc].z;
+                        v[4 * cc + 3] = outv[cc].w;
+                    }
+                    tc_st16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(TN + s * PF_A_COLS + 16 * q), v);
+                    tc_wait_st();
+                    tc_fence_before();   // the MMA thread reads the stage after the barrier
+                } else {
+                    // column 32 q + position of the chunk: atom column q / 2
+                    uint8_t *acol = sa + s * PF_A_BYTES + (q >> 1) * (PF_BM * 128);
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc)
+                        *reinterpret_cast<uint4 *>(acol + sw128_off(r, 32 * (q & 1) + 8 * cc)) = outv[cc];
+                    fence_proxy_async_smem();   // the tensor core reads these through the async proxy
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&B.full_a[s]);
             }
@@ -362,12 +349,21 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
                      mbar_wait_bounded(&B.full_b[t], (i / SB) & 1, status, HOLO_E_TIMEOUT);
                 if (!ok) break;
                 tc_fence_after();
-                const uint64_t ad = a0 + (uint64_t)((s * PF_A_BYTES) >> 4);
                 const uint64_t bd = b0 + (uint64_t)((t * TN * 256) >> 4);
+                if constexpr (AT) {
+                    // K step kk: 16 values = 8 columns of the stage
+                    const uint32_t ta = tmem + (uint32_t)(TN + s * PF_A_COLS);
 #pragma unroll
-                for (int kk = 0; kk < PF_BK / 16; ++kk)
-                    tc_mma(tmem, ad + (uint64_t)(((kk >> 2) * (PF_BM * 128) + (kk & 3) * 32) >> 4),
-                           bd + (uint64_t)(((kk >> 2) * (TN * 128) + (kk & 3) * 32) >> 4), idesc, (i | kk) != 0);
+                    for (int kk = 0; kk < PF_BK / 16; ++kk)
+                        tc_mma_ts(tmem, ta + (uint32_t)(8 * kk),
+                                  bd + (uint64_t)(((kk >> 2) * (TN * 128) + (kk & 3) * 32) >> 4), idesc, (i | kk) != 0);
+                } else {
+                    const uint64_t ad = a0 + (uint64_t)((s * PF_A_BYTES) >> 4);
+#pragma unroll
+                    for (int kk = 0; kk < PF_BK / 16; ++kk)
+                        tc_mma(tmem, ad + (uint64_t)(((kk >> 2) * (PF_BM * 128) + (kk & 3) * 32) >> 4),
+                               bd + (uint64_t)(((kk >> 2) * (TN * 128) + (kk & 3) * 32) >> 4), idesc, (i | kk) != 0);
+                }
                 tc_commit(&B.empty[s]);
                 tc_commit(&B.empty_b[t]);
             }
@@ -380,8 +376,7 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
     __syncthreads();
     if (warp == PF_MMA_WARP) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"((uint32_t)TN)
-                     : "memory");
+        tc_dealloc(tmem, TCOLS);
     }
 }
 
@@ -394,25 +389,24 @@ __global__ void pf_reduce_kernel(float *__restrict__ y, const float *__restrict_
     }
 }
 
-size_t pf_smem(int tn) {
-    return 1024 + (size_t)pf_a_stages(tn) * PF_A_BYTES + (size_t)pf_b_stages(tn) * tn * 256 +
-           (size_t)pf_raw_slots(tn) * PF_RAW_BYTES +
-           sizeof(PfBars);
+size_t pf_smem(int tn, bool at) {
+    return 1024 + (at ? 0 : (size_t)pf_a_stages(tn, at) * PF_A_BYTES) + (size_t)pf_b_stages(tn, at) * tn * 256 +
+           (size_t)pf_raw_slots(tn, at) * PF_RAW_BYTES + sizeof(PfBars);
 }
 
-template <int TYPE, int TN>
+template <int TYPE, int TN, bool AT>
 bool launch_mma(float *out, const uint8_t *W, const uint8_t *xt, int M, int N, int K, int units, int splits,
                 int kc_per_split, int mtiles, int *status, cudaStream_t st) {
-    const size_t smem = pf_smem(TN);
+    const size_t smem = pf_smem(TN, AT);
     static int configured = -1;   // the device the attribute was set for
     const int dev = holo_dev() ? holo_dev()->id : -1;
     if (configured != dev) {
-        if (cudaFuncSetAttribute(pf_mma_kernel<TYPE, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        if (cudaFuncSetAttribute(pf_mma_kernel<TYPE, TN, AT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
             return holo_check_launch("prefill: attributes");
         configured = dev;
     }
-    pf_mma_kernel<TYPE, TN><<<dim3((N + PF_BM - 1) / PF_BM, mtiles, splits), PF_THREADS, smem, st>>>(out, W, xt, M, N, K, units,
+    pf_mma_kernel<TYPE, TN, AT><<<dim3((N + PF_BM - 1) / PF_BM, mtiles, splits), PF_THREADS, smem, st>>>(out, W, xt, M, N, K, units,
                                                                                 kc_per_split, status);
     return holo_check_launch("prefill matmul");
 }
@@ -421,22 +415,33 @@ bool launch_mma(float *out, const uint8_t *W, const uint8_t *xt, int M, int N, i
 
 namespace {
 
+// dequantized weight tiles in shared memory (default) or in TMEM
+// (HOLO_PREFILL_A=tmem)
+bool pf_weights_in_tmem() {
+    static const bool at = [] {
+        const char *e = getenv("HOLO_PREFILL_A");
+        return e && strcmp(e, "tmem") == 0;
+    }();
+    return at;
+}
+
 // the launch plan of one batched matmul: token tile, K splits, scratch bytes
 struct PfPlan {
     int tn, mtiles, Mpad, splits, kc_per_split;
     size_t xt_bytes, part_bytes;
 };
 
-PfPlan pf_plan(const WeightInfo &wi, int M, int sms) {
+PfPlan pf_plan(const WeightInfo &wi, int M, int sms, int plan_rows) {
     PfPlan p;
     const int N = wi.rows, K = wi.cols, vals = wi.type == GT_Q8_0 ? 128 : 256;
+    const int NP = plan_rows > 0 ? plan_rows : N;   // rows the K split is planned for
     p.tn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
     p.mtiles = (M + p.tn - 1) / p.tn;
     p.Mpad = p.mtiles * p.tn;
     const int nkc = K / PF_BK, cpu = vals / PF_BK;
     // K splits (whole units) so that the CTAs cover the SMs when the weight
     // has few row tiles
-    const int base = (N + PF_BM - 1) / PF_BM * p.mtiles;
+    const int base = (NP + PF_BM - 1) / PF_BM * p.mtiles;
     p.splits = std::max(1, std::min(nkc / 4, sms / base));
     p.kc_per_split = ((nkc + p.splits - 1) / p.splits + cpu - 1) / cpu * cpu;
     p.splits = (nkc + p.kc_per_split - 1) / p.kc_per_split;   // every split non-empty
@@ -447,10 +452,10 @@ PfPlan pf_plan(const WeightInfo &wi, int M, int sms) {
 
 }  // namespace
 
-size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M) {
+size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M, int plan_rows) {
     if (M <= MVB_MAX_M) return holo_matmul_few_scratch(wi, M);
     HoloDevice *D = holo_dev();
-    const PfPlan p = pf_plan(wi, M, D ? D->sms : 148);
+    const PfPlan p = pf_plan(wi, M, D ? D->sms : 148, plan_rows);
     return p.xt_bytes + p.part_bytes;
 }
 
@@ -459,7 +464,7 @@ size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M) {
 // buffer of scratch_bytes (at least holo_matmul_batched_scratch), or NULL for
 // the library's shared one.
 bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st,
-                         void *scratch, size_t scratch_bytes) {
+                         void *scratch, size_t scratch_bytes, int plan_rows) {
     // a few rows: the CUDA-core kernel that reads each weight unit once for all
     // of them (matvec_batch.cu); a tensor-core tile would be mostly padding
     if (M > 0 && M <= MVB_MAX_M) return holo_matmul_few(Y, W, wi, X, M, st, scratch, scratch_bytes);
@@ -473,7 +478,7 @@ bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const fl
                                     "K a whole number of 128/256-value units");
         return false;
     }
-    const PfPlan pl = pf_plan(wi, M, D->sms);
+    const PfPlan pl = pf_plan(wi, M, D->sms, plan_rows);
     const int tn = pl.tn, mtiles = pl.mtiles, Mpad = pl.Mpad, splits = pl.splits, kc_per_split = pl.kc_per_split;
     const size_t xt_bytes = pl.xt_bytes, part_bytes = pl.part_bytes;
     uint8_t *tmp;
@@ -495,16 +500,19 @@ bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const fl
     if (!holo_check_launch("batched matmul activations")) return false;
     const uint8_t *w = static_cast<const uint8_t *>(W);
     bool ok;
-#define PF_LAUNCH(T)                                                                                              \
-    (tn == 64    ? launch_mma<T, 64>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st)  \
-     : tn == 128 ? launch_mma<T, 128>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st) \
-                 : launch_mma<T, 256>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st))
+    const bool at = pf_weights_in_tmem();
+#define PF_LAUNCH_AT(T, A)                                                                                           \
+    (tn == 64    ? launch_mma<T, 64, A>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st)  \
+     : tn == 128 ? launch_mma<T, 128, A>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st) \
+                 : launch_mma<T, 256, A>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st))
+#define PF_LAUNCH(T) (at ? PF_LAUNCH_AT(T, true) : PF_LAUNCH_AT(T, false))
     switch (wi.type) {
     case GT_Q4_K: ok = PF_LAUNCH(GT_Q4_K); break;
     case GT_Q4_0: ok = PF_LAUNCH(GT_Q4_0); break;
     default: ok = PF_LAUNCH(GT_Q8_0); break;
     }
 #undef PF_LAUNCH
+#undef PF_LAUNCH_AT
     if (!ok) return false;
     if (splits > 1) {
         const long long mn = (long long)M * N;

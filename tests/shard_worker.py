@@ -59,6 +59,10 @@ def split_prompt():
     return np.random.default_rng(SPLIT_SEED).integers(0, CFG_SPLIT["vocab"], size=N_SPLIT_PROMPT).astype(np.int32)
 
 
+def split_long_prompt():
+    return np.random.default_rng(SPLIT_SEED + 1).integers(0, CFG_SPLIT["vocab"], size=100).astype(np.int32)
+
+
 class StandInModel:
     """comm_handle / open_peers of a model, without a device."""
 
@@ -141,6 +145,12 @@ def run_gpu(rank, world, out):
         res["split_greedy"] = m.generate(sp, N_SPLIT_GREEDY, SamplerDesc(0.0, 0.95, 40, 1.1, 64), seed=5)
         m.reset()
         res["split_logits"] = np.stack([m.forward(t) for t in np.concatenate([sp, res["split_greedy"]])])
+        # a 100-row prompt pass (tensor-core matmuls whose K split is planned
+        # for the whole matrices), then one step reading its cache
+        m.reset()
+        lp = split_long_prompt()
+        m.prefill(lp[:-1], want_logits=False)
+        res["split_rows_logits"] = m.forward(int(lp[-1]))
         dist.barrier()
         m.close()
         # every rank computed the same logits and tokens

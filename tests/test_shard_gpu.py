@@ -35,7 +35,7 @@ from holo_oracle import RefModel
 
 sys.path.insert(0, str(ROOT / "tests"))
 from shard_worker import (CFG, CFG_SPLIT, N_GREEDY, N_PROMPT, N_ROWS, N_SAMPLED, N_SPLIT_GREEDY,  # noqa: E402
-                          PROMPT_SEED, SPLIT_SEED, cfg_for, split_prompt)
+                          PROMPT_SEED, SPLIT_SEED, cfg_for, split_long_prompt, split_prompt)
 
 pytestmark = pytest.mark.gpu
 
@@ -134,6 +134,20 @@ def test_sharded_split_attention_bit_identical_to_one_gpu(sharded, dev):
              if diff else ""))
     assert np.array_equal(sharded["split_greedy"], got)
     assert not diff
+
+
+def test_sharded_prompt_pass_split_planned_for_whole_matrix(sharded, dev):
+    """A 99-row prompt pass on the 32-head model: every projection's K split
+    is planned for the whole matrix, not the rank's rows, so the step after it
+    gives the one-GPU logits bit for bit."""
+    from holo_b200.model import synthetic_model
+    m = synthetic_model(CFG_SPLIT, seed=SPLIT_SEED, act_mode=hb.ACT_Q8, kv_f16=True)
+    lp = split_long_prompt()
+    m.prefill(lp[:-1], want_logits=False)
+    one = m.forward(int(lp[-1]))
+    m.close()
+    print(f"{sharded['world']} ranks, 99-row prompt pass: max abs diff {np.abs(one - sharded['split_rows_logits']).max():.3e}")
+    assert np.array_equal(one, sharded["split_rows_logits"])
 
 
 def test_sharded_prompt_pass_matches_one_gpu(sharded, dev, weights):
