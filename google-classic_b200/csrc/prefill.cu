@@ -51,6 +51,8 @@ constexpr int PF_MAX_BST = 4;
 // as its slot is free, so its copy latency is hidden behind several stages)
 // (AT: the dequantized weights go to TMEM, which frees the shared memory
 // their stages took for deeper activation and raw-weight rings)
+// (measured: deeper raw-weight rings -- 6 / 4 / 3 slots -- gained nothing at
+// TN = 64 and lost 8 % at TN = 256, where the activation ring needs the room)
 __host__ __device__ constexpr int pf_raw_slots(int tn, bool at) { return tn == 64 || (at && tn == 128) ? PF_MAX_RAW : 1; }
 __host__ __device__ constexpr int pf_b_stages(int tn, bool at) {
     return tn == 64 ? 4 : tn == 128 ? (at ? 4 : 3) : (at ? 3 : 2);
@@ -82,26 +84,44 @@ __host__ __device__ constexpr uint32_t pf_idesc(int tn) { return tc_idesc_f16(PF
 // ---- activations: Q8 per 32-block, dequantized to fp16, tiled + swizzled ---
 // xt tile (mt, kc) = rows [mt*tn, +tn) x columns [kc*128, +128), tn*256 bytes:
 // two atom columns of 64 values (tn*128 bytes each); rows past M are zero.
-// One warp per (row, 32-block), lane = element.
+// Four threads per (row, 32-block), 8 consecutive values each: two 16-byte
+// loads, the block maximum over the four lanes, one 16-byte store (8 values
+// are one 16-byte chunk of the swizzled layout).  Mpad * K / 8 threads, a
+// multiple of 32, so every warp is whole.
 __global__ void pf_act_kernel(__half *__restrict__ xt, const float *__restrict__ x, int M, int Mpad, int K,
                               int tn) {
     const int nb = K / 32;
-    const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (w >= (long long)Mpad * nb) return;
-    const int m = (int)(w / nb), b = (int)(w % nb);
-    float v = m < M ? x[(size_t)m * K + (size_t)b * 32 + lane] : 0.0f;
-    // quantize_act_q8's arithmetic: d = amax / 127, id = 1 / d, q = rint(v * id)
-    float amax = fabsf(v);
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long g = t >> 2;   // (row, block)
+    if (g >= (long long)Mpad * nb) return;
+    const int m = (int)(g / nb), b = (int)(g % nb), sub = (int)(t & 3);
+    float v[8];
+    if (m < M) {
+        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)m * K + (size_t)b * 32 + 8 * sub);
+        const float4 a = __ldg(src), c = __ldg(src + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+    } else {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+    }
+    // quantize_act_q8's arithmetic: d = amax / 127, id = 1 / d, q = rint(v * id)
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    const float q = fminf(fmaxf(rintf(__fmul_rn(v, id)), -127.0f), 127.0f);
-    const __half h = __float2half_rn(__fmul_rn(d, q));
-    const int k = b * 32 + lane, mt = m / tn, r = m % tn, kc = k / PF_BK, kk = k % PF_BK;
+    __align__(16) __half h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float q = fminf(fmaxf(rintf(__fmul_rn(v[j], id)), -127.0f), 127.0f);
+        h[j] = __float2half_rn(__fmul_rn(d, q));
+    }
+    const int k = b * 32 + 8 * sub, mt = m / tn, r = m % tn, kc = k / PF_BK, kk = k % PF_BK;
     uint8_t *tile = reinterpret_cast<uint8_t *>(xt) + ((size_t)mt * (K / PF_BK) + kc) * (size_t)tn * 256;
-    *reinterpret_cast<__half *>(tile + (kk >> 6) * tn * 128 + sw128_off(r, kk & 63)) = h;
+    *reinterpret_cast<uint4 *>(tile + (kk >> 6) * tn * 128 + sw128_off(r, kk & 63)) = *reinterpret_cast<const uint4 *>(h);
 }
 
 // ---- weight dequantization (one thread: one row, 32 positions of a chunk) ---
@@ -415,12 +435,12 @@ bool launch_mma(float *out, const uint8_t *W, const uint8_t *xt, int M, int N, i
 
 namespace {
 
-// dequantized weight tiles in shared memory (default) or in TMEM
-// (HOLO_PREFILL_A=tmem)
+// dequantized weight tiles in TMEM (default) or in shared memory
+// (HOLO_PREFILL_A=smem, the first version, kept for comparison)
 bool pf_weights_in_tmem() {
     static const bool at = [] {
         const char *e = getenv("HOLO_PREFILL_A");
-        return e && strcmp(e, "tmem") == 0;
+        return !(e && strcmp(e, "smem") == 0);
     }();
     return at;
 }
@@ -472,10 +492,10 @@ bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const fl
     if (!D) return false;
     const int N = wi.rows, K = wi.cols;
     const int vals = wi.type == GT_Q8_0 ? 128 : 256;
-    if (!Y || !W || !X || M <= 0 || K % vals ||
+    if (!Y || !W || !X || M <= 0 || K % vals || (reinterpret_cast<uintptr_t>(X) & 15) ||
         (wi.type != GT_Q4_K && wi.type != GT_Q4_0 && wi.type != GT_Q8_0)) {
         holo_set_status(HOLO_E_ARG, "batched matmul: needs a tiled Q8_0/Q4_0/Q4_K weight (cuda_upload_quant), "
-                                    "K a whole number of 128/256-value units");
+                                    "K a whole number of 128/256-value units, X 16-byte aligned");
         return false;
     }
     const PfPlan pl = pf_plan(wi, M, D->sms, plan_rows);
@@ -494,8 +514,8 @@ bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const fl
     if (!tmp) return false;
     uint8_t *xt = tmp;
     float *part = splits > 1 ? reinterpret_cast<float *>(tmp + xt_bytes) : Y;
-    const long long warps = (long long)Mpad * (K / 32);
-    pf_act_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(reinterpret_cast<__half *>(xt), X, M, Mpad,
+    const long long act_threads = (long long)Mpad * (K / 32) * 4;
+    pf_act_kernel<<<(unsigned)((act_threads + 255) / 256), 256, 0, st>>>(reinterpret_cast<__half *>(xt), X, M, Mpad,
                                                                        K, tn);
     if (!holo_check_launch("batched matmul activations")) return false;
     const uint8_t *w = static_cast<const uint8_t *>(W);

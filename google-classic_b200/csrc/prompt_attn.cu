@@ -191,6 +191,8 @@ pf_attn_tc_kernel(float *__restrict__ att, const float *__restrict__ qkv, const 
     };
 
     // ---- pass 1: each row's maximum and sum of exp(score - max), per half row ----
+    // (16 columns at a time: their maximum, then 16 independent exps)
+    const float scale = 1.0f / sqrt_hd;
     float m = -FLT_MAX, l = 0.0f;
     for (int t = 0; t < ntiles && ok; ++t) {
         ok = scores(t, true);
@@ -199,18 +201,21 @@ pf_attn_tc_kernel(float *__restrict__ att, const float *__restrict__ qkv, const 
         for (int cb = c0; cb < c0 + 64; cb += 16) {
             uint32_t v[16];
             tc_ld16(tS + lane_base + (uint32_t)cb, v);
+            // live columns (no early exit: the next tcgen05.ld is warp-wide)
+            const int nv = row_live ? min(16, my_pos - (t * AT_KT + cb) + 1) : 0;
+            if (nv > 0) {
+                float sc[16], cm = -FLT_MAX;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int p = t * AT_KT + cb + j;
-                if (row_live && p <= my_pos) {
-                    const float s = __fdiv_rn(__uint_as_float(v[j]), sqrt_hd);
-                    if (s > m) {
-                        l = l * __expf(m - s) + 1.0f;
-                        m = s;
-                    } else {
-                        l += __expf(s - m);
-                    }
+                for (int j = 0; j < 16; ++j) {
+                    sc[j] = __uint_as_float(v[j]) * scale;
+                    if (j < nv) cm = fmaxf(cm, sc[j]);
                 }
+                const float mn = fmaxf(m, cm);
+                float add = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) add += j < nv ? __expf(sc[j] - mn) : 0.0f;
+                l = l * __expf(m - mn) + add;
+                m = mn;
             }
         }
     }
@@ -239,13 +244,10 @@ pf_attn_tc_kernel(float *__restrict__ att, const float *__restrict__ qkv, const 
             uint32_t v[16];
             tc_ld16(tS + lane_base + (uint32_t)cb, v);
             __align__(16) __half pv[16];
+            const int nv = row_live ? min(16, my_pos - (t * AT_KT + cb) + 1) : 0;   // live columns
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int p = t * AT_KT + cb + j;
-                float e = 0.0f;
-                if (row_live && p <= my_pos) e = __expf(__fdiv_rn(__uint_as_float(v[j]), sqrt_hd) - m) * inv_l;
-                pv[j] = __float2half_rn(e);
-            }
+            for (int j = 0; j < 16; ++j)
+                pv[j] = __float2half_rn(j < nv ? __expf(__uint_as_float(v[j]) * scale - m) * inv_l : 0.0f);
             *reinterpret_cast<uint4 *>(sp + at_off(row, cb)) = *reinterpret_cast<const uint4 *>(&pv[0]);
             *reinterpret_cast<uint4 *>(sp + at_off(row, cb + 8)) = *reinterpret_cast<const uint4 *>(&pv[8]);
         }
