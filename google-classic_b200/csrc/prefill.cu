@@ -82,9 +82,10 @@ using namespace holo_tc;
 __host__ __device__ constexpr uint32_t pf_idesc(int tn) { return tc_idesc_f16(PF_BM, tn); }
 
 // ---- activations: Q8 per 32-block, dequantized to fp16, tiled + swizzled ---
-// xt tile (mt, kc) = rows [mt*tn, +tn) x columns [kc*128, +128), tn*256 bytes:
-// two atom columns of 64 values (tn*128 bytes each); rows past M are zero.
-// Four threads per (row, 32-block), 8 consecutive values each: two 16-byte
+// xt = [K / 128 chunks][2 atom columns of 64 values][Mpad rows][128 bytes]:
+// for a chunk and an atom column the rows are contiguous (and 128-byte
+// swizzled in 8-row atoms), so any 8-aligned run of tokens is one 1-D bulk
+// copy; rows past M are zero.  Four threads per (row, 32-block), 8 consecutive values each: two 16-byte
 // loads, the block maximum over the four lanes, one 16-byte store (8 values
 // are one 16-byte chunk of the swizzled layout).  Mpad * K / 8 threads, a
 // multiple of 32, so every warp is whole.
@@ -119,9 +120,10 @@ __global__ void pf_act_kernel(__half *__restrict__ xt, const float *__restrict__
         const float q = fminf(fmaxf(rintf(__fmul_rn(v[j], id)), -127.0f), 127.0f);
         h[j] = __float2half_rn(__fmul_rn(d, q));
     }
-    const int k = b * 32 + 8 * sub, mt = m / tn, r = m % tn, kc = k / PF_BK, kk = k % PF_BK;
-    uint8_t *tile = reinterpret_cast<uint8_t *>(xt) + ((size_t)mt * (K / PF_BK) + kc) * (size_t)tn * 256;
-    *reinterpret_cast<uint4 *>(tile + (kk >> 6) * tn * 128 + sw128_off(r, kk & 63)) = *reinterpret_cast<const uint4 *>(h);
+    const int k = b * 32 + 8 * sub, kc = k / PF_BK, kk = k % PF_BK;
+    uint8_t *col = reinterpret_cast<uint8_t *>(xt) + ((size_t)kc * 2 + (kk >> 6)) * (size_t)Mpad * 128;
+    *reinterpret_cast<uint4 *>(col + sw128_off(m, kk & 63)) = *reinterpret_cast<const uint4 *>(h);
+    (void)tn;
 }
 
 // ---- weight dequantization (one thread: one row, 32 positions of a chunk) ---
@@ -210,8 +212,8 @@ __device__ __forceinline__ void dq_block(const uint4 &h, const uint4 &p0, const 
 // bandwidth that bounded the first version.
 template <int TYPE, int TN, bool AT>
 __global__ void __launch_bounds__(PF_THREADS, 1)
-pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint8_t *__restrict__ xt, int M, int N,
-              int K, int units, int kc_per_split, int *status) {
+pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint8_t *__restrict__ xt, int M, int Mpad,
+              int N, int K, int units, int kc_per_split, int *status) {
     extern __shared__ uint8_t pf_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
     constexpr int PF_STAGES = pf_a_stages(TN, AT), SB = pf_b_stages(TN, AT), R = pf_raw_slots(TN, AT);
@@ -259,7 +261,8 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
         for (int b = 0; b < nun && ok; ++b) {
             const int rs = b % R;
             ok = mbar_wait_bounded(&B.rfull[rs], (b / R) & 1, status, HOLO_E_TIMEOUT);
-            if (!__all_sync(0xffffffffu, ok)) break;
+            ok = __all_sync(0xffffffffu, ok);   // the warp leaves together
+                if (!ok) break;
             uint4 h, p0, p1;
             dq_load<TYPE>(sr + rs * PF_RAW_BYTES + (r >> 5) * UB, lr, q, h, p0, p1);
             __syncwarp();
@@ -271,7 +274,8 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
                 dq_block<TYPE>(h, p0, p1, c2, q, outv);
                 if (i >= PF_STAGES)
                     ok = mbar_wait_bounded(&B.empty[s], ((i / PF_STAGES) + 1) & 1, status, HOLO_E_TIMEOUT);
-                if (!__all_sync(0xffffffffu, ok)) break;
+                ok = __all_sync(0xffffffffu, ok);   // the warp leaves together
+                if (!ok) break;
                 if constexpr (AT) {
                     // lane r, columns TN + 64 s + 16 q ..: positions 32 q .. 32 q + 31 in pairs
                     uint32_t v[16];
@@ -318,15 +322,19 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
     } else if (warp == PF_B_WARP) {
         // activation tiles, one bulk copy a stage, SB stages ahead
         if (lane == 0) {
-            const uint8_t *xb = xt + ((size_t)mt * (K / PF_BK)) * (size_t)TN * 256;
+            // rows [mt * TN, +TN) of both atom columns of chunk kc0 + i
+            const uint8_t *xb = xt + (size_t)mt * TN * 128;
             int issued = 0;
             for (int i = 0; i < nch; ++i) {
                 const int s = i % SB;
                 if (i >= SB && !mbar_wait_bounded(&B.empty_b[s], ((i / SB) + 1) & 1, status, HOLO_E_TIMEOUT))
                     break;
                 mbar_arrive_expect_tx(&B.full_b[s], (uint32_t)(TN * 256));
-                bulk_copy_g2s(sb + (size_t)s * TN * 256, xb + (size_t)(kc0 + i) * TN * 256, (uint32_t)(TN * 256),
-                              &B.full_b[s]);
+#pragma unroll
+                for (int a = 0; a < 2; ++a)
+                    bulk_copy_g2s(sb + (size_t)s * TN * 256 + (size_t)a * TN * 128,
+                                  xb + ((size_t)(kc0 + i) * 2 + a) * (size_t)Mpad * 128, (uint32_t)(TN * 128),
+                                  &B.full_b[s]);
                 issued = i + 1;
             }
             // every copy has landed before the CTA ends (the MMA thread may
@@ -400,6 +408,251 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
     }
 }
 
+// ---- the matmul on a persistent token-range schedule --------------------------
+// The tile grid above runs (row tiles x token tiles x K splits) CTAs; when
+// that is not a whole number of waves (224 tiles on 148 SMs at M = 512, 172
+// at the W1/W3 projection of a 127-token prompt) the last wave leaves SMs
+// idle.  Here the same work is cut along the tokens instead: the space of
+// (K split, 128-row weight tile, 16-token group) is flattened and every CTA
+// takes an equal contiguous share, in pieces of up to 256 tokens of one
+// weight tile.  Each output element is still the full K range of its split
+// accumulated in one TMEM accumulator, chunk by chunk in K order, so the
+// result does not depend on the schedule.  Between pieces the accumulator is
+// drained by the 16 warps (acc_free) before the MMA thread starts the next.
+constexpr int SG_TN = 256;        // token capacity of a piece (accumulator columns)
+constexpr int SG_STAGES = 4, SG_B = 3, SG_R = 1;
+
+struct SegBars {
+    uint64_t full_a[SG_STAGES], empty[SG_STAGES];
+    uint64_t full_b[SG_B], empty_b[SG_B];
+    uint64_t rfull[SG_R], rempty[SG_R];
+    uint64_t done, acc_free;
+    uint32_t tmem;
+};
+
+// the pieces of one CTA's share [f, f1) of the flattened group space
+struct SegWalk {
+    long long f, f1;
+    int g16, nt;
+    __device__ __forceinline__ bool next(int &ks, int &n0, int &t0, int &ng) {
+        if (f >= f1) return false;
+        const long long item = f / g16;
+        const long long end = min(f1, (item + 1) * (long long)g16);
+        ng = (int)min((long long)(SG_TN / 16), end - f);
+        ks = (int)(item / nt);
+        n0 = (int)(item % nt) * PF_BM;
+        t0 = 16 * (int)(f % g16);
+        f += ng;
+        return true;
+    }
+};
+
+template <int TYPE>
+__global__ void __launch_bounds__(PF_THREADS, 1)
+pf_seg_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint8_t *__restrict__ xt, int M, int Mpad,
+              int N, int K, int units, int kc_per_split, int g16, long long total, int *status) {
+    extern __shared__ uint8_t pf_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sb = smem;                                   // [SG_B][2 atom columns][SG_TN rows][128 B]
+    uint8_t *sr = sb + SG_B * SG_TN * 256;                // [SG_R][4 row-blocks][UB]
+    constexpr int UB = UnitGeom<TYPE>::UNIT_BYTES, CPU = UnitGeom<TYPE>::VALS / PF_BK;
+    SegBars &B = *reinterpret_cast<SegBars *>(sr + SG_R * PF_RAW_BYTES);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nkc = K / PF_BK, nt = (N + PF_BM - 1) / PF_BM;
+    const long long f0 = total * blockIdx.x / gridDim.x, f1 = total * (blockIdx.x + 1) / gridDim.x;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SG_STAGES; ++s) {
+            mbar_init(&B.full_a[s], PF_DQ_WARPS);
+            mbar_init(&B.empty[s], 1);
+        }
+        for (int s = 0; s < SG_B; ++s) {
+            mbar_init(&B.full_b[s], 1);
+            mbar_init(&B.empty_b[s], 1);
+        }
+        for (int k = 0; k < SG_R; ++k) {
+            mbar_init(&B.rfull[k], 1);
+            mbar_init(&B.rempty[k], PF_DQ_WARPS);
+        }
+        mbar_init(&B.done, 1);
+        mbar_init(&B.acc_free, PF_DQ_WARPS);
+        fence_barrier_init();
+    }
+    if (warp == PF_MMA_WARP) tc_alloc(&B.tmem, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = B.tmem;
+    SegWalk walk{f0, f1, g16, nt};
+    int ks, n0, t0, ng;
+
+    if (warp < PF_DQ_WARPS) {
+        // as pf_mma_kernel: thread -> weight row r, 32-value block q of a chunk
+        const int t = threadIdx.x, r = t & (PF_BM - 1), q = t >> 7, lr = r & 31;
+        bool ok = true;
+        int bg = 0, ig = 0, piece = 0;   // raw units, chunks, pieces so far
+        while (ok && walk.next(ks, n0, t0, ng)) {
+            const int kc0 = ks * kc_per_split, nun = (min(nkc, kc0 + kc_per_split) - kc0) / CPU;
+            for (int b = 0; b < nun && ok; ++b, ++bg) {
+                const int rs = bg % SG_R;
+                ok = mbar_wait_bounded(&B.rfull[rs], (bg / SG_R) & 1, status, HOLO_E_TIMEOUT);
+                ok = __all_sync(0xffffffffu, ok);   // the warp leaves together
+                if (!ok) break;
+                uint4 h, p0, p1;
+                dq_load<TYPE>(sr + rs * PF_RAW_BYTES + (r >> 5) * UB, lr, q, h, p0, p1);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&B.rempty[rs]);
+#pragma unroll
+                for (int c2 = 0; c2 < CPU; ++c2) {
+                    const int s = ig % SG_STAGES;
+                    uint4 outv[4];
+                    dq_block<TYPE>(h, p0, p1, c2, q, outv);
+                    if (ig >= SG_STAGES)
+                        ok = mbar_wait_bounded(&B.empty[s], ((ig / SG_STAGES) + 1) & 1, status, HOLO_E_TIMEOUT);
+                    ok = __all_sync(0xffffffffu, ok);   // the warp leaves together
+                if (!ok) break;
+                    uint32_t v[16];
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) {
+                        v[4 * cc] = outv[cc].x;
+                        v[4 * cc + 1] = outv[cc].y;
+                        v[4 * cc + 2] = outv[cc].z;
+                        v[4 * cc + 3] = outv[cc].w;
+                    }
+                    tc_st16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(SG_TN + s * PF_A_COLS + 16 * q), v);
+                    tc_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&B.full_a[s]);
+                    ++ig;
+                }
+            }
+            // the piece's accumulators -> out: warp w reads TMEM lanes
+            // 32 (w % 4).., every fourth 16-column block
+            ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(&B.done, piece & 1, status, HOLO_E_TIMEOUT));
+            tc_fence_after();
+            if (ok) {
+                const int quarter = warp & 3, colq = warp >> 2, n16 = 16 * ng;
+                const int row = n0 + 32 * quarter + lane;
+                float *o = out + (size_t)ks * M * N;
+                for (int cb = 16 * colq; cb < n16; cb += 64) {
+                    uint32_t v[16];
+                    tc_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)cb, v);
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) {
+                        const int m = t0 + cb + jj;
+                        if (m < M && row < N) o[(size_t)m * N + row] = __uint_as_float(v[jj]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.acc_free);   // the MMA thread may overwrite the accumulator
+            ++piece;
+        }
+    } else if (warp == PF_B_WARP) {
+        if (lane == 0) {
+            int ig = 0;
+            bool ok = true;
+            while (ok && walk.next(ks, n0, t0, ng)) {
+                const int kc0 = ks * kc_per_split, nch = min(nkc, kc0 + kc_per_split) - kc0;
+                const uint32_t bytes = (uint32_t)(16 * ng * 128);
+                for (int i = 0; i < nch; ++i, ++ig) {
+                    const int s = ig % SG_B;
+                    if (ig >= SG_B && !mbar_wait_bounded(&B.empty_b[s], ((ig / SG_B) + 1) & 1, status, HOLO_E_TIMEOUT)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&B.full_b[s], 2 * bytes);
+#pragma unroll
+                    for (int a = 0; a < 2; ++a)
+                        bulk_copy_g2s(sb + (size_t)s * SG_TN * 256 + (size_t)a * SG_TN * 128,
+                                      xt + (((size_t)(kc0 + i) * 2 + a) * (size_t)Mpad + t0) * 128, bytes, &B.full_b[s]);
+                }
+            }
+            for (int j = max(0, ig - SG_B); j < ig; ++j) mbar_wait_bounded(&B.full_b[j % SG_B], (j / SG_B) & 1, nullptr, 0);
+        }
+    } else if (warp == PF_RAW_WARP) {
+        if (lane == 0) {
+            int bg = 0;
+            bool ok = true;
+            while (ok && walk.next(ks, n0, t0, ng)) {
+                const int kc0 = ks * kc_per_split, nun = (min(nkc, kc0 + kc_per_split) - kc0) / CPU, u0 = kc0 / CPU;
+                const uint8_t *wrb = W + (size_t)(n0 >> 5) * units * UB;
+                const int nq = min(4, (N + 31) / 32 - (n0 >> 5));
+                for (int b = 0; b < nun; ++b, ++bg) {
+                    const int rs = bg % SG_R;
+                    if (bg >= SG_R && !mbar_wait_bounded(&B.rempty[rs], ((bg / SG_R) + 1) & 1, status, HOLO_E_TIMEOUT)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&B.rfull[rs], (uint32_t)(nq * UB));
+                    for (int qq = 0; qq < nq; ++qq)
+                        bulk_copy_g2s(sr + rs * PF_RAW_BYTES + qq * UB, wrb + ((size_t)qq * units + u0 + b) * UB,
+                                      (uint32_t)UB, &B.rfull[rs]);
+                }
+            }
+            for (int b = max(0, bg - SG_R); b < bg; ++b) mbar_wait_bounded(&B.rfull[b % SG_R], (b / SG_R) & 1, nullptr, 0);
+        }
+    } else {
+        if (lane == 0) {
+            const uint64_t b0 = sw128_desc(sb);
+            bool ok = true;
+            int ig = 0, piece = 0;
+            while (ok && walk.next(ks, n0, t0, ng)) {
+                const int kc0 = ks * kc_per_split, nch = min(nkc, kc0 + kc_per_split) - kc0;
+                const uint32_t idesc = tc_idesc_f16(PF_BM, 16 * ng);
+                if (piece > 0) {
+                    ok = mbar_wait_bounded(&B.acc_free, (piece - 1) & 1, status, HOLO_E_TIMEOUT);
+                    tc_fence_after();
+                }
+                for (int i = 0; i < nch && ok; ++i, ++ig) {
+                    const int s = ig % SG_STAGES, tb = ig % SG_B;
+                    ok = mbar_wait_bounded(&B.full_a[s], (ig / SG_STAGES) & 1, status, HOLO_E_TIMEOUT) &&
+                         mbar_wait_bounded(&B.full_b[tb], (ig / SG_B) & 1, status, HOLO_E_TIMEOUT);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint64_t bd = b0 + (uint64_t)((tb * SG_TN * 256) >> 4);
+                    const uint32_t ta = tmem + (uint32_t)(SG_TN + s * PF_A_COLS);
+#pragma unroll
+                    for (int kk = 0; kk < PF_BK / 16; ++kk)
+                        tc_mma_ts(tmem, ta + (uint32_t)(8 * kk),
+                                  bd + (uint64_t)(((kk >> 2) * (SG_TN * 128) + (kk & 3) * 32) >> 4), idesc, (i | kk) != 0);
+                    tc_commit(&B.empty[s]);
+                    tc_commit(&B.empty_b[tb]);
+                }
+                tc_commit(&B.done);   // the piece's MMAs (at once if none was issued)
+                ++piece;
+            }
+        }
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == PF_MMA_WARP) {
+        tc_fence_after();
+        tc_dealloc(tmem, 512);
+    }
+}
+
+constexpr size_t SG_SMEM = 1024 + (size_t)SG_B * SG_TN * 256 + (size_t)SG_R * PF_RAW_BYTES + sizeof(SegBars);
+
+template <int TYPE>
+bool launch_seg(float *out, const uint8_t *W, const uint8_t *xt, int M, int Mpad, int N, int K, int units,
+                int kc_per_split, int g16, long long total, int grid, int *status, cudaStream_t st) {
+    static int configured = -1;
+    const int dev = holo_dev() ? holo_dev()->id : -1;
+    if (configured != dev) {
+        if (cudaFuncSetAttribute(pf_seg_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SG_SMEM) !=
+            cudaSuccess)
+            return holo_check_launch("prefill: attributes");
+        configured = dev;
+    }
+    pf_seg_kernel<TYPE><<<grid, PF_THREADS, SG_SMEM, st>>>(out, W, xt, M, Mpad, N, K, units, kc_per_split, g16, total,
+                                                         status);
+    return holo_check_launch("prefill matmul (token-range schedule)");
+}
+
 // y[m][n] = sum over ks of part[ks][m][n], in ks order
 __global__ void pf_reduce_kernel(float *__restrict__ y, const float *__restrict__ part, long long mn, int splits) {
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += (long long)gridDim.x * blockDim.x) {
@@ -415,7 +668,7 @@ size_t pf_smem(int tn, bool at) {
 }
 
 template <int TYPE, int TN, bool AT>
-bool launch_mma(float *out, const uint8_t *W, const uint8_t *xt, int M, int N, int K, int units, int splits,
+bool launch_mma(float *out, const uint8_t *W, const uint8_t *xt, int M, int Mpad, int N, int K, int units, int splits,
                 int kc_per_split, int mtiles, int *status, cudaStream_t st) {
     const size_t smem = pf_smem(TN, AT);
     static int configured = -1;   // the device the attribute was set for
@@ -426,7 +679,7 @@ bool launch_mma(float *out, const uint8_t *W, const uint8_t *xt, int M, int N, i
             return holo_check_launch("prefill: attributes");
         configured = dev;
     }
-    pf_mma_kernel<TYPE, TN, AT><<<dim3((N + PF_BM - 1) / PF_BM, mtiles, splits), PF_THREADS, smem, st>>>(out, W, xt, M, N, K, units,
+    pf_mma_kernel<TYPE, TN, AT><<<dim3((N + PF_BM - 1) / PF_BM, mtiles, splits), PF_THREADS, smem, st>>>(out, W, xt, M, Mpad, N, K, units,
                                                                                 kc_per_split, status);
     return holo_check_launch("prefill matmul");
 }
@@ -445,10 +698,25 @@ bool pf_weights_in_tmem() {
     return at;
 }
 
-// the launch plan of one batched matmul: token tile, K splits, scratch bytes
+// the schedule: tiles (default, HOLO_PREFILL_SCHED=tiles), the token-range
+// schedule (=seg) or whichever the wave arithmetic below favours (=auto)
+int pf_sched_mode() {
+    static const int v = [] {
+        const char *e = getenv("HOLO_PREFILL_SCHED");
+        return !e ? 1 : strcmp(e, "auto") == 0 ? 0 : strcmp(e, "seg") == 0 ? 2 : 1;
+    }();
+    return v;
+}
+
+// the launch plan of one batched matmul: token tile, K splits, scratch bytes,
+// and the schedule (seg: token-range pieces on `grid` CTAs over `total`
+// (split, row tile, 16-token group) units)
 struct PfPlan {
     int tn, mtiles, Mpad, splits, kc_per_split;
     size_t xt_bytes, part_bytes;
+    bool seg;
+    int grid, g16;
+    long long total;
 };
 
 PfPlan pf_plan(const WeightInfo &wi, int M, int sms, int plan_rows) {
@@ -467,6 +735,21 @@ PfPlan pf_plan(const WeightInfo &wi, int M, int sms, int plan_rows) {
     p.splits = (nkc + p.kc_per_split - 1) / p.kc_per_split;   // every split non-empty
     p.xt_bytes = ((size_t)p.Mpad * K * 2 + 255) & ~(size_t)255;
     p.part_bytes = p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0;
+    // schedule (numerics do not depend on it): the tile grid takes whole
+    // waves of TN-token tiles; the token-range schedule spreads the same
+    // (split, row tile, token) work evenly over the SMs, at the price of a
+    // drained accumulator (about 16 tokens of work) per piece
+    const int nt = (N + PF_BM - 1) / PF_BM;
+    const long long tiles = (long long)nt * p.mtiles * p.splits;
+    const double cost_tiles = (double)((tiles + sms - 1) / sms) * p.tn;
+    p.g16 = (M + 15) / 16;
+    p.total = (long long)p.splits * nt * p.g16;
+    p.grid = (int)std::min<long long>(sms, p.total);
+    const long long per = (p.total + p.grid - 1) / p.grid;
+    const long long pieces = (per + std::min(16, p.g16) - 1) / std::min(16, p.g16) + 1;
+    const double cost_seg = 16.0 * (double)(per + pieces);
+    const int mode = pf_sched_mode();
+    p.seg = pf_weights_in_tmem() && (mode == 2 || (mode == 0 && cost_seg < 0.95 * cost_tiles));
     return p;
 }
 
@@ -521,11 +804,12 @@ bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const fl
     const uint8_t *w = static_cast<const uint8_t *>(W);
     bool ok;
     const bool at = pf_weights_in_tmem();
+#define PF_SEG(T) launch_seg<T>(part, w, xt, M, Mpad, N, K, wi.units, kc_per_split, pl.g16, pl.total, pl.grid, D->status, st)
 #define PF_LAUNCH_AT(T, A)                                                                                           \
-    (tn == 64    ? launch_mma<T, 64, A>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st)  \
-     : tn == 128 ? launch_mma<T, 128, A>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st) \
-                 : launch_mma<T, 256, A>(part, w, xt, M, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st))
-#define PF_LAUNCH(T) (at ? PF_LAUNCH_AT(T, true) : PF_LAUNCH_AT(T, false))
+    (tn == 64    ? launch_mma<T, 64, A>(part, w, xt, M, Mpad, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st)  \
+     : tn == 128 ? launch_mma<T, 128, A>(part, w, xt, M, Mpad, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st) \
+                 : launch_mma<T, 256, A>(part, w, xt, M, Mpad, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st))
+#define PF_LAUNCH(T) (pl.seg ? PF_SEG(T) : at ? PF_LAUNCH_AT(T, true) : PF_LAUNCH_AT(T, false))
     switch (wi.type) {
     case GT_Q4_K: ok = PF_LAUNCH(GT_Q4_K); break;
     case GT_Q4_0: ok = PF_LAUNCH(GT_Q4_0); break;
@@ -533,6 +817,7 @@ bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const fl
     }
 #undef PF_LAUNCH
 #undef PF_LAUNCH_AT
+#undef PF_SEG
     if (!ok) return false;
     if (splits > 1) {
         const long long mn = (long long)M * N;

@@ -127,5 +127,10 @@ def test_rejects_untiled_or_misaligned(dev):
     raw = dev.upload(np.zeros(256 * 144 // 256 * 128, np.uint8))   # not from cuda_upload_quant
     assert dev.lib.cuda_matmul_quant_batched(Yd, raw, Xd, 1, 128, 256) == hb.HOLO_E_ARG
     dev.lib.cuda_clear_status()
+    # activations not 16-byte aligned (the tensor-core path loads 16 bytes at a time)
+    Wd = dev.upload_quant(synth.quant_matrix(hb.Q4_K, 128, 256, seed=1), hb.Q4_K, 128, 256)
+    assert dev.lib.cuda_matmul_quant_batched(Yd, Wd, Xd + 4, 17, 128, 256) == hb.HOLO_E_ARG
+    dev.lib.cuda_clear_status()
+    dev.free(Wd)
     for p in (Xd, Yd, raw):
         dev.free(p)
