@@ -419,6 +419,13 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
 // accumulated in one TMEM accumulator, chunk by chunk in K order, so the
 // result does not depend on the schedule.  Between pieces the accumulator is
 // drained by the 16 warps (acc_free) before the MMA thread starts the next.
+// Measured slower than the tile grid at every prefill shape (M = 512:
+// 92 vs 63 us; M = 64: 58 vs 29 us; a 7B 127-token prompt: 7.25 vs 6.15 ms):
+// every piece dequantizes its weight tile over the whole K range, and the
+// pieces average far fewer tokens than a 256-token tile, so the extra
+// dequantization outweighs the idle SMs of the last wave.  Kept selectable
+// (HOLO_PREFILL_SCHED=seg) with its bit-identity test; a K-wise split of the
+// last wave (partial accumulators, fixed-order sum) is the remaining option.
 constexpr int SG_TN = 256;        // token capacity of a piece (accumulator columns)
 constexpr int SG_STAGES = 4, SG_B = 3, SG_R = 1;
 
@@ -698,12 +705,13 @@ bool pf_weights_in_tmem() {
     return at;
 }
 
-// the schedule: tiles (default, HOLO_PREFILL_SCHED=tiles), the token-range
-// schedule (=seg) or whichever the wave arithmetic below favours (=auto)
-int pf_sched_mode() {
-    static const int v = [] {
+// the schedule: the tile grid (default) or the token-range schedule
+// (HOLO_PREFILL_SCHED=seg, kept for comparison: measured slower, see
+// pf_seg_kernel)
+bool pf_sched_seg() {
+    static const bool v = [] {
         const char *e = getenv("HOLO_PREFILL_SCHED");
-        return !e ? 1 : strcmp(e, "auto") == 0 ? 0 : strcmp(e, "seg") == 0 ? 2 : 1;
+        return e && strcmp(e, "seg") == 0;
     }();
     return v;
 }
@@ -735,21 +743,13 @@ PfPlan pf_plan(const WeightInfo &wi, int M, int sms, int plan_rows) {
     p.splits = (nkc + p.kc_per_split - 1) / p.kc_per_split;   // every split non-empty
     p.xt_bytes = ((size_t)p.Mpad * K * 2 + 255) & ~(size_t)255;
     p.part_bytes = p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0;
-    // schedule (numerics do not depend on it): the tile grid takes whole
-    // waves of TN-token tiles; the token-range schedule spreads the same
-    // (split, row tile, token) work evenly over the SMs, at the price of a
-    // drained accumulator (about 16 tokens of work) per piece
+    // the token-range schedule (numerics do not depend on it): the same
+    // (split, row tile, 16-token group) work spread evenly over the SMs
     const int nt = (N + PF_BM - 1) / PF_BM;
-    const long long tiles = (long long)nt * p.mtiles * p.splits;
-    const double cost_tiles = (double)((tiles + sms - 1) / sms) * p.tn;
     p.g16 = (M + 15) / 16;
     p.total = (long long)p.splits * nt * p.g16;
     p.grid = (int)std::min<long long>(sms, p.total);
-    const long long per = (p.total + p.grid - 1) / p.grid;
-    const long long pieces = (per + std::min(16, p.g16) - 1) / std::min(16, p.g16) + 1;
-    const double cost_seg = 16.0 * (double)(per + pieces);
-    const int mode = pf_sched_mode();
-    p.seg = pf_weights_in_tmem() && (mode == 2 || (mode == 0 && cost_seg < 0.95 * cost_tiles));
+    p.seg = pf_weights_in_tmem() && pf_sched_seg();
     return p;
 }
 
