@@ -879,10 +879,17 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
     // every projection's K split is planned for the whole matrix (not this
     // rank's rows), so a row shard sums each row exactly as one GPU does
     const int rows_qkv = (d.n_heads + 2 * d.n_kv_heads) * hd;
+    // RMSNorm + projection: on the tensor-core path the norm is fused into the
+    // activation quantize/tile kernel (same arithmetic), else its own kernel
+    auto normed = [&](float *Y, const void *W, const WeightInfo &wi, const float *nw, int plan_rows) {
+        if (M > MVB_MAX_M)
+            return holo_matmul_batched(Y, W, wi, p.x, M, st, p.scratch, p.scratch_bytes, plan_rows, nw, d.eps);
+        return rows_norm(p, nw, d.dim, d.eps, st) &&
+               holo_matmul_batched(Y, W, wi, p.xn, M, st, p.scratch, p.scratch_bytes, plan_rows);
+    };
     for (int l = 0; l < d.n_layers && ok; ++l) {
         HoloLayer &L = m->layers[l];
-        ok = rows_norm(p, L.attn_norm, d.dim, d.eps, st) &&
-             holo_matmul_batched(p.qkv, L.wqkv, L.i_qkv, p.xn, M, st, p.scratch, p.scratch_bytes, rows_qkv);
+        ok = normed(p.qkv, L.wqkv, L.i_qkv, L.attn_norm, rows_qkv);
         const size_t es = d.kv_f16 ? 2 : 4;
         uint8_t *kc = (uint8_t *)p.kc + (size_t)l * kv_layer * es, *vc = (uint8_t *)p.vc + (size_t)l * kv_layer * es;
         const dim3 rg(std::max(m->nh, m->nkv), M), ag(m->nh, m->max_splits, M), mg(m->nh, M);
@@ -922,8 +929,7 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
         ok = ok && holo_matmul_batched(p.t, L.wo, L.i_o, att_in, M, st, p.scratch, p.scratch_bytes, d.dim);
         if (shard) ok = ok && row_exchange(m, st, p.t, M, m->dim_loc, m->d0, m->off_rt, d.dim);
         ok = ok && add(t_in);
-        ok = ok && rows_norm(p, L.ffn_norm, d.dim, d.eps, st) &&
-             holo_matmul_batched(p.hh, L.w13, L.i_13, p.xn, M, st, p.scratch, p.scratch_bytes, 2 * d.ffn_dim);
+        ok = ok && normed(p.hh, L.w13, L.i_13, L.ffn_norm, 2 * d.ffn_dim);
         if (ok) {
             const long long n = (long long)M * m->ffn_loc;
             bt_swiglu_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 2048), 256, 0, st>>>(p.h, p.hh,

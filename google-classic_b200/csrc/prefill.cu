@@ -126,6 +126,77 @@ __global__ void pf_act_kernel(__half *__restrict__ xt, const float *__restrict__
     (void)tn;
 }
 
+// Sum over the block, in the order of the batched RMSNorm's block_sum
+// (sampler.cuh): a butterfly within each warp, then warp 0 over the warps.
+__device__ __forceinline__ float pf_block_sum(float v, float *sv) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) sv[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        v = lane < (int)(blockDim.x >> 5) ? sv[lane] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) sv[0] = v;
+    }
+    __syncthreads();
+    v = sv[0];
+    __syncthreads();
+    return v;
+}
+
+// RMSNorm fused into pf_act_kernel (the projections that follow a norm):
+// block m (1024 threads) = activation row m: sum of squares and scale exactly
+// as bt_rmsnorm_kernel (rms_norm, tensor.c:242-255), x * scale * w, then the
+// Q8 quantization and the swizzled 16-byte stores of pf_act_kernel; rows
+// past M are zero.  Every lane of a warp runs each round (the 4-lane
+// shuffles), idle lanes compute on zeros and store nothing.
+__global__ void __launch_bounds__(1024) pf_act_norm_kernel(__half *__restrict__ xt, const float *__restrict__ x,
+                                                           const float *__restrict__ w, float eps, int M, int Mpad,
+                                                           int K) {
+    __shared__ float sv[32];
+    const int m = blockIdx.x, ng = K / 8;
+    float scale = 0.0f;
+    if (m < M) {
+        const float *xr = x + (size_t)m * K;
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+        ss = pf_block_sum(ss, sv);
+        scale = 1.0f / sqrtf(ss / (float)K + eps);
+    }
+    for (int g0 = 0; g0 < ng; g0 += blockDim.x) {
+        const int g = g0 + threadIdx.x;   // 8-value group; a 32-block is 4 consecutive lanes
+        const bool live = g < ng;
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+        if (live && m < M) {
+            const float *xr = x + (size_t)m * K + 8 * g;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = xr[j] * scale * w[8 * g + j];
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        __align__(16) __half h[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float q = fminf(fmaxf(rintf(__fmul_rn(v[j], id)), -127.0f), 127.0f);
+            h[j] = __float2half_rn(__fmul_rn(d, q));
+        }
+        if (live) {
+            const int k = 8 * g, kc = k / PF_BK, kk = k % PF_BK;
+            uint8_t *col = reinterpret_cast<uint8_t *>(xt) + ((size_t)kc * 2 + (kk >> 6)) * (size_t)Mpad * 128;
+            *reinterpret_cast<uint4 *>(col + sw128_off(m, kk & 63)) = *reinterpret_cast<const uint4 *>(h);
+        }
+    }
+}
+
 // ---- weight dequantization (one thread: one row, 32 positions of a chunk) ---
 // The raw unit of the thread's row-block in shared memory -> the registers a
 // unit needs: the row's head and two 16-byte planes.
@@ -767,10 +838,16 @@ size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M, int plan_rows) {
 // buffer of scratch_bytes (at least holo_matmul_batched_scratch), or NULL for
 // the library's shared one.
 bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st,
-                         void *scratch, size_t scratch_bytes, int plan_rows) {
+                         void *scratch, size_t scratch_bytes, int plan_rows, const float *norm_w, float norm_eps) {
     // a few rows: the CUDA-core kernel that reads each weight unit once for all
     // of them (matvec_batch.cu); a tensor-core tile would be mostly padding
-    if (M > 0 && M <= MVB_MAX_M) return holo_matmul_few(Y, W, wi, X, M, st, scratch, scratch_bytes);
+    if (M > 0 && M <= MVB_MAX_M) {
+        if (norm_w) {
+            holo_set_status(HOLO_E_ARG, "batched matmul: the fused RMSNorm needs more than 16 rows");
+            return false;
+        }
+        return holo_matmul_few(Y, W, wi, X, M, st, scratch, scratch_bytes);
+    }
     HoloDevice *D = holo_dev();
     if (!D) return false;
     const int N = wi.rows, K = wi.cols;
@@ -797,9 +874,13 @@ bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const fl
     if (!tmp) return false;
     uint8_t *xt = tmp;
     float *part = splits > 1 ? reinterpret_cast<float *>(tmp + xt_bytes) : Y;
-    const long long act_threads = (long long)Mpad * (K / 32) * 4;
-    pf_act_kernel<<<(unsigned)((act_threads + 255) / 256), 256, 0, st>>>(reinterpret_cast<__half *>(xt), X, M, Mpad,
-                                                                       K, tn);
+    if (norm_w) {
+        pf_act_norm_kernel<<<Mpad, 1024, 0, st>>>(reinterpret_cast<__half *>(xt), X, norm_w, norm_eps, M, Mpad, K);
+    } else {
+        const long long act_threads = (long long)Mpad * (K / 32) * 4;
+        pf_act_kernel<<<(unsigned)((act_threads + 255) / 256), 256, 0, st>>>(reinterpret_cast<__half *>(xt), X, M,
+                                                                           Mpad, K, tn);
+    }
     if (!holo_check_launch("batched matmul activations")) return false;
     const uint8_t *w = static_cast<const uint8_t *>(W);
     bool ok;
