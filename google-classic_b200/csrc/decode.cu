@@ -887,6 +887,16 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
         return rows_norm(p, nw, d.dim, d.eps, st) &&
                holo_matmul_batched(Y, W, wi, p.xn, M, st, p.scratch, p.scratch_bytes, plan_rows);
     };
+    // projection + residual (Wo, W2): one GPU on the tensor-core path adds
+    // into x inside the matmul's K-split reduction (same arithmetic); a
+    // sharded pass exchanges the rank's slice first, then adds
+    auto projected = [&](float *t, const void *W, const WeightInfo &wi, const float *in) {
+        if (!shard && M > MVB_MAX_M)
+            return holo_matmul_batched(t, W, wi, in, M, st, p.scratch, p.scratch_bytes, d.dim, nullptr, 0.0f, p.x);
+        bool r = holo_matmul_batched(t, W, wi, in, M, st, p.scratch, p.scratch_bytes, d.dim);
+        if (shard) r = r && row_exchange(m, st, t, M, m->dim_loc, m->d0, m->off_rt, d.dim);
+        return r && add(t_in);
+    };
     for (int l = 0; l < d.n_layers && ok; ++l) {
         HoloLayer &L = m->layers[l];
         ok = normed(p.qkv, L.wqkv, L.i_qkv, L.attn_norm, rows_qkv);
@@ -926,9 +936,7 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
         }
 #undef BT_ATTN
         if (shard) ok = ok && row_exchange(m, st, p.att, M, m->q_dim, m->h0 * hd, m->off_ratt, m->q_dim_g);
-        ok = ok && holo_matmul_batched(p.t, L.wo, L.i_o, att_in, M, st, p.scratch, p.scratch_bytes, d.dim);
-        if (shard) ok = ok && row_exchange(m, st, p.t, M, m->dim_loc, m->d0, m->off_rt, d.dim);
-        ok = ok && add(t_in);
+        ok = ok && projected(p.t, L.wo, L.i_o, att_in);
         ok = ok && normed(p.hh, L.w13, L.i_13, L.ffn_norm, 2 * d.ffn_dim);
         if (ok) {
             const long long n = (long long)M * m->ffn_loc;
@@ -937,9 +945,7 @@ bool enqueue_rows(HoloModel *m, cudaStream_t st, const RowPass &p) {
             ok = holo_check_launch("rows: swiglu");
         }
         if (shard) ok = ok && row_exchange(m, st, p.h, M, m->ffn_loc, m->f0, m->off_rh, d.ffn_dim);
-        ok = ok && holo_matmul_batched(p.t, L.w2, L.i_2, h_in, M, st, p.scratch, p.scratch_bytes, d.dim);
-        if (shard) ok = ok && row_exchange(m, st, p.t, M, m->dim_loc, m->d0, m->off_rt, d.dim);
-        ok = ok && add(t_in);
+        ok = ok && projected(p.t, L.w2, L.i_2, h_in);
     }
     return ok;
 }

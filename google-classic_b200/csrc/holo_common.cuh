@@ -193,10 +193,13 @@ WeightInfo holo_weight_info(int ggml_type, int rows, int cols, int q4k_layout);
 // is cut at the same K points as on one GPU); 0: the weight's own rows.
 // norm_w: X is the un-normalized activation and each row is RMS-normalized
 // with these weights on the way in (bit-identical to bt_rmsnorm_kernel
-// followed by the matmul; M > MVB_MAX_M only).
+// followed by the matmul; M > MVB_MAX_M only).  resid: the product is also
+// added into resid[M][N] (the residual stream), fused into the K-split
+// reduction when there is one -- bit-identical to an add after; Y is then
+// scratch (M > MVB_MAX_M only).
 bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st,
                          void *scratch, size_t scratch_bytes, int plan_rows = 0, const float *norm_w = nullptr,
-                         float norm_eps = 0.0f);
+                         float norm_eps = 0.0f, float *resid = nullptr);
 size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M, int plan_rows = 0);
 // the batched matmul's weights: rows a multiple of this (one MMA tile)
 constexpr int PF_ROWS_ALIGN = 128;

@@ -731,13 +731,23 @@ bool launch_seg(float *out, const uint8_t *W, const uint8_t *xt, int M, int Mpad
     return holo_check_launch("prefill matmul (token-range schedule)");
 }
 
-// y[m][n] = sum over ks of part[ks][m][n], in ks order
+// y[m][n] = sum over ks of part[ks][m][n], in ks order; RESID: y[i] += that
+// sum (a residual stream updated in place, the arithmetic of computing the
+// sum into a buffer and adding it after)
+template <bool RESID>
 __global__ void pf_reduce_kernel(float *__restrict__ y, const float *__restrict__ part, long long mn, int splits) {
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += (long long)gridDim.x * blockDim.x) {
         float s = part[i];
         for (int k = 1; k < splits; ++k) s += part[(size_t)k * mn + i];
-        y[i] = s;
+        if (RESID) y[i] = y[i] + s;
+        else y[i] = s;
     }
+}
+
+// y[i] += t[i] (the residual add after a matmul that was not K-split)
+__global__ void pf_add_kernel(float *__restrict__ y, const float *__restrict__ t, long long mn) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += (long long)gridDim.x * blockDim.x)
+        y[i] += t[i];
 }
 
 size_t pf_smem(int tn, bool at) {
@@ -838,12 +848,13 @@ size_t holo_matmul_batched_scratch(const WeightInfo &wi, int M, int plan_rows) {
 // buffer of scratch_bytes (at least holo_matmul_batched_scratch), or NULL for
 // the library's shared one.
 bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const float *X, int M, cudaStream_t st,
-                         void *scratch, size_t scratch_bytes, int plan_rows, const float *norm_w, float norm_eps) {
+                         void *scratch, size_t scratch_bytes, int plan_rows, const float *norm_w, float norm_eps,
+                         float *resid) {
     // a few rows: the CUDA-core kernel that reads each weight unit once for all
     // of them (matvec_batch.cu); a tensor-core tile would be mostly padding
     if (M > 0 && M <= MVB_MAX_M) {
-        if (norm_w) {
-            holo_set_status(HOLO_E_ARG, "batched matmul: the fused RMSNorm needs more than 16 rows");
+        if (norm_w || resid) {
+            holo_set_status(HOLO_E_ARG, "batched matmul: the fused RMSNorm / residual need more than 16 rows");
             return false;
         }
         return holo_matmul_few(Y, W, wi, X, M, st, scratch, scratch_bytes);
@@ -900,11 +911,15 @@ bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const fl
 #undef PF_LAUNCH_AT
 #undef PF_SEG
     if (!ok) return false;
+    const long long mn = (long long)M * N;
+    const unsigned rgrid = (unsigned)std::min<long long>((mn + 255) / 256, 4 * D->sms);
     if (splits > 1) {
-        const long long mn = (long long)M * N;
-        pf_reduce_kernel<<<(unsigned)std::min<long long>((mn + 255) / 256, 4 * D->sms), 256, 0, st>>>(Y, part, mn,
-                                                                                                     splits);
+        if (resid) pf_reduce_kernel<true><<<rgrid, 256, 0, st>>>(resid, part, mn, splits);
+        else pf_reduce_kernel<false><<<rgrid, 256, 0, st>>>(Y, part, mn, splits);
         if (!holo_check_launch("batched matmul reduce")) return false;
+    } else if (resid) {
+        pf_add_kernel<<<rgrid, 256, 0, st>>>(resid, Y, mn);
+        if (!holo_check_launch("batched matmul residual")) return false;
     }
     return true;
 }
