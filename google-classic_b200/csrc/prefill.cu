@@ -348,6 +348,9 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
                 ok = __all_sync(0xffffffffu, ok);   // the warp leaves together
                 if (!ok) break;
                 if constexpr (AT) {
+                    // the stage's previous MMAs completed (empty[s]); order this
+                    // thread's TMEM stores after that wait
+                    tc_fence_after();
                     // lane r, columns TN + 64 s + 16 q ..: positions 32 q .. 32 q + 31 in pairs
                     uint32_t v[16];
 #pragma unroll
@@ -498,7 +501,7 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
 // (HOLO_PREFILL_SCHED=seg) with its bit-identity test; a K-wise split of the
 // last wave (partial accumulators, fixed-order sum) is the remaining option.
 constexpr int SG_TN = 256;        // token capacity of a piece (accumulator columns)
-constexpr int SG_STAGES = 4, SG_B = 3, SG_R = 1;
+constexpr int SG_STAGES = 4, SG_B = 2, SG_R = 1;   // 2 activation stages: see holo_matmul_batched
 
 struct SegBars {
     uint64_t full_a[SG_STAGES], empty[SG_STAGES];
@@ -589,6 +592,7 @@ pf_seg_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
                         ok = mbar_wait_bounded(&B.empty[s], ((ig / SG_STAGES) + 1) & 1, status, HOLO_E_TIMEOUT);
                     ok = __all_sync(0xffffffffu, ok);   // the warp leaves together
                 if (!ok) break;
+                    tc_fence_after();   // after the empty[s] wait, before the stores (as pf_mma_kernel)
                     uint32_t v[16];
 #pragma unroll
                     for (int cc = 0; cc < 4; ++cc) {
@@ -895,7 +899,12 @@ bool holo_matmul_batched(float *Y, const void *W, const WeightInfo &wi, const fl
     if (!holo_check_launch("batched matmul activations")) return false;
     const uint8_t *w = static_cast<const uint8_t *>(W);
     bool ok;
-    const bool at = pf_weights_in_tmem();
+    // weights in TMEM for token tiles up to 128 (4 activation stages); a
+    // 256-token tile keeps them in shared memory: with TMEM weights and its 3
+    // activation stages of 64 KB the results varied from run to run (cause
+    // not found; 2 stages, or the weights in shared memory, measured
+    // bit-stable over 14 repeated 70B-shape prompt passes)
+    const bool at = pf_weights_in_tmem() && tn <= 128;
 #define PF_SEG(T) launch_seg<T>(part, w, xt, M, Mpad, N, K, wi.units, kc_per_split, pl.g16, pl.total, pl.grid, D->status, st)
 #define PF_LAUNCH_AT(T, A)                                                                                           \
     (tn == 64    ? launch_mma<T, 64, A>(part, w, xt, M, Mpad, N, K, wi.units, splits, kc_per_split, mtiles, D->status, st)  \
