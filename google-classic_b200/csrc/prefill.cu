@@ -361,7 +361,6 @@ pf_mma_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
                         v[4 * cc + 3] = outv[cc].w;
                     }
                     tc_st16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(TN + s * PF_A_COLS + 16 * q), v);
-                    tc_wait_st();
                     tc_fence_before();   // the MMA thread reads the stage after the barrier
                 } else {
                     // column 32 q + position of the chunk: atom column q / 2
@@ -602,7 +601,6 @@ pf_seg_kernel(float *__restrict__ out, const uint8_t *__restrict__ W, const uint
                         v[4 * cc + 3] = outv[cc].w;
                     }
                     tc_st16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(SG_TN + s * PF_A_COLS + 16 * q), v);
-                    tc_wait_st();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&B.full_a[s]);

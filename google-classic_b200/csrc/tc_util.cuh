@@ -48,28 +48,34 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
                  :: "r"(smem_addr(bar)) : "memory");
 }
 
-// 16 consecutive fp32 columns of this warp's 32 TMEM lanes
+// 16 consecutive fp32 columns of this warp's 32 TMEM lanes.  The load and
+// its wait are one asm statement: tcgen05.ld writes the destination
+// registers asynchronously, so the compiler must not see them as defined
+// (and move or read them) before tcgen05.wait::ld has returned.
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
           "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        : "r"(taddr)
+        : "memory");
 }
 
-// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes from registers;
-// tc_wait_st waits until this thread's stores have landed
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes from registers,
+// and the wait until they have landed, in one asm statement: tcgen05.st may
+// read its source registers after it issues, so the compiler must not reuse
+// them before tcgen05.wait::st has returned.
 __device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&v)[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n\t"
+        "tcgen05.wait::st.sync.aligned;"
         :: "r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
            "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
 }
-__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // byte offset of element (row r, column c) of a [rows][64] fp16 tile in the
 // 128-byte-swizzled K-major layout (16-byte chunk index XOR row mod 8)
